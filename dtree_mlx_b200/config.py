@@ -1,0 +1,79 @@
+"""Model shapes of the synthetic workloads.
+
+Names follow mlx-lm's Qwen3 ``ModelArgs`` (hidden_size, num_hidden_layers,
+...).  ``rms_norm_eps`` is Qwen3's 1e-6.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass, asdict
+
+
+@dataclass(frozen=True)
+class Qwen3Config:
+    hidden_size: int
+    num_hidden_layers: int
+    num_attention_heads: int
+    num_key_value_heads: int
+    head_dim: int
+    intermediate_size: int
+    vocab_size: int
+    rope_theta: float = 1_000_000.0
+    rms_norm_eps: float = 1e-6
+    tie_word_embeddings: bool = True
+    model_type: str = "qwen3"
+
+    @property
+    def q_dim(self) -> int:
+        return self.num_attention_heads * self.head_dim
+
+    @property
+    def kv_dim(self) -> int:
+        return self.num_key_value_heads * self.head_dim
+
+    def n_params(self) -> int:
+        h, f = self.hidden_size, self.intermediate_size
+        per_layer = (
+            h * (self.q_dim + 2 * self.kv_dim)  # q k v
+            + self.q_dim * h                     # o
+            + 3 * h * f                          # gate up down
+            + 2 * h + 2 * self.head_dim          # norms
+        )
+        return self.num_hidden_layers * per_layer + self.vocab_size * h + h
+
+    def as_dict(self) -> dict:
+        return asdict(self)
+
+
+PRESETS: dict[str, Qwen3Config] = {
+    # tiny Qwen3 (CPU plumbing case of the reference)
+    "qwen3-tiny": Qwen3Config(
+        hidden_size=512,
+        num_hidden_layers=4,
+        num_attention_heads=8,
+        num_key_value_heads=4,
+        head_dim=64,
+        intermediate_size=1536,
+        vocab_size=32768,
+    ),
+    # Qwen3-4B shape
+    "qwen3-4b": Qwen3Config(
+        hidden_size=2560,
+        num_hidden_layers=36,
+        num_attention_heads=32,
+        num_key_value_heads=8,
+        head_dim=128,
+        intermediate_size=9728,
+        vocab_size=151936,
+    ),
+}
+
+
+def default_layer_ids(cfg: Qwen3Config, n: int = 5) -> list[int]:
+    """Target layers whose hidden states feed the drafter (DFlash
+    ``target_layer_ids``; the checkpoint's list is not available here, so
+    ``n`` evenly spaced layers are used)."""
+    L = cfg.num_hidden_layers
+    n = min(n, L)
+    if n == 1:
+        return [L - 1]
+    return sorted({round(1 + i * (L - 3) / (n - 1)) for i in range(n)})

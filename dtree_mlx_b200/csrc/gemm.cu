@@ -1,0 +1,148 @@
+// Host side of the stream-K tcgen05 GEMM: plans (tensor maps + params),
+// dispatch over tile widths / epilogues, and the dense-linear and LM-head
+// argmax entry points.
+#include "gemm.cuh"
+
+namespace dtree {
+
+// workspace: [partials grid*2*t_pad*128 f32][tile counters][argmax keys][done]
+constexpr int kMaxTileCounters = 8192;
+constexpr int kMaxArgmaxRows = 256;
+
+struct GemmWs {
+  float* partials;
+  uint32_t* tile_cnt;
+  unsigned long long* keys;
+  uint32_t* done;
+};
+
+static size_t ws_partial_bytes(int t_pad, int grid) {
+  return (static_cast<size_t>(grid) * 2 * t_pad * 128 * 4 + 255) & ~static_cast<size_t>(255);
+}
+
+size_t gemm_ws_bytes(int t_pad, int grid) {
+  return ws_partial_bytes(t_pad, grid) + kMaxTileCounters * 4 + kMaxArgmaxRows * 8 + 256;
+}
+
+static GemmWs ws_split(void* base, int t_pad, int grid) {
+  GemmWs w;
+  char* b = static_cast<char*>(base);
+  w.partials = reinterpret_cast<float*>(b);
+  b += ws_partial_bytes(t_pad, grid);
+  w.tile_cnt = reinterpret_cast<uint32_t*>(b);
+  b += kMaxTileCounters * 4;
+  w.keys = reinterpret_cast<unsigned long long*>(b);
+  b += kMaxArgmaxRows * 8;
+  w.done = reinterpret_cast<uint32_t*>(b);
+  return w;
+}
+
+static bool valid_tpad(int t) { return t == 16 || t == 32 || t == 64 || t == 128; }
+
+int gemm_plan(GemmPlan* plan, const void* w, int n_out, int k, const void* x, int t_pad, int x_row_stride_elems,
+              int epi, int grid) {
+  DTREE_CHECK_ARG(valid_tpad(t_pad), "t_pad must be 16, 32, 64 or 128");
+  DTREE_CHECK_ARG(k % 64 == 0 && k > 0, "K must be a positive multiple of 64");
+  DTREE_CHECK_ARG(n_out > 0, "N must be positive");
+  const int m_tiles = (n_out + 127) / 128;
+  DTREE_CHECK_ARG(m_tiles <= kMaxTileCounters, "N too large");
+  int rc = make_tmap_2d_bf16(&plan->tmap_w, w, static_cast<uint64_t>(k), static_cast<uint64_t>(n_out),
+                             static_cast<uint64_t>(k) * 2, 64, 128, true);
+  if (rc) return rc;
+  rc = make_tmap_2d_bf16(&plan->tmap_x, x, static_cast<uint64_t>(k), static_cast<uint64_t>(t_pad),
+                         static_cast<uint64_t>(x_row_stride_elems) * 2, 64, static_cast<uint32_t>(t_pad), true);
+  if (rc) return rc;
+  GemmParams& p = plan->p;
+  p = GemmParams{};
+  p.n_out = n_out;
+  p.kb = k / 64;
+  p.m_tiles = m_tiles;
+  p.n_rows = t_pad;
+  const long long units = static_cast<long long>(m_tiles) * p.kb;
+  const int sms = grid > 0 ? grid : num_sms();
+  p.grid = static_cast<int>(units < sms ? units : sms);
+  plan->t_pad = t_pad;
+  plan->epi = epi;
+  return kOk;
+}
+
+int gemm_bind_ws(GemmPlan* plan, void* ws, size_t ws_bytes) {
+  DTREE_CHECK_ARG(ws != nullptr && ws_bytes >= gemm_ws_bytes(plan->t_pad, plan->p.grid), "GEMM workspace too small");
+  GemmWs w = ws_split(ws, plan->t_pad, plan->p.grid);
+  plan->p.ws = w.partials;
+  plan->p.tile_cnt = w.tile_cnt;
+  plan->p.argmax_keys = w.keys;
+  plan->p.done_cnt = w.done;
+  return kOk;
+}
+
+template <int TPAD, int EPI>
+static int launch_t(const GemmPlan& pl, cudaStream_t st) {
+  using C = GemmCfg<TPAD, EPI>;
+  auto kern = gemm_streamk_kernel<TPAD, EPI>;
+  DTREE_CUDA_RET(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem));
+  DTREE_CUDA_RET(launch_pdl(kern, dim3(pl.p.grid), dim3(kGemmThreads), static_cast<size_t>(C::kSmem), st,
+                            pl.tmap_w, pl.tmap_x, pl.p));
+  return kOk;
+}
+
+template <int TPAD>
+static int launch_epi(const GemmPlan& pl, cudaStream_t st) {
+  switch (pl.epi) {
+    case kEpiStore: return launch_t<TPAD, kEpiStore>(pl, st);
+    case kEpiResidual: return launch_t<TPAD, kEpiResidual>(pl, st);
+    case kEpiSwiglu: return launch_t<TPAD, kEpiSwiglu>(pl, st);
+    case kEpiQkv: return launch_t<TPAD, kEpiQkv>(pl, st);
+    case kEpiArgmax: return launch_t<TPAD, kEpiArgmax>(pl, st);
+  }
+  return fail(kErrInvalidArg, "unknown epilogue");
+}
+
+int gemm_launch(const GemmPlan& pl, cudaStream_t st) {
+  switch (pl.t_pad) {
+    case 16: return launch_epi<16>(pl, st);
+    case 32: return launch_epi<32>(pl, st);
+    case 64: return launch_epi<64>(pl, st);
+    case 128: return launch_epi<128>(pl, st);
+  }
+  return fail(kErrInvalidArg, "bad t_pad");
+}
+
+}  // namespace dtree
+
+using namespace dtree;
+
+extern "C" size_t dtree_linear_workspace_bytes(int t_pad, int n) {
+  (void)n;
+  return gemm_ws_bytes(t_pad, num_sms());
+}
+
+extern "C" int dtree_linear_bf16(const void* x, int t_pad, int k, const void* w, int n, void* y, void* workspace,
+                                 size_t workspace_bytes, int split_k, void* stream) {
+  DTREE_CHECK_ARG(x && w && y, "null pointer");
+  GemmPlan plan;
+  int rc = gemm_plan(&plan, w, n, k, x, t_pad, k, kEpiStore, split_k > 0 ? split_k : 0);
+  if (rc) return rc;
+  rc = gemm_bind_ws(&plan, workspace, workspace_bytes);
+  if (rc) return rc;
+  plan.p.out = static_cast<__nv_bfloat16*>(y);
+  plan.p.ldo = n;
+  return gemm_launch(plan, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" size_t dtree_lm_head_workspace_bytes(int t_pad) { return gemm_ws_bytes(t_pad, num_sms()); }
+
+extern "C" int dtree_lm_head_argmax(const void* h, int t_pad, int n_rows, int hidden, const void* embed, int vocab,
+                                    int32_t* out, void* workspace, size_t workspace_bytes, void* stream) {
+  DTREE_CHECK_ARG(h && embed && out, "null pointer");
+  DTREE_CHECK_ARG(n_rows > 0 && n_rows <= t_pad, "n_rows must be in [1, t_pad]");
+  GemmPlan plan;
+  int rc = gemm_plan(&plan, embed, vocab, hidden, h, t_pad, hidden, kEpiArgmax, 0);
+  if (rc) return rc;
+  rc = gemm_bind_ws(&plan, workspace, workspace_bytes);
+  if (rc) return rc;
+  plan.p.n_rows = n_rows;
+  plan.p.vocab = vocab;
+  plan.p.argmax_out = out;
+  return gemm_launch(plan, static_cast<cudaStream_t>(stream));
+}

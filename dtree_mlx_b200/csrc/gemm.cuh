@@ -1,0 +1,465 @@
+// Stream-K, warp-specialized tcgen05 GEMM for the skinny verify projections.
+//
+//   out[t, n] = sum_k X[t, k] * W[n, k]      t < TPAD (tree rows), n < N
+//
+// Swap-AB: W (weights, streamed once from HBM) is the MMA's M=128 A operand,
+// X (the tree's activations, L2 resident) the N=TPAD B operand; both K-major
+// bf16 tiles of 64 elements (128 B, one swizzle atom) per stage, brought in
+// by TMA with 128-byte swizzle.  The accumulator D[128 x TPAD] fp32 lives in
+// TMEM (two buffers, so the MMA of the next segment overlaps the epilogue).
+//
+// Work split: the (m_tile, k_block) units are linearized and cut into
+// `grid` equal contiguous ranges (stream-K), so every shape keeps all SMs
+// streaming weights.  A range covers whole tiles plus at most two partial
+// tiles; partial tiles are written as fp32 partials and the last CTA to
+// finish a tile sums them in CTA order (deterministic) before the epilogue.
+//
+// Warp roles (192 threads): warp 0 = TMA producer, warp 1 = MMA issuer,
+// warps 2..5 = epilogue (warp w reads TMEM lanes 32*(w%4)..+31).
+#pragma once
+
+#include "common.cuh"
+#include "../../include/dtree_b200.h"
+
+namespace dtree {
+
+enum Epi : int {
+  kEpiStore = 0,     // out[t*ldo + n] = bf16(acc)
+  kEpiResidual = 1,  // resid[t*ldo + n] = bf16(resid + bf16(acc)); optional capture copy
+  kEpiSwiglu = 2,    // rows g(64) | u(64) per tile -> act[t*ldo + j] = silu(g)*u
+  kEpiQkv = 3,       // q/k RMSNorm + RoPE -> q buffer / K cache; v -> V cache
+  kEpiArgmax = 4,    // per-row argmax over n (LM head), ties -> smallest n
+};
+
+struct GemmParams {
+  int n_out;   // rows of W
+  int kb;      // K / 64
+  int m_tiles; // ceil(n_out / 128)
+  int n_rows;  // valid tree rows (<= TPAD)
+  int grid;    // CTAs (stream-K ranges)
+  float* ws;            // [grid][2][TPAD][128] fp32 partial tiles
+  uint32_t* tile_cnt;   // [m_tiles] arrival counters (zero between launches)
+  // store / residual / swiglu
+  __nv_bfloat16* out;
+  int ldo;
+  __nv_bfloat16* capture;  // residual copy for verifier_hidden (nullable)
+  int ldc;
+  // qkv
+  __nv_bfloat16* q_out;
+  int ldq;
+  __nv_bfloat16* k_cache;  // this layer's K planes [n_kv_heads][kv_cap][head_dim]
+  __nv_bfloat16* v_cache;
+  int kv_cap, head_dim, n_q_heads, n_kv_heads;
+  const __nv_bfloat16* q_norm;
+  const __nv_bfloat16* k_norm;
+  float eps;
+  float rope_log2_theta;
+  const int32_t* positions;
+  const dtree_step_state* state;
+  // argmax
+  int vocab;
+  unsigned long long* argmax_keys;  // [TPAD], zero between launches
+  uint32_t* done_cnt;               // zero between launches
+  int32_t* argmax_out;              // [n_rows]
+};
+
+constexpr int kGemmThreads = 192;
+constexpr int kWTileBytes = 128 * 64 * 2;
+
+template <int TPAD, int EPI>
+struct GemmCfg {
+  static constexpr int kXBytes = TPAD * 64 * 2;
+  static constexpr int kStageBytes = kWTileBytes + kXBytes;
+  static constexpr int kXchBytes = (EPI == kEpiQkv || EPI == kEpiSwiglu) ? 128 * TPAD * 4 : 0;
+  static constexpr int kRedBytes = (EPI == kEpiQkv) ? 4 * TPAD * 4 : (EPI == kEpiArgmax ? 4 * TPAD * 8 + TPAD * 8 : 0);
+  // keep a CTA within ~half an SM's shared memory so the next kernel's CTA
+  // (launched early by PDL) can be resident and prefetch its weights
+  static constexpr int kBudget = 110 * 1024;
+  static constexpr int kFixed = 1024 /*align*/ + 256 /*barriers*/ + kXchBytes + kRedBytes;
+  static constexpr int kStagesRaw = (kBudget - kFixed) / kStageBytes;
+  static constexpr int kStages = kStagesRaw < 2 ? 2 : (kStagesRaw > 8 ? 8 : kStagesRaw);
+  static constexpr int kSmem = kFixed + kStages * kStageBytes;
+  static constexpr int kTmemCols = (2 * TPAD <= 32) ? 32 : (2 * TPAD <= 64 ? 64 : (2 * TPAD <= 128 ? 128 : 256));
+  static constexpr uint32_t kIdesc = idesc_bf16_f32(128, TPAD);
+};
+
+// first unit of CTA c (floor(c * U / G))
+__device__ __forceinline__ long long sk_u0(int c, long long U, int G) { return (static_cast<long long>(c) * U) / G; }
+// CTA containing unit u
+__device__ __forceinline__ int sk_cta_of(long long u, long long U, int G) {
+  return static_cast<int>(((u + 1) * G - 1) / U);
+}
+
+__device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+
+template <int TPAD, int EPI>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    gemm_streamk_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_x,
+                        GemmParams p) {
+  using C = GemmCfg<TPAD, EPI>;
+  constexpr int S = C::kStages;
+  pdl_trigger();
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* stage_base = smem;
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + S * C::kStageBytes);
+  uint64_t* empty_bar = full_bar + S;
+  uint64_t* tfull_bar = empty_bar + S;
+  uint64_t* tempty_bar = tfull_bar + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty_bar + 2);
+  int* s_flag = reinterpret_cast<int*>(tmem_slot + 1);
+  float* xch = reinterpret_cast<float*>(smem + S * C::kStageBytes + 256);
+  uint8_t* red_raw = smem + S * C::kStageBytes + 256 + C::kXchBytes;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int G = p.grid;
+  const long long U = static_cast<long long>(p.m_tiles) * p.kb;
+  const int cta = blockIdx.x;
+  const long long u0 = sk_u0(cta, U, G), u1 = sk_u0(cta + 1, U, G);
+  const int n_units = static_cast<int>(u1 - u0);
+
+  if (warp == 0) {
+    if (lane == 0) {
+      for (int s = 0; s < S; ++s) {
+        mbar_init(&full_bar[s], 1);
+        mbar_init(&empty_bar[s], 1);
+      }
+      for (int b = 0; b < 2; ++b) {
+        mbar_init(&tfull_bar[b], 1);
+        mbar_init(&tempty_bar[b], 4);
+      }
+      fence_barrier_init();
+      tma_prefetch_desc(&tmap_w);
+      tma_prefetch_desc(&tmap_x);
+    }
+    __syncwarp();
+    tmem_alloc(tmem_slot, C::kTmemCols);
+    tmem_relinquish();
+  }
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      const uint64_t pol_w = l2_policy_evict_first();
+      const uint64_t pol_x = l2_policy_evict_last();
+      const int pre = n_units < S ? n_units : S;
+      // weights do not depend on the upstream kernel: start streaming now
+      for (int i = 0; i < pre; ++i) {
+        const long long u = u0 + i;
+        const int tile = static_cast<int>(u / p.kb), kblk = static_cast<int>(u % p.kb);
+        mbar_arrive_expect_tx(&full_bar[i], C::kStageBytes);
+        tma_load_2d(stage_base + i * C::kStageBytes, &tmap_w, &full_bar[i], kblk * 64, tile * 128, pol_w);
+      }
+      pdl_wait();
+      for (int i = 0; i < pre; ++i) {
+        const int kblk = static_cast<int>((u0 + i) % p.kb);
+        tma_load_2d(stage_base + i * C::kStageBytes + kWTileBytes, &tmap_x, &full_bar[i], kblk * 64, 0, pol_x);
+      }
+      bool ok = true;
+      for (int i = pre; i < n_units && ok; ++i) {
+        const int s = i % S;
+        const uint32_t ph = static_cast<uint32_t>(i / S) & 1u;
+        ok = mbar_wait(&empty_bar[s], ph ^ 1u, 1);
+        if (!ok) break;
+        const long long u = u0 + i;
+        const int tile = static_cast<int>(u / p.kb), kblk = static_cast<int>(u % p.kb);
+        mbar_arrive_expect_tx(&full_bar[s], C::kStageBytes);
+        uint8_t* st = stage_base + s * C::kStageBytes;
+        tma_load_2d(st, &tmap_w, &full_bar[s], kblk * 64, tile * 128, pol_w);
+        tma_load_2d(st + kWTileBytes, &tmap_x, &full_bar[s], kblk * 64, 0, pol_x);
+      }
+      // drain: every issued load must land before the CTA can retire
+      const int first_undrained = n_units > S ? n_units - S : 0;
+      for (int i = first_undrained; i < n_units; ++i)
+        mbar_wait(&full_bar[i % S], static_cast<uint32_t>(i / S) & 1u, 2);
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      long long u = u0;
+      int i = 0, seg = 0;
+      bool ok = true;
+      while (u < u1) {
+        const int kblk0 = static_cast<int>(u % p.kb);
+        const int len = static_cast<int>(min(static_cast<long long>(p.kb - kblk0), u1 - u));
+        const int b = seg & 1;
+        const int use = seg >> 1;
+        if (use >= 1 && ok) ok = mbar_wait(&tempty_bar[b], static_cast<uint32_t>(use - 1) & 1u, 3);
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(b * TPAD);
+        for (int j = 0; j < len; ++j, ++i) {
+          const int s = i % S;
+          const uint32_t ph = static_cast<uint32_t>(i / S) & 1u;
+          if (ok) ok = mbar_wait(&full_bar[s], ph, 4);
+          tc_fence_after();
+          if (ok) {
+            const uint32_t a_addr = smem_u32(stage_base + s * C::kStageBytes);
+            const uint32_t b_addr = a_addr + kWTileBytes;
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk) {
+              umma_bf16(d_tmem, sw128_kmajor_desc(a_addr + kk * 32), sw128_kmajor_desc(b_addr + kk * 32), C::kIdesc,
+                        (j > 0 || kk > 0) ? 1u : 0u);
+            }
+          }
+          umma_commit(&empty_bar[s]);
+        }
+        umma_commit(&tfull_bar[b]);
+        u += len;
+        ++seg;
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int q = warp & 3;            // TMEM lane quarter
+    const int row = q * 32 + lane;     // row of the 128-row tile
+    const int et = threadIdx.x - 64;   // 0..127 epilogue thread id
+    pdl_wait();
+    float* red = reinterpret_cast<float*>(red_raw);
+    unsigned long long* s_best = reinterpret_cast<unsigned long long*>(red_raw + 4 * TPAD * 8);
+    if constexpr (EPI == kEpiArgmax) {
+      for (int t = et; t < TPAD; t += 128) s_best[t] = 0ull;
+      epi_bar();
+    }
+    int start = 0;
+    if constexpr (EPI == kEpiQkv) start = p.state ? p.state->start : 0;
+    long long u = u0;
+    int seg = 0;
+    const int first_tile = static_cast<int>(u0 / p.kb);
+    while (u < u1) {
+      const int tile = static_cast<int>(u / p.kb);
+      const int kblk0 = static_cast<int>(u % p.kb);
+      const int len = static_cast<int>(min(static_cast<long long>(p.kb - kblk0), u1 - u));
+      const bool full = (kblk0 == 0) && (len == p.kb);
+      const int b = seg & 1;
+      const int use = seg >> 1;
+      mbar_wait(&tfull_bar[b], static_cast<uint32_t>(use) & 1u, 5);
+      tc_fence_after();
+      float acc[TPAD];
+      const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(b * TPAD);
+#pragma unroll
+      for (int c = 0; c < TPAD; c += 8) {
+        uint32_t r[8];
+        tmem_ld_x8(taddr + c, r);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[c + j] = __uint_as_float(r[j]);
+      }
+      tmem_wait_ld();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty_bar[b]);
+
+      bool have = true;
+      if (!full) {
+        const int which = (tile == first_tile) ? 0 : 1;
+        float* slot = p.ws + (static_cast<size_t>(cta) * 2 + which) * TPAD * 128;
+#pragma unroll
+        for (int t = 0; t < TPAD; ++t) slot[t * 128 + row] = acc[t];
+        __threadfence();
+        epi_bar();
+        const long long tu0 = static_cast<long long>(tile) * p.kb, tu1 = tu0 + p.kb - 1;
+        const int c_first = sk_cta_of(tu0, U, G), c_last = sk_cta_of(tu1, U, G);
+        if (et == 0) {
+          const uint32_t prev = atomicAdd(&p.tile_cnt[tile], 1u);
+          *s_flag = (prev == static_cast<uint32_t>(c_last - c_first)) ? 1 : 0;
+        }
+        epi_bar();
+        have = (*s_flag != 0);
+        if (have) {
+          __threadfence();
+#pragma unroll
+          for (int t = 0; t < TPAD; ++t) acc[t] = 0.0f;
+          for (int c = c_first; c <= c_last; ++c) {
+            const int w2 = (tile == static_cast<int>(sk_u0(c, U, G) / p.kb)) ? 0 : 1;
+            const float* sl = p.ws + (static_cast<size_t>(c) * 2 + w2) * TPAD * 128;
+#pragma unroll
+            for (int t = 0; t < TPAD; ++t) acc[t] += __ldcg(&sl[t * 128 + row]);
+          }
+          if (et == 0) p.tile_cnt[tile] = 0u;
+        }
+        epi_bar();
+      }
+      if (have) {
+        const int n = tile * 128 + row;
+        if constexpr (EPI == kEpiStore) {
+          if (n < p.n_out) {
+#pragma unroll
+            for (int t = 0; t < TPAD; ++t)
+              p.out[static_cast<size_t>(t) * p.ldo + n] = __float2bfloat16_rn(t < p.n_rows ? acc[t] : 0.0f);
+          }
+        } else if constexpr (EPI == kEpiResidual) {
+          if (n < p.n_out) {
+#pragma unroll
+            for (int t = 0; t < TPAD; ++t) {
+              __nv_bfloat16* hp = p.out + static_cast<size_t>(t) * p.ldo + n;
+              if (t < p.n_rows) {
+                const float y = bf16_round(acc[t]);
+                const __nv_bfloat16 hn = __float2bfloat16_rn(__bfloat162float(*hp) + y);
+                *hp = hn;
+                if (p.capture) p.capture[static_cast<size_t>(t) * p.ldc + n] = hn;
+              } else {
+                *hp = __float2bfloat16_rn(0.0f);
+              }
+            }
+          }
+        } else if constexpr (EPI == kEpiSwiglu) {
+          if (row >= 64) {
+#pragma unroll
+            for (int t = 0; t < TPAD; ++t) xch[(row - 64) * TPAD + t] = acc[t];
+          }
+          epi_bar();
+          if (row < 64) {
+            const int j = tile * 64 + row;
+#pragma unroll
+            for (int t = 0; t < TPAD; ++t) {
+              const float g = bf16_round(acc[t]);
+              const float uu = bf16_round(xch[row * TPAD + t]);
+              const float sg = bf16_round(1.0f / (1.0f + expf(-g)));
+              const float sl = bf16_round(g * sg);
+              p.out[static_cast<size_t>(t) * p.ldo + j] = __float2bfloat16_rn(t < p.n_rows ? sl * uu : 0.0f);
+            }
+          }
+          epi_bar();
+        } else if constexpr (EPI == kEpiQkv) {
+          const int hd = p.head_dim;
+          const int gh = n / hd;   // global head index across q | k | v
+          const int d = n % hd;
+          if (gh >= p.n_q_heads + p.n_kv_heads) {
+            // v head: straight into the V cache
+            const int kvh = gh - p.n_q_heads - p.n_kv_heads;
+#pragma unroll
+            for (int t = 0; t < TPAD; ++t) {
+              if (t < p.n_rows) {
+                const int slot = start + t;
+                if (slot < p.kv_cap)
+                  p.v_cache[(static_cast<size_t>(kvh) * p.kv_cap + slot) * hd + d] = __float2bfloat16_rn(acc[t]);
+                else
+                  dev_error(0x2001u);
+              }
+            }
+          } else {
+            // RMSNorm over the head (hd rows spread over hd/32 warps), then RoPE
+#pragma unroll
+            for (int t = 0; t < TPAD; ++t) {
+              acc[t] = bf16_round(acc[t]);
+              float v = acc[t] * acc[t];
+              for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+              if (lane == 0) red[q * TPAD + t] = v;
+            }
+            epi_bar();
+            const int wph = hd / 32;  // warps per head
+            const int w0 = (q / wph) * wph;
+            const float nw = __bfloat162float((gh < p.n_q_heads ? p.q_norm : p.k_norm)[d]);
+#pragma unroll
+            for (int t = 0; t < TPAD; ++t) {
+              float ss = 0.0f;
+              for (int w = w0; w < w0 + wph; ++w) ss += red[w * TPAD + t];
+              const float rms = rsqrtf(ss / static_cast<float>(hd) + p.eps);
+              acc[t] = bf16_round(acc[t] * rms * nw);
+              xch[row * TPAD + t] = acc[t];
+            }
+            epi_bar();
+            const int half = hd / 2;
+            const int i_f = d % half;
+            const float inv_freq = exp2f(-(2.0f * static_cast<float>(i_f) / static_cast<float>(hd)) * p.rope_log2_theta);
+            const int partner = (d < half) ? row + half : row - half;
+            const bool is_q = gh < p.n_q_heads;
+            const int kvh = gh - p.n_q_heads;
+#pragma unroll
+            for (int t = 0; t < TPAD; ++t) {
+              float outv = 0.0f;
+              if (t < p.n_rows) {
+                const float pos = static_cast<float>(p.positions[t]);
+                float sn, cs;
+                sincosf(pos * inv_freq, &sn, &cs);
+                const float y = acc[t], yp = xch[partner * TPAD + t];
+                outv = (d < half) ? (y * cs - yp * sn) : (y * cs + yp * sn);
+              }
+              if (is_q) {
+                p.q_out[static_cast<size_t>(t) * p.ldq + gh * hd + d] = __float2bfloat16_rn(outv);
+              } else if (t < p.n_rows) {
+                const int slot = start + t;
+                if (slot < p.kv_cap)
+                  p.k_cache[(static_cast<size_t>(kvh) * p.kv_cap + slot) * hd + d] = __float2bfloat16_rn(outv);
+                else
+                  dev_error(0x2001u);
+              }
+            }
+            epi_bar();
+          }
+        } else if constexpr (EPI == kEpiArgmax) {
+          // per column (tree row t): max over this tile's 128 vocab rows
+          const bool valid = n < p.vocab;
+#pragma unroll
+          for (int t = 0; t < TPAD; ++t) {
+            unsigned long long key = 0ull;
+            if (valid) {
+              const float v = bf16_round(acc[t]);
+              key = (static_cast<unsigned long long>(float_order_key(v)) << 32) |
+                    static_cast<unsigned long long>(0xFFFFFFFFu - static_cast<uint32_t>(n));
+            }
+            for (int o = 16; o > 0; o >>= 1) {
+              const unsigned long long ok2 = __shfl_xor_sync(0xffffffffu, key, o);
+              key = ok2 > key ? ok2 : key;
+            }
+            if (lane == 0) reinterpret_cast<unsigned long long*>(red_raw)[q * TPAD + t] = key;
+          }
+          epi_bar();
+          for (int t = et; t < TPAD; t += 128) {
+            const unsigned long long* rk = reinterpret_cast<const unsigned long long*>(red_raw);
+            unsigned long long bk = s_best[t];
+            for (int w = 0; w < 4; ++w) bk = rk[w * TPAD + t] > bk ? rk[w * TPAD + t] : bk;
+            s_best[t] = bk;
+          }
+          epi_bar();
+        }
+      }
+      u += len;
+      ++seg;
+    }
+    if constexpr (EPI == kEpiArgmax) {
+      for (int t = et; t < p.n_rows; t += 128)
+        if (s_best[t]) atomicMax(&p.argmax_keys[t], s_best[t]);
+      __threadfence();
+      epi_bar();
+      if (et == 0) {
+        const uint32_t prev = atomicAdd(p.done_cnt, 1u);
+        *s_flag = (prev == static_cast<uint32_t>(G - 1)) ? 1 : 0;
+      }
+      epi_bar();
+      if (*s_flag) {
+        __threadfence();
+        for (int t = et; t < TPAD; t += 128) {
+          const unsigned long long k = atomicExch(&p.argmax_keys[t], 0ull);
+          if (t < p.n_rows) p.argmax_out[t] = static_cast<int32_t>(0xFFFFFFFFu - static_cast<uint32_t>(k & 0xFFFFFFFFull));
+        }
+        if (et == 0) *p.done_cnt = 0u;
+      }
+    }
+  }
+  __syncthreads();
+  if (warp == 0) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem_base, C::kTmemCols);
+  }
+}
+
+// ------------------------------------------------------------ host launcher
+struct GemmPlan {
+  CUtensorMap tmap_w;
+  CUtensorMap tmap_x;
+  GemmParams p;
+  int t_pad;
+  int epi;
+};
+
+size_t gemm_ws_bytes(int t_pad, int grid);  // fp32 partials
+int gemm_plan(GemmPlan* plan, const void* w, int n_out, int k, const void* x, int t_pad, int x_row_stride_elems,
+              int epi, int grid);
+int gemm_bind_ws(GemmPlan* plan, void* ws, size_t ws_bytes);
+int gemm_launch(const GemmPlan& plan, cudaStream_t stream);
+
+}  // namespace dtree

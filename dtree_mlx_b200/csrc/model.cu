@@ -1,0 +1,256 @@
+// Qwen3 tree-verify forward: the whole of
+// Qwen3TargetAdapter.forward_tree_with_hidden_states (adapters.py:568-597)
+// plus lm_head_argmax (adapters.py:114-118) as one launch sequence.
+//
+// Per layer (qwen3_tree.py:39-83):
+//   xn   = RMSNorm(h, input_norm)                       rmsnorm_kernel
+//   q,k,v= xn @ Wqkv^T; q/k RMSNorm + RoPE; k,v -> cache gemm<kEpiQkv>
+//   a    = softmax(q k^T / sqrt(d) + tree mask) v       tree_attn + combine
+//   h   += a @ Wo^T                                     gemm<kEpiResidual>
+//   xn   = RMSNorm(h, post_norm)                        rmsnorm_kernel
+//   act  = silu(xn Wg^T) * (xn Wu^T)                    gemm<kEpiSwiglu>
+//   h   += act @ Wd^T   (+ copy to verifier_hidden)     gemm<kEpiResidual>
+// then norm_out = RMSNorm(h, final_norm) and the fused LM-head argmax.
+#include <cmath>
+#include <vector>
+
+#include "attention.cuh"
+#include "gemm.cuh"
+
+namespace dtree {
+
+int rmsnorm_launch(const __nv_bfloat16* x, int ldx, const int32_t* tokens, const __nv_bfloat16* embed,
+                   __nv_bfloat16* h_out, const __nv_bfloat16* w, __nv_bfloat16* y, int H, int n_rows, int t_pad,
+                   float eps, cudaStream_t stream);
+
+constexpr int kAttnMaxSplits = 32;
+
+static int pad_rows(int n) {
+  if (n <= 16) return 16;
+  if (n <= 32) return 32;
+  if (n <= 64) return 64;
+  return 128;
+}
+static int tpad_index(int t) { return t == 16 ? 0 : t == 32 ? 1 : t == 64 ? 2 : 3; }
+
+struct PlanSet {
+  bool ready = false;
+  std::vector<GemmPlan> qkv, o, gu, down;
+  GemmPlan lm;
+};
+
+}  // namespace dtree
+
+struct dtree_qwen3_model {
+  dtree_qwen3_desc d;
+  std::vector<dtree_qwen3_layer> layers;
+  dtree::PlanSet plans[4];
+  void* gemm_ws = nullptr;
+  size_t gemm_ws_bytes = 0;
+  void* attn_ws = nullptr;
+  size_t attn_ws_bytes = 0;
+};
+
+namespace dtree {
+
+static size_t gemm_ws_need(const dtree_qwen3_desc& d) { return gemm_ws_bytes(pad_rows(d.t_cap), num_sms()); }
+static size_t attn_ws_need(const dtree_qwen3_desc& d) {
+  return attn_ws_bytes(d.n_heads, d.t_cap, d.head_dim, kAttnMaxSplits);
+}
+
+static int build_plans(dtree_qwen3_model* m, int t_pad) {
+  PlanSet& ps = m->plans[tpad_index(t_pad)];
+  if (ps.ready) return kOk;
+  const dtree_qwen3_desc& d = m->d;
+  const int qkv_rows = (d.n_heads + 2 * d.n_kv_heads) * d.head_dim;
+  const int qd = d.n_heads * d.head_dim;
+  ps.qkv.resize(d.layers);
+  ps.o.resize(d.layers);
+  ps.gu.resize(d.layers);
+  ps.down.resize(d.layers);
+  for (int l = 0; l < d.layers; ++l) {
+    const dtree_qwen3_layer& L = m->layers[l];
+    int rc;
+    if ((rc = gemm_plan(&ps.qkv[l], L.qkv, qkv_rows, d.hidden, d.xn, t_pad, d.hidden, kEpiQkv, 0))) return rc;
+    if ((rc = gemm_plan(&ps.o[l], L.o_proj, d.hidden, qd, d.attn, t_pad, qd, kEpiResidual, 0))) return rc;
+    if ((rc = gemm_plan(&ps.gu[l], L.gate_up, 2 * d.ffn, d.hidden, d.xn, t_pad, d.hidden, kEpiSwiglu, 0))) return rc;
+    if ((rc = gemm_plan(&ps.down[l], L.down, d.hidden, d.ffn, d.act, t_pad, d.ffn, kEpiResidual, 0))) return rc;
+    for (GemmPlan* g : {&ps.qkv[l], &ps.o[l], &ps.gu[l], &ps.down[l]})
+      if ((rc = gemm_bind_ws(g, m->gemm_ws, m->gemm_ws_bytes))) return rc;
+  }
+  int rc = gemm_plan(&ps.lm, d.embed, d.vocab, d.hidden, d.norm_out, t_pad, d.hidden, kEpiArgmax, 0);
+  if (rc) return rc;
+  if ((rc = gemm_bind_ws(&ps.lm, m->gemm_ws, m->gemm_ws_bytes))) return rc;
+  ps.ready = true;
+  return kOk;
+}
+
+}  // namespace dtree
+
+using namespace dtree;
+
+extern "C" int dtree_qwen3_buffer_bytes(const dtree_qwen3_desc* d, size_t out[9]) {
+  DTREE_CHECK_ARG(d && out, "null pointer");
+  DTREE_CHECK_ARG(d->t_cap > 0 && d->t_cap <= DTREE_MAX_TREE, "t_cap must be in [1, 128]");
+  const size_t tc = static_cast<size_t>(pad_rows(d->t_cap));
+  const size_t qd = static_cast<size_t>(d->n_heads) * d->head_dim;
+  out[0] = static_cast<size_t>(d->layers) * 2 * d->n_kv_heads * static_cast<size_t>(d->kv_capacity) * d->head_dim * 2;
+  out[1] = tc * d->hidden * 2;
+  out[2] = tc * d->hidden * 2;
+  out[3] = tc * qd * 2;
+  out[4] = tc * qd * 2;
+  out[5] = tc * d->ffn * 2;
+  out[6] = tc * d->hidden * 2;
+  out[7] = tc * d->hidden * (d->n_capture > 0 ? d->n_capture : 1) * 2;
+  out[8] = ((gemm_ws_need(*d) + 255) & ~static_cast<size_t>(255)) + attn_ws_need(*d);
+  return kOk;
+}
+
+extern "C" int dtree_qwen3_create(const dtree_qwen3_desc* desc, dtree_qwen3_model** out) {
+  DTREE_CHECK_ARG(desc && out, "null pointer");
+  const dtree_qwen3_desc& d = *desc;
+  DTREE_CHECK_ARG(d.hidden % 64 == 0 && d.ffn % 64 == 0, "hidden and ffn must be multiples of 64");
+  DTREE_CHECK_ARG(d.head_dim == 64 || d.head_dim == 128, "head_dim must be 64 or 128");
+  DTREE_CHECK_ARG(d.n_heads % d.n_kv_heads == 0, "n_heads must be a multiple of n_kv_heads");
+  DTREE_CHECK_ARG((d.n_heads * d.head_dim) % 128 == 0 && (d.n_kv_heads * d.head_dim) % 128 == 0,
+                  "q and kv projection widths must be multiples of 128");
+  DTREE_CHECK_ARG(d.t_cap > 0 && d.t_cap <= DTREE_MAX_TREE, "t_cap must be in [1, 128]");
+  DTREE_CHECK_ARG(d.n_capture >= 0 && d.n_capture <= 16, "n_capture must be in [0, 16]");
+  DTREE_CHECK_ARG(d.layer && d.embed && d.final_norm, "null weights");
+  DTREE_CHECK_ARG(d.kv_cache && d.h && d.xn && d.q && d.attn && d.act && d.norm_out && d.workspace,
+                  "null buffer");
+  DTREE_CHECK_ARG(d.n_capture == 0 || d.capture, "null capture buffer");
+  size_t need[9];
+  dtree_qwen3_buffer_bytes(desc, need);
+  DTREE_CHECK_ARG(d.workspace_bytes >= need[8], "workspace too small");
+  for (int c = 0; c < d.n_capture; ++c)
+    DTREE_CHECK_ARG(d.capture_layers[c] >= 0 && d.capture_layers[c] < d.layers, "capture layer out of range");
+  auto* m = new dtree_qwen3_model();
+  m->d = d;
+  m->layers.assign(d.layer, d.layer + d.layers);
+  m->d.layer = m->layers.data();
+  m->gemm_ws = d.workspace;
+  m->gemm_ws_bytes = gemm_ws_need(d);
+  m->attn_ws = static_cast<char*>(d.workspace) + ((m->gemm_ws_bytes + 255) & ~static_cast<size_t>(255));
+  m->attn_ws_bytes = attn_ws_need(d);
+  *out = m;
+  return kOk;
+}
+
+extern "C" int dtree_qwen3_destroy(dtree_qwen3_model* m) {
+  delete m;
+  return kOk;
+}
+
+extern "C" int dtree_qwen3_forward_tree(dtree_qwen3_model* m, const int32_t* tree_tokens, const int32_t* positions,
+                                        const uint64_t* anc_mask, int n_nodes, const dtree_step_state* state,
+                                        int32_t* posterior, void* stream_) {
+  DTREE_CHECK_ARG(m && tree_tokens && positions && anc_mask && state, "null pointer");
+  const dtree_qwen3_desc& d = m->d;
+  DTREE_CHECK_ARG(n_nodes > 0 && n_nodes <= d.t_cap, "n_nodes must be in [1, t_cap]");
+  cudaStream_t st = static_cast<cudaStream_t>(stream_);
+  const int t_pad = pad_rows(n_nodes);
+  int rc = build_plans(m, t_pad);
+  if (rc) return rc;
+  PlanSet& ps = m->plans[tpad_index(t_pad)];
+  auto bf = [](const void* p) { return static_cast<const __nv_bfloat16*>(p); };
+  auto bw = [](void* p) { return static_cast<__nv_bfloat16*>(p); };
+  const size_t plane = static_cast<size_t>(d.n_kv_heads) * d.kv_capacity * d.head_dim;
+  const int qd = d.n_heads * d.head_dim;
+  const float log2_theta = std::log2(d.rope_theta);
+  const int splits = std::min(kAttnMaxSplits, attn_default_splits(d.n_kv_heads, d.n_heads, n_nodes));
+
+  // embedding gather + first input norm
+  if ((rc = rmsnorm_launch(nullptr, 0, tree_tokens, bf(d.embed), bw(d.h), bf(m->layers[0].input_norm), bw(d.xn),
+                           d.hidden, n_nodes, t_pad, d.rms_eps, st)))
+    return rc;
+  for (int l = 0; l < d.layers; ++l) {
+    const dtree_qwen3_layer& L = m->layers[l];
+    __nv_bfloat16* kc = bw(d.kv_cache) + (static_cast<size_t>(l) * 2 + 0) * plane;
+    __nv_bfloat16* vc = bw(d.kv_cache) + (static_cast<size_t>(l) * 2 + 1) * plane;
+    if (l > 0) {
+      if ((rc = rmsnorm_launch(bf(d.h), d.hidden, nullptr, nullptr, nullptr, bf(L.input_norm), bw(d.xn), d.hidden,
+                               n_nodes, t_pad, d.rms_eps, st)))
+        return rc;
+    }
+    {  // q | k | v projection with q/k norm + RoPE, K/V into the cache
+      GemmPlan g = ps.qkv[l];
+      g.p.n_rows = n_nodes;
+      g.p.q_out = bw(d.q);
+      g.p.ldq = qd;
+      g.p.k_cache = kc;
+      g.p.v_cache = vc;
+      g.p.kv_cap = d.kv_capacity;
+      g.p.head_dim = d.head_dim;
+      g.p.n_q_heads = d.n_heads;
+      g.p.n_kv_heads = d.n_kv_heads;
+      g.p.q_norm = bf(L.q_norm);
+      g.p.k_norm = bf(L.k_norm);
+      g.p.eps = d.rms_eps;
+      g.p.rope_log2_theta = log2_theta;
+      g.p.positions = positions;
+      g.p.state = state;
+      if ((rc = gemm_launch(g, st))) return rc;
+    }
+    {  // tree attention
+      AttnParams a{};
+      a.q = bf(d.q);
+      a.ldq = qd;
+      a.k = kc;
+      a.v = vc;
+      a.cap = d.kv_capacity;
+      a.n_q_heads = d.n_heads;
+      a.n_kv_heads = d.n_kv_heads;
+      a.n_nodes = n_nodes;
+      a.state = state;
+      a.anc = anc_mask;
+      a.scale_log2 = static_cast<float>(1.4426950408889634 / std::sqrt(static_cast<double>(d.head_dim)));
+      a.splits = splits;
+      a.out = bw(d.attn);
+      if ((rc = attn_launch(a, d.head_dim, m->attn_ws, m->attn_ws_bytes, st))) return rc;
+    }
+    {  // o_proj + residual
+      GemmPlan g = ps.o[l];
+      g.p.n_rows = n_nodes;
+      g.p.out = bw(d.h);
+      g.p.ldo = d.hidden;
+      g.p.capture = nullptr;
+      if ((rc = gemm_launch(g, st))) return rc;
+    }
+    if ((rc = rmsnorm_launch(bf(d.h), d.hidden, nullptr, nullptr, nullptr, bf(L.post_norm), bw(d.xn), d.hidden,
+                             n_nodes, t_pad, d.rms_eps, st)))
+      return rc;
+    {  // gate | up + SwiGLU
+      GemmPlan g = ps.gu[l];
+      g.p.n_rows = n_nodes;
+      g.p.out = bw(d.act);
+      g.p.ldo = d.ffn;
+      if ((rc = gemm_launch(g, st))) return rc;
+    }
+    {  // down + residual (+ verifier_hidden capture)
+      GemmPlan g = ps.down[l];
+      g.p.n_rows = n_nodes;
+      g.p.out = bw(d.h);
+      g.p.ldo = d.hidden;
+      g.p.capture = nullptr;
+      for (int c = 0; c < d.n_capture; ++c) {
+        if (d.capture_layers[c] == l) {
+          g.p.capture = bw(d.capture) + static_cast<size_t>(c) * d.hidden;
+          g.p.ldc = d.hidden * d.n_capture;
+        }
+      }
+      if ((rc = gemm_launch(g, st))) return rc;
+    }
+  }
+  if ((rc = rmsnorm_launch(bf(d.h), d.hidden, nullptr, nullptr, nullptr, bf(d.final_norm), bw(d.norm_out), d.hidden,
+                           n_nodes, t_pad, d.rms_eps, st)))
+    return rc;
+  if (posterior) {
+    GemmPlan g = ps.lm;
+    g.p.n_rows = n_nodes;
+    g.p.vocab = d.vocab;
+    g.p.argmax_out = posterior;
+    if ((rc = gemm_launch(g, st))) return rc;
+  }
+  return kOk;
+}

@@ -1,0 +1,756 @@
+// Tree construction, acceptance walk, KV compaction and decode-state kernels.
+//
+// Reference semantics: dtree_mlx/dtree_runtime.py:82-208 (build / compile /
+// follow), adapters.py:635-668 (compaction), runtime.py:476-490 (DFlash
+// chain block).  All state lives on the device so a decode step needs no
+// host round trip.
+#include "common.cuh"
+#include "../../include/dtree_b200.h"
+
+namespace dtree {
+
+constexpr int kTopkThreads = 256;
+constexpr int kMaxBudget = DTREE_MAX_TREE - 1;  // 127 nodes + root
+constexpr int kMaxRows = 64;
+constexpr int kMaxK = 128;                       // k = min(budget, vocab) <= 127
+
+// ============================================================ planted logits
+__host__ __device__ __forceinline__ void philox4x32_10(uint32_t c[4], uint32_t k0, uint32_t k1) {
+  for (int r = 0; r < 10; ++r) {
+    if (r > 0) {
+      k0 += 0x9E3779B9u;
+      k1 += 0xBB67AE85u;
+    }
+    const uint64_t p0 = static_cast<uint64_t>(0xD2511F53u) * c[0];
+    const uint64_t p1 = static_cast<uint64_t>(0xCD9E8D57u) * c[2];
+    const uint32_t hi0 = static_cast<uint32_t>(p0 >> 32), lo0 = static_cast<uint32_t>(p0);
+    const uint32_t hi1 = static_cast<uint32_t>(p1 >> 32), lo1 = static_cast<uint32_t>(p1);
+    const uint32_t n0 = hi1 ^ c[1] ^ k0, n2 = hi0 ^ c[3] ^ k1;
+    c[0] = n0;
+    c[1] = lo1;
+    c[2] = n2;
+    c[3] = lo0;
+  }
+}
+
+constexpr uint32_t kNoiseTag = 0xD1CEu;
+constexpr uint32_t kPlantTag = 0xB1A5u;
+constexpr uint32_t kKeyHi = 0x5EED0001u;
+
+__device__ __forceinline__ float u24(uint32_t x) { return __fmul_rn(static_cast<float>(x >> 8), 5.9604644775390625e-08f); }
+
+// grid (ceil(vocab/256), rows), block 256
+__global__ void plant_draft_logits_kernel(float* __restrict__ logits, int rows, int vocab, uint32_t seed,
+                                          const dtree_step_state* __restrict__ state,
+                                          const int32_t* __restrict__ cont, int cont_len, float p_correct) {
+  pdl_trigger();
+  __shared__ int s_tok;
+  const int r = blockIdx.y;
+  pdl_wait();
+  const int step = state->step;
+  const int start = state->start;
+  if (threadIdx.x == 0) {
+    uint32_t c[4] = {0xFFFFFFFFu, static_cast<uint32_t>(r), static_cast<uint32_t>(step), kPlantTag};
+    philox4x32_10(c, seed, kKeyHi);
+    const bool take = u24(c[0]) < p_correct;
+    int tok = static_cast<int>(c[1] % static_cast<uint32_t>(vocab));
+    const int pos = start + r + 1;
+    if (take && pos < cont_len) tok = cont[pos];
+    s_tok = tok;
+  }
+  __syncthreads();
+  const int v = blockIdx.x * blockDim.x + threadIdx.x;
+  if (v >= vocab) return;
+  float acc = 0.0f;
+#pragma unroll
+  for (int j = 0; j < 3; ++j) {
+    uint32_t c[4] = {static_cast<uint32_t>(v), static_cast<uint32_t>(r) | (static_cast<uint32_t>(j) << 16),
+                     static_cast<uint32_t>(step), kNoiseTag};
+    philox4x32_10(c, seed, kKeyHi);
+#pragma unroll
+    for (int l = 0; l < 4; ++l) acc = __fadd_rn(acc, u24(c[l]));
+  }
+  float x = __fsub_rn(acc, 6.0f);
+  if (v == s_tok) x = __fadd_rn(x, 8.0f);
+  logits[static_cast<size_t>(r) * vocab + v] = x;
+}
+
+// ============================================================ top-k + LSE
+// Workspace layout (per row r, split s):
+//   cand_val [rows][splits][kMaxK] f32, cand_id [rows][splits][kMaxK] i32
+//   part_m [rows][splits], part_s [rows][splits]
+//   top_id [rows][kMaxK] i32, top_lp [rows][kMaxK] f32
+//   counters [rows] u32
+struct TreeWs {
+  float* cand_val;
+  int32_t* cand_id;
+  float* part_m;
+  float* part_s;
+  int32_t* top_id;
+  float* top_lp;
+  uint32_t* counters;
+};
+
+__host__ __device__ inline size_t align256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
+
+__host__ __device__ inline size_t tree_ws_layout(int rows, int splits, TreeWs* ws, char* base) {
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    size_t o = off;
+    off = align256(off + bytes);
+    return o;
+  };
+  const size_t rs = static_cast<size_t>(rows) * splits;
+  size_t o_cv = take(rs * kMaxK * 4), o_ci = take(rs * kMaxK * 4), o_pm = take(rs * 4), o_ps = take(rs * 4);
+  size_t o_ti = take(static_cast<size_t>(rows) * kMaxK * 4), o_tl = take(static_cast<size_t>(rows) * kMaxK * 4);
+  size_t o_ct = take(static_cast<size_t>(rows) * 4);
+  if (ws && base) {
+    ws->cand_val = reinterpret_cast<float*>(base + o_cv);
+    ws->cand_id = reinterpret_cast<int32_t*>(base + o_ci);
+    ws->part_m = reinterpret_cast<float*>(base + o_pm);
+    ws->part_s = reinterpret_cast<float*>(base + o_ps);
+    ws->top_id = reinterpret_cast<int32_t*>(base + o_ti);
+    ws->top_lp = reinterpret_cast<float*>(base + o_tl);
+    ws->counters = reinterpret_cast<uint32_t*>(base + o_ct);
+  }
+  return off;
+}
+
+__device__ __forceinline__ float block_reduce_max(float v, float* red) {
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  __syncthreads();
+  if (l == 0) red[w] = v;
+  __syncthreads();
+  float r = (l < (blockDim.x >> 5)) ? red[l] : -INFINITY;
+  for (int o = 16; o > 0; o >>= 1) r = fmaxf(r, __shfl_xor_sync(0xffffffffu, r, o));
+  return r;
+}
+__device__ __forceinline__ float block_reduce_sum(float v, float* red) {
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  __syncthreads();
+  if (l == 0) red[w] = v;
+  __syncthreads();
+  float r = (l < (blockDim.x >> 5)) ? red[l] : 0.0f;
+  for (int o = 16; o > 0; o >>= 1) r += __shfl_xor_sync(0xffffffffu, r, o);
+  return r;
+}
+
+// (value desc, id asc) total order
+__device__ __forceinline__ bool cand_before(float va, int ia, float vb, int ib) {
+  return (va > vb) || (va == vb && ia < ib);
+}
+
+// Sorts n (<= kMaxK * splits, held in smem) candidates by rank counting and
+// writes the first k into out_val/out_id (smem or global).
+__device__ void rank_select(const float* val, const int32_t* id, int n, int k, float* out_val, int32_t* out_id) {
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    const float vi = val[i];
+    const int ii = id[i];
+    int rank = 0;
+    for (int j = 0; j < n; ++j) rank += cand_before(val[j], id[j], vi, ii) ? 1 : 0;
+    if (rank < k) {
+      out_val[rank] = vi;
+      out_id[rank] = ii;
+    }
+  }
+}
+
+// grid (splits, rows), block 256, dynamic smem = chunk*4 + candidates
+__global__ void __launch_bounds__(kTopkThreads) topk_lse_kernel(const float* __restrict__ logits, int rows,
+                                                                 int vocab, int k, int splits, int chunk,
+                                                                 TreeWs ws) {
+  pdl_trigger();
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  float* s_x = reinterpret_cast<float*>(smem_raw);                   // [chunk]
+  float* s_cv = s_x + chunk;                                          // [splits*kMaxK] merge area
+  int32_t* s_ci = reinterpret_cast<int32_t*>(s_cv + splits * kMaxK);  // [splits*kMaxK]
+  __shared__ uint32_t s_hist[256];
+  __shared__ float s_red[32];
+  __shared__ uint32_t s_prefix, s_mask_bits, s_remaining;
+  __shared__ int s_count_gt, s_count_eq_taken;
+  __shared__ bool s_last;
+
+  const int r = blockIdx.y, s = blockIdx.x;
+  const int c0 = s * chunk;
+  const int c1 = min(vocab, c0 + chunk);
+  const int n = max(0, c1 - c0);
+  pdl_wait();
+  const float* row = logits + static_cast<size_t>(r) * vocab;
+  float lmax = -INFINITY;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    const float x = row[c0 + i];
+    s_x[i] = x;
+    lmax = fmaxf(lmax, x);
+  }
+  const float m = block_reduce_max(lmax, s_red);
+  float lsum = 0.0f;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) lsum += __expf(s_x[i] - m);
+  const float ssum = block_reduce_sum(lsum, s_red);
+
+  // radix select of the kk-th largest order key in the chunk (kk = min(k, n))
+  const int kk = min(k, n);
+  if (threadIdx.x == 0) {
+    s_prefix = 0;
+    s_mask_bits = 0;
+    s_remaining = static_cast<uint32_t>(kk);
+  }
+  __syncthreads();
+  for (int shift = 24; shift >= 0 && kk > 0; shift -= 8) {
+    for (int i = threadIdx.x; i < 256; i += blockDim.x) s_hist[i] = 0;
+    __syncthreads();
+    const uint32_t prefix = s_prefix, mask = s_mask_bits;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+      const uint32_t key = float_order_key(s_x[i]);
+      if ((key & mask) == prefix) atomicAdd(&s_hist[(key >> shift) & 0xFFu], 1u);
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      uint32_t rem = s_remaining;
+      int b = 255;
+      for (; b > 0; --b) {
+        if (s_hist[b] >= rem) break;
+        rem -= s_hist[b];
+      }
+      s_prefix = prefix | (static_cast<uint32_t>(b) << shift);
+      s_mask_bits = mask | (0xFFu << shift);
+      s_remaining = rem;
+    }
+    __syncthreads();
+  }
+  // threshold key tau = s_prefix; take all keys > tau, then the smallest-index
+  // keys == tau until kk are taken
+  const uint32_t tau = s_prefix;
+  if (threadIdx.x == 0) {
+    s_count_gt = 0;
+    s_count_eq_taken = 0;
+  }
+  __syncthreads();
+  float* cv = ws.cand_val + (static_cast<size_t>(r) * splits + s) * kMaxK;
+  int32_t* ci = ws.cand_id + (static_cast<size_t>(r) * splits + s) * kMaxK;
+  if (kk > 0) {
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+      if (float_order_key(s_x[i]) > tau) {
+        const int slot = atomicAdd(&s_count_gt, 1);
+        s_cv[slot] = s_x[i];
+        s_ci[slot] = c0 + i;
+      }
+    }
+    __syncthreads();
+    const int gt = s_count_gt;
+    const int need_eq = kk - gt;
+    // ties at the threshold: if all of them are needed, collect in parallel
+    // (the final sort orders them); otherwise take the smallest indices.
+    int cnt_local = 0;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) cnt_local += (float_order_key(s_x[i]) == tau) ? 1 : 0;
+    const int cnt_eq = static_cast<int>(block_reduce_sum(static_cast<float>(cnt_local), s_red) + 0.5f);
+    if (cnt_eq <= need_eq) {
+      for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        if (float_order_key(s_x[i]) == tau) {
+          const int slot = atomicAdd(&s_count_eq_taken, 1);
+          s_cv[gt + slot] = s_x[i];
+          s_ci[gt + slot] = c0 + i;
+        }
+      }
+      __syncthreads();
+    } else {
+      int last = -1;
+      for (int t = 0; t < need_eq; ++t) {
+        float best = 3.0e38f;  // min index > last among ties (as float: indices < 2^24)
+        for (int i = threadIdx.x; i < n; i += blockDim.x)
+          if (i > last && float_order_key(s_x[i]) == tau) best = fminf(best, static_cast<float>(i));
+        for (int o = 16; o > 0; o >>= 1) best = fminf(best, __shfl_xor_sync(0xffffffffu, best, o));
+        __syncthreads();
+        if ((threadIdx.x & 31) == 0) s_red[threadIdx.x >> 5] = best;
+        __syncthreads();
+        float b = (threadIdx.x < (blockDim.x >> 5)) ? s_red[threadIdx.x] : 3.0e38f;
+        for (int o = 16; o > 0; o >>= 1) b = fminf(b, __shfl_xor_sync(0xffffffffu, b, o));
+        last = static_cast<int>(b);
+        if (threadIdx.x == 0) {
+          s_cv[gt + t] = s_x[last];
+          s_ci[gt + t] = c0 + last;
+        }
+      }
+      if (threadIdx.x == 0) s_count_eq_taken = need_eq;
+      __syncthreads();
+    }
+    const int total = gt + s_count_eq_taken;
+    // sort this chunk's candidates (value desc, id asc) into global partials
+    rank_select(s_cv, s_ci, total, kk, cv, ci);
+  }
+  for (int i = kk + threadIdx.x; i < k; i += blockDim.x) {  // pad short chunks
+    cv[i] = -INFINITY;
+    ci[i] = 0x7FFFFFFF;
+  }
+  if (threadIdx.x == 0) {
+    ws.part_m[r * splits + s] = m;
+    ws.part_s[r * splits + s] = ssum;
+  }
+  // last CTA of this row merges the splits
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const uint32_t prev = atomicAdd(&ws.counters[r], 1u);
+    s_last = (prev == static_cast<uint32_t>(splits - 1));
+  }
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  const int total = splits * k;
+  for (int i = threadIdx.x; i < total; i += blockDim.x) {
+    const int sp = i / k, j = i % k;
+    s_cv[i] = __ldcg(&ws.cand_val[(static_cast<size_t>(r) * splits + sp) * kMaxK + j]);
+    s_ci[i] = __ldcg(&ws.cand_id[(static_cast<size_t>(r) * splits + sp) * kMaxK + j]);
+  }
+  __syncthreads();
+  rank_select(s_cv, s_ci, total, k, ws.top_lp + static_cast<size_t>(r) * kMaxK,
+              ws.top_id + static_cast<size_t>(r) * kMaxK);
+  __syncthreads();
+  __threadfence();
+  if (threadIdx.x == 0) {
+    float M = -INFINITY;
+    for (int sp = 0; sp < splits; ++sp) M = fmaxf(M, __ldcg(&ws.part_m[r * splits + sp]));
+    float S = 0.0f;
+    for (int sp = 0; sp < splits; ++sp)
+      S += __ldcg(&ws.part_s[r * splits + sp]) * expf(__ldcg(&ws.part_m[r * splits + sp]) - M);
+    s_red[0] = M + logf(S);
+    ws.counters[r] = 0;  // ready for the next launch
+  }
+  __syncthreads();
+  const float lse = s_red[0];
+  float* lp = ws.top_lp + static_cast<size_t>(r) * kMaxK;
+  for (int j = threadIdx.x; j < k; j += blockDim.x) lp[j] = __fsub_rn(__ldcg(&lp[j]), lse);
+}
+
+// ============================================================ best-first heap
+// One warp.  Entries live in shared memory; each pop is a warp-wide argmin
+// under the reference's tuple order (-logw, ranks, parent, depth, rank, logw).
+constexpr int kHeapCap = 2 * kMaxBudget + 4;
+
+struct HeapSmem {
+  double neg_logw[kHeapCap];
+  double logw[kHeapCap];
+  int parent[kHeapCap];
+  int depth[kHeapCap];
+  int rank[kHeapCap];
+  int active[kHeapCap];
+  uint8_t path[kHeapCap][kMaxRows];  // ranks tuple (length = depth)
+  uint8_t node_path[DTREE_MAX_TREE][kMaxRows];
+  int n_entries;
+};
+
+__device__ __forceinline__ bool heap_less(const HeapSmem& h, int a, int b) {
+  if (h.neg_logw[a] != h.neg_logw[b]) return h.neg_logw[a] < h.neg_logw[b];
+  const int da = h.depth[a], db = h.depth[b];
+  const int dm = min(da, db);
+  for (int i = 0; i < dm; ++i)
+    if (h.path[a][i] != h.path[b][i]) return h.path[a][i] < h.path[b][i];
+  if (da != db) return da < db;  // shorter tuple sorts first
+  if (h.parent[a] != h.parent[b]) return h.parent[a] < h.parent[b];
+  if (h.depth[a] != h.depth[b]) return h.depth[a] < h.depth[b];
+  if (h.rank[a] != h.rank[b]) return h.rank[a] < h.rank[b];
+  return h.logw[a] < h.logw[b];
+}
+
+// top_ids/top_lp: [rows][ld] with k valid columns.  block = 32 threads.
+__global__ void __launch_bounds__(32) heap_tree_kernel(const int32_t* __restrict__ top_ids,
+                                                        const float* __restrict__ top_lp, int ld, int rows, int k,
+                                                        int budget, dtree_step_state* state,
+                                                        int32_t* __restrict__ tree_tokens,
+                                                        int32_t* __restrict__ parents, int32_t* __restrict__ depths,
+                                                        int32_t* __restrict__ positions,
+                                                        uint64_t* __restrict__ anc_mask) {
+  pdl_trigger();
+  __shared__ HeapSmem h;
+  const int lane = threadIdx.x;
+  pdl_wait();
+  const int start = state->start;
+  if (lane == 0) {
+    tree_tokens[0] = state->root_token;
+    parents[0] = -1;
+    depths[0] = 0;
+    positions[0] = start;
+    anc_mask[0] = 1ull;
+    anc_mask[1] = 0ull;
+    for (int i = 0; i < kHeapCap; ++i) h.active[i] = 0;
+    h.n_entries = 0;
+    if (budget > 0 && rows > 0 && k > 0) {
+      const double lw = static_cast<double>(top_lp[0]);
+      h.neg_logw[0] = -lw;
+      h.logw[0] = lw;
+      h.parent[0] = 0;
+      h.depth[0] = 1;
+      h.rank[0] = 0;
+      h.path[0][0] = 0;
+      h.active[0] = 1;
+      h.n_entries = 1;
+    }
+  }
+  __syncwarp();
+  int n_nodes = 0;
+  while (n_nodes < budget) {
+    // warp argmin over active entries
+    int best = -1;
+    const int ne = h.n_entries;
+    for (int e = lane; e < ne; e += 32)
+      if (h.active[e] && (best < 0 || heap_less(h, e, best))) best = e;
+    for (int o = 16; o > 0; o >>= 1) {
+      const int other = __shfl_xor_sync(0xffffffffu, best, o);
+      if (other >= 0 && (best < 0 || heap_less(h, other, best))) best = other;
+    }
+    if (best < 0) break;  // heap exhausted
+    if (lane == 0) {
+      const int depth = h.depth[best], rank = h.rank[best], parent = h.parent[best];
+      const double logw = h.logw[best];
+      const int cur = n_nodes + 1;
+      tree_tokens[cur] = top_ids[(depth - 1) * ld + rank];
+      parents[cur] = parent;
+      depths[cur] = depth;
+      positions[cur] = start + depth;
+      uint64_t a0 = anc_mask[2 * parent], a1 = anc_mask[2 * parent + 1];
+      if (cur < 64) a0 |= 1ull << cur; else a1 |= 1ull << (cur - 64);
+      anc_mask[2 * cur] = a0;
+      anc_mask[2 * cur + 1] = a1;
+      for (int i = 0; i < depth; ++i) h.node_path[cur][i] = h.path[best][i];
+      h.active[best] = 0;
+      int slot = best;  // reuse the popped slot for the sibling
+      if (rank + 1 < k) {
+        const double sib = (logw - static_cast<double>(top_lp[(depth - 1) * ld + rank])) +
+                           static_cast<double>(top_lp[(depth - 1) * ld + rank + 1]);
+        h.neg_logw[slot] = -sib;
+        h.logw[slot] = sib;
+        h.parent[slot] = parent;
+        h.depth[slot] = depth;
+        h.rank[slot] = rank + 1;
+        for (int i = 0; i < depth - 1; ++i) h.path[slot][i] = h.path[best][i];
+        h.path[slot][depth - 1] = static_cast<uint8_t>(rank + 1);
+        h.active[slot] = 1;
+        slot = -1;
+      }
+      if (depth < rows) {
+        int e = slot;
+        if (e < 0) e = h.n_entries++;
+        const double ch = logw + static_cast<double>(top_lp[depth * ld + 0]);
+        h.neg_logw[e] = -ch;
+        h.logw[e] = ch;
+        h.parent[e] = cur;
+        h.depth[e] = depth + 1;
+        h.rank[e] = 0;
+        for (int i = 0; i < depth; ++i) h.path[e][i] = h.node_path[cur][i];
+        h.path[e][depth] = 0;
+        h.active[e] = 1;
+      }
+    }
+    __syncwarp();
+    ++n_nodes;
+  }
+  if (lane == 0) state->n_nodes = n_nodes + 1;
+}
+
+// ============================================================ chain (DFlash)
+// grid = rows, block 256: per-row argmax (first index on ties); then the last
+// block writes the chain tree.
+__global__ void chain_argmax_kernel(const float* __restrict__ logits, int rows, int vocab,
+                                    dtree_step_state* state, int32_t* __restrict__ tree_tokens,
+                                    int32_t* __restrict__ parents, int32_t* __restrict__ depths,
+                                    int32_t* __restrict__ positions, uint64_t* __restrict__ anc_mask) {
+  pdl_trigger();
+  __shared__ float s_v[32];
+  __shared__ int s_i[32];
+  const int r = blockIdx.x;
+  pdl_wait();
+  const float* row = logits + static_cast<size_t>(r) * vocab;
+  float bv = -INFINITY;
+  int bi = 0x7FFFFFFF;
+  for (int v = threadIdx.x; v < vocab; v += blockDim.x) {
+    const float x = row[v];
+    if (x > bv || (x == bv && v < bi)) {
+      bv = x;
+      bi = v;
+    }
+  }
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+    if (ov > bv || (ov == bv && oi < bi)) {
+      bv = ov;
+      bi = oi;
+    }
+  }
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  if (l == 0) {
+    s_v[w] = bv;
+    s_i[w] = bi;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int j = 1; j < (blockDim.x >> 5); ++j)
+      if (s_v[j] > bv || (s_v[j] == bv && s_i[j] < bi)) {
+        bv = s_v[j];
+        bi = s_i[j];
+      }
+    const int start = state->start;
+    const int i = r + 1;
+    tree_tokens[i] = bi;
+    parents[i] = r;
+    depths[i] = i;
+    positions[i] = start + i;
+    // chain visibility: nodes 0..i
+    uint64_t a0 = 0, a1 = 0;
+    for (int j = 0; j <= i; ++j) {
+      if (j < 64) a0 |= 1ull << j; else a1 |= 1ull << (j - 64);
+    }
+    anc_mask[2 * i] = a0;
+    anc_mask[2 * i + 1] = a1;
+    if (r == 0) {
+      tree_tokens[0] = state->root_token;
+      parents[0] = -1;
+      depths[0] = 0;
+      positions[0] = start;
+      anc_mask[0] = 1ull;
+      anc_mask[1] = 0ull;
+      state->n_nodes = rows + 1;
+    }
+  }
+}
+
+// ============================================================ accept walk
+__global__ void __launch_bounds__(32) accept_walk_kernel(const int32_t* __restrict__ tree_tokens,
+                                                          const int32_t* __restrict__ parents,
+                                                          const int32_t* __restrict__ posterior,
+                                                          dtree_step_state* state, int32_t* __restrict__ accepted,
+                                                          int32_t* __restrict__ out_tokens, int out_cap,
+                                                          int32_t* __restrict__ history, int hist_cap) {
+  pdl_trigger();
+  const int lane = threadIdx.x;
+  pdl_wait();
+  const int n_nodes = min(state->n_nodes, DTREE_MAX_TREE);
+  const int start = state->start;
+  int cur = 0, n = 1;
+  if (lane == 0) accepted[0] = 0;
+  int tok = posterior[0];
+  for (int it = 0; it < n_nodes; ++it) {
+    int found = -1;
+    for (int j = 1 + lane; j < n_nodes; j += 32) {
+      const bool hit = (parents[j] == cur) && (tree_tokens[j] == tok);
+      const unsigned b = __ballot_sync(__activemask(), hit);
+      if (b && found < 0) found = j - lane + (__ffs(b) - 1);
+    }
+    // lanes may disagree only if some lanes did not iterate; take the min found
+    for (int o = 16; o > 0; o >>= 1) {
+      const int of = __shfl_xor_sync(0xffffffffu, found, o);
+      if (of >= 0 && (found < 0 || of < found)) found = of;
+    }
+    if (found < 0) break;
+    cur = found;
+    if (lane == 0) accepted[n] = cur;
+    ++n;
+    tok = posterior[cur];
+  }
+  if (lane == 0) {
+    for (int i = 0; i < n; ++i) {
+      const int pos = start + i;
+      if (pos < out_cap) out_tokens[pos] = tree_tokens[accepted[i]];
+    }
+    if (start + n < out_cap) out_tokens[start + n] = tok;
+    state->n_accepted = n;
+    state->bonus_token = tok;
+    state->n_output = start + n + 1;
+    const int step = state->step;
+    if (history && step < hist_cap) history[step] = n;
+  }
+}
+
+// ============================================================ compaction
+// grid = layers*2*kv_heads planes, block 256; smem holds the accepted rows.
+__global__ void kv_compact_kernel(__nv_bfloat16* __restrict__ kv, int capacity, int head_dim,
+                                  const int32_t* __restrict__ accepted, const dtree_step_state* state) {
+  pdl_trigger();
+  extern __shared__ __align__(16) uint4 s_rows[];  // up to DTREE_MAX_TREE rows of head_dim bf16
+  pdl_wait();
+  const int n = min(state->n_accepted, DTREE_MAX_TREE);
+  const int start = state->start;
+  bool identity = true;
+  for (int i = 0; i < n; ++i) identity &= (accepted[i] == i);
+  if (identity || n <= 0) return;
+  const int vec_per_row = head_dim * 2 / 16;
+  __nv_bfloat16* plane = kv + static_cast<size_t>(blockIdx.x) * capacity * head_dim;
+  const uint4* src = reinterpret_cast<const uint4*>(plane);
+  uint4* dst = reinterpret_cast<uint4*>(plane);
+  for (int e = threadIdx.x; e < n * vec_per_row; e += blockDim.x) {
+    const int i = e / vec_per_row, v = e % vec_per_row;
+    const int srow = start + accepted[i];
+    if (srow < capacity) s_rows[e] = src[static_cast<size_t>(srow) * vec_per_row + v];
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < n * vec_per_row; e += blockDim.x) {
+    const int i = e / vec_per_row, v = e % vec_per_row;
+    const int drow = start + i;
+    if (drow < capacity && start + accepted[i] < capacity) dst[static_cast<size_t>(drow) * vec_per_row + v] = s_rows[e];
+  }
+}
+
+__global__ void gather_rows_kernel(const uint4* __restrict__ src, int vec_per_row, const int32_t* __restrict__ idx,
+                                   const dtree_step_state* state, uint4* __restrict__ dst, int max_rows) {
+  pdl_trigger();
+  pdl_wait();
+  const int n = min(state->n_accepted, max_rows);
+  for (int e = blockIdx.x * blockDim.x + threadIdx.x; e < n * vec_per_row; e += gridDim.x * blockDim.x) {
+    const int i = e / vec_per_row, v = e % vec_per_row;
+    dst[static_cast<size_t>(i) * vec_per_row + v] = src[static_cast<size_t>(idx[i]) * vec_per_row + v];
+  }
+}
+
+__global__ void step_commit_kernel(dtree_step_state* state) {
+  pdl_trigger();
+  pdl_wait();
+  if (threadIdx.x == 0 && blockIdx.x == 0) {
+    state->start += state->n_accepted;
+    state->root_token = state->bonus_token;
+    state->step += 1;
+  }
+}
+
+// splits per row for the top-k scan: ~8 CTAs per row up to 148 total
+static int topk_splits(int rows, int vocab) {
+  int splits = 8;
+  while (splits > 1 && (vocab + splits - 1) / splits < 2048) splits >>= 1;
+  (void)rows;
+  return splits;
+}
+
+}  // namespace dtree
+
+using namespace dtree;
+
+extern "C" size_t dtree_tree_build_workspace_bytes(int rows, int vocab, int budget) {
+  (void)budget;
+  if (rows <= 0 || vocab <= 0) return 0;
+  return tree_ws_layout(rows, topk_splits(rows, vocab), nullptr, nullptr);
+}
+
+extern "C" int dtree_tree_build(const float* draft_logits, int rows, int vocab, int budget,
+                                dtree_step_state* state, void* workspace, size_t workspace_bytes,
+                                int32_t* tree_tokens, int32_t* parents, int32_t* depths, int32_t* positions,
+                                uint64_t* anc_mask, int32_t* top_ids, float* top_logprobs, void* stream_) {
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  DTREE_CHECK_ARG(state && tree_tokens && parents && depths && positions && anc_mask, "null output pointer");
+  DTREE_CHECK_ARG(budget >= 0 && budget <= kMaxBudget, "budget must be in [0, 127]");
+  DTREE_CHECK_ARG(rows >= 0 && rows <= kMaxRows, "rows must be in [0, 64]");
+  DTREE_CHECK_ARG(vocab > 0, "vocab must be positive");
+  const int k = budget < vocab ? budget : vocab;
+  if (budget == 0 || rows == 0) {
+    // root only (dtree_runtime.py:88-90)
+    DTREE_CUDA_RET(launch_pdl(heap_tree_kernel, dim3(1), dim3(32), 0, stream, (const int32_t*)nullptr,
+                              (const float*)nullptr, 0, 0, 0, 0, state, tree_tokens, parents, depths, positions,
+                              anc_mask));
+    return kOk;
+  }
+  DTREE_CHECK_ARG(draft_logits != nullptr, "null draft_logits");
+  const int splits = topk_splits(rows, vocab);
+  const size_t need = tree_ws_layout(rows, splits, nullptr, nullptr);
+  DTREE_CHECK_ARG(workspace != nullptr && workspace_bytes >= need, "tree workspace too small");
+  TreeWs ws;
+  tree_ws_layout(rows, splits, &ws, static_cast<char*>(workspace));
+  const int chunk = (vocab + splits - 1) / splits;
+  const size_t smem = static_cast<size_t>(chunk) * 4 + static_cast<size_t>(splits) * kMaxK * 8;
+  DTREE_CHECK_ARG(smem <= 200 * 1024, "vocab too large for the top-k chunking");
+  DTREE_CUDA_RET(cudaFuncSetAttribute(topk_lse_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+  DTREE_CUDA_RET(launch_pdl(topk_lse_kernel, dim3(splits, rows), dim3(kTopkThreads), smem, stream, draft_logits,
+                            rows, vocab, k, splits, chunk, ws));
+  DTREE_CUDA_RET(launch_pdl(heap_tree_kernel, dim3(1), dim3(32), 0, stream, (const int32_t*)ws.top_id,
+                            (const float*)ws.top_lp, kMaxK, rows, k, budget, state, tree_tokens, parents, depths,
+                            positions, anc_mask));
+  if (top_ids) {
+    DTREE_CUDA_RET(cudaMemcpy2DAsync(top_ids, sizeof(int32_t) * k, ws.top_id, sizeof(int32_t) * kMaxK,
+                                     sizeof(int32_t) * k, rows, cudaMemcpyDeviceToDevice, stream));
+  }
+  if (top_logprobs) {
+    DTREE_CUDA_RET(cudaMemcpy2DAsync(top_logprobs, sizeof(float) * k, ws.top_lp, sizeof(float) * kMaxK,
+                                     sizeof(float) * k, rows, cudaMemcpyDeviceToDevice, stream));
+  }
+  return kOk;
+}
+
+extern "C" int dtree_tree_from_topk(const int32_t* top_ids, const float* top_logprobs, int rows, int topk,
+                                    int budget, dtree_step_state* state, int32_t* tree_tokens, int32_t* parents,
+                                    int32_t* depths, int32_t* positions, uint64_t* anc_mask, void* stream_) {
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  DTREE_CHECK_ARG(state && tree_tokens && parents && depths && positions && anc_mask, "null output pointer");
+  DTREE_CHECK_ARG(budget >= 0 && budget <= kMaxBudget, "budget must be in [0, 127]");
+  DTREE_CHECK_ARG(rows >= 0 && rows <= kMaxRows, "rows must be in [0, 64]");
+  DTREE_CHECK_ARG(topk >= 0 && topk <= kMaxK, "topk must be in [0, 128]");
+  DTREE_CHECK_ARG((rows == 0 || topk == 0) || (top_ids && top_logprobs), "null top-k inputs");
+  DTREE_CUDA_RET(launch_pdl(heap_tree_kernel, dim3(1), dim3(32), 0, stream, top_ids, top_logprobs, topk, rows, topk,
+                            (rows == 0 || topk == 0) ? 0 : budget, state, tree_tokens, parents, depths, positions,
+                            anc_mask));
+  return kOk;
+}
+
+extern "C" int dtree_chain_build(const float* draft_logits, int rows, int vocab, dtree_step_state* state,
+                                 int32_t* tree_tokens, int32_t* parents, int32_t* depths, int32_t* positions,
+                                 uint64_t* anc_mask, void* stream_) {
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  DTREE_CHECK_ARG(draft_logits && state && tree_tokens && parents && depths && positions && anc_mask,
+                  "null pointer");
+  DTREE_CHECK_ARG(rows >= 1 && rows < DTREE_MAX_TREE, "rows must be in [1, 127]");
+  DTREE_CHECK_ARG(vocab > 0, "vocab must be positive");
+  DTREE_CUDA_RET(launch_pdl(chain_argmax_kernel, dim3(rows), dim3(256), 0, stream, draft_logits, rows, vocab, state,
+                            tree_tokens, parents, depths, positions, anc_mask));
+  return kOk;
+}
+
+extern "C" int dtree_plant_draft_logits(float* logits, int rows, int vocab, uint32_t seed,
+                                        const dtree_step_state* state, const int32_t* continuation, int cont_len,
+                                        float p_correct, void* stream_) {
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  DTREE_CHECK_ARG(logits && state, "null pointer");
+  DTREE_CHECK_ARG(rows > 0 && rows <= kMaxRows && vocab > 0, "bad shape");
+  DTREE_CHECK_ARG(cont_len == 0 || continuation != nullptr, "null continuation");
+  DTREE_CUDA_RET(launch_pdl(plant_draft_logits_kernel, dim3((vocab + 255) / 256, rows), dim3(256), 0, stream, logits,
+                            rows, vocab, seed, state, continuation, cont_len, p_correct));
+  return kOk;
+}
+
+extern "C" int dtree_accept_walk(const int32_t* tree_tokens, const int32_t* parents, const int32_t* posterior,
+                                 dtree_step_state* state, int32_t* accepted, int32_t* output_tokens,
+                                 int output_capacity, int32_t* accept_history, int history_capacity, void* stream_) {
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  DTREE_CHECK_ARG(tree_tokens && parents && posterior && state && accepted && output_tokens, "null pointer");
+  DTREE_CUDA_RET(launch_pdl(accept_walk_kernel, dim3(1), dim3(32), 0, stream, tree_tokens, parents, posterior, state,
+                            accepted, output_tokens, output_capacity, accept_history, history_capacity));
+  return kOk;
+}
+
+extern "C" int dtree_kv_compact(void* kv_cache, int layers, int kv_heads, int capacity, int head_dim,
+                                const int32_t* accepted, const dtree_step_state* state, void* stream_) {
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  DTREE_CHECK_ARG(kv_cache && accepted && state, "null pointer");
+  DTREE_CHECK_ARG(layers > 0 && kv_heads > 0 && capacity > 0, "bad shape");
+  DTREE_CHECK_ARG(head_dim % 8 == 0 && head_dim <= 256, "head_dim must be a multiple of 8 and <= 256");
+  const size_t smem = static_cast<size_t>(DTREE_MAX_TREE) * head_dim * 2;
+  DTREE_CUDA_RET(cudaFuncSetAttribute(kv_compact_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      static_cast<int>(smem)));
+  DTREE_CUDA_RET(launch_pdl(kv_compact_kernel, dim3(layers * 2 * kv_heads), dim3(256), smem, stream,
+                            static_cast<__nv_bfloat16*>(kv_cache), capacity, head_dim, accepted, state));
+  return kOk;
+}
+
+extern "C" int dtree_gather_rows(const void* src, size_t row_bytes, const int32_t* accepted,
+                                 const dtree_step_state* state, void* dst, int max_rows, void* stream_) {
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  DTREE_CHECK_ARG(src && accepted && state && dst, "null pointer");
+  DTREE_CHECK_ARG(row_bytes % 16 == 0 && row_bytes > 0, "row_bytes must be a positive multiple of 16");
+  const int vec = static_cast<int>(row_bytes / 16);
+  DTREE_CUDA_RET(launch_pdl(gather_rows_kernel, dim3(64), dim3(256), 0, stream, static_cast<const uint4*>(src), vec,
+                            accepted, state, static_cast<uint4*>(dst), max_rows));
+  return kOk;
+}
+
+extern "C" int dtree_step_commit(dtree_step_state* state, void* stream_) {
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  DTREE_CHECK_ARG(state, "null state");
+  DTREE_CUDA_RET(launch_pdl(step_commit_kernel, dim3(1), dim3(32), 0, stream, state));
+  return kOk;
+}

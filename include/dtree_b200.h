@@ -1,0 +1,235 @@
+/*
+ * libdtree_b200 — C ABI of the B200 (sm_100a) DTree/DFlash speculative-decoding step.
+ *
+ * Every entry point takes plain device pointers, sizes and a cudaStream_t
+ * (passed as void*), launches asynchronously on that stream, allocates
+ * nothing, and returns 0 on success or a negative status (see DTREE_*
+ * below); dtree_last_error() then describes the failure.  Buffers are owned
+ * by the caller.  The reference (DrHB/dtree-mlx, Python/MLX) reaches these
+ * operations through the MLXTargetAdapter plugin interface
+ * (dtree_mlx/adapters.py:88-213) and the DTree runtime
+ * (dtree_mlx/dtree_runtime.py); each declaration names the reference
+ * function it replaces.
+ *
+ * Threading: entry points are reentrant across streams; a model handle must
+ * not be used by two streams at once (its activation buffers are shared).
+ */
+#ifndef DTREE_B200_H_
+#define DTREE_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define DTREE_API __attribute__((visibility("default")))
+#else
+#define DTREE_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ------------------------------------------------------------------ status */
+#define DTREE_OK 0
+#define DTREE_ERR_INVALID_ARG (-1)
+#define DTREE_ERR_CUDA (-2)
+#define DTREE_ERR_UNSUPPORTED (-3)
+#define DTREE_ERR_CAPACITY (-4)
+#define DTREE_ERR_TREE (-5)
+#define DTREE_ERR_STATE (-6)
+
+/* Largest tree (root + nodes) one verify step accepts; ancestor masks are
+ * DTREE_MASK_WORDS little-endian uint64 words per node. */
+#define DTREE_MAX_TREE 128
+#define DTREE_MASK_WORDS 2
+
+/* Thread-local description of the last failed call (never NULL). */
+DTREE_API const char* dtree_last_error(void);
+
+/* Library ABI version (major*100 + minor). */
+DTREE_API int dtree_version(void);
+
+/* Reads the device-side error word (bounded-wait timeouts, invalid device
+ * inputs; 0 = none) after synchronizing the device; clears it if clear != 0. */
+DTREE_API int dtree_device_error(uint32_t* code_out, int clear);
+
+/* ---------------------------------------------------------- decode state
+ * Per-sequence decode bookkeeping kept in device memory so that a whole
+ * decode step can run (and be graph-replayed) without a host round trip.
+ * Mirrors the loop variables of dtree_generate (dtree_runtime.py:351-354,
+ * 531-534): `start` is the number of tokens committed to the target KV cache
+ * (the reference's `start` / past_length) and `root_token` is
+ * output_tokens[start] (sampled but not yet in the cache). */
+typedef struct dtree_step_state {
+  int32_t start;        /* committed tokens in the target KV cache            */
+  int32_t root_token;   /* last posterior token; root of the next tree        */
+  int32_t step;         /* decode steps completed                             */
+  int32_t n_accepted;   /* accepted inputs of the last step (root included)   */
+  int32_t bonus_token;  /* posterior token after the accepted path            */
+  int32_t n_output;     /* tokens written to the output buffer                */
+  int32_t n_nodes;      /* nodes in the current tree (root included)          */
+  int32_t reserved;
+} dtree_step_state;
+
+/* --------------------------------------------------------- tree build
+ * Replaces build_dtree_tree + compile_dtree_tree (dtree_runtime.py:82-192):
+ * per draft row the fp32 top-k (k = min(budget, vocab); equal logits ordered
+ * by ascending token id) and log-softmax, then the best-first expansion with
+ * the reference's float64 heap key (-logw, ranks, parent, depth, rank, logw)
+ * and sibling score logw - lp[r] + lp[r+1].  Outputs (node 0 = root):
+ *   tree_tokens[i]  verify input ids (root = state->root_token)
+ *   parents[i]      parent index (-1 for the root)
+ *   depths[i]       depth (0 for the root)
+ *   positions[i]    RoPE position state->start + depth
+ *   anc_mask[i][w]  bit j set iff node j is visible to node i (visibility row)
+ *   top_ids/top_logprobs (optional, may be NULL) [rows][k] heap inputs
+ * state->n_nodes is set to 1 + number of nodes.  rows <= 64, budget <= 127.
+ * `workspace` holds per-row partials: dtree_tree_build_workspace_bytes(). */
+DTREE_API size_t dtree_tree_build_workspace_bytes(int rows, int vocab, int budget);
+DTREE_API int dtree_tree_build(const float* draft_logits, int rows, int vocab, int budget,
+                     dtree_step_state* state, void* workspace, size_t workspace_bytes,
+                     int32_t* tree_tokens, int32_t* parents, int32_t* depths, int32_t* positions,
+                     uint64_t* anc_mask, int32_t* top_ids, float* top_logprobs, void* stream);
+
+/* Heap stage only, from given top-k ids/log-probs (for parity checks against
+ * the reference's own heap inputs).  Same outputs as dtree_tree_build. */
+DTREE_API int dtree_tree_from_topk(const int32_t* top_ids, const float* top_logprobs, int rows, int topk, int budget,
+                         dtree_step_state* state, int32_t* tree_tokens, int32_t* parents, int32_t* depths,
+                         int32_t* positions, uint64_t* anc_mask, void* stream);
+
+/* Linear (DFlash) block: the chain tree of dflash_generate's verify block
+ * (runtime.py:476-490): node i+1 = argmax of draft row i, parent i, depth i+1.
+ * Argmax ties keep the first index (runtime.py:12-19 sample_tokens, T=0). */
+DTREE_API int dtree_chain_build(const float* draft_logits, int rows, int vocab, dtree_step_state* state,
+                      int32_t* tree_tokens, int32_t* parents, int32_t* depths, int32_t* positions,
+                      uint64_t* anc_mask, void* stream);
+
+/* -------------------------------------------------- planted draft logits
+ * Synthetic drafter of the benchmark workloads (stands in for
+ * DFlashDraftModel + lm_head_logits, dtree_runtime.py:366-376): row r gets
+ * Irwin-Hall(12)-6 noise from Philox4x32-10(seed, state->step, r) and +8 on
+ * continuation[state->start + r + 1] with probability p_correct (else on a
+ * Philox-chosen random token; also when the position is >= cont_len). */
+DTREE_API int dtree_plant_draft_logits(float* logits, int rows, int vocab, uint32_t seed, const dtree_step_state* state,
+                             const int32_t* continuation, int cont_len, float p_correct, void* stream);
+
+/* ---------------------------------------------------- acceptance walk
+ * Replaces follow_verified_tree (dtree_runtime.py:195-208) and the output
+ * commit (dtree_runtime.py:530-537): walks from the root while the posterior
+ * token of the current node is the token of one of its children.  Writes
+ * accepted[0..n) (node indices, ascending), state->n_accepted,
+ * state->bonus_token, appends the accepted tokens and the bonus token to
+ * output_tokens at [state->start, ...) (bounded by output_capacity), sets
+ * state->n_output, and records n_accepted in accept_history[state->step]
+ * (if non-NULL and step < history_capacity). */
+DTREE_API int dtree_accept_walk(const int32_t* tree_tokens, const int32_t* parents, const int32_t* posterior,
+                      dtree_step_state* state, int32_t* accepted, int32_t* output_tokens, int output_capacity,
+                      int32_t* accept_history, int history_capacity, void* stream);
+
+/* ------------------------------------------------------ KV compaction
+ * Replaces Qwen3TargetAdapter.compact_kv_caches (adapters.py:635-668) for
+ * every layer at once: rows [start + accepted[i]] -> [start + i] of each
+ * (layer, K|V, kv-head) plane of a cache laid out
+ * [layers][2][kv_heads][capacity][head_dim] (bf16, head_dim*2 bytes a row).
+ * All reads of a plane happen before its writes (in-place safe). */
+DTREE_API int dtree_kv_compact(void* kv_cache, int layers, int kv_heads, int capacity, int head_dim,
+                     const int32_t* accepted, const dtree_step_state* state, void* stream);
+
+/* Hidden select (dtree_runtime.py:519-522): dst[i] = src[accepted[i]] for
+ * i < state->n_accepted, rows of row_bytes (multiple of 16). */
+DTREE_API int dtree_gather_rows(const void* src, size_t row_bytes, const int32_t* accepted, const dtree_step_state* state,
+                      void* dst, int max_rows, void* stream);
+
+/* Advances the decode state after a step: start += n_accepted,
+ * root_token = bonus_token, step += 1 (dtree_runtime.py:531-534). */
+DTREE_API int dtree_step_commit(dtree_step_state* state, void* stream);
+
+/* ------------------------------------------------------- dense linear
+ * y[t, n] = sum_k x[t, k] * w[n, k]  (bf16 in, fp32 accumulate, bf16 out):
+ * the projection inside every MLX nn.Linear of the verify forward
+ * (qwen3_tree.py:50-52,78,82).  tcgen05 swap-AB GEMM: w streams through
+ * TMA into 128-row tiles, x (t_pad rows, multiple of 16, <= 256) is the
+ * N side.  k % 64 == 0.  workspace: dtree_linear_workspace_bytes(). */
+DTREE_API size_t dtree_linear_workspace_bytes(int t_pad, int n);
+DTREE_API int dtree_linear_bf16(const void* x, int t_pad, int k, const void* w, int n, void* y, void* workspace,
+                      size_t workspace_bytes, int split_k, void* stream);
+
+/* LM head fused with argmax (adapters.py:114-118 lm_head_argmax +
+ * runtime.py:12-19 at temperature 0): out[t] = argmax_v bf16(h[t]·E[v]),
+ * ties to the smallest v; logits never reach HBM.  workspace:
+ * dtree_lm_head_workspace_bytes(). */
+DTREE_API size_t dtree_lm_head_workspace_bytes(int t_pad);
+DTREE_API int dtree_lm_head_argmax(const void* h, int t_pad, int n_rows, int hidden, const void* embed, int vocab,
+                         int32_t* out, void* workspace, size_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------- Qwen3 tree verify
+ * A Qwen3 target (mlx-lm qwen3 layer math: RMSNorm, q/k RMSNorm, half-split
+ * RoPE, GQA attention, SwiGLU, tied LM head) held as device pointers.
+ * Weight layouts (bf16, row-major [out, in]):
+ *   qkv      [(n_heads + 2*n_kv_heads)*head_dim, hidden]  rows q | k | v
+ *   o_proj   [hidden, n_heads*head_dim]
+ *   gate_up  [2*ffn, hidden] in 64-row blocks g0 u0 g1 u1 ... (gate rows
+ *            64j..64j+63 then the matching up rows)
+ *   down     [hidden, ffn]
+ * kv_cache: [layers][2][n_kv_heads][kv_capacity][head_dim] bf16. */
+typedef struct dtree_qwen3_layer {
+  const void* input_norm;
+  const void* qkv;
+  const void* q_norm;
+  const void* k_norm;
+  const void* o_proj;
+  const void* post_norm;
+  const void* gate_up;
+  const void* down;
+} dtree_qwen3_layer;
+
+typedef struct dtree_qwen3_desc {
+  /* configuration */
+  int hidden, layers, n_heads, n_kv_heads, head_dim, ffn, vocab;
+  float rope_theta, rms_eps;
+  int t_cap;          /* max tree rows per forward (<= DTREE_MAX_TREE), multiple of 16 */
+  int kv_capacity;    /* positions per (layer, kv-head) plane */
+  int n_capture;      /* hidden-capture layers (verifier_hidden), <= 16 */
+  int capture_layers[16];
+  /* weights */
+  const void* embed;       /* [vocab, hidden], also the tied LM head */
+  const void* final_norm;  /* [hidden] */
+  const dtree_qwen3_layer* layer;  /* [layers] */
+  /* caller-owned buffers (sizes from dtree_qwen3_buffer_bytes) */
+  void* kv_cache;
+  void* h;            /* [t_cap, hidden] residual stream */
+  void* xn;           /* [t_cap, hidden] normalized activations */
+  void* q;            /* [t_cap, n_heads*head_dim] */
+  void* attn;         /* [t_cap, n_heads*head_dim] */
+  void* act;          /* [t_cap, ffn] */
+  void* norm_out;     /* [t_cap, hidden] final-norm hidden (norm_hidden_states) */
+  void* capture;      /* [t_cap, hidden*n_capture] verifier_hidden */
+  void* workspace;    /* fp32 split-K / attention partials + counters */
+  size_t workspace_bytes;
+} dtree_qwen3_desc;
+
+typedef struct dtree_qwen3_model dtree_qwen3_model;
+
+/* Bytes each caller buffer must hold: out[0..8] = kv_cache, h, xn, q, attn,
+ * act, norm_out, capture, workspace. */
+DTREE_API int dtree_qwen3_buffer_bytes(const dtree_qwen3_desc* desc, size_t out[9]);
+DTREE_API int dtree_qwen3_create(const dtree_qwen3_desc* desc, dtree_qwen3_model** out);
+DTREE_API int dtree_qwen3_destroy(dtree_qwen3_model* model);
+
+/* Replaces Qwen3TargetAdapter.forward_tree_with_hidden_states
+ * (adapters.py:568-597, per-layer qwen3_tree.py:39-83) fused with
+ * lm_head_argmax: embeds tree_tokens[0..n_nodes), runs every layer with
+ * per-node RoPE positions and the ancestor-mask tree attention over the
+ * cache prefix [0, state->start) plus the tree, writes the new K/V at cache
+ * slots [start, start + n_nodes), leaves norm_hidden in desc.norm_out and
+ * verifier_hidden in desc.capture, and writes the greedy posterior token of
+ * every node to `posterior` (if non-NULL).  n_nodes <= t_cap. */
+DTREE_API int dtree_qwen3_forward_tree(dtree_qwen3_model* model, const int32_t* tree_tokens, const int32_t* positions,
+                             const uint64_t* anc_mask, int n_nodes, const dtree_step_state* state,
+                             int32_t* posterior, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* DTREE_B200_H_ */

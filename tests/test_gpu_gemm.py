@@ -1,0 +1,89 @@
+"""tcgen05 stream-K GEMM and the fused LM-head argmax vs a torch fp32 reference.
+
+Tolerance for bf16 outputs: |y - ref| <= 2^-7 |ref| + 1e-3 max|ref| (one bf16
+rounding of an fp32 accumulation of the same bf16 inputs).
+"""
+from __future__ import annotations
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+@pytest.fixture(scope="module")
+def K(lib):
+    from dtree_mlx_b200 import kernels
+
+    return kernels
+
+
+def _check(y, ref):
+    err = (y.float() - ref).abs()
+    tol = ref.abs() * 2.0 ** -7 + 1e-3 * ref.abs().max()
+    bad = (err > tol).sum().item()
+    assert bad == 0, f"{bad} elements out of tolerance, max err {err.max().item()}"
+
+
+@pytest.mark.parametrize(
+    "t_pad,k,n",
+    [
+        (16, 64, 128),
+        (32, 256, 384),
+        (32, 2560, 6144),   # fused q|k|v of the 4B shape
+        (32, 4096, 2560),   # o_proj: 20 tiles -> stream-K partial tiles
+        (32, 9728, 2560),   # down_proj
+        (16, 512, 200),     # ragged N (zero-filled TMA rows)
+        (64, 1024, 1536),
+        (128, 512, 640),
+    ],
+)
+def test_linear_matches_fp32(K, t_pad, k, n):
+    g = torch.Generator(device=DEV).manual_seed(t_pad * 7 + k + n)
+    x = torch.randn(t_pad, k, device=DEV, generator=g).to(torch.bfloat16)
+    w = (torch.randn(n, k, device=DEV, generator=g) * 0.02).to(torch.bfloat16)
+    y = K.linear_bf16(x, w)
+    torch.cuda.synchronize()
+    ref = x.float() @ w.float().t()
+    _check(y, ref)
+
+
+def test_linear_deterministic(K):
+    g = torch.Generator(device=DEV).manual_seed(3)
+    x = torch.randn(32, 9728, device=DEV, generator=g).to(torch.bfloat16)
+    w = (torch.randn(2560, 9728, device=DEV, generator=g) * 0.02).to(torch.bfloat16)
+    y1 = K.linear_bf16(x, w).clone()
+    y2 = K.linear_bf16(x, w).clone()
+    assert torch.equal(y1, y2)
+
+
+@pytest.mark.parametrize("t_pad,n_rows,hidden,vocab", [(32, 25, 2560, 151936), (16, 9, 512, 32768), (64, 40, 512, 5000)])
+def test_lm_head_argmax(K, t_pad, n_rows, hidden, vocab):
+    g = torch.Generator(device=DEV).manual_seed(vocab)
+    h = torch.randn(t_pad, hidden, device=DEV, generator=g).to(torch.bfloat16)
+    e = (torch.randn(vocab, hidden, device=DEV, generator=g) * 0.02).to(torch.bfloat16)
+    out = K.lm_head_argmax(h, e, n_rows)
+    torch.cuda.synchronize()
+    logits = (h[:n_rows].double() @ e.double().t()).to(torch.bfloat16).float()
+    ref = torch.argmax(logits, dim=-1)
+    got = out.long()
+    mism = (got != ref).nonzero().flatten().tolist()
+    for t in mism:  # only near-ties may differ (one bf16 ulp at the max)
+        mx = logits[t].max()
+        assert (mx - logits[t, got[t]]).abs() <= mx.abs() * 2.0 ** -7, (t, got[t].item(), ref[t].item())
+    assert len(mism) <= max(1, n_rows // 10)
+
+
+def test_lm_head_argmax_first_index_on_ties(K):
+    """Exact ties (also across vocab tiles / CTAs) keep the smallest id."""
+    hidden, vocab = 256, 40000
+    e = torch.zeros(vocab, hidden, device=DEV, dtype=torch.bfloat16)
+    h = torch.ones(16, hidden, device=DEV, dtype=torch.bfloat16)
+    for v in (70, 5, 39000, 20000):
+        e[v] = 1.0
+    out = K.lm_head_argmax(h, e, 16)
+    assert out.tolist() == [5] * 16
+    # repeated calls: the device keys/counters reset themselves
+    out2 = K.lm_head_argmax(h, e, 16)
+    assert out2.tolist() == [5] * 16
