@@ -1,0 +1,436 @@
+"""Benchmark: accepted tokens/s of the DTree speculative-decoding step.
+
+Workload: Qwen3-4B-shaped target, bf16, random init
+(std 0.02); 256-token uniform-random prompt; greedy generation of 512 new
+tokens with spec=16, tree_budget=24; planted draft logits with top-1
+agreement p=0.85 against the target's greedy continuation.
+
+A bench "step" is one whole 512-token DTree generation after the prefill
+(~80 decode steps: planted draft -> device tree build -> tree-verify forward
+with fused LM-head argmax -> acceptance walk -> KV compaction -> commit), each
+decode step one CUDA-graph replay with no host round trip.  ``value`` =
+accepted (generated) tokens per second over all ranks.  ``e2e`` runs the same
+generation through the public API (``DFlashGenerator.generate_from_tokens``)
+with the prompt copied from host memory, the prefill, one 32-byte state read
+per decode step and the final token read-back inside the timed region.
+
+The greedy continuation the drafter plants is the target's own greedy stream
+as this engine computes it: the first warm-up generation uses unplanted
+(random) drafts, and generations repeat with the previous output planted
+until the output no longer changes (a fixed point), so every timed generation
+follows the same trees and acceptance.
+
+Roofline: the tree-verify forward (the step's dominant work, 36 layers + LM
+head, T=25 rows) is replayed on its own as a CUDA graph at prefix lengths 512
+and 2048 and timed with CUDA events; algorithmic bytes = all weights once
+(8.0445 GB) + K/V prefix read + new K/V write.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    torchrun --nproc-per-node N bench.py --gpus N ...   (independent replicas)
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+PROMPT_LEN = 256
+MAX_NEW = 512
+SPEC = 16
+BUDGET = 24
+P_CORRECT = 0.85
+PRESET = "qwen3-4b"
+KV_CAP = 2304
+METRIC = "accepted tok/s/GPU, Qwen3-4B-shape DTree b24; verify-step HBM GB/s vs peak"
+UNIT = "tokens/s"
+
+
+def dist_init():
+    import torch
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    pg = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local) if torch.cuda.is_available() else None
+        backend = "nccl" if torch.cuda.is_available() else "gloo"
+        dist.init_process_group(backend, timeout=datetime.timedelta(seconds=600))
+        pg = dist
+    elif torch.cuda.is_available():
+        torch.cuda.set_device(local)
+    return rank, world, local, pg
+
+
+def measured_peaks() -> dict:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": float(d["hbm_gbs"]), "source": "measured"}
+    return {"hbm_gbs": 6650.0, "source": "fallback"}
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle sampling during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.idx = gpu_index
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        try:
+            fd, self.path = tempfile.mkstemp(suffix=".csv")
+            os.close(fd)
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.idx), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        rows = []
+        for line in Path(self.path).read_text().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) >= 9:
+                rows.append(parts)
+        os.unlink(self.path)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+def algorithmic_verify_bytes(cfg, weights, prefix: int, t: int) -> float:
+    wbytes = sum(x.numel() * x.element_size() for x in
+                 [weights.embed, *weights.qkv, *weights.o_proj, *weights.gate_up, *weights.down])
+    kv_row = 2 * cfg.num_key_value_heads * cfg.head_dim * 2 * cfg.num_hidden_layers
+    return float(wbytes + prefix * kv_row + t * kv_row)
+
+
+# ---------------------------------------------------------------------- ours
+def run_ours(args, rank, world, local, dist) -> dict | None:
+    import torch
+
+    from dtree_mlx_b200 import DFlashGenerator
+    from dtree_mlx_b200.adapters import load_target_model
+    from dtree_mlx_b200.draft import PlantedDrafter
+    from dtree_mlx_b200.engine import DecodeSession
+    from dtree_mlx_b200.synthetic import random_prompt
+
+    dev = torch.device("cuda", local)
+    target = load_target_model(f"synthetic:{PRESET}:seed=0:kv={KV_CAP}")
+    cfg = target.model.cfg
+    drafter = PlantedDrafter(seed=1000 + rank, p_correct=P_CORRECT, block_size=SPEC)
+    gen = DFlashGenerator.from_components(target, drafter)
+    prompt = random_prompt(PROMPT_LEN, cfg.vocab_size, seed=rank)
+    gkw = dict(max_new_tokens=MAX_NEW, decode_mode="dtree", speculative_tokens=SPEC, tree_budget=BUDGET)
+
+    # fixed point of the planted continuation (untimed)
+    prev = None
+    fixed_iters = 0
+    for it in range(6):
+        r = gen.generate_from_tokens(prompt, **gkw)
+        fixed_iters = it + 1
+        if prev is not None and r.output_tokens == prev:
+            break
+        prev = r.output_tokens
+        drafter.set_continuation(prev, dev)
+    converged = prev is not None and r.output_tokens == prev
+    session: DecodeSession = target.adapter.last_session
+    n_steps = len(r.metrics["acceptance_lengths"])
+    first = r.output_tokens[PROMPT_LEN]
+    accept = r.metrics["acceptance_lengths"]
+    stream = r.output_tokens
+
+    def one_generation():
+        session.reset(PROMPT_LEN, first)
+        for _ in range(n_steps):
+            session.graph.replay()
+
+    for _ in range(args.warmup):
+        one_generation()
+    torch.cuda.synchronize()
+    assert session.output[: PROMPT_LEN + MAX_NEW].tolist() == stream[: PROMPT_LEN + MAX_NEW], "replay diverged"
+
+    sampler = ClockSampler(local) if rank == 0 else None
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    if sampler:
+        sampler.start()
+        time.sleep(0.4)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        one_generation()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    if dist:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+        dist.barrier()
+    clocks = sampler.stop() if sampler else None
+
+    # ---- roofline: verify forward replayed alone at prefix 512 and 2048
+    eng = session.engine
+    n_nodes = session.cfg.n_nodes
+    roof = {}
+    from dtree_mlx_b200 import kernels
+
+    for P in (PROMPT_LEN + MAX_NEW // 2, 2048):
+        st = kernels.new_state(dev, start=P, root_token=first)
+        post = torch.zeros(128, dtype=torch.int32, device=dev)
+        eng.forward_tree(session.tree.tokens, session.tree.positions, session.tree.anc, n_nodes, st, post)
+        torch.cuda.synchronize()
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=s):
+            eng.forward_tree(session.tree.tokens, session.tree.positions, session.tree.anc, n_nodes, st, post)
+        torch.cuda.current_stream().wait_stream(s)
+        for _ in range(3):
+            g.replay()
+        reps = 50
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        a.record()
+        for _ in range(reps):
+            g.replay()
+        b.record()
+        torch.cuda.synchronize()
+        vms = a.elapsed_time(b) / reps
+        roof[P] = (vms, algorithmic_verify_bytes(cfg, target.model.weights, P, n_nodes))
+        del g
+
+    # ---- e2e through the public API (host prompt in, host tokens out)
+    e2e_ms = []
+    for _ in range(max(1, min(args.steps, 3))):
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        rr = gen.generate_from_tokens(prompt, **gkw)
+        torch.cuda.synchronize()
+        e2e_ms.append((time.perf_counter() - t0) * 1e3)
+        assert rr.output_tokens == stream
+    e2e_tok_s = MAX_NEW / (statistics.median(e2e_ms) / 1e3)
+
+    stats = torch.tensor([MAX_NEW * args.steps, ms, n_steps, sum(accept)], dtype=torch.float64, device=dev)
+    all_stats = [stats]
+    if dist:
+        all_stats = [torch.zeros_like(stats) for _ in range(world)]
+        dist.all_gather(all_stats, stats)
+        e2e_t = torch.tensor([e2e_tok_s], device=dev)
+        dist.all_reduce(e2e_t)
+        e2e_tok_s = float(e2e_t.item())
+    if rank != 0:
+        return None
+    total_tokens = sum(float(s[0]) for s in all_stats)
+    value = total_tokens / (ms / 1e3)
+    peaks = measured_peaks()
+    vms, vbytes = roof[2048]
+    achieved = vbytes / (vms / 1e3) / 1e9
+    traffic = None
+    tp = ROOT / "profiles" / "verify_traffic.json"
+    if tp.exists():
+        try:
+            traffic = json.loads(tp.read_text()).get("bytes_per_verify")
+        except Exception:
+            traffic = None
+    launches_per_step = 8 * cfg.num_hidden_layers + 7
+    out = {
+        "metric": METRIC,
+        "value": round(value, 2),
+        "unit": UNIT,
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms / args.steps, 3),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic (random-init Qwen3-4B-shape weights, random prompt, planted drafts p=0.85)",
+        "config": {
+            "workload": "BASELINE config 1: Qwen3-4B-shape DTree, prompt 256, 512 new tokens, spec 16, budget 24",
+            "decode_steps_per_generation": n_steps,
+            "mean_accepted_per_step": round(sum(accept) / n_steps, 3),
+            "tree_rows": n_nodes,
+            "fixed_point_iterations": fixed_iters,
+            "continuation_converged": bool(converged),
+            "l2": "inputs larger than L2 (8.0 GB of weights streamed per decode step)",
+            "parallelism": f"dp{world} independent-sequence replicas",
+        },
+        "e2e": {"value": round(e2e_tok_s, 2), "unit": UNIT, "h2d_bytes_per_step": PROMPT_LEN * 4,
+                "d2h_bytes_per_step": 4 + n_steps * 32 + (PROMPT_LEN + MAX_NEW) * 4},
+        "gpu_launches": launches_per_step * n_steps * args.steps,
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                     "frac": round(achieved / peaks["hbm_gbs"], 4), "traffic": traffic,
+                     "kernel": "tree-verify forward (36 layers + fused LM-head argmax), T=25, prefix 2048",
+                     "verify_ms": round(vms, 4), "algorithmic_bytes": vbytes,
+                     "verify_ms_prefix512": round(roof[PROMPT_LEN + MAX_NEW // 2][0], 4),
+                     "peak_source": f"{peaks['source']} MEASURED_PEAKS hbm_gbs (burst)"},
+        "clocks": clocks,
+    }
+    if not args.no_cpu:
+        out["cpu_baseline"] = cpu_baseline(target, session, stream, drafter, first)
+    return out
+
+
+# ---------------------------------------------------------------------- CPU
+def cpu_baseline(target, session, stream, drafter, first) -> dict:
+    """Oracle port of the reference step timed on the host cores (bounded
+    sample: decode steps of the same workload from the same prefilled prefix)."""
+    import torch
+
+    from oracle.qwen3 import Qwen3Oracle
+    from oracle.runtime import OracleDecoder
+
+    eng = session.engine
+    orc = Qwen3Oracle(target.model.weights, kv_capacity=PROMPT_LEN + 64)
+    for l in range(eng.cfg.num_hidden_layers):
+        orc.k[l][:, :PROMPT_LEN] = eng.kv_cache[l, 0, :, :PROMPT_LEN].float().cpu()
+        orc.v[l][:, :PROMPT_LEN] = eng.kv_cache[l, 1, :, :PROMPT_LEN].float().cpu()
+    orc.offset = PROMPT_LEN
+    dec = OracleDecoder(orc, seed=drafter.seed, p_correct=drafter.p_correct, continuation=stream, block_size=SPEC)
+    dec.output = list(stream[: PROMPT_LEN]) + [first]
+    dec.start = PROMPT_LEN
+    dec.acceptance = []
+    t0 = time.perf_counter()
+    steps = 0
+    while time.perf_counter() - t0 < 15.0 and steps < 4:
+        dec.dtree_step(BUDGET)
+        steps += 1
+    dt = time.perf_counter() - t0
+    toks = sum(dec.acceptance)
+    return {"value": round(toks / dt, 3), "unit": UNIT, "cores": torch.get_num_threads(), "kind": "port",
+            "sample": f"{steps} DTree decode steps (Qwen3-4B shape, T=25, prefix 256) of the same workload on the "
+                      f"fp32 oracle port (MLX unavailable)"}
+
+
+def run_reference(args, rank, world) -> dict | None:
+    """--impl reference: the oracle port of the reference step on host cores."""
+    import torch
+
+    if rank != 0:
+        return None
+    from dtree_mlx_b200.config import PRESETS
+    from dtree_mlx_b200.synthetic import random_prompt, random_qwen3_weights
+    from oracle.qwen3 import Qwen3Oracle
+    from oracle.runtime import OracleDecoder
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    cfg = PRESETS[PRESET]
+    dev = "cuda" if torch.cuda.is_available() else "cpu"
+    w = random_qwen3_weights(cfg, seed=0, device=dev).to("cpu")
+    sample_new = 16
+    orc = Qwen3Oracle(w, kv_capacity=PROMPT_LEN + 96)
+    prompt = random_prompt(PROMPT_LEN, cfg.vocab_size, seed=0)
+    # untimed: prefill + greedy continuation for the planted drafter
+    dec0 = OracleDecoder(orc, seed=1000, p_correct=0.0, continuation=None, block_size=SPEC)
+    dec0.prefill(prompt)
+    ks = [k[:, :PROMPT_LEN].clone() for k in orc.k]
+    vs = [v[:, :PROMPT_LEN].clone() for v in orc.v]
+    first = dec0.output[-1]
+    greedy = list(prompt) + [first]
+    for _ in range(sample_new + SPEC):
+        n = len(greedy)
+        mask = [[True] * n]
+        nh, _ = orc.forward_tree([greedy[-1]], [n - 1], mask, past=n - 1)
+        greedy.append(int(orc.lm_head_argmax(nh)[0]))
+
+    def one():
+        for l in range(len(orc.k)):
+            orc.k[l][:, :PROMPT_LEN] = ks[l]
+            orc.v[l][:, :PROMPT_LEN] = vs[l]
+        orc.offset = PROMPT_LEN
+        dec = OracleDecoder(orc, seed=1000, p_correct=P_CORRECT, continuation=greedy, block_size=SPEC)
+        dec.output = list(prompt) + [first]
+        dec.start = PROMPT_LEN
+        dec.acceptance = []
+        while dec.start < PROMPT_LEN + sample_new:
+            dec.dtree_step(BUDGET)
+        return min(len(dec.output), PROMPT_LEN + sample_new + 1) - PROMPT_LEN - 1
+
+    for _ in range(args.warmup):
+        one()
+    t0 = time.perf_counter()
+    toks = 0
+    for _ in range(args.steps):
+        toks += max(one(), 0)
+    dt = time.perf_counter() - t0
+    value = toks / dt
+    return {
+        "impl": "reference",
+        "metric": METRIC,
+        "value": round(value, 4),
+        "unit": UNIT,
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(dt / args.steps * 1e3, 2),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f32",
+        "data": "synthetic (random-init Qwen3-4B-shape weights, random prompt, planted drafts p=0.85)",
+        "config": {"workload": "BASELINE config 1 (Qwen3-4B-shape DTree b24), bounded sample of 16 new tokens "
+                               "per step from the 256-token prefilled prompt", "parallelism": "host cores"},
+        "cpu_baseline": {"value": round(value, 4), "unit": UNIT, "cores": torch.get_num_threads(), "kind": "port",
+                         "sample": "16 generated tokens per step (DTree, spec 16, budget 24) on the fp32 oracle "
+                                   "port of the reference step (MLX is not installable here)"},
+        "e2e": {"value": round(value, 4), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3) if args.impl == "ours" else args.warmup
+    rank, world, local, dist = dist_init()
+    try:
+        out = run_reference(args, rank, world) if args.impl == "reference" else run_ours(args, rank, world, local,
+                                                                                         dist)
+        if out is not None:
+            print(json.dumps(out), flush=True)
+    finally:
+        if dist:
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

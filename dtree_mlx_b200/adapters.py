@@ -1,0 +1,397 @@
+"""Target adapters: the plugin interface the verify path sits behind.
+
+Mirrors dtree_mlx/adapters.py: ``MLXTargetAdapter`` (:88-213) becomes
+``TargetAdapter`` with the same method names and argument meaning,
+``Qwen3TargetAdapter`` (:451-668) runs on the B200 engine, the registry
+(:671-678), ``LoadedTargetModel`` (:681-819) and ``load_target_model``
+(:822-846) keep their shapes.  Tensors are torch CUDA tensors instead of
+``mx.array``.  Unsupported families raise ``NotImplementedError`` as in the
+reference.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass, field
+from pathlib import Path
+from typing import Any
+
+import numpy as np
+import torch
+
+from . import kernels
+from .config import PRESETS, Qwen3Config
+from .engine import Qwen3Engine, chain_anc_masks, mask_to_anc, pad_rows
+from .synthetic import Qwen3Weights, random_qwen3_weights
+
+
+@dataclass
+class SyntheticQwen3:
+    """A random-init Qwen3 target resident on one GPU."""
+
+    cfg: Qwen3Config
+    weights: Qwen3Weights
+    kv_capacity: int
+    seed: int
+    engines: dict = field(default_factory=dict)
+
+    @property
+    def args(self):
+        return self.cfg
+
+
+class LayerKVCache:
+    """Per-layer view of the engine's KV cache (mlx_lm KVCache surface:
+    keys/values [1, kv_heads, capacity, head_dim], offset, trim)."""
+
+    def __init__(self, seq: "SequenceCache", layer: int):
+        self.seq = seq
+        self.layer = layer
+
+    @property
+    def keys(self):
+        return self.seq.engine.kv_cache[self.layer, 0][None]
+
+    @property
+    def values(self):
+        return self.seq.engine.kv_cache[self.layer, 1][None]
+
+    @property
+    def offset(self) -> int:
+        return self.seq.offset
+
+    @offset.setter
+    def offset(self, v: int) -> None:
+        self.seq.offset = int(v)
+
+    def trim(self, n: int) -> int:
+        n = min(self.seq.offset, int(n))
+        self.seq.offset -= n
+        return n
+
+
+class SequenceCache(list):
+    """List of LayerKVCache sharing one offset (all layers advance together)."""
+
+    def __init__(self, engine: Qwen3Engine):
+        self.engine = engine
+        self.offset = 0
+        super().__init__(LayerKVCache(self, i) for i in range(engine.cfg.num_hidden_layers))
+
+
+class TargetAdapter:
+    """Plugin interface (adapters.py:88-213)."""
+
+    family: str = "unknown"
+
+    def resolve_target_model_path(self, path_or_repo: str) -> Path:
+        return Path(path_or_repo)
+
+    def build_prompt(self, tokenizer, prompt_text: str):
+        raise NotImplementedError
+
+    def stop_token_ids(self, tokenizer) -> set[int]:
+        raise NotImplementedError
+
+    def make_cache(self, model, speculative_linear_cache: bool = False):
+        raise NotImplementedError
+
+    def embed_tokens(self, model, tokens):
+        raise NotImplementedError
+
+    def lm_head_logits(self, model, hidden_states):
+        raise NotImplementedError
+
+    def lm_head_argmax(self, model, hidden_states):
+        logits = self.lm_head_logits(model, hidden_states)
+        return torch.argmax(logits.float(), dim=-1).to(torch.int32)
+
+    def forward_with_hidden_states(self, model, inputs, cache, layer_ids, return_rollback_records: bool = False):
+        raise NotImplementedError
+
+    def forward_verifier_states(self, model, inputs, cache, layer_ids):
+        raise NotImplementedError(f"{self.family} does not expose verifier states before the LM head.")
+
+    def supports_tree_verification(self) -> bool:
+        return False
+
+    def forward_tree_with_hidden_states(self, model, inputs, cache, layer_ids, parents, position_ids,
+                                        attention_mask):
+        raise NotImplementedError(f"{self.family} does not expose explicit tree verification.")
+
+    def rewind_kv_caches(self, cache, num_tokens: int) -> None:
+        raise NotImplementedError
+
+    def cache_summary(self, cache, offset: int | None = None) -> str:
+        raise NotImplementedError
+
+    def compact_kv_caches(self, model, cache, past_length: int, keep_current_indices: list[int]) -> None:
+        raise NotImplementedError(f"{self.family} does not implement DTree cache compaction.")
+
+
+class Qwen3TargetAdapter(TargetAdapter):
+    """Qwen3 on the B200 engine (adapters.py:451-668)."""
+
+    family = "qwen3"
+
+    def __init__(self) -> None:
+        self.last_session = None
+
+    # -- engine ------------------------------------------------------------
+    def engine(self, model: SyntheticQwen3, draft=None, layer_ids=None) -> Qwen3Engine:
+        ids = tuple(sorted(layer_ids if layer_ids is not None else getattr(draft, "target_layer_ids", []) or []))
+        eng = model.engines.get(ids)
+        if eng is None:
+            # one engine (KV cache + scratch) per capture-layer set
+            for old in list(model.engines.values()):
+                old.close()
+            model.engines.clear()
+            eng = Qwen3Engine(model.weights, model.kv_capacity, layer_ids=ids)
+            model.engines[ids] = eng
+        return eng
+
+    # -- prompt / tokens ---------------------------------------------------
+    def build_prompt(self, tokenizer, prompt_text: str):
+        return torch.tensor(tokenizer.encode(prompt_text), dtype=torch.int32)
+
+    def stop_token_ids(self, tokenizer) -> set[int]:
+        return set(getattr(tokenizer, "eos_token_ids", set()))
+
+    def make_cache(self, model, speculative_linear_cache: bool = False):
+        del speculative_linear_cache
+        return SequenceCache(self.engine(model))
+
+    def embed_tokens(self, model, tokens):
+        return model.weights.embed[tokens.to(model.weights.device).long()]
+
+    # -- LM head -------------------------------------------------------------
+    def _rows(self, hidden_states):
+        h = hidden_states.reshape(-1, hidden_states.shape[-1]).to(torch.bfloat16)
+        n = h.shape[0]
+        tp = pad_rows(min(n, 128)) if n <= 128 else 128
+        return h, n, tp
+
+    def lm_head_logits(self, model, hidden_states):
+        """Tied LM head (adapters.py:489-492) with the tcgen05 GEMM, bf16 logits."""
+        h, n, _ = self._rows(hidden_states)
+        out = []
+        for s in range(0, n, 128):
+            blk = h[s : s + 128]
+            tp = pad_rows(blk.shape[0])
+            x = torch.zeros(tp, h.shape[1], dtype=torch.bfloat16, device=h.device)
+            x[: blk.shape[0]] = blk
+            out.append(kernels.linear_bf16(x, model.weights.embed)[: blk.shape[0]])
+        return torch.cat(out, 0).reshape(*hidden_states.shape[:-1], -1)
+
+    def lm_head_argmax(self, model, hidden_states):
+        """Fused LM head + argmax (adapters.py:114-118), first index on ties."""
+        h, n, _ = self._rows(hidden_states)
+        res = []
+        for s in range(0, n, 128):
+            blk = h[s : s + 128]
+            tp = pad_rows(blk.shape[0])
+            x = torch.zeros(tp, h.shape[1], dtype=torch.bfloat16, device=h.device)
+            x[: blk.shape[0]] = blk
+            res.append(kernels.lm_head_argmax(x, model.weights.embed, blk.shape[0]))
+        return torch.cat(res).reshape(hidden_states.shape[:-1])
+
+    # -- forwards -------------------------------------------------------------
+    def _forward(self, model, tokens: list[int], cache: SequenceCache, layer_ids, anc_rows=None,
+                 positions=None):
+        eng = self.engine(model, layer_ids=layer_ids)
+        if cache.engine is not eng:
+            raise ValueError("cache belongs to a different engine (capture layers changed)")
+        dev = eng.device
+        n = len(tokens)
+        state = kernels.new_state(dev, start=cache.offset)
+        post = torch.zeros(128, dtype=torch.int32, device=dev)
+        norm_rows, cap_rows = [], []
+        s = 0
+        while s < n:
+            t = min(eng.t_cap, n - s)
+            state[0] = cache.offset + s
+            toks = torch.tensor(tokens[s : s + t], dtype=torch.int32, device=dev)
+            pos = (torch.tensor(positions[s : s + t], dtype=torch.int32, device=dev) if positions is not None
+                   else torch.arange(cache.offset + s, cache.offset + s + t, dtype=torch.int32, device=dev))
+            anc = anc_rows if anc_rows is not None else chain_anc_masks(t)
+            anc_t = torch.from_numpy(np.ascontiguousarray(anc).view(np.int64)).to(dev)
+            eng.forward_tree(toks, pos, anc_t, t, state, post)
+            norm_rows.append(eng.norm_out[:t].clone())
+            cap_rows.append(eng.capture[:t, : eng.cfg.hidden_size * max(1, len(eng.layer_ids))].clone())
+            s += t
+        cache.offset += n
+        norm = torch.cat(norm_rows)[None]
+        hid = torch.cat(cap_rows)[None]
+        if not eng.layer_ids:
+            hid = hid[..., :0]
+        return norm, hid
+
+    def forward_with_hidden_states(self, model, inputs, cache, layer_ids, return_rollback_records: bool = False):
+        """adapters.py:516-533: causal forward, full logits."""
+        norm, hid = self._forward(model, [int(t) for t in inputs.reshape(-1).tolist()], cache, layer_ids)
+        logits = self.lm_head_logits(model, norm)
+        return (logits, hid, {}) if return_rollback_records else (logits, hid)
+
+    def forward_verifier_states(self, model, inputs, cache, layer_ids):
+        norm, hid = self._forward(model, [int(t) for t in inputs.reshape(-1).tolist()], cache, layer_ids)
+        return norm, hid, {}
+
+    def supports_tree_verification(self) -> bool:
+        return True
+
+    def forward_tree_with_hidden_states(self, model, inputs, cache, layer_ids, parents, position_ids,
+                                        attention_mask):
+        """adapters.py:568-597: tree rows with per-node positions and the bool
+        mask [T, P+T] (prefix columns must be all True)."""
+        del parents
+        tokens = [int(t) for t in inputs.reshape(-1).tolist()]
+        n = len(tokens)
+        if n > 128:
+            raise ValueError("at most 128 tree rows per verify")
+        mask = torch.as_tensor(attention_mask).bool().cpu().numpy()
+        past = cache.offset
+        if mask.shape != (n, past + n) or not mask[:, :past].all():
+            raise ValueError("attention_mask must be [T, P+T] with an all-visible prefix")
+        anc = mask_to_anc(mask[:, past:])
+        pos = [int(p) for p in torch.as_tensor(position_ids).reshape(-1).tolist()]
+        return self._forward(model, tokens, cache, layer_ids, anc_rows=anc, positions=pos)
+
+    def rewind_kv_caches(self, cache, num_tokens: int) -> None:
+        cache.offset = max(0, cache.offset - int(num_tokens))
+
+    def cache_summary(self, cache, offset: int | None = None) -> str:
+        off = cache.offset if offset is None and hasattr(cache, "offset") else offset
+        return " ".join(f"{i}:kv={off}" for i in range(len(cache)))
+
+    def compact_kv_caches(self, model, cache, past_length: int, keep_current_indices: list[int]) -> None:
+        """adapters.py:635-668 via dtree_kv_compact (all layers in one launch)."""
+        keep = [int(i) for i in keep_current_indices]
+        cur = cache.offset - past_length
+        if cur <= 0:
+            return
+        if not keep:
+            cache.offset = past_length
+            return
+        if len(keep) == cur:
+            return
+        eng = cache.engine
+        dev = eng.device
+        state = kernels.new_state(dev, start=past_length)
+        state[3] = len(keep)
+        acc = torch.zeros(128, dtype=torch.int32, device=dev)
+        acc[: len(keep)] = torch.tensor(keep, dtype=torch.int32)
+        kernels.kv_compact(eng.kv_cache, acc, state)
+        cache.offset = past_length + len(keep)
+
+
+class Qwen35TargetAdapter(TargetAdapter):
+    """Qwen3.5 hybrid (gated DeltaNet + gated attention) family: registered so
+    the registry matches the reference; the hybrid verify is not built yet."""
+
+    family = "qwen3_5"
+
+
+ADAPTERS: dict[str, type[TargetAdapter]] = {
+    "qwen3": Qwen3TargetAdapter,
+    "qwen3_5": Qwen35TargetAdapter,
+}
+
+
+def adapter_for_model_type(model_type: str) -> type[TargetAdapter] | None:
+    return ADAPTERS.get(model_type)
+
+
+class ByteTokenizer:
+    """Deterministic stand-in tokenizer for synthetic targets (no vocabulary
+    files are available offline): UTF-8 bytes, no stop tokens."""
+
+    eos_token_ids: set[int] = set()
+
+    def encode(self, text: str, add_special_tokens: bool = False) -> list[int]:
+        return list(text.encode("utf-8"))
+
+    def decode(self, tokens, skip_special_tokens: bool = False) -> str:
+        return bytes(int(t) % 256 for t in tokens).decode("utf-8", errors="replace")
+
+
+@dataclass
+class LoadedTargetModel:
+    """adapters.py:681-819."""
+
+    requested_model: str
+    resolved_model_path: Path
+    model: Any
+    tokenizer: Any
+    adapter: TargetAdapter
+
+    def build_prompt(self, prompt_text: str):
+        return self.adapter.build_prompt(self.tokenizer, prompt_text)
+
+    def stop_token_ids(self) -> set[int]:
+        return self.adapter.stop_token_ids(self.tokenizer)
+
+    def make_cache(self, speculative_linear_cache: bool = False):
+        return self.adapter.make_cache(self.model, speculative_linear_cache=speculative_linear_cache)
+
+    def embed_tokens(self, tokens):
+        return self.adapter.embed_tokens(self.model, tokens)
+
+    def lm_head_logits(self, hidden_states):
+        return self.adapter.lm_head_logits(self.model, hidden_states)
+
+    def lm_head_argmax(self, hidden_states):
+        return self.adapter.lm_head_argmax(self.model, hidden_states)
+
+    def forward_with_hidden_states(self, inputs, cache, layer_ids, return_rollback_records: bool = False):
+        return self.adapter.forward_with_hidden_states(self.model, inputs, cache, layer_ids,
+                                                       return_rollback_records=return_rollback_records)
+
+    def forward_verifier_states(self, inputs, cache, layer_ids):
+        return self.adapter.forward_verifier_states(self.model, inputs, cache, layer_ids)
+
+    def supports_tree_verification(self) -> bool:
+        return self.adapter.supports_tree_verification()
+
+    def forward_tree_with_hidden_states(self, inputs, cache, layer_ids, parents, position_ids, attention_mask):
+        return self.adapter.forward_tree_with_hidden_states(self.model, inputs, cache, layer_ids, parents,
+                                                            position_ids, attention_mask)
+
+    def rewind_kv_caches(self, cache, num_tokens: int) -> None:
+        self.adapter.rewind_kv_caches(cache, num_tokens)
+
+    def cache_summary(self, cache, offset: int | None = None) -> str:
+        return self.adapter.cache_summary(cache, offset=offset)
+
+    def compact_kv_caches(self, cache, past_length: int, keep_current_indices: list[int]) -> None:
+        self.adapter.compact_kv_caches(self.model, cache, past_length, keep_current_indices)
+
+
+def parse_synthetic_spec(spec: str) -> dict:
+    """``synthetic:<preset>[:seed=N][:kv=N]`` -> settings."""
+    parts = spec.split(":")
+    if parts[0] != "synthetic" or len(parts) < 2:
+        raise ValueError(f"not a synthetic model spec: {spec!r}")
+    out = {"preset": parts[1], "seed": 0, "kv": 4096}
+    for p in parts[2:]:
+        k, v = p.split("=", 1)
+        out[k] = int(v)
+    return out
+
+
+def load_target_model(path_or_repo: str, device: str = "cuda") -> LoadedTargetModel:
+    """adapters.py:822-846.  Checkpoints are not available offline; the
+    ``synthetic:<preset>`` spec builds a seeded random-init target of a
+    BASELINE shape (``qwen3-tiny``, ``qwen3-4b``)."""
+    if not str(path_or_repo).startswith("synthetic:"):
+        raise NotImplementedError(
+            f"Unsupported target {path_or_repo!r}: checkpoint loading is not implemented in this build; "
+            f"use 'synthetic:<preset>' with preset in {sorted(PRESETS)}."
+        )
+    spec = parse_synthetic_spec(path_or_repo)
+    cfg = PRESETS.get(spec["preset"])
+    if cfg is None:
+        raise NotImplementedError(f"unknown synthetic preset {spec['preset']!r}")
+    adapter_cls = adapter_for_model_type(cfg.model_type)
+    if adapter_cls is None or adapter_cls is Qwen35TargetAdapter:
+        raise NotImplementedError(f"Unsupported model_type={cfg.model_type!r}")
+    weights = random_qwen3_weights(cfg, seed=spec["seed"], device=device)
+    model = SyntheticQwen3(cfg, weights, kv_capacity=spec["kv"], seed=spec["seed"])
+    return LoadedTargetModel(path_or_repo, Path(path_or_repo), model, ByteTokenizer(), adapter_cls())

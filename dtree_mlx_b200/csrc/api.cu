@@ -1,5 +1,6 @@
 // Library-wide state: last-error string, device error word, tensor maps.
 #include <mutex>
+#include <unordered_map>
 
 #include "common.cuh"
 #include "../../include/dtree_b200.h"
@@ -51,6 +52,17 @@ int make_tmap_2d_bf16(CUtensorMap* map, const void* base, uint64_t inner, uint64
                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(kErrCuda, "cuTensorMapEncodeTiled failed: " + std::to_string(static_cast<int>(r)));
   return kOk;
+}
+
+cudaError_t ensure_smem_attr_fn(const void* kernel, int bytes) {
+  static std::mutex mu;
+  static std::unordered_map<const void*, int> done;
+  std::lock_guard<std::mutex> lock(mu);
+  auto it = done.find(kernel);
+  if (it != done.end() && it->second >= bytes) return cudaSuccess;
+  cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e == cudaSuccess) done[kernel] = bytes;
+  return e;
 }
 
 int num_sms() {

@@ -269,10 +269,13 @@ __global__ void __launch_bounds__(kAttnWarps * 32) tree_attn_kernel(AttnParams p
   }
 }
 
-// grid = n_q_heads * n_nodes rows, block = HD threads
+// grid = n_q_heads * n_nodes rows, block = HD threads.  The per-split (m, l)
+// are loaded by one thread each, the O partials with several splits in flight.
 template <int HD>
 __global__ void attn_combine_kernel(AttnParams p) {
   pdl_trigger();
+  __shared__ float s_w[64];
+  __shared__ float s_inv_l;
   const int qrow = blockIdx.x;  // head * T + t
   const int d = threadIdx.x;
   const int T = p.n_nodes;
@@ -283,18 +286,40 @@ __global__ void attn_combine_kernel(AttnParams p) {
   const int kps = attn_keys_per_split(L, p.splits);
   const int active = min(p.splits, (L + kps - 1) / kps);
   const int rows_total = p.n_q_heads * T;
-  float M = -INFINITY;
-  for (int s = 0; s < active; ++s) M = fmaxf(M, p.part_ml[(static_cast<size_t>(s) * rows_total + qrow) * 2]);
-  const float m_use = (M == -INFINITY) ? 0.0f : M;
-  float Ls = 0.0f, acc = 0.0f;
-  for (int s = 0; s < active; ++s) {
-    const size_t r = static_cast<size_t>(s) * rows_total + qrow;
-    const float w = exp2f(p.part_ml[r * 2] - m_use);
-    Ls += w * p.part_ml[r * 2 + 1];
-    acc += w * p.part_o[r * HD + d];
+  if (d < 32) {
+    float m = -INFINITY, l = 0.0f;
+    if (d < active) {
+      const size_t r = static_cast<size_t>(d) * rows_total + qrow;
+      m = p.part_ml[r * 2];
+      l = p.part_ml[r * 2 + 1];
+    }
+    float M = m;
+    for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+    const float m_use = (M == -INFINITY) ? 0.0f : M;
+    const float w = (d < active) ? exp2f(m - m_use) : 0.0f;
+    float wl = w * l;
+    // fixed-order (split 0, 1, ...) sum of the weights: deterministic
+    float Ls = 0.0f;
+    for (int s = 0; s < active; ++s) Ls += __shfl_sync(0xffffffffu, wl, s);
+    s_w[d] = w;
+    if (d == 0) s_inv_l = Ls > 0.0f ? 1.0f / Ls : 0.0f;
   }
-  const float outv = Ls > 0.0f ? acc / Ls : 0.0f;
-  p.out[static_cast<size_t>(t) * p.ldq + head * HD + d] = __float2bfloat16_rn(outv);
+  __syncthreads();
+  float acc = 0.0f;
+  int s = 0;
+  for (; s + 3 < active; s += 4) {
+    const size_t r = static_cast<size_t>(s) * rows_total + qrow;
+    const float o0 = p.part_o[r * HD + d];
+    const float o1 = p.part_o[(r + rows_total) * HD + d];
+    const float o2 = p.part_o[(r + 2 * rows_total) * HD + d];
+    const float o3 = p.part_o[(r + 3 * rows_total) * HD + d];
+    acc += s_w[s] * o0;
+    acc += s_w[s + 1] * o1;
+    acc += s_w[s + 2] * o2;
+    acc += s_w[s + 3] * o3;
+  }
+  for (; s < active; ++s) acc += s_w[s] * p.part_o[(static_cast<size_t>(s) * rows_total + qrow) * HD + d];
+  p.out[static_cast<size_t>(t) * p.ldq + head * HD + d] = __float2bfloat16_rn(acc * s_inv_l);
 }
 
 size_t attn_ws_bytes(int n_q_heads, int t_pad, int head_dim, int splits) {
@@ -328,12 +353,12 @@ int attn_launch(const AttnParams& p0, int head_dim, void* ws, size_t ws_bytes, c
   dim3 grid(p.splits, rb, p.n_kv_heads);
   if (head_dim == 128) {
     const int smem = AttnCfg<128>::kSmem;
-    DTREE_CUDA_RET(cudaFuncSetAttribute(tree_attn_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    DTREE_CUDA_RET(ensure_smem_attr(tree_attn_kernel<128>, smem));
     DTREE_CUDA_RET(launch_pdl(tree_attn_kernel<128>, grid, dim3(kAttnWarps * 32), static_cast<size_t>(smem), stream, p));
     DTREE_CUDA_RET(launch_pdl(attn_combine_kernel<128>, dim3(p.n_q_heads * p.n_nodes), dim3(128), 0, stream, p));
   } else {
     const int smem = AttnCfg<64>::kSmem;
-    DTREE_CUDA_RET(cudaFuncSetAttribute(tree_attn_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    DTREE_CUDA_RET(ensure_smem_attr(tree_attn_kernel<64>, smem));
     DTREE_CUDA_RET(launch_pdl(tree_attn_kernel<64>, grid, dim3(kAttnWarps * 32), static_cast<size_t>(smem), stream, p));
     DTREE_CUDA_RET(launch_pdl(attn_combine_kernel<64>, dim3(p.n_q_heads * p.n_nodes), dim3(64), 0, stream, p));
   }

@@ -216,6 +216,15 @@ cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t s
   return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 
+// Opt a kernel into `bytes` of dynamic shared memory once per process (the
+// library drives one device per process), so that launches recorded into a
+// CUDA graph are plain launches.  Keyed by the kernel's address.
+cudaError_t ensure_smem_attr_fn(const void* kernel, int bytes);
+template <typename K>
+cudaError_t ensure_smem_attr(K kernel, int bytes) {
+  return ensure_smem_attr_fn(reinterpret_cast<const void*>(kernel), bytes);
+}
+
 // ---------------------------------------------------------------- host
 // cuTensorMapEncodeTiled via the runtime's driver entry point (no -lcuda)
 int make_tmap_2d_bf16(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer, uint64_t row_stride_bytes,

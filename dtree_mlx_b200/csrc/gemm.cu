@@ -5,9 +5,12 @@
 
 namespace dtree {
 
-// workspace: [partials grid*2*t_pad*128 f32][tile counters][argmax keys][done]
+// workspace: [tile counters][argmax keys][done][partials grid*2*t_pad*128 f32]
+// The counters sit at fixed offsets so every plan bound to the same workspace
+// (any grid, any t_pad) shares them; each fix-up resets its counter to zero.
 constexpr int kMaxTileCounters = 8192;
 constexpr int kMaxArgmaxRows = 256;
+constexpr size_t kCountersBytes = kMaxTileCounters * 4 + kMaxArgmaxRows * 8 + 256;
 
 struct GemmWs {
   float* partials;
@@ -20,20 +23,15 @@ static size_t ws_partial_bytes(int t_pad, int grid) {
   return (static_cast<size_t>(grid) * 2 * t_pad * 128 * 4 + 255) & ~static_cast<size_t>(255);
 }
 
-size_t gemm_ws_bytes(int t_pad, int grid) {
-  return ws_partial_bytes(t_pad, grid) + kMaxTileCounters * 4 + kMaxArgmaxRows * 8 + 256;
-}
+size_t gemm_ws_bytes(int t_pad, int grid) { return kCountersBytes + ws_partial_bytes(t_pad, grid); }
 
-static GemmWs ws_split(void* base, int t_pad, int grid) {
+static GemmWs ws_split(void* base) {
   GemmWs w;
   char* b = static_cast<char*>(base);
-  w.partials = reinterpret_cast<float*>(b);
-  b += ws_partial_bytes(t_pad, grid);
   w.tile_cnt = reinterpret_cast<uint32_t*>(b);
-  b += kMaxTileCounters * 4;
-  w.keys = reinterpret_cast<unsigned long long*>(b);
-  b += kMaxArgmaxRows * 8;
-  w.done = reinterpret_cast<uint32_t*>(b);
+  w.keys = reinterpret_cast<unsigned long long*>(b + kMaxTileCounters * 4);
+  w.done = reinterpret_cast<uint32_t*>(b + kMaxTileCounters * 4 + kMaxArgmaxRows * 8);
+  w.partials = reinterpret_cast<float*>(b + kCountersBytes);
   return w;
 }
 
@@ -59,8 +57,22 @@ int gemm_plan(GemmPlan* plan, const void* w, int n_out, int k, const void* x, in
   p.m_tiles = m_tiles;
   p.n_rows = t_pad;
   const long long units = static_cast<long long>(m_tiles) * p.kb;
-  const int sms = grid > 0 ? grid : num_sms();
-  p.grid = static_cast<int>(units < sms ? units : sms);
+  const int sms = num_sms();
+  if (epi == kEpiPartial) {
+    // tile-aligned split-K: the consumer sums the fp32 partials
+    int split = grid > 0 ? grid : sms / m_tiles;
+    if (split < 1) split = 1;
+    if (split > p.kb) split = p.kb;
+    p.split = split;
+    p.grid = m_tiles * split;
+  } else if (grid > 0) {
+    p.grid = static_cast<int>(units < grid ? units : grid);
+  } else if (m_tiles >= (sms * 9) / 10 && m_tiles <= (sms * 5) / 4) {
+    p.grid = m_tiles;  // about one whole tile per CTA: no partial tiles at all
+  } else {
+    p.grid = static_cast<int>(units < sms ? units : sms);
+  }
+  DTREE_CHECK_ARG(units * p.grid < (1ll << 31), "stream-K index range exceeds 32 bits");
   plan->t_pad = t_pad;
   plan->epi = epi;
   return kOk;
@@ -68,7 +80,7 @@ int gemm_plan(GemmPlan* plan, const void* w, int n_out, int k, const void* x, in
 
 int gemm_bind_ws(GemmPlan* plan, void* ws, size_t ws_bytes) {
   DTREE_CHECK_ARG(ws != nullptr && ws_bytes >= gemm_ws_bytes(plan->t_pad, plan->p.grid), "GEMM workspace too small");
-  GemmWs w = ws_split(ws, plan->t_pad, plan->p.grid);
+  GemmWs w = ws_split(ws);
   plan->p.ws = w.partials;
   plan->p.tile_cnt = w.tile_cnt;
   plan->p.argmax_keys = w.keys;
@@ -80,7 +92,7 @@ template <int TPAD, int EPI>
 static int launch_t(const GemmPlan& pl, cudaStream_t st) {
   using C = GemmCfg<TPAD, EPI>;
   auto kern = gemm_streamk_kernel<TPAD, EPI>;
-  DTREE_CUDA_RET(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem));
+  DTREE_CUDA_RET(ensure_smem_attr(kern, C::kSmem));
   DTREE_CUDA_RET(launch_pdl(kern, dim3(pl.p.grid), dim3(kGemmThreads), static_cast<size_t>(C::kSmem), st,
                             pl.tmap_w, pl.tmap_x, pl.p));
   return kOk;
@@ -94,6 +106,7 @@ static int launch_epi(const GemmPlan& pl, cudaStream_t st) {
     case kEpiSwiglu: return launch_t<TPAD, kEpiSwiglu>(pl, st);
     case kEpiQkv: return launch_t<TPAD, kEpiQkv>(pl, st);
     case kEpiArgmax: return launch_t<TPAD, kEpiArgmax>(pl, st);
+    case kEpiPartial: return launch_t<TPAD, kEpiPartial>(pl, st);
   }
   return fail(kErrInvalidArg, "unknown epilogue");
 }
@@ -114,7 +127,7 @@ using namespace dtree;
 
 extern "C" size_t dtree_linear_workspace_bytes(int t_pad, int n) {
   (void)n;
-  return gemm_ws_bytes(t_pad, num_sms());
+  return gemm_ws_bytes(t_pad, 2 * num_sms());
 }
 
 extern "C" int dtree_linear_bf16(const void* x, int t_pad, int k, const void* w, int n, void* y, void* workspace,
@@ -130,7 +143,7 @@ extern "C" int dtree_linear_bf16(const void* x, int t_pad, int k, const void* w,
   return gemm_launch(plan, static_cast<cudaStream_t>(stream));
 }
 
-extern "C" size_t dtree_lm_head_workspace_bytes(int t_pad) { return gemm_ws_bytes(t_pad, num_sms()); }
+extern "C" size_t dtree_lm_head_workspace_bytes(int t_pad) { return gemm_ws_bytes(t_pad, 2 * num_sms()); }
 
 extern "C" int dtree_lm_head_argmax(const void* h, int t_pad, int n_rows, int hidden, const void* embed, int vocab,
                                     int32_t* out, void* workspace, size_t workspace_bytes, void* stream) {

@@ -29,6 +29,7 @@ enum Epi : int {
   kEpiSwiglu = 2,    // rows g(64) | u(64) per tile -> act[t*ldo + j] = silu(g)*u
   kEpiQkv = 3,       // q/k RMSNorm + RoPE -> q buffer / K cache; v -> V cache
   kEpiArgmax = 4,    // per-row argmax over n (LM head), ties -> smallest n
+  kEpiPartial = 5,   // split-K: fp32 partial of split s -> out_f32[(s*TPAD + t)*ldo + n]
 };
 
 struct GemmParams {
@@ -36,7 +37,9 @@ struct GemmParams {
   int kb;      // K / 64
   int m_tiles; // ceil(n_out / 128)
   int n_rows;  // valid tree rows (<= TPAD)
-  int grid;    // CTAs (stream-K ranges)
+  int grid;    // CTAs (stream-K ranges, or m_tiles * split)
+  int split;   // > 0: tile-aligned split-K (CTA c -> tile c / split, split c % split); 0: stream-K
+  float* out_f32;  // kEpiPartial output [split][TPAD][ldo]
   float* ws;            // [grid][2][TPAD][128] fp32 partial tiles
   uint32_t* tile_cnt;   // [m_tiles] arrival counters (zero between launches)
   // store / residual / swiglu
@@ -70,8 +73,10 @@ template <int TPAD, int EPI>
 struct GemmCfg {
   static constexpr int kXBytes = TPAD * 64 * 2;
   static constexpr int kStageBytes = kWTileBytes + kXBytes;
-  static constexpr int kXchBytes = (EPI == kEpiQkv || EPI == kEpiSwiglu) ? 128 * TPAD * 4 : 0;
-  static constexpr int kRedBytes = (EPI == kEpiQkv) ? 4 * TPAD * 4 : (EPI == kEpiArgmax ? 4 * TPAD * 8 + TPAD * 8 : 0);
+  static constexpr int kXchBytes = (EPI == kEpiQkv || EPI == kEpiSwiglu) ? 128 * 8 * 4 : 0;
+  // [0,256): per-warp reductions of one 8-row chunk; then s_best / s_pos
+  // [TPAD] (8 B each) and the argmax chunk keys [4][8] (8 B each)
+  static constexpr int kRedBytes = 256 + TPAD * 8 + 4 * 8 * 8;
   // keep a CTA within ~half an SM's shared memory so the next kernel's CTA
   // (launched early by PDL) can be resident and prefetch its weights
   static constexpr int kBudget = 110 * 1024;
@@ -84,10 +89,12 @@ struct GemmCfg {
 };
 
 // first unit of CTA c (floor(c * U / G))
-__device__ __forceinline__ long long sk_u0(int c, long long U, int G) { return (static_cast<long long>(c) * U) / G; }
+__device__ __forceinline__ long long sk_u0(int c, long long U, int G) {
+  return static_cast<long long>((static_cast<unsigned>(c) * static_cast<unsigned>(U)) / static_cast<unsigned>(G));
+}
 // CTA containing unit u
 __device__ __forceinline__ int sk_cta_of(long long u, long long U, int G) {
-  return static_cast<int>(((u + 1) * G - 1) / U);
+  return static_cast<int>((static_cast<unsigned>(u + 1) * static_cast<unsigned>(G) - 1u) / static_cast<unsigned>(U));
 }
 
 __device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
@@ -115,7 +122,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   const int G = p.grid;
   const long long U = static_cast<long long>(p.m_tiles) * p.kb;
   const int cta = blockIdx.x;
-  const long long u0 = sk_u0(cta, U, G), u1 = sk_u0(cta + 1, U, G);
+  long long u0, u1;
+  if (p.split > 0) {  // tile-aligned split-K: one segment per CTA
+    const int tile = cta / p.split, sp = cta % p.split;
+    u0 = static_cast<long long>(tile) * p.kb + (sp * p.kb) / p.split;
+    u1 = static_cast<long long>(tile) * p.kb + ((sp + 1) * p.kb) / p.split;
+  } else {
+    u0 = sk_u0(cta, U, G);
+    u1 = sk_u0(cta + 1, U, G);
+  }
   const int n_units = static_cast<int>(u1 - u0);
 
   if (warp == 0) {
@@ -213,18 +228,25 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
   } else {
     // ------------------------------------------------------------ epilogue
+    // Processes the 128 x TPAD accumulator in chunks of 8 tree rows (TMEM
+    // columns) in a rolled loop: the code stays small and hot in the
+    // instruction cache although it runs only once or twice per tile.
     const int q = warp & 3;            // TMEM lane quarter
     const int row = q * 32 + lane;     // row of the 128-row tile
     const int et = threadIdx.x - 64;   // 0..127 epilogue thread id
     pdl_wait();
-    float* red = reinterpret_cast<float*>(red_raw);
-    unsigned long long* s_best = reinterpret_cast<unsigned long long*>(red_raw + 4 * TPAD * 8);
+    float* red = reinterpret_cast<float*>(red_raw);                                   // [4][8]
+    unsigned long long* s_best = reinterpret_cast<unsigned long long*>(red_raw + 256);  // argmax [TPAD]
+    float* s_pos = reinterpret_cast<float*>(red_raw + 256);                           // qkv    [TPAD]
+    int start = 0;
     if constexpr (EPI == kEpiArgmax) {
       for (int t = et; t < TPAD; t += 128) s_best[t] = 0ull;
-      epi_bar();
     }
-    int start = 0;
-    if constexpr (EPI == kEpiQkv) start = p.state ? p.state->start : 0;
+    if constexpr (EPI == kEpiQkv) {
+      start = p.state ? p.state->start : 0;
+      for (int t = et; t < TPAD; t += 128) s_pos[t] = t < p.n_rows ? static_cast<float>(p.positions[t]) : 0.0f;
+    }
+    epi_bar();
     long long u = u0;
     int seg = 0;
     const int first_tile = static_cast<int>(u0 / p.kb);
@@ -232,35 +254,32 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const int tile = static_cast<int>(u / p.kb);
       const int kblk0 = static_cast<int>(u % p.kb);
       const int len = static_cast<int>(min(static_cast<long long>(p.kb - kblk0), u1 - u));
-      const bool full = (kblk0 == 0) && (len == p.kb);
+      const bool full = (kblk0 == 0 && len == p.kb) || EPI == kEpiPartial;
       const int b = seg & 1;
       const int use = seg >> 1;
       mbar_wait(&tfull_bar[b], static_cast<uint32_t>(use) & 1u, 5);
       tc_fence_after();
-      float acc[TPAD];
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(b * TPAD);
-#pragma unroll
-      for (int c = 0; c < TPAD; c += 8) {
-        uint32_t r[8];
-        tmem_ld_x8(taddr + c, r);
-#pragma unroll
-        for (int j = 0; j < 8; ++j) acc[c + j] = __uint_as_float(r[j]);
-      }
-      tmem_wait_ld();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&tempty_bar[b]);
 
       bool have = true;
+      int c_first = cta, c_last = cta;
       if (!full) {
+        // this CTA holds part of the tile's K range: publish the partial
         const int which = (tile == first_tile) ? 0 : 1;
         float* slot = p.ws + (static_cast<size_t>(cta) * 2 + which) * TPAD * 128;
+#pragma unroll 1
+        for (int c0 = 0; c0 < TPAD; c0 += 8) {
+          uint32_t r[8];
+          tmem_ld_x8(taddr + c0, r);
+          tmem_wait_ld();
 #pragma unroll
-        for (int t = 0; t < TPAD; ++t) slot[t * 128 + row] = acc[t];
+          for (int j = 0; j < 8; ++j) slot[(c0 + j) * 128 + row] = __uint_as_float(r[j]);
+        }
         __threadfence();
         epi_bar();
         const long long tu0 = static_cast<long long>(tile) * p.kb, tu1 = tu0 + p.kb - 1;
-        const int c_first = sk_cta_of(tu0, U, G), c_last = sk_cta_of(tu1, U, G);
+        c_first = sk_cta_of(tu0, U, G);
+        c_last = sk_cta_of(tu1, U, G);
         if (et == 0) {
           const uint32_t prev = atomicAdd(&p.tile_cnt[tile], 1u);
           *s_flag = (prev == static_cast<uint32_t>(c_last - c_first)) ? 1 : 0;
@@ -269,153 +288,193 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         have = (*s_flag != 0);
         if (have) {
           __threadfence();
-#pragma unroll
-          for (int t = 0; t < TPAD; ++t) acc[t] = 0.0f;
-          for (int c = c_first; c <= c_last; ++c) {
-            const int w2 = (tile == static_cast<int>(sk_u0(c, U, G) / p.kb)) ? 0 : 1;
-            const float* sl = p.ws + (static_cast<size_t>(c) * 2 + w2) * TPAD * 128;
-#pragma unroll
-            for (int t = 0; t < TPAD; ++t) acc[t] += __ldcg(&sl[t * 128 + row]);
-          }
           if (et == 0) p.tile_cnt[tile] = 0u;
         }
-        epi_bar();
       }
       if (have) {
         const int n = tile * 128 + row;
-        if constexpr (EPI == kEpiStore) {
-          if (n < p.n_out) {
+#pragma unroll 1
+        for (int c0 = 0; c0 < TPAD; c0 += 8) {
+          float a[8];
+          if (full) {
+            uint32_t r[8];
+            tmem_ld_x8(taddr + c0, r);
+            tmem_wait_ld();
 #pragma unroll
-            for (int t = 0; t < TPAD; ++t)
-              p.out[static_cast<size_t>(t) * p.ldo + n] = __float2bfloat16_rn(t < p.n_rows ? acc[t] : 0.0f);
-          }
-        } else if constexpr (EPI == kEpiResidual) {
-          if (n < p.n_out) {
-#pragma unroll
-            for (int t = 0; t < TPAD; ++t) {
-              __nv_bfloat16* hp = p.out + static_cast<size_t>(t) * p.ldo + n;
-              if (t < p.n_rows) {
-                const float y = bf16_round(acc[t]);
-                const __nv_bfloat16 hn = __float2bfloat16_rn(__bfloat162float(*hp) + y);
-                *hp = hn;
-                if (p.capture) p.capture[static_cast<size_t>(t) * p.ldc + n] = hn;
-              } else {
-                *hp = __float2bfloat16_rn(0.0f);
-              }
-            }
-          }
-        } else if constexpr (EPI == kEpiSwiglu) {
-          if (row >= 64) {
-#pragma unroll
-            for (int t = 0; t < TPAD; ++t) xch[(row - 64) * TPAD + t] = acc[t];
-          }
-          epi_bar();
-          if (row < 64) {
-            const int j = tile * 64 + row;
-#pragma unroll
-            for (int t = 0; t < TPAD; ++t) {
-              const float g = bf16_round(acc[t]);
-              const float uu = bf16_round(xch[row * TPAD + t]);
-              const float sg = bf16_round(1.0f / (1.0f + expf(-g)));
-              const float sl = bf16_round(g * sg);
-              p.out[static_cast<size_t>(t) * p.ldo + j] = __float2bfloat16_rn(t < p.n_rows ? sl * uu : 0.0f);
-            }
-          }
-          epi_bar();
-        } else if constexpr (EPI == kEpiQkv) {
-          const int hd = p.head_dim;
-          const int gh = n / hd;   // global head index across q | k | v
-          const int d = n % hd;
-          if (gh >= p.n_q_heads + p.n_kv_heads) {
-            // v head: straight into the V cache
-            const int kvh = gh - p.n_q_heads - p.n_kv_heads;
-#pragma unroll
-            for (int t = 0; t < TPAD; ++t) {
-              if (t < p.n_rows) {
-                const int slot = start + t;
-                if (slot < p.kv_cap)
-                  p.v_cache[(static_cast<size_t>(kvh) * p.kv_cap + slot) * hd + d] = __float2bfloat16_rn(acc[t]);
-                else
-                  dev_error(0x2001u);
-              }
-            }
+            for (int j = 0; j < 8; ++j) a[j] = __uint_as_float(r[j]);
           } else {
-            // RMSNorm over the head (hd rows spread over hd/32 warps), then RoPE
+            // sum the partials in CTA order (deterministic), 8 in flight
 #pragma unroll
-            for (int t = 0; t < TPAD; ++t) {
-              acc[t] = bf16_round(acc[t]);
-              float v = acc[t] * acc[t];
-              for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-              if (lane == 0) red[q * TPAD + t] = v;
-            }
-            epi_bar();
-            const int wph = hd / 32;  // warps per head
-            const int w0 = (q / wph) * wph;
-            const float nw = __bfloat162float((gh < p.n_q_heads ? p.q_norm : p.k_norm)[d]);
+            for (int j = 0; j < 8; ++j) a[j] = 0.0f;
+            for (int c = c_first; c <= c_last; c += 8) {
+              float v[8][8];
 #pragma unroll
-            for (int t = 0; t < TPAD; ++t) {
-              float ss = 0.0f;
-              for (int w = w0; w < w0 + wph; ++w) ss += red[w * TPAD + t];
-              const float rms = rsqrtf(ss / static_cast<float>(hd) + p.eps);
-              acc[t] = bf16_round(acc[t] * rms * nw);
-              xch[row * TPAD + t] = acc[t];
-            }
-            epi_bar();
-            const int half = hd / 2;
-            const int i_f = d % half;
-            const float inv_freq = exp2f(-(2.0f * static_cast<float>(i_f) / static_cast<float>(hd)) * p.rope_log2_theta);
-            const int partner = (d < half) ? row + half : row - half;
-            const bool is_q = gh < p.n_q_heads;
-            const int kvh = gh - p.n_q_heads;
+              for (int i = 0; i < 8; ++i) {
+                if (c + i <= c_last) {
+                  const int w2 = (tile == static_cast<int>(sk_u0(c + i, U, G) / p.kb)) ? 0 : 1;
+                  const float* sl = p.ws + (static_cast<size_t>(c + i) * 2 + w2) * TPAD * 128 + c0 * 128 + row;
 #pragma unroll
-            for (int t = 0; t < TPAD; ++t) {
-              float outv = 0.0f;
-              if (t < p.n_rows) {
-                const float pos = static_cast<float>(p.positions[t]);
-                float sn, cs;
-                sincosf(pos * inv_freq, &sn, &cs);
-                const float y = acc[t], yp = xch[partner * TPAD + t];
-                outv = (d < half) ? (y * cs - yp * sn) : (y * cs + yp * sn);
+                  for (int j = 0; j < 8; ++j) v[i][j] = __ldcg(sl + j * 128);
+                }
               }
-              if (is_q) {
-                p.q_out[static_cast<size_t>(t) * p.ldq + gh * hd + d] = __float2bfloat16_rn(outv);
-              } else if (t < p.n_rows) {
-                const int slot = start + t;
-                if (slot < p.kv_cap)
-                  p.k_cache[(static_cast<size_t>(kvh) * p.kv_cap + slot) * hd + d] = __float2bfloat16_rn(outv);
-                else
-                  dev_error(0x2001u);
+#pragma unroll
+              for (int i = 0; i < 8; ++i)
+                if (c + i <= c_last) {
+#pragma unroll
+                  for (int j = 0; j < 8; ++j) a[j] += v[i][j];
+                }
+            }
+          }
+          if constexpr (EPI == kEpiPartial) {
+            if (n < p.n_out) {
+              float* o = p.out_f32 + static_cast<size_t>(cta % p.split) * TPAD * p.ldo + n;
+#pragma unroll
+              for (int j = 0; j < 8; ++j) o[static_cast<size_t>(c0 + j) * p.ldo] = a[j];
+            }
+          } else if constexpr (EPI == kEpiStore) {
+            if (n < p.n_out) {
+#pragma unroll
+              for (int j = 0; j < 8; ++j) {
+                const int t = c0 + j;
+                p.out[static_cast<size_t>(t) * p.ldo + n] = __float2bfloat16_rn(t < p.n_rows ? a[j] : 0.0f);
               }
             }
+          } else if constexpr (EPI == kEpiResidual) {
+            if (n < p.n_out) {
+              __nv_bfloat16 hv[8];
+#pragma unroll
+              for (int j = 0; j < 8; ++j) {
+                const int t = c0 + j;
+                hv[j] = t < p.n_rows ? p.out[static_cast<size_t>(t) * p.ldo + n] : __float2bfloat16_rn(0.0f);
+              }
+#pragma unroll
+              for (int j = 0; j < 8; ++j) {
+                const int t = c0 + j;
+                __nv_bfloat16 hn = __float2bfloat16_rn(0.0f);
+                if (t < p.n_rows) hn = __float2bfloat16_rn(__bfloat162float(hv[j]) + bf16_round(a[j]));
+                p.out[static_cast<size_t>(t) * p.ldo + n] = hn;
+                if (p.capture && t < p.n_rows) p.capture[static_cast<size_t>(t) * p.ldc + n] = hn;
+              }
+            }
+          } else if constexpr (EPI == kEpiSwiglu) {
+            if (row >= 64) {
+#pragma unroll
+              for (int j = 0; j < 8; ++j) xch[j * 128 + row] = a[j];
+            }
+            epi_bar();
+            if (row < 64) {
+              const int jf = tile * 64 + row;
+#pragma unroll
+              for (int j = 0; j < 8; ++j) {
+                const int t = c0 + j;
+                const float g = bf16_round(a[j]);
+                const float uu = bf16_round(xch[j * 128 + row + 64]);
+                const float sg = bf16_round(1.0f / (1.0f + expf(-g)));
+                const float sl = bf16_round(g * sg);
+                p.out[static_cast<size_t>(t) * p.ldo + jf] = __float2bfloat16_rn(t < p.n_rows ? sl * uu : 0.0f);
+              }
+            }
+            epi_bar();
+          } else if constexpr (EPI == kEpiQkv) {
+            const int hd = p.head_dim;
+            const int gh = n / hd;  // global head index across q | k | v
+            const int d = n % hd;
+            if (gh >= p.n_q_heads + p.n_kv_heads) {
+              const int kvh = gh - p.n_q_heads - p.n_kv_heads;
+#pragma unroll
+              for (int j = 0; j < 8; ++j) {
+                const int t = c0 + j;
+                if (t < p.n_rows) {
+                  const int slot = start + t;
+                  if (slot < p.kv_cap)
+                    p.v_cache[(static_cast<size_t>(kvh) * p.kv_cap + slot) * hd + d] = __float2bfloat16_rn(a[j]);
+                  else
+                    dev_error(0x2001u);
+                }
+              }
+            } else {
+              // RMSNorm over the head (hd rows = hd/32 warps), then RoPE
+#pragma unroll
+              for (int j = 0; j < 8; ++j) {
+                a[j] = bf16_round(a[j]);
+                float v = a[j] * a[j];
+                for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+                if (lane == 0) red[q * 8 + j] = v;
+              }
+              epi_bar();
+              const int wph = hd / 32;
+              const int w0 = (q / wph) * wph;
+              const float nw = __bfloat162float((gh < p.n_q_heads ? p.q_norm : p.k_norm)[d]);
+#pragma unroll
+              for (int j = 0; j < 8; ++j) {
+                float ss = 0.0f;
+                for (int w = w0; w < w0 + wph; ++w) ss += red[w * 8 + j];
+                const float rms = rsqrtf(ss / static_cast<float>(hd) + p.eps);
+                a[j] = bf16_round(a[j] * rms * nw);
+                xch[j * 128 + row] = a[j];
+              }
+              epi_bar();
+              const int half = hd / 2;
+              const int i_f = d % half;
+              const float inv_freq =
+                  exp2f(-(2.0f * static_cast<float>(i_f) / static_cast<float>(hd)) * p.rope_log2_theta);
+              const int partner = (d < half) ? row + half : row - half;
+              const bool is_q = gh < p.n_q_heads;
+              const int kvh = gh - p.n_q_heads;
+#pragma unroll
+              for (int j = 0; j < 8; ++j) {
+                const int t = c0 + j;
+                float outv = 0.0f;
+                if (t < p.n_rows) {
+                  float sn, cs;
+                  sincosf(s_pos[t] * inv_freq, &sn, &cs);
+                  const float y = a[j], yp = xch[j * 128 + partner];
+                  outv = (d < half) ? (y * cs - yp * sn) : (y * cs + yp * sn);
+                }
+                if (is_q) {
+                  p.q_out[static_cast<size_t>(t) * p.ldq + gh * hd + d] = __float2bfloat16_rn(outv);
+                } else if (t < p.n_rows) {
+                  const int slot = start + t;
+                  if (slot < p.kv_cap)
+                    p.k_cache[(static_cast<size_t>(kvh) * p.kv_cap + slot) * hd + d] = __float2bfloat16_rn(outv);
+                  else
+                    dev_error(0x2001u);
+                }
+              }
+              epi_bar();
+            }
+          } else if constexpr (EPI == kEpiArgmax) {
+            // per tree row: max over this tile's 128 vocab rows (ties -> smallest id)
+            const bool valid = n < p.vocab;
+            unsigned long long* rk = reinterpret_cast<unsigned long long*>(red_raw + 256 + TPAD * 8);  // [4][8]
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              unsigned long long key = 0ull;
+              if (valid) {
+                const float v = bf16_round(a[j]);
+                key = (static_cast<unsigned long long>(float_order_key(v)) << 32) |
+                      static_cast<unsigned long long>(0xFFFFFFFFu - static_cast<uint32_t>(n));
+              }
+              for (int o = 16; o > 0; o >>= 1) {
+                const unsigned long long ok2 = __shfl_xor_sync(0xffffffffu, key, o);
+                key = ok2 > key ? ok2 : key;
+              }
+              if (lane == 0) rk[q * 8 + j] = key;
+            }
+            epi_bar();
+            if (et < 8) {
+              unsigned long long bk = s_best[c0 + et];
+              for (int w = 0; w < 4; ++w) bk = rk[w * 8 + et] > bk ? rk[w * 8 + et] : bk;
+              s_best[c0 + et] = bk;
+            }
             epi_bar();
           }
-        } else if constexpr (EPI == kEpiArgmax) {
-          // per column (tree row t): max over this tile's 128 vocab rows
-          const bool valid = n < p.vocab;
-#pragma unroll
-          for (int t = 0; t < TPAD; ++t) {
-            unsigned long long key = 0ull;
-            if (valid) {
-              const float v = bf16_round(acc[t]);
-              key = (static_cast<unsigned long long>(float_order_key(v)) << 32) |
-                    static_cast<unsigned long long>(0xFFFFFFFFu - static_cast<uint32_t>(n));
-            }
-            for (int o = 16; o > 0; o >>= 1) {
-              const unsigned long long ok2 = __shfl_xor_sync(0xffffffffu, key, o);
-              key = ok2 > key ? ok2 : key;
-            }
-            if (lane == 0) reinterpret_cast<unsigned long long*>(red_raw)[q * TPAD + t] = key;
-          }
-          epi_bar();
-          for (int t = et; t < TPAD; t += 128) {
-            const unsigned long long* rk = reinterpret_cast<const unsigned long long*>(red_raw);
-            unsigned long long bk = s_best[t];
-            for (int w = 0; w < 4; ++w) bk = rk[w * TPAD + t] > bk ? rk[w * TPAD + t] : bk;
-            s_best[t] = bk;
-          }
-          epi_bar();
         }
       }
+      // the accumulator buffer is free once every partial / epilogue read it
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty_bar[b]);
       u += len;
       ++seg;
     }

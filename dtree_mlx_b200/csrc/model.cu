@@ -3,14 +3,21 @@
 // plus lm_head_argmax (adapters.py:114-118) as one launch sequence.
 //
 // Per layer (qwen3_tree.py:39-83):
-//   xn   = RMSNorm(h, input_norm)                       rmsnorm_kernel
-//   q,k,v= xn @ Wqkv^T; q/k RMSNorm + RoPE; k,v -> cache gemm<kEpiQkv>
+//   xn   = RMSNorm(h, input_norm)                       rmsnorm / residual_rmsnorm
+//   p    = xn @ Wqkv^T (split-K fp32 partials)          gemm<kEpiPartial>
+//   q,k,v= sum(p); q/k RMSNorm + RoPE; k,v -> cache     qkv_finish_kernel
 //   a    = softmax(q k^T / sqrt(d) + tree mask) v       tree_attn + combine
-//   h   += a @ Wo^T                                     gemm<kEpiResidual>
-//   xn   = RMSNorm(h, post_norm)                        rmsnorm_kernel
+//   p    = a @ Wo^T  (split-K fp32 partials)           gemm<kEpiPartial>
+//   h   += sum(p); xn = RMSNorm(h, post_norm)           residual_rmsnorm_kernel
 //   act  = silu(xn Wg^T) * (xn Wu^T)                    gemm<kEpiSwiglu>
-//   h   += act @ Wd^T   (+ copy to verifier_hidden)     gemm<kEpiResidual>
+//   p    = act @ Wd^T (split-K fp32 partials)           gemm<kEpiPartial>
+//   h   += sum(p) (+ copy to verifier_hidden); next layer's RMSNorm
 // then norm_out = RMSNorm(h, final_norm) and the fused LM-head argmax.
+// The hidden-width projections (N = hidden, 20 tiles at the 4B shape) are
+// split along K across ~all SMs; their partials are summed, in split order,
+// by the RMSNorm kernel that follows anyway, so the GEMM has no reduction
+// tail.
+#include <algorithm>
 #include <cmath>
 #include <vector>
 
@@ -22,8 +29,28 @@ namespace dtree {
 int rmsnorm_launch(const __nv_bfloat16* x, int ldx, const int32_t* tokens, const __nv_bfloat16* embed,
                    __nv_bfloat16* h_out, const __nv_bfloat16* w, __nv_bfloat16* y, int H, int n_rows, int t_pad,
                    float eps, cudaStream_t stream);
+int residual_rmsnorm_launch(__nv_bfloat16* h, const float* partials, int n_split, int part_rows,
+                            __nv_bfloat16* capture, int ldc, const __nv_bfloat16* w, __nv_bfloat16* xn, int H,
+                            int n_rows, int t_pad, float eps, cudaStream_t stream);
+
+struct QkvFinishParams {
+  const float* partials;
+  int split, part_rows, width;
+  int head_dim, n_q_heads, n_kv_heads;
+  const __nv_bfloat16* q_norm;
+  const __nv_bfloat16* k_norm;
+  float eps, rope_log2_theta;
+  const int32_t* positions;
+  const dtree_step_state* state;
+  __nv_bfloat16* q_out;
+  __nv_bfloat16* k_cache;
+  __nv_bfloat16* v_cache;
+  int kv_cap;
+};
+int qkv_finish_launch(const QkvFinishParams& p, int n_rows, cudaStream_t stream);
 
 constexpr int kAttnMaxSplits = 32;
+constexpr int kMaxProjSplit = 16;  // split-K of the hidden-width projections (o_proj, down_proj)
 
 static int pad_rows(int n) {
   if (n <= 16) return 16;
@@ -49,13 +76,24 @@ struct dtree_qwen3_model {
   size_t gemm_ws_bytes = 0;
   void* attn_ws = nullptr;
   size_t attn_ws_bytes = 0;
+  float* proj_partials = nullptr;  // [kMaxProjSplit][t_pad][hidden] fp32
 };
 
 namespace dtree {
 
-static size_t gemm_ws_need(const dtree_qwen3_desc& d) { return gemm_ws_bytes(pad_rows(d.t_cap), num_sms()); }
+static size_t gemm_ws_need(const dtree_qwen3_desc& d) { return gemm_ws_bytes(pad_rows(d.t_cap), 2 * num_sms()); }
 static size_t attn_ws_need(const dtree_qwen3_desc& d) {
   return attn_ws_bytes(d.n_heads, d.t_cap, d.head_dim, kAttnMaxSplits);
+}
+static int proj_split(const dtree_qwen3_desc& d, int n_out) {
+  const int tiles = (n_out + 127) / 128;
+  return std::max(1, std::min(kMaxProjSplit, num_sms() / tiles));
+}
+static int qkv_width(const dtree_qwen3_desc& d) { return (d.n_heads + 2 * d.n_kv_heads) * d.head_dim; }
+static size_t partials_need(const dtree_qwen3_desc& d) {
+  const size_t a = static_cast<size_t>(proj_split(d, d.hidden)) * d.hidden;
+  const size_t b = static_cast<size_t>(proj_split(d, qkv_width(d))) * qkv_width(d);
+  return std::max(a, b) * pad_rows(d.t_cap) * 4;
 }
 
 static int build_plans(dtree_qwen3_model* m, int t_pad) {
@@ -71,10 +109,17 @@ static int build_plans(dtree_qwen3_model* m, int t_pad) {
   for (int l = 0; l < d.layers; ++l) {
     const dtree_qwen3_layer& L = m->layers[l];
     int rc;
-    if ((rc = gemm_plan(&ps.qkv[l], L.qkv, qkv_rows, d.hidden, d.xn, t_pad, d.hidden, kEpiQkv, 0))) return rc;
-    if ((rc = gemm_plan(&ps.o[l], L.o_proj, d.hidden, qd, d.attn, t_pad, qd, kEpiResidual, 0))) return rc;
+    if ((rc = gemm_plan(&ps.qkv[l], L.qkv, qkv_rows, d.hidden, d.xn, t_pad, d.hidden, kEpiPartial,
+                        proj_split(d, qkv_rows))))
+      return rc;
+    if ((rc = gemm_plan(&ps.o[l], L.o_proj, d.hidden, qd, d.attn, t_pad, qd, kEpiPartial, proj_split(d, d.hidden))))
+      return rc;
     if ((rc = gemm_plan(&ps.gu[l], L.gate_up, 2 * d.ffn, d.hidden, d.xn, t_pad, d.hidden, kEpiSwiglu, 0))) return rc;
-    if ((rc = gemm_plan(&ps.down[l], L.down, d.hidden, d.ffn, d.act, t_pad, d.ffn, kEpiResidual, 0))) return rc;
+    if ((rc = gemm_plan(&ps.down[l], L.down, d.hidden, d.ffn, d.act, t_pad, d.ffn, kEpiPartial,
+                        proj_split(d, d.hidden))))
+      return rc;
+    if (ps.o[l].p.split > kMaxProjSplit || ps.down[l].p.split > kMaxProjSplit || ps.qkv[l].p.split > kMaxProjSplit)
+      return fail(kErrUnsupported, "projection split exceeds the partial buffer");
     for (GemmPlan* g : {&ps.qkv[l], &ps.o[l], &ps.gu[l], &ps.down[l]})
       if ((rc = gemm_bind_ws(g, m->gemm_ws, m->gemm_ws_bytes))) return rc;
   }
@@ -102,7 +147,8 @@ extern "C" int dtree_qwen3_buffer_bytes(const dtree_qwen3_desc* d, size_t out[9]
   out[5] = tc * d->ffn * 2;
   out[6] = tc * d->hidden * 2;
   out[7] = tc * d->hidden * (d->n_capture > 0 ? d->n_capture : 1) * 2;
-  out[8] = ((gemm_ws_need(*d) + 255) & ~static_cast<size_t>(255)) + attn_ws_need(*d);
+  out[8] = ((gemm_ws_need(*d) + 255) & ~static_cast<size_t>(255)) +
+           ((attn_ws_need(*d) + 255) & ~static_cast<size_t>(255)) + partials_need(*d);
   return kOk;
 }
 
@@ -133,6 +179,8 @@ extern "C" int dtree_qwen3_create(const dtree_qwen3_desc* desc, dtree_qwen3_mode
   m->gemm_ws_bytes = gemm_ws_need(d);
   m->attn_ws = static_cast<char*>(d.workspace) + ((m->gemm_ws_bytes + 255) & ~static_cast<size_t>(255));
   m->attn_ws_bytes = attn_ws_need(d);
+  m->proj_partials = reinterpret_cast<float*>(static_cast<char*>(m->attn_ws) +
+                                              ((m->attn_ws_bytes + 255) & ~static_cast<size_t>(255)));
   *out = m;
   return kOk;
 }
@@ -158,7 +206,15 @@ extern "C" int dtree_qwen3_forward_tree(dtree_qwen3_model* m, const int32_t* tre
   const size_t plane = static_cast<size_t>(d.n_kv_heads) * d.kv_capacity * d.head_dim;
   const int qd = d.n_heads * d.head_dim;
   const float log2_theta = std::log2(d.rope_theta);
+  const int qkv_rows_all = qkv_width(d);
   const int splits = std::min(kAttnMaxSplits, attn_default_splits(d.n_kv_heads, d.n_heads, n_nodes));
+  // verifier_hidden column block of layer l (nullptr if l is not captured)
+  const int ldc = d.hidden * (d.n_capture > 0 ? d.n_capture : 1);
+  auto capture_ptr = [&](int l) -> __nv_bfloat16* {
+    for (int c = 0; c < d.n_capture; ++c)
+      if (d.capture_layers[c] == l) return bw(d.capture) + static_cast<size_t>(c) * d.hidden;
+    return nullptr;
+  };
 
   // embedding gather + first input norm
   if ((rc = rmsnorm_launch(nullptr, 0, tree_tokens, bf(d.embed), bw(d.h), bf(m->layers[0].input_norm), bw(d.xn),
@@ -168,29 +224,39 @@ extern "C" int dtree_qwen3_forward_tree(dtree_qwen3_model* m, const int32_t* tre
     const dtree_qwen3_layer& L = m->layers[l];
     __nv_bfloat16* kc = bw(d.kv_cache) + (static_cast<size_t>(l) * 2 + 0) * plane;
     __nv_bfloat16* vc = bw(d.kv_cache) + (static_cast<size_t>(l) * 2 + 1) * plane;
-    if (l > 0) {
-      if ((rc = rmsnorm_launch(bf(d.h), d.hidden, nullptr, nullptr, nullptr, bf(L.input_norm), bw(d.xn), d.hidden,
-                               n_nodes, t_pad, d.rms_eps, st)))
+    if (l > 0) {  // h += down_proj(l-1) (+ capture), xn = RMSNorm(h, input_norm[l])
+      if ((rc = residual_rmsnorm_launch(bw(d.h), m->proj_partials, ps.down[l - 1].p.split, t_pad,
+                                        capture_ptr(l - 1), ldc, bf(L.input_norm), bw(d.xn), d.hidden, n_nodes,
+                                        t_pad, d.rms_eps, st)))
         return rc;
     }
-    {  // q | k | v projection with q/k norm + RoPE, K/V into the cache
+    {  // q | k | v projection: split-K fp32 partials
       GemmPlan g = ps.qkv[l];
       g.p.n_rows = n_nodes;
-      g.p.q_out = bw(d.q);
-      g.p.ldq = qd;
-      g.p.k_cache = kc;
-      g.p.v_cache = vc;
-      g.p.kv_cap = d.kv_capacity;
-      g.p.head_dim = d.head_dim;
-      g.p.n_q_heads = d.n_heads;
-      g.p.n_kv_heads = d.n_kv_heads;
-      g.p.q_norm = bf(L.q_norm);
-      g.p.k_norm = bf(L.k_norm);
-      g.p.eps = d.rms_eps;
-      g.p.rope_log2_theta = log2_theta;
-      g.p.positions = positions;
-      g.p.state = state;
+      g.p.out_f32 = m->proj_partials;
+      g.p.ldo = qkv_rows_all;
       if ((rc = gemm_launch(g, st))) return rc;
+    }
+    {  // sum partials, q/k RMSNorm + RoPE, q -> buffer, k/v -> cache slots start + t
+      QkvFinishParams f{};
+      f.partials = m->proj_partials;
+      f.split = ps.qkv[l].p.split;
+      f.part_rows = t_pad;
+      f.width = qkv_rows_all;
+      f.head_dim = d.head_dim;
+      f.n_q_heads = d.n_heads;
+      f.n_kv_heads = d.n_kv_heads;
+      f.q_norm = bf(L.q_norm);
+      f.k_norm = bf(L.k_norm);
+      f.eps = d.rms_eps;
+      f.rope_log2_theta = log2_theta;
+      f.positions = positions;
+      f.state = state;
+      f.q_out = bw(d.q);
+      f.k_cache = kc;
+      f.v_cache = vc;
+      f.kv_cap = d.kv_capacity;
+      if ((rc = qkv_finish_launch(f, n_nodes, st))) return rc;
     }
     {  // tree attention
       AttnParams a{};
@@ -209,16 +275,16 @@ extern "C" int dtree_qwen3_forward_tree(dtree_qwen3_model* m, const int32_t* tre
       a.out = bw(d.attn);
       if ((rc = attn_launch(a, d.head_dim, m->attn_ws, m->attn_ws_bytes, st))) return rc;
     }
-    {  // o_proj + residual
+    {  // o_proj split-K partials
       GemmPlan g = ps.o[l];
       g.p.n_rows = n_nodes;
-      g.p.out = bw(d.h);
+      g.p.out_f32 = m->proj_partials;
       g.p.ldo = d.hidden;
-      g.p.capture = nullptr;
       if ((rc = gemm_launch(g, st))) return rc;
     }
-    if ((rc = rmsnorm_launch(bf(d.h), d.hidden, nullptr, nullptr, nullptr, bf(L.post_norm), bw(d.xn), d.hidden,
-                             n_nodes, t_pad, d.rms_eps, st)))
+    // h += o_proj, xn = RMSNorm(h, post_norm)
+    if ((rc = residual_rmsnorm_launch(bw(d.h), m->proj_partials, ps.o[l].p.split, t_pad, nullptr, 0,
+                                      bf(L.post_norm), bw(d.xn), d.hidden, n_nodes, t_pad, d.rms_eps, st)))
       return rc;
     {  // gate | up + SwiGLU
       GemmPlan g = ps.gu[l];
@@ -227,23 +293,18 @@ extern "C" int dtree_qwen3_forward_tree(dtree_qwen3_model* m, const int32_t* tre
       g.p.ldo = d.ffn;
       if ((rc = gemm_launch(g, st))) return rc;
     }
-    {  // down + residual (+ verifier_hidden capture)
+    {  // down_proj split-K partials (added by the next residual_rmsnorm)
       GemmPlan g = ps.down[l];
       g.p.n_rows = n_nodes;
-      g.p.out = bw(d.h);
+      g.p.out_f32 = m->proj_partials;
       g.p.ldo = d.hidden;
-      g.p.capture = nullptr;
-      for (int c = 0; c < d.n_capture; ++c) {
-        if (d.capture_layers[c] == l) {
-          g.p.capture = bw(d.capture) + static_cast<size_t>(c) * d.hidden;
-          g.p.ldc = d.hidden * d.n_capture;
-        }
-      }
       if ((rc = gemm_launch(g, st))) return rc;
     }
   }
-  if ((rc = rmsnorm_launch(bf(d.h), d.hidden, nullptr, nullptr, nullptr, bf(d.final_norm), bw(d.norm_out), d.hidden,
-                           n_nodes, t_pad, d.rms_eps, st)))
+  // h += down_proj(L-1) (+ capture), norm_out = RMSNorm(h, final_norm)
+  if ((rc = residual_rmsnorm_launch(bw(d.h), m->proj_partials, ps.down[d.layers - 1].p.split, t_pad,
+                                    capture_ptr(d.layers - 1), ldc, bf(d.final_norm), bw(d.norm_out), d.hidden,
+                                    n_nodes, t_pad, d.rms_eps, st)))
     return rc;
   if (posterior) {
     GemmPlan g = ps.lm;

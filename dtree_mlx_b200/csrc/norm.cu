@@ -29,14 +29,40 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(const __nv_bfloat16* __res
   }
   const __nv_bfloat16* src = tokens ? embed + static_cast<size_t>(tokens[row]) * H : x + static_cast<size_t>(row) * ldx;
   const uint4* s4 = reinterpret_cast<const uint4*>(src);
+  const uint4* w4 = reinterpret_cast<const uint4*>(w);
+  // the row stays in registers between the two passes (H <= 4096: two
+  // 16-byte vectors per thread); wider rows re-read it
+  constexpr int kCache = 2;
+  uint4 cache[kCache], wcache[kCache];
   float ss = 0.0f;
-  for (int i = threadIdx.x; i < nv; i += blockDim.x) {
+#pragma unroll
+  for (int j = 0; j < kCache; ++j) {
+    const int i = threadIdx.x + j * blockDim.x;
+    if (i < nv) {
+      cache[j] = s4[i];
+      wcache[j] = w4[i];
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < kCache; ++j) {
+    const int i = threadIdx.x + j * blockDim.x;
+    if (i < nv) {
+      if (tokens && h_out) reinterpret_cast<uint4*>(h_out + static_cast<size_t>(row) * H)[i] = cache[j];
+      const __nv_bfloat162* b = reinterpret_cast<const __nv_bfloat162*>(&cache[j]);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float2 f = __bfloat1622float2(b[q]);
+        ss += f.x * f.x + f.y * f.y;
+      }
+    }
+  }
+  for (int i = threadIdx.x + kCache * blockDim.x; i < nv; i += blockDim.x) {
     const uint4 v = s4[i];
     if (tokens && h_out) reinterpret_cast<uint4*>(h_out + static_cast<size_t>(row) * H)[i] = v;
     const __nv_bfloat162* b = reinterpret_cast<const __nv_bfloat162*>(&v);
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const float2 f = __bfloat1622float2(b[j]);
+    for (int q = 0; q < 4; ++q) {
+      const float2 f = __bfloat1622float2(b[q]);
       ss += f.x * f.x + f.y * f.y;
     }
   }
@@ -46,21 +72,119 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(const __nv_bfloat16* __res
   float tot = 0.0f;
   for (int i = 0; i < (blockDim.x >> 5); ++i) tot += red[i];
   const float rs = rsqrtf(tot / static_cast<float>(H) + eps);
-  const uint4* w4 = reinterpret_cast<const uint4*>(w);
-  for (int i = threadIdx.x; i < nv; i += blockDim.x) {
-    const uint4 v = s4[i], wv = w4[i];
+  auto norm_vec = [&](const uint4& v, const uint4& wv) {
     const __nv_bfloat162* b = reinterpret_cast<const __nv_bfloat162*>(&v);
     const __nv_bfloat162* wb = reinterpret_cast<const __nv_bfloat162*>(&wv);
     uint4 o4;
     __nv_bfloat162* ob = reinterpret_cast<__nv_bfloat162*>(&o4);
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const float2 f = __bfloat1622float2(b[j]);
-      const float2 g = __bfloat1622float2(wb[j]);
-      ob[j] = __floats2bfloat162_rn(f.x * rs * g.x, f.y * rs * g.y);
+    for (int q = 0; q < 4; ++q) {
+      const float2 f = __bfloat1622float2(b[q]);
+      const float2 g = __bfloat1622float2(wb[q]);
+      ob[q] = __floats2bfloat162_rn(f.x * rs * g.x, f.y * rs * g.y);
     }
-    yrow[i] = o4;
+    return o4;
+  };
+#pragma unroll
+  for (int j = 0; j < kCache; ++j) {
+    const int i = threadIdx.x + j * blockDim.x;
+    if (i < nv) yrow[i] = norm_vec(cache[j], wcache[j]);
   }
+  for (int i = threadIdx.x + kCache * blockDim.x; i < nv; i += blockDim.x) yrow[i] = norm_vec(s4[i], w4[i]);
+}
+
+// Residual add of a split-K projection fused with the next RMSNorm:
+//   y      = bf16(sum_s partials[s][row])          (fixed split order)
+//   h[row] = bf16(h[row] + y)                      (qwen3_tree.py:78,82 residual adds)
+//   capture[row] = h[row]            (optional: verifier_hidden of this layer)
+//   xn[row] = RMSNorm(h[row], w)
+// grid = t_pad rows, block 256; H <= 4096 (two 8-wide vectors per thread).
+__global__ void __launch_bounds__(256) residual_rmsnorm_kernel(__nv_bfloat16* __restrict__ h,
+                                                               const float* __restrict__ partials, int n_split,
+                                                               int part_rows, __nv_bfloat16* __restrict__ capture,
+                                                               int ldc, const __nv_bfloat16* __restrict__ w,
+                                                               __nv_bfloat16* __restrict__ xn, int H, int n_rows,
+                                                               float eps) {
+  pdl_trigger();
+  __shared__ float red[8];
+  const int row = blockIdx.x;
+  const int nv = H / 8;
+  pdl_wait();
+  uint4* xrow = reinterpret_cast<uint4*>(xn + static_cast<size_t>(row) * H);
+  uint4* hrow = reinterpret_cast<uint4*>(h + static_cast<size_t>(row) * H);
+  if (row >= n_rows) {
+    const uint4 z = make_uint4(0, 0, 0, 0);
+    for (int i = threadIdx.x; i < nv; i += blockDim.x) {
+      xrow[i] = z;
+      hrow[i] = z;
+    }
+    return;
+  }
+  constexpr int kCache = 2;
+  uint4 hc[kCache];
+  float ss = 0.0f;
+#pragma unroll
+  for (int j = 0; j < kCache; ++j) {
+    const int i = threadIdx.x + j * blockDim.x;
+    if (i >= nv) continue;
+    float y[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) y[e] = 0.0f;
+    for (int sp = 0; sp < n_split; ++sp) {
+      const float4* pp =
+          reinterpret_cast<const float4*>(partials + (static_cast<size_t>(sp) * part_rows + row) * H) + 2 * i;
+      const float4 a = __ldcg(pp), b = __ldcg(pp + 1);
+      y[0] += a.x; y[1] += a.y; y[2] += a.z; y[3] += a.w;
+      y[4] += b.x; y[5] += b.y; y[6] += b.z; y[7] += b.w;
+    }
+    const uint4 hv = hrow[i];
+    const __nv_bfloat162* hb = reinterpret_cast<const __nv_bfloat162*>(&hv);
+    uint4 o;
+    __nv_bfloat162* ob = reinterpret_cast<__nv_bfloat162*>(&o);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const float2 f = __bfloat1622float2(hb[q]);
+      ob[q] = __floats2bfloat162_rn(f.x + bf16_round(y[2 * q]), f.y + bf16_round(y[2 * q + 1]));
+      const float2 g = __bfloat1622float2(ob[q]);
+      ss += g.x * g.x + g.y * g.y;
+    }
+    hc[j] = o;
+    hrow[i] = o;
+    if (capture) reinterpret_cast<uint4*>(capture + static_cast<size_t>(row) * ldc)[i] = o;
+  }
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  float tot = 0.0f;
+  for (int i = 0; i < (blockDim.x >> 5); ++i) tot += red[i];
+  const float rs = rsqrtf(tot / static_cast<float>(H) + eps);
+  const uint4* w4 = reinterpret_cast<const uint4*>(w);
+#pragma unroll
+  for (int j = 0; j < kCache; ++j) {
+    const int i = threadIdx.x + j * blockDim.x;
+    if (i >= nv) continue;
+    const uint4 wv = w4[i];
+    const __nv_bfloat162* b = reinterpret_cast<const __nv_bfloat162*>(&hc[j]);
+    const __nv_bfloat162* wb = reinterpret_cast<const __nv_bfloat162*>(&wv);
+    uint4 o4;
+    __nv_bfloat162* ob = reinterpret_cast<__nv_bfloat162*>(&o4);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const float2 f = __bfloat1622float2(b[q]);
+      const float2 g = __bfloat1622float2(wb[q]);
+      ob[q] = __floats2bfloat162_rn(f.x * rs * g.x, f.y * rs * g.y);
+    }
+    xrow[i] = o4;
+  }
+}
+
+int residual_rmsnorm_launch(__nv_bfloat16* h, const float* partials, int n_split, int part_rows,
+                            __nv_bfloat16* capture, int ldc, const __nv_bfloat16* w, __nv_bfloat16* xn, int H,
+                            int n_rows, int t_pad, float eps, cudaStream_t stream) {
+  DTREE_CHECK_ARG(H % 8 == 0 && H <= 4096, "hidden size must be a multiple of 8 and <= 4096");
+  DTREE_CUDA_RET(launch_pdl(residual_rmsnorm_kernel, dim3(t_pad), dim3(256), 0, stream, h, partials, n_split,
+                            part_rows, capture, ldc, w, xn, H, n_rows, eps));
+  return kOk;
 }
 
 int rmsnorm_launch(const __nv_bfloat16* x, int ldx, const int32_t* tokens, const __nv_bfloat16* embed,

@@ -1,0 +1,93 @@
+// Finish of the fused q|k|v projection (qwen3_tree.py:50-65): sums the
+// split-K fp32 partials of the QKV GEMM in split order, then per head
+//   q, k: RMSNorm over head_dim (q_norm / k_norm), half-split RoPE at the
+//         node's position, q -> q buffer, k -> K cache slot start + t
+//   v:    -> V cache slot start + t
+// grid = (n_rows, n_q_heads + 2 * n_kv_heads), block = head_dim threads.
+#include "common.cuh"
+#include "../../include/dtree_b200.h"
+
+namespace dtree {
+
+struct QkvFinishParams {
+  const float* partials;  // [split][part_rows][width]
+  int split, part_rows, width;
+  int head_dim, n_q_heads, n_kv_heads;
+  const __nv_bfloat16* q_norm;
+  const __nv_bfloat16* k_norm;
+  float eps, rope_log2_theta;
+  const int32_t* positions;
+  const dtree_step_state* state;
+  __nv_bfloat16* q_out;  // [t_pad][n_q_heads*head_dim]
+  __nv_bfloat16* k_cache;  // [n_kv_heads][kv_cap][head_dim]
+  __nv_bfloat16* v_cache;
+  int kv_cap;
+};
+
+__global__ void __launch_bounds__(256) qkv_finish_kernel(QkvFinishParams p) {
+  pdl_trigger();
+  __shared__ float s_red[8];
+  __shared__ float s_y[256];
+  const int t = blockIdx.x, gh = blockIdx.y, d = threadIdx.x;
+  const int hd = p.head_dim;
+  pdl_wait();
+  const int col = gh * hd + d;
+  float a = 0.0f;
+  {
+    const float* src = p.partials + static_cast<size_t>(t) * p.width + col;
+    const size_t stride = static_cast<size_t>(p.part_rows) * p.width;
+    int s = 0;
+    for (; s + 3 < p.split; s += 4) {
+      const float x0 = __ldcg(src + s * stride), x1 = __ldcg(src + (s + 1) * stride);
+      const float x2 = __ldcg(src + (s + 2) * stride), x3 = __ldcg(src + (s + 3) * stride);
+      a += x0;
+      a += x1;
+      a += x2;
+      a += x3;
+    }
+    for (; s < p.split; ++s) a += __ldcg(src + s * stride);
+  }
+  const int start = p.state->start;
+  const int slot = start + t;
+  if (gh >= p.n_q_heads + p.n_kv_heads) {  // v
+    const int kvh = gh - p.n_q_heads - p.n_kv_heads;
+    if (slot < p.kv_cap) p.v_cache[(static_cast<size_t>(kvh) * p.kv_cap + slot) * hd + d] = __float2bfloat16_rn(a);
+    else dev_error(0x2001u);
+    return;
+  }
+  const float x = bf16_round(a);  // projection output is bf16
+  float sq = x * x;
+  for (int o = 16; o > 0; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
+  if ((d & 31) == 0) s_red[d >> 5] = sq;
+  __syncthreads();
+  float ss = 0.0f;
+  for (int w = 0; w < hd / 32; ++w) ss += s_red[w];
+  const bool is_q = gh < p.n_q_heads;
+  const float nw = __bfloat162float((is_q ? p.q_norm : p.k_norm)[d]);
+  const float y = bf16_round(x * rsqrtf(ss / static_cast<float>(hd) + p.eps) * nw);
+  s_y[d] = y;
+  __syncthreads();
+  const int half = hd / 2;
+  const int i_f = d % half;
+  const float inv_freq = exp2f(-(2.0f * static_cast<float>(i_f) / static_cast<float>(hd)) * p.rope_log2_theta);
+  float sn, cs;
+  sincosf(static_cast<float>(p.positions[t]) * inv_freq, &sn, &cs);
+  const float yp = s_y[d < half ? d + half : d - half];
+  const float outv = (d < half) ? (y * cs - yp * sn) : (y * cs + yp * sn);
+  if (is_q) {
+    p.q_out[static_cast<size_t>(t) * (p.n_q_heads * hd) + gh * hd + d] = __float2bfloat16_rn(outv);
+  } else {
+    const int kvh = gh - p.n_q_heads;
+    if (slot < p.kv_cap) p.k_cache[(static_cast<size_t>(kvh) * p.kv_cap + slot) * hd + d] = __float2bfloat16_rn(outv);
+    else dev_error(0x2001u);
+  }
+}
+
+int qkv_finish_launch(const QkvFinishParams& p, int n_rows, cudaStream_t stream) {
+  DTREE_CHECK_ARG(p.head_dim % 32 == 0 && p.head_dim <= 256, "head_dim must be a multiple of 32, <= 256");
+  DTREE_CUDA_RET(launch_pdl(qkv_finish_kernel, dim3(n_rows, p.n_q_heads + 2 * p.n_kv_heads), dim3(p.head_dim), 0,
+                            stream, p));
+  return kOk;
+}
+
+}  // namespace dtree

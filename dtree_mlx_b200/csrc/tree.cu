@@ -55,7 +55,7 @@ __global__ void plant_draft_logits_kernel(float* __restrict__ logits, int rows, 
     const bool take = u24(c[0]) < p_correct;
     int tok = static_cast<int>(c[1] % static_cast<uint32_t>(vocab));
     const int pos = start + r + 1;
-    if (take && pos < cont_len) tok = cont[pos];
+    if (take && pos < cont_len && cont[pos] >= 0) tok = cont[pos];
     s_tok = tok;
   }
   __syncthreads();
@@ -656,7 +656,7 @@ extern "C" int dtree_tree_build(const float* draft_logits, int rows, int vocab, 
   const int chunk = (vocab + splits - 1) / splits;
   const size_t smem = static_cast<size_t>(chunk) * 4 + static_cast<size_t>(splits) * kMaxK * 8;
   DTREE_CHECK_ARG(smem <= 200 * 1024, "vocab too large for the top-k chunking");
-  DTREE_CUDA_RET(cudaFuncSetAttribute(topk_lse_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+  DTREE_CUDA_RET(ensure_smem_attr(topk_lse_kernel, 200 * 1024));
   DTREE_CUDA_RET(launch_pdl(topk_lse_kernel, dim3(splits, rows), dim3(kTopkThreads), smem, stream, draft_logits,
                             rows, vocab, k, splits, chunk, ws));
   DTREE_CUDA_RET(launch_pdl(heap_tree_kernel, dim3(1), dim3(32), 0, stream, (const int32_t*)ws.top_id,
@@ -730,8 +730,7 @@ extern "C" int dtree_kv_compact(void* kv_cache, int layers, int kv_heads, int ca
   DTREE_CHECK_ARG(layers > 0 && kv_heads > 0 && capacity > 0, "bad shape");
   DTREE_CHECK_ARG(head_dim % 8 == 0 && head_dim <= 256, "head_dim must be a multiple of 8 and <= 256");
   const size_t smem = static_cast<size_t>(DTREE_MAX_TREE) * head_dim * 2;
-  DTREE_CUDA_RET(cudaFuncSetAttribute(kv_compact_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                      static_cast<int>(smem)));
+  DTREE_CUDA_RET(ensure_smem_attr(kv_compact_kernel, static_cast<int>(smem)));
   DTREE_CUDA_RET(launch_pdl(kv_compact_kernel, dim3(layers * 2 * kv_heads), dim3(256), smem, stream,
                             static_cast<__nv_bfloat16*>(kv_cache), capacity, head_dim, accepted, state));
   return kOk;

@@ -1,0 +1,253 @@
+"""Device-resident Qwen3 verify engine and per-sequence decode sessions.
+
+``Qwen3Engine`` owns the C model handle (``dtree_qwen3_create``) and the
+activation / KV buffers it runs on (allocated once with torch, the device
+memory plumbing).  ``DecodeSession`` holds one sequence's device state
+(``dtree_step_state``, tree buffers, output tokens) and runs a whole decode
+step -- draft logits, tree build, tree-verify forward with the fused LM-head
+argmax, acceptance walk, KV compaction, commit -- as device launches with no
+host round trip; ``capture_step`` records that step into one CUDA graph.
+
+The step mirrors one iteration of dtree_generate's loop
+(dtree_mlx/dtree_runtime.py:364-552) and, with a chain tree, of
+dflash_generate's parallel-greedy-argmax verify (dtree_mlx/runtime.py:474-577).
+"""
+from __future__ import annotations
+
+import ctypes as C
+from dataclasses import dataclass
+
+import numpy as np
+import torch
+
+from . import _lib, kernels
+from ._lib import DTREE_MAX_TREE, Qwen3Desc, Qwen3Layer, call, ptr, stream_ptr
+from .config import Qwen3Config
+from .synthetic import Qwen3Weights
+
+
+def pad_rows(n: int) -> int:
+    for t in (16, 32, 64, 128):
+        if n <= t:
+            return t
+    raise ValueError(f"at most {DTREE_MAX_TREE} tree rows per forward, got {n}")
+
+
+def chain_anc_masks(n: int) -> np.ndarray:
+    """Causal (chain) visibility as packed bits: row i sees nodes 0..i."""
+    out = np.zeros((n, 2), dtype=np.uint64)
+    for i in range(n):
+        lo = min(i, 63)
+        out[i, 0] = np.uint64((1 << (lo + 1)) - 1) if lo < 63 else np.uint64(0xFFFFFFFFFFFFFFFF)
+        if i >= 64:
+            hi = i - 64
+            out[i, 1] = np.uint64((1 << (hi + 1)) - 1) if hi < 63 else np.uint64(0xFFFFFFFFFFFFFFFF)
+    return out
+
+
+def mask_to_anc(visibility: np.ndarray) -> np.ndarray:
+    """Bool visibility [T, T] -> packed ancestor bits [T, 2] (uint64)."""
+    t = visibility.shape[0]
+    out = np.zeros((t, 2), dtype=np.uint64)
+    for i in range(t):
+        for j in np.nonzero(visibility[i])[0]:
+            out[i, j // 64] |= np.uint64(1) << np.uint64(j % 64)
+    return out
+
+
+class Qwen3Engine:
+    """One Qwen3 target on one GPU (weights + KV cache + scratch buffers)."""
+
+    def __init__(self, weights: Qwen3Weights, kv_capacity: int, layer_ids=(), t_cap: int = DTREE_MAX_TREE):
+        cfg: Qwen3Config = weights.cfg
+        if weights.device.type != "cuda":
+            raise ValueError("engine weights must live on a CUDA device")
+        self.cfg = cfg
+        self.weights = weights
+        self.device = weights.device
+        self.layer_ids = sorted(int(i) for i in layer_ids)
+        if len(self.layer_ids) > 16:
+            raise ValueError("at most 16 hidden-capture layers")
+        self.t_cap = int(t_cap)
+        self.kv_capacity = int(kv_capacity)
+        L = cfg.num_hidden_layers
+        self._layers = (Qwen3Layer * L)()
+        for i in range(L):
+            self._layers[i] = Qwen3Layer(
+                ptr(weights.input_norm[i]), ptr(weights.qkv[i]), ptr(weights.q_norm[i]), ptr(weights.k_norm[i]),
+                ptr(weights.o_proj[i]), ptr(weights.post_norm[i]), ptr(weights.gate_up[i]), ptr(weights.down[i]),
+            )
+        d = Qwen3Desc()
+        d.hidden, d.layers = cfg.hidden_size, L
+        d.n_heads, d.n_kv_heads, d.head_dim = cfg.num_attention_heads, cfg.num_key_value_heads, cfg.head_dim
+        d.ffn, d.vocab = cfg.intermediate_size, cfg.vocab_size
+        d.rope_theta, d.rms_eps = cfg.rope_theta, cfg.rms_norm_eps
+        d.t_cap, d.kv_capacity = self.t_cap, self.kv_capacity
+        d.n_capture = len(self.layer_ids)
+        for i, l in enumerate(self.layer_ids):
+            d.capture_layers[i] = l
+        d.embed, d.final_norm = ptr(weights.embed), ptr(weights.final_norm)
+        d.layer = C.cast(self._layers, C.POINTER(Qwen3Layer))
+        sizes = (C.c_size_t * 9)()
+        call("dtree_qwen3_buffer_bytes", C.byref(d), sizes)
+        tp = pad_rows(self.t_cap)
+        dev = self.device
+        bf = torch.bfloat16
+        self.kv_cache = torch.zeros(L, 2, cfg.num_key_value_heads, self.kv_capacity, cfg.head_dim, dtype=bf, device=dev)
+        self.h = torch.zeros(tp, cfg.hidden_size, dtype=bf, device=dev)
+        self.xn = torch.zeros(tp, cfg.hidden_size, dtype=bf, device=dev)
+        self.q = torch.zeros(tp, cfg.q_dim, dtype=bf, device=dev)
+        self.attn = torch.zeros(tp, cfg.q_dim, dtype=bf, device=dev)
+        self.act = torch.zeros(tp, cfg.intermediate_size, dtype=bf, device=dev)
+        self.norm_out = torch.zeros(tp, cfg.hidden_size, dtype=bf, device=dev)
+        self.capture = torch.zeros(tp, cfg.hidden_size * max(1, len(self.layer_ids)), dtype=bf, device=dev)
+        self.workspace = torch.zeros(int(sizes[8]), dtype=torch.uint8, device=dev)
+        for t, need in zip([self.kv_cache, self.h, self.xn, self.q, self.attn, self.act, self.norm_out, self.capture],
+                           list(sizes)[:8]):
+            assert t.numel() * t.element_size() >= need
+        d.kv_cache, d.h, d.xn, d.q = ptr(self.kv_cache), ptr(self.h), ptr(self.xn), ptr(self.q)
+        d.attn, d.act, d.norm_out, d.capture = ptr(self.attn), ptr(self.act), ptr(self.norm_out), ptr(self.capture)
+        d.workspace, d.workspace_bytes = ptr(self.workspace), self.workspace.numel()
+        self._desc = d
+        handle = C.c_void_p()
+        call("dtree_qwen3_create", C.byref(d), C.byref(handle))
+        self._handle = handle
+
+    def close(self) -> None:
+        if getattr(self, "_handle", None):
+            _lib.load().dtree_qwen3_destroy(self._handle)
+            self._handle = None
+
+    def __del__(self):  # pragma: no cover - interpreter shutdown order
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def forward_tree(self, tokens: torch.Tensor, positions: torch.Tensor, anc: torch.Tensor, n_nodes: int,
+                     state: torch.Tensor, posterior: torch.Tensor | None) -> None:
+        """Tree-verify forward of rows [0, n_nodes) at prefix length state.start."""
+        call("dtree_qwen3_forward_tree", self._handle, ptr(tokens), ptr(positions), ptr(anc), int(n_nodes),
+             ptr(state), ptr(posterior), stream_ptr())
+
+    @property
+    def hidden_width(self) -> int:
+        return self.cfg.hidden_size * max(1, len(self.layer_ids))
+
+
+@dataclass
+class StepConfig:
+    mode: str            # "dtree" or "dflash"
+    rows: int            # draft rows (block_size - 1)
+    budget: int          # tree budget (dtree) / rows (dflash)
+    n_nodes: int         # tree rows per verify (root included)
+
+
+def dtree_nodes(budget: int, rows: int, vocab: int) -> int:
+    """Nodes the best-first builder emits: min(budget, reachable) + root."""
+    if budget <= 0 or rows <= 0:
+        return 1
+    k = min(budget, vocab)
+    reach, level = 0, 1
+    for _ in range(rows):
+        level *= k
+        reach += level
+        if reach >= budget:
+            return 1 + budget
+    return 1 + min(budget, reach)
+
+
+class DecodeSession:
+    """Device state of one sequence decoded with DTree or DFlash on an engine."""
+
+    def __init__(self, engine: Qwen3Engine, cfg: StepConfig, output_capacity: int, drafter, history: int = 4096):
+        self.engine = engine
+        self.cfg = cfg
+        dev = engine.device
+        self.state = kernels.new_state(dev)
+        self.tree = kernels.TreeBuffers.allocate(dev)
+        self.posterior = torch.zeros(DTREE_MAX_TREE, dtype=torch.int32, device=dev)
+        self.accepted = torch.zeros(DTREE_MAX_TREE, dtype=torch.int32, device=dev)
+        self.output = torch.zeros(int(output_capacity), dtype=torch.int32, device=dev)
+        self.history = torch.zeros(int(history), dtype=torch.int32, device=dev)
+        self.draft_logits = torch.zeros(max(cfg.rows, 1), engine.cfg.vocab_size, dtype=torch.float32, device=dev)
+        self.target_hidden = torch.zeros(DTREE_MAX_TREE, engine.hidden_width, dtype=torch.bfloat16, device=dev)
+        self.builder = (
+            kernels.TreeBuilder(cfg.rows, engine.cfg.vocab_size, cfg.budget, dev) if cfg.mode == "dtree" else None
+        )
+        self.drafter = drafter
+        self.graph: torch.cuda.CUDAGraph | None = None
+
+    # ------------------------------------------------------------ prefill
+    def prefill(self, prompt: list[int]) -> int:
+        """Causal forward of the prompt in chunks of <= t_cap rows (prefix K/V
+        into the cache).  Returns the greedy first token (runtime.py:459-465)."""
+        eng = self.engine
+        dev = eng.device
+        n = len(prompt)
+        if n <= 0:
+            raise ValueError("empty prompt")
+        chunk = eng.t_cap
+        toks = torch.tensor(prompt, dtype=torch.int32, device=dev)
+        self.output[:n] = toks
+        start = 0
+        hidden_rows = []
+        while start < n:
+            t = min(chunk, n - start)
+            self.state[0] = start
+            pos = torch.arange(start, start + t, dtype=torch.int32, device=dev)
+            anc = torch.from_numpy(chain_anc_masks(t).view(np.int64)).to(dev)
+            eng.forward_tree(toks[start:start + t].contiguous(), pos, anc, t, self.state, self.posterior)
+            hidden_rows.append(eng.capture[:t].clone())
+            start += t
+        first = int(self.posterior[t - 1].item())  # last prompt row of the last chunk
+        self.prompt_hidden = torch.cat(hidden_rows, dim=0)
+        self.reset(n, first)
+        return first
+
+    def reset(self, prompt_len: int, first_token: int) -> None:
+        """Decode state right after prefill: start = prompt_len, root = first token."""
+        self.state.zero_()
+        self.state[0] = prompt_len
+        self.state[1] = first_token
+        self.output[prompt_len] = first_token
+        self.prompt_len = prompt_len
+
+    # ------------------------------------------------------------ one step
+    def step(self) -> None:
+        """One decode step, launched on the current stream (no host sync)."""
+        eng = self.engine
+        c = self.cfg
+        self.drafter.draft(self)
+        if c.mode == "dtree":
+            self.builder.build(self.draft_logits, self.state, self.tree, keep_topk=False)
+        else:
+            kernels.chain_build(self.draft_logits[: c.rows], self.state, self.tree)
+        eng.forward_tree(self.tree.tokens, self.tree.positions, self.tree.anc, c.n_nodes, self.state, self.posterior)
+        kernels.accept_walk(self.tree, self.posterior, self.state, self.accepted, self.output, self.history)
+        if c.mode == "dtree":
+            kernels.kv_compact(eng.kv_cache, self.accepted, self.state)
+        if getattr(self.drafter, "needs_hidden", False):
+            kernels.gather_rows(eng.capture, self.accepted, self.state, self.target_hidden)
+        kernels.step_commit(self.state)
+
+    def capture_step(self) -> torch.cuda.CUDAGraph:
+        """Record ``step`` into a CUDA graph (after one eager warm-up step has
+        built every plan); replay it with ``replay``."""
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=s):
+            self.step()
+        torch.cuda.current_stream().wait_stream(s)
+        self.graph = g
+        return g
+
+    def replay(self) -> None:
+        if self.graph is None:
+            self.step()
+        else:
+            self.graph.replay()
+
+    def read_state(self) -> dict[str, int]:
+        return kernels.state_dict(self.state)

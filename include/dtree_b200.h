@@ -110,7 +110,8 @@ DTREE_API int dtree_chain_build(const float* draft_logits, int rows, int vocab, 
  * DFlashDraftModel + lm_head_logits, dtree_runtime.py:366-376): row r gets
  * Irwin-Hall(12)-6 noise from Philox4x32-10(seed, state->step, r) and +8 on
  * continuation[state->start + r + 1] with probability p_correct (else on a
- * Philox-chosen random token; also when the position is >= cont_len). */
+ * Philox-chosen random token; also when the position is >= cont_len or the
+ * continuation entry is negative, i.e. unknown). */
 DTREE_API int dtree_plant_draft_logits(float* logits, int rows, int vocab, uint32_t seed, const dtree_step_state* state,
                              const int32_t* continuation, int cont_len, float p_correct, void* stream);
 

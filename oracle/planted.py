@@ -88,13 +88,14 @@ def planted_draft_logits(seed: int, step: int, start: int, rows: int, vocab: int
                          continuation: np.ndarray, p_correct: float) -> np.ndarray:
     """Draft logits [rows, vocab] for the decode step that begins at ``start``
     (the number of committed tokens).  ``continuation[i]`` is the target's
-    greedy token at absolute output position ``i`` (length may be short:
-    positions beyond it plant on a random token)."""
+    greedy token at absolute output position ``i`` (length may be short,
+    entries may be -1: such positions plant on a random token)."""
     out = np.empty((rows, vocab), dtype=np.float32)
     for r in range(rows):
         out[r] = noise_row(seed, step, r, vocab)
         take, rand_tok = plant_choice(seed, step, r, vocab, p_correct)
         pos = start + r + 1
-        tok = int(continuation[pos]) if (take and pos < len(continuation)) else rand_tok
+        known = take and pos < len(continuation) and int(continuation[pos]) >= 0
+        tok = int(continuation[pos]) if known else rand_tok
         out[r, tok] = np.float32(out[r, tok] + SPIKE)
     return out

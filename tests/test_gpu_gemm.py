@@ -87,3 +87,15 @@ def test_lm_head_argmax_first_index_on_ties(K):
     # repeated calls: the device keys/counters reset themselves
     out2 = K.lm_head_argmax(h, e, 16)
     assert out2.tolist() == [5] * 16
+
+
+def test_shared_workspace_across_grids(K):
+    """GEMMs with different stream-K grids and tile widths share one workspace:
+    the tile counters must not be overwritten by another plan's partials."""
+    g = torch.Generator(device=DEV).manual_seed(11)
+    shapes = [(32, 512, 512), (32, 2560, 6144), (32, 1536, 512), (32, 512, 3072), (32, 512, 512)]
+    for t_pad, k, n in shapes * 2:
+        x = torch.randn(t_pad, k, device=DEV, generator=g).to(torch.bfloat16)
+        w = (torch.randn(n, k, device=DEV, generator=g) * 0.02).to(torch.bfloat16)
+        y = K.linear_bf16(x, w)
+        _check(y, x.float() @ w.float().t())
