@@ -1,7 +1,7 @@
 """Tree-verify forward and decode steps on the GPU vs the fp32 CPU oracle.
 
 Tolerances (bf16 engine vs fp32 oracle on the same bf16 weights):
-  logits        max |gpu - oracle| <= 3e-2 and mean |gpu - oracle| <= 3e-3
+  logits        max |gpu - oracle| <= 3e-2 and mean |gpu - oracle| <= 5e-3
                 (tiny config, 4 layers, 25 x 32768 logits)
   hidden states relative Frobenius error <= 2e-2
 Tree topology, acceptance indices and compaction indices are compared
@@ -22,7 +22,7 @@ from oracle.runtime import OracleDecoder, near_tie
 pytestmark = pytest.mark.gpu
 DEV = "cuda"
 LOGIT_TOL = 3e-2
-LOGIT_MEAN_TOL = 3e-3
+LOGIT_MEAN_TOL = 5e-3
 REL_TOL = 2e-2
 
 
