@@ -4,6 +4,9 @@
 // follow), adapters.py:635-668 (compaction), runtime.py:476-490 (DFlash
 // chain block).  All state lives on the device so a decode step needs no
 // host round trip.
+#include <mutex>
+#include <string>
+
 #include "common.cuh"
 #include "../../include/dtree_b200.h"
 
@@ -752,4 +755,64 @@ extern "C" int dtree_step_commit(dtree_step_state* state, void* stream_) {
   DTREE_CHECK_ARG(state, "null state");
   DTREE_CUDA_RET(launch_pdl(step_commit_kernel, dim3(1), dim3(32), 0, stream, state));
   return kOk;
+}
+
+// ============================================================ no-allocation variant
+// Tree build for callers that cannot allocate device memory: for example a
+// serving loop that must not call cudaMalloc (or any allocating library
+// routine) while it runs, or a host runtime that hands this library only the
+// buffers it owns.  The top-k scratch lives in this fixed device array instead
+// of a caller workspace.  Every GPU that loads the library holds it until the
+// process exits.  All calls share it, so calls whose GPU work overlaps (other
+// streams, other threads) race on it and must be serialized by the caller.
+namespace dtree {
+constexpr size_t kNoAllocScratchBytes = 1u << 20;  // 1 MiB: rows <= 64 at any vocab size
+static __device__ __align__(256) unsigned char g_tree_scratch[kNoAllocScratchBytes];
+constexpr int kMaxDevices = 64;
+static void* g_tree_scratch_ptr[kMaxDevices] = {};
+static std::mutex g_tree_scratch_mu;
+
+// Device address of g_tree_scratch on the current device.  The host-side
+// symbol is only a stand-in, so the address is looked up once per device,
+// with that device current.
+static int tree_scratch_ptr(void** out) {
+  int dev = 0;
+  DTREE_CUDA_RET(cudaGetDevice(&dev));
+  DTREE_CHECK_ARG(dev >= 0 && dev < kMaxDevices, "device ordinal out of range");
+  std::lock_guard<std::mutex> lock(g_tree_scratch_mu);
+  if (g_tree_scratch_ptr[dev] == nullptr) {
+    void* p = nullptr;
+    DTREE_CUDA_RET(cudaGetSymbolAddress(&p, g_tree_scratch));
+    g_tree_scratch_ptr[dev] = p;
+  }
+  *out = g_tree_scratch_ptr[dev];
+  return kOk;
+}
+}  // namespace dtree
+
+extern "C" size_t dtree_tree_build_noalloc_max_bytes(void) { return dtree::kNoAllocScratchBytes; }
+
+extern "C" int dtree_tree_build_noalloc(const float* draft_logits, int rows, int vocab, int budget,
+                                        dtree_step_state* state, int32_t* tree_tokens, int32_t* parents,
+                                        int32_t* depths, int32_t* positions, uint64_t* anc_mask, void* stream_) {
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  DTREE_CHECK_ARG(rows >= 0 && rows <= kMaxRows, "rows must be in [0, 64]");
+  DTREE_CHECK_ARG(vocab > 0, "vocab must be positive");
+  const size_t need = dtree_tree_build_workspace_bytes(rows, vocab, budget);
+  if (need > kNoAllocScratchBytes)
+    return fail(kErrCapacity, "dtree_tree_build_noalloc: needs " + std::to_string(need) +
+                                  " bytes of scratch, the fixed device scratch holds " +
+                                  std::to_string(kNoAllocScratchBytes));
+  void* scratch = nullptr;
+  int rc = tree_scratch_ptr(&scratch);
+  if (rc) return rc;
+  if (budget > 0 && rows > 0) {
+    // the per-row arrival counters must start at zero (a completed call leaves
+    // them at zero; an interrupted one may not)
+    TreeWs ws;
+    tree_ws_layout(rows, topk_splits(rows, vocab), &ws, static_cast<char*>(scratch));
+    DTREE_CUDA_RET(cudaMemsetAsync(ws.counters, 0, sizeof(uint32_t) * rows, stream));
+  }
+  return dtree_tree_build(draft_logits, rows, vocab, budget, state, scratch, kNoAllocScratchBytes, tree_tokens,
+                          parents, depths, positions, anc_mask, nullptr, nullptr, stream_);
 }

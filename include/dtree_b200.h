@@ -92,6 +92,23 @@ DTREE_API int dtree_tree_build(const float* draft_logits, int rows, int vocab, i
                      int32_t* tree_tokens, int32_t* parents, int32_t* depths, int32_t* positions,
                      uint64_t* anc_mask, int32_t* top_ids, float* top_logprobs, void* stream);
 
+/* Same as dtree_tree_build, but allocates nothing and takes no workspace:
+ * for callers that cannot allocate device memory while they decode (a
+ * serving loop with a fixed memory budget, or a host runtime that only passes
+ * buffers it already owns).  No counterpart in the reference, which builds
+ * the tree on the host.  The scratch is a fixed 1 MiB device array inside
+ * the library (dtree_tree_build_noalloc_max_bytes()), held by every GPU that
+ * loads the library until the process exits; sizes needing more scratch
+ * (dtree_tree_build_workspace_bytes() above the limit) are rejected with
+ * DTREE_ERR_CAPACITY.  The first call on a device looks up the scratch
+ * address for that device; make that first call before any stream capture.
+ * All calls share the scratch and it keeps the last call's contents: calls
+ * whose GPU work overlaps (other streams or threads) race on it. */
+DTREE_API size_t dtree_tree_build_noalloc_max_bytes(void);
+DTREE_API int dtree_tree_build_noalloc(const float* draft_logits, int rows, int vocab, int budget,
+                                       dtree_step_state* state, int32_t* tree_tokens, int32_t* parents,
+                                       int32_t* depths, int32_t* positions, uint64_t* anc_mask, void* stream);
+
 /* Heap stage only, from given top-k ids/log-probs (for parity checks against
  * the reference's own heap inputs).  Same outputs as dtree_tree_build. */
 DTREE_API int dtree_tree_from_topk(const int32_t* top_ids, const float* top_logprobs, int rows, int topk, int budget,
