@@ -6,7 +6,8 @@ tokens with spec=16, tree_budget=24; planted draft logits with top-1
 agreement p=0.85 against the target's greedy continuation.
 
 A bench "step" is one whole 512-token DTree generation after the prefill
-(~80 decode steps: planted draft -> device tree build -> tree-verify forward
+(about 240 decode steps at the 2.1 tokens per step the planted drafts give
+against a 151936-token vocabulary: planted draft -> device tree build -> tree-verify forward
 with fused LM-head argmax -> acceptance walk -> KV compaction -> commit), each
 decode step one CUDA-graph replay with no host round trip.  ``value`` =
 accepted (generated) tokens per second over all ranks.  ``e2e`` runs the same
@@ -157,7 +158,7 @@ def run_ours(args, rank, world, local, dist) -> dict | None:
     # fixed point of the planted continuation (untimed)
     prev = None
     fixed_iters = 0
-    for it in range(6):
+    for it in range(12):
         r = gen.generate_from_tokens(prompt, **gkw)
         fixed_iters = it + 1
         if prev is not None and r.output_tokens == prev:
@@ -189,10 +190,12 @@ def run_ours(args, rank, world, local, dist) -> dict | None:
         sampler.start()
         time.sleep(0.4)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.nvtx.range_push("timed")  # lets a profiler scope the timed region
     e0.record()
     for _ in range(args.steps):
         one_generation()
     e1.record()
+    torch.cuda.nvtx.range_pop()
     torch.cuda.synchronize()
     ms = e0.elapsed_time(e1)
     if dist:
@@ -266,7 +269,10 @@ def run_ours(args, rank, world, local, dist) -> dict | None:
             traffic = json.loads(tp.read_text()).get("bytes_per_verify")
         except Exception:
             traffic = None
-    launches_per_step = 8 * cfg.num_hidden_layers + 7
+    # per layer: input norm, QKV GEMM, QKV finish, attention, combine, O GEMM,
+    # post norm, gate/up GEMM, down GEMM; per step: final norm, LM head,
+    # plant, top-k, heap, walk, compaction, commit
+    launches_per_step = 9 * cfg.num_hidden_layers + 8
     out = {
         "metric": METRIC,
         "value": round(value, 2),

@@ -1,0 +1,192 @@
+"""Isolated tree-verify step timing (BASELINE config 2 sweep).
+
+Qwen3-4B shape (or another preset), bf16 random-init weights, K/V prefix of
+random bf16 values (std 1), trees built on the GPU best-first from 16 rows of
+draft log-probs sampled from Dirichlet(alpha=0.1) over a random top-32
+support (seeded).  For every (prefix, tree budget) the tree-verify forward
+(``dtree_qwen3_forward_tree``: all layers + fused LM-head argmax) is captured
+in a CUDA graph and replayed; time per verify from CUDA events, HBM figures
+against algorithmic bytes (all weights once + K/V prefix read + new K/V
+write).  Mirrors the role of the reference's scripts/micro_verify.py and
+scripts/micro_scaling.py.
+
+    python -m dtree_mlx_b200.verify_sweep [--preset qwen3-4b] [--layers N]
+        [--prefix 512,2048,8192] [--budget 8,24,64] [--iters 50] [--json]
+"""
+from __future__ import annotations
+
+import argparse
+import json
+from dataclasses import replace
+from pathlib import Path
+
+import numpy as np
+import torch
+
+from . import kernels
+from .config import PRESETS
+from .engine import Qwen3Engine
+from .synthetic import random_qwen3_weights
+
+
+def dirichlet_draft_logits(rows: int, vocab: int, seed: int, support: int = 32, alpha: float = 0.1) -> np.ndarray:
+    """Draft log-probs: Dirichlet(alpha) mass over a random top-`support` set,
+    every other token at log(1e-30)."""
+    rng = np.random.default_rng(seed)
+    out = np.full((rows, vocab), np.log(1e-30), dtype=np.float32)
+    for r in range(rows):
+        ids = rng.choice(vocab, size=support, replace=False)
+        p = rng.dirichlet(np.full(support, alpha))
+        out[r, ids] = np.log(np.maximum(p, 1e-30)).astype(np.float32)
+    return out
+
+
+def algorithmic_bytes(cfg, weights, prefix: int, t: int) -> float:
+    wbytes = sum(x.numel() * x.element_size() for x in
+                 [weights.embed, *weights.qkv, *weights.o_proj, *weights.gate_up, *weights.down])
+    kv_row = 2 * cfg.num_key_value_heads * cfg.head_dim * 2 * cfg.num_hidden_layers
+    return float(wbytes + prefix * kv_row + t * kv_row)
+
+
+def measured_hbm_gbs() -> tuple[float, str]:
+    p = Path(__file__).resolve().parents[1] / "MEASURED_PEAKS.json"
+    if p.exists():
+        return float(json.loads(p.read_text())["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def run(preset: str, layers: int | None, prefixes: list[int], budgets: list[int], iters: int, seed: int = 0,
+        eager_only: bool = False) -> list[dict]:
+    cfg = PRESETS[preset]
+    if layers:
+        cfg = replace(cfg, num_hidden_layers=layers)
+    dev = torch.device("cuda")
+    w = random_qwen3_weights(cfg, seed=seed, device=dev)
+    eng = Qwen3Engine(w, kv_capacity=max(prefixes) + 160)
+    g = torch.Generator(device=dev).manual_seed(seed + 1)
+    eng.kv_cache.copy_(torch.randn(eng.kv_cache.shape, generator=g, device=dev).to(torch.bfloat16))
+    peak, peak_src = measured_hbm_gbs()
+    results = []
+    for budget in budgets:
+        logits = torch.from_numpy(dirichlet_draft_logits(16, cfg.vocab_size, seed + budget)).to(dev)
+        for P in prefixes:
+            st = kernels.new_state(dev, start=P, root_token=1)
+            tree = kernels.TreeBuffers.allocate(dev)
+            kernels.TreeBuilder(16, cfg.vocab_size, budget, dev).build(logits, st, tree, keep_topk=False)
+            n = int(st[6].item())
+            post = torch.zeros(128, dtype=torch.int32, device=dev)
+
+            def fwd():
+                eng.forward_tree(tree.tokens, tree.positions, tree.anc, n, st, post)
+
+            for _ in range(3):
+                fwd()
+            torch.cuda.synchronize()
+            graph = None
+            if not eager_only:
+                s = torch.cuda.Stream()
+                s.wait_stream(torch.cuda.current_stream())
+                graph = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(graph, stream=s):
+                    fwd()
+                torch.cuda.current_stream().wait_stream(s)
+                for _ in range(3):
+                    graph.replay()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            torch.cuda.synchronize()
+            a.record()
+            for _ in range(iters):
+                graph.replay() if graph is not None else fwd()
+            b.record()
+            torch.cuda.synchronize()
+            ms = a.elapsed_time(b) / iters
+            nbytes = algorithmic_bytes(cfg, w, P, n)
+            gbs = nbytes / (ms / 1e3) / 1e9
+            results.append({"prefix": P, "tree_budget": budget, "tree_rows": n, "verify_ms": round(ms, 4),
+                            "algorithmic_gb": round(nbytes / 1e9, 4), "achieved_gbs": round(gbs, 1),
+                            "frac_of_hbm": round(gbs / peak, 4), "peak_gbs": peak, "peak_source": peak_src,
+                            "layers": cfg.num_hidden_layers})
+            del graph
+    eng.close()
+    return results
+
+
+KERNEL_GROUPS = (
+    ("lm_head", lambda k: k.startswith("gemm_streamk_kernel") and k.endswith(", 4>")),
+    ("gemm", lambda k: k.startswith("gemm_streamk_kernel")),
+    ("attention", lambda k: k.startswith(("tree_attn_kernel", "attn_combine_kernel"))),
+    ("norm_rope", lambda k: k.startswith(("residual_rmsnorm_kernel", "rmsnorm_kernel", "qkv_finish_kernel"))),
+    ("tree_build", lambda k: k.startswith(("topk_lse_kernel", "heap_tree_kernel"))),
+)
+
+
+def summarize_launches(csv_path: str, forwards_per_config: int) -> list[dict]:
+    """Attention / GEMM split per sweep configuration from an ncu launch list
+    (``--metrics gpu__time_duration.sum --csv``) of an ``--eager`` sweep.
+
+    Each configuration starts with its tree build (``topk_lse_kernel``), then
+    runs ``forwards_per_config`` verify forwards (3 warm-up + ``--iters``).
+    Times are ncu's serialised, cache-flushed per-launch durations: compare
+    shares, not absolute milliseconds."""
+    import csv
+    import re
+
+    rows = list(csv.reader(open(csv_path)))
+    hi = next(i for i, r in enumerate(rows) if "Kernel Name" in r)
+    hdr = rows[hi]
+    ki, vi, ui = hdr.index("Kernel Name"), hdr.index("Metric Value"), hdr.index("Metric Unit")
+    scale = {"nsecond": 1e-3, "ns": 1e-3, "usecond": 1.0, "us": 1.0, "msecond": 1e3, "ms": 1e3}
+    segments: list[dict[str, float]] = []
+    for r in rows[hi + 1:]:
+        if len(r) <= vi:
+            continue
+        name = re.sub(r"\(.*", "", r[ki]).replace("void ", "").replace("dtree::", "").strip()
+        us = float(r[vi].replace(",", "")) * scale[r[ui]]
+        if name.startswith("topk_lse_kernel"):
+            segments.append({})
+        if not segments:
+            continue
+        group = next((g for g, match in KERNEL_GROUPS if match(name)), "other")
+        segments[-1][group] = segments[-1].get(group, 0.0) + us
+    out = []
+    for seg in segments:
+        fwd = {g: v / forwards_per_config for g, v in seg.items() if g != "tree_build"}
+        total = sum(fwd.values())
+        out.append({"per_forward_us": {g: round(v, 1) for g, v in sorted(fwd.items())},
+                    "share": {g: round(v / total, 4) for g, v in sorted(fwd.items())},
+                    "tree_build_us": round(seg.get("tree_build", 0.0), 1)})
+    return out
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--preset", default="qwen3-4b")
+    ap.add_argument("--layers", type=int, default=None, help="override the layer count (smaller captures)")
+    ap.add_argument("--prefix", default="512,2048,8192")
+    ap.add_argument("--budget", default="8,24,64")
+    ap.add_argument("--iters", type=int, default=50)
+    ap.add_argument("--eager", action="store_true", help="launch eagerly (no CUDA graph), e.g. under a profiler")
+    ap.add_argument("--json", action="store_true")
+    ap.add_argument("--launches", default=None,
+                    help="summarise an ncu launch-list CSV of an --eager sweep (attention/GEMM split) and exit")
+    a = ap.parse_args()
+    if a.launches:
+        prefixes, budgets = a.prefix.split(","), a.budget.split(",")
+        split = summarize_launches(a.launches, 3 + a.iters)
+        labels = [(int(b), int(p)) for b in budgets for p in prefixes]
+        for (b, p), row in zip(labels, split):
+            print(json.dumps({"prefix": p, "tree_budget": b, **row}))
+        return
+    res = run(a.preset, a.layers, [int(x) for x in a.prefix.split(",")], [int(x) for x in a.budget.split(",")],
+              a.iters, eager_only=a.eager)
+    if a.json:
+        print(json.dumps(res))
+    else:
+        for r in res:
+            print(f"prefix {r['prefix']:5d} budget {r['tree_budget']:3d} rows {r['tree_rows']:3d}: "
+                  f"{r['verify_ms']:.3f} ms  {r['achieved_gbs']:7.1f} GB/s  ({100 * r['frac_of_hbm']:.1f}% of "
+                  f"{r['peak_source']} HBM)")
+
+
+if __name__ == "__main__":
+    main()
