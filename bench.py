@@ -52,6 +52,11 @@ P_CORRECT = 0.85
 PRESET = "qwen3-4b"
 KV_CAP = 2304
 METRIC = "accepted tok/s/GPU, Qwen3-4B-shape DTree b24; verify-step HBM GB/s vs peak"
+WORKLOADS = {
+    16: "BASELINE config 1: Qwen3-4B-shape DTree, prompt 256, 512 new tokens, spec 16, budget 24",
+    4: "BASELINE config 3: Qwen3-4B-shape DTree with MLX affine 4-bit projections (group 64), prompt 256, "
+       "512 new tokens, spec 16, budget 24",
+}
 UNIT = "tokens/s"
 
 
@@ -131,8 +136,7 @@ class ClockSampler:
 
 
 def algorithmic_verify_bytes(cfg, weights, prefix: int, t: int) -> float:
-    wbytes = sum(x.numel() * x.element_size() for x in
-                 [weights.embed, *weights.qkv, *weights.o_proj, *weights.gate_up, *weights.down])
+    wbytes = weights.streamed_bytes()
     kv_row = 2 * cfg.num_key_value_heads * cfg.head_dim * 2 * cfg.num_hidden_layers
     return float(wbytes + prefix * kv_row + t * kv_row)
 
@@ -142,13 +146,15 @@ def run_ours(args, rank, world, local, dist) -> dict | None:
     import torch
 
     from dtree_mlx_b200 import DFlashGenerator
-    from dtree_mlx_b200.adapters import load_target_model
+    from dtree_mlx_b200.adapters import load_target_model, quantize_target_model
     from dtree_mlx_b200.draft import PlantedDrafter
     from dtree_mlx_b200.engine import DecodeSession
     from dtree_mlx_b200.synthetic import random_prompt
 
     dev = torch.device("cuda", local)
     target = load_target_model(f"synthetic:{PRESET}:seed=0:kv={KV_CAP}")
+    if args.quant_bits == 4:
+        quantize_target_model(target, 4, 64)
     cfg = target.model.cfg
     drafter = PlantedDrafter(seed=1000 + rank, p_correct=P_CORRECT, block_size=SPEC)
     gen = DFlashGenerator.from_components(target, drafter)
@@ -264,7 +270,7 @@ def run_ours(args, rank, world, local, dist) -> dict | None:
     achieved = vbytes / (vms / 1e3) / 1e9
     traffic = None
     tp = ROOT / "profiles" / "verify_traffic.json"
-    if tp.exists():
+    if tp.exists() and args.quant_bits == 16:
         try:
             traffic = json.loads(tp.read_text()).get("bytes_per_verify")
         except Exception:
@@ -284,16 +290,17 @@ def run_ours(args, rank, world, local, dist) -> dict | None:
         "higher_is_better": True,
         "scaling": "weak",
         "vs_baseline": None,
-        "dtype": "bf16",
+        "dtype": "bf16" if args.quant_bits == 16 else "u4 weights (affine, group 64), bf16 activations",
         "data": "synthetic (random-init Qwen3-4B-shape weights, random prompt, planted drafts p=0.85)",
         "config": {
-            "workload": "BASELINE config 1: Qwen3-4B-shape DTree, prompt 256, 512 new tokens, spec 16, budget 24",
+            "workload": WORKLOADS[args.quant_bits],
             "decode_steps_per_generation": n_steps,
             "mean_accepted_per_step": round(sum(accept) / n_steps, 3),
             "tree_rows": n_nodes,
             "fixed_point_iterations": fixed_iters,
             "continuation_converged": bool(converged),
-            "l2": "inputs larger than L2 (8.0 GB of weights streamed per decode step)",
+            "l2": f"inputs larger than L2 ({target.model.weights.streamed_bytes() / 1e9:.1f} GB of weights "
+                  f"streamed per decode step)",
             "parallelism": f"dp{world} independent-sequence replicas",
         },
         "e2e": {"value": round(e2e_tok_s, 2), "unit": UNIT, "h2d_bytes_per_step": PROMPT_LEN * 4,
@@ -425,6 +432,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
+    ap.add_argument("--quant-bits", type=int, default=16, choices=[16, 4],
+                    help="4: BASELINE config 3 (MLX affine 4-bit projections, group 64)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3) if args.impl == "ours" else args.warmup
     rank, world, local, dist = dist_init()

@@ -62,6 +62,19 @@ class Qwen3Layer(C.Structure):
     ]
 
 
+class Qwen3Q4Layer(C.Structure):
+    _fields_ = [
+        ("qkv_scales", C.c_void_p),
+        ("qkv_biases", C.c_void_p),
+        ("o_scales", C.c_void_p),
+        ("o_biases", C.c_void_p),
+        ("gate_up_scales", C.c_void_p),
+        ("gate_up_biases", C.c_void_p),
+        ("down_scales", C.c_void_p),
+        ("down_biases", C.c_void_p),
+    ]
+
+
 class Qwen3Desc(C.Structure):
     _fields_ = [
         ("hidden", C.c_int),
@@ -90,6 +103,9 @@ class Qwen3Desc(C.Structure):
         ("capture", C.c_void_p),
         ("workspace", C.c_void_p),
         ("workspace_bytes", C.c_size_t),
+        ("quant_bits", C.c_int),
+        ("group_size", C.c_int),
+        ("q4_layer", C.POINTER(Qwen3Q4Layer)),
     ]
 
 
@@ -115,6 +131,7 @@ PROTOTYPES = {
     "dtree_step_commit": (I, [P, P]),
     "dtree_linear_workspace_bytes": (SZ, [I, I]),
     "dtree_linear_bf16": (I, [P, I, I, P, I, P, P, SZ, I, P]),
+    "dtree_linear_q4": (I, [P, I, I, P, P, P, I, P, P, SZ, I, P]),
     "dtree_lm_head_workspace_bytes": (SZ, [I]),
     "dtree_lm_head_argmax": (I, [P, I, I, I, P, I, P, P, SZ, P]),
     "dtree_qwen3_buffer_bytes": (I, [C.POINTER(Qwen3Desc), C.POINTER(C.c_size_t)]),

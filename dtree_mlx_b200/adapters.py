@@ -376,6 +376,21 @@ def parse_synthetic_spec(spec: str) -> dict:
     return out
 
 
+def quantize_target_model(target: "LoadedTargetModel", bits: int = 4, group_size: int = 64) -> dict:
+    """``quantize_model`` on a loaded target (api.py:46-54): its projections
+    become MLX affine 4-bit, engines built for the bf16 weights are released.
+    Returns the ``quantization`` config entry."""
+    from .synthetic import quantize_weights
+
+    model = target.model
+    for eng in list(model.engines.values()):
+        eng.close()
+    model.engines.clear()
+    model.weights = quantize_weights(model.weights, bits, group_size)
+    torch.cuda.empty_cache()
+    return {"group_size": group_size, "bits": bits}
+
+
 def load_target_model(path_or_repo: str, device: str = "cuda") -> LoadedTargetModel:
     """adapters.py:822-846.  Checkpoints are not available offline; the
     ``synthetic:<preset>`` spec builds a seeded random-init target of a

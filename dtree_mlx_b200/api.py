@@ -8,7 +8,7 @@ from typing import Any
 
 import torch
 
-from .adapters import LoadedTargetModel, load_target_model
+from .adapters import LoadedTargetModel, load_target_model, quantize_target_model
 from .draft import load_draft_model
 from .dtree_runtime import dtree_generate
 from .runtime import dflash_generate
@@ -26,8 +26,10 @@ class DFlashResult:
 
 
 class DFlashGenerator:
-    """api.py:29-166.  ``target_quant_bits`` (4-bit affine weights) and a trained
-    drafter are not available in this build and raise NotImplementedError."""
+    """api.py:29-166.  ``target_quant_bits=4`` (group size 64) quantizes the
+    target's projections to MLX affine 4-bit (api.py:46-54) and the verify
+    GEMMs dequantize them on the fly; other bit widths and a trained,
+    quantized drafter raise NotImplementedError."""
 
     def __init__(
         self,
@@ -43,12 +45,14 @@ class DFlashGenerator:
         torch.manual_seed(seed)
         self.requested_target_model = target_model
         self.requested_draft_model = draft_model
-        if target_quant_bits is not None:
-            raise NotImplementedError("target_quant_bits: the fused 4-bit verify GEMM is not built yet")
+        if target_quant_bits is not None and (target_quant_bits != 4 or target_quant_group_size != 64):
+            raise NotImplementedError("target quantization: only bits=4 with group_size=64 is supported")
         if draft_quant_bits is not None:
             raise NotImplementedError("draft_quant_bits: the trained drafter is not available")
         self.target: LoadedTargetModel = load_target_model(target_model)
         self.target_quantization = None
+        if target_quant_bits is not None:
+            self.target_quantization = quantize_target_model(self.target, target_quant_bits, target_quant_group_size)
         self.draft, self.draft_path = load_draft_model(draft_model)
         self.draft_attention_mask = "none" if draft_attention_mask == "auto" else draft_attention_mask
         self.draft_quantization = None

@@ -37,18 +37,18 @@ static GemmWs ws_split(void* base) {
 
 static bool valid_tpad(int t) { return t == 16 || t == 32 || t == 64 || t == 128; }
 
-int gemm_plan(GemmPlan* plan, const void* w, int n_out, int k, const void* x, int t_pad, int x_row_stride_elems,
-              int epi, int grid) {
+// activation map, split / grid choice and parameters shared by both weight formats
+// `wide` kernels (the q4 variant: 448 threads, ~146 KB shared memory) fit
+// one CTA per SM, so a grid above the SM count would run a second wave.
+static int plan_common(GemmPlan* plan, int n_out, int k, const void* x, int t_pad, int x_row_stride_elems, int epi,
+                       int grid, bool wide) {
   DTREE_CHECK_ARG(valid_tpad(t_pad), "t_pad must be 16, 32, 64 or 128");
   DTREE_CHECK_ARG(k % 64 == 0 && k > 0, "K must be a positive multiple of 64");
   DTREE_CHECK_ARG(n_out > 0, "N must be positive");
   const int m_tiles = (n_out + 127) / 128;
   DTREE_CHECK_ARG(m_tiles <= kMaxTileCounters, "N too large");
-  int rc = make_tmap_2d_bf16(&plan->tmap_w, w, static_cast<uint64_t>(k), static_cast<uint64_t>(n_out),
-                             static_cast<uint64_t>(k) * 2, 64, 128, true);
-  if (rc) return rc;
-  rc = make_tmap_2d_bf16(&plan->tmap_x, x, static_cast<uint64_t>(k), static_cast<uint64_t>(t_pad),
-                         static_cast<uint64_t>(x_row_stride_elems) * 2, 64, static_cast<uint32_t>(t_pad), true);
+  int rc = make_tmap_2d_bf16(&plan->tmap_x, x, static_cast<uint64_t>(k), static_cast<uint64_t>(t_pad),
+                             static_cast<uint64_t>(x_row_stride_elems) * 2, 64, static_cast<uint32_t>(t_pad), true);
   if (rc) return rc;
   GemmParams& p = plan->p;
   p = GemmParams{};
@@ -67,14 +67,40 @@ int gemm_plan(GemmPlan* plan, const void* w, int n_out, int k, const void* x, in
     p.grid = m_tiles * split;
   } else if (grid > 0) {
     p.grid = static_cast<int>(units < grid ? units : grid);
-  } else if (m_tiles >= (sms * 9) / 10 && m_tiles <= (sms * 5) / 4) {
-    p.grid = m_tiles;  // about one whole tile per CTA: no partial tiles at all
+  } else if (m_tiles >= (sms * 9) / 10 && m_tiles <= (wide ? sms : (sms * 5) / 4)) {
+    p.grid = m_tiles;  // about one whole tile per CTA (two CTAs fit an SM): no partial tiles at all
   } else {
     p.grid = static_cast<int>(units < sms ? units : sms);
   }
   DTREE_CHECK_ARG(units * p.grid < (1ll << 31), "stream-K index range exceeds 32 bits");
   plan->t_pad = t_pad;
   plan->epi = epi;
+  plan->q4 = false;
+  return kOk;
+}
+
+int gemm_plan(GemmPlan* plan, const void* w, int n_out, int k, const void* x, int t_pad, int x_row_stride_elems,
+              int epi, int grid) {
+  int rc = plan_common(plan, n_out, k, x, t_pad, x_row_stride_elems, epi, grid, false);
+  if (rc) return rc;
+  return make_tmap_2d_bf16(&plan->tmap_w, w, static_cast<uint64_t>(k), static_cast<uint64_t>(n_out),
+                           static_cast<uint64_t>(k) * 2, 64, 128, true);
+}
+
+int gemm_plan_q4(GemmPlan* plan, const void* w_packed, const void* scales, const void* biases, int n_out, int k,
+                 const void* x, int t_pad, int x_row_stride_elems, int epi, int grid) {
+  DTREE_CHECK_ARG(w_packed && scales && biases, "null q4 weight pointer");
+  DTREE_CHECK_ARG(epi == kEpiStore || epi == kEpiPartial || epi == kEpiSwiglu,
+                  "q4 GEMM supports the store, split-K partial and SwiGLU epilogues");
+  int rc = plan_common(plan, n_out, k, x, t_pad, x_row_stride_elems, epi, grid, true);
+  if (rc) return rc;
+  // packed weight map: box 8 words (64 elements, one group) x 128 rows
+  rc = make_tmap_2d_u32(&plan->tmap_w, w_packed, static_cast<uint64_t>(k / 8), static_cast<uint64_t>(n_out),
+                        static_cast<uint64_t>(k / 2), 8, 128);
+  if (rc) return rc;
+  plan->p.q_scales = static_cast<const __nv_bfloat16*>(scales);
+  plan->p.q_biases = static_cast<const __nv_bfloat16*>(biases);
+  plan->q4 = true;
   return kOk;
 }
 
@@ -88,18 +114,26 @@ int gemm_bind_ws(GemmPlan* plan, void* ws, size_t ws_bytes) {
   return kOk;
 }
 
-template <int TPAD, int EPI>
+template <int TPAD, int EPI, bool Q4 = false>
 static int launch_t(const GemmPlan& pl, cudaStream_t st) {
-  using C = GemmCfg<TPAD, EPI>;
-  auto kern = gemm_streamk_kernel<TPAD, EPI>;
+  using C = GemmCfg<TPAD, EPI, Q4>;
+  auto kern = gemm_streamk_kernel<TPAD, EPI, Q4>;
   DTREE_CUDA_RET(ensure_smem_attr(kern, C::kSmem));
-  DTREE_CUDA_RET(launch_pdl(kern, dim3(pl.p.grid), dim3(kGemmThreads), static_cast<size_t>(C::kSmem), st,
-                            pl.tmap_w, pl.tmap_x, pl.p));
+  DTREE_CUDA_RET(launch_pdl(kern, dim3(pl.p.grid), dim3(Q4 ? kGemmThreadsQ4 : kGemmThreads),
+                            static_cast<size_t>(C::kSmem), st, pl.tmap_w, pl.tmap_x, pl.p));
   return kOk;
 }
 
 template <int TPAD>
 static int launch_epi(const GemmPlan& pl, cudaStream_t st) {
+  if (pl.q4) {
+    switch (pl.epi) {
+      case kEpiStore: return launch_t<TPAD, kEpiStore, true>(pl, st);
+      case kEpiSwiglu: return launch_t<TPAD, kEpiSwiglu, true>(pl, st);
+      case kEpiPartial: return launch_t<TPAD, kEpiPartial, true>(pl, st);
+    }
+    return fail(kErrInvalidArg, "epilogue not available for q4 weights");
+  }
   switch (pl.epi) {
     case kEpiStore: return launch_t<TPAD, kEpiStore>(pl, st);
     case kEpiResidual: return launch_t<TPAD, kEpiResidual>(pl, st);
@@ -135,6 +169,20 @@ extern "C" int dtree_linear_bf16(const void* x, int t_pad, int k, const void* w,
   DTREE_CHECK_ARG(x && w && y, "null pointer");
   GemmPlan plan;
   int rc = gemm_plan(&plan, w, n, k, x, t_pad, k, kEpiStore, split_k > 0 ? split_k : 0);
+  if (rc) return rc;
+  rc = gemm_bind_ws(&plan, workspace, workspace_bytes);
+  if (rc) return rc;
+  plan.p.out = static_cast<__nv_bfloat16*>(y);
+  plan.p.ldo = n;
+  return gemm_launch(plan, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int dtree_linear_q4(const void* x, int t_pad, int k, const void* w_packed, const void* scales,
+                               const void* biases, int n, void* y, void* workspace, size_t workspace_bytes,
+                               int split_k, void* stream) {
+  DTREE_CHECK_ARG(x && y, "null pointer");
+  GemmPlan plan;
+  int rc = gemm_plan_q4(&plan, w_packed, scales, biases, n, k, x, t_pad, k, kEpiStore, split_k > 0 ? split_k : 0);
   if (rc) return rc;
   rc = gemm_bind_ws(&plan, workspace, workspace_bytes);
   if (rc) return rc;

@@ -16,6 +16,13 @@
 //
 // Warp roles (192 threads): warp 0 = TMA producer, warp 1 = MMA issuer,
 // warps 2..5 = epilogue (warp w reads TMEM lanes 32*(w%4)..+31).
+//
+// Q4 variant (4-bit affine weights, group 64 along K, MLX layout: packed
+// uint32 [N][K/8] with element 8j+i in bits 4i..4i+3 of word j, bf16 scales
+// and biases [N][K/64]): TMA brings the packed 128x64 tile (4 KB) instead of
+// the bf16 one, and 8 more warps (6..13) dequantize it, w = scale*q + bias
+// rounded once to bf16 (fma.rn.bf16x2), straight into the 128-byte-swizzled
+// K-major layout the MMA reads.  One K block of 64 is exactly one group.
 #pragma once
 
 #include "common.cuh"
@@ -64,25 +71,38 @@ struct GemmParams {
   unsigned long long* argmax_keys;  // [TPAD], zero between launches
   uint32_t* done_cnt;               // zero between launches
   int32_t* argmax_out;              // [n_rows]
+  // q4 weights: bf16 scale / bias per (row, group of 64); row stride = kb
+  const __nv_bfloat16* q_scales;
+  const __nv_bfloat16* q_biases;
 };
 
 constexpr int kGemmThreads = 192;
+constexpr int kGemmThreadsQ4 = 192 + 256;  // + 8 dequant warps
 constexpr int kWTileBytes = 128 * 64 * 2;
+constexpr int kPkTileBytes = 128 * 64 / 2;  // packed 4-bit tile
 
-template <int TPAD, int EPI>
+template <int TPAD, int EPI, bool Q4 = false>
 struct GemmCfg {
   static constexpr int kXBytes = TPAD * 64 * 2;
-  static constexpr int kStageBytes = kWTileBytes + kXBytes;
+  // bf16 stage: [W 16 KB][X]; q4 stage: [X][packed 4 KB] (X stays 1024-aligned)
+  static constexpr int kStageBytes = (Q4 ? kPkTileBytes : kWTileBytes) + kXBytes;
+  static constexpr int kXOff = Q4 ? 0 : kWTileBytes;
+  static constexpr int kWOff = Q4 ? kXBytes : 0;
+  static constexpr int kDeq = Q4 ? 3 : 0;  // dequantized bf16 W buffers (16 KB each)
+  static constexpr int kBarBytes = Q4 ? 512 : 256;
   static constexpr int kXchBytes = (EPI == kEpiQkv || EPI == kEpiSwiglu) ? 128 * 8 * 4 : 0;
   // [0,256): per-warp reductions of one 8-row chunk; then s_best / s_pos
   // [TPAD] (8 B each) and the argmax chunk keys [4][8] (8 B each)
   static constexpr int kRedBytes = 256 + TPAD * 8 + 4 * 8 * 8;
   // keep a CTA within ~half an SM's shared memory so the next kernel's CTA
   // (launched early by PDL) can be resident and prefetch its weights
-  static constexpr int kBudget = 110 * 1024;
-  static constexpr int kFixed = 1024 /*align*/ + 256 /*barriers*/ + kXchBytes + kRedBytes;
+  // (q4 stages are a quarter as large; a deeper ring keeps enough packed
+  // bytes in flight)
+  static constexpr int kBudget = (Q4 ? 150 : 110) * 1024;
+  static constexpr int kFixed = 1024 /*align*/ + kBarBytes + kXchBytes + kRedBytes + kDeq * kWTileBytes;
   static constexpr int kStagesRaw = (kBudget - kFixed) / kStageBytes;
-  static constexpr int kStages = kStagesRaw < 2 ? 2 : (kStagesRaw > 8 ? 8 : kStagesRaw);
+  static constexpr int kMaxStages = Q4 ? 16 : 8;
+  static constexpr int kStages = kStagesRaw < 2 ? 2 : (kStagesRaw > kMaxStages ? kMaxStages : kStagesRaw);
   static constexpr int kSmem = kFixed + kStages * kStageBytes;
   static constexpr int kTmemCols = (2 * TPAD <= 32) ? 32 : (2 * TPAD <= 64 ? 64 : (2 * TPAD <= 128 ? 128 : 256));
   static constexpr uint32_t kIdesc = idesc_bf16_f32(128, TPAD);
@@ -99,24 +119,59 @@ __device__ __forceinline__ int sk_cta_of(long long u, long long U, int G) {
 
 __device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
 
-template <int TPAD, int EPI>
-__global__ void __launch_bounds__(kGemmThreads, 1)
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
+  uint32_t d;
+  asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(sel));
+  return d;
+}
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+__device__ __forceinline__ __nv_bfloat162 u32_as_bf162(uint32_t v) { return *reinterpret_cast<__nv_bfloat162*>(&v); }
+__device__ __forceinline__ uint32_t bf162_as_u32(__nv_bfloat162 v) { return *reinterpret_cast<uint32_t*>(&v); }
+
+// 8 packed 4-bit weights (one uint32, element i in bits 4i..4i+3) -> 8 bf16
+// scale*q + bias as 4 bf16x2 words in element order.  (0x43 << 8 | q) is the
+// bf16 of 128 + q exactly, so (128 + q) - 128 = q exactly and the fma rounds
+// once.
+__device__ __forceinline__ uint4 dequant8(uint32_t x, __nv_bfloat162 s2, __nv_bfloat162 b2) {
+  const uint32_t lo = x & 0x0F0F0F0Fu;         // elements 0,2,4,6 (one per byte)
+  const uint32_t hi = (x >> 4) & 0x0F0F0F0Fu;  // elements 1,3,5,7
+  const uint32_t a = prmt(lo, hi, 0x5140u);    // bytes q0 q1 q2 q3
+  const uint32_t b = prmt(lo, hi, 0x7362u);    // bytes q4 q5 q6 q7
+  const uint32_t c43 = 0x43434343u;
+  const __nv_bfloat162 k128 = u32_as_bf162(0x43004300u);
+  uint4 o;
+  o.x = bf162_as_u32(__hfma2(__hsub2(u32_as_bf162(prmt(a, c43, 0x4140u)), k128), s2, b2));
+  o.y = bf162_as_u32(__hfma2(__hsub2(u32_as_bf162(prmt(a, c43, 0x4342u)), k128), s2, b2));
+  o.z = bf162_as_u32(__hfma2(__hsub2(u32_as_bf162(prmt(b, c43, 0x4140u)), k128), s2, b2));
+  o.w = bf162_as_u32(__hfma2(__hsub2(u32_as_bf162(prmt(b, c43, 0x4342u)), k128), s2, b2));
+  return o;
+}
+
+template <int TPAD, int EPI, bool Q4>
+__global__ void __launch_bounds__(Q4 ? kGemmThreadsQ4 : kGemmThreads, 1)
     gemm_streamk_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_x,
                         GemmParams p) {
-  using C = GemmCfg<TPAD, EPI>;
+  using C = GemmCfg<TPAD, EPI, Q4>;
   constexpr int S = C::kStages;
+  constexpr int D = C::kDeq > 0 ? C::kDeq : 1;  // (bf16: deq barriers unused)
   pdl_trigger();
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* stage_base = smem;
-  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + S * C::kStageBytes);
+  uint8_t* deq_base = smem + S * C::kStageBytes;  // [D][128 rows x 128 B] swizzled bf16 W (q4 only)
+  uint8_t* bar_base = deq_base + C::kDeq * kWTileBytes;
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(bar_base);
   uint64_t* empty_bar = full_bar + S;
   uint64_t* tfull_bar = empty_bar + S;
   uint64_t* tempty_bar = tfull_bar + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty_bar + 2);
+  uint64_t* deq_full = tempty_bar + 2;   // [D] (q4 only)
+  uint64_t* deq_empty = deq_full + D;    // [D]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(deq_empty + D);
   int* s_flag = reinterpret_cast<int*>(tmem_slot + 1);
-  float* xch = reinterpret_cast<float*>(smem + S * C::kStageBytes + 256);
-  uint8_t* red_raw = smem + S * C::kStageBytes + 256 + C::kXchBytes;
+  float* xch = reinterpret_cast<float*>(bar_base + C::kBarBytes);
+  uint8_t* red_raw = bar_base + C::kBarBytes + C::kXchBytes;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int G = p.grid;
@@ -143,6 +198,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         mbar_init(&tfull_bar[b], 1);
         mbar_init(&tempty_bar[b], 4);
       }
+      for (int b = 0; b < D; ++b) {
+        mbar_init(&deq_full[b], 8);  // one arrival per dequant warp
+        mbar_init(&deq_empty[b], 1);
+      }
       fence_barrier_init();
       tma_prefetch_desc(&tmap_w);
       tma_prefetch_desc(&tmap_x);
@@ -166,12 +225,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         const long long u = u0 + i;
         const int tile = static_cast<int>(u / p.kb), kblk = static_cast<int>(u % p.kb);
         mbar_arrive_expect_tx(&full_bar[i], C::kStageBytes);
-        tma_load_2d(stage_base + i * C::kStageBytes, &tmap_w, &full_bar[i], kblk * 64, tile * 128, pol_w);
+        tma_load_2d(stage_base + i * C::kStageBytes + C::kWOff, &tmap_w, &full_bar[i], kblk * (Q4 ? 8 : 64),
+                    tile * 128, pol_w);
       }
       pdl_wait();
       for (int i = 0; i < pre; ++i) {
         const int kblk = static_cast<int>((u0 + i) % p.kb);
-        tma_load_2d(stage_base + i * C::kStageBytes + kWTileBytes, &tmap_x, &full_bar[i], kblk * 64, 0, pol_x);
+        tma_load_2d(stage_base + i * C::kStageBytes + C::kXOff, &tmap_x, &full_bar[i], kblk * 64, 0, pol_x);
       }
       bool ok = true;
       for (int i = pre; i < n_units && ok; ++i) {
@@ -183,8 +243,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         const int tile = static_cast<int>(u / p.kb), kblk = static_cast<int>(u % p.kb);
         mbar_arrive_expect_tx(&full_bar[s], C::kStageBytes);
         uint8_t* st = stage_base + s * C::kStageBytes;
-        tma_load_2d(st, &tmap_w, &full_bar[s], kblk * 64, tile * 128, pol_w);
-        tma_load_2d(st + kWTileBytes, &tmap_x, &full_bar[s], kblk * 64, 0, pol_x);
+        tma_load_2d(st + C::kWOff, &tmap_w, &full_bar[s], kblk * (Q4 ? 8 : 64), tile * 128, pol_w);
+        tma_load_2d(st + C::kXOff, &tmap_x, &full_bar[s], kblk * 64, 0, pol_x);
       }
       // drain: every issued load must land before the CTA can retire
       const int first_undrained = n_units > S ? n_units - S : 0;
@@ -209,10 +269,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           const int s = i % S;
           const uint32_t ph = static_cast<uint32_t>(i / S) & 1u;
           if (ok) ok = mbar_wait(&full_bar[s], ph, 4);
+          if constexpr (Q4) {
+            if (ok) ok = mbar_wait(&deq_full[i % D], static_cast<uint32_t>(i / D) & 1u, 8);
+          }
           tc_fence_after();
           if (ok) {
-            const uint32_t a_addr = smem_u32(stage_base + s * C::kStageBytes);
-            const uint32_t b_addr = a_addr + kWTileBytes;
+            const uint32_t a_addr =
+                Q4 ? smem_u32(deq_base + (i % D) * kWTileBytes) : smem_u32(stage_base + s * C::kStageBytes);
+            const uint32_t b_addr = smem_u32(stage_base + s * C::kStageBytes + C::kXOff);
 #pragma unroll
             for (int kk = 0; kk < 4; ++kk) {
               umma_bf16(d_tmem, sw128_kmajor_desc(a_addr + kk * 32), sw128_kmajor_desc(b_addr + kk * 32), C::kIdesc,
@@ -220,11 +284,87 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             }
           }
           umma_commit(&empty_bar[s]);
+          if constexpr (Q4) umma_commit(&deq_empty[i % D]);
         }
         umma_commit(&tfull_bar[b]);
         u += len;
         ++seg;
       }
+    }
+  } else if (Q4 && warp >= 6) {
+    // ------------------------------------------------------------ dequant (q4)
+    // thread t: row t/2 of the tile, half t%2 of its 64 K elements (16 packed
+    // bytes -> four 16-byte chunks of the swizzled bf16 row)
+    // Scales / biases (no upstream dependency) come 8 groups per 16-byte
+    // load when rows are 16-byte aligned (kb % 8 == 0): `cur` holds the
+    // 8-group block of the current unit, `nxt` the following block, loaded
+    // one block ahead so its latency hides behind 8 units of work.
+    const int t = threadIdx.x - kGemmThreads;
+    const int r = t >> 1, h = t & 1;
+    const bool vec = (p.kb & 7) == 0 &&
+                     ((reinterpret_cast<uintptr_t>(p.q_scales) | reinterpret_cast<uintptr_t>(p.q_biases)) & 15u) == 0;
+    long long cur_key = -1, nxt_key = -1;  // (tile * kb + first kblk) of the block held
+    uint4 cur_s = make_uint4(0, 0, 0, 0), cur_b = cur_s, nxt_s = cur_s, nxt_b = cur_s;
+    auto load_block = [&](long long ub, uint4& vs, uint4& vb) {
+      const int tl = static_cast<int>(ub / p.kb), kb0 = static_cast<int>(ub % p.kb);
+      const int nn = tl * 128 + r;
+      if (nn < p.n_out) {
+        const size_t off = static_cast<size_t>(nn) * p.kb + kb0;
+        vs = __ldg(reinterpret_cast<const uint4*>(p.q_scales + off));
+        vb = __ldg(reinterpret_cast<const uint4*>(p.q_biases + off));
+      } else {
+        vs = make_uint4(0, 0, 0, 0);
+        vb = vs;
+      }
+    };
+    bool ok = true;
+    for (int i = 0; i < n_units && ok; ++i) {
+      const long long u = u0 + i;
+      const int tile = static_cast<int>(u / p.kb), kblk = static_cast<int>(u % p.kb);
+      const int n = tile * 128 + r;
+      __nv_bfloat16 sc = __float2bfloat16_rn(0.0f), bi = sc;
+      if (vec) {
+        const long long key = u - (kblk & 7);
+        if (key != cur_key) {
+          if (key == nxt_key) {
+            cur_s = nxt_s;
+            cur_b = nxt_b;
+          } else {
+            load_block(key, cur_s, cur_b);
+          }
+          cur_key = key;
+          // prefetch the next block of this CTA's range
+          const long long nk = key + 8;
+          if (nk < u1) {
+            load_block(nk, nxt_s, nxt_b);
+            nxt_key = nk;
+          }
+        }
+        const int g = kblk & 7, wi = g >> 1;
+        const uint32_t ws = wi == 0 ? cur_s.x : wi == 1 ? cur_s.y : wi == 2 ? cur_s.z : cur_s.w;
+        const uint32_t wb = wi == 0 ? cur_b.x : wi == 1 ? cur_b.y : wi == 2 ? cur_b.z : cur_b.w;
+        const int sh = (g & 1) * 16;
+        sc = __ushort_as_bfloat16(static_cast<unsigned short>((ws >> sh) & 0xFFFFu));
+        bi = __ushort_as_bfloat16(static_cast<unsigned short>((wb >> sh) & 0xFFFFu));
+      } else if (n < p.n_out) {
+        sc = p.q_scales[static_cast<size_t>(n) * p.kb + kblk];
+        bi = p.q_biases[static_cast<size_t>(n) * p.kb + kblk];
+      }
+      const int s = i % S, d = i % D;
+      ok = mbar_wait(&full_bar[s], static_cast<uint32_t>(i / S) & 1u, 6);
+      if (ok && i >= D) ok = mbar_wait(&deq_empty[d], (static_cast<uint32_t>(i / D) & 1u) ^ 1u, 7);
+      if (!ok) break;
+      const uint4 pk = *reinterpret_cast<const uint4*>(stage_base + s * C::kStageBytes + C::kWOff + r * 32 + h * 16);
+      const __nv_bfloat162 s2 = __halves2bfloat162(sc, sc), b2 = __halves2bfloat162(bi, bi);
+      uint8_t* dst = deq_base + d * kWTileBytes + r * 128;
+      const int sw = r & 7;
+      *reinterpret_cast<uint4*>(dst + (((4 * h + 0) ^ sw) << 4)) = dequant8(pk.x, s2, b2);
+      *reinterpret_cast<uint4*>(dst + (((4 * h + 1) ^ sw) << 4)) = dequant8(pk.y, s2, b2);
+      *reinterpret_cast<uint4*>(dst + (((4 * h + 2) ^ sw) << 4)) = dequant8(pk.z, s2, b2);
+      *reinterpret_cast<uint4*>(dst + (((4 * h + 3) ^ sw) << 4)) = dequant8(pk.w, s2, b2);
+      fence_proxy_async_smem();  // generic-proxy writes -> visible to tcgen05.mma
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&deq_full[d]);
     }
   } else {
     // ------------------------------------------------------------ epilogue
@@ -513,11 +653,16 @@ struct GemmPlan {
   GemmParams p;
   int t_pad;
   int epi;
+  bool q4;
 };
 
 size_t gemm_ws_bytes(int t_pad, int grid);  // fp32 partials
 int gemm_plan(GemmPlan* plan, const void* w, int n_out, int k, const void* x, int t_pad, int x_row_stride_elems,
               int epi, int grid);
+// 4-bit affine weights (MLX layout): packed uint32 [n_out][k/8], bf16
+// scales / biases [n_out][k/64]; epilogues kEpiStore, kEpiPartial, kEpiSwiglu
+int gemm_plan_q4(GemmPlan* plan, const void* w_packed, const void* scales, const void* biases, int n_out, int k,
+                 const void* x, int t_pad, int x_row_stride_elems, int epi, int grid);
 int gemm_bind_ws(GemmPlan* plan, void* ws, size_t ws_bytes);
 int gemm_launch(const GemmPlan& plan, cudaStream_t stream);
 

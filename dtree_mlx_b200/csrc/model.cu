@@ -71,6 +71,7 @@ struct PlanSet {
 struct dtree_qwen3_model {
   dtree_qwen3_desc d;
   std::vector<dtree_qwen3_layer> layers;
+  std::vector<dtree_qwen3_q4_layer> q4_layers;
   dtree::PlanSet plans[4];
   void* gemm_ws = nullptr;
   size_t gemm_ws_bytes = 0;
@@ -106,17 +107,28 @@ static int build_plans(dtree_qwen3_model* m, int t_pad) {
   ps.o.resize(d.layers);
   ps.gu.resize(d.layers);
   ps.down.resize(d.layers);
+  const bool q4 = d.quant_bits == 4;
   for (int l = 0; l < d.layers; ++l) {
     const dtree_qwen3_layer& L = m->layers[l];
+    // bf16 or MLX 4-bit weights behind the same plan
+    auto plan = [&](GemmPlan* g, const void* w, const void* sc, const void* bi, int n, int k, const void* x,
+                    int epi, int grid) {
+      return q4 ? gemm_plan_q4(g, w, sc, bi, n, k, x, t_pad, k, epi, grid)
+                : gemm_plan(g, w, n, k, x, t_pad, k, epi, grid);
+    };
+    const dtree_qwen3_q4_layer Q = q4 ? m->q4_layers[l] : dtree_qwen3_q4_layer{};
     int rc;
-    if ((rc = gemm_plan(&ps.qkv[l], L.qkv, qkv_rows, d.hidden, d.xn, t_pad, d.hidden, kEpiPartial,
-                        proj_split(d, qkv_rows))))
+    if ((rc = plan(&ps.qkv[l], L.qkv, Q.qkv_scales, Q.qkv_biases, qkv_rows, d.hidden, d.xn, kEpiPartial,
+                   proj_split(d, qkv_rows))))
       return rc;
-    if ((rc = gemm_plan(&ps.o[l], L.o_proj, d.hidden, qd, d.attn, t_pad, qd, kEpiPartial, proj_split(d, d.hidden))))
+    if ((rc = plan(&ps.o[l], L.o_proj, Q.o_scales, Q.o_biases, d.hidden, qd, d.attn, kEpiPartial,
+                   proj_split(d, d.hidden))))
       return rc;
-    if ((rc = gemm_plan(&ps.gu[l], L.gate_up, 2 * d.ffn, d.hidden, d.xn, t_pad, d.hidden, kEpiSwiglu, 0))) return rc;
-    if ((rc = gemm_plan(&ps.down[l], L.down, d.hidden, d.ffn, d.act, t_pad, d.ffn, kEpiPartial,
-                        proj_split(d, d.hidden))))
+    if ((rc = plan(&ps.gu[l], L.gate_up, Q.gate_up_scales, Q.gate_up_biases, 2 * d.ffn, d.hidden, d.xn, kEpiSwiglu,
+                   0)))
+      return rc;
+    if ((rc = plan(&ps.down[l], L.down, Q.down_scales, Q.down_biases, d.hidden, d.ffn, d.act, kEpiPartial,
+                   proj_split(d, d.hidden))))
       return rc;
     if (ps.o[l].p.split > kMaxProjSplit || ps.down[l].p.split > kMaxProjSplit || ps.qkv[l].p.split > kMaxProjSplit)
       return fail(kErrUnsupported, "projection split exceeds the partial buffer");
@@ -171,10 +183,26 @@ extern "C" int dtree_qwen3_create(const dtree_qwen3_desc* desc, dtree_qwen3_mode
   DTREE_CHECK_ARG(d.workspace_bytes >= need[8], "workspace too small");
   for (int c = 0; c < d.n_capture; ++c)
     DTREE_CHECK_ARG(d.capture_layers[c] >= 0 && d.capture_layers[c] < d.layers, "capture layer out of range");
+  DTREE_CHECK_ARG(d.quant_bits == 0 || d.quant_bits == 16 || d.quant_bits == 4,
+                  "quant_bits must be 0/16 (bf16) or 4 (MLX affine)");
+  if (d.quant_bits == 4) {
+    DTREE_CHECK_ARG(d.group_size == 64, "4-bit weights need group_size 64");
+    DTREE_CHECK_ARG(d.q4_layer != nullptr, "null q4_layer");
+    for (int l = 0; l < d.layers; ++l) {
+      const dtree_qwen3_q4_layer& Q = d.q4_layer[l];
+      DTREE_CHECK_ARG(Q.qkv_scales && Q.qkv_biases && Q.o_scales && Q.o_biases && Q.gate_up_scales &&
+                          Q.gate_up_biases && Q.down_scales && Q.down_biases,
+                      "null q4 scales / biases");
+    }
+  }
   auto* m = new dtree_qwen3_model();
   m->d = d;
   m->layers.assign(d.layer, d.layer + d.layers);
   m->d.layer = m->layers.data();
+  if (d.quant_bits == 4) {
+    m->q4_layers.assign(d.q4_layer, d.q4_layer + d.layers);
+    m->d.q4_layer = m->q4_layers.data();
+  }
   m->gemm_ws = d.workspace;
   m->gemm_ws_bytes = gemm_ws_need(d);
   m->attn_ws = static_cast<char*>(d.workspace) + ((m->gemm_ws_bytes + 255) & ~static_cast<size_t>(255));

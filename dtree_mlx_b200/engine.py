@@ -21,9 +21,14 @@ import numpy as np
 import torch
 
 from . import _lib, kernels
-from ._lib import DTREE_MAX_TREE, Qwen3Desc, Qwen3Layer, call, ptr, stream_ptr
+from ._lib import DTREE_MAX_TREE, Qwen3Desc, Qwen3Layer, Qwen3Q4Layer, call, ptr, stream_ptr
 from .config import Qwen3Config
-from .synthetic import Qwen3Weights
+from .synthetic import Q4Tensor, Qwen3Weights
+
+
+def _wptr(t) -> int:
+    """Device pointer of a projection weight (packed words for a Q4Tensor)."""
+    return ptr(t.packed) if isinstance(t, Q4Tensor) else ptr(t)
 
 
 def pad_rows(n: int) -> int:
@@ -74,9 +79,17 @@ class Qwen3Engine:
         self._layers = (Qwen3Layer * L)()
         for i in range(L):
             self._layers[i] = Qwen3Layer(
-                ptr(weights.input_norm[i]), ptr(weights.qkv[i]), ptr(weights.q_norm[i]), ptr(weights.k_norm[i]),
-                ptr(weights.o_proj[i]), ptr(weights.post_norm[i]), ptr(weights.gate_up[i]), ptr(weights.down[i]),
+                ptr(weights.input_norm[i]), _wptr(weights.qkv[i]), ptr(weights.q_norm[i]), ptr(weights.k_norm[i]),
+                _wptr(weights.o_proj[i]), ptr(weights.post_norm[i]), _wptr(weights.gate_up[i]),
+                _wptr(weights.down[i]),
             )
+        self.quant_bits = weights.quant_bits
+        self._q4 = None
+        if self.quant_bits == 4:
+            self._q4 = (Qwen3Q4Layer * L)()
+            for i in range(L):
+                qs = [weights.qkv[i], weights.o_proj[i], weights.gate_up[i], weights.down[i]]
+                self._q4[i] = Qwen3Q4Layer(*[p for t in qs for p in (ptr(t.scales), ptr(t.biases))])
         d = Qwen3Desc()
         d.hidden, d.layers = cfg.hidden_size, L
         d.n_heads, d.n_kv_heads, d.head_dim = cfg.num_attention_heads, cfg.num_key_value_heads, cfg.head_dim
@@ -88,6 +101,9 @@ class Qwen3Engine:
             d.capture_layers[i] = l
         d.embed, d.final_norm = ptr(weights.embed), ptr(weights.final_norm)
         d.layer = C.cast(self._layers, C.POINTER(Qwen3Layer))
+        if self._q4 is not None:
+            d.quant_bits, d.group_size = 4, 64
+            d.q4_layer = C.cast(self._q4, C.POINTER(Qwen3Q4Layer))
         sizes = (C.c_size_t * 9)()
         call("dtree_qwen3_buffer_bytes", C.byref(d), sizes)
         tp = pad_rows(self.t_cap)

@@ -171,6 +171,26 @@ def linear_bf16(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor | None = Non
     return out
 
 
+def linear_q4(x: torch.Tensor, w, out: torch.Tensor | None = None, split_k: int = 0) -> torch.Tensor:
+    """x [t_pad, K] bf16 @ dequant(w)^T -> [t_pad, N] bf16, w a ``Q4Tensor``
+    (MLX affine 4-bit, group 64): mx.quantized_matmul(transpose=True)."""
+    _cuda(x, "x", torch.bfloat16)
+    _cuda(w.packed, "w.packed", torch.int32)
+    _cuda(w.scales, "w.scales", torch.bfloat16)
+    _cuda(w.biases, "w.biases", torch.bfloat16)
+    t_pad, k = x.shape
+    n, kw = w.shape
+    if kw != k:
+        raise ValueError(f"x has K={k} but w has K={kw}")
+    if out is None:
+        out = torch.empty(t_pad, n, dtype=torch.bfloat16, device=x.device)
+    nbytes = int(_lib.load().dtree_linear_workspace_bytes(t_pad, n))
+    ws = _workspace(("gemm", t_pad), nbytes, x.device)
+    call("dtree_linear_q4", ptr(x), t_pad, k, ptr(w.packed), ptr(w.scales), ptr(w.biases), n, ptr(out), ptr(ws),
+         ws.numel(), int(split_k), stream_ptr())
+    return out
+
+
 def lm_head_argmax(h: torch.Tensor, embed: torch.Tensor, n_rows: int, out: torch.Tensor | None = None):
     """argmax_v bf16(h[t] . embed[v]) for t < n_rows (first index on ties)."""
     _cuda(h, "h", torch.bfloat16)

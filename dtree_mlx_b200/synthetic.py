@@ -12,6 +12,12 @@ for the verify GEMMs:
 
 ``reference_weights()`` returns mlx-lm-named views (q_proj, gate_proj, ...)
 of the same storage for the CPU oracle.
+
+``quantize_weights(w, bits=4, group_size=64)`` turns the four projections of
+every layer into MLX affine 4-bit tensors (``Q4Tensor``: packed uint32
+[N, K/8], bf16 scales / biases [N, K/64]), which is what the reference's
+``quantize_model`` does to a loaded target (dtree_mlx/api.py:46-54).  The
+embedding (the tied LM head) and the norms stay bf16.
 """
 from __future__ import annotations
 
@@ -34,11 +40,71 @@ def interleave_gate_up(gate: torch.Tensor, up: torch.Tensor) -> torch.Tensor:
     return out
 
 
-def split_gate_up(gate_up: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
-    two_f, h = gate_up.shape
+def split_gate_up(gate_up):
+    """Inverse of ``interleave_gate_up`` (also for a ``Q4Tensor``)."""
+    if isinstance(gate_up, Q4Tensor):
+        parts = [split_gate_up(t) for t in (gate_up.packed, gate_up.scales, gate_up.biases)]
+        return tuple(Q4Tensor(*(p[i] for p in parts), gate_up.group_size) for i in range(2))
+    two_f = gate_up.shape[0]
     f = two_f // 2
-    v = gate_up.view(f // 64, 2, 64, h)
-    return v[:, 0].reshape(f, h), v[:, 1].reshape(f, h)
+    v = gate_up.view(f // 64, 2, 64, -1)
+    return v[:, 0].reshape(f, -1), v[:, 1].reshape(f, -1)
+
+
+@dataclass
+class Q4Tensor:
+    """MLX affine 4-bit matrix: w[n, k] ~ scales[n, k//64] * q[n, k] + biases[n, k//64].
+
+    ``packed`` is int32 [N, K/8] holding uint32 words, element 8j+i of a row in
+    bits 4i..4i+3 of word j (MLX ``quantize`` layout); ``scales`` and
+    ``biases`` are bf16 [N, K/64]."""
+
+    packed: torch.Tensor
+    scales: torch.Tensor
+    biases: torch.Tensor
+    group_size: int = 64
+
+    @property
+    def shape(self) -> tuple[int, int]:
+        return (self.packed.shape[0], self.packed.shape[1] * 8)
+
+    @property
+    def device(self) -> torch.device:
+        return self.packed.device
+
+    def nbytes(self) -> int:
+        return sum(t.numel() * t.element_size() for t in (self.packed, self.scales, self.biases))
+
+    def rows(self, sl) -> "Q4Tensor":
+        return Q4Tensor(self.packed[sl], self.scales[sl], self.biases[sl], self.group_size)
+
+    def to(self, device) -> "Q4Tensor":
+        return Q4Tensor(self.packed.to(device), self.scales.to(device), self.biases.to(device), self.group_size)
+
+
+def tensor_bytes(t) -> int:
+    """Bytes of a bf16 tensor or a Q4Tensor (packed + scales + biases)."""
+    return t.nbytes() if isinstance(t, Q4Tensor) else t.numel() * t.element_size()
+
+
+def quantize_affine_q4(w: torch.Tensor, group_size: int = 64) -> Q4Tensor:
+    """MLX affine quantization (documented for ``mlx.core.quantize``) with
+    bits = 4: per group of ``group_size`` consecutive inputs, beta = min,
+    alpha = max, scale = (alpha - beta) / 15, q = round((w - beta) / scale)
+    clipped to [0, 15]; scale and bias are stored in bf16."""
+    n, k = w.shape
+    if k % group_size or group_size != 64:
+        raise ValueError("group_size must be 64 and divide the input dimension")
+    g = w.float().view(n, k // group_size, group_size)
+    lo = g.amin(-1, keepdim=True)
+    hi = g.amax(-1, keepdim=True)
+    scale = ((hi - lo) / 15.0).clamp_min(1e-8)
+    q = torch.round((g - lo) / scale).clamp_(0, 15).to(torch.int64).view(n, k // 8, 8)
+    shifts = (torch.arange(8, device=w.device, dtype=torch.int64) * 4)
+    words = (q << shifts).sum(-1)  # < 2^32
+    packed = torch.where(words >= 2**31, words - 2**32, words).to(torch.int32)
+    return Q4Tensor(packed.contiguous(), scale.view(n, -1).to(torch.bfloat16).contiguous(),
+                    lo.view(n, -1).to(torch.bfloat16).contiguous(), group_size)
 
 
 @dataclass
@@ -59,22 +125,34 @@ class Qwen3Weights:
     def device(self) -> torch.device:
         return self.embed.device
 
+    @property
+    def quant_bits(self) -> int:
+        return 4 if isinstance(self.qkv[0], Q4Tensor) else 16
+
     def nbytes(self) -> int:
         ts = [self.embed, self.final_norm]
         for name in ("input_norm", "qkv", "q_norm", "k_norm", "o_proj", "post_norm", "gate_up", "down"):
             ts += getattr(self, name)
-        return sum(t.numel() * t.element_size() for t in ts)
+        return sum(tensor_bytes(t) for t in ts)
 
-    def reference_weights(self, layer: int) -> dict[str, torch.Tensor]:
-        """mlx-lm Qwen3 names for one layer (views / splits of the packed storage)."""
+    def streamed_bytes(self) -> int:
+        """Bytes one verify forward must read: embedding (tied LM head) + the
+        four projections of every layer (norm vectors are negligible)."""
+        ts = [self.embed, *self.qkv, *self.o_proj, *self.gate_up, *self.down]
+        return sum(tensor_bytes(t) for t in ts)
+
+    def reference_weights(self, layer: int) -> dict:
+        """mlx-lm Qwen3 names for one layer (views / splits of the packed
+        storage; ``Q4Tensor`` row slices when quantized)."""
         c = self.cfg
         qkv = self.qkv[layer]
         gate, up = split_gate_up(self.gate_up[layer])
+        rows = (lambda t, sl: t.rows(sl)) if isinstance(qkv, Q4Tensor) else (lambda t, sl: t[sl])
         return {
             "input_layernorm": self.input_norm[layer],
-            "q_proj": qkv[: c.q_dim],
-            "k_proj": qkv[c.q_dim : c.q_dim + c.kv_dim],
-            "v_proj": qkv[c.q_dim + c.kv_dim :],
+            "q_proj": rows(qkv, slice(0, c.q_dim)),
+            "k_proj": rows(qkv, slice(c.q_dim, c.q_dim + c.kv_dim)),
+            "v_proj": rows(qkv, slice(c.q_dim + c.kv_dim, None)),
             "q_norm": self.q_norm[layer],
             "k_norm": self.k_norm[layer],
             "o_proj": self.o_proj[layer],
@@ -90,6 +168,19 @@ class Qwen3Weights:
         for name in ("input_norm", "qkv", "q_norm", "k_norm", "o_proj", "post_norm", "gate_up", "down"):
             setattr(w, name, [mv(t) for t in getattr(self, name)])
         return w
+
+
+def quantize_weights(w: Qwen3Weights, bits: int = 4, group_size: int = 64) -> Qwen3Weights:
+    """The target after ``quantize_model(model, bits, group_size)``
+    (dtree_mlx/api.py:46-54): every layer's q/k/v, o, gate/up and down
+    projections become 4-bit affine; embedding and norms are kept."""
+    if bits != 4 or group_size != 64:
+        raise NotImplementedError("only 4-bit affine weights with group_size 64 are supported")
+    q = Qwen3Weights(w.cfg, w.embed, w.final_norm, list(w.input_norm), [], list(w.q_norm), list(w.k_norm), [],
+                     list(w.post_norm), [], [])
+    for name in ("qkv", "o_proj", "gate_up", "down"):
+        setattr(q, name, [quantize_affine_q4(t, group_size) for t in getattr(w, name)])
+    return q
 
 
 def random_qwen3_weights(cfg: Qwen3Config, seed: int = 0, device="cuda", dtype=torch.bfloat16,

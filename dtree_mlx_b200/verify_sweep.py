@@ -1,4 +1,5 @@
-"""Isolated tree-verify step timing (BASELINE config 2 sweep).
+"""Isolated tree-verify step timing (BASELINE config 2 sweep; with
+``--quant-bits 4`` the config-3 target with MLX affine 4-bit projections).
 
 Qwen3-4B shape (or another preset), bf16 random-init weights, K/V prefix of
 random bf16 values (std 1), trees built on the GPU best-first from 16 rows of
@@ -26,7 +27,7 @@ import torch
 from . import kernels
 from .config import PRESETS
 from .engine import Qwen3Engine
-from .synthetic import random_qwen3_weights
+from .synthetic import quantize_weights, random_qwen3_weights
 
 
 def dirichlet_draft_logits(rows: int, vocab: int, seed: int, support: int = 32, alpha: float = 0.1) -> np.ndarray:
@@ -42,8 +43,7 @@ def dirichlet_draft_logits(rows: int, vocab: int, seed: int, support: int = 32, 
 
 
 def algorithmic_bytes(cfg, weights, prefix: int, t: int) -> float:
-    wbytes = sum(x.numel() * x.element_size() for x in
-                 [weights.embed, *weights.qkv, *weights.o_proj, *weights.gate_up, *weights.down])
+    wbytes = weights.streamed_bytes()
     kv_row = 2 * cfg.num_key_value_heads * cfg.head_dim * 2 * cfg.num_hidden_layers
     return float(wbytes + prefix * kv_row + t * kv_row)
 
@@ -56,12 +56,15 @@ def measured_hbm_gbs() -> tuple[float, str]:
 
 
 def run(preset: str, layers: int | None, prefixes: list[int], budgets: list[int], iters: int, seed: int = 0,
-        eager_only: bool = False) -> list[dict]:
+        eager_only: bool = False, quant_bits: int = 16) -> list[dict]:
     cfg = PRESETS[preset]
     if layers:
         cfg = replace(cfg, num_hidden_layers=layers)
     dev = torch.device("cuda")
     w = random_qwen3_weights(cfg, seed=seed, device=dev)
+    if quant_bits == 4:
+        w = quantize_weights(w)
+        torch.cuda.empty_cache()
     eng = Qwen3Engine(w, kv_capacity=max(prefixes) + 160)
     g = torch.Generator(device=dev).manual_seed(seed + 1)
     eng.kv_cache.copy_(torch.randn(eng.kv_cache.shape, generator=g, device=dev).to(torch.bfloat16))
@@ -105,7 +108,7 @@ def run(preset: str, layers: int | None, prefixes: list[int], budgets: list[int]
             results.append({"prefix": P, "tree_budget": budget, "tree_rows": n, "verify_ms": round(ms, 4),
                             "algorithmic_gb": round(nbytes / 1e9, 4), "achieved_gbs": round(gbs, 1),
                             "frac_of_hbm": round(gbs / peak, 4), "peak_gbs": peak, "peak_source": peak_src,
-                            "layers": cfg.num_hidden_layers})
+                            "layers": cfg.num_hidden_layers, "quant_bits": quant_bits})
             del graph
     eng.close()
     return results
@@ -166,6 +169,8 @@ def main() -> None:
     ap.add_argument("--budget", default="8,24,64")
     ap.add_argument("--iters", type=int, default=50)
     ap.add_argument("--eager", action="store_true", help="launch eagerly (no CUDA graph), e.g. under a profiler")
+    ap.add_argument("--quant-bits", type=int, default=16, choices=[16, 4],
+                    help="4: MLX affine 4-bit projections, group 64 (BASELINE config 3)")
     ap.add_argument("--json", action="store_true")
     ap.add_argument("--launches", default=None,
                     help="summarise an ncu launch-list CSV of an --eager sweep (attention/GEMM split) and exit")
@@ -178,7 +183,7 @@ def main() -> None:
             print(json.dumps({"prefix": p, "tree_budget": b, **row}))
         return
     res = run(a.preset, a.layers, [int(x) for x in a.prefix.split(",")], [int(x) for x in a.budget.split(",")],
-              a.iters, eager_only=a.eager)
+              a.iters, eager_only=a.eager, quant_bits=a.quant_bits)
     if a.json:
         print(json.dumps(res))
     else:

@@ -173,6 +173,18 @@ DTREE_API size_t dtree_linear_workspace_bytes(int t_pad, int n);
 DTREE_API int dtree_linear_bf16(const void* x, int t_pad, int k, const void* w, int n, void* y, void* workspace,
                       size_t workspace_bytes, int split_k, void* stream);
 
+/* 4-bit affine linear: y[t, n] = sum_k x[t, k] * (scales[n, k/64] * q[n, k]
+ * + biases[n, k/64]), the forward of the MLX QuantizedLinear layers that
+ * quantize_model(bits=4, group_size=64) puts in the target (api.py:46-54;
+ * mx.quantized_matmul(transpose=True), also adapters.py:63-71).  MLX layout:
+ * w_packed uint32 [n][k/8], element 8j+i of a row in bits 4i..4i+3 of word
+ * j; scales, biases bf16 [n][k/64].  The weights are dequantized into shared
+ * memory (one bf16 rounding of scale*q + bias) and fed to the same tcgen05
+ * GEMM as dtree_linear_bf16.  k % 64 == 0; workspace as dtree_linear_bf16. */
+DTREE_API int dtree_linear_q4(const void* x, int t_pad, int k, const void* w_packed, const void* scales,
+                    const void* biases, int n, void* y, void* workspace, size_t workspace_bytes, int split_k,
+                    void* stream);
+
 /* LM head fused with argmax (adapters.py:114-118 lm_head_argmax +
  * runtime.py:12-19 at temperature 0): out[t] = argmax_v bf16(h[t]·E[v]),
  * ties to the smallest v; logits never reach HBM.  workspace:
@@ -190,7 +202,11 @@ DTREE_API int dtree_lm_head_argmax(const void* h, int t_pad, int n_rows, int hid
  *   gate_up  [2*ffn, hidden] in 64-row blocks g0 u0 g1 u1 ... (gate rows
  *            64j..64j+63 then the matching up rows)
  *   down     [hidden, ffn]
- * kv_cache: [layers][2][n_kv_heads][kv_capacity][head_dim] bf16. */
+ * kv_cache: [layers][2][n_kv_heads][kv_capacity][head_dim] bf16.
+ * With quant_bits == 4 the four projection pointers of each layer are MLX
+ * packed 4-bit weights (uint32 [rows][in/8], same row order as above) and
+ * q4_layer[l] holds their bf16 scales / biases ([rows][in/64]); embedding
+ * and norms stay bf16 (the tied LM head is not quantized). */
 typedef struct dtree_qwen3_layer {
   const void* input_norm;
   const void* qkv;
@@ -201,6 +217,17 @@ typedef struct dtree_qwen3_layer {
   const void* gate_up;
   const void* down;
 } dtree_qwen3_layer;
+
+typedef struct dtree_qwen3_q4_layer {
+  const void* qkv_scales;
+  const void* qkv_biases;
+  const void* o_scales;
+  const void* o_biases;
+  const void* gate_up_scales;
+  const void* gate_up_biases;
+  const void* down_scales;
+  const void* down_biases;
+} dtree_qwen3_q4_layer;
 
 typedef struct dtree_qwen3_desc {
   /* configuration */
@@ -225,6 +252,11 @@ typedef struct dtree_qwen3_desc {
   void* capture;      /* [t_cap, hidden*n_capture] verifier_hidden */
   void* workspace;    /* fp32 split-K / attention partials + counters */
   size_t workspace_bytes;
+  /* weight quantization: 0 / 16 = bf16; 4 = MLX affine 4-bit, group_size 64
+   * (api.py:46-54 target_quant_bits / target_quant_group_size) */
+  int quant_bits;
+  int group_size;
+  const dtree_qwen3_q4_layer* q4_layer;  /* [layers] when quant_bits == 4 */
 } dtree_qwen3_desc;
 
 typedef struct dtree_qwen3_model dtree_qwen3_model;

@@ -45,6 +45,30 @@ def apply_rope(x: torch.Tensor, positions: torch.Tensor, theta: float) -> torch.
     return torch.cat([x1 * cos - x2 * sin, x1 * sin + x2 * cos], dim=-1)
 
 
+def dequant_affine_q4(packed: torch.Tensor, scales: torch.Tensor, biases: torch.Tensor,
+                      group_size: int = 64) -> torch.Tensor:
+    """fp32 weights of an MLX affine 4-bit matrix: w[n, k] = scales[n, k/g] *
+    q[n, k] + biases[n, k/g], q = bits 4i..4i+3 of word k/8 (i = k % 8) of row
+    n.  This is the weight the reference's QuantizedLinear layers multiply by
+    after quantize_model(bits=4, group_size=64) (dtree_mlx/api.py:46-54; the
+    chunked argmax of adapters.py:63-71 goes through the same
+    quantized_matmul)."""
+    words = packed.to(torch.int64) & 0xFFFFFFFF  # [N, K/8]
+    n = words.shape[0]
+    q = torch.stack([(words >> (4 * i)) & 0xF for i in range(8)], dim=-1).reshape(n, -1).float()
+    s = scales.float().repeat_interleave(group_size, dim=1)
+    b = biases.float().repeat_interleave(group_size, dim=1)
+    return s * q + b
+
+
+def _dense(t):
+    """Oracle view of a projection weight: the tensor itself, or the fp32
+    dequantization of a 4-bit one (objects with packed / scales / biases)."""
+    if hasattr(t, "packed"):
+        return dequant_affine_q4(t.packed, t.scales, t.biases, t.group_size)
+    return t
+
+
 class Qwen3Oracle:
     """fp32 CPU model over a ``Qwen3Weights`` (weights are copied to CPU)."""
 
@@ -52,7 +76,8 @@ class Qwen3Oracle:
         self.w = weights.to("cpu") if weights.device.type != "cpu" else weights
         self.cfg = self.w.cfg
         c = self.cfg
-        self.layers = [self.w.reference_weights(i) for i in range(c.num_hidden_layers)]
+        self.layers = [{k: _dense(v) for k, v in self.w.reference_weights(i).items()}
+                       for i in range(c.num_hidden_layers)]
         self.cap = int(kv_capacity)
         self.k = [torch.zeros(c.num_key_value_heads, self.cap, c.head_dim) for _ in self.layers]
         self.v = [torch.zeros(c.num_key_value_heads, self.cap, c.head_dim) for _ in self.layers]

@@ -49,6 +49,45 @@ def test_linear_matches_fp32(K, t_pad, k, n):
     _check(y, ref)
 
 
+@pytest.mark.parametrize(
+    "t_pad,k,n,split_k",
+    [
+        (16, 64, 128, 0),
+        (32, 2560, 6144, 0),    # q|k|v of the 4B shape, stream-K
+        (32, 4096, 2560, 0),    # o_proj
+        (32, 9728, 2560, 7),    # down_proj, tile-aligned split-K grid
+        (16, 512, 200, 0),      # ragged N
+        (64, 1024, 1536, 0),
+        (128, 512, 640, 0),
+    ],
+)
+def test_linear_q4_matches_dequantized_fp32(K, t_pad, k, n, split_k):
+    """The fused dequant GEMM equals x @ bf16(scale*q + bias)^T accumulated in
+    fp32: the oracle dequantizes the MLX-packed weights independently."""
+    from dtree_mlx_b200.synthetic import quantize_affine_q4
+    from oracle.qwen3 import dequant_affine_q4
+
+    g = torch.Generator(device=DEV).manual_seed(t_pad * 5 + k + n)
+    x = torch.randn(t_pad, k, device=DEV, generator=g).to(torch.bfloat16)
+    w = quantize_affine_q4((torch.randn(n, k, device=DEV, generator=g) * 0.02).to(torch.bfloat16))
+    y = K.linear_q4(x, w, split_k=split_k)
+    torch.cuda.synchronize()
+    wd = dequant_affine_q4(w.packed.cpu(), w.scales.cpu(), w.biases.cpu()).to(torch.bfloat16).float()
+    ref = x.float().cpu() @ wd.t()
+    _check(y.cpu(), ref)
+
+
+def test_linear_q4_deterministic(K):
+    from dtree_mlx_b200.synthetic import quantize_affine_q4
+
+    g = torch.Generator(device=DEV).manual_seed(4)
+    x = torch.randn(32, 2560, device=DEV, generator=g).to(torch.bfloat16)
+    w = quantize_affine_q4((torch.randn(9728, 2560, device=DEV, generator=g) * 0.02).to(torch.bfloat16))
+    y1 = K.linear_q4(x, w).clone()
+    y2 = K.linear_q4(x, w).clone()
+    assert torch.equal(y1, y2)
+
+
 def test_linear_deterministic(K):
     g = torch.Generator(device=DEV).manual_seed(3)
     x = torch.randn(32, 9728, device=DEV, generator=g).to(torch.bfloat16)

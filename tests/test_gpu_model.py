@@ -26,13 +26,17 @@ LOGIT_MEAN_TOL = 5e-3
 REL_TOL = 2e-2
 
 
-@pytest.fixture(scope="module")
-def tiny(lib):
+@pytest.fixture(scope="module", params=["bf16", "q4"])
+def tiny(lib, request):
+    """Tiny Qwen3 target, bf16 or with MLX affine 4-bit projections (the
+    oracle dequantizes the packed weights itself)."""
     from dtree_mlx_b200.config import PRESETS
-    from dtree_mlx_b200.synthetic import random_qwen3_weights
+    from dtree_mlx_b200.synthetic import quantize_weights, random_qwen3_weights
 
     cfg = PRESETS["qwen3-tiny"]
     w = random_qwen3_weights(cfg, seed=0, device=DEV, norm_jitter=0.1)
+    if request.param == "q4":
+        w = quantize_weights(w)
     return cfg, w
 
 
@@ -161,11 +165,14 @@ def test_decode_steps_lockstep_with_oracle(tiny, mode):
     eng.close()
 
 
-def test_generate_api_tiny(lib):
+@pytest.mark.parametrize("quant_bits", [None, 4])
+def test_generate_api_tiny(lib, quant_bits):
     from dtree_mlx_b200 import DFlashGenerator
     from dtree_mlx_b200.synthetic import random_prompt
 
-    gen = DFlashGenerator(target_model="synthetic:qwen3-tiny:seed=0:kv=1024", draft_model="planted:p=0.8:seed=1")
+    gen = DFlashGenerator(target_model="synthetic:qwen3-tiny:seed=0:kv=1024", draft_model="planted:p=0.8:seed=1",
+                          target_quant_bits=quant_bits)
+    assert gen.target_quantization == (None if quant_bits is None else {"group_size": 64, "bits": 4})
     prompt = random_prompt(128, 32768, seed=0)
     r_tree = gen.generate_from_tokens(prompt, max_new_tokens=64, decode_mode="dtree", speculative_tokens=16,
                                       tree_budget=24)
