@@ -109,6 +109,41 @@ class Qwen3Desc(C.Structure):
     ]
 
 
+class Qwen35LinearLayer(C.Structure):
+    _fields_ = [(n, C.c_void_p) for n in ("input_norm", "in_proj", "conv_weight", "norm", "out_proj", "post_norm",
+                                          "gate_up", "down")]
+
+
+class Qwen35AttnLayer(C.Structure):
+    _fields_ = [(n, C.c_void_p) for n in ("input_norm", "qkv", "q_norm", "k_norm", "o_proj", "post_norm", "gate_up",
+                                          "down")]
+
+
+class Qwen35Desc(C.Structure):
+    _fields_ = [
+        *[(n, C.c_int) for n in ("hidden", "layers", "full_attention_interval", "ffn", "vocab", "n_heads",
+                                  "n_kv_heads", "head_dim")],
+        ("rope_theta", C.c_float),
+        ("partial_rotary_factor", C.c_float),
+        ("rms_eps", C.c_float),
+        *[(n, C.c_int) for n in ("lin_k_heads", "lin_v_heads", "lin_k_dim", "lin_v_dim", "conv_kernel", "t_cap",
+                                  "kv_capacity", "n_capture")],
+        ("capture_layers", C.c_int * 16),
+        ("embed", C.c_void_p),
+        ("final_norm", C.c_void_p),
+        ("linear_layers", C.POINTER(Qwen35LinearLayer)),
+        ("attn_layers", C.POINTER(Qwen35AttnLayer)),
+        ("a_log", C.c_void_p),
+        ("dt_bias", C.c_void_p),
+        *[(n, C.c_void_p) for n in ("kv_cache", "conv_state", "rec_state", "h", "xn", "q", "gate", "attn", "act",
+                                     "norm_out", "capture", "lin_proj", "lin_qkv", "workspace")],
+        ("workspace_bytes", C.c_size_t),
+    ]
+
+
+QWEN35_BUFFERS = ("kv_cache", "conv_state", "rec_state", "h", "xn", "q", "gate", "attn", "act", "norm_out",
+                  "capture", "lin_proj", "lin_qkv", "workspace")
+
 P = C.c_void_p
 I = C.c_int
 SZ = C.c_size_t
@@ -132,6 +167,15 @@ PROTOTYPES = {
     "dtree_linear_workspace_bytes": (SZ, [I, I]),
     "dtree_linear_bf16": (I, [P, I, I, P, I, P, P, SZ, I, P]),
     "dtree_linear_q4": (I, [P, I, I, P, P, P, I, P, P, SZ, I, P]),
+    "dtree_tree_conv1d": (I, [P, I, P, P, P, I, I, I, I, P, P, P]),
+    "dtree_tree_gated_delta": (I, [P, P, P, P, P, P, P, I, I, I, I, I, I, I, P, P, P]),
+    "dtree_gated_delta_commit": (I, [P, P, P, P, P, P, P, I, I, I, I, I, I, I, P, P]),
+    "dtree_conv_state_commit": (I, [P, I, P, P, P, I, I, I, I, P, P]),
+    "dtree_qwen35_buffer_bytes": (I, [C.POINTER(Qwen35Desc), C.POINTER(C.c_size_t)]),
+    "dtree_qwen35_create": (I, [C.POINTER(Qwen35Desc), C.POINTER(C.c_void_p)]),
+    "dtree_qwen35_destroy": (I, [P]),
+    "dtree_qwen35_forward": (I, [P, P, P, P, P, I, I, P, P, P]),
+    "dtree_qwen35_commit": (I, [P, P, P, P, P]),
     "dtree_lm_head_workspace_bytes": (SZ, [I]),
     "dtree_lm_head_argmax": (I, [P, I, I, I, P, I, P, P, SZ, P]),
     "dtree_qwen3_buffer_bytes": (I, [C.POINTER(Qwen3Desc), C.POINTER(C.c_size_t)]),

@@ -77,3 +77,95 @@ def default_layer_ids(cfg: Qwen3Config, n: int = 5) -> list[int]:
     if n == 1:
         return [L - 1]
     return sorted({round(1 + i * (L - 3) / (n - 1)) for i in range(n)})
+
+
+@dataclass(frozen=True)
+class Qwen35Config:
+    """Qwen3.5 text model (dtree_mlx/custom_qwen35_model.py:716-774 TextModelArgs):
+    gated DeltaNet layers, every ``full_attention_interval``-th layer a gated
+    full-attention layer with partial RoPE."""
+
+    hidden_size: int
+    num_hidden_layers: int
+    intermediate_size: int
+    vocab_size: int
+    num_attention_heads: int
+    num_key_value_heads: int
+    head_dim: int
+    linear_num_key_heads: int
+    linear_num_value_heads: int
+    linear_key_head_dim: int
+    linear_value_head_dim: int
+    linear_conv_kernel_dim: int = 4
+    full_attention_interval: int = 4
+    rope_theta: float = 100_000.0
+    partial_rotary_factor: float = 0.25
+    rms_norm_eps: float = 1e-6
+    tie_word_embeddings: bool = True
+    model_type: str = "qwen3_5"
+
+    def is_linear(self, layer: int) -> bool:
+        return (layer + 1) % self.full_attention_interval != 0
+
+    @property
+    def key_dim(self) -> int:
+        return self.linear_num_key_heads * self.linear_key_head_dim
+
+    @property
+    def value_dim(self) -> int:
+        return self.linear_num_value_heads * self.linear_value_head_dim
+
+    @property
+    def conv_dim(self) -> int:
+        return 2 * self.key_dim + self.value_dim
+
+    @property
+    def q_dim(self) -> int:
+        return self.num_attention_heads * self.head_dim
+
+    @property
+    def kv_dim(self) -> int:
+        return self.num_key_value_heads * self.head_dim
+
+    @property
+    def n_linear(self) -> int:
+        return sum(1 for l in range(self.num_hidden_layers) if self.is_linear(l))
+
+    @property
+    def n_attn(self) -> int:
+        return self.num_hidden_layers - self.n_linear
+
+    def as_dict(self) -> dict:
+        return asdict(self)
+
+
+QWEN35_PRESETS: dict[str, Qwen35Config] = {
+    # BASELINE config 4: Qwen3.5-9B-style hybrid (3 DeltaNet : 1 full attention)
+    "qwen35-9b": Qwen35Config(
+        hidden_size=4096,
+        num_hidden_layers=32,
+        intermediate_size=12288,
+        vocab_size=248320,
+        num_attention_heads=16,
+        num_key_value_heads=4,
+        head_dim=256,
+        linear_num_key_heads=16,
+        linear_num_value_heads=32,
+        linear_key_head_dim=128,
+        linear_value_head_dim=128,
+    ),
+    # small model of the same architecture for parity tests
+    "qwen35-tiny": Qwen35Config(
+        hidden_size=512,
+        num_hidden_layers=4,
+        intermediate_size=1024,
+        vocab_size=8192,
+        num_attention_heads=4,
+        num_key_value_heads=2,
+        head_dim=256,
+        linear_num_key_heads=2,
+        linear_num_value_heads=4,
+        linear_key_head_dim=128,
+        linear_value_head_dim=128,
+    ),
+}

@@ -12,6 +12,12 @@
 // 64-key K/V chunks through shared memory with cp.async double buffering, and
 // runs bf16 mma.sync with an fp32 online softmax.  Partial (m, l, O) go to a
 // workspace; attn_combine_kernel merges the splits (log-sum-exp) into bf16.
+//
+// head_dim 256 (Qwen3.5 full attention): a CTA computes QK^T over all 256
+// features but only one 128-wide half of V / O (grid z = kv head x half),
+// which keeps the per-thread accumulators within the register file.  The
+// combine optionally applies the Qwen3.5 output gate: out =
+// bf16(bf16(o) * bf16(sigmoid(gate))) (qwen35_tree.py:537-538).
 #include "attention.cuh"
 
 namespace dtree {
@@ -22,12 +28,15 @@ constexpr int kAttnWarps = 8;
 constexpr int kAttnRows = kAttnWarps * 16;
 constexpr int kChunk = 64;
 
-template <int HD>
+template <int HD, int HDV = HD>
 struct AttnCfg {
-  static constexpr int kLd = HD + 8;  // padded smem row (bank-conflict free ldmatrix)
+  static constexpr int kLd = HD + 8;    // padded smem row (bank-conflict free ldmatrix)
+  static constexpr int kLdV = HDV + 8;
   static constexpr int kQBytes = kAttnRows * kLd * 2;
-  static constexpr int kKVBytes = kChunk * kLd * 2;
-  static constexpr int kSmem = kQBytes + 4 * kKVBytes;  // Q + 2 x (K, V)
+  static constexpr int kKBytes = kChunk * kLd * 2;
+  static constexpr int kVBytes = kChunk * kLdV * 2;
+  static constexpr int kSmem = kQBytes + 2 * (kKBytes + kVBytes);  // Q + 2 x (K, V)
+  static constexpr bool kQInRegs = HD <= 128;  // else Q fragments are re-read from smem
 };
 
 __device__ __forceinline__ void cp_async16(void* smem, const void* gmem, bool pred) {
@@ -70,16 +79,19 @@ __device__ __forceinline__ int attn_keys_per_split(int L, int splits) {
   return ((kps + kChunk - 1) / kChunk) * kChunk;
 }
 
-template <int HD>
+template <int HD, int HDV>
 __global__ void __launch_bounds__(kAttnWarps * 32) tree_attn_kernel(AttnParams p) {
-  using C = AttnCfg<HD>;
+  using C = AttnCfg<HD, HDV>;
   constexpr int LD = C::kLd;
+  constexpr int LDV = C::kLdV;
+  constexpr int NVH = HD / HDV;  // V halves
   pdl_trigger();
   extern __shared__ __align__(128) uint8_t smem_raw[];
   __nv_bfloat16* sq = reinterpret_cast<__nv_bfloat16*>(smem_raw);
-  __nv_bfloat16* skv = reinterpret_cast<__nv_bfloat16*>(smem_raw + C::kQBytes);  // [2][K|V][kChunk][LD]
+  uint8_t* skv = smem_raw + C::kQBytes;  // [2][K (kChunk x LD) | V (kChunk x LDV)]
 
-  const int split = blockIdx.x, rb = blockIdx.y, kvh = blockIdx.z;
+  const int split = blockIdx.x, rb = blockIdx.y, kvh = blockIdx.z / NVH;
+  const int v_off = (blockIdx.z % NVH) * HDV;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int G = p.n_q_heads / p.n_kv_heads;
   const int T = p.n_nodes;
@@ -108,17 +120,30 @@ __global__ void __launch_bounds__(kAttnWarps * 32) tree_attn_kernel(AttnParams p
 
   const __nv_bfloat16* kplane = p.k + static_cast<size_t>(kvh) * p.cap * HD;
   const __nv_bfloat16* vplane = p.v + static_cast<size_t>(kvh) * p.cap * HD;
+  constexpr int VPRV = HDV / 8;
+  auto sk_of = [&](int buf) {
+    return reinterpret_cast<__nv_bfloat16*>(skv + buf * (C::kKBytes + C::kVBytes));
+  };
+  auto sv_of = [&](int buf) {
+    return reinterpret_cast<__nv_bfloat16*>(skv + buf * (C::kKBytes + C::kVBytes) + C::kKBytes);
+  };
   auto load_chunk = [&](int c, int buf) {
     const int key0 = k_begin + c * kChunk;
-    __nv_bfloat16* sk = skv + (buf * 2 + 0) * kChunk * LD;
-    __nv_bfloat16* sv = skv + (buf * 2 + 1) * kChunk * LD;
+    __nv_bfloat16* sk = sk_of(buf);
+    __nv_bfloat16* sv = sv_of(buf);
     for (int e = threadIdx.x; e < kChunk * VPR; e += blockDim.x) {
       const int r = e / VPR, v = e % VPR;
       const int key = key0 + r;
       const bool ok = key < k_end;
       const size_t off = static_cast<size_t>(ok ? key : 0) * HD + v * 8;
       cp_async16(sk + r * LD + v * 8, kplane + off, ok);
-      cp_async16(sv + r * LD + v * 8, vplane + off, ok);
+    }
+    for (int e = threadIdx.x; e < kChunk * VPRV; e += blockDim.x) {
+      const int r = e / VPRV, v = e % VPRV;
+      const int key = key0 + r;
+      const bool ok = key < k_end;
+      const size_t off = static_cast<size_t>(ok ? key : 0) * HD + v_off + v * 8;
+      cp_async16(sv + r * LDV + v * 8, vplane + off, ok);
     }
   };
   if (n_chunks > 0) load_chunk(0, 0);
@@ -139,18 +164,22 @@ __global__ void __launch_bounds__(kAttnWarps * 32) tree_attn_kernel(AttnParams p
 
   cp_async_wait<1>();  // Q landed
   __syncthreads();
-  uint32_t qf[HD / 16][4];
-#pragma unroll
-  for (int kk = 0; kk < HD / 16; ++kk) {
+  auto load_qf = [&](int kk, uint32_t (&f)[4]) {
     const int mi = lane >> 3, i = lane & 7;
     const int r = warp * 16 + i + 8 * (mi & 1);
     const int col = kk * 16 + 8 * (mi >> 1);
-    ldmatrix_x4(qf[kk], sq + r * LD + col);
+    ldmatrix_x4(f, sq + r * LD + col);
+  };
+  constexpr int QF = C::kQInRegs ? HD / 16 : 1;
+  uint32_t qf[QF][4];
+  if constexpr (C::kQInRegs) {
+#pragma unroll
+    for (int kk = 0; kk < HD / 16; ++kk) load_qf(kk, qf[kk]);
   }
 
-  float o[HD / 8][4];
+  float o[HDV / 8][4];
 #pragma unroll
-  for (int j = 0; j < HD / 8; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.0f;
+  for (int j = 0; j < HDV / 8; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.0f;
   float m_run[2] = {-INFINITY, -INFINITY}, l_run[2] = {0.0f, 0.0f};
 
   for (int c = 0; c < n_chunks; ++c) {
@@ -159,23 +188,40 @@ __global__ void __launch_bounds__(kAttnWarps * 32) tree_attn_kernel(AttnParams p
     cp_async_commit();
     cp_async_wait<1>();
     __syncthreads();
-    const __nv_bfloat16* sk = skv + (buf * 2 + 0) * kChunk * LD;
-    const __nv_bfloat16* sv = skv + (buf * 2 + 1) * kChunk * LD;
+    const __nv_bfloat16* sk = sk_of(buf);
+    const __nv_bfloat16* sv = sv_of(buf);
     const int key0 = k_begin + c * kChunk;
 
     // S = Q K^T  (16 rows x 64 keys per warp)
     float s[kChunk / 8][4];
 #pragma unroll
     for (int nt = 0; nt < kChunk / 8; ++nt) s[nt][0] = s[nt][1] = s[nt][2] = s[nt][3] = 0.0f;
+    if constexpr (C::kQInRegs) {
 #pragma unroll
-    for (int nt = 0; nt < kChunk / 8; ++nt) {
+      for (int nt = 0; nt < kChunk / 8; ++nt) {
 #pragma unroll
+        for (int kk = 0; kk < HD / 16; kk += 2) {
+          uint32_t b[4];
+          const int mi = lane >> 3, i = lane & 7;
+          ldmatrix_x4(b, sk + (nt * 8 + i) * LD + kk * 16 + 8 * mi);
+          mma_bf16_16816(s[nt], qf[kk], b[0], b[1]);
+          mma_bf16_16816(s[nt], qf[kk + 1], b[2], b[3]);
+        }
+      }
+    } else {
+#pragma unroll 1
       for (int kk = 0; kk < HD / 16; kk += 2) {
-        uint32_t b[4];
-        const int mi = lane >> 3, i = lane & 7;
-        ldmatrix_x4(b, sk + (nt * 8 + i) * LD + kk * 16 + 8 * mi);
-        mma_bf16_16816(s[nt], qf[kk], b[0], b[1]);
-        mma_bf16_16816(s[nt], qf[kk + 1], b[2], b[3]);
+        uint32_t qa[4], qb[4];
+        load_qf(kk, qa);
+        load_qf(kk + 1, qb);
+#pragma unroll
+        for (int nt = 0; nt < kChunk / 8; ++nt) {
+          uint32_t b[4];
+          const int mi = lane >> 3, i = lane & 7;
+          ldmatrix_x4(b, sk + (nt * 8 + i) * LD + kk * 16 + 8 * mi);
+          mma_bf16_16816(s[nt], qa, b[0], b[1]);
+          mma_bf16_16816(s[nt], qb, b[2], b[3]);
+        }
       }
     }
     // mask + online softmax (log2 domain)
@@ -226,7 +272,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32) tree_attn_kernel(AttnParams p
       l_run[h] = l_run[h] * alpha[h] + rs[h];
     }
 #pragma unroll
-    for (int j = 0; j < HD / 8; ++j) {
+    for (int j = 0; j < HDV / 8; ++j) {
       o[j][0] *= alpha[0];
       o[j][1] *= alpha[0];
       o[j][2] *= alpha[1];
@@ -237,10 +283,10 @@ __global__ void __launch_bounds__(kAttnWarps * 32) tree_attn_kernel(AttnParams p
     for (int kt = 0; kt < kChunk / 16; ++kt) {
       const uint32_t a[4] = {pf[kt][0], pf[kt][1], pf[kt][2], pf[kt][3]};
 #pragma unroll
-      for (int nt = 0; nt < HD / 8; nt += 2) {
+      for (int nt = 0; nt < HDV / 8; nt += 2) {
         uint32_t b[4];
         const int mi = lane >> 3, i = lane & 7;
-        ldmatrix_x4_trans(b, sv + (kt * 16 + i + 8 * (mi & 1)) * LD + nt * 8 + 8 * (mi >> 1));
+        ldmatrix_x4_trans(b, sv + (kt * 16 + i + 8 * (mi & 1)) * LDV + nt * 8 + 8 * (mi >> 1));
         mma_bf16_16816(o[nt], a, b[0], b[1]);
         mma_bf16_16816(o[nt + 1], a, b[2], b[3]);
       }
@@ -255,13 +301,13 @@ __global__ void __launch_bounds__(kAttnWarps * 32) tree_attn_kernel(AttnParams p
     if (!row_ok[h]) continue;
     const int g = row_g[h] / T, t = node[h];
     const int qrow = (kvh * G + g) * T + t;  // [head][node]
-    float* po = p.part_o + (static_cast<size_t>(split) * rows_total + qrow) * HD;
+    float* po = p.part_o + (static_cast<size_t>(split) * rows_total + qrow) * HD + v_off;
 #pragma unroll
-    for (int j = 0; j < HD / 8; ++j) {
+    for (int j = 0; j < HDV / 8; ++j) {
       const int d = j * 8 + 2 * (lane & 3);
       *reinterpret_cast<float2*>(po + d) = make_float2(o[j][2 * h], o[j][2 * h + 1]);
     }
-    if ((lane & 3) == 0) {
+    if ((lane & 3) == 0 && v_off == 0) {
       float* pml = p.part_ml + (static_cast<size_t>(split) * rows_total + qrow) * 2;
       pml[0] = m_run[h];
       pml[1] = l_run[h];
@@ -319,7 +365,12 @@ __global__ void attn_combine_kernel(AttnParams p) {
     acc += s_w[s + 3] * o3;
   }
   for (; s < active; ++s) acc += s_w[s] * p.part_o[(static_cast<size_t>(s) * rows_total + qrow) * HD + d];
-  p.out[static_cast<size_t>(t) * p.ldq + head * HD + d] = __float2bfloat16_rn(acc * s_inv_l);
+  float o = acc * s_inv_l;
+  if (p.gate) {
+    const float gt = __bfloat162float(p.gate[static_cast<size_t>(t) * p.ldq + head * HD + d]);
+    o = bf16_round(o) * bf16_round(1.0f / (1.0f + expf(-gt)));
+  }
+  p.out[static_cast<size_t>(t) * p.ldq + head * HD + d] = __float2bfloat16_rn(o);
 }
 
 size_t attn_ws_bytes(int n_q_heads, int t_pad, int head_dim, int splits) {
@@ -337,9 +388,21 @@ int attn_default_splits(int n_kv_heads, int n_q_heads, int n_nodes) {
   return s;
 }
 
+template <int HD, int HDV>
+static int attn_launch_t(const AttnParams& p, int rb, cudaStream_t stream) {
+  const int smem = AttnCfg<HD, HDV>::kSmem;
+  auto kern = tree_attn_kernel<HD, HDV>;
+  DTREE_CUDA_RET(ensure_smem_attr(kern, smem));
+  dim3 grid(p.splits, rb, p.n_kv_heads * (HD / HDV));
+  DTREE_CUDA_RET(launch_pdl(kern, grid, dim3(kAttnWarps * 32), static_cast<size_t>(smem), stream, p));
+  DTREE_CUDA_RET(launch_pdl(attn_combine_kernel<HD>, dim3(p.n_q_heads * p.n_nodes), dim3(HD), 0, stream, p));
+  return kOk;
+}
+
 int attn_launch(const AttnParams& p0, int head_dim, void* ws, size_t ws_bytes, cudaStream_t stream) {
   AttnParams p = p0;
-  DTREE_CHECK_ARG(head_dim == 64 || head_dim == 128, "tree attention supports head_dim 64 or 128");
+  DTREE_CHECK_ARG(head_dim == 64 || head_dim == 128 || head_dim == 256,
+                  "tree attention supports head_dim 64, 128 or 256");
   DTREE_CHECK_ARG(p.n_nodes > 0 && p.n_nodes <= DTREE_MAX_TREE, "n_nodes out of range");
   DTREE_CHECK_ARG(p.n_q_heads % p.n_kv_heads == 0, "n_q_heads must be a multiple of n_kv_heads");
   const size_t need = attn_ws_bytes(p.n_q_heads, p.n_nodes, head_dim, p.splits);
@@ -350,19 +413,9 @@ int attn_launch(const AttnParams& p0, int head_dim, void* ws, size_t ws_bytes, c
                                        ((static_cast<size_t>(p.splits) * rows * head_dim * 4 + 255) & ~static_cast<size_t>(255)));
   const int G = p.n_q_heads / p.n_kv_heads;
   const int rb = (G * p.n_nodes + kAttnRows - 1) / kAttnRows;
-  dim3 grid(p.splits, rb, p.n_kv_heads);
-  if (head_dim == 128) {
-    const int smem = AttnCfg<128>::kSmem;
-    DTREE_CUDA_RET(ensure_smem_attr(tree_attn_kernel<128>, smem));
-    DTREE_CUDA_RET(launch_pdl(tree_attn_kernel<128>, grid, dim3(kAttnWarps * 32), static_cast<size_t>(smem), stream, p));
-    DTREE_CUDA_RET(launch_pdl(attn_combine_kernel<128>, dim3(p.n_q_heads * p.n_nodes), dim3(128), 0, stream, p));
-  } else {
-    const int smem = AttnCfg<64>::kSmem;
-    DTREE_CUDA_RET(ensure_smem_attr(tree_attn_kernel<64>, smem));
-    DTREE_CUDA_RET(launch_pdl(tree_attn_kernel<64>, grid, dim3(kAttnWarps * 32), static_cast<size_t>(smem), stream, p));
-    DTREE_CUDA_RET(launch_pdl(attn_combine_kernel<64>, dim3(p.n_q_heads * p.n_nodes), dim3(64), 0, stream, p));
-  }
-  return kOk;
+  if (head_dim == 256) return attn_launch_t<256, 128>(p, rb, stream);
+  if (head_dim == 128) return attn_launch_t<128, 128>(p, rb, stream);
+  return attn_launch_t<64, 64>(p, rb, stream);
 }
 
 }  // namespace dtree

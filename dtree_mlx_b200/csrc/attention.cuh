@@ -22,6 +22,7 @@ struct AttnParams {
   float* part_ml;       // [splits][n_q_heads*n_nodes][2]
   __nv_bfloat16* out;   // [t_pad][n_q_heads*hd]
   int causal_prefix;    // unused (0): tree mask only
+  const __nv_bfloat16* gate;  // [t_pad][n_q_heads*hd] output gate (nullable)
 };
 
 size_t attn_ws_bytes(int n_q_heads, int t_pad, int head_dim, int splits);

@@ -46,6 +46,9 @@ struct QkvFinishParams {
   __nv_bfloat16* k_cache;
   __nv_bfloat16* v_cache;
   int kv_cap;
+  int gated;
+  __nv_bfloat16* gate_out;
+  int rot_dims;
 };
 int qkv_finish_launch(const QkvFinishParams& p, int n_rows, cudaStream_t stream);
 

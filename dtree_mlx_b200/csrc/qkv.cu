@@ -4,6 +4,13 @@
 //         node's position, q -> q buffer, k -> K cache slot start + t
 //   v:    -> V cache slot start + t
 // grid = (n_rows, n_q_heads + 2 * n_kv_heads), block = head_dim threads.
+//
+// Gated variant (Qwen3.5 full attention, qwen35_tree.py:500-527): each q
+// head's projection rows are [q (head_dim) | gate (head_dim)]; the gate is
+// written (bf16) to gate_out for the attention output gating, and RoPE
+// rotates only the first rot_dims features (partial_rotary_factor), pairs
+// (i, i + rot_dims/2) with inv_freq_i = theta^(-2i/rot_dims) (mlx RoPE with
+// dims = rot_dims, traditional = False); the rest pass through.
 #include "common.cuh"
 #include "../../include/dtree_b200.h"
 
@@ -22,6 +29,9 @@ struct QkvFinishParams {
   __nv_bfloat16* k_cache;  // [n_kv_heads][kv_cap][head_dim]
   __nv_bfloat16* v_cache;
   int kv_cap;
+  int gated;                // q rows are [q | gate] per head
+  __nv_bfloat16* gate_out;  // [t_pad][n_q_heads*head_dim] (gated only)
+  int rot_dims;             // rotated features per head (0: all)
 };
 
 __global__ void __launch_bounds__(256) qkv_finish_kernel(QkvFinishParams p) {
@@ -31,11 +41,12 @@ __global__ void __launch_bounds__(256) qkv_finish_kernel(QkvFinishParams p) {
   const int t = blockIdx.x, gh = blockIdx.y, d = threadIdx.x;
   const int hd = p.head_dim;
   pdl_wait();
-  const int col = gh * hd + d;
-  float a = 0.0f;
-  {
-    const float* src = p.partials + static_cast<size_t>(t) * p.width + col;
-    const size_t stride = static_cast<size_t>(p.part_rows) * p.width;
+  const int qcols = p.gated ? 2 * hd : hd;  // projection columns per q head
+  const int col = gh < p.n_q_heads ? gh * qcols + d : p.n_q_heads * qcols + (gh - p.n_q_heads) * hd + d;
+  const size_t stride = static_cast<size_t>(p.part_rows) * p.width;
+  auto sum_splits = [&](int c) {
+    const float* src = p.partials + static_cast<size_t>(t) * p.width + c;
+    float a = 0.0f;
     int s = 0;
     for (; s + 3 < p.split; s += 4) {
       const float x0 = __ldcg(src + s * stride), x1 = __ldcg(src + (s + 1) * stride);
@@ -46,7 +57,11 @@ __global__ void __launch_bounds__(256) qkv_finish_kernel(QkvFinishParams p) {
       a += x3;
     }
     for (; s < p.split; ++s) a += __ldcg(src + s * stride);
-  }
+    return a;
+  };
+  const float a = sum_splits(col);
+  if (p.gated && gh < p.n_q_heads)
+    p.gate_out[static_cast<size_t>(t) * (p.n_q_heads * hd) + gh * hd + d] = __float2bfloat16_rn(sum_splits(col + hd));
   const int start = p.state->start;
   const int slot = start + t;
   if (gh >= p.n_q_heads + p.n_kv_heads) {  // v
@@ -67,13 +82,17 @@ __global__ void __launch_bounds__(256) qkv_finish_kernel(QkvFinishParams p) {
   const float y = bf16_round(x * rsqrtf(ss / static_cast<float>(hd) + p.eps) * nw);
   s_y[d] = y;
   __syncthreads();
-  const int half = hd / 2;
-  const int i_f = d % half;
-  const float inv_freq = exp2f(-(2.0f * static_cast<float>(i_f) / static_cast<float>(hd)) * p.rope_log2_theta);
-  float sn, cs;
-  sincosf(static_cast<float>(p.positions[t]) * inv_freq, &sn, &cs);
-  const float yp = s_y[d < half ? d + half : d - half];
-  const float outv = (d < half) ? (y * cs - yp * sn) : (y * cs + yp * sn);
+  const int rd = p.rot_dims > 0 ? p.rot_dims : hd;
+  float outv = y;
+  if (d < rd) {
+    const int half = rd / 2;
+    const int i_f = d % half;
+    const float inv_freq = exp2f(-(2.0f * static_cast<float>(i_f) / static_cast<float>(rd)) * p.rope_log2_theta);
+    float sn, cs;
+    sincosf(static_cast<float>(p.positions[t]) * inv_freq, &sn, &cs);
+    const float yp = s_y[d < half ? d + half : d - half];
+    outv = (d < half) ? (y * cs - yp * sn) : (y * cs + yp * sn);
+  }
   if (is_q) {
     p.q_out[static_cast<size_t>(t) * (p.n_q_heads * hd) + gh * hd + d] = __float2bfloat16_rn(outv);
   } else {
@@ -85,6 +104,8 @@ __global__ void __launch_bounds__(256) qkv_finish_kernel(QkvFinishParams p) {
 
 int qkv_finish_launch(const QkvFinishParams& p, int n_rows, cudaStream_t stream) {
   DTREE_CHECK_ARG(p.head_dim % 32 == 0 && p.head_dim <= 256, "head_dim must be a multiple of 32, <= 256");
+  DTREE_CHECK_ARG(p.rot_dims >= 0 && p.rot_dims <= p.head_dim && p.rot_dims % 2 == 0, "bad rot_dims");
+  DTREE_CHECK_ARG(!p.gated || p.gate_out, "gated projection needs gate_out");
   DTREE_CUDA_RET(launch_pdl(qkv_finish_kernel, dim3(n_rows, p.n_q_heads + 2 * p.n_kv_heads), dim3(p.head_dim), 0,
                             stream, p));
   return kOk;

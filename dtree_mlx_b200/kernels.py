@@ -204,3 +204,65 @@ def lm_head_argmax(h: torch.Tensor, embed: torch.Tensor, n_rows: int, out: torch
     call("dtree_lm_head_argmax", ptr(h), t_pad, n_rows, hidden, ptr(embed), vocab, ptr(out), ptr(ws), ws.numel(),
          stream_ptr())
     return out
+
+
+# ------------------------------------------------- Qwen3.5 DeltaNet kernels
+_DT = {torch.float32: 0, torch.bfloat16: 1}
+
+
+def _dtype_code(t: torch.Tensor, name: str) -> int:
+    if t.dtype not in _DT:
+        raise TypeError(f"{name} must be float32 or bfloat16, got {t.dtype}")
+    return _DT[t.dtype]
+
+
+def tree_conv1d(qkv: torch.Tensor, base: torch.Tensor, weight: torch.Tensor, parents: torch.Tensor,
+                want_states: bool = False):
+    """tree_conv1d_kernel (qwen35_tree_kernels.py:180-206): qkv [T, C],
+    base [keep, C], weight [keep+1, C] -> (conv_out [T, C], states or None)."""
+    for t, n in ((qkv, "qkv"), (base, "base"), (weight, "weight")):
+        _cuda(t, n, qkv.dtype)
+    _cuda(parents, "parents", torch.int32)
+    T, C = qkv.shape
+    keep = base.shape[0]
+    out = torch.empty(T, C, dtype=qkv.dtype, device=qkv.device)
+    states = torch.empty(T, keep, C, dtype=qkv.dtype, device=qkv.device) if want_states else None
+    call("dtree_tree_conv1d", ptr(qkv), qkv.stride(0), ptr(base), ptr(weight), ptr(parents), T, C, keep,
+         _dtype_code(qkv, "qkv"), ptr(out), ptr(states), stream_ptr())
+    return out, states
+
+
+def tree_gated_delta(q, k, v, g, beta, state, parents, want_states: bool = False):
+    """tree_gated_delta_kernel (qwen35_tree_kernels.py:207-224): q, k
+    [T, Hk, Dk]; v [T, Hv, Dv]; g f32 [T, Hv]; beta [T, Hv]; state
+    [Hv, Dv, Dk] -> (y [T, Hv, Dv], node states or None)."""
+    for t, n in ((q, "q"), (k, "k"), (v, "v"), (beta, "beta")):
+        _cuda(t, n, q.dtype)
+    _cuda(g, "g", torch.float32)
+    _cuda(state, "state")
+    _cuda(parents, "parents", torch.int32)
+    T, Hk, Dk = k.shape
+    Hv, Dv = v.shape[1:]
+    y = torch.empty(T, Hv, Dv, dtype=q.dtype, device=q.device)
+    ns = torch.empty(T, Hv, Dv, Dk, dtype=state.dtype, device=q.device) if want_states else None
+    call("dtree_tree_gated_delta", ptr(q), ptr(k), ptr(v), ptr(g), ptr(beta), ptr(state), ptr(parents), T, Hk, Hv,
+         Dk, Dv, _dtype_code(q, "q"), _dtype_code(state, "state"), ptr(y), ptr(ns), stream_ptr())
+    return y, ns
+
+
+def gated_delta_commit(q, k, v, g, beta, accepted: torch.Tensor, st: torch.Tensor, state: torch.Tensor) -> None:
+    """Advance ``state`` in place along accepted[0:st.n_accepted] (commit_qwen35_tree_path)."""
+    _cuda(accepted, "accepted", torch.int32)
+    _cuda(st, "state struct", torch.int32)
+    T, Hk, Dk = k.shape
+    Hv, Dv = v.shape[1:]
+    call("dtree_gated_delta_commit", ptr(q), ptr(k), ptr(v), ptr(g), ptr(beta), ptr(accepted), ptr(st), T, Hk, Hv,
+         Dk, Dv, _dtype_code(q, "q"), _dtype_code(state, "state"), ptr(state), stream_ptr())
+
+
+def conv_state_commit(qkv: torch.Tensor, parents: torch.Tensor, accepted: torch.Tensor, st: torch.Tensor,
+                      base: torch.Tensor) -> None:
+    """base <- the conv window of the deepest accepted node (in place)."""
+    T, C = qkv.shape
+    call("dtree_conv_state_commit", ptr(qkv), qkv.stride(0), ptr(parents), ptr(accepted), ptr(st), T, C,
+         base.shape[0], _dtype_code(qkv, "qkv"), ptr(base), stream_ptr())

@@ -223,3 +223,111 @@ def random_prompt(n: int, vocab: int, seed: int = 0) -> list[int]:
     """Uniform-random prompt token ids (128 / 256 / 2048)."""
     g = torch.Generator().manual_seed(int(seed) + 7919)
     return torch.randint(0, vocab, (n,), generator=g).tolist()
+
+
+# ------------------------------------------------------------ Qwen3.5 hybrid
+@dataclass
+class Qwen35Weights:
+    """Seeded random-init Qwen3.5 hybrid in the engine's layouts.
+
+    DeltaNet layer: ``in_proj`` = rows in_proj_qkv | in_proj_z | in_proj_b |
+    in_proj_a (one GEMM), ``conv_weight`` [kernel, conv_dim] (the reference's
+    conv1d.weight[:, :, 0].T, qwen35_tree.py:389), ``norm`` (RMSNormGated),
+    ``out_proj``.  Attention layer: ``qkv`` = q_proj rows (per head [q | gate])
+    | k_proj | v_proj.  ``a_log`` f32 [n_linear, Hv], ``dt_bias`` [n_linear, Hv].
+    Linear and embedding weights N(0, 0.02); conv weights U(-0.5, 0.5) (MLX
+    Conv1d's default scale for a depthwise width-4 kernel); A = U(0, 16),
+    A_log = log A and dt_bias = 1 as GatedDeltaNet initializes them
+    (custom_qwen35_model.py:812-815); norm weights 1 (or 1 + N(0, jitter))."""
+
+    cfg: "object"
+    embed: torch.Tensor
+    final_norm: torch.Tensor
+    layers: list = field(default_factory=list)
+    a_log: torch.Tensor | None = None
+    dt_bias: torch.Tensor | None = None
+
+    @property
+    def device(self) -> torch.device:
+        return self.embed.device
+
+    def streamed_bytes(self) -> int:
+        """Weights one verify forward reads (embedding = tied LM head once)."""
+        n = tensor_bytes(self.embed)
+        for L in self.layers:
+            for k in ("in_proj", "out_proj", "qkv", "o_proj", "gate_up", "down", "conv_weight"):
+                if k in L:
+                    n += tensor_bytes(L[k])
+        return n
+
+    def reference_layer(self, l: int) -> dict:
+        """mlx-lm names of layer l (views of the packed storage)."""
+        c = self.cfg
+        L = self.layers[l]
+        gate, up = split_gate_up(L["gate_up"])
+        out = {"input_layernorm": L["input_norm"], "post_attention_layernorm": L["post_norm"],
+               "gate_proj": gate, "up_proj": up, "down_proj": L["down"]}
+        if c.is_linear(l):
+            li = sum(1 for j in range(l) if c.is_linear(j))
+            w = L["in_proj"]
+            kd, vd, hv = c.key_dim, c.value_dim, c.linear_num_value_heads
+            out.update(in_proj_qkv=w[: c.conv_dim], in_proj_z=w[c.conv_dim : c.conv_dim + vd],
+                       in_proj_b=w[c.conv_dim + vd : c.conv_dim + vd + hv],
+                       in_proj_a=w[c.conv_dim + vd + hv :], conv_weight=L["conv_weight"], norm=L["norm"],
+                       out_proj=L["out_proj"], A_log=self.a_log[li], dt_bias=self.dt_bias[li])
+            del kd
+        else:
+            w = L["qkv"]
+            out.update(q_proj=w[: 2 * c.q_dim], k_proj=w[2 * c.q_dim : 2 * c.q_dim + c.kv_dim],
+                       v_proj=w[2 * c.q_dim + c.kv_dim :], q_norm=L["q_norm"], k_norm=L["k_norm"],
+                       o_proj=L["o_proj"])
+        return out
+
+    def to(self, device) -> "Qwen35Weights":
+        w = Qwen35Weights(self.cfg, self.embed.to(device), self.final_norm.to(device),
+                          a_log=self.a_log.to(device), dt_bias=self.dt_bias.to(device))
+        w.layers = [{k: v.to(device) for k, v in L.items()} for L in self.layers]
+        return w
+
+
+def random_qwen35_weights(cfg, seed: int = 0, device="cuda", dtype=torch.bfloat16,
+                          norm_jitter: float = 0.0) -> Qwen35Weights:
+    g = torch.Generator(device=device).manual_seed(int(seed))
+
+    def randn(*shape):
+        return (torch.randn(*shape, generator=g, device=device, dtype=torch.float32) * STD).to(dtype)
+
+    def uniform(lo, hi, *shape):
+        return (torch.rand(*shape, generator=g, device=device, dtype=torch.float32) * (hi - lo) + lo)
+
+    def ones(n):
+        if norm_jitter > 0:
+            return (1.0 + torch.randn(n, generator=g, device=device) * norm_jitter).to(dtype)
+        return torch.ones(n, dtype=dtype, device=device)
+
+    h, f = cfg.hidden_size, cfg.intermediate_size
+    w = Qwen35Weights(cfg, embed=randn(cfg.vocab_size, h), final_norm=ones(h))
+    a_log, dt_bias = [], []
+    for l in range(cfg.num_hidden_layers):
+        L = {"input_norm": ones(h), "post_norm": ones(h)}
+        if cfg.is_linear(l):
+            hv = cfg.linear_num_value_heads
+            L["in_proj"] = torch.cat([randn(cfg.conv_dim, h), randn(cfg.value_dim, h), randn(hv, h),
+                                      randn(hv, h)], dim=0).contiguous()
+            L["conv_weight"] = uniform(-0.5, 0.5, cfg.linear_conv_kernel_dim, cfg.conv_dim).to(dtype)
+            L["norm"] = ones(cfg.linear_value_head_dim)
+            L["out_proj"] = randn(h, cfg.value_dim)
+            a_log.append(torch.log(uniform(0.0, 16.0, hv).clamp_min(1e-3)))
+            dt_bias.append(torch.ones(hv, dtype=dtype, device=device))
+        else:
+            L["qkv"] = torch.cat([randn(2 * cfg.q_dim, h), randn(cfg.kv_dim, h), randn(cfg.kv_dim, h)],
+                                 dim=0).contiguous()
+            L["q_norm"] = ones(cfg.head_dim)
+            L["k_norm"] = ones(cfg.head_dim)
+            L["o_proj"] = randn(h, cfg.q_dim)
+        L["gate_up"] = interleave_gate_up(randn(f, h), randn(f, h))
+        L["down"] = randn(h, f)
+        w.layers.append(L)
+    w.a_log = torch.stack(a_log).float().contiguous()
+    w.dt_bias = torch.stack(dt_bias).contiguous()
+    return w

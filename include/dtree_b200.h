@@ -193,6 +193,53 @@ DTREE_API size_t dtree_lm_head_workspace_bytes(int t_pad);
 DTREE_API int dtree_lm_head_argmax(const void* h, int t_pad, int n_rows, int hidden, const void* embed, int vocab,
                          int32_t* out, void* workspace, size_t workspace_bytes, void* stream);
 
+/* ------------------------------------- Qwen3.5 gated-DeltaNet tree kernels
+ * dtype / state_dtype: 0 = f32, 1 = bf16 (the reference's InT / StT).
+ * parents[t] < t for t > 0, parents[0] = -1 (the base state).
+ *
+ * Replaces tree_conv1d_kernel (qwen35_tree_kernels.py:86-134, 180-206): the
+ * depthwise causal conv (width keep+1) of every tree node over the `keep`
+ * inputs before it on its root path (base_conv_state [keep][conv_dim] when
+ * the path is shorter), SiLU, rounded to dtype.  qkv row t starts at
+ * qkv + t*ld_qkv; conv_weight is [keep+1][conv_dim] (weight k multiplies
+ * the k-th oldest input, the last one the node's own input); conv_out
+ * [n_nodes][conv_dim]; conv_states (nullable) [n_nodes][keep][conv_dim]
+ * receives each node's window as the reference does. */
+DTREE_API int dtree_tree_conv1d(const void* qkv, int ld_qkv, const void* base_conv_state, const void* conv_weight,
+                      const int32_t* parents, int n_nodes, int conv_dim, int keep, int dtype, void* conv_out,
+                      void* conv_states, void* stream);
+
+/* Replaces tree_gated_delta_kernel (qwen35_tree_kernels.py:8-82, 207-224):
+ * per node, S = S_parent * g; kv = S k; delta = (v - kv) * beta;
+ * S += k delta; y = S q; the node's state is S rounded to dtype.
+ * q, k [n_nodes][n_k_heads][head_k_dim]; v, y [n_nodes][n_v_heads][head_v_dim];
+ * g f32 and beta (dtype) [n_nodes][n_v_heads]; state_in (state_dtype)
+ * [n_v_heads][head_v_dim][head_k_dim]; node_states (nullable, state_dtype)
+ * [n_nodes][n_v_heads][head_v_dim][head_k_dim].  head_k_dim in {32, 64,
+ * 128, 256}. */
+DTREE_API int dtree_tree_gated_delta(const void* q, const void* k, const void* v, const float* g, const void* beta,
+                           const void* state_in, const int32_t* parents, int n_nodes, int n_k_heads, int n_v_heads,
+                           int head_k_dim, int head_v_dim, int dtype, int state_dtype, void* y, void* node_states,
+                           void* stream);
+
+/* Recurrent half of commit_qwen35_tree_path (qwen35_tree.py:708-732):
+ * recurrent_state <- the state of the deepest accepted node, obtained by
+ * replaying the accepted path accepted[0 .. state->n_accepted) (root first)
+ * from recurrent_state with the per-node arithmetic and rounding of
+ * dtree_tree_gated_delta, so per-node states never need to be stored.
+ * Inputs as dtree_tree_gated_delta. */
+DTREE_API int dtree_gated_delta_commit(const void* q, const void* k, const void* v, const float* g, const void* beta,
+                             const int32_t* accepted, const dtree_step_state* state, int n_nodes, int n_k_heads,
+                             int n_v_heads, int head_k_dim, int head_v_dim, int dtype, int state_dtype,
+                             void* recurrent_state, void* stream);
+
+/* Conv half of commit_qwen35_tree_path: base_conv_state <- the window of the
+ * deepest accepted node (its last `keep` inputs), read from the tree's conv
+ * inputs qkv (as in dtree_tree_conv1d) and the old base state. */
+DTREE_API int dtree_conv_state_commit(const void* qkv, int ld_qkv, const int32_t* parents, const int32_t* accepted,
+                            const dtree_step_state* state, int n_nodes, int conv_dim, int keep, int dtype,
+                            void* base_conv_state, void* stream);
+
 /* ------------------------------------------------- Qwen3 tree verify
  * A Qwen3 target (mlx-lm qwen3 layer math: RMSNorm, q/k RMSNorm, half-split
  * RoPE, GQA attention, SwiGLU, tied LM head) held as device pointers.
@@ -278,6 +325,104 @@ DTREE_API int dtree_qwen3_destroy(dtree_qwen3_model* model);
 DTREE_API int dtree_qwen3_forward_tree(dtree_qwen3_model* model, const int32_t* tree_tokens, const int32_t* positions,
                              const uint64_t* anc_mask, int n_nodes, const dtree_step_state* state,
                              int32_t* posterior, void* stream);
+
+/* ------------------------------------------ Qwen3.5 hybrid tree verify
+ * A Qwen3.5 text model (custom_qwen35_model.py:777-924): layer l is a gated
+ * DeltaNet layer unless (l + 1) % full_attention_interval == 0, then a gated
+ * full-attention layer; SwiGLU MLP and RMSNorms around both; tied LM head.
+ * Weights bf16, row-major [out, in]:
+ *   DeltaNet in_proj  [2*lin_key_dim + lin_value_dim + 2*lin_v_heads, hidden]
+ *                     rows: in_proj_qkv | in_proj_z | in_proj_b | in_proj_a
+ *            conv_weight [conv_kernel][conv_dim] (conv1d.weight[:, :, 0].T)
+ *   attention qkv     [n_heads*2*head_dim + 2*n_kv_heads*head_dim, hidden]:
+ *                     q_proj rows (per head [q | gate]), then k_proj, v_proj
+ *   gate_up as dtree_qwen3_layer.  lin_key_dim = lin_k_heads*lin_k_dim etc.
+ * State (caller-owned, persists across steps):
+ *   kv_cache   [n_attn][2][n_kv_heads][kv_capacity][head_dim] bf16
+ *   conv_state [n_linear][conv_kernel-1][conv_dim] bf16
+ *   rec_state  [n_linear][lin_v_heads][lin_v_dim][lin_k_dim] f32 */
+typedef struct dtree_qwen35_linear_layer {
+  const void* input_norm;
+  const void* in_proj;
+  const void* conv_weight;
+  const void* norm;      /* [lin_v_dim] RMSNormGated weight */
+  const void* out_proj;  /* [hidden, lin_v_heads*lin_v_dim] */
+  const void* post_norm;
+  const void* gate_up;
+  const void* down;
+} dtree_qwen35_linear_layer;
+
+typedef struct dtree_qwen35_attn_layer {
+  const void* input_norm;
+  const void* qkv;
+  const void* q_norm;  /* [head_dim] */
+  const void* k_norm;
+  const void* o_proj;  /* [hidden, n_heads*head_dim] */
+  const void* post_norm;
+  const void* gate_up;
+  const void* down;
+} dtree_qwen35_attn_layer;
+
+typedef struct dtree_qwen35_desc {
+  int hidden, layers, full_attention_interval, ffn, vocab;
+  int n_heads, n_kv_heads, head_dim;
+  float rope_theta, partial_rotary_factor, rms_eps;
+  int lin_k_heads, lin_v_heads, lin_k_dim, lin_v_dim, conv_kernel;
+  int t_cap, kv_capacity, n_capture;
+  int capture_layers[16];
+  const void* embed;       /* [vocab, hidden], also the tied LM head */
+  const void* final_norm;
+  const dtree_qwen35_linear_layer* linear_layers;  /* [n_linear], layer order */
+  const dtree_qwen35_attn_layer* attn_layers;      /* [n_attn] */
+  const float* a_log;      /* [n_linear][lin_v_heads] f32 */
+  const void* dt_bias;     /* [n_linear][lin_v_heads] bf16 */
+  /* caller-owned state and buffers (sizes from dtree_qwen35_buffer_bytes) */
+  void* kv_cache;
+  void* conv_state;
+  void* rec_state;
+  void* h;         /* [t_cap, hidden] residual stream */
+  void* xn;        /* [t_cap, hidden] */
+  void* q;         /* [t_cap, max(n_heads*head_dim, lin_v_heads*lin_v_dim)] */
+  void* gate;      /* [t_cap, n_heads*head_dim] attention output gate */
+  void* attn;      /* [t_cap, max(n_heads*head_dim, lin_v_heads*lin_v_dim)] */
+  void* act;       /* [t_cap, ffn] */
+  void* norm_out;  /* [t_cap, hidden] */
+  void* capture;   /* [t_cap, hidden*n_capture] */
+  void* lin_proj;  /* [n_linear][t_cap][in_proj rows] DeltaNet projections (kept for commit) */
+  void* lin_qkv;   /* [n_linear][t_cap][conv_dim] conv outputs (kept for commit) */
+  void* workspace;
+  size_t workspace_bytes;
+} dtree_qwen35_desc;
+
+typedef struct dtree_qwen35_model dtree_qwen35_model;
+
+/* out[0..13] = kv_cache, conv_state, rec_state, h, xn, q, gate, attn, act,
+ * norm_out, capture, lin_proj, lin_qkv, workspace. */
+DTREE_API int dtree_qwen35_buffer_bytes(const dtree_qwen35_desc* desc, size_t out[14]);
+DTREE_API int dtree_qwen35_create(const dtree_qwen35_desc* desc, dtree_qwen35_model** out);
+DTREE_API int dtree_qwen35_destroy(dtree_qwen35_model* model);
+
+/* mode 0 -- tree verify, replaces forward_qwen35_tree_with_hidden_states
+ * (qwen35_tree.py:629-705) + lm_head_argmax: DeltaNet layers run the tree
+ * conv / gated-delta kernels from the committed conv / recurrent state with
+ * per-node rounding (state is not modified); attention layers attend to the
+ * cache prefix [0, state->start) plus the tree (ancestor masks) and write
+ * the tree's K/V at slots start + t.  parents[t] < t, parents[0] = -1.
+ * mode 1 -- sequence (prefill chunk, adapters.py:494-533): parents must be a
+ * chain, no per-node rounding, and the conv / recurrent states advance to
+ * the last token.  posterior (nullable) receives the greedy token per node. */
+DTREE_API int dtree_qwen35_forward(dtree_qwen35_model* model, const int32_t* tokens, const int32_t* positions,
+                         const int32_t* parents, const uint64_t* anc_mask, int n_nodes, int mode,
+                         const dtree_step_state* state, int32_t* posterior, void* stream);
+
+/* commit_qwen35_tree_path (qwen35_tree.py:708-732) for the accepted path
+ * accepted[0 .. state->n_accepted) (root first) of the last tree forward:
+ * attention layers keep the accepted K/V rows (moved to start .. start+n-1),
+ * DeltaNet layers take the deepest accepted node's conv window and
+ * recurrent state (replayed from the committed state).  Call before
+ * dtree_step_commit. */
+DTREE_API int dtree_qwen35_commit(dtree_qwen35_model* model, const int32_t* parents, const int32_t* accepted,
+                        const dtree_step_state* state, void* stream);
 
 #ifdef __cplusplus
 }

@@ -1,0 +1,135 @@
+"""Qwen3.5 hybrid (gated DeltaNet + gated full attention) on the GPU vs the
+CPU oracle: prefill, two tree-verify steps, each followed by the commit of
+the accepted path, compared after every stage.
+
+Two oracles run side by side on the same bf16 weights and the same trees:
+* ``fp32``: the reference arithmetic in fp32 (node states rounded to bf16
+  per node, as the reference's tree kernel does);
+* ``bf16``: the same with every activation rounded to bf16 where a bf16
+  MLX model materializes it.
+The two oracles differ from each other by max |d logits| ~ 0.065 (mean
+~ 0.009, logit std 0.46) on this model: that is bf16 rounding noise, not a
+semantic difference, and it bounds how close any bf16 implementation can
+get.  Tolerances, with S = the measured oracle-to-oracle spread of the same
+step (max and mean |d logits|):
+  vs bf16 oracle  logits max <= 1.5 S_max, mean <= 1.5 S_mean; hidden / states rel <= 3e-2
+  vs fp32 oracle  logits max <= 2 S_max,   mean <= 2 S_mean;   hidden / states rel <= 4e-2
+Posterior tokens must equal the bf16 oracle's argmax except at near-ties
+(top-2 gap below S_max), which are counted.
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import tree as OT
+from oracle.qwen35 import Qwen35Oracle
+from oracle.runtime import near_tie
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+SPREAD = {"bf16": 1.5, "fp32": 2.0}   # logit tolerance in units of the oracle-to-oracle spread
+REL = {"bf16": 3e-2, "fp32": 4e-2}
+
+
+def _rel(a, b):
+    a = torch.as_tensor(np.asarray(a.float().cpu() if torch.is_tensor(a) else a)).double()
+    b = torch.as_tensor(np.asarray(b.float().cpu() if torch.is_tensor(b) else b)).double()
+    return float((a - b).norm() / max(float(b.norm()), 1e-30))
+
+
+@pytest.fixture(scope="module")
+def hybrid(lib):
+    from dtree_mlx_b200.config import QWEN35_PRESETS
+    from dtree_mlx_b200.synthetic import random_qwen35_weights
+
+    cfg = QWEN35_PRESETS["qwen35-tiny"]
+    return cfg, random_qwen35_weights(cfg, seed=0, device=DEV, norm_jitter=0.1)
+
+
+def _states_match(eng, orcs, cfg, past, n, tag):
+    lin = [l for l in range(cfg.num_hidden_layers) if cfg.is_linear(l)]
+    att = [l for l in range(cfg.num_hidden_layers) if not cfg.is_linear(l)]
+    for name, orc in orcs.items():
+        rel = REL[name]
+        for li, l in enumerate(lin):
+            assert _rel(eng.conv_state[li], orc.conv[l]) < rel, (tag, name, "conv", l)
+            assert _rel(eng.rec_state[li], orc.rec[l]) < rel, (tag, name, "rec", l)
+        for ai, l in enumerate(att):
+            assert _rel(eng.kv_cache[ai, 0, :, past:past + n], orc.k[l][:, past:past + n]) < rel, (tag, name, "k")
+            assert _rel(eng.kv_cache[ai, 1, :, past:past + n], orc.v[l][:, past:past + n]) < rel, (tag, name, "v")
+
+
+def test_prefill_tree_commit_match_oracle(hybrid):
+    from dtree_mlx_b200 import _lib, kernels
+    from dtree_mlx_b200.engine import chain_anc_masks, mask_to_anc
+    from dtree_mlx_b200.engine35 import Qwen35Engine
+
+    cfg, w = hybrid
+    eng = Qwen35Engine(w, kv_capacity=512)
+    orcs = {"fp32": Qwen35Oracle(w, kv_capacity=512), "bf16": Qwen35Oracle(w, kv_capacity=512, bf16_acts=True)}
+    rng = np.random.default_rng(0)
+    P = 40
+    prompt = rng.integers(cfg.vocab_size, size=P).tolist()
+    tok = lambda a: torch.as_tensor(np.asarray(a), dtype=torch.int32, device=DEV)  # noqa: E731
+    st = kernels.new_state(DEV, start=0)
+    post = torch.zeros(128, dtype=torch.int32, device=DEV)
+    eng.forward(tok(prompt), tok(np.arange(P)), tok(np.arange(-1, P - 1)),
+                torch.from_numpy(chain_anc_masks(P).view(np.int64)).to(DEV), P, st, post, mode=1)
+    torch.cuda.synchronize()
+    for name, orc in orcs.items():
+        o_norm, _ = orc.prefill(prompt)
+        rel = _rel(eng.norm_out[:P], o_norm)
+        print(f"prefill vs {name}: norm_out rel {rel:.2e}")
+        assert rel < REL[name]
+    _states_match(eng, orcs, cfg, 0, P, "prefill")
+
+    root, past = int(post[P - 1].item()), P
+    for step in range(2):
+        dl = (rng.standard_normal((15, cfg.vocab_size)) * 2).astype(np.float32)
+        node_tokens, node_depths, parents, child_maps, vis = OT.build_dtree_tree(dl, 24)
+        ids, pos = OT.compile_dtree_tree(root, past, node_tokens, node_depths)
+        toks, positions = ids.astype(np.int32).tolist(), pos.astype(np.int32).tolist()
+        T = len(toks)
+        st = kernels.new_state(DEV, start=past, root_token=root)
+        eng.forward(tok(toks), tok(positions), tok(parents), torch.from_numpy(mask_to_anc(vis).view(np.int64)).to(DEV),
+                    T, st, post, mode=0)
+        torch.cuda.synchronize()
+        x = torch.zeros(32, cfg.hidden_size, dtype=torch.bfloat16, device=DEV)
+        x[:T] = eng.norm_out[:T]
+        g_log = kernels.linear_bf16(x, w.embed)[:T].float().cpu()
+        gpost = post[:T].tolist()
+        mask = OT.tree_attention_mask(vis, past)
+        outs = {name: orc.forward(toks, positions, parents, mask, past, tree=True)[0] for name, orc in orcs.items()}
+        logs = {name: orcs[name].lm_head_logits(o) for name, o in outs.items()}
+        spread = (logs["fp32"] - logs["bf16"]).abs()
+        s_max, s_mean = float(spread.max()), float(spread.mean())
+        print(f"step {step}: oracle spread max {s_max:.3e} mean {s_mean:.3e}")
+        for name in orcs:
+            err = (g_log - logs[name]).abs()
+            rel = _rel(eng.norm_out[:T], outs[name])
+            print(f"step {step} vs {name}: norm_out rel {rel:.2e} logits max {err.max():.3e} mean {err.mean():.3e}")
+            k = SPREAD[name]
+            assert rel < REL[name] and err.max() <= k * s_max and err.mean() <= k * s_mean, (step, name)
+        near = 0
+        for t in range(T):
+            ref = int(torch.argmax(logs["bf16"][t]))
+            if gpost[t] != ref:
+                assert near_tie(logs["bf16"][t], gpost[t], ref, s_max), (step, t)
+                near += 1
+        print(f"step {step}: near-tie posterior mismatches {near}/{T}")
+        accepted, nxt = OT.follow_verified_tree(child_maps, gpost)
+        acc = torch.zeros(128, dtype=torch.int32, device=DEV)
+        acc[: len(accepted)] = torch.tensor(accepted, dtype=torch.int32)
+        st[3] = len(accepted)
+        eng.commit(tok(parents), acc, st)
+        torch.cuda.synchronize()
+        for orc in orcs.values():
+            orc.commit(accepted)
+        _states_match(eng, orcs, cfg, past, len(accepted), f"commit {step}")
+        print(f"step {step}: accepted {len(accepted)}")
+        past += len(accepted)
+        root = nxt
+    assert _lib.device_error() == 0
+    eng.close()
