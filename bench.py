@@ -53,6 +53,8 @@ PRESET = "qwen3-4b"
 KV_CAP = 2304
 METRIC = "accepted tok/s/GPU, Qwen3-4B-shape DTree b24; verify-step HBM GB/s vs peak"
 WORKLOADS = {
+    "qwen35-9b": "BASELINE config 4: Qwen3.5-9B-style hybrid (24 gated DeltaNet + 8 gated attention layers) DTree, "
+                 "prompt 2048, 512 new tokens, spec 16, budget 24",
     16: "BASELINE config 1: Qwen3-4B-shape DTree, prompt 256, 512 new tokens, spec 16, budget 24",
     4: "BASELINE config 3: Qwen3-4B-shape DTree with MLX affine 4-bit projections (group 64), prompt 256, "
        "512 new tokens, spec 16, budget 24",
@@ -135,7 +137,19 @@ class ClockSampler:
                 "reasons": reasons, "samples": len(rows)}
 
 
+def verify_call(eng, tree, n: int, st, post) -> None:
+    """One tree-verify forward of either engine (Qwen3 or Qwen3.5 hybrid)."""
+    if hasattr(eng, "forward_tree"):
+        eng.forward_tree(tree.tokens, tree.positions, tree.anc, n, st, post)
+    else:
+        eng.forward(tree.tokens, tree.positions, tree.parents, tree.anc, n, st, post, mode=0)
+
+
 def algorithmic_verify_bytes(cfg, weights, prefix: int, t: int) -> float:
+    if PRESET.startswith("qwen35"):
+        from dtree_mlx_b200.verify_sweep import hybrid_algorithmic_bytes
+
+        return hybrid_algorithmic_bytes(cfg, weights, prefix, t)
     wbytes = weights.streamed_bytes()
     kv_row = 2 * cfg.num_key_value_heads * cfg.head_dim * 2 * cfg.num_hidden_layers
     return float(wbytes + prefix * kv_row + t * kv_row)
@@ -220,13 +234,13 @@ def run_ours(args, rank, world, local, dist) -> dict | None:
     for P in (PROMPT_LEN + MAX_NEW // 2, 2048):
         st = kernels.new_state(dev, start=P, root_token=first)
         post = torch.zeros(128, dtype=torch.int32, device=dev)
-        eng.forward_tree(session.tree.tokens, session.tree.positions, session.tree.anc, n_nodes, st, post)
+        verify_call(eng, session.tree, n_nodes, st, post)
         torch.cuda.synchronize()
         s = torch.cuda.Stream()
         s.wait_stream(torch.cuda.current_stream())
         g = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g, stream=s):
-            eng.forward_tree(session.tree.tokens, session.tree.positions, session.tree.anc, n_nodes, st, post)
+            verify_call(eng, session.tree, n_nodes, st, post)
         torch.cuda.current_stream().wait_stream(s)
         for _ in range(3):
             g.replay()
@@ -270,15 +284,17 @@ def run_ours(args, rank, world, local, dist) -> dict | None:
     achieved = vbytes / (vms / 1e3) / 1e9
     traffic = None
     tp = ROOT / "profiles" / "verify_traffic.json"
-    if tp.exists() and args.quant_bits == 16:
+    if tp.exists() and args.quant_bits == 16 and PRESET == "qwen3-4b":
         try:
             traffic = json.loads(tp.read_text()).get("bytes_per_verify")
         except Exception:
             traffic = None
     # per layer: input norm, QKV GEMM, QKV finish, attention, combine, O GEMM,
-    # post norm, gate/up GEMM, down GEMM; per step: final norm, LM head,
-    # plant, top-k, heap, walk, compaction, commit
-    launches_per_step = 9 * cfg.num_hidden_layers + 8
+    # post norm, gate/up GEMM, down GEMM (DeltaNet layers: input norm, in_proj
+    # GEMM, tree conv, tree gated delta, gated norm, out_proj GEMM, post norm,
+    # gate/up, down); per step: final norm, LM head, plant, top-k, heap, walk,
+    # compaction (hybrid: + DeltaNet state replay + conv-state commit), commit
+    launches_per_step = 9 * cfg.num_hidden_layers + (10 if PRESET.startswith("qwen35") else 8)
     out = {
         "metric": METRIC,
         "value": round(value, 2),
@@ -291,9 +307,9 @@ def run_ours(args, rank, world, local, dist) -> dict | None:
         "scaling": "weak",
         "vs_baseline": None,
         "dtype": "bf16" if args.quant_bits == 16 else "u4 weights (affine, group 64), bf16 activations",
-        "data": "synthetic (random-init Qwen3-4B-shape weights, random prompt, planted drafts p=0.85)",
+        "data": f"synthetic (random-init {PRESET}-shape weights, random prompt, planted drafts p=0.85)",
         "config": {
-            "workload": WORKLOADS[args.quant_bits],
+            "workload": WORKLOADS[PRESET if PRESET.startswith("qwen35") else args.quant_bits],
             "decode_steps_per_generation": n_steps,
             "mean_accepted_per_step": round(sum(accept) / n_steps, 3),
             "tree_rows": n_nodes,
@@ -308,7 +324,8 @@ def run_ours(args, rank, world, local, dist) -> dict | None:
         "gpu_launches": launches_per_step * n_steps * args.steps,
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
                      "frac": round(achieved / peaks["hbm_gbs"], 4), "traffic": traffic,
-                     "kernel": "tree-verify forward (36 layers + fused LM-head argmax), T=25, prefix 2048",
+                     "kernel": f"tree-verify forward ({cfg.num_hidden_layers} layers + fused LM-head argmax), "
+                               f"T={n_nodes}, prefix 2048",
                      "verify_ms": round(vms, 4), "algorithmic_bytes": vbytes,
                      "verify_ms_prefix512": round(roof[PROMPT_LEN + MAX_NEW // 2][0], 4),
                      "peak_source": f"{peaks['source']} MEASURED_PEAKS hbm_gbs (burst)"},
@@ -434,8 +451,14 @@ def main():
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
     ap.add_argument("--quant-bits", type=int, default=16, choices=[16, 4],
                     help="4: BASELINE config 3 (MLX affine 4-bit projections, group 64)")
+    ap.add_argument("--target", default="qwen3-4b", choices=["qwen3-4b", "qwen35-9b"],
+                    help="qwen35-9b: BASELINE config 4 (hybrid, 2048-token prompt; no CPU baseline sample)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3) if args.impl == "ours" else args.warmup
+    if args.target == "qwen35-9b":
+        global PRESET, PROMPT_LEN, KV_CAP
+        PRESET, PROMPT_LEN, KV_CAP = "qwen35-9b", 2048, 2048 + 512 + 160
+        args.no_cpu = True
     rank, world, local, dist = dist_init()
     try:
         out = run_reference(args, rank, world) if args.impl == "reference" else run_ours(args, rank, world, local,

@@ -18,7 +18,7 @@ import numpy as np
 import torch
 
 from . import kernels
-from .config import PRESETS, Qwen3Config
+from .config import PRESETS, QWEN35_PRESETS, Qwen3Config
 from .engine import Qwen3Engine, chain_anc_masks, mask_to_anc, pad_rows
 from .synthetic import Qwen3Weights, random_qwen3_weights
 
@@ -282,11 +282,109 @@ class Qwen3TargetAdapter(TargetAdapter):
         cache.offset = past_length + len(keep)
 
 
-class Qwen35TargetAdapter(TargetAdapter):
-    """Qwen3.5 hybrid (gated DeltaNet + gated attention) family: registered so
-    the registry matches the reference; the hybrid verify is not built yet."""
+class Qwen35TargetAdapter(Qwen3TargetAdapter):
+    """Qwen3.5 hybrid (gated DeltaNet + gated attention) on the B200 engine
+    (adapters.py:216-450).  Tree verification keeps the per-layer DeltaNet
+    inputs on the device in place of the reference's pending per-node state
+    (``_pending_tree_state``, :430); ``compact_kv_caches`` commits the
+    accepted path from them (commit_qwen35_tree_path, qwen35_tree.py:708-732)."""
 
     family = "qwen3_5"
+
+    def __init__(self) -> None:
+        super().__init__()
+        self._pending = None
+
+    def engine(self, model, draft=None, layer_ids=None):
+        from .engine35 import Qwen35Engine
+
+        ids = tuple(sorted(layer_ids if layer_ids is not None else getattr(draft, "target_layer_ids", []) or []))
+        eng = model.engines.get(ids)
+        if eng is None:
+            for old in list(model.engines.values()):
+                old.close()
+            model.engines.clear()
+            eng = Qwen35Engine(model.weights, model.kv_capacity, layer_ids=ids)
+            model.engines[ids] = eng
+        return eng
+
+    def make_cache(self, model, speculative_linear_cache: bool = False):
+        """A new sequence: zero conv / recurrent states and an empty KV prefix."""
+        cache = super().make_cache(model, speculative_linear_cache)
+        cache.engine.reset_states()
+        return cache
+
+    def _forward(self, model, tokens, cache, layer_ids, anc_rows=None, positions=None, parents=None):
+        eng = self.engine(model, layer_ids=layer_ids)
+        if cache.engine is not eng:
+            raise ValueError("cache belongs to a different engine (capture layers changed)")
+        dev = eng.device
+        n = len(tokens)
+        state = kernels.new_state(dev, start=cache.offset)
+        post = torch.zeros(128, dtype=torch.int32, device=dev)
+        toks = torch.tensor(tokens, dtype=torch.int32, device=dev)
+        if parents is not None:  # tree verify: one forward, states stay committed
+            if n > eng.t_cap:
+                raise ValueError("at most 128 tree rows per verify")
+            pos = torch.tensor(positions, dtype=torch.int32, device=dev)
+            par = torch.tensor(parents, dtype=torch.int32, device=dev)
+            anc_t = torch.from_numpy(np.ascontiguousarray(anc_rows).view(np.int64)).to(dev)
+            eng.forward(toks, pos, par, anc_t, n, state, post, mode=0)
+            self._pending = (cache.offset, par)
+            cache.offset += n
+            norm = eng.norm_out[:n].clone()[None]
+            hid = eng.capture[:n].clone()[None]
+        else:  # causal sequence: states advance chunk by chunk
+            norm_rows, cap_rows = [], []
+            s = 0
+            while s < n:
+                t = min(eng.t_cap, n - s)
+                state[0] = cache.offset + s
+                pos = torch.arange(cache.offset + s, cache.offset + s + t, dtype=torch.int32, device=dev)
+                anc_t = torch.from_numpy(chain_anc_masks(t).view(np.int64)).to(dev)
+                eng.prefill_chunk(toks[s:s + t].contiguous(), pos, anc_t, t, state, post)
+                norm_rows.append(eng.norm_out[:t].clone())
+                cap_rows.append(eng.capture[:t].clone())
+                s += t
+            cache.offset += n
+            norm, hid = torch.cat(norm_rows)[None], torch.cat(cap_rows)[None]
+        if not eng.layer_ids:
+            hid = hid[..., :0]
+        return norm, hid
+
+    def forward_tree_with_hidden_states(self, model, inputs, cache, layer_ids, parents, position_ids,
+                                        attention_mask):
+        """adapters.py:410-430 (forward_qwen35_tree_with_hidden_states)."""
+        tokens = [int(t) for t in inputs.reshape(-1).tolist()]
+        n = len(tokens)
+        par = [int(p) for p in parents]
+        if len(par) != n or par[0] != -1 or any(not (0 <= p < i) for i, p in enumerate(par) if i > 0):
+            raise ValueError("parents must list a tree in topological order with the root first")
+        mask = torch.as_tensor(attention_mask).bool().cpu().numpy()
+        past = cache.offset
+        if mask.shape != (n, past + n) or not mask[:, :past].all():
+            raise ValueError("attention_mask must be [T, P+T] with an all-visible prefix")
+        pos = [int(p) for p in torch.as_tensor(position_ids).reshape(-1).tolist()]
+        return self._forward(model, tokens, cache, layer_ids, anc_rows=mask_to_anc(mask[:, past:]), positions=pos,
+                             parents=par)
+
+    def compact_kv_caches(self, model, cache, past_length: int, keep_current_indices: list[int]) -> None:
+        """adapters.py:432-448: commit the accepted path of the last tree verify."""
+        if self._pending is None:
+            raise RuntimeError("Qwen3.5 tree compaction requires pending tree state.")
+        keep = [int(i) for i in keep_current_indices]
+        past, par = self._pending
+        if past != past_length:
+            raise ValueError("past_length does not match the pending tree verify")
+        eng = cache.engine
+        dev = eng.device
+        state = kernels.new_state(dev, start=past_length)
+        state[3] = len(keep)
+        acc = torch.zeros(128, dtype=torch.int32, device=dev)
+        acc[: len(keep)] = torch.tensor(keep, dtype=torch.int32)
+        eng.commit(par, acc, state)
+        cache.offset = past_length + len(keep)
+        self._pending = None
 
 
 ADAPTERS: dict[str, type[TargetAdapter]] = {
@@ -380,9 +478,11 @@ def quantize_target_model(target: "LoadedTargetModel", bits: int = 4, group_size
     """``quantize_model`` on a loaded target (api.py:46-54): its projections
     become MLX affine 4-bit, engines built for the bf16 weights are released.
     Returns the ``quantization`` config entry."""
-    from .synthetic import quantize_weights
+    from .synthetic import Qwen35Weights, quantize_weights
 
     model = target.model
+    if isinstance(model.weights, Qwen35Weights):
+        raise NotImplementedError("4-bit weights are implemented for the Qwen3 target only")
     for eng in list(model.engines.values()):
         eng.close()
     model.engines.clear()
@@ -394,18 +494,26 @@ def quantize_target_model(target: "LoadedTargetModel", bits: int = 4, group_size
 def load_target_model(path_or_repo: str, device: str = "cuda") -> LoadedTargetModel:
     """adapters.py:822-846.  Checkpoints are not available offline; the
     ``synthetic:<preset>`` spec builds a seeded random-init target of a
-    BASELINE shape (``qwen3-tiny``, ``qwen3-4b``)."""
+    BASELINE shape (``qwen3-tiny``, ``qwen3-4b``, ``qwen35-tiny``,
+    ``qwen35-9b``)."""
     if not str(path_or_repo).startswith("synthetic:"):
         raise NotImplementedError(
             f"Unsupported target {path_or_repo!r}: checkpoint loading is not implemented in this build; "
             f"use 'synthetic:<preset>' with preset in {sorted(PRESETS)}."
         )
     spec = parse_synthetic_spec(path_or_repo)
+    if spec["preset"] in QWEN35_PRESETS:
+        from .synthetic import random_qwen35_weights
+
+        cfg = QWEN35_PRESETS[spec["preset"]]
+        weights = random_qwen35_weights(cfg, seed=spec["seed"], device=device)
+        model = SyntheticQwen3(cfg, weights, kv_capacity=spec["kv"], seed=spec["seed"])
+        return LoadedTargetModel(path_or_repo, Path(path_or_repo), model, ByteTokenizer(), Qwen35TargetAdapter())
     cfg = PRESETS.get(spec["preset"])
     if cfg is None:
         raise NotImplementedError(f"unknown synthetic preset {spec['preset']!r}")
     adapter_cls = adapter_for_model_type(cfg.model_type)
-    if adapter_cls is None or adapter_cls is Qwen35TargetAdapter:
+    if adapter_cls is None:
         raise NotImplementedError(f"Unsupported model_type={cfg.model_type!r}")
     weights = random_qwen3_weights(cfg, seed=spec["seed"], device=device)
     model = SyntheticQwen3(cfg, weights, kv_capacity=spec["kv"], seed=spec["seed"])

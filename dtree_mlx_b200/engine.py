@@ -150,6 +150,20 @@ class Qwen3Engine:
     def hidden_width(self) -> int:
         return self.cfg.hidden_size * max(1, len(self.layer_ids))
 
+    # -- decode-session hooks (shared with the Qwen3.5 engine) ---------------
+    def prefill_chunk(self, tokens, positions, anc, n: int, state, posterior) -> None:
+        self.forward_tree(tokens, positions, anc, n, state, posterior)
+
+    def verify(self, session) -> None:
+        self.forward_tree(session.tree.tokens, session.tree.positions, session.tree.anc, session.cfg.n_nodes,
+                          session.state, session.posterior)
+
+    def commit_step(self, session) -> None:
+        """compact_kv_caches (adapters.py:635-668); a DFlash chain keeps its
+        accepted rows where they are."""
+        if session.cfg.mode == "dtree":
+            kernels.kv_compact(self.kv_cache, session.accepted, session.state)
+
 
 @dataclass
 class StepConfig:
@@ -206,6 +220,8 @@ class DecodeSession:
         chunk = eng.t_cap
         toks = torch.tensor(prompt, dtype=torch.int32, device=dev)
         self.output[:n] = toks
+        if hasattr(eng, "reset_states"):  # a new sequence starts from zero recurrent state
+            eng.reset_states()
         start = 0
         hidden_rows = []
         while start < n:
@@ -213,11 +229,14 @@ class DecodeSession:
             self.state[0] = start
             pos = torch.arange(start, start + t, dtype=torch.int32, device=dev)
             anc = torch.from_numpy(chain_anc_masks(t).view(np.int64)).to(dev)
-            eng.forward_tree(toks[start:start + t].contiguous(), pos, anc, t, self.state, self.posterior)
+            eng.prefill_chunk(toks[start:start + t].contiguous(), pos, anc, t, self.state, self.posterior)
             hidden_rows.append(eng.capture[:t].clone())
             start += t
         first = int(self.posterior[t - 1].item())  # last prompt row of the last chunk
         self.prompt_hidden = torch.cat(hidden_rows, dim=0)
+        # recurrent targets: remember the post-prompt states so that ``reset``
+        # can restart decoding from the prompt (the KV prefix needs no copy)
+        self._snapshot = eng.snapshot_states() if hasattr(eng, "snapshot_states") else None
         self.reset(n, first)
         return first
 
@@ -228,6 +247,8 @@ class DecodeSession:
         self.state[1] = first_token
         self.output[prompt_len] = first_token
         self.prompt_len = prompt_len
+        if getattr(self, "_snapshot", None) is not None:
+            self.engine.restore_states(self._snapshot)
 
     # ------------------------------------------------------------ one step
     def step(self) -> None:
@@ -239,10 +260,9 @@ class DecodeSession:
             self.builder.build(self.draft_logits, self.state, self.tree, keep_topk=False)
         else:
             kernels.chain_build(self.draft_logits[: c.rows], self.state, self.tree)
-        eng.forward_tree(self.tree.tokens, self.tree.positions, self.tree.anc, c.n_nodes, self.state, self.posterior)
+        eng.verify(self)
         kernels.accept_walk(self.tree, self.posterior, self.state, self.accepted, self.output, self.history)
-        if c.mode == "dtree":
-            kernels.kv_compact(eng.kv_cache, self.accepted, self.state)
+        eng.commit_step(self)
         if getattr(self.drafter, "needs_hidden", False):
             kernels.gather_rows(eng.capture, self.accepted, self.state, self.target_hidden)
         kernels.step_commit(self.state)

@@ -75,7 +75,8 @@ class Qwen35Engine:
             n_lin, cfg.linear_num_value_heads, cfg.linear_value_head_dim, cfg.linear_key_head_dim)
         tp = 16 if self.t_cap <= 16 else 32 if self.t_cap <= 32 else 64 if self.t_cap <= 64 else 128
         self.norm_out = self.buffers["norm_out"][: tp * cfg.hidden_size].view(tp, cfg.hidden_size)
-        self.capture = self.buffers["capture"]
+        cw = cfg.hidden_size * max(1, len(self.layer_ids))
+        self.capture = self.buffers["capture"][: tp * cw].view(tp, cw)
         self._desc = d
         handle = C.c_void_p()
         call("dtree_qwen35_create", C.byref(d), C.byref(handle))
@@ -98,3 +99,37 @@ class Qwen35Engine:
 
     def commit(self, parents, accepted, state) -> None:
         call("dtree_qwen35_commit", self._handle, ptr(parents), ptr(accepted), ptr(state), stream_ptr())
+
+    def reset_states(self) -> None:
+        """Fresh sequence: zero conv / recurrent states (make_cache, adapters.py:216-240)."""
+        self.conv_state.zero_()
+        self.rec_state.zero_()
+
+    def snapshot_states(self) -> tuple[torch.Tensor, torch.Tensor]:
+        """Copy of the DeltaNet conv / recurrent states (snapshot_linear_caches,
+        custom_qwen35_model.py:1099-1109)."""
+        return self.conv_state.clone(), self.rec_state.clone()
+
+    def restore_states(self, snap) -> None:
+        """restore_linear_caches (custom_qwen35_model.py:1111-1121)."""
+        self.conv_state.copy_(snap[0])
+        self.rec_state.copy_(snap[1])
+
+    @property
+    def hidden_width(self) -> int:
+        return self.cfg.hidden_size * max(1, len(self.layer_ids))
+
+    # -- decode-session hooks (same as the Qwen3 engine's) -------------------
+    def prefill_chunk(self, tokens, positions, anc, n: int, state, posterior) -> None:
+        """Sequence forward (mode 1): chain parents, states advance."""
+        parents = torch.arange(-1, n - 1, dtype=torch.int32, device=self.device)
+        self.forward(tokens, positions, parents, anc, n, state, posterior, mode=1)
+
+    def verify(self, session) -> None:
+        t = session.tree
+        self.forward(t.tokens, t.positions, t.parents, t.anc, session.cfg.n_nodes, session.state,
+                     session.posterior, mode=0)
+
+    def commit_step(self, session) -> None:
+        """commit_qwen35_tree_path for the accepted path (DTree and DFlash)."""
+        self.commit(session.tree.parents, session.accepted, session.state)

@@ -215,13 +215,11 @@ def _profiled_step(session: DecodeSession, stages: dict[str, float]) -> None:
     else:
         kernels.chain_build(session.draft_logits[: c.rows], session.state, session.tree)
     ev[2].record()
-    eng.forward_tree(session.tree.tokens, session.tree.positions, session.tree.anc, c.n_nodes, session.state,
-                     session.posterior)
+    eng.verify(session)
     ev[3].record()
     kernels.accept_walk(session.tree, session.posterior, session.state, session.accepted, session.output,
                         session.history)
-    if c.mode == "dtree":
-        kernels.kv_compact(eng.kv_cache, session.accepted, session.state)
+    eng.commit_step(session)
     if getattr(session.drafter, "needs_hidden", False):
         kernels.gather_rows(eng.capture, session.accepted, session.state, session.target_hidden)
     kernels.step_commit(session.state)

@@ -25,9 +25,9 @@ import numpy as np
 import torch
 
 from . import kernels
-from .config import PRESETS
+from .config import PRESETS, QWEN35_PRESETS
 from .engine import Qwen3Engine
-from .synthetic import quantize_weights, random_qwen3_weights
+from .synthetic import quantize_weights, random_qwen35_weights, random_qwen3_weights
 
 
 def dirichlet_draft_logits(rows: int, vocab: int, seed: int, support: int = 32, alpha: float = 0.1) -> np.ndarray:
@@ -48,6 +48,15 @@ def algorithmic_bytes(cfg, weights, prefix: int, t: int) -> float:
     return float(wbytes + prefix * kv_row + t * kv_row)
 
 
+def hybrid_algorithmic_bytes(cfg, weights, prefix: int, t: int) -> float:
+    """Weights once + attention-layer K/V prefix read + new K/V write +
+    DeltaNet conv / recurrent base states read (Qwen3.5 hybrid)."""
+    kv_row = 2 * cfg.num_key_value_heads * cfg.head_dim * 2 * cfg.n_attn
+    states = cfg.n_linear * (cfg.linear_num_value_heads * cfg.linear_value_head_dim * cfg.linear_key_head_dim * 4
+                             + (cfg.linear_conv_kernel_dim - 1) * cfg.conv_dim * 2)
+    return float(weights.streamed_bytes() + prefix * kv_row + t * kv_row + states)
+
+
 def measured_hbm_gbs() -> tuple[float, str]:
     p = Path(__file__).resolve().parents[1] / "MEASURED_PEAKS.json"
     if p.exists():
@@ -57,6 +66,8 @@ def measured_hbm_gbs() -> tuple[float, str]:
 
 def run(preset: str, layers: int | None, prefixes: list[int], budgets: list[int], iters: int, seed: int = 0,
         eager_only: bool = False, quant_bits: int = 16) -> list[dict]:
+    if preset in QWEN35_PRESETS:
+        return run_hybrid(preset, layers, prefixes, budgets, iters, seed, eager_only)
     cfg = PRESETS[preset]
     if layers:
         cfg = replace(cfg, num_hidden_layers=layers)
@@ -114,12 +125,80 @@ def run(preset: str, layers: int | None, prefixes: list[int], budgets: list[int]
     return results
 
 
+def _time(fn, iters: int, eager_only: bool) -> float:
+    for _ in range(3):
+        fn()
+    torch.cuda.synchronize()
+    graph = None
+    if not eager_only:
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=s):
+            fn()
+        torch.cuda.current_stream().wait_stream(s)
+        for _ in range(3):
+            graph.replay()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    a.record()
+    for _ in range(iters):
+        graph.replay() if graph is not None else fn()
+    b.record()
+    torch.cuda.synchronize()
+    del graph
+    return a.elapsed_time(b) / iters
+
+
+def run_hybrid(preset: str, layers: int | None, prefixes: list[int], budgets: list[int], iters: int, seed: int,
+               eager_only: bool) -> list[dict]:
+    """BASELINE config 4 verify: the Qwen3.5 hybrid tree forward
+    (``dtree_qwen35_forward`` mode 0, LM-head argmax included) on random
+    committed states and a random bf16 K/V prefix."""
+    from .engine35 import Qwen35Engine
+
+    cfg = QWEN35_PRESETS[preset]
+    if layers:
+        cfg = replace(cfg, num_hidden_layers=layers)
+    dev = torch.device("cuda")
+    w = random_qwen35_weights(cfg, seed=seed, device=dev)
+    eng = Qwen35Engine(w, kv_capacity=max(prefixes) + 160)
+    g = torch.Generator(device=dev).manual_seed(seed + 1)
+    eng.kv_cache.copy_(torch.randn(eng.kv_cache.shape, generator=g, device=dev).to(torch.bfloat16))
+    eng.rec_state.copy_(torch.randn(eng.rec_state.shape, generator=g, device=dev) * 0.05)
+    eng.conv_state.copy_((torch.randn(eng.conv_state.shape, generator=g, device=dev) * 0.05).to(torch.bfloat16))
+    peak, peak_src = measured_hbm_gbs()
+    results = []
+    for budget in budgets:
+        logits = torch.from_numpy(dirichlet_draft_logits(16, cfg.vocab_size, seed + budget)).to(dev)
+        for P in prefixes:
+            st = kernels.new_state(dev, start=P, root_token=1)
+            tree = kernels.TreeBuffers.allocate(dev)
+            kernels.TreeBuilder(16, cfg.vocab_size, budget, dev).build(logits, st, tree, keep_topk=False)
+            n = int(st[6].item())
+            post = torch.zeros(128, dtype=torch.int32, device=dev)
+
+            def fwd():
+                eng.forward(tree.tokens, tree.positions, tree.parents, tree.anc, n, st, post, mode=0)
+
+            ms = _time(fwd, iters, eager_only)
+            nbytes = hybrid_algorithmic_bytes(cfg, w, P, n)
+            gbs = nbytes / (ms / 1e3) / 1e9
+            results.append({"preset": preset, "prefix": P, "tree_budget": budget, "tree_rows": n,
+                            "verify_ms": round(ms, 4), "algorithmic_gb": round(nbytes / 1e9, 4),
+                            "achieved_gbs": round(gbs, 1), "frac_of_hbm": round(gbs / peak, 4), "peak_gbs": peak,
+                            "peak_source": peak_src, "layers": cfg.num_hidden_layers})
+    eng.close()
+    return results
+
+
 KERNEL_GROUPS = (
     ("lm_head", lambda k: k.startswith("gemm_streamk_kernel") and k.endswith(", 4>")),
     ("gemm", lambda k: k.startswith("gemm_streamk_kernel")),
     ("attention", lambda k: k.startswith(("tree_attn_kernel", "attn_combine_kernel"))),
     ("norm_rope", lambda k: k.startswith(("residual_rmsnorm_kernel", "rmsnorm_kernel", "qkv_finish_kernel"))),
     ("tree_build", lambda k: k.startswith(("topk_lse_kernel", "heap_tree_kernel"))),
+    ("deltanet", lambda k: k.startswith(("tree_conv1d_kernel", "tree_gated_delta_kernel", "rmsnorm_gated_kernel"))),
 )
 
 

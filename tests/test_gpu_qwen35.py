@@ -133,3 +133,26 @@ def test_prefill_tree_commit_match_oracle(hybrid):
         root = nxt
     assert _lib.device_error() == 0
     eng.close()
+
+
+def test_generate_api_hybrid(lib):
+    """DTree and DFlash decoding of the tiny hybrid through DFlashGenerator:
+    both are exact greedy decoders of the same target, so their outputs agree
+    (until a near-tie flips a token) and every step accepts at least one."""
+    from dtree_mlx_b200 import DFlashGenerator
+    from dtree_mlx_b200.synthetic import random_prompt
+
+    gen = DFlashGenerator(target_model="synthetic:qwen35-tiny:seed=0:kv=1024", draft_model="planted:p=0.8:seed=1")
+    prompt = random_prompt(200, 8192, seed=0)  # > 128: two prefill chunks
+    r_tree = gen.generate_from_tokens(prompt, max_new_tokens=48, decode_mode="dtree", speculative_tokens=16,
+                                      tree_budget=24)
+    r_lin = gen.generate_from_tokens(prompt, max_new_tokens=48, decode_mode="dflash", speculative_tokens=16,
+                                     verify_mode="parallel-greedy-argmax")
+    for r in (r_tree, r_lin):
+        assert len(r.output_tokens) == 200 + 48 and r.output_tokens[:200] == prompt
+        assert r.metrics["num_output_tokens"] == 48
+    first_diff = next((i for i, (a, b) in enumerate(zip(r_tree.generated_tokens, r_lin.generated_tokens)) if a != b),
+                      48)
+    print(f"hybrid dtree vs dflash: first difference at {first_diff}/48, accept "
+          f"{r_tree.metrics['avg_acceptance_length']:.2f} / {r_lin.metrics['avg_acceptance_length']:.2f}")
+    assert first_diff >= 8
