@@ -53,7 +53,7 @@ class DFlashGenerator:
         self.target_quantization = None
         if target_quant_bits is not None:
             self.target_quantization = quantize_target_model(self.target, target_quant_bits, target_quant_group_size)
-        self.draft, self.draft_path = load_draft_model(draft_model)
+        self.draft, self.draft_path = load_draft_model(draft_model, target=self.target)
         self.draft_attention_mask = "none" if draft_attention_mask == "auto" else draft_attention_mask
         self.draft_quantization = None
         del target_quant_group_size, draft_quant_group_size

@@ -169,3 +169,44 @@ QWEN35_PRESETS: dict[str, Qwen35Config] = {
         linear_value_head_dim=128,
     ),
 }
+
+
+@dataclass(frozen=True)
+class DraftConfig:
+    """DFlash block drafter (dtree_mlx/draft.py:26-70 DraftArgs): Qwen3 decoder
+    layers over the target's hidden size, ``fc`` from the concatenated target
+    hiddens of ``target_layer_ids``.  The trained checkpoints' configs are not
+    available offline, so these shapes are chosen to match their targets."""
+
+    hidden_size: int
+    num_hidden_layers: int
+    num_attention_heads: int
+    num_key_value_heads: int
+    head_dim: int
+    intermediate_size: int
+    vocab_size: int
+    target_layer_ids: tuple
+    block_size: int = 16
+    mask_token_id: int = 0
+    rope_theta: float = 1_000_000.0
+    rms_norm_eps: float = 1e-6
+
+    @property
+    def q_dim(self) -> int:
+        return self.num_attention_heads * self.head_dim
+
+    @property
+    def kv_dim(self) -> int:
+        return self.num_key_value_heads * self.head_dim
+
+
+DRAFT_PRESETS: dict[str, DraftConfig] = {
+    # drafter for the Qwen3-4B-shaped target (5 target layers, 5 drafter layers)
+    "qwen3-4b": DraftConfig(hidden_size=2560, num_hidden_layers=5, num_attention_heads=32, num_key_value_heads=8,
+                            head_dim=128, intermediate_size=9728, vocab_size=151936,
+                            target_layer_ids=(1, 9, 18, 26, 34), mask_token_id=151669),
+    # small drafter for the tiny target of the parity tests
+    "qwen3-tiny": DraftConfig(hidden_size=512, num_hidden_layers=2, num_attention_heads=8, num_key_value_heads=4,
+                              head_dim=64, intermediate_size=1536, vocab_size=32768, target_layer_ids=(1, 3),
+                              mask_token_id=32767),
+}

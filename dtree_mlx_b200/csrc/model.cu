@@ -23,6 +23,7 @@
 
 #include "attention.cuh"
 #include "gemm.cuh"
+#include "qkv.cuh"
 
 namespace dtree {
 
@@ -33,24 +34,7 @@ int residual_rmsnorm_launch(__nv_bfloat16* h, const float* partials, int n_split
                             __nv_bfloat16* capture, int ldc, const __nv_bfloat16* w, __nv_bfloat16* xn, int H,
                             int n_rows, int t_pad, float eps, cudaStream_t stream);
 
-struct QkvFinishParams {
-  const float* partials;
-  int split, part_rows, width;
-  int head_dim, n_q_heads, n_kv_heads;
-  const __nv_bfloat16* q_norm;
-  const __nv_bfloat16* k_norm;
-  float eps, rope_log2_theta;
-  const int32_t* positions;
-  const dtree_step_state* state;
-  __nv_bfloat16* q_out;
-  __nv_bfloat16* k_cache;
-  __nv_bfloat16* v_cache;
-  int kv_cap;
-  int gated;
-  __nv_bfloat16* gate_out;
-  int rot_dims;
-};
-int qkv_finish_launch(const QkvFinishParams& p, int n_rows, cudaStream_t stream);
+// QkvFinishParams, qkv_finish_launch: qkv.cuh
 
 constexpr int kAttnMaxSplits = 32;
 constexpr int kMaxProjSplit = 16;  // split-K of the hidden-width projections (o_proj, down_proj)
@@ -67,6 +51,7 @@ struct PlanSet {
   bool ready = false;
   std::vector<GemmPlan> qkv, o, gu, down;
   GemmPlan lm;
+  GemmPlan lm_logits;  // fp32 logits (kEpiPartial, one split) for drafters
 };
 
 }  // namespace dtree
@@ -141,6 +126,9 @@ static int build_plans(dtree_qwen3_model* m, int t_pad) {
   int rc = gemm_plan(&ps.lm, d.embed, d.vocab, d.hidden, d.norm_out, t_pad, d.hidden, kEpiArgmax, 0);
   if (rc) return rc;
   if ((rc = gemm_bind_ws(&ps.lm, m->gemm_ws, m->gemm_ws_bytes))) return rc;
+  if ((rc = gemm_plan(&ps.lm_logits, d.embed, d.vocab, d.hidden, d.norm_out, t_pad, d.hidden, kEpiPartial, 1)))
+    return rc;
+  if ((rc = gemm_bind_ws(&ps.lm_logits, m->gemm_ws, m->gemm_ws_bytes))) return rc;
   ps.ready = true;
   return kOk;
 }
@@ -221,9 +209,90 @@ extern "C" int dtree_qwen3_destroy(dtree_qwen3_model* m) {
   return kOk;
 }
 
+static int forward_impl(dtree_qwen3_model* m, const int32_t* tree_tokens, const int32_t* positions,
+                        const uint64_t* anc_mask, int n_nodes, const dtree_step_state* state, int32_t* posterior,
+                        float* logits, void* stream_);
+
 extern "C" int dtree_qwen3_forward_tree(dtree_qwen3_model* m, const int32_t* tree_tokens, const int32_t* positions,
                                         const uint64_t* anc_mask, int n_nodes, const dtree_step_state* state,
                                         int32_t* posterior, void* stream_) {
+  return forward_impl(m, tree_tokens, positions, anc_mask, n_nodes, state, posterior, nullptr, stream_);
+}
+
+extern "C" int dtree_qwen3_forward_logits(dtree_qwen3_model* m, const int32_t* tokens, const int32_t* positions,
+                                          const uint64_t* anc_mask, int n_rows, const dtree_step_state* state,
+                                          float* logits, void* stream_) {
+  DTREE_CHECK_ARG(logits, "null logits");
+  return forward_impl(m, tokens, positions, anc_mask, n_rows, state, nullptr, logits, stream_);
+}
+
+extern "C" int dtree_dflash_context(dtree_qwen3_model* m, const void* fc_weight, const void* hidden_norm,
+                                    const void* target_hidden, int ld_hidden, int width, int n_rows, int ctx_base,
+                                    const dtree_step_state* state, void* stream_) {
+  DTREE_CHECK_ARG(m && fc_weight && hidden_norm && target_hidden && state, "null pointer");
+  const dtree_qwen3_desc& d = m->d;
+  DTREE_CHECK_ARG(n_rows > 0 && n_rows <= d.t_cap, "n_rows must be in [1, t_cap]");
+  DTREE_CHECK_ARG(width % 64 == 0 && ld_hidden >= width, "context width must be a multiple of 64 <= ld_hidden");
+  cudaStream_t st = static_cast<cudaStream_t>(stream_);
+  const int t_pad = pad_rows(n_rows);
+  auto bw = [](void* p) { return static_cast<__nv_bfloat16*>(p); };
+  // ctx = RMSNorm(fc(target_hidden), hidden_norm)   (draft.py:329-330)
+  GemmPlan fc;
+  int rc = gemm_plan(&fc, fc_weight, d.hidden, width, target_hidden, t_pad, ld_hidden, kEpiStore, 0);
+  if (rc) return rc;
+  if ((rc = gemm_bind_ws(&fc, m->gemm_ws, m->gemm_ws_bytes))) return rc;
+  fc.p.n_rows = n_rows;
+  fc.p.out = bw(d.norm_out);
+  fc.p.ldo = d.hidden;
+  if ((rc = gemm_launch(fc, st))) return rc;
+  if ((rc = rmsnorm_launch(static_cast<const __nv_bfloat16*>(d.norm_out), d.hidden, nullptr, nullptr, nullptr,
+                           static_cast<const __nv_bfloat16*>(hidden_norm), bw(d.xn), d.hidden, n_rows, t_pad,
+                           d.rms_eps, st)))
+    return rc;
+  // per layer: k_norm(k_proj(ctx)) with RoPE at the rows' positions, v_proj(ctx)
+  // -> draft cache slots (DFlashAttention.precompute_context_kv, draft.py:172-187)
+  const int kvw = 2 * d.n_kv_heads * d.head_dim;
+  const int qd = d.n_heads * d.head_dim;
+  const size_t plane = static_cast<size_t>(d.n_kv_heads) * d.kv_capacity * d.head_dim;
+  for (int l = 0; l < d.layers; ++l) {
+    const dtree_qwen3_layer& L = m->layers[l];
+    GemmPlan g;
+    const void* wkv = static_cast<const __nv_bfloat16*>(L.qkv) + static_cast<size_t>(qd) * d.hidden;
+    if ((rc = gemm_plan(&g, wkv, kvw, d.hidden, d.xn, t_pad, d.hidden, kEpiPartial, proj_split(d, kvw)))) return rc;
+    DTREE_CHECK_ARG(static_cast<size_t>(g.p.split) * kvw * t_pad * 4 <= partials_need(d),
+                    "context K/V partials exceed the workspace");
+    if ((rc = gemm_bind_ws(&g, m->gemm_ws, m->gemm_ws_bytes))) return rc;
+    g.p.n_rows = n_rows;
+    g.p.out_f32 = m->proj_partials;
+    g.p.ldo = kvw;
+    if ((rc = gemm_launch(g, st))) return rc;
+    QkvFinishParams f{};
+    f.partials = m->proj_partials;
+    f.split = g.p.split;
+    f.part_rows = t_pad;
+    f.width = kvw;
+    f.head_dim = d.head_dim;
+    f.n_q_heads = 0;
+    f.n_kv_heads = d.n_kv_heads;
+    f.q_norm = static_cast<const __nv_bfloat16*>(L.q_norm);
+    f.k_norm = static_cast<const __nv_bfloat16*>(L.k_norm);
+    f.eps = d.rms_eps;
+    f.rope_log2_theta = std::log2(d.rope_theta);
+    f.state = state;
+    f.k_cache = bw(d.kv_cache) + (static_cast<size_t>(l) * 2 + 0) * plane;
+    f.v_cache = bw(d.kv_cache) + (static_cast<size_t>(l) * 2 + 1) * plane;
+    f.kv_cap = d.kv_capacity;
+    f.slot_mode = ctx_base >= 0 ? 2 : 1;
+    f.ctx_base = ctx_base;
+    f.ctx_count = n_rows;
+    if ((rc = qkv_finish_launch(f, n_rows, st))) return rc;
+  }
+  return kOk;
+}
+
+static int forward_impl(dtree_qwen3_model* m, const int32_t* tree_tokens, const int32_t* positions,
+                        const uint64_t* anc_mask, int n_nodes, const dtree_step_state* state, int32_t* posterior,
+                        float* logits, void* stream_) {
   DTREE_CHECK_ARG(m && tree_tokens && positions && anc_mask && state, "null pointer");
   const dtree_qwen3_desc& d = m->d;
   DTREE_CHECK_ARG(n_nodes > 0 && n_nodes <= d.t_cap, "n_nodes must be in [1, t_cap]");
@@ -337,6 +406,13 @@ extern "C" int dtree_qwen3_forward_tree(dtree_qwen3_model* m, const int32_t* tre
                                     capture_ptr(d.layers - 1), ldc, bf(d.final_norm), bw(d.norm_out), d.hidden,
                                     n_nodes, t_pad, d.rms_eps, st)))
     return rc;
+  if (logits) {  // full fp32 logits [t_pad][vocab]
+    GemmPlan g = ps.lm_logits;
+    g.p.n_rows = n_nodes;
+    g.p.out_f32 = logits;
+    g.p.ldo = d.vocab;
+    if ((rc = gemm_launch(g, st))) return rc;
+  }
   if (posterior) {
     GemmPlan g = ps.lm;
     g.p.n_rows = n_nodes;

@@ -11,28 +11,11 @@
 // rotates only the first rot_dims features (partial_rotary_factor), pairs
 // (i, i + rot_dims/2) with inv_freq_i = theta^(-2i/rot_dims) (mlx RoPE with
 // dims = rot_dims, traditional = False); the rest pass through.
-#include "common.cuh"
-#include "../../include/dtree_b200.h"
+#include "qkv.cuh"
 
 namespace dtree {
 
-struct QkvFinishParams {
-  const float* partials;  // [split][part_rows][width]
-  int split, part_rows, width;
-  int head_dim, n_q_heads, n_kv_heads;
-  const __nv_bfloat16* q_norm;
-  const __nv_bfloat16* k_norm;
-  float eps, rope_log2_theta;
-  const int32_t* positions;
-  const dtree_step_state* state;
-  __nv_bfloat16* q_out;  // [t_pad][n_q_heads*head_dim]
-  __nv_bfloat16* k_cache;  // [n_kv_heads][kv_cap][head_dim]
-  __nv_bfloat16* v_cache;
-  int kv_cap;
-  int gated;                // q rows are [q | gate] per head
-  __nv_bfloat16* gate_out;  // [t_pad][n_q_heads*head_dim] (gated only)
-  int rot_dims;             // rotated features per head (0: all)
-};
+
 
 __global__ void __launch_bounds__(256) qkv_finish_kernel(QkvFinishParams p) {
   pdl_trigger();
@@ -63,10 +46,20 @@ __global__ void __launch_bounds__(256) qkv_finish_kernel(QkvFinishParams p) {
   if (p.gated && gh < p.n_q_heads)
     p.gate_out[static_cast<size_t>(t) * (p.n_q_heads * hd) + gh * hd + d] = __float2bfloat16_rn(sum_splits(col + hd));
   const int start = p.state->start;
-  const int slot = start + t;
+  int slot = start + t;
+  float pos_t = 0.0f;
+  if (p.slot_mode != 0) {
+    const int cnt = p.slot_mode == 1 ? p.state->n_accepted : p.ctx_count;
+    const int base = p.slot_mode == 1 ? start - cnt : p.ctx_base;
+    if (t >= cnt) return;  // uniform per block
+    slot = base + t;
+    pos_t = static_cast<float>(slot);
+  } else {
+    pos_t = static_cast<float>(p.positions[t]);
+  }
   if (gh >= p.n_q_heads + p.n_kv_heads) {  // v
     const int kvh = gh - p.n_q_heads - p.n_kv_heads;
-    if (slot < p.kv_cap) p.v_cache[(static_cast<size_t>(kvh) * p.kv_cap + slot) * hd + d] = __float2bfloat16_rn(a);
+    if (slot >= 0 && slot < p.kv_cap) p.v_cache[(static_cast<size_t>(kvh) * p.kv_cap + slot) * hd + d] = __float2bfloat16_rn(a);
     else dev_error(0x2001u);
     return;
   }
@@ -89,7 +82,7 @@ __global__ void __launch_bounds__(256) qkv_finish_kernel(QkvFinishParams p) {
     const int i_f = d % half;
     const float inv_freq = exp2f(-(2.0f * static_cast<float>(i_f) / static_cast<float>(rd)) * p.rope_log2_theta);
     float sn, cs;
-    sincosf(static_cast<float>(p.positions[t]) * inv_freq, &sn, &cs);
+    sincosf(pos_t * inv_freq, &sn, &cs);
     const float yp = s_y[d < half ? d + half : d - half];
     outv = (d < half) ? (y * cs - yp * sn) : (y * cs + yp * sn);
   }
@@ -97,7 +90,7 @@ __global__ void __launch_bounds__(256) qkv_finish_kernel(QkvFinishParams p) {
     p.q_out[static_cast<size_t>(t) * (p.n_q_heads * hd) + gh * hd + d] = __float2bfloat16_rn(outv);
   } else {
     const int kvh = gh - p.n_q_heads;
-    if (slot < p.kv_cap) p.k_cache[(static_cast<size_t>(kvh) * p.kv_cap + slot) * hd + d] = __float2bfloat16_rn(outv);
+    if (slot >= 0 && slot < p.kv_cap) p.k_cache[(static_cast<size_t>(kvh) * p.kv_cap + slot) * hd + d] = __float2bfloat16_rn(outv);
     else dev_error(0x2001u);
   }
 }

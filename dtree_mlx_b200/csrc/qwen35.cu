@@ -24,6 +24,7 @@
 #include "attention.cuh"
 #include "deltanet.cuh"
 #include "gemm.cuh"
+#include "qkv.cuh"
 
 namespace dtree {
 
@@ -34,24 +35,7 @@ int residual_rmsnorm_launch(__nv_bfloat16* h, const float* partials, int n_split
                             __nv_bfloat16* capture, int ldc, const __nv_bfloat16* w, __nv_bfloat16* xn, int H,
                             int n_rows, int t_pad, float eps, cudaStream_t stream);
 
-struct QkvFinishParams {
-  const float* partials;
-  int split, part_rows, width;
-  int head_dim, n_q_heads, n_kv_heads;
-  const __nv_bfloat16* q_norm;
-  const __nv_bfloat16* k_norm;
-  float eps, rope_log2_theta;
-  const int32_t* positions;
-  const dtree_step_state* state;
-  __nv_bfloat16* q_out;
-  __nv_bfloat16* k_cache;
-  __nv_bfloat16* v_cache;
-  int kv_cap;
-  int gated;
-  __nv_bfloat16* gate_out;
-  int rot_dims;
-};
-int qkv_finish_launch(const QkvFinishParams& p, int n_rows, cudaStream_t stream);
+// QkvFinishParams, qkv_finish_launch: qkv.cuh
 
 namespace {
 

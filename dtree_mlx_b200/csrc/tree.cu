@@ -726,6 +726,28 @@ extern "C" int dtree_accept_walk(const int32_t* tree_tokens, const int32_t* pare
   return kOk;
 }
 
+// DFlash block input (dtree_runtime.py:366-368): [current token, mask x
+// (block-1)] at positions start .. start+block-1.
+__global__ void dflash_block_kernel(const dtree_step_state* state, int mask_token_id, int block, int32_t* tokens,
+                                    int32_t* positions) {
+  pdl_trigger();
+  pdl_wait();
+  const int i = threadIdx.x;
+  if (i < block) {
+    tokens[i] = i == 0 ? state->root_token : mask_token_id;
+    positions[i] = state->start + i;
+  }
+}
+
+extern "C" int dtree_dflash_block(const dtree_step_state* state, int mask_token_id, int block, int32_t* tokens,
+                                  int32_t* positions, void* stream) {
+  DTREE_CHECK_ARG(state && tokens && positions, "null pointer");
+  DTREE_CHECK_ARG(block > 0 && block <= DTREE_MAX_TREE, "block must be in [1, 128]");
+  DTREE_CUDA_RET(launch_pdl(dflash_block_kernel, dim3(1), dim3(128), 0, static_cast<cudaStream_t>(stream), state,
+                            mask_token_id, block, tokens, positions));
+  return kOk;
+}
+
 extern "C" int dtree_kv_compact(void* kv_cache, int layers, int kv_heads, int capacity, int head_dim,
                                 const int32_t* accepted, const dtree_step_state* state, void* stream_) {
   cudaStream_t stream = static_cast<cudaStream_t>(stream_);

@@ -238,6 +238,8 @@ class DecodeSession:
         # can restart decoding from the prompt (the KV prefix needs no copy)
         self._snapshot = eng.snapshot_states() if hasattr(eng, "snapshot_states") else None
         self.reset(n, first)
+        if hasattr(self.drafter, "begin"):  # a model drafter ingests the prompt context
+            self.drafter.begin(self)
         return first
 
     def reset(self, prompt_len: int, first_token: int) -> None:

@@ -326,6 +326,35 @@ DTREE_API int dtree_qwen3_forward_tree(dtree_qwen3_model* model, const int32_t* 
                              const uint64_t* anc_mask, int n_nodes, const dtree_step_state* state,
                              int32_t* posterior, void* stream);
 
+/* ----------------------------------------------- DFlash block drafter
+ * The drafter (DFlashDraftModel, draft.py:318-367) is a stack of Qwen3
+ * decoder layers held as a dtree_qwen3 model whose `embed` is the TARGET's
+ * embedding (noise embedding and LM head, dtree_runtime.py:366-375) and
+ * whose KV cache is the draft cache.  One draft step:
+ *   dtree_dflash_context  -- precompute_context_kv (draft.py:172-187, 329-
+ *       336): ctx = RMSNorm(fc(target_hidden), hidden_norm); every layer's
+ *       k_norm(k_proj(ctx)) (RoPE at the row's position) and v_proj(ctx) go to
+ *       the draft cache.  ctx_base >= 0: rows [0, n_rows) at positions
+ *       ctx_base + t (prompt context); ctx_base < 0: the rows the last step
+ *       accepted, count state->n_accepted at positions state->start - count + t
+ *       (target_hidden row t = accepted node t, as dtree_gather_rows leaves it).
+ *       target_hidden is [n_rows][ld_hidden] bf16, the first `width` columns
+ *       used (hidden * number of target layers); fc_weight [hidden][width].
+ *   dtree_dflash_block    -- block tokens [state->root_token, mask ...] and
+ *       positions state->start + i.
+ *   dtree_qwen3_forward_logits -- the noise forward (attention to the whole
+ *       draft cache plus the block, no mask: anc rows all ones) with the
+ *       final RMSNorm and fp32 logits [pad16(n_rows)][vocab] of every row;
+ *       rows 1 .. block-1 are the draft logits (dtree_runtime.py:375). */
+DTREE_API int dtree_dflash_context(dtree_qwen3_model* model, const void* fc_weight, const void* hidden_norm,
+                         const void* target_hidden, int ld_hidden, int width, int n_rows, int ctx_base,
+                         const dtree_step_state* state, void* stream);
+DTREE_API int dtree_dflash_block(const dtree_step_state* state, int mask_token_id, int block, int32_t* tokens,
+                       int32_t* positions, void* stream);
+DTREE_API int dtree_qwen3_forward_logits(dtree_qwen3_model* model, const int32_t* tokens, const int32_t* positions,
+                               const uint64_t* anc_mask, int n_rows, const dtree_step_state* state, float* logits,
+                               void* stream);
+
 /* ------------------------------------------ Qwen3.5 hybrid tree verify
  * A Qwen3.5 text model (custom_qwen35_model.py:777-924): layer l is a gated
  * DeltaNet layer unless (l + 1) % full_attention_interval == 0, then a gated
