@@ -163,6 +163,7 @@ def run_ours(args, rank, world, local, dist) -> dict | None:
     from dtree_mlx_b200.adapters import load_target_model, quantize_target_model
     from dtree_mlx_b200.draft import PlantedDrafter
     from dtree_mlx_b200.engine import DecodeSession
+    from dtree_mlx_b200.replicas import gather_replica_stats, max_over_ranks, sum_over_ranks
     from dtree_mlx_b200.synthetic import random_prompt
 
     dev = torch.device("cuda", local)
@@ -219,9 +220,7 @@ def run_ours(args, rank, world, local, dist) -> dict | None:
     torch.cuda.synchronize()
     ms = e0.elapsed_time(e1)
     if dist:
-        t = torch.tensor([ms], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
+        ms = max_over_ranks(dist, ms, dev)
         dist.barrier()
     clocks = sampler.stop() if sampler else None
 
@@ -267,18 +266,11 @@ def run_ours(args, rank, world, local, dist) -> dict | None:
         assert rr.output_tokens == stream
     e2e_tok_s = MAX_NEW / (statistics.median(e2e_ms) / 1e3)
 
-    stats = torch.tensor([MAX_NEW * args.steps, ms, n_steps, sum(accept)], dtype=torch.float64, device=dev)
-    all_stats = [stats]
-    if dist:
-        all_stats = [torch.zeros_like(stats) for _ in range(world)]
-        dist.all_gather(all_stats, stats)
-        e2e_t = torch.tensor([e2e_tok_s], device=dev)
-        dist.all_reduce(e2e_t)
-        e2e_tok_s = float(e2e_t.item())
+    agg = gather_replica_stats(dist, world, MAX_NEW * args.steps, ms, n_steps, sum(accept), dev)
+    e2e_tok_s = sum_over_ranks(dist, e2e_tok_s, dev)
     if rank != 0:
         return None
-    total_tokens = sum(float(s[0]) for s in all_stats)
-    value = total_tokens / (ms / 1e3)
+    value = agg["total_tokens"] / (ms / 1e3)
     peaks = measured_peaks()
     vms, vbytes = roof[2048]
     achieved = vbytes / (vms / 1e3) / 1e9

@@ -105,7 +105,10 @@ int gemm_plan_q4(GemmPlan* plan, const void* w_packed, const void* scales, const
 }
 
 int gemm_bind_ws(GemmPlan* plan, void* ws, size_t ws_bytes) {
-  DTREE_CHECK_ARG(ws != nullptr && ws_bytes >= gemm_ws_bytes(plan->t_pad, plan->p.grid), "GEMM workspace too small");
+  // split-K partial plans write every tile straight to out_f32: only the
+  // counter block of the workspace is touched
+  const size_t need = plan->epi == kEpiPartial ? kCountersBytes : gemm_ws_bytes(plan->t_pad, plan->p.grid);
+  DTREE_CHECK_ARG(ws != nullptr && ws_bytes >= need, "GEMM workspace too small");
   GemmWs w = ws_split(ws);
   plan->p.ws = w.partials;
   plan->p.tile_cnt = w.tile_cnt;

@@ -192,6 +192,41 @@ def run_hybrid(preset: str, layers: int | None, prefixes: list[int], budgets: li
     return results
 
 
+def run_drafter(preset: str, prefix: int, iters: int, eager_only: bool, seed: int = 0) -> dict:
+    """One DFlash draft step at the Qwen3-4B shape: append 16 accepted rows of
+    target hiddens to the draft cache, run the 16-token block through the
+    drafter layers against a ``prefix``-row context and produce fp32 logits
+    through the target's LM head (draft.py:318-367, dtree_runtime.py:366-376)."""
+    from types import SimpleNamespace
+
+    from .config import DRAFT_PRESETS
+    from .draft import DFlashDrafter, random_dflash_weights
+    from .synthetic import STD
+
+    cfg = DRAFT_PRESETS[preset]
+    dev = torch.device("cuda")
+    g = torch.Generator(device=dev).manual_seed(seed)
+    embed = (torch.randn(cfg.vocab_size, cfg.hidden_size, generator=g, device=dev) * STD).to(torch.bfloat16)
+    w = random_dflash_weights(cfg, embed, seed=seed)
+    d = DFlashDrafter(w, kv_capacity=prefix + 64)
+    d.engine.kv_cache.copy_(torch.randn(d.engine.kv_cache.shape, generator=g, device=dev).to(torch.bfloat16))
+    st = kernels.new_state(dev, start=prefix, root_token=1)
+    st[3] = 16  # the last step accepted 16 rows
+    width = w.fc.shape[1]
+    sess = SimpleNamespace(state=st, draft_logits=d.logits[1:16],
+                           target_hidden=(torch.randn(128, width, generator=g, device=dev) * 0.5).to(torch.bfloat16))
+    ms = _time(lambda: d.draft(sess), iters, eager_only)
+    wbytes = sum(x.numel() * x.element_size() for x in [embed, w.fc, *w.layers.qkv, *w.layers.o_proj,
+                                                          *w.layers.gate_up, *w.layers.down])
+    kv = prefix * 2 * cfg.kv_dim * 2 * cfg.num_hidden_layers
+    nbytes = wbytes + kv + cfg.vocab_size * 16 * 4  # + the fp32 logits written
+    peak, src = measured_hbm_gbs()
+    d.engine.close()
+    return {"drafter": preset, "prefix": prefix, "draft_ms": round(ms, 4), "algorithmic_gb": round(nbytes / 1e9, 4),
+            "achieved_gbs": round(nbytes / (ms / 1e3) / 1e9, 1), "frac_of_hbm": round(nbytes / (ms / 1e3) / 1e9 / peak, 4),
+            "peak_source": src, "layers": cfg.num_hidden_layers}
+
+
 KERNEL_GROUPS = (
     ("lm_head", lambda k: k.startswith("gemm_streamk_kernel") and k.endswith(", 4>")),
     ("gemm", lambda k: k.startswith("gemm_streamk_kernel")),
@@ -251,9 +286,14 @@ def main() -> None:
     ap.add_argument("--quant-bits", type=int, default=16, choices=[16, 4],
                     help="4: MLX affine 4-bit projections, group 64 (BASELINE config 3)")
     ap.add_argument("--json", action="store_true")
+    ap.add_argument("--drafter", default=None, help="time one DFlash draft step of this drafter preset and exit")
     ap.add_argument("--launches", default=None,
                     help="summarise an ncu launch-list CSV of an --eager sweep (attention/GEMM split) and exit")
     a = ap.parse_args()
+    if a.drafter:
+        for P in [int(x) for x in a.prefix.split(",")]:
+            print(json.dumps(run_drafter(a.drafter, P, a.iters, a.eager)))
+        return
     if a.launches:
         prefixes, budgets = a.prefix.split(","), a.budget.split(",")
         split = summarize_launches(a.launches, 3 + a.iters)
