@@ -332,6 +332,12 @@ __global__ void attn_combine_kernel(AttnParams p) {
   const int kps = attn_keys_per_split(L, p.splits);
   const int active = min(p.splits, (L + kps - 1) / kps);
   const int rows_total = p.n_q_heads * T;
+  // this thread's O partials of every split: loaded before the weights are
+  // known so the two reads overlap (splits <= 32)
+  float ov[32];
+#pragma unroll
+  for (int s = 0; s < 32; ++s)
+    ov[s] = s < active ? p.part_o[(static_cast<size_t>(s) * rows_total + qrow) * HD + d] : 0.0f;
   if (d < 32) {
     float m = -INFINITY, l = 0.0f;
     if (d < active) {
@@ -352,19 +358,9 @@ __global__ void attn_combine_kernel(AttnParams p) {
   }
   __syncthreads();
   float acc = 0.0f;
-  int s = 0;
-  for (; s + 3 < active; s += 4) {
-    const size_t r = static_cast<size_t>(s) * rows_total + qrow;
-    const float o0 = p.part_o[r * HD + d];
-    const float o1 = p.part_o[(r + rows_total) * HD + d];
-    const float o2 = p.part_o[(r + 2 * rows_total) * HD + d];
-    const float o3 = p.part_o[(r + 3 * rows_total) * HD + d];
-    acc += s_w[s] * o0;
-    acc += s_w[s + 1] * o1;
-    acc += s_w[s + 2] * o2;
-    acc += s_w[s + 3] * o3;
-  }
-  for (; s < active; ++s) acc += s_w[s] * p.part_o[(static_cast<size_t>(s) * rows_total + qrow) * HD + d];
+#pragma unroll
+  for (int s = 0; s < 32; ++s)
+    if (s < active) acc += s_w[s] * ov[s];
   float o = acc * s_inv_l;
   if (p.gate) {
     const float gt = __bfloat162float(p.gate[static_cast<size_t>(t) * p.ldq + head * HD + d]);
@@ -404,6 +400,7 @@ int attn_launch(const AttnParams& p0, int head_dim, void* ws, size_t ws_bytes, c
   DTREE_CHECK_ARG(head_dim == 64 || head_dim == 128 || head_dim == 256,
                   "tree attention supports head_dim 64, 128 or 256");
   DTREE_CHECK_ARG(p.n_nodes > 0 && p.n_nodes <= DTREE_MAX_TREE, "n_nodes out of range");
+  DTREE_CHECK_ARG(p.splits >= 1 && p.splits <= 32, "attention splits must be in [1, 32]");
   DTREE_CHECK_ARG(p.n_q_heads % p.n_kv_heads == 0, "n_q_heads must be a multiple of n_kv_heads");
   const size_t need = attn_ws_bytes(p.n_q_heads, p.n_nodes, head_dim, p.splits);
   DTREE_CHECK_ARG(ws && ws_bytes >= need, "attention workspace too small");
