@@ -97,7 +97,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsign
 __device__ __forceinline__ void tma_prefetch_desc(const void* desc) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(desc) : "memory");
 }
-// 2D tiled bulk tensor load global -> shared, completion on `bar` (no multicast)
+// 2D tiled bulk tensor load global -> shared of this CTA, completion on `bar`
 __device__ __forceinline__ void tma_load_2d(void* smem_dst, const void* desc, uint64_t* bar, int x, int y,
                                             uint64_t cache_hint) {
   asm volatile(
