@@ -74,9 +74,12 @@ def dist_init():
 
         import torch.distributed as dist
 
-        torch.cuda.set_device(local) if torch.cuda.is_available() else None
+        kw = {}
+        if torch.cuda.is_available():
+            torch.cuda.set_device(local)
+            kw["device_id"] = torch.device("cuda", local)  # explicit rank -> GPU mapping
         backend = "nccl" if torch.cuda.is_available() else "gloo"
-        dist.init_process_group(backend, timeout=datetime.timedelta(seconds=600))
+        dist.init_process_group(backend, timeout=datetime.timedelta(seconds=600), **kw)
         pg = dist
     elif torch.cuda.is_available():
         torch.cuda.set_device(local)
@@ -323,7 +326,7 @@ def run_ours(args, rank, world, local, dist) -> dict | None:
                      "peak_source": f"{peaks['source']} MEASURED_PEAKS hbm_gbs (burst)"},
         "clocks": clocks,
     }
-    if not args.no_cpu:
+    if not args.no_cpu and world == 1:  # the CPU sample is taken at N=1 only
         out["cpu_baseline"] = cpu_baseline(target, session, stream, drafter, first)
     return out
 
