@@ -12,7 +12,7 @@
 
 namespace dtree {
 
-constexpr int kTopkThreads = 256;
+constexpr int kTopkThreads = 512;
 constexpr int kMaxBudget = DTREE_MAX_TREE - 1;  // 127 nodes + root
 constexpr int kMaxRows = 64;
 constexpr int kMaxK = 128;                       // k = min(budget, vocab) <= 127
@@ -160,127 +160,149 @@ __device__ void rank_select(const float* val, const int32_t* id, int n, int k, f
   }
 }
 
-// grid (splits, rows), block 256, dynamic smem = chunk*4 + candidates
+// 64-bit selection key of (value, index): larger key = earlier in the
+// (value desc, index asc) order; unique per element
+__device__ __forceinline__ unsigned long long topk_key(float v, int idx) {
+  return (static_cast<unsigned long long>(float_order_key(v)) << 32) |
+         static_cast<unsigned long long>(0xFFFFFFFFu - static_cast<uint32_t>(idx));
+}
+__device__ __forceinline__ float topk_key_value(unsigned long long key) {
+  const uint32_t k = static_cast<uint32_t>(key >> 32);
+  return __uint_as_float((k & 0x80000000u) ? (k & 0x7FFFFFFFu) : ~k);
+}
+__device__ __forceinline__ int topk_key_index(unsigned long long key) {
+  return static_cast<int>(0xFFFFFFFFu - static_cast<uint32_t>(key & 0xFFFFFFFFull));
+}
+__device__ __forceinline__ unsigned long long block_reduce_max_u64(unsigned long long v, unsigned long long* red) {
+  for (int o = 16; o > 0; o >>= 1) {
+    const unsigned long long w = __shfl_xor_sync(0xffffffffu, v, o);
+    v = w > v ? w : v;
+  }
+  const int wp = threadIdx.x >> 5, l = threadIdx.x & 31;
+  __syncthreads();
+  if (l == 0) red[wp] = v;
+  __syncthreads();
+  unsigned long long r = (l < (blockDim.x >> 5)) ? red[l] : 0ull;
+  for (int o = 16; o > 0; o >>= 1) {
+    const unsigned long long w = __shfl_xor_sync(0xffffffffu, r, o);
+    r = w > r ? w : r;
+  }
+  return r;
+}
+
+constexpr int kTopkElems = 48;     // elements per thread (registers)
+constexpr int kTopkCandCap = 1024;  // candidates above the threshold kept in shared memory
+
+// Per-row top-k (value desc, index asc; k <= 127) of the draft logits and
+// their logsumexp (dtree_runtime.py:92-107).  grid (splits, rows), block
+// kTopkThreads; split s covers the chunk [s*chunk, (s+1)*chunk) of its row,
+// thread t the elements t + i*blockDim (coalesced), held in registers.
+//   theta = the kk-th largest of the per-thread maximum keys: at least kk
+//           elements reach theta, so every top-kk element is >= theta;
+//   the elements >= theta (few: the strided layout spreads large values over
+//           threads) are ranked in shared memory.  If more than
+//           kTopkCandCap reach theta, kk rounds of a block-wide maximum
+//           below the previous key select them instead (exact, slower).
+// The last CTA of a row merges the splits' sorted candidates and subtracts
+// the row's logsumexp, as the heap stage reads them.
 __global__ void __launch_bounds__(kTopkThreads) topk_lse_kernel(const float* __restrict__ logits, int rows,
                                                                  int vocab, int k, int splits, int chunk,
                                                                  TreeWs ws) {
   pdl_trigger();
   extern __shared__ __align__(16) unsigned char smem_raw[];
-  float* s_x = reinterpret_cast<float*>(smem_raw);                   // [chunk]
-  float* s_cv = s_x + chunk;                                          // [splits*kMaxK] merge area
+  float* s_cv = reinterpret_cast<float*>(smem_raw);                   // [splits*kMaxK] merge area (last CTA)
   int32_t* s_ci = reinterpret_cast<int32_t*>(s_cv + splits * kMaxK);  // [splits*kMaxK]
-  __shared__ uint32_t s_hist[256];
+  __shared__ unsigned long long s_tmax[kTopkThreads];
+  __shared__ unsigned long long s_cand[kTopkCandCap];
+  __shared__ unsigned long long s_kred[32];
   __shared__ float s_red[32];
-  __shared__ uint32_t s_prefix, s_mask_bits, s_remaining;
-  __shared__ int s_count_gt, s_count_eq_taken;
+  __shared__ int s_ncand;
   __shared__ bool s_last;
 
   const int r = blockIdx.y, s = blockIdx.x;
   const int c0 = s * chunk;
   const int c1 = min(vocab, c0 + chunk);
   const int n = max(0, c1 - c0);
+  const int kk = min(k, n);
   pdl_wait();
   const float* row = logits + static_cast<size_t>(r) * vocab;
+  float x[kTopkElems];
   float lmax = -INFINITY;
-  for (int i = threadIdx.x; i < n; i += blockDim.x) {
-    const float x = row[c0 + i];
-    s_x[i] = x;
-    lmax = fmaxf(lmax, x);
+#pragma unroll
+  for (int i = 0; i < kTopkElems; ++i) {
+    const int idx = c0 + threadIdx.x + i * kTopkThreads;
+    x[i] = idx < c1 ? __ldcs(row + idx) : -INFINITY;
+    lmax = fmaxf(lmax, x[i]);
   }
   const float m = block_reduce_max(lmax, s_red);
   float lsum = 0.0f;
-  for (int i = threadIdx.x; i < n; i += blockDim.x) lsum += __expf(s_x[i] - m);
+  unsigned long long tmax = 0ull;
+#pragma unroll
+  for (int i = 0; i < kTopkElems; ++i) {
+    const int idx = c0 + threadIdx.x + i * kTopkThreads;
+    if (idx < c1) {
+      lsum += __expf(x[i] - m);
+      const unsigned long long key = topk_key(x[i], idx);
+      tmax = key > tmax ? key : tmax;
+    }
+  }
   const float ssum = block_reduce_sum(lsum, s_red);
 
-  // radix select of the kk-th largest order key in the chunk (kk = min(k, n))
-  const int kk = min(k, n);
-  if (threadIdx.x == 0) {
-    s_prefix = 0;
-    s_mask_bits = 0;
-    s_remaining = static_cast<uint32_t>(kk);
-  }
-  __syncthreads();
-  for (int shift = 24; shift >= 0 && kk > 0; shift -= 8) {
-    for (int i = threadIdx.x; i < 256; i += blockDim.x) s_hist[i] = 0;
-    __syncthreads();
-    const uint32_t prefix = s_prefix, mask = s_mask_bits;
-    for (int i = threadIdx.x; i < n; i += blockDim.x) {
-      const uint32_t key = float_order_key(s_x[i]);
-      if ((key & mask) == prefix) atomicAdd(&s_hist[(key >> shift) & 0xFFu], 1u);
-    }
-    __syncthreads();
-    if (threadIdx.x == 0) {
-      uint32_t rem = s_remaining;
-      int b = 255;
-      for (; b > 0; --b) {
-        if (s_hist[b] >= rem) break;
-        rem -= s_hist[b];
-      }
-      s_prefix = prefix | (static_cast<uint32_t>(b) << shift);
-      s_mask_bits = mask | (0xFFu << shift);
-      s_remaining = rem;
-    }
-    __syncthreads();
-  }
-  // threshold key tau = s_prefix; take all keys > tau, then the smallest-index
-  // keys == tau until kk are taken
-  const uint32_t tau = s_prefix;
-  if (threadIdx.x == 0) {
-    s_count_gt = 0;
-    s_count_eq_taken = 0;
-  }
-  __syncthreads();
   float* cv = ws.cand_val + (static_cast<size_t>(r) * splits + s) * kMaxK;
   int32_t* ci = ws.cand_id + (static_cast<size_t>(r) * splits + s) * kMaxK;
   if (kk > 0) {
-    for (int i = threadIdx.x; i < n; i += blockDim.x) {
-      if (float_order_key(s_x[i]) > tau) {
-        const int slot = atomicAdd(&s_count_gt, 1);
-        s_cv[slot] = s_x[i];
-        s_ci[slot] = c0 + i;
+    // theta: the smallest of the kk largest per-thread maxima
+    s_tmax[threadIdx.x] = tmax;
+    if (threadIdx.x == 0) s_ncand = 0;
+    __syncthreads();
+    int rank = 0;
+    for (int j = 0; j < kTopkThreads; ++j) rank += s_tmax[j] > tmax ? 1 : 0;
+    const unsigned long long mine = (rank < kk && tmax != 0ull) ? ~tmax : 0ull;  // max of ~key = min key
+    const unsigned long long theta = ~block_reduce_max_u64(mine, s_kred);
+    const unsigned long long th = (theta == ~0ull) ? 0ull : theta;  // fewer than kk non-empty threads
+#pragma unroll
+    for (int i = 0; i < kTopkElems; ++i) {
+      const int idx = c0 + threadIdx.x + i * kTopkThreads;
+      if (idx < c1) {
+        const unsigned long long key = topk_key(x[i], idx);
+        if (key >= th) {
+          const int slot = atomicAdd(&s_ncand, 1);
+          if (slot < kTopkCandCap) s_cand[slot] = key;
+        }
       }
     }
     __syncthreads();
-    const int gt = s_count_gt;
-    const int need_eq = kk - gt;
-    // ties at the threshold: if all of them are needed, collect in parallel
-    // (the final sort orders them); otherwise take the smallest indices.
-    int cnt_local = 0;
-    for (int i = threadIdx.x; i < n; i += blockDim.x) cnt_local += (float_order_key(s_x[i]) == tau) ? 1 : 0;
-    const int cnt_eq = static_cast<int>(block_reduce_sum(static_cast<float>(cnt_local), s_red) + 0.5f);
-    if (cnt_eq <= need_eq) {
-      for (int i = threadIdx.x; i < n; i += blockDim.x) {
-        if (float_order_key(s_x[i]) == tau) {
-          const int slot = atomicAdd(&s_count_eq_taken, 1);
-          s_cv[gt + slot] = s_x[i];
-          s_ci[gt + slot] = c0 + i;
+    const int nc = s_ncand;
+    if (nc <= kTopkCandCap) {
+      for (int c = threadIdx.x; c < nc; c += blockDim.x) {
+        const unsigned long long key = s_cand[c];
+        int rk = 0;
+        for (int j = 0; j < nc; ++j) rk += s_cand[j] > key ? 1 : 0;
+        if (rk < kk) {
+          cv[rk] = topk_key_value(key);
+          ci[rk] = topk_key_index(key);
         }
       }
-      __syncthreads();
     } else {
-      int last = -1;
-      for (int t = 0; t < need_eq; ++t) {
-        float best = 3.0e38f;  // min index > last among ties (as float: indices < 2^24)
-        for (int i = threadIdx.x; i < n; i += blockDim.x)
-          if (i > last && float_order_key(s_x[i]) == tau) best = fminf(best, static_cast<float>(i));
-        for (int o = 16; o > 0; o >>= 1) best = fminf(best, __shfl_xor_sync(0xffffffffu, best, o));
-        __syncthreads();
-        if ((threadIdx.x & 31) == 0) s_red[threadIdx.x >> 5] = best;
-        __syncthreads();
-        float b = (threadIdx.x < (blockDim.x >> 5)) ? s_red[threadIdx.x] : 3.0e38f;
-        for (int o = 16; o > 0; o >>= 1) b = fminf(b, __shfl_xor_sync(0xffffffffu, b, o));
-        last = static_cast<int>(b);
-        if (threadIdx.x == 0) {
-          s_cv[gt + t] = s_x[last];
-          s_ci[gt + t] = c0 + last;
+      unsigned long long prev = ~0ull;
+      for (int t = 0; t < kk; ++t) {
+        unsigned long long best = 0ull;
+#pragma unroll
+        for (int i = 0; i < kTopkElems; ++i) {
+          const int idx = c0 + threadIdx.x + i * kTopkThreads;
+          if (idx < c1) {
+            const unsigned long long key = topk_key(x[i], idx);
+            if (key < prev && key > best) best = key;
+          }
         }
+        best = block_reduce_max_u64(best, s_kred);
+        if (threadIdx.x == 0) {
+          cv[t] = topk_key_value(best);
+          ci[t] = topk_key_index(best);
+        }
+        prev = best;
       }
-      if (threadIdx.x == 0) s_count_eq_taken = need_eq;
-      __syncthreads();
     }
-    const int total = gt + s_count_eq_taken;
-    // sort this chunk's candidates (value desc, id asc) into global partials
-    rank_select(s_cv, s_ci, total, kk, cv, ci);
   }
   for (int i = kk + threadIdx.x; i < k; i += blockDim.x) {  // pad short chunks
     cv[i] = -INFINITY;
@@ -340,6 +362,7 @@ struct HeapSmem {
   int active[kHeapCap];
   uint8_t path[kHeapCap][kMaxRows];  // ranks tuple (length = depth)
   uint8_t node_path[DTREE_MAX_TREE][kMaxRows];
+  uint64_t anc[DTREE_MAX_TREE][2];  // emitted nodes' ancestor masks
   int n_entries;
 };
 
@@ -366,9 +389,19 @@ __global__ void __launch_bounds__(32) heap_tree_kernel(const int32_t* __restrict
                                                         uint64_t* __restrict__ anc_mask) {
   pdl_trigger();
   __shared__ HeapSmem h;
+  // the top-k table [rows][k] in shared memory: no global round trip per pop
+  extern __shared__ __align__(16) unsigned char heap_dyn[];
+  float* s_lp = reinterpret_cast<float*>(heap_dyn);
+  int32_t* s_id = reinterpret_cast<int32_t*>(s_lp + rows * k);
   const int lane = threadIdx.x;
   pdl_wait();
   const int start = state->start;
+  for (int e = lane; e < rows * k; e += 32) {
+    s_lp[e] = top_lp[(e / k) * ld + e % k];
+    s_id[e] = top_ids[(e / k) * ld + e % k];
+  }
+  for (int i = lane; i < kHeapCap; i += 32) h.active[i] = 0;
+  __syncwarp();
   if (lane == 0) {
     tree_tokens[0] = state->root_token;
     parents[0] = -1;
@@ -376,10 +409,11 @@ __global__ void __launch_bounds__(32) heap_tree_kernel(const int32_t* __restrict
     positions[0] = start;
     anc_mask[0] = 1ull;
     anc_mask[1] = 0ull;
-    for (int i = 0; i < kHeapCap; ++i) h.active[i] = 0;
+    h.anc[0][0] = 1ull;
+    h.anc[0][1] = 0ull;
     h.n_entries = 0;
     if (budget > 0 && rows > 0 && k > 0) {
-      const double lw = static_cast<double>(top_lp[0]);
+      const double lw = static_cast<double>(s_lp[0]);
       h.neg_logw[0] = -lw;
       h.logw[0] = lw;
       h.parent[0] = 0;
@@ -393,54 +427,72 @@ __global__ void __launch_bounds__(32) heap_tree_kernel(const int32_t* __restrict
   __syncwarp();
   int n_nodes = 0;
   while (n_nodes < budget) {
-    // warp argmin over active entries
+    // warp argmin over active entries: compare -logw in registers and fall
+    // back to the full tuple order only on exact ties
     int best = -1;
+    double bnl = 0.0;
     const int ne = h.n_entries;
-    for (int e = lane; e < ne; e += 32)
-      if (h.active[e] && (best < 0 || heap_less(h, e, best))) best = e;
+    for (int e = lane; e < ne; e += 32) {
+      if (!h.active[e]) continue;
+      const double nl = h.neg_logw[e];
+      if (best < 0 || nl < bnl || (nl == bnl && heap_less(h, e, best))) {
+        best = e;
+        bnl = nl;
+      }
+    }
     for (int o = 16; o > 0; o >>= 1) {
       const int other = __shfl_xor_sync(0xffffffffu, best, o);
-      if (other >= 0 && (best < 0 || heap_less(h, other, best))) best = other;
+      const double onl = __shfl_xor_sync(0xffffffffu, bnl, o);
+      if (other >= 0 && (best < 0 || onl < bnl || (onl == bnl && heap_less(h, other, best)))) {
+        best = other;
+        bnl = onl;
+      }
     }
     if (best < 0) break;  // heap exhausted
+    // every lane reads the popped entry; lane 0 does the scalar updates and the
+    // lanes share the byte-wise ranks-tuple copies
+    const int depth = h.depth[best], rank = h.rank[best], parent = h.parent[best];
+    const double logw = h.logw[best];
+    const int cur = n_nodes + 1;
+    const bool has_sib = rank + 1 < k;
+    const bool has_child = depth < rows;
+    // the sibling reuses the popped slot; the child takes a fresh slot when a
+    // sibling exists, else the popped one (whose tuple prefix is already right)
+    const int child_slot = has_sib ? h.n_entries : best;
+    for (int i = lane; i < depth; i += 32) h.node_path[cur][i] = h.path[best][i];
+    __syncwarp();
+    if (has_child && has_sib)
+      for (int i = lane; i < depth; i += 32) h.path[child_slot][i] = h.node_path[cur][i];
     if (lane == 0) {
-      const int depth = h.depth[best], rank = h.rank[best], parent = h.parent[best];
-      const double logw = h.logw[best];
-      const int cur = n_nodes + 1;
-      tree_tokens[cur] = top_ids[(depth - 1) * ld + rank];
+      tree_tokens[cur] = s_id[(depth - 1) * k + rank];
       parents[cur] = parent;
       depths[cur] = depth;
       positions[cur] = start + depth;
-      uint64_t a0 = anc_mask[2 * parent], a1 = anc_mask[2 * parent + 1];
+      uint64_t a0 = h.anc[parent][0], a1 = h.anc[parent][1];
       if (cur < 64) a0 |= 1ull << cur; else a1 |= 1ull << (cur - 64);
+      h.anc[cur][0] = a0;
+      h.anc[cur][1] = a1;
       anc_mask[2 * cur] = a0;
       anc_mask[2 * cur + 1] = a1;
-      for (int i = 0; i < depth; ++i) h.node_path[cur][i] = h.path[best][i];
       h.active[best] = 0;
-      int slot = best;  // reuse the popped slot for the sibling
-      if (rank + 1 < k) {
-        const double sib = (logw - static_cast<double>(top_lp[(depth - 1) * ld + rank])) +
-                           static_cast<double>(top_lp[(depth - 1) * ld + rank + 1]);
-        h.neg_logw[slot] = -sib;
-        h.logw[slot] = sib;
-        h.parent[slot] = parent;
-        h.depth[slot] = depth;
-        h.rank[slot] = rank + 1;
-        for (int i = 0; i < depth - 1; ++i) h.path[slot][i] = h.path[best][i];
-        h.path[slot][depth - 1] = static_cast<uint8_t>(rank + 1);
-        h.active[slot] = 1;
-        slot = -1;
+      if (has_sib) {
+        const double sib = (logw - static_cast<double>(s_lp[(depth - 1) * k + rank])) +
+                           static_cast<double>(s_lp[(depth - 1) * k + rank + 1]);
+        h.neg_logw[best] = -sib;
+        h.logw[best] = sib;
+        h.rank[best] = rank + 1;  // parent and depth unchanged
+        h.path[best][depth - 1] = static_cast<uint8_t>(rank + 1);
+        h.active[best] = 1;
       }
-      if (depth < rows) {
-        int e = slot;
-        if (e < 0) e = h.n_entries++;
-        const double ch = logw + static_cast<double>(top_lp[depth * ld + 0]);
+      if (has_child) {
+        if (has_sib) ++h.n_entries;
+        const int e = child_slot;
+        const double ch = logw + static_cast<double>(s_lp[depth * k + 0]);
         h.neg_logw[e] = -ch;
         h.logw[e] = ch;
         h.parent[e] = cur;
         h.depth[e] = depth + 1;
         h.rank[e] = 0;
-        for (int i = 0; i < depth; ++i) h.path[e][i] = h.node_path[cur][i];
         h.path[e][depth] = 0;
         h.active[e] = 1;
       }
@@ -615,11 +667,16 @@ __global__ void step_commit_kernel(dtree_step_state* state) {
   }
 }
 
-// splits per row for the top-k scan: ~8 CTAs per row up to 148 total
+// splits per row for the top-k scan: enough that a chunk fits the registers
+// of one CTA (kTopkThreads * kTopkElems elements), at least ~8 CTAs per row
+// for large vocabularies, and a workspace within the no-allocation scratch
+// (1 MiB) for every row count the entry points accept
 static int topk_splits(int rows, int vocab) {
-  int splits = 8;
-  while (splits > 1 && (vocab + splits - 1) / splits < 2048) splits >>= 1;
-  (void)rows;
+  const int per_cta = kTopkThreads * kTopkElems;
+  int splits = (vocab + per_cta - 1) / per_cta;
+  if (splits < 8) splits = vocab >= 8 * 4096 ? 8 : (vocab + 4095) / 4096;
+  if (splits < 1) splits = 1;
+  while (splits > 1 && tree_ws_layout(rows, splits, nullptr, nullptr) > (static_cast<size_t>(1) << 20)) --splits;
   return splits;
 }
 
@@ -657,12 +714,14 @@ extern "C" int dtree_tree_build(const float* draft_logits, int rows, int vocab, 
   TreeWs ws;
   tree_ws_layout(rows, splits, &ws, static_cast<char*>(workspace));
   const int chunk = (vocab + splits - 1) / splits;
-  const size_t smem = static_cast<size_t>(chunk) * 4 + static_cast<size_t>(splits) * kMaxK * 8;
-  DTREE_CHECK_ARG(smem <= 200 * 1024, "vocab too large for the top-k chunking");
-  DTREE_CUDA_RET(ensure_smem_attr(topk_lse_kernel, 200 * 1024));
+  const size_t smem = static_cast<size_t>(splits) * kMaxK * 8;
+  DTREE_CHECK_ARG(chunk <= kTopkThreads * kTopkElems, "vocab too large for the top-k chunking");
+  DTREE_CUDA_RET(ensure_smem_attr(topk_lse_kernel, static_cast<int>(smem)));
   DTREE_CUDA_RET(launch_pdl(topk_lse_kernel, dim3(splits, rows), dim3(kTopkThreads), smem, stream, draft_logits,
                             rows, vocab, k, splits, chunk, ws));
-  DTREE_CUDA_RET(launch_pdl(heap_tree_kernel, dim3(1), dim3(32), 0, stream, (const int32_t*)ws.top_id,
+  const size_t heap_smem = static_cast<size_t>(rows) * k * 8;
+  DTREE_CUDA_RET(ensure_smem_attr(heap_tree_kernel, static_cast<int>(heap_smem)));
+  DTREE_CUDA_RET(launch_pdl(heap_tree_kernel, dim3(1), dim3(32), heap_smem, stream, (const int32_t*)ws.top_id,
                             (const float*)ws.top_lp, kMaxK, rows, k, budget, state, tree_tokens, parents, depths,
                             positions, anc_mask));
   if (top_ids) {
@@ -685,7 +744,9 @@ extern "C" int dtree_tree_from_topk(const int32_t* top_ids, const float* top_log
   DTREE_CHECK_ARG(rows >= 0 && rows <= kMaxRows, "rows must be in [0, 64]");
   DTREE_CHECK_ARG(topk >= 0 && topk <= kMaxK, "topk must be in [0, 128]");
   DTREE_CHECK_ARG((rows == 0 || topk == 0) || (top_ids && top_logprobs), "null top-k inputs");
-  DTREE_CUDA_RET(launch_pdl(heap_tree_kernel, dim3(1), dim3(32), 0, stream, top_ids, top_logprobs, topk, rows, topk,
+  const size_t heap_smem = (rows == 0 || topk == 0) ? 0 : static_cast<size_t>(rows) * topk * 8;
+  DTREE_CUDA_RET(ensure_smem_attr(heap_tree_kernel, static_cast<int>(heap_smem)));
+  DTREE_CUDA_RET(launch_pdl(heap_tree_kernel, dim3(1), dim3(32), heap_smem, stream, top_ids, top_logprobs, topk, rows, topk,
                             (rows == 0 || topk == 0) ? 0 : budget, state, tree_tokens, parents, depths, positions,
                             anc_mask));
   return kOk;
