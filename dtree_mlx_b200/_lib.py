@@ -179,6 +179,8 @@ PROTOTYPES = {
     "dtree_dflash_context": (I, [P, P, P, P, I, I, I, I, P, P]),
     "dtree_dflash_block": (I, [P, I, I, P, P, P]),
     "dtree_qwen3_forward_logits": (I, [P, P, P, P, I, P, P, P]),
+    "dtree_tree_attention_workspace_bytes": (SZ, [I, I, I, I]),
+    "dtree_tree_attention": (I, [P, I, P, P, I, I, I, I, I, P, P, P, I, P, SZ, P]),
     "dtree_lm_head_workspace_bytes": (SZ, [I]),
     "dtree_lm_head_argmax": (I, [P, I, I, I, P, I, P, P, SZ, P]),
     "dtree_qwen3_buffer_bytes": (I, [C.POINTER(Qwen3Desc), C.POINTER(C.c_size_t)]),

@@ -18,6 +18,12 @@
 // which keeps the per-thread accumulators within the register file.  The
 // combine optionally applies the Qwen3.5 output gate: out =
 // bf16(bf16(o) * bf16(sigmoid(gate))) (qwen35_tree.py:537-538).
+#include <algorithm>
+#include <cmath>
+#include <map>
+#include <mutex>
+#include <tuple>
+
 #include "attention.cuh"
 
 namespace dtree {
@@ -72,11 +78,12 @@ __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
   return *reinterpret_cast<uint32_t*>(&v);
 }
 
-// keys per split for a live key count L: at least 2 chunks, multiple of kChunk
-__device__ __forceinline__ int attn_keys_per_split(int L, int splits) {
+// keys per split for a live key count L: at least 128, a multiple of `align`
+// (64: the mma.sync kernel's chunk; 128: one tcgen05 pass)
+__device__ __forceinline__ int attn_keys_per_split(int L, int splits, int align) {
   int kps = (L + splits - 1) / splits;
   if (kps < 2 * kChunk) kps = 2 * kChunk;
-  return ((kps + kChunk - 1) / kChunk) * kChunk;
+  return ((kps + align - 1) / align) * align;
 }
 
 template <int HD, int HDV>
@@ -97,10 +104,26 @@ __global__ void __launch_bounds__(kAttnWarps * 32) tree_attn_kernel(AttnParams p
   const int T = p.n_nodes;
   const int rows_kv = G * T;
 
+  if (threadIdx.x == 0) {
+    // The cache prefix [0, start) is not written by this forward: pull this
+    // CTA's prefix keys into L2 while the upstream kernels finish.  `start`
+    // read before the dependency wait only steers this hint (never the
+    // result); the range is clamped to the cache.
+    const int P0 = p.state->start;
+    const int kps0 = attn_keys_per_split(P0 + T, p.splits, p.key_align);
+    const int lo = split * kps0;
+    const int hi = min(min(P0, lo + kps0), p.cap);
+    if (lo >= 0 && hi > lo) {
+      const size_t off = static_cast<size_t>(kvh) * p.cap * HD + static_cast<size_t>(lo) * HD;
+      const uint32_t bytes = static_cast<uint32_t>(hi - lo) * HD * 2;
+      l2_prefetch_bulk(p.k + off, bytes);
+      l2_prefetch_bulk(p.v + off, bytes);
+    }
+  }
   pdl_wait();
   const int P = p.state->start;
   const int L = P + T;
-  const int kps = attn_keys_per_split(L, p.splits);
+  const int kps = attn_keys_per_split(L, p.splits, p.key_align);
   const int k_begin = split * kps;
   if (k_begin >= L) return;  // idle split (short prefix)
   const int k_end = min(L, k_begin + kps);
@@ -315,6 +338,323 @@ __global__ void __launch_bounds__(kAttnWarps * 32) tree_attn_kernel(AttnParams p
   }
 }
 
+// ------------------------------------------------------------ tcgen05 path
+// head_dim 64 / 128.  One CTA = 128 query rows (row r -> query head
+// kvh*G + r / n_nodes, node r % n_nodes) x the split's keys, taken 128 keys
+// per pass:
+//   TMA      K, V rows [kvh*cap + k0, +128) -> smem (128-byte swizzle, two
+//            64-feature boxes when head_dim = 128)
+//   tcgen05  S[128 x 128] = Q K^T -> TMEM columns [0, 128)
+//   softmax  8 warps: warp w reads TMEM lanes 32*(w%4).. (its rows) and key
+//            half w/4 of each row; row max / sum meet in shared memory;
+//            P = bf16(p) -> smem (K-major, 128-byte swizzle)
+//   tcgen05  O[128 x HD] (+)= P V -> TMEM columns [128, 128 + HD); V is the
+//            MN-major operand straight from its TMA boxes
+// Passes after the first rescale O in TMEM by exp2(m_old - m_new).  Output
+// is the same (m, l, unnormalised O) split partial as the mma.sync kernel,
+// merged by attn_combine_kernel.
+constexpr int kTcThreads = 256;
+constexpr int kTcKeys = 128;
+constexpr uint32_t kTcBlock = 128 * 128;  // one [128 rows x 128 B] swizzled block
+
+template <int HD>
+struct TcCfg {
+  static constexpr int kNA = HD / 64;  // 64-feature blocks
+  static constexpr uint32_t kQ = 0;
+  static constexpr uint32_t kK = kQ + kNA * kTcBlock;
+  static constexpr uint32_t kV = kK + kNA * kTcBlock;
+  // P (128 rows x 128 keys = 2 blocks) reuses K's space when it is as large
+  static constexpr uint32_t kP = kNA == 2 ? kK : kV + kNA * kTcBlock;
+  static constexpr uint32_t kBar = (kNA == 2 ? kV + kNA * kTcBlock : kP + 2 * kTcBlock);
+  static constexpr uint32_t kRed = kBar + 64;  // [2 halves][128 rows] max, then sum
+  static constexpr int kSmem = 1024 + kRed + 2 * 2 * 128 * 4;
+  static constexpr uint32_t kIdescS = idesc_bf16_f32(128, kTcKeys);
+  static constexpr uint32_t kIdescO = idesc_bf16_f32(128, HD) | (1u << 16);  // B (V) MN-major
+  static constexpr uint32_t kTmemCols = 256;
+};
+
+__device__ __forceinline__ uint32_t sw128_off(int row, int chunk16) {
+  return static_cast<uint32_t>(row * 128 + ((chunk16 ^ (row & 7)) << 4));
+}
+
+template <int HD>
+__global__ void __launch_bounds__(kTcThreads) tree_attn_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
+                                                                   const __grid_constant__ CUtensorMap tmap_v,
+                                                                   AttnParams p) {
+  using C = TcCfg<HD>;
+  constexpr int NA = C::kNA;
+  constexpr int KH = kTcKeys / 2;  // keys per thread and pass
+  constexpr int OH = HD / 2;       // O columns per thread
+  pdl_trigger();
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sq = sm + C::kQ;
+  uint8_t* sk = sm + C::kK;
+  uint8_t* sv = sm + C::kV;
+  uint8_t* sp = sm + C::kP;
+  uint64_t* bar = reinterpret_cast<uint64_t*>(sm + C::kBar);  // [0] K/V landed, [1] S done, [2] O done
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 4);
+  float* red_max = reinterpret_cast<float*>(sm + C::kRed);  // [2][128]
+  float* red_sum = red_max + 2 * 128;                       // [2][128]
+
+  const int split = blockIdx.x, rb = blockIdx.y, kvh = blockIdx.z;
+  const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
+  const int r = (warp & 3) * 32 + lane;  // softmax / output row (TMEM lane)
+  const int h = warp >> 2;               // key half (S) and column half (O)
+  const int G = p.n_q_heads / p.n_kv_heads;
+  const int T = p.n_nodes;
+  const int rows_kv = G * T;
+
+  if (t == 0) {
+    // prefix keys into L2 while the upstream kernels finish (see the mma.sync
+    // kernel: `start` read before the dependency wait only steers this hint)
+    const int P0 = p.state->start;
+    const int kps0 = attn_keys_per_split(P0 + T, p.splits, p.key_align);
+    const int lo = split * kps0;
+    const int hi = min(min(P0, lo + kps0), p.cap);
+    if (lo >= 0 && hi > lo) {
+      const size_t off = static_cast<size_t>(kvh) * p.cap * HD + static_cast<size_t>(lo) * HD;
+      const uint32_t bytes = static_cast<uint32_t>(hi - lo) * HD * 2;
+      l2_prefetch_bulk(p.k + off, bytes);
+      l2_prefetch_bulk(p.v + off, bytes);
+    }
+    for (int i = 0; i < 3; ++i) mbar_init(&bar[i], 1);
+    fence_barrier_init();
+    tma_prefetch_desc(&tmap_k);
+    tma_prefetch_desc(&tmap_v);
+  }
+  if (warp == 0) {
+    tmem_alloc(tmem_slot, C::kTmemCols);
+    tmem_relinquish();
+  }
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t t_lane = static_cast<uint32_t>((warp & 3) * 32) << 16;
+
+  pdl_wait();
+  // Q (from the upstream kernel) is loaded while `start` is read; thread t
+  // stages half t/128 of row t%128
+  const int qr = t & 127, qh = t >> 7;
+  const int qrg = rb * 128 + qr;
+  const bool q_ok = qrg < rows_kv;
+  uint4 qv[HD / 16];
+  {
+    const int qg = q_ok ? qrg / T : 0, qn = q_ok ? qrg % T : 0;
+    const uint4* src = reinterpret_cast<const uint4*>(p.q + static_cast<size_t>(qn) * p.ldq + (kvh * G + qg) * HD) +
+                       qh * (HD / 16);
+#pragma unroll
+    for (int c = 0; c < HD / 16; ++c) qv[c] = q_ok ? __ldg(src + c) : make_uint4(0, 0, 0, 0);
+  }
+  const int rg = rb * 128 + r;
+  const bool row_ok = rg < rows_kv;
+  const int g = row_ok ? rg / T : 0, node = row_ok ? rg % T : 0;
+  const uint64_t anc0 = row_ok ? p.anc[2 * node] : 0ull;
+  const uint64_t anc1 = row_ok ? p.anc[2 * node + 1] : 0ull;
+  const int P = p.state->start;
+  const int L = P + T;
+  const int kps = attn_keys_per_split(L, p.splits, p.key_align);
+  const int k_begin = split * kps;
+  const int k_end = min(L, k_begin + kps);
+  const int n_pass = k_begin < k_end ? (k_end - k_begin + kTcKeys - 1) / kTcKeys : 0;
+
+  auto issue_kv = [&](int k0) {
+    const uint64_t pol = l2_policy_evict_first();
+    mbar_arrive_expect_tx(&bar[0], 2u * NA * kTcBlock);
+    const int y = kvh * p.cap + k0;
+#pragma unroll
+    for (int a = 0; a < NA; ++a) {
+      tma_load_2d(sk + a * kTcBlock, &tmap_k, &bar[0], a * 64, y, pol);
+      tma_load_2d(sv + a * kTcBlock, &tmap_v, &bar[0], a * 64, y, pol);
+    }
+  };
+  if (t == 0 && n_pass > 0) issue_kv(k_begin);
+  if (n_pass > 0) {
+#pragma unroll
+    for (int c = 0; c < HD / 16; ++c) {
+      const int cc = qh * (HD / 16) + c;  // 16-byte chunk of the row
+      *reinterpret_cast<uint4*>(sq + (cc >> 3) * kTcBlock + sw128_off(qr, cc & 7)) = qv[c];
+    }
+    fence_proxy_async_smem();
+  }
+
+  float m_run = -INFINITY, l_run = 0.0f;
+  bool ok = true;
+  int fail_bar = 0;
+  uint32_t ph = 0;
+  for (int j = 0; j < n_pass && ok; ++j, ph ^= 1u) {
+    const int k0 = k_begin + j * kTcKeys;
+    if (t == 0 && j > 0) issue_kv(k0);
+    ok = mbar_wait(&bar[0], ph, 0x31);
+    // V rows past the live keys may hold anything (NaN included): zero them so
+    // that P = 0 there contributes exactly 0
+    if (ok && qh < NA && k0 + qr >= k_end) {
+      uint4* row = reinterpret_cast<uint4*>(sv + qh * kTcBlock + qr * 128);
+#pragma unroll
+      for (int c = 0; c < 8; ++c) row[c] = make_uint4(0, 0, 0, 0);
+    }
+    fence_proxy_async_smem();
+    // every wait's outcome is made CTA-uniform so all threads take the same path
+    if (!__syncthreads_and(ok)) {
+      ok = false;
+      fail_bar = 0;
+      break;
+    }
+    if (t == 0) {
+      tc_fence_after();
+#pragma unroll
+      for (int s = 0; s < HD / 16; ++s) {
+        const uint32_t off = (s >> 2) * kTcBlock + (s & 3) * 32;
+        umma_bf16(tmem, sw128_kmajor_desc(smem_u32(sq) + off), sw128_kmajor_desc(smem_u32(sk) + off), C::kIdescS,
+                  s > 0 ? 1u : 0u);
+      }
+      umma_commit(&bar[1]);
+    }
+    if (!__syncthreads_and(mbar_wait(&bar[1], ph, 0x32))) {
+      ok = false;
+      fail_bar = 1;
+      break;
+    }
+    tc_fence_after();
+
+    // ---- softmax: row r, keys k0 + h*64 .. +63 of this pass
+    float x[KH];
+#pragma unroll
+    for (int c = 0; c < KH / 32; ++c) {
+      uint32_t v[32];
+      tmem_ld_x32(tmem + t_lane + h * KH + c * 32, v);
+#pragma unroll
+      for (int i = 0; i < 32; ++i) x[c * 32 + i] = __uint_as_float(v[i]);
+    }
+    tmem_wait_ld();
+    // visibility of keys kb + i (i < 64) as one bitmask: prefix keys, then
+    // the tree slots' ancestor bits, cut at the split's end
+    const int kb = k0 + h * KH;
+    uint64_t vis = 0ull;
+    if (row_ok) {
+      const int np = P - kb;  // prefix keys among the 64
+      const uint64_t pre = np >= 64 ? ~0ull : (np <= 0 ? 0ull : (1ull << np) - 1ull);
+      uint64_t tree = 0ull;
+      if (np < 64) {
+        const int sh = -np;  // tree slot of key kb (negative: slot 0 sits at bit np)
+        if (sh >= 128) tree = 0ull;
+        else if (sh >= 64) tree = anc1 >> (sh - 64);
+        else if (sh > 0) tree = (anc0 >> sh) | (anc1 << (64 - sh));
+        else if (sh == 0) tree = anc0;
+        else tree = anc0 << np;  // np in (0, 64)
+      }
+      const int ne = k_end - kb;  // live keys among the 64
+      const uint64_t live = ne >= 64 ? ~0ull : (ne <= 0 ? 0ull : (1ull << ne) - 1ull);
+      vis = (pre | (tree & ~pre)) & live;
+    }
+    float mx = -INFINITY;
+#pragma unroll
+    for (int i = 0; i < KH; ++i) {
+      x[i] = ((vis >> i) & 1ull) ? x[i] * p.scale_log2 : -INFINITY;
+      mx = fmaxf(mx, x[i]);
+    }
+    red_max[h * 128 + r] = mx;
+    __syncthreads();
+    const float m_new = fmaxf(m_run, fmaxf(red_max[r], red_max[128 + r]));
+    const float m_use = (m_new == -INFINITY) ? 0.0f : m_new;
+    const float alpha = exp2f(m_run - m_use);
+    float rs = 0.0f;
+#pragma unroll
+    for (int c = 0; c < KH / 8; ++c) {
+      uint4 pk;
+      uint32_t* pw = reinterpret_cast<uint32_t*>(&pk);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float p0 = exp2f(x[c * 8 + 2 * i] - m_use), p1 = exp2f(x[c * 8 + 2 * i + 1] - m_use);
+        rs += p0 + p1;
+        pw[i] = pack_bf16(p0, p1);
+      }
+      *reinterpret_cast<uint4*>(sp + h * kTcBlock + sw128_off(r, c)) = pk;
+    }
+    red_sum[h * 128 + r] = rs;
+    if (j > 0) {  // rescale this thread's half of the running O of row r
+#pragma unroll 1
+      for (int c = 0; c < OH / 32; ++c) {
+        uint32_t v[32];
+        tmem_ld_x32(tmem + t_lane + kTcKeys + h * OH + c * 32, v);
+        tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] = __float_as_uint(__uint_as_float(v[i]) * alpha);
+        tmem_st_x32(tmem + t_lane + kTcKeys + h * OH + c * 32, v);
+      }
+      tmem_wait_st();
+    }
+    fence_proxy_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    l_run = l_run * alpha + (red_sum[r] + red_sum[128 + r]);
+    m_run = m_new;
+    if (t == 0) {
+      tc_fence_after();
+#pragma unroll
+      for (int s = 0; s < kTcKeys / 16; ++s) {
+        const uint32_t a_off = (s >> 2) * kTcBlock + (s & 3) * 32;
+        umma_bf16(tmem + kTcKeys, sw128_kmajor_desc(smem_u32(sp) + a_off),
+                  sw128_mnmajor_desc(smem_u32(sv) + s * 2048, kTcBlock, 1024), C::kIdescO,
+                  (j > 0 || s > 0) ? 1u : 0u);
+      }
+      umma_commit(&bar[2]);
+    }
+    ok = __syncthreads_and(mbar_wait(&bar[2], ph, 0x33)) != 0;
+    if (!ok) {
+      fail_bar = 2;
+      break;
+    }
+    tc_fence_after();
+  }
+  if (!ok && t == 0) mbar_wait(&bar[fail_bar], ph, 0x34);  // let the async op in flight land
+
+  // ---- split partials (unnormalised O, m, l).  Each warp stages its 32 rows x
+  // OH columns in the (now idle) Q/K/V space, then writes whole row segments.
+  if (ok && n_pass > 0) {
+    constexpr int LDS = OH + 4;  // padded row (floats): conflict-free 16-byte stores
+    static_assert(8 * 32 * LDS * 4 <= C::kBar, "staging exceeds the operand space");
+    float* stage = reinterpret_cast<float*>(sq) + warp * 32 * LDS;
+#pragma unroll 1
+    for (int c = 0; c < OH / 32; ++c) {
+      uint32_t v[32];
+      tmem_ld_x32(tmem + t_lane + kTcKeys + h * OH + c * 32, v);
+      tmem_wait_ld();
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        *reinterpret_cast<float4*>(stage + lane * LDS + c * 32 + 4 * i) =
+            make_float4(__uint_as_float(v[4 * i]), __uint_as_float(v[4 * i + 1]), __uint_as_float(v[4 * i + 2]),
+                        __uint_as_float(v[4 * i + 3]));
+    }
+    const int rows_total = p.n_q_heads * T;
+    if (row_ok && h == 0) {
+      const int qrow = (kvh * G + g) * T + node;  // [head][node]
+      float* pml = p.part_ml + (static_cast<size_t>(split) * rows_total + qrow) * 2;
+      pml[0] = m_run;
+      pml[1] = l_run;
+    }
+    __syncwarp();
+    constexpr int VPR = OH / 4;       // float4 per staged row
+    constexpr int RPI = 32 / VPR;     // rows per warp instruction
+    const int sub = lane / VPR, vi = lane % VPR;
+#pragma unroll 4
+    for (int rr = sub; rr < 32; rr += RPI) {
+      const int rg2 = rb * 128 + (warp & 3) * 32 + rr;
+      if (rg2 < rows_kv) {
+        const int qrow = (kvh * G + rg2 / T) * T + rg2 % T;
+        float4* dst = reinterpret_cast<float4*>(p.part_o + (static_cast<size_t>(split) * rows_total + qrow) * HD + h * OH);
+        dst[vi] = *reinterpret_cast<const float4*>(stage + rr * LDS + vi * 4);
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem, C::kTmemCols);
+  }
+}
+
 // grid = n_q_heads * n_nodes rows, block = HD threads.  The per-split (m, l)
 // are loaded by one thread each, the O partials with several splits in flight.
 template <int HD>
@@ -329,7 +669,7 @@ __global__ void attn_combine_kernel(AttnParams p) {
   pdl_wait();
   const int P = p.state->start;
   const int L = P + T;
-  const int kps = attn_keys_per_split(L, p.splits);
+  const int kps = attn_keys_per_split(L, p.splits, p.key_align);
   const int active = min(p.splits, (L + kps - 1) / kps);
   const int rows_total = p.n_q_heads * T;
   // this thread's O partials of every split: loaded before the weights are
@@ -395,6 +735,44 @@ static int attn_launch_t(const AttnParams& p, int rb, cudaStream_t stream) {
   return kOk;
 }
 
+// K / V plane tensor maps ([n_kv_heads * cap] rows x HD, boxes of 64 features
+// x 128 keys), encoded once per (plane, rows, HD)
+static int plane_tmap(CUtensorMap* out, const void* plane, int rows, int hd) {
+  static std::mutex mu;
+  static std::map<std::tuple<const void*, int, int>, CUtensorMap> cache;
+  std::lock_guard<std::mutex> lock(mu);
+  const auto key = std::make_tuple(plane, rows, hd);
+  auto it = cache.find(key);
+  if (it != cache.end()) {
+    *out = it->second;
+    return kOk;
+  }
+  if (cache.size() > 4096) cache.clear();
+  CUtensorMap m;
+  int rc = make_tmap_2d_bf16(&m, plane, static_cast<uint64_t>(hd), static_cast<uint64_t>(rows),
+                             static_cast<uint64_t>(hd) * 2, 64, kTcKeys, true);
+  if (rc) return rc;
+  cache.emplace(key, m);
+  *out = m;
+  return kOk;
+}
+
+template <int HD>
+static int attn_launch_tc(const AttnParams& p, int rb, cudaStream_t stream) {
+  using C = TcCfg<HD>;
+  CUtensorMap tk, tv;
+  const int rows = p.n_kv_heads * p.cap;
+  int rc = plane_tmap(&tk, p.k, rows, HD);
+  if (rc) return rc;
+  if ((rc = plane_tmap(&tv, p.v, rows, HD))) return rc;
+  auto kern = tree_attn_tc_kernel<HD>;
+  DTREE_CUDA_RET(ensure_smem_attr(kern, C::kSmem));
+  DTREE_CUDA_RET(launch_pdl(kern, dim3(p.splits, rb, p.n_kv_heads), dim3(kTcThreads), static_cast<size_t>(C::kSmem),
+                            stream, tk, tv, p));
+  DTREE_CUDA_RET(launch_pdl(attn_combine_kernel<HD>, dim3(p.n_q_heads * p.n_nodes), dim3(HD), 0, stream, p));
+  return kOk;
+}
+
 int attn_launch(const AttnParams& p0, int head_dim, void* ws, size_t ws_bytes, cudaStream_t stream) {
   AttnParams p = p0;
   DTREE_CHECK_ARG(head_dim == 64 || head_dim == 128 || head_dim == 256,
@@ -410,9 +788,52 @@ int attn_launch(const AttnParams& p0, int head_dim, void* ws, size_t ws_bytes, c
                                        ((static_cast<size_t>(p.splits) * rows * head_dim * 4 + 255) & ~static_cast<size_t>(255)));
   const int G = p.n_q_heads / p.n_kv_heads;
   const int rb = (G * p.n_nodes + kAttnRows - 1) / kAttnRows;
-  if (head_dim == 256) return attn_launch_t<256, 128>(p, rb, stream);
-  if (head_dim == 128) return attn_launch_t<128, 128>(p, rb, stream);
-  return attn_launch_t<64, 64>(p, rb, stream);
+  if (head_dim == 256) {
+    p.key_align = kChunk;
+    return attn_launch_t<256, 128>(p, rb, stream);
+  }
+  p.key_align = kTcKeys;
+  if (head_dim == 128) return attn_launch_tc<128>(p, rb, stream);
+  return attn_launch_tc<64>(p, rb, stream);
 }
 
 }  // namespace dtree
+
+using namespace dtree;
+
+// Standalone tree attention (the attention step of qwen3_tree.py:67-76:
+// softmax(q k^T * scale + tree mask) v over the cache prefix and the tree's
+// own slots): q [n_nodes][ldq] bf16 (post q-norm / RoPE), K / V planes
+// [n_kv_heads][kv_cap][head_dim] bf16 with the tree keys already at slots
+// start..start+n_nodes-1, anc_mask [n_nodes][2]; out [n_nodes][ldq] bf16.
+extern "C" size_t dtree_tree_attention_workspace_bytes(int n_q_heads, int n_nodes, int head_dim, int splits) {
+  if (n_q_heads <= 0 || n_nodes <= 0 || head_dim <= 0) return 0;
+  if (splits <= 0) splits = 32;
+  return attn_ws_bytes(n_q_heads, n_nodes, head_dim, splits);
+}
+
+extern "C" int dtree_tree_attention(const void* q, int ldq, const void* k_plane, const void* v_plane, int kv_cap,
+                                    int n_q_heads, int n_kv_heads, int head_dim, int n_nodes,
+                                    const dtree_step_state* state, const uint64_t* anc_mask, void* out, int splits,
+                                    void* workspace, size_t workspace_bytes, void* stream) {
+  DTREE_CHECK_ARG(q && k_plane && v_plane && state && anc_mask && out, "null pointer");
+  DTREE_CHECK_ARG(n_q_heads > 0 && n_kv_heads > 0, "head counts must be positive");
+  DTREE_CHECK_ARG(ldq >= n_q_heads * head_dim && ldq % 8 == 0, "ldq must be >= n_q_heads * head_dim, multiple of 8");
+  DTREE_CHECK_ARG(kv_cap > 0, "kv_cap must be positive");
+  AttnParams p{};
+  p.q = static_cast<const __nv_bfloat16*>(q);
+  p.ldq = ldq;
+  p.k = static_cast<const __nv_bfloat16*>(k_plane);
+  p.v = static_cast<const __nv_bfloat16*>(v_plane);
+  p.cap = kv_cap;
+  p.n_q_heads = n_q_heads;
+  p.n_kv_heads = n_kv_heads;
+  p.n_nodes = n_nodes;
+  p.state = state;
+  p.anc = anc_mask;
+  p.scale_log2 = static_cast<float>(1.4426950408889634 / std::sqrt(static_cast<double>(head_dim)));
+  p.splits = splits > 0 ? splits : std::min(32, attn_default_splits(n_kv_heads, n_q_heads, n_nodes));
+  p.out = static_cast<__nv_bfloat16*>(out);
+  return attn_launch(p, head_dim, workspace, workspace_bytes, static_cast<cudaStream_t>(stream));
+}
+

@@ -23,6 +23,7 @@ struct AttnParams {
   __nv_bfloat16* out;   // [t_pad][n_q_heads*hd]
   int causal_prefix;    // unused (0): tree mask only
   const __nv_bfloat16* gate;  // [t_pad][n_q_heads*hd] output gate (nullable)
+  int key_align;        // keys per split are a multiple of this (set by attn_launch)
 };
 
 size_t attn_ws_bytes(int n_q_heads, int t_pad, int head_dim, int splits);

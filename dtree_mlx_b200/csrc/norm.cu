@@ -98,41 +98,44 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(const __nv_bfloat16* __res
 //   h[row] = bf16(h[row] + y)                      (qwen3_tree.py:78,82 residual adds)
 //   capture[row] = h[row]            (optional: verifier_hidden of this layer)
 //   xn[row] = RMSNorm(h[row], w)
-// grid = t_pad rows, block 256; H <= 4096 (two 8-wide vectors per thread).
-__global__ void __launch_bounds__(256) residual_rmsnorm_kernel(__nv_bfloat16* __restrict__ h,
-                                                               const float* __restrict__ partials, int n_split,
-                                                               int part_rows, __nv_bfloat16* __restrict__ capture,
-                                                               int ldc, const __nv_bfloat16* __restrict__ w,
-                                                               __nv_bfloat16* __restrict__ xn, int H, int n_rows,
-                                                               float eps) {
+// A row is spread over a cluster of kNormCluster CTAs (grid (kNormCluster,
+// t_pad)), one 8-wide column vector per thread, so every load of the row is
+// in flight at once; the CTAs' sums of squares meet through distributed
+// shared memory (summed in CTA-rank order: deterministic).  H <= 4096.
+constexpr int kNormCluster = 4;
+constexpr int kNormThreads = 128;
+
+__global__ void __launch_bounds__(kNormThreads) residual_rmsnorm_kernel(
+    __nv_bfloat16* __restrict__ h, const float* __restrict__ partials, int n_split, int part_rows,
+    __nv_bfloat16* __restrict__ capture, int ldc, const __nv_bfloat16* __restrict__ w,
+    __nv_bfloat16* __restrict__ xn, int H, int n_rows, float eps) {
   pdl_trigger();
-  __shared__ float red[8];
-  const int row = blockIdx.x;
+  __shared__ float red[kNormThreads / 32];
+  __shared__ float s_ss;  // this CTA's share of the row's sum of squares
+  const int rank = blockIdx.x, row = blockIdx.y;
   const int nv = H / 8;
+  const int per = (nv + kNormCluster - 1) / kNormCluster;
+  const int i = rank * per + threadIdx.x;
+  const bool act = threadIdx.x < per && i < nv;
   pdl_wait();
   uint4* xrow = reinterpret_cast<uint4*>(xn + static_cast<size_t>(row) * H);
   uint4* hrow = reinterpret_cast<uint4*>(h + static_cast<size_t>(row) * H);
-  if (row >= n_rows) {
-    const uint4 z = make_uint4(0, 0, 0, 0);
-    for (int i = threadIdx.x; i < nv; i += blockDim.x) {
-      xrow[i] = z;
-      hrow[i] = z;
+  if (row >= n_rows) {  // uniform over the cluster: no cluster barrier is entered
+    if (act) {
+      xrow[i] = make_uint4(0, 0, 0, 0);
+      hrow[i] = make_uint4(0, 0, 0, 0);
     }
     return;
   }
-  constexpr int kCache = 2;
-  uint4 hc[kCache];
   float ss = 0.0f;
-#pragma unroll
-  for (int j = 0; j < kCache; ++j) {
-    const int i = threadIdx.x + j * blockDim.x;
-    if (i >= nv) continue;
+  uint4 o = make_uint4(0, 0, 0, 0);
+  if (act) {
     float y[8];
 #pragma unroll
     for (int e = 0; e < 8; ++e) y[e] = 0.0f;
     const uint4 hv = hrow[i];
-    // all splits' loads of a batch are in flight together (one L2 round
-    // trip per 8 splits); the sum still runs in split order
+    // all splits' loads of a batch are in flight together; the sum still
+    // runs in split order
     for (int s0 = 0; s0 < n_split; s0 += 8) {
       float4 a[8], b[8];
 #pragma unroll
@@ -153,7 +156,6 @@ __global__ void __launch_bounds__(256) residual_rmsnorm_kernel(__nv_bfloat16* __
       }
     }
     const __nv_bfloat162* hb = reinterpret_cast<const __nv_bfloat162*>(&hv);
-    uint4 o;
     __nv_bfloat162* ob = reinterpret_cast<__nv_bfloat162*>(&o);
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
@@ -162,23 +164,26 @@ __global__ void __launch_bounds__(256) residual_rmsnorm_kernel(__nv_bfloat16* __
       const float2 g = __bfloat1622float2(ob[q]);
       ss += g.x * g.x + g.y * g.y;
     }
-    hc[j] = o;
     hrow[i] = o;
     if (capture) reinterpret_cast<uint4*>(capture + static_cast<size_t>(row) * ldc)[i] = o;
   }
-  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
   if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
   __syncthreads();
+  if (threadIdx.x == 0) {
+    float t = 0.0f;
+    for (int k = 0; k < kNormThreads / 32; ++k) t += red[k];
+    s_ss = t;
+  }
+  cluster_arrive();  // s_ss of every CTA is published
+  cluster_wait();
   float tot = 0.0f;
-  for (int i = 0; i < (blockDim.x >> 5); ++i) tot += red[i];
+  for (int r = 0; r < kNormCluster; ++r) tot += ld_dsmem_f32(&s_ss, static_cast<uint32_t>(r));
+  cluster_arrive();  // done reading the other CTAs' shared memory
   const float rs = rsqrtf(tot / static_cast<float>(H) + eps);
-  const uint4* w4 = reinterpret_cast<const uint4*>(w);
-#pragma unroll
-  for (int j = 0; j < kCache; ++j) {
-    const int i = threadIdx.x + j * blockDim.x;
-    if (i >= nv) continue;
-    const uint4 wv = w4[i];
-    const __nv_bfloat162* b = reinterpret_cast<const __nv_bfloat162*>(&hc[j]);
+  if (act) {
+    const uint4 wv = reinterpret_cast<const uint4*>(w)[i];
+    const __nv_bfloat162* b = reinterpret_cast<const __nv_bfloat162*>(&o);
     const __nv_bfloat162* wb = reinterpret_cast<const __nv_bfloat162*>(&wv);
     uint4 o4;
     __nv_bfloat162* ob = reinterpret_cast<__nv_bfloat162*>(&o4);
@@ -190,14 +195,16 @@ __global__ void __launch_bounds__(256) residual_rmsnorm_kernel(__nv_bfloat16* __
     }
     xrow[i] = o4;
   }
+  cluster_wait();  // no CTA leaves while another may still read its s_ss
 }
 
 int residual_rmsnorm_launch(__nv_bfloat16* h, const float* partials, int n_split, int part_rows,
                             __nv_bfloat16* capture, int ldc, const __nv_bfloat16* w, __nv_bfloat16* xn, int H,
                             int n_rows, int t_pad, float eps, cudaStream_t stream) {
-  DTREE_CHECK_ARG(H % 8 == 0 && H <= 4096, "hidden size must be a multiple of 8 and <= 4096");
-  DTREE_CUDA_RET(launch_pdl(residual_rmsnorm_kernel, dim3(t_pad), dim3(256), 0, stream, h, partials, n_split,
-                            part_rows, capture, ldc, w, xn, H, n_rows, eps));
+  DTREE_CHECK_ARG(H % 8 == 0 && H / 8 <= kNormCluster * kNormThreads, "hidden size must be a multiple of 8 and <= 4096");
+  DTREE_CUDA_RET(launch_pdl_cluster(residual_rmsnorm_kernel, dim3(kNormCluster, t_pad), dim3(kNormThreads), 0, stream,
+                                    kNormCluster, h, partials, n_split, part_rows, capture, ldc, w, xn, H, n_rows,
+                                    eps));
   return kOk;
 }
 

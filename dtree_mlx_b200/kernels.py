@@ -206,6 +206,25 @@ def lm_head_argmax(h: torch.Tensor, embed: torch.Tensor, n_rows: int, out: torch
     return out
 
 
+def tree_attention(q: torch.Tensor, k_plane: torch.Tensor, v_plane: torch.Tensor, state: torch.Tensor,
+                   anc: torch.Tensor, n_nodes: int, n_q_heads: int, splits: int = 0,
+                   out: torch.Tensor | None = None) -> torch.Tensor:
+    """Tree-masked attention of n_nodes query rows q [n_nodes, n_q_heads*hd]
+    against K/V planes [n_kv_heads, kv_cap, hd] (prefix [0, start) plus the
+    tree slots start..start+n_nodes-1), ancestor masks anc [n_nodes, 2]."""
+    _cuda(q, "q", torch.bfloat16)
+    _cuda(k_plane, "k_plane", torch.bfloat16)
+    _cuda(v_plane, "v_plane", torch.bfloat16)
+    n_kv_heads, kv_cap, hd = k_plane.shape
+    if out is None:
+        out = torch.empty(n_nodes, n_q_heads * hd, dtype=torch.bfloat16, device=q.device)
+    nbytes = int(_lib.load().dtree_tree_attention_workspace_bytes(n_q_heads, n_nodes, hd, splits))
+    ws = _workspace(("attn", n_q_heads, n_nodes, hd, splits), nbytes, q.device)
+    call("dtree_tree_attention", ptr(q), q.stride(0), ptr(k_plane), ptr(v_plane), kv_cap, n_q_heads, n_kv_heads, hd,
+         n_nodes, ptr(state), ptr(anc), ptr(out), splits, ptr(ws), ws.numel(), stream_ptr())
+    return out
+
+
 # ------------------------------------------------- Qwen3.5 DeltaNet kernels
 _DT = {torch.float32: 0, torch.bfloat16: 1}
 

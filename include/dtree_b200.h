@@ -193,6 +193,22 @@ DTREE_API size_t dtree_lm_head_workspace_bytes(int t_pad);
 DTREE_API int dtree_lm_head_argmax(const void* h, int t_pad, int n_rows, int hidden, const void* embed, int vocab,
                          int32_t* out, void* workspace, size_t workspace_bytes, void* stream);
 
+/* ----------------------------------------------------- tree attention
+ * softmax(q k^T / sqrt(head_dim) + tree mask) v for the tree rows of one
+ * verify forward (replaces the masked scaled_dot_product_attention call of
+ * dtree_mlx/qwen3_tree.py:67-76 with the ancestor mask of
+ * dtree_mlx/dtree_runtime.py:190-191).  q: [n_nodes][ldq] bf16 (after q-norm
+ * and RoPE); k_plane / v_plane: [n_kv_heads][kv_cap][head_dim] bf16 holding
+ * the prefix [0, state->start) and the tree keys at slots start..start+n-1;
+ * anc_mask: [n_nodes][2] (bit j of node t: tree slot j visible); out:
+ * [n_nodes][ldq] bf16.  head_dim 64, 128 (tcgen05) or 256; splits <= 32
+ * (0: one CTA per SM). */
+DTREE_API size_t dtree_tree_attention_workspace_bytes(int n_q_heads, int n_nodes, int head_dim, int splits);
+DTREE_API int dtree_tree_attention(const void* q, int ldq, const void* k_plane, const void* v_plane, int kv_cap,
+                                   int n_q_heads, int n_kv_heads, int head_dim, int n_nodes,
+                                   const dtree_step_state* state, const uint64_t* anc_mask, void* out, int splits,
+                                   void* workspace, size_t workspace_bytes, void* stream);
+
 /* ------------------------------------- Qwen3.5 gated-DeltaNet tree kernels
  * dtype / state_dtype: 0 = f32, 1 = bf16 (the reference's InT / StT).
  * parents[t] < t for t > 0, parents[0] = -1 (the base state).

@@ -1,0 +1,80 @@
+"""Tree attention (dtree_tree_attention) against a plain PyTorch fp32 reference.
+
+The reference is the masked scaled_dot_product_attention of
+dtree_mlx/qwen3_tree.py:67-76 with the ancestor mask of
+dtree_mlx/dtree_runtime.py:190-191: every prefix key is visible, tree slot j
+is visible to node t iff j is t or one of its ancestors.  Cache rows past the
+live keys are filled with NaN: they must not reach the output.
+Tolerance: max |out - ref| <= 2e-2 (bf16 probabilities and bf16 output).
+"""
+import math
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _random_tree(n: int, gen: torch.Generator) -> tuple[list[int], torch.Tensor]:
+    """Random parents (node i > 0 under a uniform earlier node): ancestor
+    masks as Python ints and as the [n, 2] int64 words the kernels read."""
+    parents = [-1] + [int(torch.randint(0, i, (1,), generator=gen)) for i in range(1, n)]
+    masks = []
+    for i in range(n):
+        m = 1 << i
+        p = parents[i]
+        while p >= 0:
+            m |= 1 << p
+            p = parents[p]
+        masks.append(m)
+    words = []
+    for m in masks:
+        lo, hi = m & ((1 << 64) - 1), m >> 64
+        words.append([lo - (1 << 64) if lo >= 1 << 63 else lo, hi - (1 << 64) if hi >= 1 << 63 else hi])
+    return masks, torch.tensor(words, dtype=torch.int64)
+
+
+def _reference(q, k_plane, v_plane, start, n, masks, n_q_heads):
+    n_kv, _, hd = k_plane.shape
+    group = n_q_heads // n_kv
+    L = start + n
+    k = k_plane[:, :L].float()
+    v = v_plane[:, :L].float()
+    vis = torch.ones(n, L, dtype=torch.bool, device=q.device)
+    for t in range(n):
+        m = masks[t]
+        for j in range(n):
+            vis[t, start + j] = bool((m >> j) & 1)
+    qf = q.float().view(n, n_q_heads, hd)
+    out = torch.empty(n, n_q_heads, hd, device=q.device)
+    for h in range(n_q_heads):
+        s = qf[:, h] @ k[h // group].T / math.sqrt(hd)
+        s = s.masked_fill(~vis, float("-inf"))
+        out[:, h] = torch.softmax(s, dim=-1) @ v[h // group]
+    return out.view(n, n_q_heads * hd)
+
+
+@pytest.mark.parametrize("heads", [(32, 8, 128), (8, 4, 64), (16, 4, 256)])
+@pytest.mark.parametrize("start,n,splits", [(0, 1, 0), (5, 25, 0), (200, 64, 0), (2048, 25, 0), (3000, 25, 0),
+                                            (2048, 25, 3), (777, 7, 0)])
+def test_tree_attention_matches_fp32(lib, heads, start, n, splits):
+    from dtree_mlx_b200 import kernels
+
+    n_q, n_kv, hd = heads
+    dev = torch.device("cuda")
+    gen = torch.Generator().manual_seed(start * 131 + n * 7 + hd + splits)
+    cap = start + n + 300
+    k_plane = torch.randn(n_kv, cap, hd, generator=gen).to(torch.bfloat16)
+    v_plane = torch.randn(n_kv, cap, hd, generator=gen).to(torch.bfloat16)
+    k_plane[:, start + n:] = float("nan")
+    v_plane[:, start + n:] = float("nan")
+    q = torch.randn(n, n_q * hd, generator=gen).to(torch.bfloat16)
+    masks, anc = _random_tree(n, gen)
+    k_plane, v_plane, q, anc = k_plane.to(dev), v_plane.to(dev), q.to(dev), anc.to(dev)
+    state = kernels.new_state(dev, start=start)
+    out = kernels.tree_attention(q, k_plane, v_plane, state, anc, n, n_q, splits=splits)
+    ref = _reference(q, k_plane, v_plane, start, n, masks, n_q)
+    torch.cuda.synchronize()
+    assert torch.isfinite(out.float()).all()
+    err = (out.float() - ref).abs().max().item()
+    assert err <= 2e-2, f"max abs err {err}"
