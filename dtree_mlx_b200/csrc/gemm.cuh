@@ -77,7 +77,13 @@ struct GemmParams {
 };
 
 constexpr int kGemmThreads = 192;
-constexpr int kGemmThreadsQ4 = 192 + 256;  // + 8 dequant warps
+constexpr int kDeqWarps = 8;                             // q4 dequant warps
+constexpr int kQ4BudgetKB = 150;                         // q4 CTA shared memory (one CTA per SM)
+constexpr int kDeqGroups = 2;                            // units dequantized concurrently
+constexpr int kDeqGroupWarps = kDeqWarps / kDeqGroups;
+constexpr int kGemmThreadsQ4 = 192 + kDeqWarps * 32;
+constexpr int kDeqTpr = kDeqGroupWarps * 32 / 128;       // threads per tile row (within a group)
+constexpr int kDeqWpt = 8 / kDeqTpr;                     // packed words (8 weights) per thread
 constexpr int kWTileBytes = 128 * 64 * 2;
 constexpr int kPkTileBytes = 128 * 64 / 2;  // packed 4-bit tile
 
@@ -88,7 +94,8 @@ struct GemmCfg {
   static constexpr int kStageBytes = (Q4 ? kPkTileBytes : kWTileBytes) + kXBytes;
   static constexpr int kXOff = Q4 ? 0 : kWTileBytes;
   static constexpr int kWOff = Q4 ? kXBytes : 0;
-  static constexpr int kDeq = Q4 ? 3 : 0;  // dequantized bf16 W buffers (16 KB each)
+  // dequantized bf16 W buffers: 2 per group (1 from TPAD 64), at most the stage count
+  static constexpr int kDeq = Q4 ? kDeqGroups * (TPAD >= 64 ? 1 : 2) : 0;  // dequantized bf16 W buffers (16 KB each)
   static constexpr int kBarBytes = Q4 ? 512 : 256;
   static constexpr int kXchBytes = (EPI == kEpiQkv || EPI == kEpiSwiglu) ? 128 * 8 * 4 : 0;
   // [0,256): per-warp reductions of one 8-row chunk; then s_best / s_pos
@@ -98,11 +105,16 @@ struct GemmCfg {
   // (launched early by PDL) can be resident and prefetch its weights
   // (q4 stages are a quarter as large; a deeper ring keeps enough packed
   // bytes in flight)
-  static constexpr int kBudget = (Q4 ? 150 : 110) * 1024;
+  static constexpr int kBudget = (Q4 ? kQ4BudgetKB : 110) * 1024;
   static constexpr int kFixed = 1024 /*align*/ + kBarBytes + kXchBytes + kRedBytes + kDeq * kWTileBytes;
   static constexpr int kStagesRaw = (kBudget - kFixed) / kStageBytes;
   static constexpr int kMaxStages = Q4 ? 16 : 8;
-  static constexpr int kStages = kStagesRaw < 2 ? 2 : (kStagesRaw > kMaxStages ? kMaxStages : kStagesRaw);
+  // units per empty / deq_full barrier phase: the MMA thread's mbarrier
+  // operations (a few hundred cycles each next to in-flight MMAs) are paid
+  // once per pair of q4 units
+  static constexpr int kUpb = Q4 ? 2 : 1;
+  static constexpr int kStages0 = kStagesRaw < 2 ? 2 : (kStagesRaw > kMaxStages ? kMaxStages : kStagesRaw);
+  static constexpr int kStages = (kStages0 / kUpb) * kUpb;
   static constexpr int kSmem = kFixed + kStages * kStageBytes;
   static constexpr int kTmemCols = (2 * TPAD <= 32) ? 32 : (2 * TPAD <= 64 ? 64 : (2 * TPAD <= 128 ? 128 : 256));
   static constexpr uint32_t kIdesc = idesc_bf16_f32(128, TPAD);
@@ -163,9 +175,12 @@ __global__ void __launch_bounds__(Q4 ? kGemmThreadsQ4 : kGemmThreads, 1)
   uint64_t* empty_bar = full_bar + S;
   uint64_t* tfull_bar = empty_bar + S;
   uint64_t* tempty_bar = tfull_bar + 2;
+  // q4: deq_full[d] completes when the dequant warps have written buffer d
+  // (and, through their own wait, the stage's X tile has landed).  Buffer d
+  // of unit i is free again once the MMA of unit i - D completed, which the
+  // dequant warps read off that unit's empty_bar phase: one commit per unit.
   uint64_t* deq_full = tempty_bar + 2;   // [D] (q4 only)
-  uint64_t* deq_empty = deq_full + D;    // [D]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(deq_empty + D);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(deq_full + 2 * D);
   int* s_flag = reinterpret_cast<int*>(tmem_slot + 1);
   float* xch = reinterpret_cast<float*>(bar_base + C::kBarBytes);
   uint8_t* red_raw = bar_base + C::kBarBytes + C::kXchBytes;
@@ -196,8 +211,7 @@ __global__ void __launch_bounds__(Q4 ? kGemmThreadsQ4 : kGemmThreads, 1)
         mbar_init(&tempty_bar[b], 4);
       }
       for (int b = 0; b < D; ++b) {
-        mbar_init(&deq_full[b], 8);  // one arrival per dequant warp
-        mbar_init(&deq_empty[b], 1);
+        mbar_init(&deq_full[b], kDeqWarps);  // a pair of units: one arrival per dequant warp
       }
       fence_barrier_init();
       tma_prefetch_desc(&tmap_w);
@@ -231,17 +245,24 @@ __global__ void __launch_bounds__(Q4 ? kGemmThreadsQ4 : kGemmThreads, 1)
         tma_load_2d(stage_base + i * C::kStageBytes + C::kXOff, &tmap_x, &full_bar[i], kblk * 64, 0, pol_x);
       }
       bool ok = true;
+      // (tile, kblk) of unit `pre`, advanced incrementally (no 64-bit division per unit)
+      int tile = static_cast<int>((u0 + pre) / p.kb), kblk = static_cast<int>((u0 + pre) % p.kb);
+      int s = pre % S;
       for (int i = pre; i < n_units && ok; ++i) {
-        const int s = i % S;
-        const uint32_t ph = static_cast<uint32_t>(i / S) & 1u;
-        ok = mbar_wait(&empty_bar[s], ph ^ 1u, 1);
+        {  // the MMA of unit i - S (its pair's commit) released this stage
+          const int jp = (i - S) / C::kUpb;
+          ok = mbar_wait(&empty_bar[jp % (S / C::kUpb)], static_cast<uint32_t>(jp / (S / C::kUpb)) & 1u, 1);
+        }
         if (!ok) break;
-        const long long u = u0 + i;
-        const int tile = static_cast<int>(u / p.kb), kblk = static_cast<int>(u % p.kb);
         mbar_arrive_expect_tx(&full_bar[s], C::kStageBytes);
         uint8_t* st = stage_base + s * C::kStageBytes;
         tma_load_2d(st + C::kWOff, &tmap_w, &full_bar[s], kblk * (Q4 ? 8 : 64), tile * 128, pol_w);
         tma_load_2d(st + C::kXOff, &tmap_x, &full_bar[s], kblk * 64, 0, pol_x);
+        if (++kblk == p.kb) {
+          kblk = 0;
+          ++tile;
+        }
+        if (++s == S) s = 0;
       }
       // drain: every issued load must land before the CTA can retire
       const int first_undrained = n_units > S ? n_units - S : 0;
@@ -251,8 +272,15 @@ __global__ void __launch_bounds__(Q4 ? kGemmThreadsQ4 : kGemmThreads, 1)
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
+      // Lean per-unit loop (this thread's issue rate bounds the unit rate):
+      // descriptors are a base plus a 16-byte-unit offset, ring slots and
+      // phases advance incrementally.
+      const uint64_t a_base = sw128_kmajor_desc(smem_u32(Q4 ? deq_base : stage_base));
+      const uint64_t b_base = sw128_kmajor_desc(smem_u32(stage_base + C::kXOff));
       long long u = u0;
       int i = 0, seg = 0;
+      int s = 0, d = 0, dp = 0;  // stage, dequant buffer, deq_full pair slot
+      uint32_t ph = 0, phd = 0;
       bool ok = true;
       while (u < u1) {
         const int kblk0 = static_cast<int>(u % p.kb);
@@ -263,25 +291,37 @@ __global__ void __launch_bounds__(Q4 ? kGemmThreadsQ4 : kGemmThreads, 1)
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(b * TPAD);
         for (int j = 0; j < len; ++j, ++i) {
-          const int s = i % S;
-          const uint32_t ph = static_cast<uint32_t>(i / S) & 1u;
-          if (ok) ok = mbar_wait(&full_bar[s], ph, 4);
-          if constexpr (Q4) {
-            if (ok) ok = mbar_wait(&deq_full[i % D], static_cast<uint32_t>(i / D) & 1u, 8);
+          if (i % C::kUpb == 0) {  // first unit of a barrier pair
+            if constexpr (Q4) {
+              if (ok) ok = mbar_wait(&deq_full[dp], phd, 8);
+            } else {
+              if (ok) ok = mbar_wait(&full_bar[s], ph, 4);
+            }
+            tc_fence_after();
           }
-          tc_fence_after();
           if (ok) {
-            const uint32_t a_addr =
-                Q4 ? smem_u32(deq_base + (i % D) * kWTileBytes) : smem_u32(stage_base + s * C::kStageBytes);
-            const uint32_t b_addr = smem_u32(stage_base + s * C::kStageBytes + C::kXOff);
+            const uint64_t a0 = a_base + ((Q4 ? d * kWTileBytes : s * C::kStageBytes) >> 4);
+            const uint64_t b0 = b_base + ((s * C::kStageBytes) >> 4);
 #pragma unroll
-            for (int kk = 0; kk < 4; ++kk) {
-              umma_bf16(d_tmem, sw128_kmajor_desc(a_addr + kk * 32), sw128_kmajor_desc(b_addr + kk * 32), C::kIdesc,
-                        (j > 0 || kk > 0) ? 1u : 0u);
+            for (int kk = 0; kk < 4; ++kk)
+              umma_bf16(d_tmem, a0 + kk * 2, b0 + kk * 2, C::kIdesc, (j > 0 || kk > 0) ? 1u : 0u);
+          }
+          if (i % C::kUpb == C::kUpb - 1 || i == n_units - 1) {
+            umma_commit(&empty_bar[(i / C::kUpb) % (S / C::kUpb)]);
+            if constexpr (Q4) {
+              if (++dp == D / C::kUpb) {
+                dp = 0;
+                phd ^= 1u;
+              }
             }
           }
-          umma_commit(&empty_bar[s]);
-          if constexpr (Q4) umma_commit(&deq_empty[i % D]);
+          if (++s == S) {
+            s = 0;
+            ph ^= 1u;
+          }
+          if constexpr (Q4) {
+            if (++d == D) d = 0;
+          }
         }
         umma_commit(&tfull_bar[b]);
         u += len;
@@ -290,20 +330,25 @@ __global__ void __launch_bounds__(Q4 ? kGemmThreadsQ4 : kGemmThreads, 1)
     }
   } else if (Q4 && warp >= 6) {
     // ------------------------------------------------------------ dequant (q4)
-    // thread t: row t/2 of the tile, half t%2 of its 64 K elements (16 packed
-    // bytes -> four 16-byte chunks of the swizzled bf16 row)
+    // kDeqGroups groups of warps work on different units at once (group g:
+    // units i = g, g + kDeqGroups, ...), so the per-unit chain of waits,
+    // shared-memory round trips and arrivals of one unit overlaps the
+    // others'.  Within a group, thread tt dequantizes row tt / kDeqTpr, part
+    // tt % kDeqTpr of the unit (kDeqWpt packed words -> kDeqWpt 16-byte
+    // chunks of the 128-byte-swizzled bf16 row).
     // Scales / biases (no upstream dependency) come 8 groups per 16-byte
     // load when rows are 16-byte aligned (kb % 8 == 0): `cur` holds the
-    // 8-group block of the current unit, `nxt` the following block, loaded
-    // one block ahead so its latency hides behind 8 units of work.
+    // 8-group block of the current unit, `nxt` the following block.
     const int t = threadIdx.x - kGemmThreads;
-    const int r = t >> 1, h = t & 1;
+    const int grp = t / (kDeqGroupWarps * 32), tt = t % (kDeqGroupWarps * 32);
+    const int r = tt / kDeqTpr, h = tt % kDeqTpr;
     const bool vec = (p.kb & 7) == 0 &&
                      ((reinterpret_cast<uintptr_t>(p.q_scales) | reinterpret_cast<uintptr_t>(p.q_biases)) & 15u) == 0;
-    long long cur_key = -1, nxt_key = -1;  // (tile * kb + first kblk) of the block held
+    const long long ug = u0 + grp;
+    int tile = static_cast<int>(ug / p.kb), kblk = static_cast<int>(ug % p.kb);
+    int cur_t = -1, cur_k = -1, nxt_t = -1, nxt_k = -1;  // 8-group blocks held in cur / nxt
     uint4 cur_s = make_uint4(0, 0, 0, 0), cur_b = cur_s, nxt_s = cur_s, nxt_b = cur_s;
-    auto load_block = [&](long long ub, uint4& vs, uint4& vb) {
-      const int tl = static_cast<int>(ub / p.kb), kb0 = static_cast<int>(ub % p.kb);
+    auto load_block = [&](int tl, int kb0, uint4& vs, uint4& vb) {
       const int nn = tl * 128 + r;
       if (nn < p.n_out) {
         const size_t off = static_cast<size_t>(nn) * p.kb + kb0;
@@ -314,54 +359,79 @@ __global__ void __launch_bounds__(Q4 ? kGemmThreadsQ4 : kGemmThreads, 1)
         vb = vs;
       }
     };
+    static_assert(!Q4 || S >= D, "q4 needs at least as many stages as dequant buffers");
+    static_assert(!Q4 || D % kDeqGroups == 0, "dequant buffers per group must be whole");
+    static_assert(!Q4 || (kDeqGroups == C::kUpb && D % C::kUpb == 0 && S >= D + C::kUpb),
+                  "q4 barrier pairs: one unit per group, whole pairs of buffers, stages ahead of buffers");
     bool ok = true;
-    for (int i = 0; i < n_units && ok; ++i) {
-      const long long u = u0 + i;
-      const int tile = static_cast<int>(u / p.kb), kblk = static_cast<int>(u % p.kb);
-      const int n = tile * 128 + r;
-      __nv_bfloat16 sc = __float2bfloat16_rn(0.0f), bi = sc;
-      if (vec) {
-        const long long key = u - (kblk & 7);
-        if (key != cur_key) {
-          if (key == nxt_key) {
-            cur_s = nxt_s;
-            cur_b = nxt_b;
-          } else {
-            load_block(key, cur_s, cur_b);
+    // every pair of units gets one arrival per dequant warp on its deq_full
+    // barrier, also the missing half of a CTA's last, odd pair
+    const int n_pairs_units = ((n_units + C::kUpb - 1) / C::kUpb) * C::kUpb;
+    for (int i = grp; i < n_pairs_units && ok; i += kDeqGroups) {
+      if (i < n_units) {
+        const int n = tile * 128 + r;
+        __nv_bfloat16 sc = __float2bfloat16_rn(0.0f), bi = sc;
+        if (vec) {
+          const int k8 = kblk & ~7;
+          if (tile != cur_t || k8 != cur_k) {
+            if (tile == nxt_t && k8 == nxt_k) {
+              cur_s = nxt_s;
+              cur_b = nxt_b;
+            } else {
+              load_block(tile, k8, cur_s, cur_b);
+            }
+            cur_t = tile;
+            cur_k = k8;
+            // prefetch the following block if this CTA's range reaches it
+            if (n_units - i > 8 - (kblk & 7)) {
+              nxt_t = k8 + 8 < p.kb ? tile : tile + 1;
+              nxt_k = k8 + 8 < p.kb ? k8 + 8 : 0;
+              load_block(nxt_t, nxt_k, nxt_s, nxt_b);
+            }
           }
-          cur_key = key;
-          // prefetch the next block of this CTA's range
-          const long long nk = key + 8;
-          if (nk < u1) {
-            load_block(nk, nxt_s, nxt_b);
-            nxt_key = nk;
-          }
+          const int g = kblk & 7, wi = g >> 1;
+          const uint32_t ws = wi == 0 ? cur_s.x : wi == 1 ? cur_s.y : wi == 2 ? cur_s.z : cur_s.w;
+          const uint32_t wb = wi == 0 ? cur_b.x : wi == 1 ? cur_b.y : wi == 2 ? cur_b.z : cur_b.w;
+          const int sh = (g & 1) * 16;
+          sc = __ushort_as_bfloat16(static_cast<unsigned short>((ws >> sh) & 0xFFFFu));
+          bi = __ushort_as_bfloat16(static_cast<unsigned short>((wb >> sh) & 0xFFFFu));
+        } else if (n < p.n_out) {
+          sc = p.q_scales[static_cast<size_t>(n) * p.kb + kblk];
+          bi = p.q_biases[static_cast<size_t>(n) * p.kb + kblk];
         }
-        const int g = kblk & 7, wi = g >> 1;
-        const uint32_t ws = wi == 0 ? cur_s.x : wi == 1 ? cur_s.y : wi == 2 ? cur_s.z : cur_s.w;
-        const uint32_t wb = wi == 0 ? cur_b.x : wi == 1 ? cur_b.y : wi == 2 ? cur_b.z : cur_b.w;
-        const int sh = (g & 1) * 16;
-        sc = __ushort_as_bfloat16(static_cast<unsigned short>((ws >> sh) & 0xFFFFu));
-        bi = __ushort_as_bfloat16(static_cast<unsigned short>((wb >> sh) & 0xFFFFu));
-      } else if (n < p.n_out) {
-        sc = p.q_scales[static_cast<size_t>(n) * p.kb + kblk];
-        bi = p.q_biases[static_cast<size_t>(n) * p.kb + kblk];
+        const int s = i % S, d = i % D;
+        ok = mbar_wait(&full_bar[s], static_cast<uint32_t>(i / S) & 1u, 6);
+        // buffer d was last read by the MMA of unit i - D: wait for its pair's commit
+        if (ok && i >= D) {
+          const int jp = (i - D) / C::kUpb;
+          ok = mbar_wait(&empty_bar[jp % (S / C::kUpb)], static_cast<uint32_t>(jp / (S / C::kUpb)) & 1u, 7);
+        }
+        if (!ok) break;
+        const uint8_t* src = stage_base + s * C::kStageBytes + C::kWOff + r * 32 + h * (kDeqWpt * 4);
+        uint32_t pk[kDeqWpt];
+#pragma unroll
+        for (int j = 0; j < kDeqWpt; j += 4) {
+          const uint4 v = *reinterpret_cast<const uint4*>(src + j * 4);
+          pk[j] = v.x;
+          pk[j + 1] = v.y;
+          pk[j + 2] = v.z;
+          pk[j + 3] = v.w;
+        }
+        const __nv_bfloat162 s2 = __halves2bfloat162(sc, sc), b2 = __halves2bfloat162(bi, bi);
+        uint8_t* dst = deq_base + d * kWTileBytes + r * 128;
+        const int sw = r & 7;
+#pragma unroll
+        for (int j = 0; j < kDeqWpt; ++j)
+          *reinterpret_cast<uint4*>(dst + (((kDeqWpt * h + j) ^ sw) << 4)) = dequant8(pk[j], s2, b2);
+        fence_proxy_async_smem();  // generic-proxy writes -> visible to tcgen05.mma
       }
-      const int s = i % S, d = i % D;
-      ok = mbar_wait(&full_bar[s], static_cast<uint32_t>(i / S) & 1u, 6);
-      if (ok && i >= D) ok = mbar_wait(&deq_empty[d], (static_cast<uint32_t>(i / D) & 1u) ^ 1u, 7);
-      if (!ok) break;
-      const uint4 pk = *reinterpret_cast<const uint4*>(stage_base + s * C::kStageBytes + C::kWOff + r * 32 + h * 16);
-      const __nv_bfloat162 s2 = __halves2bfloat162(sc, sc), b2 = __halves2bfloat162(bi, bi);
-      uint8_t* dst = deq_base + d * kWTileBytes + r * 128;
-      const int sw = r & 7;
-      *reinterpret_cast<uint4*>(dst + (((4 * h + 0) ^ sw) << 4)) = dequant8(pk.x, s2, b2);
-      *reinterpret_cast<uint4*>(dst + (((4 * h + 1) ^ sw) << 4)) = dequant8(pk.y, s2, b2);
-      *reinterpret_cast<uint4*>(dst + (((4 * h + 2) ^ sw) << 4)) = dequant8(pk.z, s2, b2);
-      *reinterpret_cast<uint4*>(dst + (((4 * h + 3) ^ sw) << 4)) = dequant8(pk.w, s2, b2);
-      fence_proxy_async_smem();  // generic-proxy writes -> visible to tcgen05.mma
       __syncwarp();
-      if (lane == 0) mbar_arrive(&deq_full[d]);
+      if (lane == 0) mbar_arrive(&deq_full[(i / C::kUpb) % (D / C::kUpb)]);
+      kblk += kDeqGroups;
+      while (kblk >= p.kb) {
+        kblk -= p.kb;
+        ++tile;
+      }
     }
   } else {
     // ------------------------------------------------------------ epilogue
