@@ -94,8 +94,11 @@ struct GemmCfg {
   static constexpr int kStageBytes = (Q4 ? kPkTileBytes : kWTileBytes) + kXBytes;
   static constexpr int kXOff = Q4 ? 0 : kWTileBytes;
   static constexpr int kWOff = Q4 ? kXBytes : 0;
-  // dequantized bf16 W buffers: 2 per group (1 from TPAD 64), at most the stage count
-  static constexpr int kDeq = Q4 ? kDeqGroups * (TPAD >= 64 ? 1 : 2) : 0;  // dequantized bf16 W buffers (16 KB each)
+  // dequantized W units in TMEM (32 columns each, beside the accumulators).
+  // The producer loads unit i only once the MMA of unit i - kDeq is done, so
+  // a landed stage also means a free buffer: kDeq is the q4 load lookahead.
+  static constexpr int kDeq = Q4 ? (TPAD >= 128 ? 4 : (TPAD >= 64 ? 8 : 14)) : 0;
+  static constexpr int kLookahead = Q4 ? kDeq : 0;  // 0: the whole ring
   static constexpr int kBarBytes = Q4 ? 512 : 256;
   static constexpr int kXchBytes = (EPI == kEpiQkv || EPI == kEpiSwiglu) ? 128 * 8 * 4 : 0;
   // [0,256): per-warp reductions of one 8-row chunk; then s_best / s_pos
@@ -106,7 +109,7 @@ struct GemmCfg {
   // (q4 stages are a quarter as large; a deeper ring keeps enough packed
   // bytes in flight)
   static constexpr int kBudget = (Q4 ? kQ4BudgetKB : 110) * 1024;
-  static constexpr int kFixed = 1024 /*align*/ + kBarBytes + kXchBytes + kRedBytes + kDeq * kWTileBytes;
+  static constexpr int kFixed = 1024 /*align*/ + kBarBytes + kXchBytes + kRedBytes;
   static constexpr int kStagesRaw = (kBudget - kFixed) / kStageBytes;
   static constexpr int kMaxStages = Q4 ? 16 : 8;
   // units per empty / deq_full barrier phase: the MMA thread's mbarrier
@@ -116,7 +119,14 @@ struct GemmCfg {
   static constexpr int kStages0 = kStagesRaw < 2 ? 2 : (kStagesRaw > kMaxStages ? kMaxStages : kStagesRaw);
   static constexpr int kStages = (kStages0 / kUpb) * kUpb;
   static constexpr int kSmem = kFixed + kStages * kStageBytes;
-  static constexpr int kTmemCols = (2 * TPAD <= 32) ? 32 : (2 * TPAD <= 64 ? 64 : (2 * TPAD <= 128 ? 128 : 256));
+  // TMEM: accumulator buffers (two, so a segment's MMAs overlap the previous
+  // segment's epilogue; one for q4 at TPAD 128) and, for q4, the dequantized
+  // W units (the MMA's A operand: 128 lanes x 32 columns of bf16 pairs each)
+  static constexpr int kAccBufs = (Q4 && TPAD >= 128) ? 1 : 2;
+  static constexpr int kTmemAcc = kAccBufs * TPAD;
+  static constexpr int kTmemNeed = kTmemAcc + (Q4 ? kDeq * 32 : 0);
+  static constexpr int kTmemCols =
+      kTmemNeed <= 32 ? 32 : (kTmemNeed <= 64 ? 64 : (kTmemNeed <= 128 ? 128 : (kTmemNeed <= 256 ? 256 : 512)));
   static constexpr uint32_t kIdesc = idesc_bf16_f32(128, TPAD);
 };
 
@@ -169,8 +179,7 @@ __global__ void __launch_bounds__(Q4 ? kGemmThreadsQ4 : kGemmThreads, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* stage_base = smem;
-  uint8_t* deq_base = smem + S * C::kStageBytes;  // [D][128 rows x 128 B] swizzled bf16 W (q4 only)
-  uint8_t* bar_base = deq_base + C::kDeq * kWTileBytes;
+  uint8_t* bar_base = smem + S * C::kStageBytes;
   uint64_t* full_bar = reinterpret_cast<uint64_t*>(bar_base);
   uint64_t* empty_bar = full_bar + S;
   uint64_t* tfull_bar = empty_bar + S;
@@ -230,7 +239,8 @@ __global__ void __launch_bounds__(Q4 ? kGemmThreadsQ4 : kGemmThreads, 1)
     if (lane == 0) {
       const uint64_t pol_w = l2_policy_evict_first();
       const uint64_t pol_x = l2_policy_evict_last();
-      const int pre = n_units < S ? n_units : S;
+      constexpr int LA = C::kLookahead > 0 ? C::kLookahead : S;  // units in flight
+      const int pre = n_units < LA ? n_units : LA;
       // weights do not depend on the upstream kernel: start streaming now
       for (int i = 0; i < pre; ++i) {
         const long long u = u0 + i;
@@ -249,8 +259,9 @@ __global__ void __launch_bounds__(Q4 ? kGemmThreadsQ4 : kGemmThreads, 1)
       int tile = static_cast<int>((u0 + pre) / p.kb), kblk = static_cast<int>((u0 + pre) % p.kb);
       int s = pre % S;
       for (int i = pre; i < n_units && ok; ++i) {
-        {  // the MMA of unit i - S (its pair's commit) released this stage
-          const int jp = (i - S) / C::kUpb;
+        {  // the MMA of unit i - LA (its pair's commit) released this stage (and,
+           // for q4, TMEM buffer i % D)
+          const int jp = (i - LA) / C::kUpb;
           ok = mbar_wait(&empty_bar[jp % (S / C::kUpb)], static_cast<uint32_t>(jp / (S / C::kUpb)) & 1u, 1);
         }
         if (!ok) break;
@@ -275,7 +286,7 @@ __global__ void __launch_bounds__(Q4 ? kGemmThreadsQ4 : kGemmThreads, 1)
       // Lean per-unit loop (this thread's issue rate bounds the unit rate):
       // descriptors are a base plus a 16-byte-unit offset, ring slots and
       // phases advance incrementally.
-      const uint64_t a_base = sw128_kmajor_desc(smem_u32(Q4 ? deq_base : stage_base));
+      const uint64_t a_base = sw128_kmajor_desc(smem_u32(stage_base));
       const uint64_t b_base = sw128_kmajor_desc(smem_u32(stage_base + C::kXOff));
       long long u = u0;
       int i = 0, seg = 0;
@@ -285,8 +296,8 @@ __global__ void __launch_bounds__(Q4 ? kGemmThreadsQ4 : kGemmThreads, 1)
       while (u < u1) {
         const int kblk0 = static_cast<int>(u % p.kb);
         const int len = static_cast<int>(min(static_cast<long long>(p.kb - kblk0), u1 - u));
-        const int b = seg & 1;
-        const int use = seg >> 1;
+        const int b = seg % C::kAccBufs;
+        const int use = seg / C::kAccBufs;
         if (use >= 1 && ok) ok = mbar_wait(&tempty_bar[b], static_cast<uint32_t>(use - 1) & 1u, 3);
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(b * TPAD);
@@ -300,11 +311,18 @@ __global__ void __launch_bounds__(Q4 ? kGemmThreadsQ4 : kGemmThreads, 1)
             tc_fence_after();
           }
           if (ok) {
-            const uint64_t a0 = a_base + ((Q4 ? d * kWTileBytes : s * C::kStageBytes) >> 4);
             const uint64_t b0 = b_base + ((s * C::kStageBytes) >> 4);
+            if constexpr (Q4) {  // A = the dequantized unit in TMEM, 8 columns per K step of 16
+              const uint32_t a_tmem = tmem_base + static_cast<uint32_t>(C::kTmemAcc + d * 32);
 #pragma unroll
-            for (int kk = 0; kk < 4; ++kk)
-              umma_bf16(d_tmem, a0 + kk * 2, b0 + kk * 2, C::kIdesc, (j > 0 || kk > 0) ? 1u : 0u);
+              for (int kk = 0; kk < 4; ++kk)
+                umma_bf16_ts(d_tmem, a_tmem + kk * 8, b0 + kk * 2, C::kIdesc, (j > 0 || kk > 0) ? 1u : 0u);
+            } else {
+              const uint64_t a0 = a_base + ((s * C::kStageBytes) >> 4);
+#pragma unroll
+              for (int kk = 0; kk < 4; ++kk)
+                umma_bf16(d_tmem, a0 + kk * 2, b0 + kk * 2, C::kIdesc, (j > 0 || kk > 0) ? 1u : 0u);
+            }
           }
           if (i % C::kUpb == C::kUpb - 1 || i == n_units - 1) {
             umma_commit(&empty_bar[(i / C::kUpb) % (S / C::kUpb)]);
@@ -341,7 +359,12 @@ __global__ void __launch_bounds__(Q4 ? kGemmThreadsQ4 : kGemmThreads, 1)
     // 8-group block of the current unit, `nxt` the following block.
     const int t = threadIdx.x - kGemmThreads;
     const int grp = t / (kDeqGroupWarps * 32), tt = t % (kDeqGroupWarps * 32);
-    const int r = tt / kDeqTpr, h = tt % kDeqTpr;
+    // one tile row per thread: the TMEM lane this warp may write (lanes
+    // 32 * (warp % 4) ..), which the group's four warps cover once
+    static_assert(kDeqTpr == 1 && kDeqWpt == 8, "q4 dequant: one thread per tile row");
+    const int r = 32 * (warp & 3) + lane;
+    const uint32_t t_lane = static_cast<uint32_t>(32 * (warp & 3)) << 16;
+    (void)tt;
     const bool vec = (p.kb & 7) == 0 &&
                      ((reinterpret_cast<uintptr_t>(p.q_scales) | reinterpret_cast<uintptr_t>(p.q_biases)) & 15u) == 0;
     const long long ug = u0 + grp;
@@ -361,7 +384,7 @@ __global__ void __launch_bounds__(Q4 ? kGemmThreadsQ4 : kGemmThreads, 1)
     };
     static_assert(!Q4 || S >= D, "q4 needs at least as many stages as dequant buffers");
     static_assert(!Q4 || D % kDeqGroups == 0, "dequant buffers per group must be whole");
-    static_assert(!Q4 || (kDeqGroups == C::kUpb && D % C::kUpb == 0 && S >= D + C::kUpb),
+    static_assert(!Q4 || (kDeqGroups == C::kUpb && D % C::kUpb == 0 && S >= C::kLookahead + C::kUpb),
                   "q4 barrier pairs: one unit per group, whole pairs of buffers, stages ahead of buffers");
     bool ok = true;
     // every pair of units gets one arrival per dequant warp on its deq_full
@@ -401,29 +424,29 @@ __global__ void __launch_bounds__(Q4 ? kGemmThreadsQ4 : kGemmThreads, 1)
         }
         const int s = i % S, d = i % D;
         ok = mbar_wait(&full_bar[s], static_cast<uint32_t>(i / S) & 1u, 6);
-        // buffer d was last read by the MMA of unit i - D: wait for its pair's commit
-        if (ok && i >= D) {
-          const int jp = (i - D) / C::kUpb;
-          ok = mbar_wait(&empty_bar[jp % (S / C::kUpb)], static_cast<uint32_t>(jp / (S / C::kUpb)) & 1u, 7);
-        }
+        // (the producer loaded unit i after the MMA of unit i - D, the last
+        // reader of buffer d, completed)
+        ok = __all_sync(0xffffffffu, ok);  // the TMEM store below is warp-wide
         if (!ok) break;
-        const uint8_t* src = stage_base + s * C::kStageBytes + C::kWOff + r * 32 + h * (kDeqWpt * 4);
-        uint32_t pk[kDeqWpt];
-#pragma unroll
-        for (int j = 0; j < kDeqWpt; j += 4) {
-          const uint4 v = *reinterpret_cast<const uint4*>(src + j * 4);
-          pk[j] = v.x;
-          pk[j + 1] = v.y;
-          pk[j + 2] = v.z;
-          pk[j + 3] = v.w;
-        }
+        tc_fence_after();
+        // the row's 64 packed weights -> 32 columns of bf16 pairs (K order) in
+        // the unit's TMEM buffer
+        const uint4* src = reinterpret_cast<const uint4*>(stage_base + s * C::kStageBytes + C::kWOff + r * 32);
+        const uint4 pa = src[0], pb = src[1];
         const __nv_bfloat162 s2 = __halves2bfloat162(sc, sc), b2 = __halves2bfloat162(bi, bi);
-        uint8_t* dst = deq_base + d * kWTileBytes + r * 128;
-        const int sw = r & 7;
+        const uint32_t pk[8] = {pa.x, pa.y, pa.z, pa.w, pb.x, pb.y, pb.z, pb.w};
+        uint32_t v[32];
 #pragma unroll
-        for (int j = 0; j < kDeqWpt; ++j)
-          *reinterpret_cast<uint4*>(dst + (((kDeqWpt * h + j) ^ sw) << 4)) = dequant8(pk[j], s2, b2);
-        fence_proxy_async_smem();  // generic-proxy writes -> visible to tcgen05.mma
+        for (int j = 0; j < 8; ++j) {
+          const uint4 q = dequant8(pk[j], s2, b2);
+          v[4 * j] = q.x;
+          v[4 * j + 1] = q.y;
+          v[4 * j + 2] = q.z;
+          v[4 * j + 3] = q.w;
+        }
+        tmem_st_x32(tmem_base + t_lane + static_cast<uint32_t>(C::kTmemAcc + d * 32), v);
+        tmem_wait_st();
+        tc_fence_before();
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&deq_full[(i / C::kUpb) % (D / C::kUpb)]);
@@ -462,8 +485,8 @@ __global__ void __launch_bounds__(Q4 ? kGemmThreadsQ4 : kGemmThreads, 1)
       const int kblk0 = static_cast<int>(u % p.kb);
       const int len = static_cast<int>(min(static_cast<long long>(p.kb - kblk0), u1 - u));
       const bool full = (kblk0 == 0 && len == p.kb) || EPI == kEpiPartial;
-      const int b = seg & 1;
-      const int use = seg >> 1;
+      const int b = seg % C::kAccBufs;
+      const int use = seg / C::kAccBufs;
       mbar_wait(&tfull_bar[b], static_cast<uint32_t>(use) & 1u, 5);
       tc_fence_after();
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(b * TPAD);
