@@ -259,8 +259,8 @@ __global__ void __launch_bounds__(Q4 ? kGemmThreadsQ4 : kGemmThreads, 1)
       int tile = static_cast<int>((u0 + pre) / p.kb), kblk = static_cast<int>((u0 + pre) % p.kb);
       int s = pre % S;
       for (int i = pre; i < n_units && ok; ++i) {
-        {  // the MMA of unit i - LA (its pair's commit) released this stage (and,
-           // for q4, TMEM buffer i % D)
+        if ((i - LA) % C::kUpb == 0) {  // the MMA of units i - LA .. (their pair's commit)
+          // released this stage and the next (and, for q4, TMEM buffer i % D)
           const int jp = (i - LA) / C::kUpb;
           ok = mbar_wait(&empty_bar[jp % (S / C::kUpb)], static_cast<uint32_t>(jp / (S / C::kUpb)) & 1u, 1);
         }
