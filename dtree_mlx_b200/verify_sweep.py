@@ -230,7 +230,7 @@ def run_drafter(preset: str, prefix: int, iters: int, eager_only: bool, seed: in
 KERNEL_GROUPS = (
     ("lm_head", lambda k: k.startswith("gemm_streamk_kernel") and k.endswith(", 4>")),
     ("gemm", lambda k: k.startswith("gemm_streamk_kernel")),
-    ("attention", lambda k: k.startswith(("tree_attn_kernel", "attn_combine_kernel"))),
+    ("attention", lambda k: k.startswith(("tree_attn_kernel", "tree_attn_tc_kernel", "attn_combine_kernel"))),
     ("norm_rope", lambda k: k.startswith(("residual_rmsnorm_kernel", "rmsnorm_kernel", "qkv_finish_kernel"))),
     ("tree_build", lambda k: k.startswith(("topk_lse_kernel", "heap_tree_kernel"))),
     ("deltanet", lambda k: k.startswith(("tree_conv1d_kernel", "tree_gated_delta_kernel", "rmsnorm_gated_kernel"))),
