@@ -59,6 +59,8 @@ def test_linear_matches_fp32(K, t_pad, k, n):
         (16, 512, 200, 0),      # ragged N
         (64, 1024, 1536, 0),
         (128, 512, 640, 0),
+        (32, 320, 1280, 0),     # K/64 = 5: scalar scale loads, one unit per CTA
+        (16, 192, 384, 2),      # one or two units per CTA (a lone unit pair)
     ],
 )
 def test_linear_q4_matches_dequantized_fp32(K, t_pad, k, n, split_k):
