@@ -228,7 +228,7 @@ def run_drafter(preset: str, prefix: int, iters: int, eager_only: bool, seed: in
 
 
 KERNEL_GROUPS = (
-    ("lm_head", lambda k: k.startswith("gemm_streamk_kernel") and k.endswith(", 4>")),
+    ("lm_head", lambda k: k.startswith("gemm_streamk_kernel<") and k.split("<")[1].split(",")[1].strip() == "4"),
     ("gemm", lambda k: k.startswith("gemm_streamk_kernel")),
     ("attention", lambda k: k.startswith(("tree_attn_kernel", "tree_attn_tc_kernel", "attn_combine_kernel"))),
     ("norm_rope", lambda k: k.startswith(("residual_rmsnorm_kernel", "rmsnorm_kernel", "qkv_finish_kernel"))),
