@@ -97,7 +97,7 @@ struct GemmCfg {
   // dequantized W units in TMEM (32 columns each, beside the accumulators).
   // The producer loads unit i only once the MMA of unit i - kDeq is done, so
   // a landed stage also means a free buffer: kDeq is the q4 load lookahead.
-  static constexpr int kDeq = Q4 ? (TPAD >= 128 ? 4 : (TPAD >= 64 ? 8 : 14)) : 0;
+  static constexpr int kDeq = Q4 ? (TPAD >= 128 ? 4 : (TPAD >= 64 ? 8 : 12)) : 0;
   static constexpr int kLookahead = Q4 ? kDeq : 0;  // 0: the whole ring
   static constexpr int kBarBytes = Q4 ? 512 : 256;
   static constexpr int kXchBytes = (EPI == kEpiQkv || EPI == kEpiSwiglu) ? 128 * 8 * 4 : 0;
@@ -114,8 +114,8 @@ struct GemmCfg {
   static constexpr int kMaxStages = Q4 ? 16 : 8;
   // units per empty / deq_full barrier phase: the MMA thread's mbarrier
   // operations (a few hundred cycles each next to in-flight MMAs) are paid
-  // once per pair of q4 units
-  static constexpr int kUpb = Q4 ? 2 : 1;
+  // once per group of kUpb q4 units
+  static constexpr int kUpb = Q4 ? (TPAD >= 64 ? 2 : 4) : 1;
   static constexpr int kStages0 = kStagesRaw < 2 ? 2 : (kStagesRaw > kMaxStages ? kMaxStages : kStagesRaw);
   static constexpr int kStages = (kStages0 / kUpb) * kUpb;
   static constexpr int kSmem = kFixed + kStages * kStageBytes;
@@ -220,7 +220,7 @@ __global__ void __launch_bounds__(Q4 ? kGemmThreadsQ4 : kGemmThreads, 1)
         mbar_init(&tempty_bar[b], 4);
       }
       for (int b = 0; b < D; ++b) {
-        mbar_init(&deq_full[b], kDeqWarps);  // a pair of units: one arrival per dequant warp
+        mbar_init(&deq_full[b], kDeqWarps * (C::kUpb / kDeqGroups));  // one arrival per dequant warp and unit
       }
       fence_barrier_init();
       tma_prefetch_desc(&tmap_w);
@@ -259,8 +259,8 @@ __global__ void __launch_bounds__(Q4 ? kGemmThreadsQ4 : kGemmThreads, 1)
       int tile = static_cast<int>((u0 + pre) / p.kb), kblk = static_cast<int>((u0 + pre) % p.kb);
       int s = pre % S;
       for (int i = pre; i < n_units && ok; ++i) {
-        if ((i - LA) % C::kUpb == 0) {  // the MMA of units i - LA .. (their pair's commit)
-          // released this stage and the next (and, for q4, TMEM buffer i % D)
+        if ((i - LA) % C::kUpb == 0) {  // the MMA of units i - LA .. (their phase's commit)
+          // released this stage and the next kUpb - 1 (and, for q4, their TMEM buffers)
           const int jp = (i - LA) / C::kUpb;
           ok = mbar_wait(&empty_bar[jp % (S / C::kUpb)], static_cast<uint32_t>(jp / (S / C::kUpb)) & 1u, 1);
         }
@@ -290,7 +290,7 @@ __global__ void __launch_bounds__(Q4 ? kGemmThreadsQ4 : kGemmThreads, 1)
       const uint64_t b_base = sw128_kmajor_desc(smem_u32(stage_base + C::kXOff));
       long long u = u0;
       int i = 0, seg = 0;
-      int s = 0, d = 0, dp = 0;  // stage, dequant buffer, deq_full pair slot
+      int s = 0, d = 0, dp = 0;  // stage, dequant buffer, deq_full phase slot
       uint32_t ph = 0, phd = 0;
       bool ok = true;
       while (u < u1) {
@@ -302,7 +302,7 @@ __global__ void __launch_bounds__(Q4 ? kGemmThreadsQ4 : kGemmThreads, 1)
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(b * TPAD);
         for (int j = 0; j < len; ++j, ++i) {
-          if (i % C::kUpb == 0) {  // first unit of a barrier pair
+          if (i % C::kUpb == 0) {  // first unit of a barrier phase
             if constexpr (Q4) {
               if (ok) ok = mbar_wait(&deq_full[dp], phd, 8);
             } else {
@@ -384,13 +384,23 @@ __global__ void __launch_bounds__(Q4 ? kGemmThreadsQ4 : kGemmThreads, 1)
     };
     static_assert(!Q4 || S >= D, "q4 needs at least as many stages as dequant buffers");
     static_assert(!Q4 || D % kDeqGroups == 0, "dequant buffers per group must be whole");
-    static_assert(!Q4 || (kDeqGroups == C::kUpb && D % C::kUpb == 0 && S >= C::kLookahead + C::kUpb),
-                  "q4 barrier pairs: one unit per group, whole pairs of buffers, stages ahead of buffers");
+    static_assert(!Q4 || (C::kUpb % kDeqGroups == 0 && D % C::kUpb == 0 && S >= C::kLookahead + C::kUpb),
+                  "q4 barrier phases: whole units per group, whole phases of buffers, stages ahead of buffers");
+    constexpr int NS = D / C::kUpb;  // deq_full slots
     bool ok = true;
-    // every pair of units gets one arrival per dequant warp on its deq_full
-    // barrier, also the missing half of a CTA's last, odd pair
+    // every unit of a phase gets one arrival per warp of its group on the
+    // phase's deq_full barrier, also the units past the CTA's last one that
+    // fill its last phase
     const int n_pairs_units = ((n_units + C::kUpb - 1) / C::kUpb) * C::kUpb;
     for (int i = grp; i < n_pairs_units && ok; i += kDeqGroups) {
+      if (i >= n_units) {
+        // no load orders this arrival after the slot's previous phase
+        // (phase jp - NS): wait for that phase to complete first
+        const int jp = i / C::kUpb;
+        if (jp >= NS) ok = mbar_wait(&deq_full[jp % NS], static_cast<uint32_t>((jp - NS) / NS) & 1u, 9);
+        ok = __all_sync(0xffffffffu, ok);
+        if (!ok) break;
+      }
       if (i < n_units) {
         const int n = tile * 128 + r;
         __nv_bfloat16 sc = __float2bfloat16_rn(0.0f), bi = sc;
@@ -449,7 +459,7 @@ __global__ void __launch_bounds__(Q4 ? kGemmThreadsQ4 : kGemmThreads, 1)
         tc_fence_before();
       }
       __syncwarp();
-      if (lane == 0) mbar_arrive(&deq_full[(i / C::kUpb) % (D / C::kUpb)]);
+      if (lane == 0) mbar_arrive(&deq_full[(i / C::kUpb) % NS]);
       kblk += kDeqGroups;
       while (kblk >= p.kb) {
         kblk -= p.kb;
