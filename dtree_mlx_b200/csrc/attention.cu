@@ -394,6 +394,7 @@ __global__ void __launch_bounds__(kTcThreads) tree_attn_tc_kernel(const __grid_c
   uint8_t* sp = sm + C::kP;
   uint64_t* bar = reinterpret_cast<uint64_t*>(sm + C::kBar);  // [0] K/V landed, [1] S done, [2] O done
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 4);
+  int* s_p0 = reinterpret_cast<int*>(tmem_slot + 1);        // `start` as read before the wait
   float* red_max = reinterpret_cast<float*>(sm + C::kRed);  // [2][128]
   float* red_sum = red_max + 2 * 128;                       // [2][128]
 
@@ -406,9 +407,11 @@ __global__ void __launch_bounds__(kTcThreads) tree_attn_tc_kernel(const __grid_c
   const int rows_kv = G * T;
 
   if (t == 0) {
-    // prefix keys into L2 while the upstream kernels finish (see the mma.sync
-    // kernel: `start` read before the dependency wait only steers this hint)
+    // prefix keys into L2 while the upstream kernels finish.  `start` read
+    // before the dependency wait only steers this hint and the speculative
+    // first K/V load below (re-read and checked after the wait)
     const int P0 = p.state->start;
+    *s_p0 = P0;
     const int kps0 = attn_keys_per_split(P0 + T, p.splits, p.key_align);
     const int lo = split * kps0;
     const int hi = min(min(P0, lo + kps0), p.cap);
@@ -432,9 +435,27 @@ __global__ void __launch_bounds__(kTcThreads) tree_attn_tc_kernel(const __grid_c
   const uint32_t tmem = *tmem_slot;
   const uint32_t t_lane = static_cast<uint32_t>((warp & 3) * 32) << 16;
 
+  auto issue_kv = [&](int k0) {
+    const uint64_t pol = l2_policy_evict_first();
+    mbar_arrive_expect_tx(&bar[0], 2u * NA * kTcBlock);
+    const int y = kvh * p.cap + k0;
+#pragma unroll
+    for (int a = 0; a < NA; ++a) {
+      tma_load_2d(sk + a * kTcBlock, &tmap_k, &bar[0], a * 64, y, pol);
+      tma_load_2d(sv + a * kTcBlock, &tmap_v, &bar[0], a * 64, y, pol);
+    }
+  };
+  // this split's first pass as implied by the early `start` (a sane one only)
+  const int P0 = *s_p0;
+  const bool p0_ok = P0 >= 0 && P0 + T <= p.cap;
+  const int kps0 = p0_ok ? attn_keys_per_split(P0 + T, p.splits, p.key_align) : 0;
+  const int k_begin0 = split * kps0;
+  const bool spec = p0_ok && k_begin0 < min(P0 + T, k_begin0 + kps0);
+
   pdl_wait();
-  // Q (from the upstream kernel) is loaded while `start` is read; thread t
-  // stages half t/128 of row t%128
+  // the K/V tiles (written upstream) go first; Q is loaded while `start` is
+  // re-read; thread t stages half t/128 of row t%128
+  if (t == 0 && spec) issue_kv(k_begin0);
   const int qr = t & 127, qh = t >> 7;
   const int qrg = rb * 128 + qr;
   const bool q_ok = qrg < rows_kv;
@@ -457,18 +478,17 @@ __global__ void __launch_bounds__(kTcThreads) tree_attn_tc_kernel(const __grid_c
   const int k_begin = split * kps;
   const int k_end = min(L, k_begin + kps);
   const int n_pass = k_begin < k_end ? (k_end - k_begin + kTcKeys - 1) / kTcKeys : 0;
-
-  auto issue_kv = [&](int k0) {
-    const uint64_t pol = l2_policy_evict_first();
-    mbar_arrive_expect_tx(&bar[0], 2u * NA * kTcBlock);
-    const int y = kvh * p.cap + k0;
-#pragma unroll
-    for (int a = 0; a < NA; ++a) {
-      tma_load_2d(sk + a * kTcBlock, &tmap_k, &bar[0], a * 64, y, pol);
-      tma_load_2d(sv + a * kTcBlock, &tmap_v, &bar[0], a * 64, y, pol);
+  // `start` is the same before and after the wait unless a kernel that had
+  // not completed when this one started changed it: then the speculative
+  // load lands unused (phase 0 of bar[0]) and the right one follows
+  uint32_t ph_kv = 0;
+  if (!(spec && P == P0 && k_begin == k_begin0)) {
+    if (spec) ph_kv = 1;
+    if (t == 0) {
+      if (spec) mbar_wait(&bar[0], 0, 0x35);
+      if (n_pass > 0) issue_kv(k_begin);
     }
-  };
-  if (t == 0 && n_pass > 0) issue_kv(k_begin);
+  }
   if (n_pass > 0) {
 #pragma unroll
     for (int c = 0; c < HD / 16; ++c) {
@@ -482,10 +502,10 @@ __global__ void __launch_bounds__(kTcThreads) tree_attn_tc_kernel(const __grid_c
   bool ok = true;
   int fail_bar = 0;
   uint32_t ph = 0;
-  for (int j = 0; j < n_pass && ok; ++j, ph ^= 1u) {
+  for (int j = 0; j < n_pass && ok; ++j, ph ^= 1u, ph_kv ^= 1u) {
     const int k0 = k_begin + j * kTcKeys;
     if (t == 0 && j > 0) issue_kv(k0);
-    ok = mbar_wait(&bar[0], ph, 0x31);
+    ok = mbar_wait(&bar[0], ph_kv, 0x31);
     // V rows past the live keys may hold anything (NaN included): zero them so
     // that P = 0 there contributes exactly 0
     if (ok && qh < NA && k0 + qr >= k_end) {
@@ -607,7 +627,7 @@ __global__ void __launch_bounds__(kTcThreads) tree_attn_tc_kernel(const __grid_c
     }
     tc_fence_after();
   }
-  if (!ok && t == 0) mbar_wait(&bar[fail_bar], ph, 0x34);  // let the async op in flight land
+  if (!ok && t == 0) mbar_wait(&bar[fail_bar], fail_bar == 0 ? ph_kv : ph, 0x34);  // let the async op in flight land
 
   // ---- split partials (unnormalised O, m, l).  Each warp stages its 32 rows x
   // OH columns in the (now idle) Q/K/V space, then writes whole row segments.
@@ -667,23 +687,30 @@ __global__ void attn_combine_kernel(AttnParams p) {
   const int T = p.n_nodes;
   const int head = qrow / T, t = qrow % T;
   pdl_wait();
+  const int rows_total = p.n_q_heads * T;
+  // this thread's O partials of every launched split (splits <= 32, all in
+  // the workspace) and the splits' (m, l), loaded together with `start`:
+  // which splits hold keys is known only from `start`, so it selects among
+  // the loaded values instead of gating the loads
+  float ov[32];
+#pragma unroll
+  for (int s = 0; s < 32; ++s)
+    ov[s] = s < p.splits ? p.part_o[(static_cast<size_t>(s) * rows_total + qrow) * HD + d] : 0.0f;
+  float m_ld = -INFINITY, l_ld = 0.0f;
+  if (d < p.splits) {
+    const size_t r = static_cast<size_t>(d) * rows_total + qrow;
+    m_ld = p.part_ml[r * 2];
+    l_ld = p.part_ml[r * 2 + 1];
+  }
   const int P = p.state->start;
   const int L = P + T;
   const int kps = attn_keys_per_split(L, p.splits, p.key_align);
   const int active = min(p.splits, (L + kps - 1) / kps);
-  const int rows_total = p.n_q_heads * T;
-  // this thread's O partials of every split: loaded before the weights are
-  // known so the two reads overlap (splits <= 32)
-  float ov[32];
-#pragma unroll
-  for (int s = 0; s < 32; ++s)
-    ov[s] = s < active ? p.part_o[(static_cast<size_t>(s) * rows_total + qrow) * HD + d] : 0.0f;
   if (d < 32) {
     float m = -INFINITY, l = 0.0f;
     if (d < active) {
-      const size_t r = static_cast<size_t>(d) * rows_total + qrow;
-      m = p.part_ml[r * 2];
-      l = p.part_ml[r * 2 + 1];
+      m = m_ld;
+      l = l_ld;
     }
     float M = m;
     for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
