@@ -454,12 +454,18 @@ def main():
         global PRESET, PROMPT_LEN, KV_CAP
         PRESET, PROMPT_LEN, KV_CAP = "qwen35-9b", 2048, 2048 + 512 + 160
         args.no_cpu = True
+    # stdout carries the one JSON line only: everything else written to it
+    # (libraries' banners such as NCCL's version line included) goes to stderr
+    sys.stdout.flush()
+    json_out = os.fdopen(os.dup(1), "w")
+    os.dup2(2, 1)
     rank, world, local, dist = dist_init()
     try:
         out = run_reference(args, rank, world) if args.impl == "reference" else run_ours(args, rank, world, local,
                                                                                          dist)
         if out is not None:
-            print(json.dumps(out), flush=True)
+            json_out.write(json.dumps(out) + "\n")
+            json_out.flush()
     finally:
         if dist:
             dist.destroy_process_group()
