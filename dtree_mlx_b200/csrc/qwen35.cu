@@ -66,9 +66,10 @@ Dims dims_of(const dtree_qwen35_desc& d) {
 
 bool is_attn_layer(const dtree_qwen35_desc& d, int l) { return (l + 1) % d.full_attention_interval == 0; }
 
+// split-K of a projection: two CTAs per SM (see the Qwen3 model)
 int proj_split(int n_out) {
   const int tiles = (n_out + 127) / 128;
-  return std::max(1, std::min(kProjSplitMax, num_sms() / tiles));
+  return std::max(1, std::min(kProjSplitMax, 2 * num_sms() / tiles));
 }
 
 size_t align256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
