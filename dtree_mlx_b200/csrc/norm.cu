@@ -136,10 +136,11 @@ __global__ void __launch_bounds__(kNormThreads) residual_rmsnorm_kernel(
     const uint4 hv = hrow[i];
     // all splits' loads of a batch are in flight together; the sum still
     // runs in split order
-    for (int s0 = 0; s0 < n_split; s0 += 8) {
-      float4 a[8], b[8];
+    constexpr int kB = 16;  // splits per batch: the projections' split-K (<= 16) in one round trip
+    for (int s0 = 0; s0 < n_split; s0 += kB) {
+      float4 a[kB], b[kB];
 #pragma unroll
-      for (int k = 0; k < 8; ++k) {
+      for (int k = 0; k < kB; ++k) {
         if (s0 + k < n_split) {
           const float4* pp =
               reinterpret_cast<const float4*>(partials + (static_cast<size_t>(s0 + k) * part_rows + row) * H) + 2 * i;
@@ -148,7 +149,7 @@ __global__ void __launch_bounds__(kNormThreads) residual_rmsnorm_kernel(
         }
       }
 #pragma unroll
-      for (int k = 0; k < 8; ++k) {
+      for (int k = 0; k < kB; ++k) {
         if (s0 + k < n_split) {
           y[0] += a[k].x; y[1] += a[k].y; y[2] += a[k].z; y[3] += a[k].w;
           y[4] += b[k].x; y[5] += b[k].y; y[6] += b[k].z; y[7] += b[k].w;
