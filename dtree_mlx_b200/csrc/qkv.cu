@@ -28,18 +28,18 @@ __global__ void __launch_bounds__(256) qkv_finish_kernel(QkvFinishParams p) {
   const int col = gh < p.n_q_heads ? gh * qcols + d : p.n_q_heads * qcols + (gh - p.n_q_heads) * hd + d;
   const size_t stride = static_cast<size_t>(p.part_rows) * p.width;
   auto sum_splits = [&](int c) {
+    // up to 16 splits' loads in flight at once (one round trip), summed in
+    // split order
     const float* src = p.partials + static_cast<size_t>(t) * p.width + c;
     float a = 0.0f;
-    int s = 0;
-    for (; s + 3 < p.split; s += 4) {
-      const float x0 = __ldcg(src + s * stride), x1 = __ldcg(src + (s + 1) * stride);
-      const float x2 = __ldcg(src + (s + 2) * stride), x3 = __ldcg(src + (s + 3) * stride);
-      a += x0;
-      a += x1;
-      a += x2;
-      a += x3;
+    for (int s0 = 0; s0 < p.split; s0 += 16) {
+      float x[16];
+#pragma unroll
+      for (int k = 0; k < 16; ++k) x[k] = s0 + k < p.split ? __ldcg(src + (s0 + k) * stride) : 0.0f;
+#pragma unroll
+      for (int k = 0; k < 16; ++k)
+        if (s0 + k < p.split) a += x[k];
     }
-    for (; s < p.split; ++s) a += __ldcg(src + s * stride);
     return a;
   };
   const float a = sum_splits(col);
