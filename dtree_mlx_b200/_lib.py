@@ -153,10 +153,12 @@ PROTOTYPES = {
     "dtree_last_error": (C.c_char_p, []),
     "dtree_version": (I, []),
     "dtree_device_error": (I, [C.POINTER(C.c_uint32), I]),
+    "dtree_test_delayed_store": (I, [P, C.c_int32, I, P]),
     "dtree_tree_build_workspace_bytes": (SZ, [I, I, I]),
     "dtree_tree_build": (I, [P, I, I, I, P, P, SZ, P, P, P, P, P, P, P, P]),
     "dtree_tree_from_topk": (I, [P, P, I, I, I, P, P, P, P, P, P, P]),
     "dtree_tree_build_noalloc_max_bytes": (SZ, []),
+    "dtree_tree_build_noalloc_max_vocab": (I, [I]),
     "dtree_tree_build_noalloc": (I, [P, I, I, I, P, P, P, P, P, P, P]),
     "dtree_chain_build": (I, [P, I, I, P, P, P, P, P, P, P]),
     "dtree_plant_draft_logits": (I, [P, I, I, C.c_uint32, P, P, I, C.c_float, P]),

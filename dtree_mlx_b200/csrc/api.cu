@@ -111,3 +111,30 @@ extern "C" int dtree_device_error(uint32_t* code_out, int clear) {
   }
   return dtree::kOk;
 }
+
+// ------------------------------------------------------------ test hook
+namespace dtree {
+// One thread: let the next kernel on the stream start (programmatic dependent
+// launch), wait `delay_ns` on the global timer (bounded: at most 2^22 polls),
+// then store `value` -- a device write that lands while a dependent kernel
+// that read the old value early is already running.
+__global__ void delayed_store_kernel(int32_t* dst, int32_t value, unsigned long long delay_ns) {
+  pdl_trigger();
+  unsigned long long t0, t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
+  for (uint32_t i = 0; i < (1u << 22); ++i) {
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    if (t - t0 >= delay_ns) break;
+  }
+  *dst = value;
+}
+}  // namespace dtree
+
+extern "C" int dtree_test_delayed_store(int32_t* dst, int32_t value, int delay_ns, void* stream) {
+  DTREE_CHECK_ARG(dst, "null pointer");
+  DTREE_CHECK_ARG(delay_ns >= 0 && delay_ns <= 10000000, "delay_ns must be in [0, 1e7]");
+  DTREE_CUDA_RET(dtree::launch_pdl(dtree::delayed_store_kernel, dim3(1), dim3(1), 0,
+                                   static_cast<cudaStream_t>(stream), dst, value,
+                                   static_cast<unsigned long long>(delay_ns)));
+  return dtree::kOk;
+}

@@ -480,14 +480,17 @@ __global__ void __launch_bounds__(kTcThreads) tree_attn_tc_kernel(const __grid_c
   const int n_pass = k_begin < k_end ? (k_end - k_begin + kTcKeys - 1) / kTcKeys : 0;
   // `start` is the same before and after the wait unless a kernel that had
   // not completed when this one started changed it: then the speculative
-  // load lands unused (phase 0 of bar[0]) and the right one follows
+  // load lands unused (phase 0 of bar[0]) and the right one follows.  Every
+  // thread waits for that phase: a thread that went on to the pass-0 wait
+  // (parity 1) while phase 0 is still open would return at once and zero the
+  // V tail rows that the two loads in flight can still overwrite.
   uint32_t ph_kv = 0;
   if (!(spec && P == P0 && k_begin == k_begin0)) {
-    if (spec) ph_kv = 1;
-    if (t == 0) {
-      if (spec) mbar_wait(&bar[0], 0, 0x35);
-      if (n_pass > 0) issue_kv(k_begin);
+    if (spec) {
+      ph_kv = 1;
+      mbar_wait(&bar[0], 0, 0x35);
     }
+    if (t == 0 && n_pass > 0) issue_kv(k_begin);
   }
   if (n_pass > 0) {
 #pragma unroll

@@ -668,37 +668,41 @@ __global__ void step_commit_kernel(dtree_step_state* state) {
 }
 
 // splits per row for the top-k scan: enough that a chunk fits the registers
-// of one CTA (kTopkThreads * kTopkElems elements), at least ~8 CTAs per row
-// for large vocabularies, and a workspace within the no-allocation scratch
-// (1 MiB) for every row count the entry points accept
-static int topk_splits(int rows, int vocab) {
+// of one CTA (kTopkThreads * kTopkElems elements) and at least ~8 CTAs per
+// row for large vocabularies.  `cap_bytes` bounds the workspace (the
+// no-allocation scratch): splits shrink until it fits, and the caller checks
+// that a chunk still fits one CTA.
+constexpr int kTopkMaxSplits = 200;  // merge table splits * kMaxK * 8 B of shared memory
+static int topk_splits(int rows, int vocab, size_t cap_bytes) {
   const int per_cta = kTopkThreads * kTopkElems;
   int splits = (vocab + per_cta - 1) / per_cta;
   if (splits < 8) splits = vocab >= 8 * 4096 ? 8 : (vocab + 4095) / 4096;
   if (splits < 1) splits = 1;
-  while (splits > 1 && tree_ws_layout(rows, splits, nullptr, nullptr) > (static_cast<size_t>(1) << 20)) --splits;
+  if (splits > kTopkMaxSplits) splits = kTopkMaxSplits;
+  while (splits > 1 && tree_ws_layout(rows, splits, nullptr, nullptr) > cap_bytes) --splits;
   return splits;
 }
+constexpr size_t kNoCap = ~static_cast<size_t>(0);
 
-}  // namespace dtree
-
-using namespace dtree;
-
-extern "C" size_t dtree_tree_build_workspace_bytes(int rows, int vocab, int budget) {
-  (void)budget;
-  if (rows <= 0 || vocab <= 0) return 0;
-  return tree_ws_layout(rows, topk_splits(rows, vocab), nullptr, nullptr);
-}
-
-extern "C" int dtree_tree_build(const float* draft_logits, int rows, int vocab, int budget,
-                                dtree_step_state* state, void* workspace, size_t workspace_bytes,
-                                int32_t* tree_tokens, int32_t* parents, int32_t* depths, int32_t* positions,
-                                uint64_t* anc_mask, int32_t* top_ids, float* top_logprobs, void* stream_) {
-  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+// argument checks shared by the workspace and no-allocation builds
+static int tree_build_check(const float* draft_logits, int rows, int vocab, int budget, const dtree_step_state* state,
+                            const int32_t* tree_tokens, const int32_t* parents, const int32_t* depths,
+                            const int32_t* positions, const uint64_t* anc_mask) {
   DTREE_CHECK_ARG(state && tree_tokens && parents && depths && positions && anc_mask, "null output pointer");
   DTREE_CHECK_ARG(budget >= 0 && budget <= kMaxBudget, "budget must be in [0, 127]");
   DTREE_CHECK_ARG(rows >= 0 && rows <= kMaxRows, "rows must be in [0, 64]");
   DTREE_CHECK_ARG(vocab > 0, "vocab must be positive");
+  DTREE_CHECK_ARG(budget == 0 || rows == 0 || draft_logits != nullptr, "null draft_logits");
+  return kOk;
+}
+
+static int tree_build_impl(const float* draft_logits, int rows, int vocab, int budget, dtree_step_state* state,
+                           void* workspace, size_t workspace_bytes, int splits, int32_t* tree_tokens,
+                           int32_t* parents, int32_t* depths, int32_t* positions, uint64_t* anc_mask,
+                           int32_t* top_ids, float* top_logprobs, cudaStream_t stream) {
+  int rc = tree_build_check(draft_logits, rows, vocab, budget, state, tree_tokens, parents, depths, positions,
+                            anc_mask);
+  if (rc) return rc;
   const int k = budget < vocab ? budget : vocab;
   if (budget == 0 || rows == 0) {
     // root only (dtree_runtime.py:88-90)
@@ -707,15 +711,15 @@ extern "C" int dtree_tree_build(const float* draft_logits, int rows, int vocab, 
                               anc_mask));
     return kOk;
   }
-  DTREE_CHECK_ARG(draft_logits != nullptr, "null draft_logits");
-  const int splits = topk_splits(rows, vocab);
   const size_t need = tree_ws_layout(rows, splits, nullptr, nullptr);
   DTREE_CHECK_ARG(workspace != nullptr && workspace_bytes >= need, "tree workspace too small");
+  const int chunk = (vocab + splits - 1) / splits;
+  DTREE_CHECK_ARG(chunk <= kTopkThreads * kTopkElems,
+                  "vocab too large for the top-k chunking (at most " +
+                      std::to_string(static_cast<long long>(splits) * kTopkThreads * kTopkElems) + " here)");
   TreeWs ws;
   tree_ws_layout(rows, splits, &ws, static_cast<char*>(workspace));
-  const int chunk = (vocab + splits - 1) / splits;
   const size_t smem = static_cast<size_t>(splits) * kMaxK * 8;
-  DTREE_CHECK_ARG(chunk <= kTopkThreads * kTopkElems, "vocab too large for the top-k chunking");
   DTREE_CUDA_RET(ensure_smem_attr(topk_lse_kernel, static_cast<int>(smem)));
   DTREE_CUDA_RET(launch_pdl(topk_lse_kernel, dim3(splits, rows), dim3(kTopkThreads), smem, stream, draft_logits,
                             rows, vocab, k, splits, chunk, ws));
@@ -733,6 +737,26 @@ extern "C" int dtree_tree_build(const float* draft_logits, int rows, int vocab, 
                                      sizeof(float) * k, rows, cudaMemcpyDeviceToDevice, stream));
   }
   return kOk;
+}
+
+}  // namespace dtree
+
+using namespace dtree;
+
+extern "C" size_t dtree_tree_build_workspace_bytes(int rows, int vocab, int budget) {
+  (void)budget;
+  if (rows <= 0 || vocab <= 0) return 0;
+  return tree_ws_layout(rows, topk_splits(rows, vocab, kNoCap), nullptr, nullptr);
+}
+
+extern "C" int dtree_tree_build(const float* draft_logits, int rows, int vocab, int budget,
+                                dtree_step_state* state, void* workspace, size_t workspace_bytes,
+                                int32_t* tree_tokens, int32_t* parents, int32_t* depths, int32_t* positions,
+                                uint64_t* anc_mask, int32_t* top_ids, float* top_logprobs, void* stream_) {
+  const int splits = (rows > 0 && vocab > 0) ? topk_splits(rows, vocab, kNoCap) : 1;
+  return tree_build_impl(draft_logits, rows, vocab, budget, state, workspace, workspace_bytes, splits, tree_tokens,
+                         parents, depths, positions, anc_mask, top_ids, top_logprobs,
+                         static_cast<cudaStream_t>(stream_));
 }
 
 extern "C" int dtree_tree_from_topk(const int32_t* top_ids, const float* top_logprobs, int rows, int topk,
@@ -849,7 +873,9 @@ extern "C" int dtree_step_commit(dtree_step_state* state, void* stream_) {
 // process exits.  All calls share it, so calls whose GPU work overlaps (other
 // streams, other threads) race on it and must be serialized by the caller.
 namespace dtree {
-constexpr size_t kNoAllocScratchBytes = 1u << 20;  // 1 MiB: rows <= 64 at any vocab size
+// 1 MiB: draft rows <= 64; the vocabulary limit follows from the split count
+// that fits (dtree_tree_build_noalloc_max_vocab)
+constexpr size_t kNoAllocScratchBytes = 1u << 20;
 static __device__ __align__(256) unsigned char g_tree_scratch[kNoAllocScratchBytes];
 constexpr int kMaxDevices = 64;
 static void* g_tree_scratch_ptr[kMaxDevices] = {};
@@ -857,7 +883,9 @@ static std::mutex g_tree_scratch_mu;
 
 // Device address of g_tree_scratch on the current device.  The host-side
 // symbol is only a stand-in, so the address is looked up once per device,
-// with that device current.
+// with that device current, and cached for the life of the process (a
+// cudaDeviceReset invalidates it: do not reset a device this library has
+// used and then call the no-allocation entry point on it again).
 static int tree_scratch_ptr(void** out) {
   int dev = 0;
   DTREE_CUDA_RET(cudaGetDevice(&dev));
@@ -875,27 +903,45 @@ static int tree_scratch_ptr(void** out) {
 
 extern "C" size_t dtree_tree_build_noalloc_max_bytes(void) { return dtree::kNoAllocScratchBytes; }
 
+extern "C" int dtree_tree_build_noalloc_max_vocab(int rows) {
+  if (rows <= 0 || rows > kMaxRows) return 0;
+  // the largest split count whose workspace fits the scratch, times a CTA's chunk
+  int splits = kTopkMaxSplits;
+  while (splits > 1 && tree_ws_layout(rows, splits, nullptr, nullptr) > kNoAllocScratchBytes) --splits;
+  return splits * kTopkThreads * kTopkElems;
+}
+
 extern "C" int dtree_tree_build_noalloc(const float* draft_logits, int rows, int vocab, int budget,
                                         dtree_step_state* state, int32_t* tree_tokens, int32_t* parents,
                                         int32_t* depths, int32_t* positions, uint64_t* anc_mask, void* stream_) {
   cudaStream_t stream = static_cast<cudaStream_t>(stream_);
-  DTREE_CHECK_ARG(rows >= 0 && rows <= kMaxRows, "rows must be in [0, 64]");
-  DTREE_CHECK_ARG(vocab > 0, "vocab must be positive");
-  const size_t need = dtree_tree_build_workspace_bytes(rows, vocab, budget);
-  if (need > kNoAllocScratchBytes)
-    return fail(kErrCapacity, "dtree_tree_build_noalloc: needs " + std::to_string(need) +
-                                  " bytes of scratch, the fixed device scratch holds " +
-                                  std::to_string(kNoAllocScratchBytes));
-  void* scratch = nullptr;
-  int rc = tree_scratch_ptr(&scratch);
+  // every check comes before the first GPU work, so a rejected call leaves the
+  // shared scratch untouched
+  int rc = tree_build_check(draft_logits, rows, vocab, budget, state, tree_tokens, parents, depths, positions,
+                            anc_mask);
   if (rc) return rc;
-  if (budget > 0 && rows > 0) {
+  const bool heap_only = budget == 0 || rows == 0;
+  const int splits = heap_only ? 1 : topk_splits(rows, vocab, kNoAllocScratchBytes);
+  if (!heap_only) {
+    const size_t need = tree_ws_layout(rows, splits, nullptr, nullptr);
+    const int max_vocab = dtree_tree_build_noalloc_max_vocab(rows);
+    if (need > kNoAllocScratchBytes || vocab > max_vocab)
+      return fail(kErrCapacity, "dtree_tree_build_noalloc: " + std::to_string(rows) + " draft rows of vocab " +
+                                    std::to_string(vocab) + " need more than the fixed " +
+                                    std::to_string(kNoAllocScratchBytes) +
+                                    "-byte device scratch (at most vocab " + std::to_string(max_vocab) +
+                                    " at this row count)");
+  }
+  void* scratch = nullptr;
+  rc = tree_scratch_ptr(&scratch);
+  if (rc) return rc;
+  if (!heap_only) {
     // the per-row arrival counters must start at zero (a completed call leaves
     // them at zero; an interrupted one may not)
     TreeWs ws;
-    tree_ws_layout(rows, topk_splits(rows, vocab), &ws, static_cast<char*>(scratch));
+    tree_ws_layout(rows, splits, &ws, static_cast<char*>(scratch));
     DTREE_CUDA_RET(cudaMemsetAsync(ws.counters, 0, sizeof(uint32_t) * rows, stream));
   }
-  return dtree_tree_build(draft_logits, rows, vocab, budget, state, scratch, kNoAllocScratchBytes, tree_tokens,
-                          parents, depths, positions, anc_mask, nullptr, nullptr, stream_);
+  return tree_build_impl(draft_logits, rows, vocab, budget, state, scratch, kNoAllocScratchBytes, splits,
+                         tree_tokens, parents, depths, positions, anc_mask, nullptr, nullptr, stream);
 }

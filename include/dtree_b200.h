@@ -54,6 +54,13 @@ DTREE_API int dtree_version(void);
  * inputs; 0 = none) after synchronizing the device; clears it if clear != 0. */
 DTREE_API int dtree_device_error(uint32_t* code_out, int clear);
 
+/* Test support, no counterpart in the reference: stores `value` to the device
+ * int at `dst` about delay_ns after launch, while letting the next kernel on
+ * the stream start early (programmatic dependent launch).  Used to make a
+ * kernel observe a decode-state field change between its early read and its
+ * dependency wait. */
+DTREE_API int dtree_test_delayed_store(int32_t* dst, int32_t value, int delay_ns, void* stream);
+
 /* ---------------------------------------------------------- decode state
  * Per-sequence decode bookkeeping kept in device memory so that a whole
  * decode step can run (and be graph-replayed) without a host round trip.
@@ -98,13 +105,16 @@ DTREE_API int dtree_tree_build(const float* draft_logits, int rows, int vocab, i
  * buffers it already owns).  No counterpart in the reference, which builds
  * the tree on the host.  The scratch is a fixed 1 MiB device array inside
  * the library (dtree_tree_build_noalloc_max_bytes()), held by every GPU that
- * loads the library until the process exits; sizes needing more scratch
- * (dtree_tree_build_workspace_bytes() above the limit) are rejected with
- * DTREE_ERR_CAPACITY.  The first call on a device looks up the scratch
- * address for that device; make that first call before any stream capture.
- * All calls share the scratch and it keeps the last call's contents: calls
- * whose GPU work overlaps (other streams or threads) race on it. */
+ * loads the library until the process exits.  It bounds the vocabulary:
+ * dtree_tree_build_noalloc_max_vocab(rows) (about 344k at 64 draft rows,
+ * 1.4M at 16); larger sizes are rejected with DTREE_ERR_CAPACITY before any
+ * GPU work.  The first call on a device looks up the scratch address for
+ * that device and caches it for the life of the process (it does not survive
+ * a cudaDeviceReset); make that first call before any stream capture.  All
+ * calls share the scratch and it keeps the last call's contents: calls whose
+ * GPU work overlaps (other streams or threads) race on it. */
 DTREE_API size_t dtree_tree_build_noalloc_max_bytes(void);
+DTREE_API int dtree_tree_build_noalloc_max_vocab(int rows);
 DTREE_API int dtree_tree_build_noalloc(const float* draft_logits, int rows, int vocab, int budget,
                                        dtree_step_state* state, int32_t* tree_tokens, int32_t* parents,
                                        int32_t* depths, int32_t* positions, uint64_t* anc_mask, void* stream);

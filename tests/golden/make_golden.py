@@ -380,4 +380,6 @@ def main(reference: str) -> None:
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    if len(sys.argv) != 2:
+        sys.exit(f"usage: python {Path(__file__).name} <path to a dtree-mlx source checkout>")
+    main(sys.argv[1])

@@ -56,7 +56,8 @@ def _reference(q, k_plane, v_plane, start, n, masks, n_q_heads):
 
 @pytest.mark.parametrize("heads", [(32, 8, 128), (8, 4, 64), (16, 4, 256)])
 @pytest.mark.parametrize("start,n,splits", [(0, 1, 0), (5, 25, 0), (200, 64, 0), (2048, 25, 0), (3000, 25, 0),
-                                            (2048, 25, 3), (777, 7, 0)])
+                                            (2048, 25, 3), (777, 7, 0), (2048, 65, 0), (8192, 65, 0),
+                                            (8192, 25, 0), (513, 100, 0), (8192, 128, 0), (0, 128, 0)])
 def test_tree_attention_matches_fp32(lib, heads, start, n, splits):
     from dtree_mlx_b200 import kernels
 
@@ -78,3 +79,44 @@ def test_tree_attention_matches_fp32(lib, heads, start, n, splits):
     assert torch.isfinite(out.float()).all()
     err = (out.float() - ref).abs().max().item()
     assert err <= 2e-2, f"max abs err {err}"
+
+
+@pytest.mark.parametrize("p_early,p_late", [(3000, 2048), (1024, 2900), (2047, 2048)])
+def test_tree_attention_start_changed_upstream(lib, p_early, p_late):
+    """The attention kernel reads `start` before its dependency wait to begin
+    loading K/V early; when a kernel still running upstream changes `start`,
+    the early load must land unused and the result must be the one for the
+    new prefix.  Cache rows past the live keys hold NaN, so a zeroed V tail
+    overwritten by a late load would show up as a non-finite output."""
+    from dtree_mlx_b200 import _lib, kernels
+
+    n_q, n_kv, hd, n = 32, 8, 128, 25
+    dev = torch.device("cuda")
+    gen = torch.Generator().manual_seed(p_early + p_late)
+    cap = max(p_early, p_late) + n + 200
+    k_plane = torch.randn(n_kv, cap, hd, generator=gen).to(torch.bfloat16)
+    v_plane = torch.randn(n_kv, cap, hd, generator=gen).to(torch.bfloat16)
+    k_plane[:, p_late + n:] = float("nan")
+    v_plane[:, p_late + n:] = float("nan")
+    q = torch.randn(n, n_q * hd, generator=gen).to(torch.bfloat16)
+    masks, anc = _random_tree(n, gen)
+    k_plane, v_plane, q, anc = k_plane.to(dev), v_plane.to(dev), q.to(dev), anc.to(dev)
+    state = kernels.new_state(dev, start=p_early)
+    out = torch.empty(n, n_q * hd, dtype=torch.bfloat16, device=dev)
+    nbytes = int(lib.dtree_tree_attention_workspace_bytes(n_q, n, hd, 0))
+    ws = torch.zeros(nbytes, dtype=torch.uint8, device=dev)
+    torch.cuda.synchronize()
+    st = _lib.stream_ptr()
+    for _ in range(3):  # the store lands ~30 us after the attention kernel started
+        state[0] = p_early
+        _lib.call("dtree_test_delayed_store", state.data_ptr(), p_late, 30000, st)
+        _lib.call("dtree_tree_attention", q.data_ptr(), q.stride(0), k_plane.data_ptr(), v_plane.data_ptr(), cap,
+                  n_q, n_kv, hd, n, state.data_ptr(), anc.data_ptr(), out.data_ptr(), 0, ws.data_ptr(),
+                  ws.numel(), st)
+        torch.cuda.synchronize()
+        assert int(state[0].item()) == p_late
+        ref = _reference(q, k_plane, v_plane, p_late, n, masks, n_q)
+        assert torch.isfinite(out.float()).all()
+        err = (out.float() - ref).abs().max().item()
+        assert err <= 2e-2, f"max abs err {err}"
+    assert _lib.device_error() == 0

@@ -111,6 +111,27 @@ def test_tree_build_random_vs_oracle(K, budget):
         assert g_toks[1:] == toks and g_parents == parents and g_depths[1:] == depths
 
 
+def test_tree_build_vocab_beyond_the_noalloc_scratch(K, lib):
+    """The workspace build has no 1 MiB cap: 64 draft rows over a vocabulary
+    larger than the no-allocation scratch covers still match the oracle."""
+    rows, vocab, budget = 64, 400_000, 24
+    assert vocab > int(lib.dtree_tree_build_noalloc_max_vocab(rows))
+    rng = np.random.default_rng(7)
+    lg = (rng.standard_normal((rows, vocab)) * 2).astype(np.float32)
+    lg[:, rng.integers(vocab, size=4)] += 6.0
+    state = K.new_state(DEV, start=3, root_token=1)
+    tb = K.TreeBuilder(rows, vocab, budget, DEV)
+    out = K.TreeBuffers.allocate(DEV)
+    tb.build(torch.from_numpy(lg).to(DEV), state, out)
+    ids = tb.top_ids[:rows, :budget].cpu().numpy().astype(np.int64)
+    ref_ids, _ = OT.topk_log_probs(lg, budget)
+    assert np.array_equal(ids, ref_ids)
+    toks, depths, parents, _ = OT.heap_build(ids, tb.top_lp[:rows, :budget].cpu().numpy(), budget)
+    n = int(state[6].item())
+    g_toks, g_parents, _, _ = _tree_lists(out, n)
+    assert g_toks[1:] == toks and g_parents == parents
+
+
 def test_tree_build_ties_by_token_id(K):
     lg = np.zeros((4, 300), dtype=np.float32)
     lg[:, [7, 250, 3, 99]] = 5.0  # exact ties across chunks
@@ -170,8 +191,6 @@ def test_kv_compact_matches_reference(K, golden_dir):
         meta = z[f"c{c}_meta"].tolist()
         past, t, nkeep = meta[:3]
         keep = meta[3:3 + nkeep]
-        if nkeep == 0:
-            continue  # the device path always keeps the root
         ks = [torch.from_numpy(z[f"c{c}_k_in_{li}"][0]) for li in range(2)]
         vs = [torch.from_numpy(z[f"c{c}_v_in_{li}"][0]) for li in range(2)]
         cache = torch.stack([torch.stack([ks[li], vs[li]]) for li in range(2)]).to(torch.bfloat16).to(DEV).contiguous()
@@ -179,7 +198,11 @@ def test_kv_compact_matches_reference(K, golden_dir):
         state[3] = nkeep
         acc = torch.tensor(keep + [0] * (128 - nkeep), dtype=torch.int32, device=DEV)
         K.kv_compact(cache, acc, state)
+        K.step_commit(state)
         got = cache.cpu()
+        # the committed length is the reference's new cache offset (past when
+        # nothing is kept: the rows stay, the offset is trimmed)
+        assert int(state[0].item()) == int(z[f"c{c}_offset_0"])
         for li in range(2):
             ek = torch.from_numpy(z[f"c{c}_k_out_{li}"][0]).to(torch.bfloat16)
             ev = torch.from_numpy(z[f"c{c}_v_out_{li}"][0]).to(torch.bfloat16)

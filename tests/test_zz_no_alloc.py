@@ -72,3 +72,14 @@ def test_noalloc_rejects_oversized_requests(lib):
     rc = lib.dtree_tree_build_noalloc(st, 65, 1000, 8, st, st, st, st, st, st, None)
     assert rc == -1 and "rows" in _lib.last_error()
     assert int(lib.dtree_tree_build_noalloc_max_bytes()) == 1 << 20
+
+
+def test_noalloc_rejects_vocab_beyond_the_scratch(lib):
+    """The fixed scratch bounds the vocabulary (per draft-row count); a larger
+    one is refused with DTREE_ERR_CAPACITY before any GPU work."""
+    st = C.c_void_p(1)
+    vmax = int(lib.dtree_tree_build_noalloc_max_vocab(64))
+    assert 300_000 < vmax < 400_000
+    assert int(lib.dtree_tree_build_noalloc_max_vocab(16)) > vmax
+    rc = lib.dtree_tree_build_noalloc(st, 64, vmax + 1, 24, st, st, st, st, st, st, None)
+    assert rc == -4 and "vocab" in _lib.last_error()
