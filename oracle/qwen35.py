@@ -137,15 +137,19 @@ class Qwen35Oracle:
     custom_qwen35_model.py:823-891: no per-step state rounding) and
     commit_qwen35_tree_path (:708-732).  Node states of the tree mode are
     rounded to bf16 per node as the reference's tree kernel does for bf16
-    inputs; everything else is fp32 on the same bf16 weights.
+    inputs (``state_dtype="f32"``: kept in fp32, as it does for an fp32
+    model); everything else is fp32 on the same bf16 weights.
 
     ``bf16_acts=True`` additionally rounds every activation to bf16 where a
     bf16 MLX model materializes it (projection outputs, norms, conv and
     gated-delta outputs, gates, residual adds), which separates rounding
     noise from real differences when checking a bf16 implementation."""
 
-    def __init__(self, weights, kv_capacity: int, bf16_acts: bool = False):
+    def __init__(self, weights, kv_capacity: int, bf16_acts: bool = False, state_dtype: str = "bf16"):
         self.bf16_acts = bool(bf16_acts)
+        # tree-mode node states are kept in the model's dtype by the
+        # reference's kernel: bf16 for the bf16 engine, fp32 for an fp32 model
+        self.state_dtype = state_dtype
         import torch
 
         self.w = weights.to("cpu") if weights.device.type != "cpu" else weights
@@ -217,7 +221,8 @@ class Qwen35Oracle:
             g = compute_g(L["A_log"].numpy(), a, L["dt_bias"].numpy())
         beta = r(sigmoid(b))
         y, states = tree_gated_delta(q, k, v, g, beta, self.rec[l], parents,
-                                     dtype="bf16" if (tree or self.bf16_acts) else "f32")
+                                     dtype="bf16" if ((tree and self.state_dtype == "bf16") or self.bf16_acts)
+                                     else "f32")
         if not tree:  # sequence mode: the state is not rounded per step
             _, states = tree_gated_delta(q, k, v, g, beta, self.rec[l], parents, dtype="f32")
         zz = z.reshape(T, -1, Dv)
