@@ -72,7 +72,11 @@ def _dense(t):
 class Qwen3Oracle:
     """fp32 CPU model over a ``Qwen3Weights`` (weights are copied to CPU)."""
 
-    def __init__(self, weights, kv_capacity: int):
+    def __init__(self, weights, kv_capacity: int, bf16_acts: bool = False):
+        # bf16_acts: round every activation a bf16 model materializes (norm
+        # outputs, projections, attention output, SwiGLU, residual stream) to
+        # bf16 -- an estimate of the bf16 rounding noise floor, not a bar
+        self.bf16_acts = bool(bf16_acts)
         self.w = weights.to("cpu") if weights.device.type != "cpu" else weights
         self.cfg = self.w.cfg
         c = self.cfg
@@ -88,15 +92,16 @@ class Qwen3Oracle:
         c = self.cfg
         L = self.layers[i]
         T = h.shape[0]
-        x = rms_norm(h, L["input_layernorm"], c.rms_norm_eps)
-        q = x @ L["q_proj"].float().t()
-        k = x @ L["k_proj"].float().t()
-        v = x @ L["v_proj"].float().t()
-        q = rms_norm(q.view(T, c.num_attention_heads, c.head_dim), L["q_norm"], c.rms_norm_eps)
-        k = rms_norm(k.view(T, c.num_key_value_heads, c.head_dim), L["k_norm"], c.rms_norm_eps)
+        r = self._r
+        x = r(rms_norm(h, L["input_layernorm"], c.rms_norm_eps))
+        q = r(x @ L["q_proj"].float().t())
+        k = r(x @ L["k_proj"].float().t())
+        v = r(x @ L["v_proj"].float().t())
+        q = r(rms_norm(q.view(T, c.num_attention_heads, c.head_dim), L["q_norm"], c.rms_norm_eps))
+        k = r(rms_norm(k.view(T, c.num_key_value_heads, c.head_dim), L["k_norm"], c.rms_norm_eps))
         v = v.view(T, c.num_key_value_heads, c.head_dim)
-        q = apply_rope(q, positions, c.rope_theta)
-        k = apply_rope(k, positions, c.rope_theta)
+        q = r(apply_rope(q, positions, c.rope_theta))
+        k = r(apply_rope(k, positions, c.rope_theta))
         # new K/V appended after the prefix (cache.update_and_fetch, qwen3_tree.py:146)
         self.k[i][:, past : past + T] = k.transpose(0, 1)
         self.v[i][:, past : past + T] = v.transpose(0, 1)
@@ -108,13 +113,16 @@ class Qwen3Oracle:
         qh = q.transpose(0, 1)  # [Hq, T, d]
         scores = (qh @ keys.transpose(1, 2)) / math.sqrt(c.head_dim)
         scores = scores.masked_fill(~mask[None, :, :], float("-inf"))
-        attn = torch.softmax(scores, dim=-1) @ vals  # [Hq, T, d]
-        h = h + attn.transpose(0, 1).reshape(T, c.q_dim) @ L["o_proj"].float().t()
-        x = rms_norm(h, L["post_attention_layernorm"], c.rms_norm_eps)
-        gate = x @ L["gate_proj"].float().t()
-        up = x @ L["up_proj"].float().t()
-        h = h + (torch.nn.functional.silu(gate) * up) @ L["down_proj"].float().t()
+        attn = r(torch.softmax(scores, dim=-1) @ vals)  # [Hq, T, d]
+        h = r(h + r(attn.transpose(0, 1).reshape(T, c.q_dim) @ L["o_proj"].float().t()))
+        x = r(rms_norm(h, L["post_attention_layernorm"], c.rms_norm_eps))
+        gate = r(x @ L["gate_proj"].float().t())
+        up = r(x @ L["up_proj"].float().t())
+        h = r(h + r(r(torch.nn.functional.silu(gate)) * up) @ L["down_proj"].float().t())
         return h
+
+    def _r(self, x: torch.Tensor) -> torch.Tensor:
+        return x.to(torch.bfloat16).float() if self.bf16_acts else x
 
     def forward_tree(self, tokens, positions, mask, past: int, layer_ids=()):
         """tokens/positions [T] ints, mask bool [T, past+T].  Writes the new K/V at
@@ -130,7 +138,7 @@ class Qwen3Oracle:
             h = self._block(i, h, positions, mask, past)
             if i in ids:
                 picked.append(h.clone())
-        norm_h = rms_norm(h, self.w.final_norm, c.rms_norm_eps)
+        norm_h = self._r(rms_norm(h, self.w.final_norm, c.rms_norm_eps))
         vh = torch.cat(picked, dim=-1) if picked else h[:, :0]
         self.offset = past + len(tokens)
         return norm_h, vh

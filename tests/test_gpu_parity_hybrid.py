@@ -1,0 +1,124 @@
+"""Parity of the Qwen3.5 hybrid at the real layer shapes: four layers of the
+config-4 model (three gated DeltaNet layers, then one gated full-attention
+layer; hidden 4096, DeltaNet 16 / 32 heads of 128, attention 16 / 4 heads of
+256, FFN 12288, vocab 248320) on the GPU against the fp32 CPU oracle (pinned
+to transformers' Qwen3.5 in tests/test_oracle_pin.py): a 256-token prefill,
+then a budget-24 tree verify and the commit of its accepted path.
+
+Tolerances (fixed; bf16 engine vs fp32 oracle, tree node states rounded to
+bf16 per node in both, as the reference's kernel does for a bf16 model):
+  logits             max |d| <= 0.35, mean <= 0.04   (logit std ~1.3)
+  norm output        relative Frobenius error <= 3e-2
+  conv / recurrent states, new K/V   relative error <= 3e-2
+(The oracle with every activation rounded to bf16 differs from the fp32 one
+by max 0.21 / mean 0.026 on this model: bf16 rounding noise.)
+Posterior tokens equal the oracle's argmax except at near-ties (both within
+0.35 of the row maximum).
+"""
+from __future__ import annotations
+
+import dataclasses
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import tree as OT
+from oracle.qwen35 import Qwen35Oracle
+from oracle.runtime import near_tie
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+LOGIT_MAX = 0.35
+LOGIT_MEAN = 0.04
+REL = 3e-2
+
+
+def _rel(a, b):
+    a = torch.as_tensor(np.asarray(a.float().cpu() if torch.is_tensor(a) else a)).double()
+    b = torch.as_tensor(np.asarray(b.float().cpu() if torch.is_tensor(b) else b)).double()
+    return float((a - b).norm() / max(float(b.norm()), 1e-30))
+
+
+def test_hybrid_real_shape_prefill_verify_commit(lib):
+    from dtree_mlx_b200 import _lib, kernels
+    from dtree_mlx_b200.config import QWEN35_PRESETS
+    from dtree_mlx_b200.engine import chain_anc_masks, mask_to_anc
+    from dtree_mlx_b200.engine35 import Qwen35Engine
+    from dtree_mlx_b200.synthetic import random_qwen35_weights
+
+    cfg = dataclasses.replace(QWEN35_PRESETS["qwen35-9b"], num_hidden_layers=4)
+    w = random_qwen35_weights(cfg, seed=0, device=DEV, norm_jitter=0.1)
+    eng = Qwen35Engine(w, kv_capacity=512)
+    orc = Qwen35Oracle(w, kv_capacity=512)
+    rng = np.random.default_rng(0)
+    P = 256
+    prompt = rng.integers(cfg.vocab_size, size=P).tolist()
+    tok = lambda a: torch.as_tensor(np.asarray(a), dtype=torch.int32, device=DEV)  # noqa: E731
+    post = torch.zeros(128, dtype=torch.int32, device=DEV)
+    eng.reset_states()
+    for s in range(0, P, 128):  # prefill in chunks of 128 rows (sequence mode)
+        st = kernels.new_state(DEV, start=s)
+        eng.prefill_chunk(tok(prompt[s:s + 128]), tok(np.arange(s, s + 128)),
+                          torch.from_numpy(chain_anc_masks(128).view(np.int64)).to(DEV), 128, st, post)
+    torch.cuda.synchronize()
+    o_norm, _ = orc.prefill(prompt)
+    rel = _rel(eng.norm_out[:128], o_norm[P - 128:])
+    print(f"prefill: last chunk norm_out rel {rel:.2e}")
+    assert rel <= REL
+    lin = [l for l in range(cfg.num_hidden_layers) if cfg.is_linear(l)]
+    for li, l in enumerate(lin):
+        assert _rel(eng.conv_state[li], orc.conv[l]) <= REL, ("conv", l)
+        assert _rel(eng.rec_state[li], orc.rec[l]) <= REL, ("rec", l)
+    assert _rel(eng.kv_cache[0, 0, :, :P], orc.k[3][:, :P]) <= REL
+    assert _rel(eng.kv_cache[0, 1, :, :P], orc.v[3][:, :P]) <= REL
+
+    root = int(post[127].item())
+    dl = (rng.standard_normal((15, cfg.vocab_size)) * 2).astype(np.float32)
+    node_tokens, node_depths, parents, child_maps, vis = OT.build_dtree_tree(dl, 24)
+    ids, pos = OT.compile_dtree_tree(root, P, node_tokens, node_depths)
+    toks, positions = ids.astype(np.int32).tolist(), pos.astype(np.int32).tolist()
+    T = len(toks)
+    st = kernels.new_state(DEV, start=P, root_token=root)
+    eng.forward(tok(toks), tok(positions), tok(parents), torch.from_numpy(mask_to_anc(vis).view(np.int64)).to(DEV),
+                T, st, post, mode=0)
+    torch.cuda.synchronize()
+    x = torch.zeros(32, cfg.hidden_size, dtype=torch.bfloat16, device=DEV)
+    x[:T] = eng.norm_out[:T]
+    g_log = kernels.linear_bf16(x, w.embed)[:T].float().cpu()
+    o_norm, _ = orc.forward(toks, positions, parents, OT.tree_attention_mask(vis, P), P, tree=True)
+    o_log = orc.lm_head_logits(o_norm)
+    err = (g_log - o_log).abs()
+    rel = _rel(eng.norm_out[:T], o_norm)
+    print(f"tree verify T={T}: logits max {err.max():.4f} mean {err.mean():.5f}, norm_out rel {rel:.2e}")
+    assert err.max() <= LOGIT_MAX and err.mean() <= LOGIT_MEAN and rel <= REL
+    gpost = post[:T].tolist()
+    near = 0
+    for t in range(T):
+        ref = int(torch.argmax(o_log[t].to(torch.bfloat16).float()))
+        if gpost[t] != ref:
+            assert near_tie(o_log[t], gpost[t], ref, LOGIT_MAX), t
+            near += 1
+    print(f"posterior near-tie mismatches {near}/{T}")
+
+    accepted, _ = OT.follow_verified_tree(child_maps, gpost)
+    if len(accepted) < 3:  # commit a deeper path than the random drafts reach
+        leaf = max(range(T), key=lambda i: node_depths[i - 1] if i > 0 else 0)
+        path = [leaf]
+        while parents[path[-1]] >= 0:
+            path.append(parents[path[-1]])
+        accepted = path[::-1]
+    acc = torch.zeros(128, dtype=torch.int32, device=DEV)
+    acc[: len(accepted)] = torch.tensor(accepted, dtype=torch.int32)
+    st[3] = len(accepted)
+    eng.commit(tok(parents), acc, st)
+    torch.cuda.synchronize()
+    orc.commit(accepted)
+    for li, l in enumerate(lin):
+        assert _rel(eng.conv_state[li], orc.conv[l]) <= REL, ("commit conv", l)
+        assert _rel(eng.rec_state[li], orc.rec[l]) <= REL, ("commit rec", l)
+    n = len(accepted)
+    assert _rel(eng.kv_cache[0, 0, :, P:P + n], orc.k[3][:, P:P + n]) <= REL
+    print(f"committed path of {n} nodes")
+    assert _lib.device_error() == 0
+    eng.close()
