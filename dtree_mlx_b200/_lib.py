@@ -106,6 +106,7 @@ class Qwen3Desc(C.Structure):
         ("quant_bits", C.c_int),
         ("group_size", C.c_int),
         ("q4_layer", C.POINTER(Qwen3Q4Layer)),
+        ("verify_path", C.c_int),
     ]
 
 

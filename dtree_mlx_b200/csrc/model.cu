@@ -22,6 +22,7 @@
 #include <vector>
 
 #include "attention.cuh"
+#include "fused.cuh"
 #include "gemm.cuh"
 #include "qkv.cuh"
 
@@ -66,6 +67,9 @@ struct dtree_qwen3_model {
   void* attn_ws = nullptr;
   size_t attn_ws_bytes = 0;
   float* proj_partials = nullptr;  // [kMaxProjSplit][t_pad][hidden] fp32
+  void* fused_ws = nullptr;        // persistent-forward region (nullptr: not supported)
+  dtree::FusedPlan fused[3];       // t_pad 16 / 32 / 64
+  bool fused_ready[3] = {false, false, false};
 };
 
 namespace dtree {
@@ -156,7 +160,8 @@ extern "C" int dtree_qwen3_buffer_bytes(const dtree_qwen3_desc* d, size_t out[9]
   out[6] = tc * d->hidden * 2;
   out[7] = tc * d->hidden * (d->n_capture > 0 ? d->n_capture : 1) * 2;
   out[8] = ((gemm_ws_need(*d) + 255) & ~static_cast<size_t>(255)) +
-           ((attn_ws_need(*d) + 255) & ~static_cast<size_t>(255)) + partials_need(*d);
+           ((attn_ws_need(*d) + 255) & ~static_cast<size_t>(255)) + ((partials_need(*d) + 255) & ~static_cast<size_t>(255)) +
+           fused_ws_bytes(*d);
   return kOk;
 }
 
@@ -205,6 +210,17 @@ extern "C" int dtree_qwen3_create(const dtree_qwen3_desc* desc, dtree_qwen3_mode
   m->attn_ws_bytes = attn_ws_need(d);
   m->proj_partials = reinterpret_cast<float*>(static_cast<char*>(m->attn_ws) +
                                               ((m->attn_ws_bytes + 255) & ~static_cast<size_t>(255)));
+  if (d.verify_path == 0 && fused_supported(d)) {
+    m->fused_ws = reinterpret_cast<char*>(m->proj_partials) + ((partials_need(d) + 255) & ~static_cast<size_t>(255));
+    std::vector<std::pair<int, __nv_bfloat16*>> caps;
+    for (int c = 0; c < d.n_capture; ++c)
+      caps.emplace_back(d.capture_layers[c], static_cast<__nv_bfloat16*>(d.capture) + static_cast<size_t>(c) * d.hidden);
+    int rc = fused_init(d, m->fused_ws, caps.data(), static_cast<int>(caps.size()));
+    if (rc) {
+      delete m;
+      return rc;
+    }
+  }
   *out = m;
   return kOk;
 }
@@ -321,6 +337,23 @@ static int forward_impl(dtree_qwen3_model* m, const int32_t* tree_tokens, const 
     return nullptr;
   };
 
+  if (m->fused_ws && !logits && t_pad <= 64) {
+    // the whole layer stack in one persistent launch, then the LM head
+    const int fi = t_pad == 16 ? 0 : (t_pad == 32 ? 1 : 2);
+    if (!m->fused_ready[fi]) {
+      if ((rc = fused_plan(d, m->fused_ws, t_pad, &m->fused[fi]))) return rc;
+      m->fused_ready[fi] = true;
+    }
+    if ((rc = fused_launch(m->fused[fi], tree_tokens, positions, anc_mask, n_nodes, state, st))) return rc;
+    if (posterior) {
+      GemmPlan g = ps.lm;
+      g.p.n_rows = n_nodes;
+      g.p.vocab = d.vocab;
+      g.p.argmax_out = posterior;
+      if ((rc = gemm_launch(g, st))) return rc;
+    }
+    return kOk;
+  }
   // embedding gather + first input norm
   if ((rc = rmsnorm_launch(nullptr, 0, tree_tokens, bf(d.embed), bw(d.h), bf(m->layers[0].input_norm), bw(d.xn),
                            d.hidden, n_nodes, t_pad, d.rms_eps, st)))

@@ -8,12 +8,14 @@ prefixes are random bf16 (std 1) written identically to both caches.
 
 Tolerances (fixed; bf16 engine vs fp32 oracle on the same bf16 weights):
   logits   max |gpu - oracle| <= 0.40, mean <= 0.06   (logit std ~1.0)
-  hidden   relative Frobenius error of the final norm output <= 4e-2
+  hidden   relative Frobenius error of the final norm output and of the
+           captured verifier hiddens <= 8e-2
   new K/V  relative Frobenius error per layer <= 4e-2
-At this depth bf16 rounding alone moves the logits this much: the same oracle
-with every activation rounded to bf16 where a bf16 model materializes it
-differs from the fp32 oracle by max 0.25 / mean 0.038 at T=25, P=2048, so
-the reference's own bf16 model could not meet a tighter bar either.
+At this depth bf16 rounding alone moves the results this much: the same
+oracle with every activation rounded to bf16 where a bf16 model materializes
+it differs from the fp32 oracle by logits max 0.25 / mean 0.038, norm output
+4.6e-2 and captured hiddens 3.9e-2 (relative) at T=25, P=2048, so the
+reference's own bf16 model could not meet a tighter bar either.
 Posterior tokens must equal the oracle's bf16 argmax except at near-ties
 (both within 0.40 of the row maximum), which are counted and printed; tree
 topology and acceptance / compaction indices are compared bit-exactly.
@@ -32,6 +34,7 @@ pytestmark = pytest.mark.gpu
 DEV = "cuda"
 LOGIT_MAX = 0.40
 LOGIT_MEAN = 0.06
+REL_HIDDEN = 8e-2
 REL = 4e-2
 CAP = 8192 + 128 + 64
 
@@ -110,7 +113,7 @@ def test_verify_forward_full_shape(pair, P, budget):
     print(f"P={P} T={n}: logits max {err.max():.4f} mean {err.mean():.5f}; norm_out rel {rel_h:.2e}, "
           f"captured hidden rel {rel_c:.2e}")
     assert err.max() <= LOGIT_MAX and err.mean() <= LOGIT_MEAN
-    assert rel_h <= REL and rel_c <= REL
+    assert rel_h <= REL_HIDDEN and rel_c <= REL_HIDDEN
     for l in (0, 17, 35):
         assert _rel(eng.kv_cache[l, 0, :, P:P + n], orc.k[l][:, P:P + n]) <= REL, l
         assert _rel(eng.kv_cache[l, 1, :, P:P + n], orc.v[l][:, P:P + n]) <= REL, l
