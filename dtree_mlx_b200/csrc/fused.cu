@@ -133,12 +133,31 @@ __device__ __forceinline__ void gbar(int g) {  // one 128-thread half of the com
   asm volatile("bar.sync %0, 128;" ::"r"(2 + g) : "memory");
 }
 
+// compute-warp barrier that also ANDs / ORs a predicate over its threads
+__device__ __forceinline__ bool cbar_and(bool v) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.u32 p, %1, 0;\n\tbar.red.and.pred p, 1, 256, p;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(r)
+      : "r"(v ? 1u : 0u)
+      : "memory");
+  return r != 0;
+}
+__device__ __forceinline__ bool cbar_or(bool v) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.u32 p, %1, 0;\n\tbar.red.or.pred p, 1, 256, p;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(r)
+      : "r"(v ? 1u : 0u)
+      : "memory");
+  return r != 0;
+}
 // compute warps: one thread waits, the rest follow; result uniform
 __device__ __forceinline__ bool cwait(const uint32_t* cnt, uint32_t target, uint32_t* abort_word, unsigned where,
-                                      int ct, int* s_ok) {
-  if (ct == 0) *s_ok = wait_count(cnt, target, abort_word, where) ? 1 : 0;
-  cbar();
-  return *s_ok != 0;
+                                      int ct) {
+  bool ok = true;
+  if (ct == 0) ok = wait_count(cnt, target, abort_word, where);
+  return cbar_and(ok);
 }
 // compute warps: every thread's writes are done; one thread publishes
 __device__ __forceinline__ void csignal(uint32_t* cnt, int ct) {
@@ -206,7 +225,12 @@ __device__ void fused_norm_row(const FusedParams& p, int row, const float* part,
   uint4 hv0 = make_uint4(0, 0, 0, 0), hv1 = hv0;
   float ss = 0.0f;
   __nv_bfloat16* hrow = p.h + static_cast<size_t>(row) * H;
-  const __nv_bfloat16* src = embed_row ? p.embed + static_cast<size_t>(p.tokens[row]) * H : hrow;
+  int tok = embed_row ? p.tokens[row] : 0;
+  if (tok < 0 || tok >= p.vocab) {
+    if (ct == 0) dev_error(0x2002u);
+    tok = 0;
+  }
+  const __nv_bfloat16* src = embed_row ? p.embed + static_cast<size_t>(tok) * H : hrow;
 #pragma unroll 1
   for (int k = 0; k < 2; ++k) {
     const int i = ct + k * 256;
@@ -404,7 +428,7 @@ __device__ void fused_att_task(const FusedParams& p, int l, int kvh, int rbi, in
   const int kps = att_kps(L, p.att_splits);
   const int k_begin = sp * kps;
   if (k_begin >= L) return;  // uniform over the CTA
-  const int k_end = min(L, k_begin + kps);
+  const int k_end = min(min(L, k_begin + kps), p.kv_cap);  // (P + T > kv_cap is flagged by the K/V write)
   const int n_chunks = (k_end - k_begin + kAttChunk - 1) / kAttChunk;
   const size_t plane = static_cast<size_t>(p.n_kv_heads) * p.kv_cap * 128;
   const __nv_bfloat16* kpl = p.kv + static_cast<size_t>(l) * 2 * plane + static_cast<size_t>(kvh) * p.kv_cap * 128;
@@ -629,9 +653,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
   uint64_t* tfull = empty_bar + S;
   uint64_t* tempty = tfull + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
-  int* s_ok = reinterpret_cast<int*>(tmem_slot + 1);
-  int* s_flag = s_ok + 1;
-  float* red = reinterpret_cast<float*>(s_flag + 3);  // [8] (16-byte aligned: misc + 8*(2S+4) + 16)
+  float* red = reinterpret_cast<float*>(tmem_slot + 4);  // [8]
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int c = blockIdx.x;
@@ -691,10 +713,6 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
           }
         }
       }
-      if (!ok) {  // let every load in flight land before the CTA can retire
-        const uint64_t t0 = gtimer();
-        while (gtimer() - t0 < 200000ull) __nanosleep(1000);
-      }
     }
   } else if (warp == 1) {
     // ---------------------------------------------------------------- activations
@@ -733,10 +751,6 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
           }
         }
       }
-      if (!ok) {
-        const uint64_t t0 = gtimer();
-        while (gtimer() - t0 < 200000ull) __nanosleep(1000);
-      }
     }
   } else if (warp == 2) {
     // ---------------------------------------------------------------- MMA
@@ -774,10 +788,6 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
           }
         }
       }
-      if (!ok) {  // let issued MMAs finish before the accumulators are freed
-        const uint64_t t0 = gtimer();
-        while (gtimer() - t0 < 200000ull) __nanosleep(1000);
-      }
     }
   } else if (warp >= 4) {
     // ---------------------------------------------------------------- compute
@@ -801,9 +811,9 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
       const FJob J = fused_job(p, j);
       for (int q = 0; q < ns && ok; ++q, ++seg) {
         const int b = seg & 1, use = seg >> 1;
-        if (ct == 0) *s_ok = mbar_wait_ab(&tfull[b], static_cast<uint32_t>(use) & 1u, abort_word, 5) ? 1 : 0;
-        cbar();
-        ok = *s_ok != 0;
+        bool w_ok = true;
+        if (ct == 0) w_ok = mbar_wait_ab(&tfull[b], static_cast<uint32_t>(use) & 1u, abort_word, 5);
+        ok = cbar_and(w_ok);
         if (!ok) break;
         tc_fence_after();
         const uint32_t taddr = tmem_base + (static_cast<uint32_t>(qd * 32) << 16) + static_cast<uint32_t>(b * TPAD);
@@ -854,7 +864,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
           cap = nullptr;
           sig = cnt(l, kCntN2);
         }
-        if (wc) ok = cwait(wc, static_cast<uint32_t>(G), abort_word, 0x20 + half, ct, s_ok);
+        if (wc) ok = cwait(wc, static_cast<uint32_t>(G), abort_word, 0x20 + half, ct);
         if (!ok) break;
         for (int r = c; r < p.n_rows; r += G) {
           fused_norm_row<TPAD>(p, r, part, split, w, out, cap, step == 0, ct, red);
@@ -872,7 +882,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
         const int sp = c % p.att_splits;
         const int kvh = c / (p.att_rb * p.att_splits);
         const int kps = att_kps(start + p.n_rows, p.att_splits);
-        const int lo = sp * kps, hi = min(start, lo + kps);
+        const int lo = sp * kps, hi = min(min(start, lo + kps), p.kv_cap);
         if (hi > lo) {
           const size_t plane = static_cast<size_t>(Hkv) * p.kv_cap * 128;
           const __nv_bfloat16* kpl = p.kv + static_cast<size_t>(l) * 2 * plane + static_cast<size_t>(kvh) * p.kv_cap * 128;
@@ -882,13 +892,13 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
         }
       }
       // ---- FIN: q/k RMSNorm + RoPE, K/V -> cache
-      ok = cwait(cnt(l, kCntQkv), static_cast<uint32_t>(G), abort_word, 0x21, ct, s_ok);
+      ok = cwait(cnt(l, kCntQkv), static_cast<uint32_t>(G), abort_word, 0x21, ct);
       if (!ok) break;
       for (int it = c * kFusedWarpsCompute + cw; it < p.n_rows * NH; it += G * kFusedWarpsCompute)
         fused_fin_item<TPAD>(p, l, it / NH, it % NH, start, lane);
       csignal(cnt(l, kCntFin), ct);
       // ---- ATT
-      ok = cwait(cnt(l, kCntFin), static_cast<uint32_t>(G), abort_word, 0x22, ct, s_ok);
+      ok = cwait(cnt(l, kCntFin), static_cast<uint32_t>(G), abort_word, 0x22, ct);
       if (!ok) break;
       for (int task = c; task < tasks_att; task += G) {
         const int kvh = task / (p.att_rb * p.att_splits);
@@ -897,7 +907,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
       }
       csignal(cnt(l, kCntAtt), ct);
       // ---- CMB
-      ok = cwait(cnt(l, kCntAtt), static_cast<uint32_t>(G), abort_word, 0x23, ct, s_ok);
+      ok = cwait(cnt(l, kCntAtt), static_cast<uint32_t>(G), abort_word, 0x23, ct);
       if (!ok) break;
       for (int it = c * kFusedWarpsCompute + cw; it < p.n_rows * p.n_heads; it += G * kFusedWarpsCompute)
         fused_cmb_item(p, it / p.n_heads, it % p.n_heads, start, lane);
@@ -917,9 +927,9 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
         const int first_tile = ns > 0 ? sg[0].tile : 0;
         for (int q = 0; q < ns && ok; ++q, ++seg) {
           const int b = seg & 1, use = seg >> 1;
-          if (ct == 0) *s_ok = mbar_wait_ab(&tfull[b], static_cast<uint32_t>(use) & 1u, abort_word, 6) ? 1 : 0;
-          cbar();
-          ok = *s_ok != 0;
+          bool w_ok = true;
+          if (ct == 0) w_ok = mbar_wait_ab(&tfull[b], static_cast<uint32_t>(use) & 1u, abort_word, 6);
+          ok = cbar_and(w_ok);
           if (!ok) break;
           tc_fence_after();
           const uint32_t taddr = tmem_base + (static_cast<uint32_t>(qd * 32) << 16) + static_cast<uint32_t>(b * TPAD);
@@ -942,12 +952,13 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
             cbar();
             c_first = gu_cta_of(static_cast<long long>(tile) * kb, U, G);
             c_last = gu_cta_of(static_cast<long long>(tile) * kb + kb - 1, U, G);
+            bool last = false;
             if (ct == 0) {
+              __threadfence();
               const uint32_t prev = atomicAdd(&p.gu_tile_cnt[tile], 1u);
-              *s_flag = (prev == static_cast<uint32_t>(c_last - c_first)) ? 1 : 0;
+              last = prev == static_cast<uint32_t>(c_last - c_first);
             }
-            cbar();
-            have = *s_flag != 0;
+            have = cbar_or(last);
             if (have) {
               __threadfence();
               if (ct == 0) p.gu_tile_cnt[tile] = 0u;
@@ -1007,6 +1018,12 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
       }
     }
   }
+  if (threadIdx.x == 0 && ld_relaxed(abort_word)) {
+    // aborted: let every TMA load and MMA already issued land before the
+    // CTA's shared and tensor memory are released
+    const uint64_t t0 = gtimer();
+    while (gtimer() - t0 < 200000ull) __nanosleep(1000);
+  }
   __syncthreads();
   if (warp == 2) {
     tc_fence_after();
@@ -1026,6 +1043,9 @@ bool fused_supported(const dtree_qwen3_desc& d) {
   if (d.hidden % 128 != 0 || d.ffn % 64 != 0 || (2 * d.ffn) % 128 != 0 || d.hidden > 4096) return false;
   if (d.layers < 1 || d.layers > kFusedMaxLayers) return false;
   if (d.n_heads % d.n_kv_heads != 0) return false;
+  // a CTA's stream-K range of gate|up units spans at most three tiles
+  const long long gu_units = static_cast<long long>(2 * d.ffn / 128) * (d.hidden / 64);
+  if ((gu_units + num_sms() - 1) / num_sms() > d.hidden / 64 + 2) return false;
   return true;
 }
 
@@ -1140,6 +1160,7 @@ int fused_plan(const dtree_qwen3_desc& d, void* ws, int t_pad, FusedPlan* plan) 
   p.rope_log2_theta = std::log2(d.rope_theta);
   p.scale_log2 = static_cast<float>(1.4426950408889634 / std::sqrt(128.0));
   p.kv_cap = d.kv_capacity;
+  p.vocab = d.vocab;
   p.ldc = d.hidden * (d.n_capture > 0 ? d.n_capture : 1);
   p.embed = static_cast<const __nv_bfloat16*>(d.embed);
   p.final_norm = static_cast<const __nv_bfloat16*>(d.final_norm);

@@ -42,7 +42,7 @@ struct FusedParams {
   const dtree_step_state* state;
   int n_rows;
   // model
-  int layers, hidden, n_heads, n_kv_heads, ffn;
+  int layers, hidden, n_heads, n_kv_heads, ffn, vocab;
   float eps, rope_log2_theta, scale_log2;
   int kv_cap;
   int ldc;  // row stride of the verifier_hidden capture buffer (elements)
