@@ -48,10 +48,12 @@
 namespace dtree {
 
 constexpr int kFusedWarpsCompute = 8;
-constexpr int kAttChunk = 64;                          // keys per shared-memory chunk
-constexpr int kAttLd = 128 + 8;                        // padded row (bf16): conflict-free ldmatrix
-constexpr int kAttBytes = 2 * kAttChunk * kAttLd * 2;  // K + V chunk
+constexpr int kAttChunk = 32;                              // keys per shared-memory chunk
+constexpr int kAttLd = 128 + 8;                            // padded row (bf16): conflict-free ldmatrix
+constexpr int kAttStage = 2 * kAttChunk * kAttLd * 2;      // K + V chunk
+constexpr int kAttBytes = 2 * kAttStage;                   // double buffered
 constexpr unsigned long long kFusedTimeoutNs = 2000000000ull;  // 2 s per wait
+constexpr int kFusedL2Ahead = 0;  // weight units prefetched into L2 beyond the shared-memory ring
 
 template <int TPAD>
 struct FusedCfg {
@@ -98,14 +100,13 @@ __device__ bool wait_count(const uint32_t* cnt, uint32_t target, uint32_t* abort
   const uint64_t t0 = gtimer();
   for (uint32_t i = 1;; ++i) {
     if (ld_acquire(cnt) >= target) return true;
-    if ((i & 31) == 0) {
+    if ((i & 63) == 0) {
       if (ld_relaxed(abort_word)) return false;
       if (gtimer() - t0 > kFusedTimeoutNs) {
         abort_set(abort_word, 0x3000u | where);
         return false;
       }
     }
-    __nanosleep(64);
   }
 }
 
@@ -115,7 +116,7 @@ __device__ bool mbar_wait_ab(uint64_t* bar, uint32_t parity, uint32_t* abort_wor
   uint64_t t0 = 0;
   for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
-    if ((i & 15) == 0) {
+    if ((i & 255) == 0) {
       if (ld_relaxed(abort_word)) return false;
       const uint64_t t = gtimer();
       if (t0 == 0) {
@@ -159,14 +160,14 @@ __device__ __forceinline__ bool cwait(const uint32_t* cnt, uint32_t target, uint
   if (ct == 0) ok = wait_count(cnt, target, abort_word, where);
   return cbar_and(ok);
 }
-// compute warps: every thread's writes are done; one thread publishes
+__device__ __forceinline__ void red_release_add(uint32_t* p, uint32_t v) {
+  asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+// compute warps: every thread's writes are done (the barrier orders them
+// before thread 0's release, which is cumulative); one thread publishes
 __device__ __forceinline__ void csignal(uint32_t* cnt, int ct) {
-  __threadfence();
   cbar();
-  if (ct == 0) {
-    __threadfence();
-    atomicAdd(cnt, 1u);
-  }
+  if (ct == 0) red_release_add(cnt, 1u);
 }
 
 // ------------------------------------------------------------------ jobs
@@ -209,57 +210,102 @@ __device__ int fused_segs(const FusedParams& p, int j, int c, FSeg* s) {
   }
   return n;
 }
+// walks a CTA's (layer, projection, segment, k-block) units in stream order
+struct UnitCursor {
+  int l, j, q, k, ns;
+  FSeg sg[3];
+  __device__ __forceinline__ void skip_empty(const FusedParams& p, int c) {
+    while (l < p.layers && q >= ns) {
+      if (++j == kFusedJobs) {
+        j = 0;
+        ++l;
+      }
+      if (l < p.layers) {
+        ns = fused_segs(p, j, c, sg);
+        q = 0;
+        k = 0;
+      }
+    }
+  }
+  __device__ __forceinline__ void init(const FusedParams& p, int c) {
+    l = 0;
+    j = 0;
+    q = 0;
+    k = 0;
+    ns = fused_segs(p, 0, c, sg);
+    skip_empty(p, c);
+  }
+  __device__ __forceinline__ bool valid(const FusedParams& p) const { return l < p.layers; }
+  __device__ __forceinline__ void next(const FusedParams& p, int c) {
+    if (++k >= sg[q].len) {
+      k = 0;
+      ++q;
+      skip_empty(p, c);
+    }
+  }
+};
+
+__device__ __forceinline__ void l2_prefetch_tile(const void* tmap, int x, int y) {
+  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(tmap), "r"(x), "r"(y)
+               : "memory");
+}
+
 __device__ __forceinline__ int gu_cta_of(long long u, long long U, int G) {
   return static_cast<int>(((u + 1) * G - 1) / U);
 }
 __device__ __forceinline__ long long gu_u0(int c, long long U, int G) { return (static_cast<long long>(c) * U) / G; }
 
 // ------------------------------------------------------------------ glue phases
-// residual add of a split-K projection + RMSNorm of one row (256 threads).
-// first layer: the row is the token's embedding.  Numerics as
+// Row norms are spread over the CTAs: ns slices per row (ns = grid / rows,
+// at most 8), one 8-wide vector per thread.
+__device__ __forceinline__ int norm_slices(int n_rows, int G) {
+  int ns = G / n_rows;
+  return ns < 1 ? 1 : (ns > 8 ? 8 : ns);
+}
+
+// residual add of a split-K projection + RMSNorm of one slice of one row
+// (256 threads).  The slices' sums of squares meet in `ssbuf` (per-row
+// arrival counter `rowcnt`, summed in slice order: deterministic).  First
+// layer: the row is the token's embedding.  Numerics as
 // residual_rmsnorm_kernel: h = bf16(h + bf16(sum of partials)).
 template <int TPAD>
-__device__ void fused_norm_row(const FusedParams& p, int row, const float* part, int split, const __nv_bfloat16* w,
-                               __nv_bfloat16* out, __nv_bfloat16* capture, bool embed_row, int ct, float* red) {
+__device__ bool fused_norm_slice(const FusedParams& p, int row, int slice, int ns, const float* part, int split,
+                                 const __nv_bfloat16* w, __nv_bfloat16* out, __nv_bfloat16* capture, bool embed_row,
+                                 int ct, float* red, uint32_t* rowcnt, uint32_t* abort_word) {
   const int H = p.hidden, nv = H / 8;
-  uint4 hv0 = make_uint4(0, 0, 0, 0), hv1 = hv0;
-  float ss = 0.0f;
+  const int v0 = (slice * nv) / ns, v1 = ((slice + 1) * nv) / ns;
+  const int i = v0 + ct;
+  const bool act = i < v1;
   __nv_bfloat16* hrow = p.h + static_cast<size_t>(row) * H;
-  int tok = embed_row ? p.tokens[row] : 0;
-  if (tok < 0 || tok >= p.vocab) {
-    if (ct == 0) dev_error(0x2002u);
-    tok = 0;
-  }
-  const __nv_bfloat16* src = embed_row ? p.embed + static_cast<size_t>(tok) * H : hrow;
-#pragma unroll 1
-  for (int k = 0; k < 2; ++k) {
-    const int i = ct + k * 256;
-    if (i >= nv) continue;
-    const uint4 h0 = reinterpret_cast<const uint4*>(src)[i];
-    uint4 o = h0;
-    if (!embed_row) {
+  uint4 o = make_uint4(0, 0, 0, 0);
+  float ss = 0.0f;
+  if (act) {
+    if (embed_row) {
+      int tok = p.tokens[row];
+      if (tok < 0 || tok >= p.vocab) {
+        dev_error(0x2002u);
+        tok = 0;
+      }
+      o = reinterpret_cast<const uint4*>(p.embed + static_cast<size_t>(tok) * H)[i];
+    } else {
+      const uint4 h0 = __ldcg(reinterpret_cast<const uint4*>(hrow) + i);
       float y[8];
 #pragma unroll
       for (int e = 0; e < 8; ++e) y[e] = 0.0f;
-      // four splits' loads in flight per batch, summed in split order
-#pragma unroll 1
-      for (int s0 = 0; s0 < split; s0 += 4) {
-        float4 a[4], b[4];
+      float4 a[8], b[8];  // every split's loads in flight at once (split <= 8)
 #pragma unroll
-        for (int s = 0; s < 4; ++s) {
-          if (s0 + s < split) {
-            const float4* pp =
-                reinterpret_cast<const float4*>(part + (static_cast<size_t>(s0 + s) * TPAD + row) * H) + 2 * i;
-            a[s] = __ldcg(pp);
-            b[s] = __ldcg(pp + 1);
-          }
+      for (int s = 0; s < 8; ++s) {
+        if (s < split) {
+          const float4* pp = reinterpret_cast<const float4*>(part + (static_cast<size_t>(s) * TPAD + row) * H) + 2 * i;
+          a[s] = __ldcg(pp);
+          b[s] = __ldcg(pp + 1);
         }
+      }
 #pragma unroll
-        for (int s = 0; s < 4; ++s) {
-          if (s0 + s < split) {
-            y[0] += a[s].x; y[1] += a[s].y; y[2] += a[s].z; y[3] += a[s].w;
-            y[4] += b[s].x; y[5] += b[s].y; y[6] += b[s].z; y[7] += b[s].w;
-          }
+      for (int s = 0; s < 8; ++s) {
+        if (s < split) {
+          y[0] += a[s].x; y[1] += a[s].y; y[2] += a[s].z; y[3] += a[s].w;
+          y[4] += b[s].x; y[5] += b[s].y; y[6] += b[s].z; y[7] += b[s].w;
         }
       }
       const __nv_bfloat162* hb = reinterpret_cast<const __nv_bfloat162*>(&h0);
@@ -276,25 +322,28 @@ __device__ void fused_norm_row(const FusedParams& p, int row, const float* part,
       const float2 g = __bfloat1622float2(ob[q]);
       ss += g.x * g.x + g.y * g.y;
     }
-    if (k == 0) hv0 = o;
-    else hv1 = o;
     reinterpret_cast<uint4*>(hrow)[i] = o;
     if (capture) reinterpret_cast<uint4*>(capture + static_cast<size_t>(row) * p.ldc)[i] = o;
   }
   for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
   if ((ct & 31) == 0) red[ct >> 5] = ss;
   cbar();
-  float tot = 0.0f;
+  bool ok = true;
+  if (ct == 0) {
+    float t = 0.0f;
 #pragma unroll
-  for (int k = 0; k < kFusedWarpsCompute; ++k) tot += red[k];
+    for (int k = 0; k < kFusedWarpsCompute; ++k) t += red[k];
+    p.norm_ss[row * 8 + slice] = t;
+    red_release_add(&rowcnt[row], 1u);
+    ok = wait_count(&rowcnt[row], static_cast<uint32_t>(ns), abort_word, 0x30);
+  }
+  if (!cbar_and(ok)) return false;
+  float tot = 0.0f;
+  for (int k = 0; k < ns; ++k) tot += __ldcg(p.norm_ss + row * 8 + k);
   const float rs = rsqrtf(tot / static_cast<float>(H) + p.eps);
-#pragma unroll 1
-  for (int k = 0; k < 2; ++k) {
-    const int i = ct + k * 256;
-    if (i >= nv) continue;
-    const uint4 hv = k == 0 ? hv0 : hv1;
+  if (act) {
     const uint4 wv = reinterpret_cast<const uint4*>(w)[i];
-    const __nv_bfloat162* b = reinterpret_cast<const __nv_bfloat162*>(&hv);
+    const __nv_bfloat162* b = reinterpret_cast<const __nv_bfloat162*>(&o);
     const __nv_bfloat162* wb = reinterpret_cast<const __nv_bfloat162*>(&wv);
     uint4 o4;
     __nv_bfloat162* ob = reinterpret_cast<__nv_bfloat162*>(&o4);
@@ -306,7 +355,7 @@ __device__ void fused_norm_row(const FusedParams& p, int row, const float* part,
     }
     reinterpret_cast<uint4*>(out + static_cast<size_t>(row) * H)[i] = o4;
   }
-  cbar();  // red is reused by the next row / phase
+  return true;
 }
 
 // q/k RMSNorm + RoPE (q -> buffer, k -> cache) or v -> cache for one (row,
@@ -411,15 +460,13 @@ __device__ __forceinline__ int att_kps(int L, int splits) {
   return ((kps + kAttChunk - 1) / kAttChunk) * kAttChunk;
 }
 
-// split-KV tree attention of one (kv head, row block, key split): 64 query
+// split-KV tree attention of one (kv head, row block, key split): 128 query
 // rows per task (row r -> q head kvh*G + r / T, node r % T); warp cw owns
-// rows 16*(cw/2) .. +15 and output features 64*(cw%2) .. +63 (the score
-// block is computed by both warps of a row group, which halves the
-// accumulators a thread holds).  64-key chunks of K / V through shared
-// memory, bf16 mma.sync with an fp32 online softmax.  Visibility: every
+// rows 16*cw .. +15.  32-key chunks of K / V through shared memory (double
+// buffered), bf16 mma.sync with an fp32 online softmax.  Visibility: every
 // prefix key, and tree slot j iff bit j of the node's ancestor mask
 // (dtree_runtime.py:190-191).  Writes (m, l, unnormalised O).
-constexpr int kAttRows = 64;
+constexpr int kAttRows = 128;
 __device__ void fused_att_task(const FusedParams& p, int l, int kvh, int rbi, int sp, int P, int cw, int lane, int ct,
                                uint8_t* sm) {
   const int T = p.n_rows, G = p.n_heads / p.n_kv_heads;
@@ -433,9 +480,7 @@ __device__ void fused_att_task(const FusedParams& p, int l, int kvh, int rbi, in
   const size_t plane = static_cast<size_t>(p.n_kv_heads) * p.kv_cap * 128;
   const __nv_bfloat16* kpl = p.kv + static_cast<size_t>(l) * 2 * plane + static_cast<size_t>(kvh) * p.kv_cap * 128;
   const __nv_bfloat16* vpl = kpl + plane;
-  __nv_bfloat16* sk = reinterpret_cast<__nv_bfloat16*>(sm);
-  __nv_bfloat16* sv = sk + kAttChunk * kAttLd;
-  const int rgrp = cw >> 1, dh = cw & 1;
+  const int rgrp = cw;
 
   // this thread's rows: lane/4 and lane/4 + 8 of the warp's 16
   int node[2], qh[2];
@@ -459,19 +504,22 @@ __device__ void fused_att_task(const FusedParams& p, int l, int kvh, int rbi, in
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
         const __nv_bfloat16* qp = p.q + static_cast<size_t>(node[h]) * (p.n_heads * 128) + qh[h] * 128 + kk * 16 + c2;
-        qf[kk][h] = rok[h] ? *reinterpret_cast<const uint32_t*>(qp) : 0u;
-        qf[kk][2 + h] = rok[h] ? *reinterpret_cast<const uint32_t*>(qp + 8) : 0u;
+        // (q is rewritten every layer by other CTAs: read through L2)
+        qf[kk][h] = rok[h] ? __ldcg(reinterpret_cast<const unsigned int*>(qp)) : 0u;
+        qf[kk][2 + h] = rok[h] ? __ldcg(reinterpret_cast<const unsigned int*>(qp + 8)) : 0u;
       }
     }
   }
-  float o[8][4];
+  float o[16][4];
 #pragma unroll
-  for (int j = 0; j < 8; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.0f;
+  for (int j = 0; j < 16; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.0f;
   float m_run[2] = {-INFINITY, -INFINITY}, l_run[2] = {0.0f, 0.0f};
 
-#pragma unroll 1
-  for (int c = 0; c < n_chunks; ++c) {
+  // 32-key chunks of K and V, double buffered: chunk c + 1 loads while c computes
+  auto load_chunk = [&](int c, int buf) {
     const int key0 = k_begin + c * kAttChunk;
+    __nv_bfloat16* sk = reinterpret_cast<__nv_bfloat16*>(sm + buf * kAttStage);
+    __nv_bfloat16* sv = sk + kAttChunk * kAttLd;
     for (int e = ct; e < kAttChunk * 16; e += 256) {
       const int r = e >> 4, v = e & 15;
       const int key = key0 + r;
@@ -481,13 +529,22 @@ __device__ void fused_att_task(const FusedParams& p, int l, int kvh, int rbi, in
       f_cp_async16(sv + r * kAttLd + v * 8, vpl + off, ok);
     }
     asm volatile("cp.async.commit_group;" ::: "memory");
-    asm volatile("cp.async.wait_group 0;" ::: "memory");
-    cbar();
-    // two sub-blocks of 32 keys (fewer live score registers), each an online
-    // softmax update
+  };
+  load_chunk(0, 0);
 #pragma unroll 1
-    for (int sub = 0; sub < 2; ++sub) {
-      const int kb0 = sub * 32;
+  for (int c = 0; c < n_chunks; ++c) {
+    const int key0 = k_begin + c * kAttChunk;
+    if (c + 1 < n_chunks) {
+      load_chunk(c + 1, (c + 1) & 1);
+      asm volatile("cp.async.wait_group 1;" ::: "memory");
+    } else {
+      asm volatile("cp.async.wait_group 0;" ::: "memory");
+    }
+    cbar();
+    const __nv_bfloat16* sk = reinterpret_cast<const __nv_bfloat16*>(sm + (c & 1) * kAttStage);
+    const __nv_bfloat16* sv = sk + kAttChunk * kAttLd;
+    {
+      constexpr int kb0 = 0;
       float s[4][4];
 #pragma unroll
       for (int nt = 0; nt < 4; ++nt) s[nt][0] = s[nt][1] = s[nt][2] = s[nt][3] = 0.0f;
@@ -548,7 +605,7 @@ __device__ void fused_att_task(const FusedParams& p, int l, int kvh, int rbi, in
         l_run[h] = l_run[h] * alpha[h] + rs[h];
       }
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
+      for (int j = 0; j < 16; ++j) {
         o[j][0] *= alpha[0];
         o[j][1] *= alpha[0];
         o[j][2] *= alpha[1];
@@ -557,29 +614,29 @@ __device__ void fused_att_task(const FusedParams& p, int l, int kvh, int rbi, in
 #pragma unroll
       for (int kt = 0; kt < 2; ++kt) {
 #pragma unroll
-        for (int nt = 0; nt < 8; nt += 2) {
+        for (int nt = 0; nt < 16; nt += 2) {
           uint32_t b[4];
           const int mi = lane >> 3, i = lane & 7;
-          f_ldsm_x4_t(b, sv + (kb0 + kt * 16 + i + 8 * (mi & 1)) * kAttLd + dh * 64 + nt * 8 + 8 * (mi >> 1));
+          f_ldsm_x4_t(b, sv + (kb0 + kt * 16 + i + 8 * (mi & 1)) * kAttLd + nt * 8 + 8 * (mi >> 1));
           f_mma(o[nt], pf[kt], b[0], b[1]);
           f_mma(o[nt + 1], pf[kt], b[2], b[3]);
         }
       }
     }
-    cbar();  // the chunk buffer is refilled next
+    cbar();  // buffer c & 1 is refilled by the next iteration's prefetch
   }
   const int rows_total = p.n_heads * T;
 #pragma unroll
   for (int h = 0; h < 2; ++h) {
     if (!rok[h]) continue;
     const int qrow = qh[h] * T + node[h];
-    float* po = p.att_o + (static_cast<size_t>(sp) * rows_total + qrow) * 128 + dh * 64;
+    float* po = p.att_o + (static_cast<size_t>(sp) * rows_total + qrow) * 128;
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
+    for (int j = 0; j < 16; ++j) {
       const int d = j * 8 + 2 * (lane & 3);
       *reinterpret_cast<float2*>(po + d) = make_float2(o[j][2 * h], o[j][2 * h + 1]);
     }
-    if ((lane & 3) == 0 && dh == 0) {
+    if ((lane & 3) == 0) {
       float* pml = p.att_ml + (static_cast<size_t>(sp) * rows_total + qrow) * 2;
       pml[0] = m_run[h];
       pml[1] = l_run[h];
@@ -686,32 +743,38 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
 
   if (warp == 0) {
     // ---------------------------------------------------------------- weights
+    // TMA loads fill the ring as slots free up; L2 prefetches of the units
+    // after the ring run kFusedL2Ahead units further ahead, so the stream
+    // keeps DRAM busy while the ring is full and the glue phases run.
     if (lane == 0) {
       const uint64_t pol = l2_policy_evict_first();
       int s = 0;
       uint32_t ph = 0;
       bool ok = true;
-      long long i = 0;
-      for (int l = 0; l < p.layers && ok; ++l) {
-        for (int j = 0; j < kFusedJobs && ok; ++j) {
-          const CUtensorMap* wm = p.wmaps + l * kFusedJobs + j;
-          FSeg sg[3];
-          const int ns = fused_segs(p, j, c, sg);
-          for (int q = 0; q < ns && ok; ++q) {
-            for (int k = 0; k < sg[q].len; ++k, ++i) {
-              if (i >= S) {
-                ok = mbar_wait_ab(&empty_bar[s], ph ^ 1u, abort_word, 1);
-                if (!ok) break;
-              }
-              mbar_arrive_expect_tx(&full_bar[s], C::kWBytes);
-              tma_load_2d(stages + s * C::kStageBytes, wm, &full_bar[s], (sg[q].kb0 + k) * 64, sg[q].tile * 128, pol);
-              if (++s == S) {
-                s = 0;
-                ph ^= 1u;
-              }
-            }
-          }
+      long long i = 0, ipf = 0;
+      UnitCursor cur, pf;
+      cur.init(p, c);
+      pf.init(p, c);
+      while (cur.valid(p) && ok) {
+        while (pf.valid(p) && ipf < i + S + kFusedL2Ahead) {
+          if (ipf >= i + S)
+            l2_prefetch_tile(p.wmaps + pf.l * kFusedJobs + pf.j, (pf.sg[pf.q].kb0 + pf.k) * 64, pf.sg[pf.q].tile * 128);
+          pf.next(p, c);
+          ++ipf;
         }
+        if (i >= S) {
+          ok = mbar_wait_ab(&empty_bar[s], ph ^ 1u, abort_word, 1);
+          if (!ok) break;
+        }
+        mbar_arrive_expect_tx(&full_bar[s], C::kWBytes);
+        tma_load_2d(stages + s * C::kStageBytes, p.wmaps + cur.l * kFusedJobs + cur.j, &full_bar[s],
+                    (cur.sg[cur.q].kb0 + cur.k) * 64, cur.sg[cur.q].tile * 128, pol);
+        if (++s == S) {
+          s = 0;
+          ph ^= 1u;
+        }
+        cur.next(p, c);
+        ++i;
       }
     }
   } else if (warp == 1) {
@@ -730,7 +793,8 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
           // the projection's input is complete
           const uint32_t* wc = j == 0 ? cnt(l, kCntN1) : j == 1 ? cnt(l, kCntCmb) : j == 2 ? cnt(l, kCntN2)
                                                                                           : cnt(l, kCntGu);
-          const uint32_t target = (j == 0 || j == 2) ? static_cast<uint32_t>(p.n_rows) : static_cast<uint32_t>(G);
+          const uint32_t target = (j == 0 || j == 2) ? static_cast<uint32_t>(p.n_rows * norm_slices(p.n_rows, G))
+                                                     : static_cast<uint32_t>(G);
           ok = wait_count(wc, target, abort_word, 0x10 + j);
           if (!ok) break;
           fence_proxy_async_global();  // generic-proxy writes of other CTAs -> this thread's TMA reads
@@ -866,8 +930,11 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
         }
         if (wc) ok = cwait(wc, static_cast<uint32_t>(G), abort_word, 0x20 + half, ct);
         if (!ok) break;
-        for (int r = c; r < p.n_rows; r += G) {
-          fused_norm_row<TPAD>(p, r, part, split, w, out, cap, step == 0, ct, red);
+        const int ns = norm_slices(p.n_rows, G);
+        if (c < p.n_rows * ns) {
+          ok = fused_norm_slice<TPAD>(p, c / ns, c % ns, ns, part, split, w, out, cap, step == 0, ct, red,
+                                      p.norm_cnt + step * 64, abort_word);
+          if (!ok) break;
           if (sig) csignal(sig, ct);
         }
       }
@@ -946,23 +1013,21 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
               tmem_ld_x8(taddr + c0, r);
               tmem_wait_ld();
 #pragma unroll
-              for (int e = 0; e < 8; ++e) slot[(c0 + e) * 128 + row] = __uint_as_float(r[e]);
+              for (int e = 0; e < 8; ++e)
+                if (c0 + e < p.n_rows) slot[(c0 + e) * 128 + row] = __uint_as_float(r[e]);
             }
-            __threadfence();
-            cbar();
+            cbar();  // the partial is written (ordered before thread 0's release below)
             c_first = gu_cta_of(static_cast<long long>(tile) * kb, U, G);
             c_last = gu_cta_of(static_cast<long long>(tile) * kb + kb - 1, U, G);
             bool last = false;
             if (ct == 0) {
-              __threadfence();
-              const uint32_t prev = atomicAdd(&p.gu_tile_cnt[tile], 1u);
+              uint32_t prev;
+              asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(prev) : "l"(&p.gu_tile_cnt[tile])
+                           : "memory");
               last = prev == static_cast<uint32_t>(c_last - c_first);
+              if (last) p.gu_tile_cnt[tile] = 0u;  // every contributor has arrived: reset for the next layer
             }
             have = cbar_or(last);
-            if (have) {
-              __threadfence();
-              if (ct == 0) p.gu_tile_cnt[tile] = 0u;
-            }
           }
           if (have) {
 #pragma unroll 1
@@ -977,11 +1042,24 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
               } else {
 #pragma unroll
                 for (int e = 0; e < 8; ++e) a[e] = 0.0f;
-                for (int cc = c_first; cc <= c_last; ++cc) {
-                  const int w2 = (tile == static_cast<int>(gu_u0(cc, U, G) / kb)) ? 0 : 1;
-                  const float* sl = p.gu_ws + (static_cast<size_t>(cc) * 2 + w2) * TPAD * 128 + c0 * 128 + row;
+                for (int cb = c_first; cb <= c_last; cb += 4) {  // four contributors' loads in flight
+                  float v[4][8];
 #pragma unroll
-                  for (int e = 0; e < 8; ++e) a[e] += __ldcg(sl + e * 128);
+                  for (int k2 = 0; k2 < 4; ++k2) {
+                    const int cc = cb + k2;
+                    if (cc <= c_last) {
+                      const int w2 = (tile == static_cast<int>(gu_u0(cc, U, G) / kb)) ? 0 : 1;
+                      const float* sl = p.gu_ws + (static_cast<size_t>(cc) * 2 + w2) * TPAD * 128 + c0 * 128 + row;
+#pragma unroll
+                      for (int e = 0; e < 8; ++e) v[k2][e] = __ldcg(sl + e * 128);
+                    }
+                  }
+#pragma unroll
+                  for (int k2 = 0; k2 < 4; ++k2)
+                    if (cb + k2 <= c_last) {
+#pragma unroll
+                      for (int e = 0; e < 8; ++e) a[e] += v[k2][e];
+                    }
                 }
               }
               if (row >= 64) {
@@ -1049,8 +1127,13 @@ bool fused_supported(const dtree_qwen3_desc& d) {
   return true;
 }
 
+// phase counters, the abort word, then per-(norm step, row) arrival counters
+static size_t fused_cnt_words(int layers) {
+  return static_cast<size_t>(layers) * kCntPerLayer + 8 + static_cast<size_t>(2 * layers + 1) * 64;
+}
+
 struct FusedLayout {
-  size_t maps, lp, cnt, qkv_part, o_part, dn_part, gu_ws, gu_cnt, att_o, att_ml, total;
+  size_t maps, lp, cnt, norm_ss, qkv_part, o_part, dn_part, gu_ws, gu_cnt, att_o, att_ml, total;
   int qkv_split, o_split, dn_split, att_splits, att_rb, grid;
 };
 
@@ -1080,20 +1163,28 @@ static FusedLayout fused_layout(const dtree_qwen3_desc& d, int t_pad) {
   };
   L.maps = take(static_cast<size_t>(d.layers) * kFusedJobs * sizeof(CUtensorMap));
   L.lp = take(static_cast<size_t>(d.layers) * sizeof(FusedLayerPtrs));
-  L.cnt = take((static_cast<size_t>(d.layers) * kCntPerLayer + 8) * 4);
+  L.cnt = take(fused_cnt_words(d.layers) * 4);
+  L.norm_ss = take(64 * 8 * 4);
   L.qkv_part = take(static_cast<size_t>(L.qkv_split) * t_pad * qkv_width(d) * 4);
   L.o_part = take(static_cast<size_t>(L.o_split) * t_pad * d.hidden * 4);
   L.dn_part = take(static_cast<size_t>(L.dn_split) * t_pad * d.hidden * 4);
   L.gu_ws = take(static_cast<size_t>(G) * 2 * t_pad * 128 * 4);
   L.gu_cnt = take(static_cast<size_t>(2 * d.ffn / 128) * 4);
-  L.att_o = take(static_cast<size_t>(L.att_splits) * d.n_heads * t_pad * 128 * 4);
-  L.att_ml = take(static_cast<size_t>(L.att_splits) * d.n_heads * t_pad * 2 * 4);
+  // attention partials: room for the largest splits x rows of any t_pad up to this one
+  size_t att_rows = 0;
+  for (int tp = 16; tp <= t_pad; tp *= 2) {
+    const int rb = (Gq * tp + kAttRows - 1) / kAttRows;
+    const int sp = std::max(1, std::min(32, G / (d.n_kv_heads * rb)));
+    att_rows = std::max(att_rows, static_cast<size_t>(sp) * tp);
+  }
+  L.att_o = take(att_rows * d.n_heads * 128 * 4);
+  L.att_ml = take(att_rows * d.n_heads * 2 * 4);
   L.total = off;
   return L;
 }
 
 size_t fused_ws_bytes(const dtree_qwen3_desc& d) {
-  if (d.verify_path != 0 || !fused_supported(d)) return 0;
+  if (d.verify_path != 1 || !fused_supported(d)) return 0;
   return fused_layout(d, fused_tpad_max(d)).total;
 }
 
@@ -1181,12 +1272,14 @@ int fused_plan(const dtree_qwen3_desc& d, void* ws, int t_pad, FusedPlan* plan) 
   p.att_o = reinterpret_cast<float*>(base + L.att_o);
   p.att_ml = reinterpret_cast<float*>(base + L.att_ml);
   p.cnt = reinterpret_cast<uint32_t*>(base + L.cnt);
+  p.norm_cnt = p.cnt + static_cast<size_t>(d.layers) * kCntPerLayer + 8;
+  p.norm_ss = reinterpret_cast<float*>(base + L.norm_ss);
   p.qkv_split = L.qkv_split;
   p.o_split = L.o_split;
   p.dn_split = L.dn_split;
   p.att_splits = Lt.att_splits;
   p.att_rb = Lt.att_rb;
-  DTREE_CHECK_ARG(static_cast<size_t>(Lt.att_splits) * t_pad <= static_cast<size_t>(L.att_splits) * fused_tpad_max(d),
+  DTREE_CHECK_ARG(static_cast<size_t>(Lt.att_splits) * t_pad * d.n_heads * 128 * 4 <= L.att_ml - L.att_o,
                   "fused verify: attention partials exceed the workspace");
   p.grid = L.grid;
   plan->t_pad = t_pad;
@@ -1220,7 +1313,7 @@ int fused_launch(FusedPlan& plan, const int32_t* tokens, const int32_t* position
   plan.p.anc = anc;
   plan.p.state = state;
   plan.p.n_rows = n_rows;
-  DTREE_CUDA_RET(cudaMemsetAsync(plan.p.cnt, 0, (static_cast<size_t>(plan.p.layers) * kCntPerLayer + 8) * 4, stream));
+  DTREE_CUDA_RET(cudaMemsetAsync(plan.p.cnt, 0, fused_cnt_words(plan.p.layers) * 4, stream));
   if (plan.t_pad == 16) return fused_launch_t<16>(plan, stream);
   if (plan.t_pad == 32) return fused_launch_t<32>(plan, stream);
   return fused_launch_t<64>(plan, stream);

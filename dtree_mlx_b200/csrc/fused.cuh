@@ -66,6 +66,8 @@ struct FusedParams {
   float* att_o;           // [att_splits][n_heads * n_rows][128]
   float* att_ml;          // [att_splits][n_heads * n_rows][2]
   uint32_t* cnt;          // [layers][kCntPerLayer], then the abort word
+  uint32_t* norm_cnt;     // [2 * layers + 1][64] per-row slice arrivals of each norm step
+  float* norm_ss;         // [64][8] per-slice sums of squares of the current norm step
   int qkv_split, o_split, dn_split, att_splits, att_rb;
   int grid;
 };

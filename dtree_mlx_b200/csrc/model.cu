@@ -210,7 +210,7 @@ extern "C" int dtree_qwen3_create(const dtree_qwen3_desc* desc, dtree_qwen3_mode
   m->attn_ws_bytes = attn_ws_need(d);
   m->proj_partials = reinterpret_cast<float*>(static_cast<char*>(m->attn_ws) +
                                               ((m->attn_ws_bytes + 255) & ~static_cast<size_t>(255)));
-  if (d.verify_path == 0 && fused_supported(d)) {
+  if (d.verify_path == 1 && fused_supported(d)) {
     m->fused_ws = reinterpret_cast<char*>(m->proj_partials) + ((partials_need(d) + 255) & ~static_cast<size_t>(255));
     std::vector<std::pair<int, __nv_bfloat16*>> caps;
     for (int c = 0; c < d.n_capture; ++c)

@@ -64,12 +64,12 @@ class Qwen3Engine:
     """One Qwen3 target on one GPU (weights + KV cache + scratch buffers)."""
 
     def __init__(self, weights: Qwen3Weights, kv_capacity: int, layer_ids=(), t_cap: int = DTREE_MAX_TREE,
-                 verify_path: str = "auto"):
-        """``verify_path``: "auto" runs the verify forward as one persistent
-        launch where the model supports it (bf16, head_dim 128, <= 64 rows),
-        "chain" always as the per-kernel chain."""
-        if verify_path not in ("auto", "chain"):
-            raise ValueError("verify_path must be 'auto' or 'chain'")
+                 verify_path: str = "chain"):
+        """``verify_path``: "chain" runs the verify forward as the per-kernel
+        chain; "persistent" as one persistent launch (one CTA per SM) where
+        the model supports it (bf16, head_dim 128, <= 64 rows)."""
+        if verify_path not in ("chain", "persistent"):
+            raise ValueError("verify_path must be 'chain' or 'persistent'")
         cfg: Qwen3Config = weights.cfg
         if weights.device.type != "cuda":
             raise ValueError("engine weights must live on a CUDA device")
@@ -102,7 +102,7 @@ class Qwen3Engine:
         d.ffn, d.vocab = cfg.intermediate_size, cfg.vocab_size
         d.rope_theta, d.rms_eps = cfg.rope_theta, cfg.rms_norm_eps
         d.t_cap, d.kv_capacity = self.t_cap, self.kv_capacity
-        d.verify_path = 0 if verify_path == "auto" else 1
+        d.verify_path = 1 if verify_path == "persistent" else 0
         d.n_capture = len(self.layer_ids)
         for i, l in enumerate(self.layer_ids):
             d.capture_layers[i] = l

@@ -330,9 +330,10 @@ typedef struct dtree_qwen3_desc {
   int quant_bits;
   int group_size;
   const dtree_qwen3_q4_layer* q4_layer;  /* [layers] when quant_bits == 4 */
-  /* verify forward schedule: 0 = the persistent single-launch forward when
-   * the model supports it (bf16 weights, head_dim 128, <= 64 tree rows),
-   * else the per-kernel chain; 1 = always the per-kernel chain */
+  /* verify forward schedule: 0 = the per-kernel chain (default); 1 = the
+   * persistent single-launch forward (one CTA per SM, weights streamed
+   * through the glue phases) where the model supports it (bf16 weights,
+   * head_dim 128, <= 64 tree rows), else the chain */
   int verify_path;
 } dtree_qwen3_desc;
 

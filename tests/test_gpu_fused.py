@@ -5,9 +5,9 @@ Both compute the same bf16 pipeline (qwen3_tree.py:39-83); they differ only
 in the order of fp32 split-K / attention-split sums, so their outputs agree
 to within bf16 rounding: relative Frobenius error <= 2e-2 on the final norm
 output, the captured hiddens and the new K/V rows; posterior tokens equal
-except at near-ties (top-2 logits within 5e-2).  The fused path's parity
-with the fp32 oracle at full depth is covered by tests/test_gpu_parity_4b.py
-(the 36-layer Qwen3-4B engine runs it).
+except at near-ties (top-2 logits within 5e-2).  The chain (the default
+schedule) is checked against the fp32 oracle at full depth in
+tests/test_gpu_parity_4b.py.
 """
 from __future__ import annotations
 
@@ -35,8 +35,8 @@ def engines(lib):
 
     cfg = dataclasses.replace(PRESETS["qwen3-4b"], num_hidden_layers=4)
     w = random_qwen3_weights(cfg, seed=3, device=DEV, norm_jitter=0.1)
-    fused = Qwen3Engine(w, kv_capacity=4096, layer_ids=[1, 3])
-    chain = Qwen3Engine(w, kv_capacity=4096, layer_ids=[1, 3], verify_path="chain")
+    fused = Qwen3Engine(w, kv_capacity=4096, layer_ids=[1, 3], verify_path="persistent")
+    chain = Qwen3Engine(w, kv_capacity=4096, layer_ids=[1, 3])
     yield cfg, w, fused, chain
     fused.close()
     chain.close()
