@@ -186,6 +186,10 @@ PROTOTYPES = {
     "dtree_tree_attention": (I, [P, I, P, P, I, I, I, I, I, P, P, P, I, P, SZ, P]),
     "dtree_lm_head_workspace_bytes": (SZ, [I]),
     "dtree_lm_head_argmax": (I, [P, I, I, I, P, I, P, P, SZ, P]),
+    "dtree_lm_head_sample": (I, [P, I, I, I, P, I, C.c_float, C.c_uint32, P, P, P, SZ, P]),
+    "dtree_chain_sample": (I, [P, I, I, C.c_float, C.c_uint32, P, P, P, P, P, P, P]),
+    "dtree_qwen3_set_sampling": (I, [P, C.c_float, C.c_uint32]),
+    "dtree_qwen35_set_sampling": (I, [P, C.c_float, C.c_uint32]),
     "dtree_qwen3_buffer_bytes": (I, [C.POINTER(Qwen3Desc), C.POINTER(C.c_size_t)]),
     "dtree_qwen3_create": (I, [C.POINTER(Qwen3Desc), C.POINTER(C.c_void_p)]),
     "dtree_qwen3_destroy": (I, [P]),

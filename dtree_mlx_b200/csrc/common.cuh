@@ -257,6 +257,39 @@ __host__ __device__ constexpr uint32_t idesc_bf16_f32(int m, int n) {
          | (static_cast<uint32_t>(m >> 4) << 24);   // M / 16
 }
 
+// ---------------------------------------------------------------- random
+// Philox4x32 with 10 rounds (Salmon et al., SC'11): counter c, key (k0, k1).
+__host__ __device__ __forceinline__ void philox4x32_10(uint32_t c[4], uint32_t k0, uint32_t k1) {
+  for (int r = 0; r < 10; ++r) {
+    if (r > 0) {
+      k0 += 0x9E3779B9u;
+      k1 += 0xBB67AE85u;
+    }
+    const uint64_t p0 = static_cast<uint64_t>(0xD2511F53u) * c[0];
+    const uint64_t p1 = static_cast<uint64_t>(0xCD9E8D57u) * c[2];
+    const uint32_t hi0 = static_cast<uint32_t>(p0 >> 32), lo0 = static_cast<uint32_t>(p0);
+    const uint32_t hi1 = static_cast<uint32_t>(p1 >> 32), lo1 = static_cast<uint32_t>(p1);
+    const uint32_t n0 = hi1 ^ c[1] ^ k0, n2 = hi0 ^ c[3] ^ k1;
+    c[0] = n0;
+    c[1] = lo1;
+    c[2] = n2;
+    c[3] = lo0;
+  }
+}
+
+// Standard Gumbel variate for categorical sampling by the Gumbel-max rule
+// (argmax_i x_i / T + G_i is distributed as softmax(x / T)): one Philox draw
+// keyed by (seed, stream tag) with counter (column, row, step);
+// u = (24 random bits + 0.5) * 2^-24 lies strictly inside (0, 1).
+__device__ __forceinline__ float gumbel_noise(uint32_t seed, uint32_t tag, uint32_t step, uint32_t row, uint32_t col) {
+  uint32_t c[4] = {col, row, step, tag};
+  philox4x32_10(c, seed, 0x6A4B5C3Du);
+  const float u = (static_cast<float>(c[0] >> 8) + 0.5f) * 5.9604644775390625e-08f;
+  return -logf(-logf(u));
+}
+constexpr uint32_t kSampleTagVerify = 0x5A11u;  // posterior tokens of the verify LM head
+constexpr uint32_t kSampleTagDraft = 0xD5A7u;   // drafted tokens of a DFlash block
+
 // ---------------------------------------------------------------- numerics
 __device__ __forceinline__ float bf16_round(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
 

@@ -196,6 +196,26 @@ extern "C" int dtree_linear_q4(const void* x, int t_pad, int k, const void* w_pa
 
 extern "C" size_t dtree_lm_head_workspace_bytes(int t_pad) { return gemm_ws_bytes(t_pad, 2 * num_sms()); }
 
+extern "C" int dtree_lm_head_sample(const void* h, int t_pad, int n_rows, int hidden, const void* embed, int vocab,
+                                    float temperature, uint32_t seed, const dtree_step_state* state, int32_t* out,
+                                    void* workspace, size_t workspace_bytes, void* stream) {
+  DTREE_CHECK_ARG(h && embed && out, "null pointer");
+  DTREE_CHECK_ARG(n_rows > 0 && n_rows <= t_pad, "n_rows must be in [1, t_pad]");
+  DTREE_CHECK_ARG(temperature >= 0.0f, "temperature must be >= 0");
+  GemmPlan plan;
+  int rc = gemm_plan(&plan, embed, vocab, hidden, h, t_pad, hidden, kEpiArgmax, 0);
+  if (rc) return rc;
+  rc = gemm_bind_ws(&plan, workspace, workspace_bytes);
+  if (rc) return rc;
+  plan.p.n_rows = n_rows;
+  plan.p.vocab = vocab;
+  plan.p.argmax_out = out;
+  plan.p.inv_temp = temperature < 1e-5f ? 0.0f : 1.0f / temperature;
+  plan.p.sample_seed = seed;
+  plan.p.sample_state = state;
+  return gemm_launch(plan, static_cast<cudaStream_t>(stream));
+}
+
 extern "C" int dtree_lm_head_argmax(const void* h, int t_pad, int n_rows, int hidden, const void* embed, int vocab,
                                     int32_t* out, void* workspace, size_t workspace_bytes, void* stream) {
   DTREE_CHECK_ARG(h && embed && out, "null pointer");

@@ -71,6 +71,12 @@ struct GemmParams {
   unsigned long long* argmax_keys;  // [TPAD], zero between launches
   uint32_t* done_cnt;               // zero between launches
   int32_t* argmax_out;              // [n_rows]
+  // sampling (inv_temp > 0): argmax of logit * inv_temp + Gumbel noise keyed
+  // by (sample_seed, sample_state->step, row, column) = a draw from
+  // softmax(logits / T); 0: greedy argmax
+  float inv_temp;
+  uint32_t sample_seed;
+  const dtree_step_state* sample_state;
   // q4 weights: bf16 scale / bias per (row, group of 64); row stride = kb
   const __nv_bfloat16* q_scales;
   const __nv_bfloat16* q_biases;
@@ -479,8 +485,10 @@ __global__ void __launch_bounds__(Q4 ? kGemmThreadsQ4 : kGemmThreads, 1)
     unsigned long long* s_best = reinterpret_cast<unsigned long long*>(red_raw + 256);  // argmax [TPAD]
     float* s_pos = reinterpret_cast<float*>(red_raw + 256);                           // qkv    [TPAD]
     int start = 0;
+    uint32_t sample_step = 0;
     if constexpr (EPI == kEpiArgmax) {
       for (int t = et; t < TPAD; t += 128) s_best[t] = 0ull;
+      if (p.sample_state) sample_step = static_cast<uint32_t>(p.sample_state->step);
     }
     if constexpr (EPI == kEpiQkv) {
       start = p.state ? p.state->start : 0;
@@ -691,7 +699,10 @@ __global__ void __launch_bounds__(Q4 ? kGemmThreadsQ4 : kGemmThreads, 1)
             for (int j = 0; j < 8; ++j) {
               unsigned long long key = 0ull;
               if (valid) {
-                const float v = bf16_round(a[j]);
+                float v = bf16_round(a[j]);
+                if (p.inv_temp > 0.0f)
+                  v = v * p.inv_temp + gumbel_noise(p.sample_seed, kSampleTagVerify, sample_step,
+                                                    static_cast<uint32_t>(c0 + j), static_cast<uint32_t>(n));
                 key = (static_cast<unsigned long long>(float_order_key(v)) << 32) |
                       static_cast<unsigned long long>(0xFFFFFFFFu - static_cast<uint32_t>(n));
               }

@@ -70,6 +70,8 @@ struct dtree_qwen3_model {
   void* fused_ws = nullptr;        // persistent-forward region (nullptr: not supported)
   dtree::FusedPlan fused[3];       // t_pad 16 / 32 / 64
   bool fused_ready[3] = {false, false, false};
+  float inv_temp = 0.0f;  // posterior sampling (0: greedy argmax)
+  uint32_t sample_seed = 0;
 };
 
 namespace dtree {
@@ -350,6 +352,9 @@ static int forward_impl(dtree_qwen3_model* m, const int32_t* tree_tokens, const 
       g.p.n_rows = n_nodes;
       g.p.vocab = d.vocab;
       g.p.argmax_out = posterior;
+      g.p.inv_temp = m->inv_temp;
+      g.p.sample_seed = m->sample_seed;
+      g.p.sample_state = state;
       if ((rc = gemm_launch(g, st))) return rc;
     }
     return kOk;
@@ -456,7 +461,18 @@ static int forward_impl(dtree_qwen3_model* m, const int32_t* tree_tokens, const 
     g.p.n_rows = n_nodes;
     g.p.vocab = d.vocab;
     g.p.argmax_out = posterior;
+    g.p.inv_temp = m->inv_temp;
+    g.p.sample_seed = m->sample_seed;
+    g.p.sample_state = state;
     if ((rc = gemm_launch(g, st))) return rc;
   }
+  return kOk;
+}
+
+extern "C" int dtree_qwen3_set_sampling(dtree_qwen3_model* m, float temperature, uint32_t seed) {
+  DTREE_CHECK_ARG(m, "null model");
+  DTREE_CHECK_ARG(temperature >= 0.0f, "temperature must be >= 0");
+  m->inv_temp = temperature < 1e-5f ? 0.0f : 1.0f / temperature;
+  m->sample_seed = seed;
   return kOk;
 }

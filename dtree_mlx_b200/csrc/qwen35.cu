@@ -96,6 +96,8 @@ struct dtree_qwen35_model {
   void* attn_ws = nullptr;
   size_t attn_ws_bytes = 0;
   float* partials = nullptr;
+  float inv_temp = 0.0f;  // posterior sampling (0: greedy argmax)
+  uint32_t sample_seed = 0;
 };
 
 namespace dtree {
@@ -415,8 +417,19 @@ extern "C" int dtree_qwen35_forward(dtree_qwen35_model* m, const int32_t* tokens
     g.p.n_rows = n;
     g.p.vocab = d.vocab;
     g.p.argmax_out = posterior;
+    g.p.inv_temp = m->inv_temp;
+    g.p.sample_seed = m->sample_seed;
+    g.p.sample_state = state;
     if ((rc = gemm_launch(g, st))) return rc;
   }
+  return kOk;
+}
+
+extern "C" int dtree_qwen35_set_sampling(dtree_qwen35_model* m, float temperature, uint32_t seed) {
+  DTREE_CHECK_ARG(m, "null model");
+  DTREE_CHECK_ARG(temperature >= 0.0f, "temperature must be >= 0");
+  m->inv_temp = temperature < 1e-5f ? 0.0f : 1.0f / temperature;
+  m->sample_seed = seed;
   return kOk;
 }
 

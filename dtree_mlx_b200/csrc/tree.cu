@@ -18,24 +18,6 @@ constexpr int kMaxRows = 64;
 constexpr int kMaxK = 128;                       // k = min(budget, vocab) <= 127
 
 // ============================================================ planted logits
-__host__ __device__ __forceinline__ void philox4x32_10(uint32_t c[4], uint32_t k0, uint32_t k1) {
-  for (int r = 0; r < 10; ++r) {
-    if (r > 0) {
-      k0 += 0x9E3779B9u;
-      k1 += 0xBB67AE85u;
-    }
-    const uint64_t p0 = static_cast<uint64_t>(0xD2511F53u) * c[0];
-    const uint64_t p1 = static_cast<uint64_t>(0xCD9E8D57u) * c[2];
-    const uint32_t hi0 = static_cast<uint32_t>(p0 >> 32), lo0 = static_cast<uint32_t>(p0);
-    const uint32_t hi1 = static_cast<uint32_t>(p1 >> 32), lo1 = static_cast<uint32_t>(p1);
-    const uint32_t n0 = hi1 ^ c[1] ^ k0, n2 = hi0 ^ c[3] ^ k1;
-    c[0] = n0;
-    c[1] = lo1;
-    c[2] = n2;
-    c[3] = lo0;
-  }
-}
-
 constexpr uint32_t kNoiseTag = 0xD1CEu;
 constexpr uint32_t kPlantTag = 0xB1A5u;
 constexpr uint32_t kKeyHi = 0x5EED0001u;
@@ -506,20 +488,25 @@ __global__ void __launch_bounds__(32) heap_tree_kernel(const int32_t* __restrict
 // ============================================================ chain (DFlash)
 // grid = rows, block 256: per-row argmax (first index on ties); then the last
 // block writes the chain tree.
+// inv_temp > 0: the drafted token is sampled from softmax(logits * inv_temp)
+// (sample_tokens, runtime.py:12-19) by the Gumbel-max rule; 0: argmax
 __global__ void chain_argmax_kernel(const float* __restrict__ logits, int rows, int vocab,
                                     dtree_step_state* state, int32_t* __restrict__ tree_tokens,
                                     int32_t* __restrict__ parents, int32_t* __restrict__ depths,
-                                    int32_t* __restrict__ positions, uint64_t* __restrict__ anc_mask) {
+                                    int32_t* __restrict__ positions, uint64_t* __restrict__ anc_mask, float inv_temp,
+                                    uint32_t seed) {
   pdl_trigger();
   __shared__ float s_v[32];
   __shared__ int s_i[32];
   const int r = blockIdx.x;
   pdl_wait();
+  const uint32_t step = static_cast<uint32_t>(state->step);
   const float* row = logits + static_cast<size_t>(r) * vocab;
   float bv = -INFINITY;
   int bi = 0x7FFFFFFF;
   for (int v = threadIdx.x; v < vocab; v += blockDim.x) {
-    const float x = row[v];
+    float x = row[v];
+    if (inv_temp > 0.0f) x = x * inv_temp + gumbel_noise(seed, kSampleTagDraft, step, r, v);
     if (x > bv || (x == bv && v < bi)) {
       bv = x;
       bi = v;
@@ -785,7 +772,22 @@ extern "C" int dtree_chain_build(const float* draft_logits, int rows, int vocab,
   DTREE_CHECK_ARG(rows >= 1 && rows < DTREE_MAX_TREE, "rows must be in [1, 127]");
   DTREE_CHECK_ARG(vocab > 0, "vocab must be positive");
   DTREE_CUDA_RET(launch_pdl(chain_argmax_kernel, dim3(rows), dim3(256), 0, stream, draft_logits, rows, vocab, state,
-                            tree_tokens, parents, depths, positions, anc_mask));
+                            tree_tokens, parents, depths, positions, anc_mask, 0.0f, 0u));
+  return kOk;
+}
+
+extern "C" int dtree_chain_sample(const float* draft_logits, int rows, int vocab, float temperature, uint32_t seed,
+                                  dtree_step_state* state, int32_t* tree_tokens, int32_t* parents, int32_t* depths,
+                                  int32_t* positions, uint64_t* anc_mask, void* stream_) {
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  DTREE_CHECK_ARG(draft_logits && state && tree_tokens && parents && depths && positions && anc_mask,
+                  "null pointer");
+  DTREE_CHECK_ARG(rows >= 1 && rows < DTREE_MAX_TREE, "rows must be in [1, 127]");
+  DTREE_CHECK_ARG(vocab > 0, "vocab must be positive");
+  DTREE_CHECK_ARG(temperature >= 0.0f, "temperature must be >= 0");
+  const float inv_temp = temperature < 1e-5f ? 0.0f : 1.0f / temperature;
+  DTREE_CUDA_RET(launch_pdl(chain_argmax_kernel, dim3(rows), dim3(256), 0, stream, draft_logits, rows, vocab, state,
+                            tree_tokens, parents, depths, positions, anc_mask, inv_temp, seed));
   return kOk;
 }
 

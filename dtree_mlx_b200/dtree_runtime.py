@@ -100,7 +100,9 @@ def follow_verified_tree(child_maps: list[dict[int, int]], posterior_tokens: lis
 def dtree_generate(target, draft, prompt_tokens, max_new_tokens: int, temperature: float, stop_token_ids,
                    layer_ids, speculative_tokens: int | None, tree_budget: int | None = None,
                    verify_mode: str = "parallel-replay", profile: bool = False):
-    """dtree_runtime.py:293-586 (temperature 0)."""
+    """dtree_runtime.py:293-586.  ``parallel-replay`` at temperature >= 1e-5
+    samples every node's posterior token (dtree_runtime.py:455-470) on the
+    device; the tree itself does not depend on the temperature."""
     del layer_ids
     if not target.supports_tree_verification():
         raise NotImplementedError(f"DTree is not implemented for target adapter family={target.adapter.family!r}.")
@@ -108,8 +110,6 @@ def dtree_generate(target, draft, prompt_tokens, max_new_tokens: int, temperatur
         raise ValueError("DTree only supports verify_mode='parallel-replay' or 'parallel-greedy-argmax'.")
     if verify_mode == "parallel-greedy-argmax" and temperature >= 1e-5:
         raise ValueError("DTree parallel-greedy-argmax only supports temperature=0.")
-    if temperature >= 1e-5:
-        raise NotImplementedError("temperature > 0 (sampled verify) is not implemented on the B200 path yet")
     if speculative_tokens is None:
         block_size = draft.block_size
     else:
@@ -120,6 +120,6 @@ def dtree_generate(target, draft, prompt_tokens, max_new_tokens: int, temperatur
     if budget > 127:
         raise ValueError("tree_budget must be <= 127 (128 tree rows per verify)")
     out, metrics = run_decode(target, draft, prompt_tokens, max_new_tokens, set(stop_token_ids or ()), "dtree",
-                              block_size, budget, profile=profile)
+                              block_size, budget, profile=profile, temperature=temperature)
     metrics["verify_mode"] = verify_mode
     return out, metrics

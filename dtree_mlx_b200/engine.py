@@ -147,6 +147,11 @@ class Qwen3Engine:
         except Exception:
             pass
 
+    def set_sampling(self, temperature: float, seed: int) -> None:
+        """Posterior tokens of later forwards: greedy (temperature < 1e-5) or
+        sampled at `temperature` with Philox noise keyed by seed and step."""
+        call("dtree_qwen3_set_sampling", self._handle, float(temperature), int(seed) & 0xFFFFFFFF)
+
     def forward_tree(self, tokens: torch.Tensor, positions: torch.Tensor, anc: torch.Tensor, n_nodes: int,
                      state: torch.Tensor, posterior: torch.Tensor | None) -> None:
         """Tree-verify forward of rows [0, n_nodes) at prefix length state.start."""
@@ -178,6 +183,8 @@ class StepConfig:
     rows: int            # draft rows (block_size - 1)
     budget: int          # tree budget (dtree) / rows (dflash)
     n_nodes: int         # tree rows per verify (root included)
+    temperature: float = 0.0  # sampled drafts / posteriors above 1e-5 (runtime.py:12-19)
+    seed: int = 0             # Philox key of the sampling noise
 
 
 def dtree_nodes(budget: int, rows: int, vocab: int) -> int:
@@ -229,6 +236,9 @@ class DecodeSession:
         self.output[:n] = toks
         if hasattr(eng, "reset_states"):  # a new sequence starts from zero recurrent state
             eng.reset_states()
+        # the prompt's sampling noise (temperature > 0) gets its own stream:
+        # step -1, never used by a decode step
+        self.state[2] = -1
         start = 0
         hidden_rows = []
         while start < n:
@@ -268,7 +278,7 @@ class DecodeSession:
         if c.mode == "dtree":
             self.builder.build(self.draft_logits, self.state, self.tree, keep_topk=False)
         else:
-            kernels.chain_build(self.draft_logits[: c.rows], self.state, self.tree)
+            kernels.chain_build(self.draft_logits[: c.rows], self.state, self.tree, c.temperature, c.seed)
         eng.verify(self)
         kernels.accept_walk(self.tree, self.posterior, self.state, self.accepted, self.output, self.history)
         eng.commit_step(self)

@@ -97,6 +97,10 @@ class Qwen35Engine:
         call("dtree_qwen35_forward", self._handle, ptr(tokens), ptr(positions), ptr(parents), ptr(anc),
              int(n_nodes), int(mode), ptr(state), ptr(posterior), stream_ptr())
 
+    def set_sampling(self, temperature: float, seed: int) -> None:
+        """As Qwen3Engine.set_sampling."""
+        call("dtree_qwen35_set_sampling", self._handle, float(temperature), int(seed) & 0xFFFFFFFF)
+
     def commit(self, parents, accepted, state) -> None:
         call("dtree_qwen35_commit", self._handle, ptr(parents), ptr(accepted), ptr(state), stream_ptr())
 

@@ -99,11 +99,19 @@ def tree_from_topk(top_ids: torch.Tensor, top_lp: torch.Tensor, budget: int, sta
          ptr(out.parents), ptr(out.depths), ptr(out.positions), ptr(out.anc), stream_ptr())
 
 
-def chain_build(draft_logits: torch.Tensor, state: torch.Tensor, out: TreeBuffers) -> None:
+def chain_build(draft_logits: torch.Tensor, state: torch.Tensor, out: TreeBuffers, temperature: float = 0.0,
+                seed: int = 0) -> None:
+    """DFlash chain: drafted token of row i = argmax (temperature < 1e-5) or a
+    draw from softmax(row / temperature) (sample_tokens, runtime.py:12-19)."""
     _cuda(draft_logits, "draft_logits", torch.float32)
     rows, vocab = draft_logits.shape
-    call("dtree_chain_build", ptr(draft_logits), rows, vocab, ptr(state), ptr(out.tokens), ptr(out.parents),
-         ptr(out.depths), ptr(out.positions), ptr(out.anc), stream_ptr())
+    if temperature < 1e-5:
+        call("dtree_chain_build", ptr(draft_logits), rows, vocab, ptr(state), ptr(out.tokens), ptr(out.parents),
+             ptr(out.depths), ptr(out.positions), ptr(out.anc), stream_ptr())
+    else:
+        call("dtree_chain_sample", ptr(draft_logits), rows, vocab, float(temperature), int(seed) & 0xFFFFFFFF,
+             ptr(state), ptr(out.tokens), ptr(out.parents), ptr(out.depths), ptr(out.positions), ptr(out.anc),
+             stream_ptr())
 
 
 def plant_draft_logits(out: torch.Tensor, seed: int, state: torch.Tensor, continuation: torch.Tensor | None,
@@ -188,6 +196,24 @@ def linear_q4(x: torch.Tensor, w, out: torch.Tensor | None = None, split_k: int 
     ws = _workspace(("gemm", t_pad), nbytes, x.device)
     call("dtree_linear_q4", ptr(x), t_pad, k, ptr(w.packed), ptr(w.scales), ptr(w.biases), n, ptr(out), ptr(ws),
          ws.numel(), int(split_k), stream_ptr())
+    return out
+
+
+def lm_head_sample(h: torch.Tensor, embed: torch.Tensor, n_rows: int, temperature: float, seed: int,
+                   state: torch.Tensor, out: torch.Tensor | None = None):
+    """Token per row t < n_rows drawn from softmax(bf16(h[t] . embed) / T)
+    (Gumbel-max, Philox keyed by seed and state.step); T < 1e-5: argmax."""
+    _cuda(h, "h", torch.bfloat16)
+    _cuda(embed, "embed", torch.bfloat16)
+    _cuda(state, "state", torch.int32)
+    t_pad, hidden = h.shape
+    vocab = embed.shape[0]
+    if out is None:
+        out = torch.empty(n_rows, dtype=torch.int32, device=h.device)
+    nbytes = int(_lib.load().dtree_lm_head_workspace_bytes(t_pad))
+    ws = _workspace(("lmhead", t_pad), nbytes, h.device)
+    call("dtree_lm_head_sample", ptr(h), t_pad, n_rows, hidden, ptr(embed), vocab, float(temperature),
+         int(seed) & 0xFFFFFFFF, ptr(state), ptr(out), ptr(ws), ws.numel(), stream_ptr())
     return out
 
 

@@ -86,11 +86,25 @@ class _StateReader:
         return self.host.tolist()
 
 
+def _sampling_seed(temperature: float) -> int:
+    """Philox key of one sampled generation, drawn from torch's generator (so
+    DFlashGenerator(seed=...) fixes the sequence of generations)."""
+    if temperature < 1e-5:
+        return 0
+    return int(torch.randint(0, 2**31 - 1, (1,)).item())
+
+
 def run_decode(target, draft, prompt_tokens, max_new_tokens: int, stop_token_ids: set[int], mode: str,
                block_size: int, budget: int, profile: bool = False, use_graph: bool = True,
-               session: DecodeSession | None = None) -> tuple[list[int], dict[str, Any]]:
-    """Device decode loop shared by dtree_generate and dflash_generate."""
+               session: DecodeSession | None = None, temperature: float = 0.0,
+               seed: int | None = None) -> tuple[list[int], dict[str, Any]]:
+    """Device decode loop shared by dtree_generate and dflash_generate.
+    temperature >= 1e-5 samples the first token, the posterior of every
+    tree / chain node and (DFlash) the drafted tokens (runtime.py:12-19)."""
     engine = target.adapter.engine(target.model, draft)
+    temperature = float(temperature)
+    seed = _sampling_seed(temperature) if seed is None else int(seed)
+    engine.set_sampling(temperature, seed)
     prompt = _as_list(prompt_tokens)
     prompt_len = len(prompt)
     total_max_tokens = prompt_len + int(max_new_tokens)
@@ -102,7 +116,8 @@ def run_decode(target, draft, prompt_tokens, max_new_tokens: int, stop_token_ids
             f"prompt + max_new_tokens + tree ({total_max_tokens + n_nodes + 1}) exceeds the KV capacity "
             f"{engine.kv_capacity}"
         )
-    cfg = StepConfig(mode=mode, rows=rows, budget=budget if mode == "dtree" else rows, n_nodes=n_nodes)
+    cfg = StepConfig(mode=mode, rows=rows, budget=budget if mode == "dtree" else rows, n_nodes=n_nodes,
+                     temperature=temperature if temperature >= 1e-5 else 0.0, seed=seed)
     if hasattr(draft, "_buffer"):
         draft._buffer(engine.device)  # fix the drafter's device buffers before any capture
     if session is None:
@@ -213,7 +228,7 @@ def _profiled_step(session: DecodeSession, stages: dict[str, float]) -> None:
     if c.mode == "dtree":
         session.builder.build(session.draft_logits, session.state, session.tree, keep_topk=False)
     else:
-        kernels.chain_build(session.draft_logits[: c.rows], session.state, session.tree)
+        kernels.chain_build(session.draft_logits[: c.rows], session.state, session.tree, c.temperature, c.seed)
     ev[2].record()
     eng.verify(session)
     ev[3].record()
@@ -234,15 +249,19 @@ def _profiled_step(session: DecodeSession, stages: dict[str, float]) -> None:
 def dflash_generate(target, draft, prompt_tokens, max_new_tokens: int, temperature: float, stop_token_ids,
                     layer_ids, speculative_tokens: int | None, verify_mode: str, verify_chunk_size: int = 4,
                     profile: bool = False):
-    """runtime.py:430-610 (greedy ``parallel-greedy-argmax`` / ``parallel-replay``
-    at temperature 0): verify the drafted block as a chain tree."""
+    """runtime.py:430-610: verify the drafted block as a chain tree.  Every
+    verify mode reduces to the same device step: the block's posterior tokens
+    (greedy, or sampled at ``temperature`` like sample_tokens in the
+    parallel-replay / lazy-logits / stream / chunked verifiers) and the
+    longest prefix match of the drafted tokens (drafted by argmax, or sampled
+    at ``temperature``, runtime.py:486)."""
     del layer_ids, verify_chunk_size
     if verify_mode not in {"parallel-replay", "parallel-greedy-argmax", "parallel-lazy-logits", "stream", "chunked"}:
         raise ValueError(f"Unknown verify_mode={verify_mode!r}")
-    if temperature >= 1e-5:
-        raise NotImplementedError("temperature > 0 (sampled verify) is not implemented on the B200 path yet")
+    if verify_mode == "parallel-greedy-argmax" and temperature >= 1e-5:
+        raise ValueError("parallel-greedy-argmax only supports temperature=0.")
     block_size = draft.block_size if speculative_tokens is None else max(1, min(speculative_tokens, draft.block_size))
     if block_size < 2:
         raise ValueError("DFlash requires speculative_tokens >= 2 on the B200 path.")
     return run_decode(target, draft, prompt_tokens, max_new_tokens, set(stop_token_ids or ()), "dflash",
-                      block_size, block_size - 1, profile=profile)
+                      block_size, block_size - 1, profile=profile, temperature=temperature)

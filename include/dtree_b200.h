@@ -132,6 +132,15 @@ DTREE_API int dtree_chain_build(const float* draft_logits, int rows, int vocab, 
                       int32_t* tree_tokens, int32_t* parents, int32_t* depths, int32_t* positions,
                       uint64_t* anc_mask, void* stream);
 
+/* The same chain with the drafted tokens sampled at `temperature`
+ * (sample_tokens, runtime.py:12-19, called on the draft logits at
+ * runtime.py:486): node i+1 = a draw from softmax(draft row i / T) by the
+ * Gumbel-max rule with Philox noise keyed by (seed, state->step, row,
+ * token); temperature < 1e-5 is the argmax of dtree_chain_build. */
+DTREE_API int dtree_chain_sample(const float* draft_logits, int rows, int vocab, float temperature, uint32_t seed,
+                      dtree_step_state* state, int32_t* tree_tokens, int32_t* parents, int32_t* depths,
+                      int32_t* positions, uint64_t* anc_mask, void* stream);
+
 /* -------------------------------------------------- planted draft logits
  * Synthetic drafter of the benchmark workloads (stands in for
  * DFlashDraftModel + lm_head_logits, dtree_runtime.py:366-376): row r gets
@@ -202,6 +211,17 @@ DTREE_API int dtree_linear_q4(const void* x, int t_pad, int k, const void* w_pac
 DTREE_API size_t dtree_lm_head_workspace_bytes(int t_pad);
 DTREE_API int dtree_lm_head_argmax(const void* h, int t_pad, int n_rows, int hidden, const void* embed, int vocab,
                          int32_t* out, void* workspace, size_t workspace_bytes, void* stream);
+
+/* LM head fused with sampling at `temperature` (runtime.py:12-19
+ * sample_tokens: categorical over logits / T, used by the parallel-replay
+ * verify, runtime.py:177 and dtree_runtime.py:460): out[t] = argmax_v
+ * (bf16(h[t]·E[v]) / T + G), G standard Gumbel noise from Philox keyed by
+ * (seed, state->step, t, v) -- a draw from softmax(logits / T) without
+ * writing the logits.  temperature < 1e-5: the argmax above (state may then
+ * be NULL). */
+DTREE_API int dtree_lm_head_sample(const void* h, int t_pad, int n_rows, int hidden, const void* embed, int vocab,
+                         float temperature, uint32_t seed, const dtree_step_state* state, int32_t* out,
+                         void* workspace, size_t workspace_bytes, void* stream);
 
 /* ----------------------------------------------------- tree attention
  * softmax(q k^T / sqrt(head_dim) + tree mask) v for the tree rows of one
@@ -357,6 +377,13 @@ DTREE_API int dtree_qwen3_forward_tree(dtree_qwen3_model* model, const int32_t* 
                              const uint64_t* anc_mask, int n_nodes, const dtree_step_state* state,
                              int32_t* posterior, void* stream);
 
+/* Posterior tokens of later forwards are sampled at `temperature`
+ * (dtree_lm_head_sample with this seed and the forward's state->step)
+ * instead of the greedy argmax; temperature < 1e-5 restores the argmax.
+ * Replaces the temperature argument of the parallel-replay verify
+ * (runtime.py:160-215, dtree_runtime.py:455-470). */
+DTREE_API int dtree_qwen3_set_sampling(dtree_qwen3_model* model, float temperature, uint32_t seed);
+
 /* ----------------------------------------------- DFlash block drafter
  * The drafter (DFlashDraftModel, draft.py:318-367) is a stack of Qwen3
  * decoder layers held as a dtree_qwen3 model whose `embed` is the TARGET's
@@ -483,6 +510,9 @@ DTREE_API int dtree_qwen35_forward(dtree_qwen35_model* model, const int32_t* tok
  * dtree_step_commit. */
 DTREE_API int dtree_qwen35_commit(dtree_qwen35_model* model, const int32_t* parents, const int32_t* accepted,
                         const dtree_step_state* state, void* stream);
+
+/* As dtree_qwen3_set_sampling, for the hybrid model. */
+DTREE_API int dtree_qwen35_set_sampling(dtree_qwen35_model* model, float temperature, uint32_t seed);
 
 #ifdef __cplusplus
 }
