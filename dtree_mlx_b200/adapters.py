@@ -491,16 +491,42 @@ def quantize_target_model(target: "LoadedTargetModel", bits: int = 4, group_size
     return {"group_size": group_size, "bits": bits}
 
 
-def load_target_model(path_or_repo: str, device: str = "cuda") -> LoadedTargetModel:
-    """adapters.py:822-846.  Checkpoints are not available offline; the
-    ``synthetic:<preset>`` spec builds a seeded random-init target of a
-    BASELINE shape (``qwen3-tiny``, ``qwen3-4b``, ``qwen35-tiny``,
-    ``qwen35-9b``)."""
+def _tokenizer_for(path: Path):
+    """The checkpoint's own tokenizer when its files are present (transformers,
+    local files only); else the byte stand-in."""
+    try:
+        from transformers import AutoTokenizer
+
+        tok = AutoTokenizer.from_pretrained(str(path), local_files_only=True)
+        eos = tok.eos_token_id
+        tok.eos_token_ids = set(eos if isinstance(eos, list) else ([eos] if eos is not None else []))
+        return tok
+    except Exception:
+        return ByteTokenizer()
+
+
+def load_target_model(path_or_repo: str, device: str = "cuda", kv_capacity: int = 4096) -> LoadedTargetModel:
+    """adapters.py:822-846.  ``path_or_repo`` is a checkpoint directory
+    (config.json + model*.safetensors, MLX or Hugging Face layout: see
+    ``weights_io``) or ``synthetic:<preset>[:seed=N][:kv=N]``, a seeded
+    random-init target of a BASELINE shape (``qwen3-tiny``, ``qwen3-4b``,
+    ``qwen35-tiny``, ``qwen35-9b``).  There is no hub download offline."""
     if not str(path_or_repo).startswith("synthetic:"):
-        raise NotImplementedError(
-            f"Unsupported target {path_or_repo!r}: checkpoint loading is not implemented in this build; "
-            f"use 'synthetic:<preset>' with preset in {sorted(PRESETS)}."
-        )
+        path = Path(path_or_repo)
+        if not (path / "config.json").exists():
+            raise NotImplementedError(
+                f"Unsupported target {path_or_repo!r}: expected a local checkpoint directory with config.json "
+                f"or 'synthetic:<preset>' with preset in {sorted(PRESETS) + sorted(QWEN35_PRESETS)}."
+            )
+        from .weights_io import load_target_weights
+
+        model_type, weights = load_target_weights(path, device)
+        adapter_cls = adapter_for_model_type(model_type)
+        if adapter_cls is None:
+            registered = ", ".join(sorted(ADAPTERS))
+            raise NotImplementedError(f"Unsupported target model_type={model_type!r}. Current adapters: {registered}.")
+        model = SyntheticQwen3(weights.cfg, weights, kv_capacity=int(kv_capacity), seed=0)
+        return LoadedTargetModel(str(path_or_repo), path, model, _tokenizer_for(path), adapter_cls())
     spec = parse_synthetic_spec(path_or_repo)
     if spec["preset"] in QWEN35_PRESETS:
         from .synthetic import random_qwen35_weights
