@@ -180,6 +180,7 @@ PROTOTYPES = {
     "dtree_qwen35_forward": (I, [P, P, P, P, P, I, I, P, P, P]),
     "dtree_qwen35_commit": (I, [P, P, P, P, P]),
     "dtree_dflash_context": (I, [P, P, P, P, I, I, I, I, P, P]),
+    "dtree_dflash_context_ring": (I, [P, P, P, P, I, I, I, I, P, P, I, I, P]),
     "dtree_dflash_block": (I, [P, I, I, P, P, P]),
     "dtree_qwen3_forward_logits": (I, [P, P, P, P, I, P, P, P]),
     "dtree_tree_attention_workspace_bytes": (SZ, [I, I, I, I]),

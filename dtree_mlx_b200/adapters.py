@@ -410,6 +410,22 @@ class ByteTokenizer:
         return bytes(int(t) % 256 for t in tokens).decode("utf-8", errors="replace")
 
 
+class Qwen35TextModel:
+    """The text model of a Qwen3.5 target as lazy_follow_tree_exact reaches it
+    (``target.model.model``; custom_qwen35_model.py ``forward_dflash``): a
+    causal forward of the given tokens that appends their K/V and advances
+    the DeltaNet conv / recurrent states, returning (norm_hidden,
+    verifier_hidden) [1, n, ...]."""
+
+    def __init__(self, adapter: "Qwen35TargetAdapter", container: SyntheticQwen3):
+        self._adapter = adapter
+        self._container = container
+
+    def forward_dflash(self, inputs, cache, layer_ids):
+        tokens = [int(t) for t in torch.as_tensor(inputs).reshape(-1).tolist()]
+        return self._adapter._forward(self._container, tokens, cache, layer_ids)
+
+
 @dataclass
 class LoadedTargetModel:
     """adapters.py:681-819."""
@@ -419,6 +435,10 @@ class LoadedTargetModel:
     model: Any
     tokenizer: Any
     adapter: TargetAdapter
+
+    def __post_init__(self):
+        if isinstance(self.adapter, Qwen35TargetAdapter) and not hasattr(self.model, "model"):
+            self.model.model = Qwen35TextModel(self.adapter, self.model)
 
     def build_prompt(self, prompt_text: str):
         return self.adapter.build_prompt(self.tokenizer, prompt_text)

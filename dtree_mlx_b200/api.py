@@ -55,6 +55,9 @@ class DFlashGenerator:
             self.target_quantization = quantize_target_model(self.target, target_quant_bits, target_quant_group_size)
         self.draft, self.draft_path = load_draft_model(draft_model, target=self.target)
         self.draft_attention_mask = "none" if draft_attention_mask == "auto" else draft_attention_mask
+        if hasattr(self.draft, "cache_mode"):
+            # api.py:62-64: the drafter keeps a context-only cache for Qwen3.5 targets
+            self.draft.cache_mode = "context-only" if self.target.adapter.family == "qwen3_5" else "kv"
         self.draft_quantization = None
         del target_quant_group_size, draft_quant_group_size
 

@@ -249,9 +249,50 @@ extern "C" int dtree_qwen3_forward_logits(dtree_qwen3_model* m, const int32_t* t
   return forward_impl(m, tokens, positions, anc_mask, n_rows, state, nullptr, logits, stream_);
 }
 
+// context-only draft cache bookkeeping after an append of `host_count` rows
+// (>= 0) or of state->n_accepted rows (host_count < 0): reserved (rows
+// appended so far) grows by that count, start (the attended context
+// length) = min(reserved, sink + window)
+__global__ void ring_advance_kernel(dtree_step_state* ring, const dtree_step_state* state, int host_count, int sink,
+                                    int window) {
+  pdl_trigger();
+  pdl_wait();
+  if (threadIdx.x == 0 && blockIdx.x == 0) {
+    const int n = host_count >= 0 ? host_count : state->n_accepted;
+    const int total = ring->reserved + n;
+    ring->reserved = total;
+    ring->start = total < sink + window ? total : sink + window;
+  }
+}
+
+static int dflash_context_impl(dtree_qwen3_model* m, const void* fc_weight, const void* hidden_norm,
+                               const void* target_hidden, int ld_hidden, int width, int n_rows, int ctx_base,
+                               const dtree_step_state* state, dtree_step_state* ring_state, int sink, int window,
+                               void* stream_);
+
+extern "C" int dtree_dflash_context_ring(dtree_qwen3_model* m, const void* fc_weight, const void* hidden_norm,
+                                         const void* target_hidden, int ld_hidden, int width, int n_rows,
+                                         int ctx_base, const dtree_step_state* state, dtree_step_state* ring_state,
+                                         int sink, int window, void* stream_) {
+  DTREE_CHECK_ARG(ring_state, "null ring state");
+  DTREE_CHECK_ARG(sink >= 0 && window > 0, "sink must be >= 0 and window > 0");
+  DTREE_CHECK_ARG(m && sink + window + m->d.t_cap <= m->d.kv_capacity,
+                  "draft cache capacity below sink + window + block rows");
+  return dflash_context_impl(m, fc_weight, hidden_norm, target_hidden, ld_hidden, width, n_rows, ctx_base, state,
+                             ring_state, sink, window, stream_);
+}
+
 extern "C" int dtree_dflash_context(dtree_qwen3_model* m, const void* fc_weight, const void* hidden_norm,
                                     const void* target_hidden, int ld_hidden, int width, int n_rows, int ctx_base,
                                     const dtree_step_state* state, void* stream_) {
+  return dflash_context_impl(m, fc_weight, hidden_norm, target_hidden, ld_hidden, width, n_rows, ctx_base, state,
+                             nullptr, 0, 0, stream_);
+}
+
+static int dflash_context_impl(dtree_qwen3_model* m, const void* fc_weight, const void* hidden_norm,
+                               const void* target_hidden, int ld_hidden, int width, int n_rows, int ctx_base,
+                               const dtree_step_state* state, dtree_step_state* ring_state, int sink, int window,
+                               void* stream_) {
   DTREE_CHECK_ARG(m && fc_weight && hidden_norm && target_hidden && state, "null pointer");
   const dtree_qwen3_desc& d = m->d;
   DTREE_CHECK_ARG(n_rows > 0 && n_rows <= d.t_cap, "n_rows must be in [1, t_cap]");
@@ -308,8 +349,14 @@ extern "C" int dtree_dflash_context(dtree_qwen3_model* m, const void* fc_weight,
     f.slot_mode = ctx_base >= 0 ? 2 : 1;
     f.ctx_base = ctx_base;
     f.ctx_count = n_rows;
+    f.ring_state = ring_state;
+    f.ring_sink = ring_state ? sink : 0;
+    f.ring_window = ring_state ? window : 0;
     if ((rc = qkv_finish_launch(f, n_rows, st))) return rc;
   }
+  if (ring_state)
+    DTREE_CUDA_RET(launch_pdl(ring_advance_kernel, dim3(1), dim3(32), 0, st, ring_state, state,
+                              ctx_base >= 0 ? n_rows : -1, sink, window));
   return kOk;
 }
 

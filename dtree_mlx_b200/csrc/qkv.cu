@@ -54,6 +54,10 @@ __global__ void __launch_bounds__(256) qkv_finish_kernel(QkvFinishParams p) {
     if (t >= cnt) return;  // uniform per block
     slot = base + t;
     pos_t = static_cast<float>(slot);
+    if (p.ring_window > 0) {
+      const int r = (p.slot_mode == 1 ? p.ring_state->reserved : base) + t;
+      slot = ring_slot(r, p.ring_sink, p.ring_window);
+    }
   } else {
     pos_t = static_cast<float>(p.positions[t]);
   }

@@ -28,7 +28,19 @@ struct QkvFinishParams {
   // step accepted) and slot_mode 2 the host values ctx_base / ctx_count
   int slot_mode;
   int ctx_base, ctx_count;
+  // context-only draft cache (sink + sliding window, draft.py:69-112): the
+  // context row r (r-th row appended since the prompt) goes to slot r for
+  // r < ring_sink, else ring_sink + (r - ring_sink) % ring_window; in
+  // slot_mode 1 the rows continue at ring_state->reserved (rows appended so
+  // far).  ring_window 0: slot = row position.
+  const dtree_step_state* ring_state;
+  int ring_sink, ring_window;
 };
+
+// slot of context row r in a sink + window ring
+__device__ __forceinline__ int ring_slot(int r, int sink, int window) {
+  return r < sink ? r : sink + (r - sink) % window;
+}
 
 int qkv_finish_launch(const QkvFinishParams& p, int n_rows, cudaStream_t stream);
 

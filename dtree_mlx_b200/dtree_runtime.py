@@ -3,10 +3,14 @@
 ``build_dtree_tree``, ``compile_dtree_tree`` and ``follow_verified_tree``
 keep the reference's signatures and return values but run on the GPU
 (``dtree_tree_build`` / ``dtree_accept_walk``); ``dtree_generate`` is the
-device-resident decode loop (see runtime.run_decode).
+device-resident decode loop (see runtime.run_decode), or for a Qwen3.5
+target the lazy branch-following loop (``lazy_follow_tree_exact``,
+runtime.run_decode_lazy) unless ``DTREE_QWEN35_TREE_MODE=full_tree``, as in
+dtree_runtime.py:355-361.
 """
 from __future__ import annotations
 
+import os
 import time
 
 import numpy as np
@@ -97,6 +101,55 @@ def follow_verified_tree(child_maps: list[dict[int, int]], posterior_tokens: lis
     return acc[: st["n_accepted"]].tolist(), st["bonus_token"]
 
 
+def _text_model(target):
+    model = target.model
+    if hasattr(model, "language_model") and hasattr(model.language_model, "model"):
+        return model.language_model.model
+    if hasattr(model, "model"):
+        return model.model
+    raise AttributeError(f"Unsupported qwen3_5 target model: {type(model)!r}")
+
+
+def lazy_follow_tree_exact(target, target_cache, layer_ids, tree_tokens: list[int],
+                           child_maps: list[dict[int, int]], temperature: float, verify_mode: str,
+                           profile_times: dict[str, float] | None):
+    """dtree_runtime.py:211-290: verify only the branch the target follows.
+    Starting at the root, each step runs ONE token through the target as a
+    plain causal decode (its K/V appended, the DeltaNet states advanced), takes
+    the posterior token (argmax for parallel-greedy-argmax, else
+    sample_tokens at ``temperature``) and moves to the child with that token;
+    it stops at the first posterior that is not a child.  The cache then
+    holds exactly the accepted path, so nothing is compacted or rolled back.
+    Returns (accepted node indices, posterior token, verifier hiddens of the
+    accepted nodes concatenated along axis 1)."""
+    from .runtime import sample_tokens
+
+    if target.adapter.family != "qwen3_5":
+        raise NotImplementedError("lazy_follow_tree_exact is only implemented for qwen3_5.")
+    text_model = _text_model(target)
+    accepted: list[int] = []
+    hidden_chunks = []
+    current = 0
+    while True:
+        t0 = time.perf_counter()
+        ids = torch.tensor([[int(tree_tokens[current])]], dtype=torch.int32)
+        norm_hidden, verifier_hidden = text_model.forward_dflash(ids, target_cache, layer_ids)
+        if profile_times is not None:
+            profile_times["verify_tree_forward_time_s"] = profile_times.get("verify_tree_forward_time_s", 0.0) + (
+                time.perf_counter() - t0)
+        accepted.append(current)
+        hidden_chunks.append(verifier_hidden)
+        if verify_mode == "parallel-greedy-argmax":
+            posterior = target.lm_head_argmax(norm_hidden)
+        else:
+            posterior = sample_tokens(target.lm_head_logits(norm_hidden), temperature)
+        token = int(torch.as_tensor(posterior).reshape(-1)[0].item())
+        nxt = child_maps[current].get(token)
+        if nxt is None:
+            return accepted, token, torch.cat([torch.as_tensor(h) for h in hidden_chunks], dim=1)
+        current = nxt
+
+
 def dtree_generate(target, draft, prompt_tokens, max_new_tokens: int, temperature: float, stop_token_ids,
                    layer_ids, speculative_tokens: int | None, tree_budget: int | None = None,
                    verify_mode: str = "parallel-replay", profile: bool = False):
@@ -119,7 +172,15 @@ def dtree_generate(target, draft, prompt_tokens, max_new_tokens: int, temperatur
     budget = max(tree_budget if tree_budget is not None else block_size - 1, 0)
     if budget > 127:
         raise ValueError("tree_budget must be <= 127 (128 tree rows per verify)")
-    out, metrics = run_decode(target, draft, prompt_tokens, max_new_tokens, set(stop_token_ids or ()), "dtree",
-                              block_size, budget, profile=profile, temperature=temperature)
+    if target.adapter.family == "qwen3_5" and os.environ.get("DTREE_QWEN35_TREE_MODE") != "full_tree":
+        # the reference's default for the hybrid (dtree_runtime.py:355-361):
+        # follow only the taken branch, one token per target forward
+        from .runtime import run_decode_lazy
+
+        out, metrics = run_decode_lazy(target, draft, prompt_tokens, max_new_tokens, set(stop_token_ids or ()),
+                                       block_size, budget, temperature, verify_mode, profile=profile)
+    else:
+        out, metrics = run_decode(target, draft, prompt_tokens, max_new_tokens, set(stop_token_ids or ()), "dtree",
+                                  block_size, budget, profile=profile, temperature=temperature)
     metrics["verify_mode"] = verify_mode
     return out, metrics

@@ -217,6 +217,114 @@ def run_decode(target, draft, prompt_tokens, max_new_tokens: int, stop_token_ids
     return output_tokens, metrics
 
 
+def run_decode_lazy(target, draft, prompt_tokens, max_new_tokens: int, stop_token_ids: set[int], block_size: int,
+                    budget: int, temperature: float, verify_mode: str, profile: bool = False
+                    ) -> tuple[list[int], dict[str, Any]]:
+    """dtree_generate's loop (dtree_runtime.py:364-552) with the lazy
+    Qwen3.5 verify (``lazy_follow_tree_exact``): per step the draft and the
+    best-first tree run on the device; the host then walks the tree one
+    target token at a time (each a causal 1-token forward through the
+    engine, whose cache ends up holding exactly the accepted path) and
+    commits the accepted tokens and the posterior token."""
+    from .adapters import SequenceCache
+    from .dtree_runtime import lazy_follow_tree_exact
+
+    engine = target.adapter.engine(target.model, draft)
+    prompt = _as_list(prompt_tokens)
+    prompt_len = len(prompt)
+    total = prompt_len + int(max_new_tokens)
+    vocab = engine.cfg.vocab_size
+    rows = block_size - 1
+    n_nodes = dtree_nodes(budget, rows, vocab)
+    if total + n_nodes + 1 > engine.kv_capacity:
+        raise ValueError(f"prompt + max_new_tokens + tree ({total + n_nodes + 1}) exceeds the KV capacity "
+                         f"{engine.kv_capacity}")
+    temperature = float(temperature)
+    seed = _sampling_seed(temperature)
+    engine.set_sampling(temperature, seed)
+    cfg = StepConfig(mode="dtree", rows=rows, budget=budget, n_nodes=n_nodes,
+                     temperature=temperature if temperature >= 1e-5 else 0.0, seed=seed)
+    if hasattr(draft, "_buffer"):
+        draft._buffer(engine.device)
+    session = DecodeSession(engine, cfg, total + n_nodes + 2, draft)
+    target.adapter.last_session = session
+    layer_ids = list(engine.layer_ids)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    first = session.prefill(prompt)
+    torch.cuda.synchronize()
+    prefill_time = time.perf_counter() - t0
+    cache = SequenceCache(engine)
+    cache.offset = prompt_len
+    output = prompt + [int(first)]
+    start = prompt_len
+    acceptance: list[int] = []
+    stages = {"draft_time_s": 0.0, "tree_build_time_s": 0.0, "verify_time_s": 0.0} if profile else None
+    decode_start = time.perf_counter()
+    steps = 0
+    while start < total:
+        ta = time.perf_counter()
+        session.drafter.draft(session)
+        session.builder.build(session.draft_logits, session.state, session.tree, keep_topk=False)
+        n = int(session.state[6].item())
+        tb = time.perf_counter()
+        tokens = session.tree.tokens[:n].tolist()
+        parents = session.tree.parents[:n].tolist()
+        child_maps: list[dict[int, int]] = [dict() for _ in range(n)]
+        for i in range(1, n):
+            child_maps[parents[i]][tokens[i]] = i
+        accepted, posterior, hidden = lazy_follow_tree_exact(target, cache, layer_ids, tokens, child_maps,
+                                                             temperature, verify_mode, None)
+        tc = time.perf_counter()
+        keep = len(accepted)
+        output = output[:start] + [tokens[i] for i in accepted] + [int(posterior)]
+        start += keep
+        acceptance.append(keep)
+        steps += 1
+        # device decode state for the next draft: start, root, step, accepted
+        new_state = torch.tensor([start, int(posterior), steps, keep, int(posterior), 0, n, 0], dtype=torch.int32)
+        session.state.copy_(new_state.to(session.state.device))
+        if getattr(session.drafter, "needs_hidden", False) and keep > 0:
+            session.target_hidden[:keep] = hidden.reshape(keep, -1)[:, : session.target_hidden.shape[1]]
+        if stages is not None:
+            torch.cuda.synchronize()
+            stages["draft_time_s"] += tb - ta
+            stages["verify_time_s"] += tc - tb
+        if stop_token_ids and any(t in stop_token_ids for t in output[prompt_len:]):
+            break
+    torch.cuda.synchronize()
+    decode_time = time.perf_counter() - decode_start
+    end = min(start + 1, total)
+    if stop_token_ids:
+        hit = stop_position(output, prompt_len, stop_token_ids)
+        if hit is not None:
+            end = min(end, hit + 1)
+    output = output[:end]
+    generated = generated_token_count(output, prompt_len)
+    total_time = prefill_time + decode_time
+    metrics: dict[str, Any] = {
+        "decode_mode": "dtree",
+        "qwen35_tree_mode": "lazy",
+        "num_input_tokens": prompt_len,
+        "num_output_tokens": generated,
+        "prefill_time_s": prefill_time,
+        "decode_time_s": decode_time,
+        "total_time_s": total_time,
+        "prompt_tps": prompt_len / max(prefill_time, 1e-9),
+        "generation_tps": generated / max(decode_time, 1e-9),
+        "end_to_end_tps": generated / max(total_time, 1e-9),
+        "avg_acceptance_length": sum(acceptance) / max(len(acceptance), 1),
+        "acceptance_lengths": acceptance,
+        "peak_memory_gb": torch.cuda.max_memory_allocated() / 1e9,
+        "target_cache_summary": target.cache_summary([None] * engine.cfg.num_hidden_layers, offset=start),
+        "speculative_tokens": block_size,
+        "tree_budget": budget,
+    }
+    if stages is not None:
+        metrics["profile"] = {**stages, "steps": steps}
+    return output, metrics
+
+
 def _profiled_step(session: DecodeSession, stages: dict[str, float]) -> None:
     """Eager step with CUDA-event stage timers (dtree_runtime.py:24-56 keys)."""
     ev = [torch.cuda.Event(enable_timing=True) for _ in range(5)]

@@ -407,6 +407,26 @@ DTREE_API int dtree_qwen3_set_sampling(dtree_qwen3_model* model, float temperatu
 DTREE_API int dtree_dflash_context(dtree_qwen3_model* model, const void* fc_weight, const void* hidden_norm,
                          const void* target_hidden, int ld_hidden, int width, int n_rows, int ctx_base,
                          const dtree_step_state* state, void* stream);
+
+/* dtree_dflash_context for a context-only draft cache
+ * (ContextOnlyDraftKVCache, draft.py:69-112, which the reference uses for
+ * Qwen3.5 targets, api.py:62-64): only context rows are cached, the first
+ * `sink` of them and a sliding window of the last `window`, as a ring --
+ * context row r (counted from the prompt's first row) sits in slot r if
+ * r < sink, else sink + (r - sink) % window.  RoPE positions stay the rows'
+ * real positions, so the attended set equals the reference's sink + window
+ * concatenation.  ring_state (a dtree_step_state the caller owns, zeroed for
+ * a new sequence): `reserved` counts the rows appended so far, `start` =
+ * min(reserved, sink + window) is the attended context length -- pass
+ * ring_state as the state of dtree_qwen3_forward_logits for the block (its
+ * rows land in slots start..start+block-1, positions from the positions
+ * buffer).  Rows appended: n_rows at positions ctx_base + t when
+ * ctx_base >= 0 (prompt), else state->n_accepted rows ending at
+ * state->start.  kv_capacity >= sink + window + t_cap. */
+DTREE_API int dtree_dflash_context_ring(dtree_qwen3_model* model, const void* fc_weight, const void* hidden_norm,
+                                        const void* target_hidden, int ld_hidden, int width, int n_rows,
+                                        int ctx_base, const dtree_step_state* state, dtree_step_state* ring_state,
+                                        int sink, int window, void* stream);
 DTREE_API int dtree_dflash_block(const dtree_step_state* state, int mask_token_id, int block, int32_t* tokens,
                        int32_t* positions, void* stream);
 DTREE_API int dtree_qwen3_forward_logits(dtree_qwen3_model* model, const int32_t* tokens, const int32_t* positions,

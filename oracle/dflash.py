@@ -15,6 +15,8 @@ the model) and its use per decode step (dtree_runtime.py:366-376):
       (scale head_dim^-0.5), o_proj, residual, SwiGLU MLP, residual  :189-309
   logits = norm(h) @ embed^T (the target's tied LM head)            :375
   the block's own K/V are trimmed from the cache afterwards          :377
+With a context-only cache (Qwen3.5 targets) the context is windowed
+(ContextOnlyDraftKVCache, :69-112).
 """
 from __future__ import annotations
 
@@ -27,7 +29,14 @@ from .qwen3 import apply_rope, rms_norm
 
 
 class DFlashOracle:
-    def __init__(self, weights, target_embed):
+    """``sink`` / ``window``: the context-only draft cache
+    (ContextOnlyDraftKVCache, draft.py:69-112): after every append the cache
+    keeps its first ``sink`` rows and its last ``window`` rows; positions keep
+    counting every appended row (cache.offset)."""
+
+    def __init__(self, weights, target_embed, sink: int | None = None, window: int | None = None):
+        self.sink, self.window = sink, window
+        self.appended = 0
         w = weights
         self.cfg = c = w.cfg
         L = w.layers.to("cpu") if w.layers.device.type != "cpu" else w.layers
@@ -41,7 +50,7 @@ class DFlashOracle:
 
     @property
     def offset(self) -> int:
-        return self.k[0].shape[1]
+        return self.appended if self.window is not None else self.k[0].shape[1]
 
     def _kv(self, L, x, pos):
         c = self.cfg
@@ -60,6 +69,10 @@ class DFlashOracle:
             k, v = self._kv(L, th, pos)
             self.k[i] = torch.cat([self.k[i], k.transpose(0, 1)], dim=1)
             self.v[i] = torch.cat([self.v[i], v.transpose(0, 1)], dim=1)
+            if self.window is not None and self.k[i].shape[1] > self.sink + self.window:  # _apply_window, :95-106
+                self.k[i] = torch.cat([self.k[i][:, : self.sink], self.k[i][:, -self.window:]], dim=1)
+                self.v[i] = torch.cat([self.v[i][:, : self.sink], self.v[i][:, -self.window:]], dim=1)
+        self.appended += th.shape[0]
 
     def block_logits(self, token: int) -> torch.Tensor:
         """Logits [block, vocab] of the block [token, mask x (bs-1)]; the cache

@@ -82,3 +82,38 @@ def test_dtree_generation_with_dflash_drafter(lib):
     print(f"dflash-drafter DTree vs planted DFlash: first difference {first_diff}/32, "
           f"accept {r.metrics['avg_acceptance_length']:.2f}")
     assert len(r.generated_tokens) == 32 and first_diff >= 8
+
+
+def test_context_only_draft_cache_matches_windowed_oracle(lib):
+    """ContextOnlyDraftKVCache (draft.py:69-112): with a small sink and window
+    the device ring must attend over exactly the reference's sink + last
+    window rows (at their real positions) once the context overflows."""
+    from dtree_mlx_b200.adapters import load_target_model
+    from dtree_mlx_b200.draft import load_draft_model
+    from dtree_mlx_b200.engine import DecodeSession, StepConfig, dtree_nodes
+    from dtree_mlx_b200.synthetic import random_prompt
+
+    target = load_target_model("synthetic:qwen3-tiny:seed=0:kv=1024")
+    drafter, _ = load_draft_model("dflash:qwen3-tiny:seed=3", target=target)
+    drafter.cache_mode, drafter.sink_size, drafter.window_size = "context-only", 8, 40
+    cfg = drafter.cfg
+    eng = target.adapter.engine(target.model, drafter)
+    sess = DecodeSession(eng, StepConfig("dtree", 15, 24, dtree_nodes(24, 15, cfg.vocab_size)), output_capacity=512,
+                         drafter=drafter)
+    sess.prefill(random_prompt(44, cfg.vocab_size, seed=6))  # 44 > 8 + 40 - ... overflows within a few steps
+    orc = DFlashOracle(drafter.weights, target.model.weights.embed, sink=8, window=40)
+    orc.context(sess.prompt_hidden.float().cpu())
+    for step in range(6):
+        st = sess.read_state()
+        sess.step()
+        torch.cuda.synchronize()
+        g = drafter.logits[1:16].float().cpu()
+        o = orc.block_logits(st["root_token"])[1:16]
+        _check(g, o, f"ring step {step}")
+        new = sess.read_state()
+        orc.context(sess.target_hidden[: new["n_accepted"]].float().cpu())
+        ring = drafter.ring_state.tolist()
+        assert ring[7] == orc.appended == new["start"] and ring[0] == min(orc.appended, 48)
+    from dtree_mlx_b200 import _lib
+
+    assert _lib.device_error() == 0

@@ -156,3 +156,29 @@ def test_generate_api_hybrid(lib):
     print(f"hybrid dtree vs dflash: first difference at {first_diff}/48, accept "
           f"{r_tree.metrics['avg_acceptance_length']:.2f} / {r_lin.metrics['avg_acceptance_length']:.2f}")
     assert first_diff >= 8
+
+
+def test_lazy_tree_mode_matches_full_tree(lib, monkeypatch):
+    """The reference's default Qwen3.5 DTree verify follows only the taken
+    branch one token at a time (lazy_follow_tree_exact, dtree_runtime.py:
+    211-290); DTREE_QWEN35_TREE_MODE=full_tree verifies the whole tree with
+    per-node states.  Both are exact greedy decoders of the same target, so
+    their outputs agree (until a near-tie flips a token)."""
+    from dtree_mlx_b200 import DFlashGenerator
+    from dtree_mlx_b200.synthetic import random_prompt
+
+    gen = DFlashGenerator(target_model="synthetic:qwen35-tiny:seed=0:kv=1024", draft_model="planted:p=0.8:seed=1")
+    prompt = random_prompt(150, 8192, seed=4)
+    kw = dict(max_new_tokens=40, decode_mode="dtree", speculative_tokens=16, tree_budget=24)
+    monkeypatch.setenv("DTREE_QWEN35_TREE_MODE", "full_tree")
+    full = gen.generate_from_tokens(prompt, **kw)
+    monkeypatch.delenv("DTREE_QWEN35_TREE_MODE")
+    lazy = gen.generate_from_tokens(prompt, **kw)
+    assert lazy.metrics.get("qwen35_tree_mode") == "lazy" and "qwen35_tree_mode" not in full.metrics
+    assert len(lazy.output_tokens) == 150 + 40 and lazy.output_tokens[:150] == prompt
+    assert min(lazy.metrics["acceptance_lengths"]) >= 1
+    first_diff = next((i for i, (a, b) in enumerate(zip(lazy.generated_tokens, full.generated_tokens)) if a != b),
+                      40)
+    print(f"lazy vs full tree: first difference {first_diff}/40, accept {lazy.metrics['avg_acceptance_length']:.2f}"
+          f" / {full.metrics['avg_acceptance_length']:.2f}")
+    assert first_diff >= 8

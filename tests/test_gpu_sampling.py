@@ -21,6 +21,9 @@ DEV = "cuda"
 def _chi2_pvalue(counts: np.ndarray, probs: np.ndarray) -> float:
     from scipy.stats import chisquare
 
+    probs = np.asarray(probs, dtype=np.float64)
+    probs = probs / probs.sum()
+    counts = np.asarray(counts, dtype=np.float64)
     n = counts.sum()
     keep = probs * n >= 5  # pool the rare tokens
     obs = np.append(counts[keep], counts[~keep].sum())

@@ -173,7 +173,8 @@ def test_checkpoint_target_and_drafter_generate_like_synthetic(tmp_path, lib):
     from dtree_mlx_b200.draft import DFlashDraftModel, PlantedDrafter, load_draft_model, random_dflash_weights
     from dtree_mlx_b200.synthetic import random_prompt
 
-    W.save_qwen3_mlx(random_qwen3_weights(PRESETS["qwen3-tiny"], seed=0, device="cpu"), tmp_path / "t")
+    # the synthetic spec draws its weights on the GPU: save those same weights
+    W.save_qwen3_mlx(random_qwen3_weights(PRESETS["qwen3-tiny"], seed=0, device="cuda"), tmp_path / "t")
     prompt = random_prompt(96, 32768, seed=1)
     kw = dict(max_new_tokens=40, decode_mode="dtree", speculative_tokens=16, tree_budget=24)
     ref = DFlashGenerator(target_model="synthetic:qwen3-tiny:seed=0:kv=1024",
