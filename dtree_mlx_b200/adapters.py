@@ -126,6 +126,16 @@ class TargetAdapter:
     def compact_kv_caches(self, model, cache, past_length: int, keep_current_indices: list[int]) -> None:
         raise NotImplementedError(f"{self.family} does not implement DTree cache compaction.")
 
+    # linear (recurrent) caches: only hybrid targets have them (adapters.py:174-197)
+    def snapshot_linear_caches(self, model, cache):
+        return {}
+
+    def restore_linear_caches(self, model, cache, snapshots) -> None:
+        return None
+
+    def rollback_linear_caches(self, model, cache, rollback_records, accepted_inputs: int) -> None:
+        return None
+
 
 class Qwen3TargetAdapter(TargetAdapter):
     """Qwen3 on the B200 engine (adapters.py:451-668)."""
@@ -352,6 +362,46 @@ class Qwen35TargetAdapter(Qwen3TargetAdapter):
             hid = hid[..., :0]
         return norm, hid
 
+    # -- linear-cache rollback (adapters.py:350-388; RecurrentRollbackCache,
+    # qwen35_target.py:23-175; rollback_linear_caches, custom_qwen35_model.py:
+    # 1124-1169).  The device decode loop never needs it: its verify keeps the
+    # committed DeltaNet state and replays the accepted path on commit.  These
+    # methods give host callers of the adapter interface the reference's
+    # snapshot / rollback contract on the same engine.
+    def forward_with_hidden_states(self, model, inputs, cache, layer_ids, return_rollback_records: bool = False):
+        """Causal forward (states advance through every token); with
+        ``return_rollback_records`` the pre-forward DeltaNet states and the
+        tokens are recorded so rollback_linear_caches can keep a prefix."""
+        tokens = [int(t) for t in inputs.reshape(-1).tolist()]
+        records = {}
+        if return_rollback_records:
+            eng = self.engine(model, layer_ids=layer_ids)
+            records = {"snapshot": eng.snapshot_states(), "past": cache.offset, "tokens": tokens}
+        norm, hid = self._forward(model, tokens, cache, layer_ids)
+        logits = self.lm_head_logits(model, norm)
+        return (logits, hid, records) if return_rollback_records else (logits, hid)
+
+    def snapshot_linear_caches(self, model, cache):
+        return cache.engine.snapshot_states()
+
+    def restore_linear_caches(self, model, cache, snapshots) -> None:
+        cache.engine.restore_states(snapshots)
+
+    def rollback_linear_caches(self, model, cache, rollback_records, accepted_inputs: int) -> None:
+        """Keep the first ``accepted_inputs`` tokens of the recorded forward:
+        restore the recorded DeltaNet states and advance them through those
+        tokens again (the K/V rows they rewrite are identical)."""
+        if not rollback_records:
+            return
+        eng = cache.engine
+        eng.restore_states(rollback_records["snapshot"])
+        keep = int(accepted_inputs)
+        if keep > 0:
+            offset = cache.offset
+            cache.offset = rollback_records["past"]
+            self._forward(model, rollback_records["tokens"][:keep], cache, list(eng.layer_ids))
+            cache.offset = max(offset, rollback_records["past"] + keep)
+
     def forward_tree_with_hidden_states(self, model, inputs, cache, layer_ids, parents, position_ids,
                                         attention_mask):
         """adapters.py:410-430 (forward_qwen35_tree_with_hidden_states)."""
@@ -480,6 +530,15 @@ class LoadedTargetModel:
 
     def compact_kv_caches(self, cache, past_length: int, keep_current_indices: list[int]) -> None:
         self.adapter.compact_kv_caches(self.model, cache, past_length, keep_current_indices)
+
+    def snapshot_linear_caches(self, cache):
+        return self.adapter.snapshot_linear_caches(self.model, cache)
+
+    def restore_linear_caches(self, cache, snapshots) -> None:
+        self.adapter.restore_linear_caches(self.model, cache, snapshots)
+
+    def rollback_linear_caches(self, cache, rollback_records, accepted_inputs: int) -> None:
+        self.adapter.rollback_linear_caches(self.model, cache, rollback_records, accepted_inputs)
 
 
 def parse_synthetic_spec(spec: str) -> dict:

@@ -181,4 +181,44 @@ def test_lazy_tree_mode_matches_full_tree(lib, monkeypatch):
                       40)
     print(f"lazy vs full tree: first difference {first_diff}/40, accept {lazy.metrics['avg_acceptance_length']:.2f}"
           f" / {full.metrics['avg_acceptance_length']:.2f}")
-    assert first_diff >= 8
+    if first_diff < 40:
+        # lazy decodes with unrounded sequence states, the full tree with
+        # bf16-rounded node states (as the reference's two modes do): they
+        # may split only at a near-tie of the fp32 target
+        orc = Qwen35Oracle(gen.target.model.weights, kv_capacity=512)
+        o_norm, _ = orc.prefill(prompt + lazy.generated_tokens[:first_diff])
+        logits = orc.lm_head_logits(o_norm[-1:])[0]
+        a, b = lazy.generated_tokens[first_diff], full.generated_tokens[first_diff]
+        assert near_tie(logits, a, b, 0.15), (first_diff, a, b)
+
+
+def test_linear_cache_rollback_keeps_the_accepted_prefix(lib):
+    """The adapter's rollback contract (forward_with_hidden_states with
+    rollback records, rewind_kv_caches, rollback_linear_caches: runtime.py:
+    186-210): after a 16-token block of which 5 are accepted, the DeltaNet
+    states and the next forward equal those of a forward of just the 5."""
+    from dtree_mlx_b200.adapters import load_target_model
+
+    t = load_target_model("synthetic:qwen35-tiny:seed=0:kv=512")
+    rng = np.random.default_rng(9)
+    prompt = rng.integers(8192, size=30).tolist()
+    block = rng.integers(8192, size=16).tolist()
+    nxt = rng.integers(8192, size=3).tolist()
+    tok = lambda a: torch.tensor(a, dtype=torch.int32)  # noqa: E731
+
+    ref_cache = t.make_cache()
+    t.forward_with_hidden_states(tok(prompt), ref_cache, [])
+    t.forward_with_hidden_states(tok(block[:5]), ref_cache, [])
+    ref_states = ref_cache.engine.snapshot_states()
+    ref_logits, _ = t.forward_with_hidden_states(tok(nxt), ref_cache, [])
+
+    cache = t.make_cache()
+    t.forward_with_hidden_states(tok(prompt), cache, [])
+    _, _, rec = t.forward_with_hidden_states(tok(block), cache, [], return_rollback_records=True)
+    t.rewind_kv_caches(cache, 16 - 5)
+    t.rollback_linear_caches(cache, rec, 5)
+    assert cache.offset == 35
+    states = cache.engine.snapshot_states()
+    assert torch.equal(states[0], ref_states[0]) and torch.equal(states[1], ref_states[1])
+    logits, _ = t.forward_with_hidden_states(tok(nxt), cache, [])
+    assert torch.equal(logits, ref_logits)
