@@ -35,14 +35,14 @@ static GemmWs ws_split(void* base) {
   return w;
 }
 
-static bool valid_tpad(int t) { return t == 16 || t == 32 || t == 64 || t == 128; }
+static bool valid_tpad(int t) { return t == 16 || t == 32 || t == 64 || t == 80 || t == 128; }
 
 // activation map, split / grid choice and parameters shared by both weight formats
 // `wide` kernels (the q4 variant: 448 threads, ~146 KB shared memory) fit
 // one CTA per SM, so a grid above the SM count would run a second wave.
 static int plan_common(GemmPlan* plan, int n_out, int k, const void* x, int t_pad, int x_row_stride_elems, int epi,
                        int grid, bool wide) {
-  DTREE_CHECK_ARG(valid_tpad(t_pad), "t_pad must be 16, 32, 64 or 128");
+  DTREE_CHECK_ARG(valid_tpad(t_pad), "t_pad must be 16, 32, 64, 80 or 128");
   DTREE_CHECK_ARG(k % 64 == 0 && k > 0, "K must be a positive multiple of 64");
   DTREE_CHECK_ARG(n_out > 0, "N must be positive");
   const int m_tiles = (n_out + 127) / 128;
@@ -153,6 +153,7 @@ int gemm_launch(const GemmPlan& pl, cudaStream_t st) {
     case 16: return launch_epi<16>(pl, st);
     case 32: return launch_epi<32>(pl, st);
     case 64: return launch_epi<64>(pl, st);
+    case 80: return launch_epi<80>(pl, st);
     case 128: return launch_epi<128>(pl, st);
   }
   return fail(kErrInvalidArg, "bad t_pad");

@@ -40,13 +40,16 @@ int residual_rmsnorm_launch(__nv_bfloat16* h, const float* partials, int n_split
 constexpr int kAttnMaxSplits = 32;
 constexpr int kMaxProjSplit = 16;  // split-K of the hidden-width projections (o_proj, down_proj)
 
+// tree rows padded to a legal UMMA N (multiple of 16): budget 64 (65 rows)
+// pads to 80, not 128
 static int pad_rows(int n) {
   if (n <= 16) return 16;
   if (n <= 32) return 32;
   if (n <= 64) return 64;
+  if (n <= 80) return 80;
   return 128;
 }
-static int tpad_index(int t) { return t == 16 ? 0 : t == 32 ? 1 : t == 64 ? 2 : 3; }
+static int tpad_index(int t) { return t == 16 ? 0 : t == 32 ? 1 : t == 64 ? 2 : t == 80 ? 3 : 4; }
 
 struct PlanSet {
   bool ready = false;
@@ -61,7 +64,7 @@ struct dtree_qwen3_model {
   dtree_qwen3_desc d;
   std::vector<dtree_qwen3_layer> layers;
   std::vector<dtree_qwen3_q4_layer> q4_layers;
-  dtree::PlanSet plans[4];
+  dtree::PlanSet plans[5];
   void* gemm_ws = nullptr;
   size_t gemm_ws_bytes = 0;
   void* attn_ws = nullptr;

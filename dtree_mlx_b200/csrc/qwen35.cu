@@ -42,8 +42,8 @@ namespace {
 constexpr int kAttnSplitsMax = 32;
 constexpr int kProjSplitMax = 16;
 
-int pad_rows35(int n) { return n <= 16 ? 16 : n <= 32 ? 32 : n <= 64 ? 64 : 128; }
-int tpad_idx(int t) { return t == 16 ? 0 : t == 32 ? 1 : t == 64 ? 2 : 3; }
+int pad_rows35(int n) { return n <= 16 ? 16 : n <= 32 ? 32 : n <= 64 ? 64 : n <= 80 ? 80 : 128; }
+int tpad_idx(int t) { return t == 16 ? 0 : t == 32 ? 1 : t == 64 ? 2 : t == 80 ? 3 : 4; }
 
 struct Dims {
   int n_attn, n_lin, key_dim, value_dim, conv_dim, proj_w, qkv_w, q_dim, keep, wide;
@@ -90,7 +90,7 @@ struct dtree_qwen35_model {
   std::vector<dtree_qwen35_linear_layer> lin;
   std::vector<dtree_qwen35_attn_layer> att;
   std::vector<int> slot;  // layer -> index among its kind
-  dtree::Qwen35Plans plans[4];
+  dtree::Qwen35Plans plans[5];
   void* gemm_ws = nullptr;
   size_t gemm_ws_bytes = 0;
   void* attn_ws = nullptr;

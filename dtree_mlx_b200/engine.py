@@ -32,7 +32,8 @@ def _wptr(t) -> int:
 
 
 def pad_rows(n: int) -> int:
-    for t in (16, 32, 64, 128):
+    """Tree rows padded to a legal UMMA N: 16, 32, 64, 80 or 128."""
+    for t in (16, 32, 64, 80, 128):
         if n <= t:
             return t
     raise ValueError(f"at most {DTREE_MAX_TREE} tree rows per forward, got {n}")

@@ -36,6 +36,8 @@ def _check(y, ref):
         (32, 9728, 2560),   # down_proj
         (16, 512, 200),     # ragged N (zero-filled TMA rows)
         (64, 1024, 1536),
+        (80, 2560, 6144),   # 65 tree rows (budget 64) pad to 80 (a legal UMMA N)
+        (80, 9728, 2560),
         (128, 512, 640),
     ],
 )
@@ -58,6 +60,7 @@ def test_linear_matches_fp32(K, t_pad, k, n):
         (32, 9728, 2560, 7),    # down_proj, tile-aligned split-K grid
         (16, 512, 200, 0),      # ragged N
         (64, 1024, 1536, 0),
+        (80, 2560, 6144, 0),    # 65 tree rows pad to 80
         (128, 512, 640, 0),
         (32, 320, 1280, 0),     # K/64 = 5: scalar scale loads, one unit per CTA
         (16, 192, 384, 2),      # one or two units per CTA (a lone unit pair)
@@ -99,7 +102,8 @@ def test_linear_deterministic(K):
     assert torch.equal(y1, y2)
 
 
-@pytest.mark.parametrize("t_pad,n_rows,hidden,vocab", [(32, 25, 2560, 151936), (16, 9, 512, 32768), (64, 40, 512, 5000)])
+@pytest.mark.parametrize("t_pad,n_rows,hidden,vocab", [(32, 25, 2560, 151936), (16, 9, 512, 32768), (64, 40, 512, 5000),
+                                                      (80, 65, 2560, 151936)])
 def test_lm_head_argmax(K, t_pad, n_rows, hidden, vocab):
     g = torch.Generator(device=DEV).manual_seed(vocab)
     h = torch.randn(t_pad, hidden, device=DEV, generator=g).to(torch.bfloat16)
