@@ -215,6 +215,21 @@ class Qwen3TargetAdapter(TargetAdapter):
         post = torch.zeros(128, dtype=torch.int32, device=dev)
         norm_rows, cap_rows = [], []
         s = 0
+        if anc_rows is None and positions is None and n > eng.t_cap:
+            # a causal sequence longer than one verify forward: dense prefill
+            width = eng.cfg.hidden_size * max(1, len(eng.layer_ids))
+            norm = torch.zeros(n, eng.cfg.hidden_size, dtype=torch.bfloat16, device=dev)
+            hid = torch.zeros(n, width, dtype=torch.bfloat16, device=dev)
+            nxt = torch.zeros(1, dtype=torch.int32, device=dev)
+            toks_all = torch.tensor(tokens, dtype=torch.int32, device=dev)
+            while s < n:
+                t = min(eng.max_prefill_rows, n - s)
+                state[0] = cache.offset + s
+                eng.prefill_dense(toks_all[s:s + t], state, hid[s:s + t] if eng.layer_ids else None, nxt,
+                                  norm_out=norm[s:s + t])
+                s += t
+            cache.offset += n
+            return norm[None], (hid if eng.layer_ids else hid[..., :0])[None]
         while s < n:
             t = min(eng.t_cap, n - s)
             state[0] = cache.offset + s
@@ -344,6 +359,20 @@ class Qwen35TargetAdapter(Qwen3TargetAdapter):
             cache.offset += n
             norm = eng.norm_out[:n].clone()[None]
             hid = eng.capture[:n].clone()[None]
+        elif n > eng.t_cap:  # a long causal sequence: dense prefill, states advance to its end
+            width = eng.cfg.hidden_size * max(1, len(eng.layer_ids))
+            norm = torch.zeros(n, eng.cfg.hidden_size, dtype=torch.bfloat16, device=dev)
+            hid = torch.zeros(n, width, dtype=torch.bfloat16, device=dev)
+            nxt = torch.zeros(1, dtype=torch.int32, device=dev)
+            s = 0
+            while s < n:
+                t = min(eng.max_prefill_rows, n - s)
+                state[0] = cache.offset + s
+                eng.prefill_dense(toks[s:s + t], state, hid[s:s + t] if eng.layer_ids else None, nxt,
+                                  norm_out=norm[s:s + t])
+                s += t
+            cache.offset += n
+            norm, hid = norm[None], hid[None]
         else:  # causal sequence: states advance chunk by chunk
             norm_rows, cap_rows = [], []
             s = 0

@@ -398,19 +398,26 @@ __global__ void __launch_bounds__(kTcThreads) tree_attn_tc_kernel(const __grid_c
   float* red_max = reinterpret_cast<float*>(sm + C::kRed);  // [2][128]
   float* red_sum = red_max + 2 * 128;                       // [2][128]
 
-  const int split = blockIdx.x, rb = blockIdx.y, kvh = blockIdx.z;
+  const int split = blockIdx.x, kvh = blockIdx.z;
   const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
   const int r = (warp & 3) * 32 + lane;  // softmax / output row (TMEM lane)
   const int h = warp >> 2;               // key half (S) and column half (O)
   const int G = p.n_q_heads / p.n_kv_heads;
-  const int T = p.n_nodes;
+  // prompt mode: blockIdx.y = chunk * chunk_rbs + row block; the chunk's
+  // rows are queries row0 .. row0 + T - 1 at slots start + row0 ..
+  const bool chunked = p.chunk_rows > 0;
+  const int chunk = chunked ? static_cast<int>(blockIdx.y) / p.chunk_rbs : 0;
+  const int rb = chunked ? static_cast<int>(blockIdx.y) % p.chunk_rbs : static_cast<int>(blockIdx.y);
+  const int row0 = chunk * p.chunk_rows;
+  const int T = chunked ? min(p.chunk_rows, p.n_nodes - row0) : p.n_nodes;
   const int rows_kv = G * T;
+  if (rb * 128 >= rows_kv) return;  // row block past a ragged last chunk (CTA-uniform)
 
   if (t == 0) {
     // prefix keys into L2 while the upstream kernels finish.  `start` read
     // before the dependency wait only steers this hint and the speculative
     // first K/V load below (re-read and checked after the wait)
-    const int P0 = p.state->start;
+    const int P0 = p.state->start + row0;
     *s_p0 = P0;
     const int kps0 = attn_keys_per_split(P0 + T, p.splits, p.key_align);
     const int lo = split * kps0;
@@ -462,8 +469,9 @@ __global__ void __launch_bounds__(kTcThreads) tree_attn_tc_kernel(const __grid_c
   uint4 qv[HD / 16];
   {
     const int qg = q_ok ? qrg / T : 0, qn = q_ok ? qrg % T : 0;
-    const uint4* src = reinterpret_cast<const uint4*>(p.q + static_cast<size_t>(qn) * p.ldq + (kvh * G + qg) * HD) +
-                       qh * (HD / 16);
+    const uint4* src =
+        reinterpret_cast<const uint4*>(p.q + static_cast<size_t>(row0 + qn) * p.ldq + (kvh * G + qg) * HD) +
+        qh * (HD / 16);
 #pragma unroll
     for (int c = 0; c < HD / 16; ++c) qv[c] = q_ok ? __ldg(src + c) : make_uint4(0, 0, 0, 0);
   }
@@ -472,7 +480,7 @@ __global__ void __launch_bounds__(kTcThreads) tree_attn_tc_kernel(const __grid_c
   const int g = row_ok ? rg / T : 0, node = row_ok ? rg % T : 0;
   const uint64_t anc0 = row_ok ? p.anc[2 * node] : 0ull;
   const uint64_t anc1 = row_ok ? p.anc[2 * node + 1] : 0ull;
-  const int P = p.state->start;
+  const int P = p.state->start + row0;
   const int L = P + T;
   const int kps = attn_keys_per_split(L, p.splits, p.key_align);
   const int k_begin = split * kps;
@@ -650,18 +658,37 @@ __global__ void __launch_bounds__(kTcThreads) tree_attn_tc_kernel(const __grid_c
                         __uint_as_float(v[4 * i + 3]));
     }
     const int rows_total = p.n_q_heads * T;
-    if (row_ok && h == 0) {
+    constexpr int VPR = OH / 4;       // float4 per staged row
+    constexpr int RPI = 32 / VPR;     // rows per warp instruction
+    const int sub = lane / VPR, vi = lane % VPR;
+    if (chunked) {
+      // O / l as bf16 straight into the output rows (one split holds every key)
+      stage[lane * LDS + OH] = l_run > 0.0f ? 1.0f / l_run : 0.0f;
+      __syncwarp();
+#pragma unroll 4
+      for (int rr = sub; rr < 32; rr += RPI) {
+        const int rg2 = rb * 128 + (warp & 3) * 32 + rr;
+        if (rg2 < rows_kv) {
+          const float il = stage[rr * LDS + OH];
+          const float4 o4 = *reinterpret_cast<const float4*>(stage + rr * LDS + vi * 4);
+          uint2 pk;
+          pk.x = pack_bf16(o4.x * il, o4.y * il);
+          pk.y = pack_bf16(o4.z * il, o4.w * il);
+          __nv_bfloat16* dst =
+              p.out + static_cast<size_t>(row0 + rg2 % T) * p.ldq + (kvh * G + rg2 / T) * HD + h * OH;
+          *reinterpret_cast<uint2*>(dst + vi * 4) = pk;
+        }
+      }
+    }
+    if (row_ok && h == 0 && !chunked) {
       const int qrow = (kvh * G + g) * T + node;  // [head][node]
       float* pml = p.part_ml + (static_cast<size_t>(split) * rows_total + qrow) * 2;
       pml[0] = m_run;
       pml[1] = l_run;
     }
     __syncwarp();
-    constexpr int VPR = OH / 4;       // float4 per staged row
-    constexpr int RPI = 32 / VPR;     // rows per warp instruction
-    const int sub = lane / VPR, vi = lane % VPR;
 #pragma unroll 4
-    for (int rr = sub; rr < 32; rr += RPI) {
+    for (int rr = sub; rr < 32 && !chunked; rr += RPI) {
       const int rg2 = rb * 128 + (warp & 3) * 32 + rr;
       if (rg2 < rows_kv) {
         const int qrow = (kvh * G + rg2 / T) * T + rg2 % T;
@@ -800,6 +827,39 @@ static int attn_launch_tc(const AttnParams& p, int rb, cudaStream_t stream) {
   DTREE_CUDA_RET(launch_pdl(kern, dim3(p.splits, rb, p.n_kv_heads), dim3(kTcThreads), static_cast<size_t>(C::kSmem),
                             stream, tk, tv, p));
   DTREE_CUDA_RET(launch_pdl(attn_combine_kernel<HD>, dim3(p.n_q_heads * p.n_nodes), dim3(HD), 0, stream, p));
+  return kOk;
+}
+
+int attn_prefill_launch(const AttnParams& p0, int head_dim, cudaStream_t stream) {
+  AttnParams p = p0;
+  DTREE_CHECK_ARG(head_dim == 64 || head_dim == 128, "prompt attention supports head_dim 64 or 128");
+  DTREE_CHECK_ARG(p.n_nodes > 0 && p.n_q_heads % p.n_kv_heads == 0 && p.q && p.out && p.anc && p.state,
+                  "bad prompt attention arguments");
+  DTREE_CHECK_ARG(p.gate == nullptr, "prompt attention has no output gate");
+  p.chunk_rows = kTcKeys;
+  const int G = p.n_q_heads / p.n_kv_heads;
+  p.chunk_rbs = (G * p.chunk_rows + 127) / 128;
+  const int chunks = (p.n_nodes + p.chunk_rows - 1) / p.chunk_rows;
+  DTREE_CHECK_ARG(static_cast<long long>(chunks) * p.chunk_rbs < 65536, "prompt too long for one launch");
+  p.splits = 1;
+  p.key_align = kTcKeys;
+  p.part_o = nullptr;
+  p.part_ml = nullptr;
+  CUtensorMap tk, tv;
+  const int rows = p.n_kv_heads * p.cap;
+  int rc = plane_tmap(&tk, p.k, rows, head_dim);
+  if (rc) return rc;
+  if ((rc = plane_tmap(&tv, p.v, rows, head_dim))) return rc;
+  const dim3 grid(1, chunks * p.chunk_rbs, p.n_kv_heads);
+  if (head_dim == 128) {
+    DTREE_CUDA_RET(ensure_smem_attr(tree_attn_tc_kernel<128>, TcCfg<128>::kSmem));
+    DTREE_CUDA_RET(launch_pdl(tree_attn_tc_kernel<128>, grid, dim3(kTcThreads),
+                              static_cast<size_t>(TcCfg<128>::kSmem), stream, tk, tv, p));
+  } else {
+    DTREE_CUDA_RET(ensure_smem_attr(tree_attn_tc_kernel<64>, TcCfg<64>::kSmem));
+    DTREE_CUDA_RET(launch_pdl(tree_attn_tc_kernel<64>, grid, dim3(kTcThreads),
+                              static_cast<size_t>(TcCfg<64>::kSmem), stream, tk, tv, p));
+  }
   return kOk;
 }
 

@@ -24,10 +24,19 @@ struct AttnParams {
   int causal_prefix;    // unused (0): tree mask only
   const __nv_bfloat16* gate;  // [t_pad][n_q_heads*hd] output gate (nullable)
   int key_align;        // keys per split are a multiple of this (set by attn_launch)
+  // prompt mode (chunk_rows > 0, tcgen05 path, one split): the n_nodes rows
+  // are causal chunks of chunk_rows; chunk c holds rows [c*chunk_rows, ..)
+  // at cache slots start + row, sees every key before its first row and the
+  // chain mask `anc` within the chunk, and writes O / l straight to `out`
+  int chunk_rows;
+  int chunk_rbs;        // 128-row blocks per chunk (set by attn_prefill_launch)
 };
 
 size_t attn_ws_bytes(int n_q_heads, int t_pad, int head_dim, int splits);
 int attn_default_splits(int n_kv_heads, int n_q_heads, int n_nodes);
 int attn_launch(const AttnParams& p, int head_dim, void* ws, size_t ws_bytes, cudaStream_t stream);
+// prompt (causal) attention over n_nodes rows in chunks of 128; anc = the
+// 128-row chain masks; head_dim 64 or 128; no workspace
+int attn_prefill_launch(const AttnParams& p, int head_dim, cudaStream_t stream);
 
 }  // namespace dtree

@@ -255,6 +255,101 @@ __global__ void tree_gated_delta_kernel(DeltaParams p) {
   }
 }
 
+// Prompt (sequence) recurrence: rows 0..n_nodes-1 form one chain from
+// state_in, the state stays in f32 registers from the first row to the last
+// (mlx-lm's sequence kernel; no per-row rounding) and is written to
+// final_state.  One warp per state row (hv, dv), Dk/32 elements per lane,
+// every warp independent (no shared memory, no block barrier); each row's
+// q / k / v / a / b are loaded kPf rows ahead into registers.  Per row
+//   S' = S g;  kv = S' k;  delta = (v - kv) beta;  S'' = S' + k delta;
+//   y = S'' q = g (S q) + delta (k q)
+// so the two reductions of a row (S k and S q of the incoming state, plus
+// the state-free k q) run side by side instead of one after the other.
+constexpr int kSeqPf = 4;
+
+template <typename InT, typename StT, int DK>
+__global__ void __launch_bounds__(256) gated_delta_seq_kernel(DeltaParams p) {
+  constexpr int NP = DK / 32;
+  pdl_trigger();
+  const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  const bool live = row < p.n_v_heads * p.dv;
+  const int hv = live ? row / p.dv : 0, dv = live ? row % p.dv : 0;
+  const int hk = hv / (p.n_v_heads / p.n_k_heads);
+  pdl_wait();
+  if (!live) return;  // (whole warps)
+  const InT* q = static_cast<const InT*>(p.q) + hk * DK + lane * NP;
+  const InT* k = static_cast<const InT*>(p.k) + hk * DK + lane * NP;
+  const InT* v = static_cast<const InT*>(p.v) + hv * p.dv + dv;
+  const InT* a = static_cast<const InT*>(p.a) + hv;
+  const InT* b = static_cast<const InT*>(p.b) + hv;
+  const float dt_b = ld_f(static_cast<const InT*>(p.dt_bias) + hv);
+  const float ea = expf(p.a_log[hv]);
+  const StT* st_in = static_cast<const StT*>(p.state_in) + (static_cast<size_t>(hv) * p.dv + dv) * DK + lane * NP;
+  float s[NP];
+#pragma unroll
+  for (int i = 0; i < NP; ++i) s[i] = ld_f(st_in + i);
+  InT* y = static_cast<InT*>(p.y) + hv * p.dv + dv;
+  const int T = p.n_nodes;
+  // register ring of the next kPf rows' inputs
+  InT rq[kSeqPf][NP], rk[kSeqPf][NP];
+  float rv[kSeqPf], ra[kSeqPf], rb[kSeqPf];
+  auto fetch = [&](int j, int t) {
+    if (t < T) {
+#pragma unroll
+      for (int i = 0; i < NP; ++i) {
+        rq[j][i] = q[static_cast<size_t>(t) * p.ldqk + i];
+        rk[j][i] = k[static_cast<size_t>(t) * p.ldqk + i];
+      }
+      rv[j] = ld_f(v + static_cast<size_t>(t) * p.ldv);
+      ra[j] = ld_f(a + static_cast<size_t>(t) * p.ldab);
+      rb[j] = ld_f(b + static_cast<size_t>(t) * p.ldab);
+    }
+  };
+#pragma unroll
+  for (int j = 0; j < kSeqPf; ++j) fetch(j, j);
+  for (int t0 = 0; t0 < T; t0 += kSeqPf) {
+#pragma unroll
+    for (int j = 0; j < kSeqPf; ++j) {
+      const int t = t0 + j;
+      if (t >= T) break;
+      float kk[NP], qq[NP];
+#pragma unroll
+      for (int i = 0; i < NP; ++i) {
+        kk[i] = ld_f(&rk[j][i]);
+        qq[i] = ld_f(&rq[j][i]);
+      }
+      const float vv = rv[j];
+      // gates (node_gates with a, b): g = exp(-exp(A_log) softplus(a + dt_bias)), beta = sigmoid(b)
+      const float x = round_to<InT>(ra[j] + dt_b);
+      const float sp = round_to<InT>(x > 20.0f ? x : log1pf(expf(x)));
+      const float g = expf(-ea * sp);
+      const float beta = round_to<InT>(1.0f / (1.0f + expf(-rb[j])));
+      fetch(j, t + kSeqPf);
+      float sk = 0.0f, sq = 0.0f, kq = 0.0f;
+#pragma unroll
+      for (int i = 0; i < NP; ++i) {
+        sk = fmaf(s[i], kk[i], sk);
+        sq = fmaf(s[i], qq[i], sq);
+        kq = fmaf(kk[i], qq[i], kq);
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        sk += __shfl_xor_sync(0xffffffffu, sk, o);
+        sq += __shfl_xor_sync(0xffffffffu, sq, o);
+        kq += __shfl_xor_sync(0xffffffffu, kq, o);
+      }
+      const float delta = (vv - g * sk) * beta;
+#pragma unroll
+      for (int i = 0; i < NP; ++i) s[i] = fmaf(kk[i], delta, s[i] * g);
+      if (lane == 0) st_f(y + static_cast<size_t>(t) * p.ldy, fmaf(g, sq, delta * kq));
+    }
+  }
+  StT* fs = static_cast<StT*>(p.final_state) + (static_cast<size_t>(hv) * p.dv + dv) * DK + lane * NP;
+#pragma unroll
+  for (int i = 0; i < NP; ++i) st_f(fs + i, s[i]);
+}
+
 // Commit: advance each layer's recurrent state along the accepted path with
 // the tree kernel's per-node arithmetic.  grid (Hv*Dv/4, layers), 4 warps.
 template <typename InT, typename StT, int DK>
@@ -391,6 +486,20 @@ static int delta_launch_t(DeltaParams p, int dk, cudaStream_t st) {
     case 256: return go(tree_gated_delta_kernel<InT, StT, 256>);
   }
   return fail(kErrInvalidArg, "head_k_dim must be 32, 64, 128 or 256");
+}
+
+int gated_delta_seq_launch(const DeltaParams& p, int dk, cudaStream_t st) {
+  DTREE_CHECK_ARG(p.q && p.k && p.v && p.a && p.b && p.a_log && p.dt_bias && p.state_in && p.final_state && p.y,
+                  "sequence gated delta: null pointer (gates come from a / b)");
+  DTREE_CHECK_ARG(p.n_nodes > 0 && p.n_v_heads % p.n_k_heads == 0, "bad sequence gated delta shape");
+  const int rows = p.n_v_heads * p.dv;
+  const dim3 grid((rows + 7) / 8), block(256);
+  using B = __nv_bfloat16;
+  switch (dk) {
+    case 64: DTREE_CUDA_RET(launch_pdl(gated_delta_seq_kernel<B, float, 64>, grid, block, 0, st, p)); return kOk;
+    case 128: DTREE_CUDA_RET(launch_pdl(gated_delta_seq_kernel<B, float, 128>, grid, block, 0, st, p)); return kOk;
+  }
+  return fail(kErrInvalidArg, "sequence gated delta: head_k_dim must be 64 or 128");
 }
 
 int tree_gated_delta_launch(const DeltaParams& p, int dk, int dtype, int state_dtype, cudaStream_t st) {

@@ -64,6 +64,9 @@ struct DeltaParams {
 
 int tree_conv1d_launch(const ConvParams& p, int dtype, int block, cudaStream_t st);
 int tree_gated_delta_launch(const DeltaParams& p, int dk, int dtype, int state_dtype, cudaStream_t st);
+// prompt rows as one chain, bf16 inputs, f32 state (state_in -> final_state;
+// gates from a / b); any n_nodes
+int gated_delta_seq_launch(const DeltaParams& p, int dk, cudaStream_t st);
 int gated_delta_replay_launch(const DeltaParams& p, int dk, int dtype, int state_dtype, int layers, cudaStream_t st);
 int conv_state_commit_launch(const ConvParams& p, int dtype, const int32_t* path, const dtree_step_state* state,
                              int layers, size_t layer_stride_x, size_t layer_stride_base, int fixed_node,

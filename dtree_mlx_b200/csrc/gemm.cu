@@ -1,6 +1,8 @@
 // Host side of the stream-K tcgen05 GEMM: plans (tensor maps + params),
 // dispatch over tile widths / epilogues, and the dense-linear and LM-head
 // argmax entry points.
+#include <algorithm>
+
 #include "gemm.cuh"
 
 namespace dtree {
@@ -24,6 +26,40 @@ static size_t ws_partial_bytes(int t_pad, int grid) {
 }
 
 size_t gemm_ws_bytes(int t_pad, int grid) { return kCountersBytes + ws_partial_bytes(t_pad, grid); }
+size_t gemm_ws_counter_bytes() { return kCountersBytes; }
+
+// MLX affine 4-bit weights -> bf16 [n_out][k] (the prompt path's dense GEMMs
+// read bf16): thread = one packed word (8 weights, one 16-byte store), the
+// same bf16 fma rounding as the fused q4 verify GEMM (dequant8).
+__global__ void __launch_bounds__(256) dequant_q4_kernel(const uint32_t* __restrict__ packed,
+                                                         const __nv_bfloat16* __restrict__ scales,
+                                                         const __nv_bfloat16* __restrict__ biases, int n_out, int k,
+                                                         uint4* __restrict__ out) {
+  pdl_trigger();
+  const int wpr = k / 8;  // words per row
+  const size_t total = static_cast<size_t>(n_out) * wpr;
+  pdl_wait();
+  for (size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+       i += static_cast<size_t>(gridDim.x) * blockDim.x) {
+    const size_t row = i / wpr;
+    const int w = static_cast<int>(i % wpr);
+    const size_t g = row * (k / 64) + w / 8;
+    const __nv_bfloat16 sc = scales[g], bi = biases[g];
+    out[i] = dequant8(__ldg(packed + i), __halves2bfloat162(sc, sc), __halves2bfloat162(bi, bi));
+  }
+}
+
+int dequant_q4_launch(const void* packed, const void* scales, const void* biases, int n_out, int k, void* out,
+                      cudaStream_t st) {
+  DTREE_CHECK_ARG(packed && scales && biases && out, "null pointer");
+  DTREE_CHECK_ARG(k % 64 == 0 && n_out > 0, "K must be a multiple of 64");
+  const size_t total = static_cast<size_t>(n_out) * (k / 8);
+  const int grid = static_cast<int>(std::min<size_t>((total + 255) / 256, static_cast<size_t>(num_sms()) * 8));
+  DTREE_CUDA_RET(launch_pdl(dequant_q4_kernel, dim3(grid), dim3(256), 0, st, static_cast<const uint32_t*>(packed),
+                            static_cast<const __nv_bfloat16*>(scales), static_cast<const __nv_bfloat16*>(biases),
+                            n_out, k, static_cast<uint4*>(out)));
+  return kOk;
+}
 
 static GemmWs ws_split(void* base) {
   GemmWs w;
@@ -56,6 +92,7 @@ static int plan_common(GemmPlan* plan, int n_out, int k, const void* x, int t_pa
   p.kb = k / 64;
   p.m_tiles = m_tiles;
   p.n_rows = t_pad;
+  p.n_tiles = 1;
   const long long units = static_cast<long long>(m_tiles) * p.kb;
   const int sms = num_sms();
   if (epi == kEpiPartial) {
@@ -101,6 +138,40 @@ int gemm_plan_q4(GemmPlan* plan, const void* w_packed, const void* scales, const
   plan->p.q_scales = static_cast<const __nv_bfloat16*>(scales);
   plan->p.q_biases = static_cast<const __nv_bfloat16*>(biases);
   plan->q4 = true;
+  return kOk;
+}
+
+int gemm_plan_dense(GemmPlan* plan, const void* w, int n_out, int k, const void* x, int n_rows, int x_rows,
+                    int x_row_stride_elems, int epi) {
+  DTREE_CHECK_ARG(w && x, "null pointer");
+  DTREE_CHECK_ARG(epi == kEpiStore || epi == kEpiResidual || epi == kEpiSwiglu,
+                  "dense GEMM supports the store, residual and SwiGLU epilogues");
+  DTREE_CHECK_ARG(k % 64 == 0 && k > 0, "K must be a positive multiple of 64");
+  DTREE_CHECK_ARG(n_out > 0 && n_rows > 0, "N and rows must be positive");
+  const int n_tiles = (n_rows + kDenseRows - 1) / kDenseRows;
+  DTREE_CHECK_ARG(x_rows >= n_tiles * kDenseRows, "activation buffer must hold the rows padded to 256");
+  const int m_tiles = (n_out + 127) / 128;
+  DTREE_CHECK_ARG(static_cast<long long>(m_tiles) * n_tiles <= kMaxTileCounters, "N x rows too large");
+  int rc = make_tmap_2d_bf16(&plan->tmap_x, x, static_cast<uint64_t>(k), static_cast<uint64_t>(x_rows),
+                             static_cast<uint64_t>(x_row_stride_elems) * 2, 64, kDenseRows, true);
+  if (rc) return rc;
+  if ((rc = make_tmap_2d_bf16(&plan->tmap_w, w, static_cast<uint64_t>(k), static_cast<uint64_t>(n_out),
+                              static_cast<uint64_t>(k) * 2, 64, 128, true)))
+    return rc;
+  GemmParams& p = plan->p;
+  p = GemmParams{};
+  p.n_out = n_out;
+  p.kb = k / 64;
+  p.m_tiles = m_tiles;
+  p.n_tiles = n_tiles;
+  p.n_rows = n_rows;
+  const long long units = static_cast<long long>(m_tiles) * n_tiles * p.kb;
+  const int sms = num_sms();
+  p.grid = static_cast<int>(units < sms ? units : sms);
+  DTREE_CHECK_ARG(units * p.grid < (1ll << 31), "stream-K index range exceeds 32 bits");
+  plan->t_pad = kDenseRows;
+  plan->epi = epi;
+  plan->q4 = false;
   return kOk;
 }
 
@@ -155,6 +226,13 @@ int gemm_launch(const GemmPlan& pl, cudaStream_t st) {
     case 64: return launch_epi<64>(pl, st);
     case 80: return launch_epi<80>(pl, st);
     case 128: return launch_epi<128>(pl, st);
+    case kDenseRows:
+      switch (pl.epi) {  // dense (prefill) tiles: bf16 weights, no split-K / argmax / q|k|v epilogues
+        case kEpiStore: return launch_t<kDenseRows, kEpiStore>(pl, st);
+        case kEpiResidual: return launch_t<kDenseRows, kEpiResidual>(pl, st);
+        case kEpiSwiglu: return launch_t<kDenseRows, kEpiSwiglu>(pl, st);
+      }
+      return fail(kErrInvalidArg, "epilogue not available for dense tiles");
   }
   return fail(kErrInvalidArg, "bad t_pad");
 }

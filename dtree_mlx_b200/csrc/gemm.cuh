@@ -2,6 +2,13 @@
 //
 //   out[t, n] = sum_k X[t, k] * W[n, k]      t < TPAD (tree rows), n < N
 //
+// Dense mode (prompt prefill, n_tiles > 1): the token rows are cut into
+// n_tiles tiles of TPAD = 256 (the largest UMMA N at M = 128); tile index
+// = m_tile * n_tiles + token_tile, so the CTAs working at one time share
+// weight tiles (read from HBM once, the rest from L2) and the activations
+// (rows x K bf16, tens of MB) stay L2 resident.  The stream-K split is the
+// same over (tile, k_block) units.
+//
 // Swap-AB: W (weights, streamed once from HBM) is the MMA's M=128 A operand,
 // X (the tree's activations, L2 resident) the N=TPAD B operand; both K-major
 // bf16 tiles of 64 elements (128 B, one swizzle atom) per stage, brought in
@@ -43,7 +50,9 @@ struct GemmParams {
   int n_out;   // rows of W
   int kb;      // K / 64
   int m_tiles; // ceil(n_out / 128)
-  int n_rows;  // valid tree rows (<= TPAD)
+  int n_rows;  // valid tree rows (<= TPAD; dense mode: token rows, <= n_tiles * TPAD)
+  int n_tiles; // token tiles of TPAD rows (1: tree verify)
+  int w_dep;   // weights written by the upstream kernel (dequantized): load them after the dependency wait
   int grid;    // CTAs (stream-K ranges, or m_tiles * split)
   int split;   // > 0: tile-aligned split-K (CTA c -> tile c / split, split c % split); 0: stream-K
   float* out_f32;  // kEpiPartial output [split][TPAD][ldo]
@@ -114,7 +123,8 @@ struct GemmCfg {
   // (launched early by PDL) can be resident and prefetch its weights
   // (q4 stages are a quarter as large; a deeper ring keeps enough packed
   // bytes in flight)
-  static constexpr int kBudget = (Q4 ? kQ4BudgetKB : 110) * 1024;
+  // (TPAD 256, dense prefill: one CTA per SM with a 4-stage ring)
+  static constexpr int kBudget = (Q4 ? kQ4BudgetKB : (TPAD >= 256 ? 200 : 110)) * 1024;
   static constexpr int kFixed = 1024 /*align*/ + kBarBytes + kXchBytes + kRedBytes;
   static constexpr int kStagesRaw = (kBudget - kFixed) / kStageBytes;
   static constexpr int kMaxStages = Q4 ? 16 : 8;
@@ -202,7 +212,7 @@ __global__ void __launch_bounds__(Q4 ? kGemmThreadsQ4 : kGemmThreads, 1)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int G = p.grid;
-  const long long U = static_cast<long long>(p.m_tiles) * p.kb;
+  const long long U = static_cast<long long>(p.m_tiles) * p.n_tiles * p.kb;
   const int cta = blockIdx.x;
   long long u0, u1;
   if (p.split > 0) {  // tile-aligned split-K: one segment per CTA
@@ -247,22 +257,27 @@ __global__ void __launch_bounds__(Q4 ? kGemmThreadsQ4 : kGemmThreads, 1)
       const uint64_t pol_x = l2_policy_evict_last();
       constexpr int LA = C::kLookahead > 0 ? C::kLookahead : S;  // units in flight
       const int pre = n_units < LA ? n_units : LA;
-      // weights do not depend on the upstream kernel: start streaming now
+      // weights do not depend on the upstream kernel (unless w_dep): start
+      // streaming now
+      if (p.w_dep) pdl_wait();
       for (int i = 0; i < pre; ++i) {
         const long long u = u0 + i;
         const int tile = static_cast<int>(u / p.kb), kblk = static_cast<int>(u % p.kb);
         mbar_arrive_expect_tx(&full_bar[i], C::kStageBytes);
         tma_load_2d(stage_base + i * C::kStageBytes + C::kWOff, &tmap_w, &full_bar[i], kblk * (Q4 ? 8 : 64),
-                    tile * 128, pol_w);
+                    (tile / p.n_tiles) * 128, pol_w);
       }
       pdl_wait();
       for (int i = 0; i < pre; ++i) {
-        const int kblk = static_cast<int>((u0 + i) % p.kb);
-        tma_load_2d(stage_base + i * C::kStageBytes + C::kXOff, &tmap_x, &full_bar[i], kblk * 64, 0, pol_x);
+        const long long u = u0 + i;
+        const int tile = static_cast<int>(u / p.kb), kblk = static_cast<int>(u % p.kb);
+        tma_load_2d(stage_base + i * C::kStageBytes + C::kXOff, &tmap_x, &full_bar[i], kblk * 64,
+                    (tile % p.n_tiles) * TPAD, pol_x);
       }
       bool ok = true;
       // (tile, kblk) of unit `pre`, advanced incrementally (no 64-bit division per unit)
       int tile = static_cast<int>((u0 + pre) / p.kb), kblk = static_cast<int>((u0 + pre) % p.kb);
+      int mt = tile / p.n_tiles, nt = tile % p.n_tiles;  // weight tile, token tile
       int s = pre % S;
       for (int i = pre; i < n_units && ok; ++i) {
         if ((i - LA) % C::kUpb == 0) {  // the MMA of units i - LA .. (their phase's commit)
@@ -273,11 +288,14 @@ __global__ void __launch_bounds__(Q4 ? kGemmThreadsQ4 : kGemmThreads, 1)
         if (!ok) break;
         mbar_arrive_expect_tx(&full_bar[s], C::kStageBytes);
         uint8_t* st = stage_base + s * C::kStageBytes;
-        tma_load_2d(st + C::kWOff, &tmap_w, &full_bar[s], kblk * (Q4 ? 8 : 64), tile * 128, pol_w);
-        tma_load_2d(st + C::kXOff, &tmap_x, &full_bar[s], kblk * 64, 0, pol_x);
+        tma_load_2d(st + C::kWOff, &tmap_w, &full_bar[s], kblk * (Q4 ? 8 : 64), mt * 128, pol_w);
+        tma_load_2d(st + C::kXOff, &tmap_x, &full_bar[s], kblk * 64, nt * TPAD, pol_x);
         if (++kblk == p.kb) {
           kblk = 0;
-          ++tile;
+          if (++nt == p.n_tiles) {
+            nt = 0;
+            ++mt;
+          }
         }
         if (++s == S) s = 0;
       }
@@ -540,7 +558,9 @@ __global__ void __launch_bounds__(Q4 ? kGemmThreadsQ4 : kGemmThreads, 1)
         }
       }
       if (have) {
-        const int n = tile * 128 + row;
+        const int mt = tile / p.n_tiles;        // weight tile
+        const int tb = (tile % p.n_tiles) * TPAD;  // first token row of the tile
+        const int n = mt * 128 + row;
 #pragma unroll 1
         for (int c0 = 0; c0 < TPAD; c0 += 8) {
           float a[8];
@@ -583,7 +603,7 @@ __global__ void __launch_bounds__(Q4 ? kGemmThreadsQ4 : kGemmThreads, 1)
             if (n < p.n_out) {
 #pragma unroll
               for (int j = 0; j < 8; ++j) {
-                const int t = c0 + j;
+                const int t = tb + c0 + j;
                 p.out[static_cast<size_t>(t) * p.ldo + n] = __float2bfloat16_rn(t < p.n_rows ? a[j] : 0.0f);
               }
             }
@@ -592,12 +612,12 @@ __global__ void __launch_bounds__(Q4 ? kGemmThreadsQ4 : kGemmThreads, 1)
               __nv_bfloat16 hv[8];
 #pragma unroll
               for (int j = 0; j < 8; ++j) {
-                const int t = c0 + j;
+                const int t = tb + c0 + j;
                 hv[j] = t < p.n_rows ? p.out[static_cast<size_t>(t) * p.ldo + n] : __float2bfloat16_rn(0.0f);
               }
 #pragma unroll
               for (int j = 0; j < 8; ++j) {
-                const int t = c0 + j;
+                const int t = tb + c0 + j;
                 __nv_bfloat16 hn = __float2bfloat16_rn(0.0f);
                 if (t < p.n_rows) hn = __float2bfloat16_rn(__bfloat162float(hv[j]) + bf16_round(a[j]));
                 p.out[static_cast<size_t>(t) * p.ldo + n] = hn;
@@ -611,10 +631,10 @@ __global__ void __launch_bounds__(Q4 ? kGemmThreadsQ4 : kGemmThreads, 1)
             }
             epi_bar();
             if (row < 64) {
-              const int jf = tile * 64 + row;
+              const int jf = mt * 64 + row;
 #pragma unroll
               for (int j = 0; j < 8; ++j) {
-                const int t = c0 + j;
+                const int t = tb + c0 + j;
                 const float g = bf16_round(a[j]);
                 const float uu = bf16_round(xch[j * 128 + row + 64]);
                 const float sg = bf16_round(1.0f / (1.0f + expf(-g)));
@@ -768,12 +788,23 @@ struct GemmPlan {
 };
 
 size_t gemm_ws_bytes(int t_pad, int grid);  // fp32 partials
+// Dense (prompt) GEMM: out[t, n] for t < n_rows token rows, cut into tiles of
+// kDenseRows; x holds x_rows >= the rows padded to kDenseRows (the padding
+// rows are read, their outputs skipped or written as zero rows).  Workspace:
+// gemm_ws_bytes(kDenseRows, num_sms()).
+constexpr int kDenseRows = 256;
+int gemm_plan_dense(GemmPlan* plan, const void* w, int n_out, int k, const void* x, int n_rows, int x_rows,
+                    int x_row_stride_elems, int epi);
 int gemm_plan(GemmPlan* plan, const void* w, int n_out, int k, const void* x, int t_pad, int x_row_stride_elems,
               int epi, int grid);
 // 4-bit affine weights (MLX layout): packed uint32 [n_out][k/8], bf16
 // scales / biases [n_out][k/64]; epilogues kEpiStore, kEpiPartial, kEpiSwiglu
 int gemm_plan_q4(GemmPlan* plan, const void* w_packed, const void* scales, const void* biases, int n_out, int k,
                  const void* x, int t_pad, int x_row_stride_elems, int epi, int grid);
+size_t gemm_ws_counter_bytes();  // the counter block at the start of a workspace (zero between launches)
+// 4-bit affine weights (MLX layout) -> bf16 [n_out][k]
+int dequant_q4_launch(const void* packed, const void* scales, const void* biases, int n_out, int k, void* out,
+                      cudaStream_t st);
 int gemm_bind_ws(GemmPlan* plan, void* ws, size_t ws_bytes);
 int gemm_launch(const GemmPlan& plan, cudaStream_t stream);
 

@@ -519,6 +519,200 @@ static int forward_impl(dtree_qwen3_model* m, const int32_t* tree_tokens, const 
   return kOk;
 }
 
+// ------------------------------------------------------------ prompt prefill
+// Dense causal forward of the prompt (Qwen3TargetAdapter._forward_states over
+// the prompt, adapters.py:494-533, as called by dtree_runtime.py:342-349):
+// every projection is one dense tcgen05 GEMM over all prompt rows (tiles of
+// 128 weight rows x 256 tokens), so the weights stream once per prompt
+// instead of once per 128 rows, and the attention runs the prompt's 128-row
+// chunks in one launch per layer.  Same bf16 rounding points as the verify
+// forward: projections are bf16, residual adds round once, RMSNorm in fp32.
+namespace dtree {
+
+__global__ void chain_masks_kernel(uint64_t* anc) {
+  const int i = threadIdx.x;  // row i of a 128-row chain sees rows 0..i
+  anc[2 * i] = i >= 63 ? ~0ull : ((1ull << (i + 1)) - 1ull);
+  anc[2 * i + 1] = i < 64 ? 0ull : (i >= 127 ? ~0ull : ((1ull << (i - 63)) - 1ull));
+}
+
+struct PrefillLayout {
+  size_t h, xn, big, q, attn, lm_in, anc, wdq, gemm, total;
+  int n_pad;
+};
+
+static PrefillLayout prefill_layout(const dtree_qwen3_desc& d, int n_rows) {
+  PrefillLayout L{};
+  L.n_pad = ((n_rows + kDenseRows - 1) / kDenseRows) * kDenseRows;
+  const size_t np = static_cast<size_t>(L.n_pad);
+  const size_t qd = static_cast<size_t>(d.n_heads) * d.head_dim;
+  const size_t wide = std::max<size_t>(qkv_width(d), d.ffn);
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    const size_t o = off;
+    off += (bytes + 255) & ~static_cast<size_t>(255);
+    return o;
+  };
+  L.h = take(np * d.hidden * 2);
+  L.xn = take(np * d.hidden * 2);
+  L.big = take(np * wide * 2);
+  L.q = take(np * qd * 2);
+  L.attn = take(np * qd * 2);
+  L.lm_in = take(static_cast<size_t>(16) * d.hidden * 2);
+  L.anc = take(128 * 16);
+  // 4-bit weights: the largest matrix dequantized to bf16 ahead of its GEMM
+  const size_t wmax = std::max({static_cast<size_t>(qkv_width(d)) * d.hidden, static_cast<size_t>(d.hidden) * qd,
+                                static_cast<size_t>(2) * d.ffn * d.hidden, static_cast<size_t>(d.hidden) * d.ffn});
+  L.wdq = d.quant_bits == 4 ? take(wmax * 2) : off;
+  L.gemm = take(gemm_ws_bytes(kDenseRows, num_sms()));
+  L.total = off;
+  return L;
+}
+
+}  // namespace dtree
+
+extern "C" size_t dtree_qwen3_prefill_workspace_bytes(const dtree_qwen3_desc* d, int n_rows) {
+  if (!d || n_rows <= 0) return 0;
+  return prefill_layout(*d, n_rows).total;
+}
+
+extern "C" int dtree_qwen3_prefill(dtree_qwen3_model* m, const int32_t* tokens, const int32_t* positions, int n_rows,
+                                   const dtree_step_state* state, void* hidden_out, int ld_hidden_out,
+                                   void* norm_out, int32_t* next_token, void* workspace, size_t workspace_bytes,
+                                   void* stream_) {
+  DTREE_CHECK_ARG(m && tokens && positions && state && next_token && workspace, "null pointer");
+  const dtree_qwen3_desc& d = m->d;
+  DTREE_CHECK_ARG(n_rows > 0 && n_rows <= d.kv_capacity, "n_rows must be in [1, kv_capacity]");
+  DTREE_CHECK_ARG(d.n_capture == 0 || hidden_out, "null hidden_out with captured layers");
+  DTREE_CHECK_ARG(!hidden_out || ld_hidden_out >= d.hidden * d.n_capture, "ld_hidden_out below n_capture * hidden");
+  const PrefillLayout Lo = prefill_layout(d, n_rows);
+  DTREE_CHECK_ARG(workspace_bytes >= Lo.total, "prefill workspace too small");
+  cudaStream_t st = static_cast<cudaStream_t>(stream_);
+  char* ws = static_cast<char*>(workspace);
+  auto at = [&](size_t off) { return reinterpret_cast<__nv_bfloat16*>(ws + off); };
+  auto bf = [](const void* p) { return static_cast<const __nv_bfloat16*>(p); };
+  __nv_bfloat16 *h = at(Lo.h), *xn = at(Lo.xn), *big = at(Lo.big), *q = at(Lo.q), *attn = at(Lo.attn);
+  __nv_bfloat16* wdq = at(Lo.wdq);
+  uint64_t* anc = reinterpret_cast<uint64_t*>(ws + Lo.anc);
+  void* gws = ws + Lo.gemm;
+  const size_t gws_bytes = Lo.total - Lo.gemm;
+  const int np = Lo.n_pad;
+  const int qd = d.n_heads * d.head_dim;
+  const int qkvw = qkv_width(d);
+  const size_t plane = static_cast<size_t>(d.n_kv_heads) * d.kv_capacity * d.head_dim;
+  const bool q4 = d.quant_bits == 4;
+  DTREE_CUDA_RET(cudaMemsetAsync(gws, 0, gemm_ws_counter_bytes(), st));
+  DTREE_CUDA_RET(launch_pdl(chain_masks_kernel, dim3(1), dim3(128), 0, st, anc));
+  int rc;
+  // dense GEMM out = x @ W^T with W bf16, or dequantized from 4 bits first
+  auto dense = [&](const void* w, const void* sc, const void* bi, int n_out, int k, const __nv_bfloat16* x, int epi,
+                   __nv_bfloat16* out, int ldo, __nv_bfloat16* capture, int ldc) -> int {
+    const void* wb = w;
+    if (q4) {
+      int r = dequant_q4_launch(w, sc, bi, n_out, k, wdq, st);
+      if (r) return r;
+      wb = wdq;
+    }
+    GemmPlan g;
+    int r = gemm_plan_dense(&g, wb, n_out, k, x, n_rows, np, k, epi);
+    if (r) return r;
+    if ((r = gemm_bind_ws(&g, gws, gws_bytes))) return r;
+    g.p.out = out;
+    g.p.ldo = ldo;
+    g.p.capture = capture;
+    g.p.ldc = ldc;
+    g.p.w_dep = q4 ? 1 : 0;  // the dequant kernel just before writes W
+    return gemm_launch(g, st);
+  };
+  auto capture_ptr = [&](int l) -> __nv_bfloat16* {
+    for (int c = 0; c < d.n_capture; ++c)
+      if (d.capture_layers[c] == l) return static_cast<__nv_bfloat16*>(hidden_out) + static_cast<size_t>(c) * d.hidden;
+    return nullptr;
+  };
+  // embedding gather + first input norm (rows n_rows..n_pad-1 zero)
+  if ((rc = rmsnorm_launch(nullptr, 0, tokens, bf(d.embed), h, bf(m->layers[0].input_norm), xn, d.hidden, n_rows, np,
+                           d.rms_eps, st)))
+    return rc;
+  for (int l = 0; l < d.layers; ++l) {
+    const dtree_qwen3_layer& L = m->layers[l];
+    const dtree_qwen3_q4_layer Q = q4 ? m->q4_layers[l] : dtree_qwen3_q4_layer{};
+    __nv_bfloat16* kc = static_cast<__nv_bfloat16*>(d.kv_cache) + (static_cast<size_t>(l) * 2 + 0) * plane;
+    __nv_bfloat16* vc = static_cast<__nv_bfloat16*>(d.kv_cache) + (static_cast<size_t>(l) * 2 + 1) * plane;
+    if ((rc = dense(L.qkv, Q.qkv_scales, Q.qkv_biases, qkvw, d.hidden, xn, kEpiStore, big, qkvw, nullptr, 0)))
+      return rc;
+    {  // q/k RMSNorm + RoPE, q -> buffer, k/v -> cache slots start + t
+      QkvFinishParams f{};
+      f.dense = big;
+      f.width = qkvw;
+      f.head_dim = d.head_dim;
+      f.n_q_heads = d.n_heads;
+      f.n_kv_heads = d.n_kv_heads;
+      f.q_norm = bf(L.q_norm);
+      f.k_norm = bf(L.k_norm);
+      f.eps = d.rms_eps;
+      f.rope_log2_theta = std::log2(d.rope_theta);
+      f.positions = positions;
+      f.state = state;
+      f.q_out = q;
+      f.k_cache = kc;
+      f.v_cache = vc;
+      f.kv_cap = d.kv_capacity;
+      if ((rc = qkv_finish_launch(f, n_rows, st))) return rc;
+    }
+    {  // causal attention, 128-row chunks
+      AttnParams a{};
+      a.q = q;
+      a.ldq = qd;
+      a.k = kc;
+      a.v = vc;
+      a.cap = d.kv_capacity;
+      a.n_q_heads = d.n_heads;
+      a.n_kv_heads = d.n_kv_heads;
+      a.n_nodes = n_rows;
+      a.state = state;
+      a.anc = anc;
+      a.scale_log2 = static_cast<float>(1.4426950408889634 / std::sqrt(static_cast<double>(d.head_dim)));
+      a.out = attn;
+      if ((rc = attn_prefill_launch(a, d.head_dim, st))) return rc;
+    }
+    // h += attn @ Wo^T; xn = RMSNorm(h, post_norm)
+    if ((rc = dense(L.o_proj, Q.o_scales, Q.o_biases, d.hidden, qd, attn, kEpiResidual, h, d.hidden, nullptr, 0)))
+      return rc;
+    if ((rc = rmsnorm_launch(h, d.hidden, nullptr, nullptr, nullptr, bf(L.post_norm), xn, d.hidden, n_rows, np,
+                             d.rms_eps, st)))
+      return rc;
+    if ((rc = dense(L.gate_up, Q.gate_up_scales, Q.gate_up_biases, 2 * d.ffn, d.hidden, xn, kEpiSwiglu, big, d.ffn,
+                    nullptr, 0)))
+      return rc;
+    // h += act @ Wd^T (+ the captured layer's hidden rows)
+    if ((rc = dense(L.down, Q.down_scales, Q.down_biases, d.hidden, d.ffn, big, kEpiResidual, h, d.hidden,
+                    capture_ptr(l), ld_hidden_out)))
+      return rc;
+    if (l + 1 < d.layers &&
+        (rc = rmsnorm_launch(h, d.hidden, nullptr, nullptr, nullptr, bf(m->layers[l + 1].input_norm), xn, d.hidden,
+                             n_rows, np, d.rms_eps, st)))
+      return rc;
+  }
+  if (norm_out &&  // RMSNorm(h, final_norm) of every row
+      (rc = rmsnorm_launch(h, d.hidden, nullptr, nullptr, nullptr, bf(d.final_norm),
+                           static_cast<__nv_bfloat16*>(norm_out), d.hidden, n_rows, n_rows, d.rms_eps, st)))
+    return rc;
+  // the next token from the last prompt row only
+  __nv_bfloat16* lm_in = at(Lo.lm_in);
+  if ((rc = rmsnorm_launch(h + static_cast<size_t>(n_rows - 1) * d.hidden, d.hidden, nullptr, nullptr, nullptr,
+                           bf(d.final_norm), lm_in, d.hidden, 1, 16, d.rms_eps, st)))
+    return rc;
+  GemmPlan g;
+  if ((rc = gemm_plan(&g, d.embed, d.vocab, d.hidden, lm_in, 16, d.hidden, kEpiArgmax, 0))) return rc;
+  if ((rc = gemm_bind_ws(&g, gws, gws_bytes))) return rc;
+  g.p.n_rows = 1;
+  g.p.vocab = d.vocab;
+  g.p.argmax_out = next_token;
+  g.p.inv_temp = m->inv_temp;
+  g.p.sample_seed = m->sample_seed;
+  g.p.sample_state = state;
+  return gemm_launch(g, st);
+}
+
 extern "C" int dtree_qwen3_set_sampling(dtree_qwen3_model* m, float temperature, uint32_t seed) {
   DTREE_CHECK_ARG(m, "null model");
   DTREE_CHECK_ARG(temperature >= 0.0f, "temperature must be >= 0");

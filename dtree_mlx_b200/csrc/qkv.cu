@@ -1,5 +1,6 @@
 // Finish of the fused q|k|v projection (qwen3_tree.py:50-65): sums the
-// split-K fp32 partials of the QKV GEMM in split order, then per head
+// split-K fp32 partials of the QKV GEMM in split order (or reads the bf16
+// projection of a dense prompt GEMM, the same bf16 value), then per head
 //   q, k: RMSNorm over head_dim (q_norm / k_norm), half-split RoPE at the
 //         node's position, q -> q buffer, k -> K cache slot start + t
 //   v:    -> V cache slot start + t
@@ -28,6 +29,7 @@ __global__ void __launch_bounds__(256) qkv_finish_kernel(QkvFinishParams p) {
   const int col = gh < p.n_q_heads ? gh * qcols + d : p.n_q_heads * qcols + (gh - p.n_q_heads) * hd + d;
   const size_t stride = static_cast<size_t>(p.part_rows) * p.width;
   auto sum_splits = [&](int c) {
+    if (p.dense) return __bfloat162float(p.dense[static_cast<size_t>(t) * p.width + c]);
     // up to 16 splits' loads in flight at once (one round trip), summed in
     // split order
     const float* src = p.partials + static_cast<size_t>(t) * p.width + c;

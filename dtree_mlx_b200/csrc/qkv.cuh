@@ -9,6 +9,7 @@ namespace dtree {
 struct QkvFinishParams {
   const float* partials;  // [split][part_rows][width]
   int split, part_rows, width;
+  const __nv_bfloat16* dense;  // non-null: the projection as bf16 [rows][width] instead of partials
   int head_dim, n_q_heads, n_kv_heads;
   const __nv_bfloat16* q_norm;
   const __nv_bfloat16* k_norm;

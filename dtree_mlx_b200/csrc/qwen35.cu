@@ -425,6 +425,261 @@ extern "C" int dtree_qwen35_forward(dtree_qwen35_model* m, const int32_t* tokens
   return kOk;
 }
 
+// ------------------------------------------------------------ prompt prefill
+// Dense causal forward of the prompt for the hybrid (Qwen35TargetAdapter's
+// forward_with_hidden_states over the prompt, adapters.py:216-450 with the
+// prefill of dtree_runtime.py:342-349): every projection is one dense
+// tcgen05 GEMM over all rows; a DeltaNet layer runs its causal conv over all
+// rows in one launch (chain parents), the recurrence as one sequence kernel
+// (state in f32 registers from the first row to the last, as mlx-lm's
+// sequence kernel) and advances the layer's conv / recurrent state to the
+// last row; a gated attention layer attends per 128-row chunk.
+namespace dtree {
+namespace {
+
+__global__ void prefill35_init_kernel(int32_t* parents, int n, uint64_t* anc, dtree_step_state* chunk_states,
+                                      int chunks, const dtree_step_state* state) {
+  pdl_trigger();
+  pdl_wait();
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) parents[i] = i - 1;
+  if (i < 128) {  // row i of a 128-row chain sees rows 0..i
+    anc[2 * i] = i >= 63 ? ~0ull : ((1ull << (i + 1)) - 1ull);
+    anc[2 * i + 1] = i < 64 ? 0ull : (i >= 127 ? ~0ull : ((1ull << (i - 63)) - 1ull));
+  }
+  if (i < chunks) {  // attention chunk i: rows from i*128 at slots start + i*128
+    dtree_step_state s = *state;
+    s.start += i * 128;
+    chunk_states[i] = s;
+  }
+}
+
+struct Prefill35Layout {
+  size_t h, xn, big, qkvn, mix, q, gate, parents, anc, states, lm_in, gemm, total;
+  int n_pad, chunks;
+};
+
+Prefill35Layout prefill35_layout(const dtree_qwen35_desc& d, const Dims& x, int n_rows) {
+  Prefill35Layout L{};
+  L.n_pad = ((n_rows + kDenseRows - 1) / kDenseRows) * kDenseRows;
+  L.chunks = (n_rows + 127) / 128;
+  const size_t np = static_cast<size_t>(L.n_pad);
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    const size_t o = off;
+    off += align256(bytes);
+    return o;
+  };
+  L.h = take(np * d.hidden * 2);
+  L.xn = take(np * d.hidden * 2);
+  L.big = take(np * std::max({x.proj_w, x.qkv_w, d.ffn}) * 2);
+  L.qkvn = take(np * x.conv_dim * 2);
+  L.mix = take(np * x.wide * 2);
+  L.q = take(np * x.wide * 2);
+  L.gate = take(np * x.q_dim * 2);
+  L.parents = take(np * 4);
+  L.anc = take(128 * 16);
+  L.states = take(static_cast<size_t>(L.chunks) * sizeof(dtree_step_state));
+  L.lm_in = take(static_cast<size_t>(16) * d.hidden * 2);
+  L.gemm = take(gemm_ws_bytes(kDenseRows, num_sms()));
+  L.total = off;
+  return L;
+}
+
+}  // namespace
+}  // namespace dtree
+
+extern "C" size_t dtree_qwen35_prefill_workspace_bytes(const dtree_qwen35_desc* d, int n_rows) {
+  if (!d || n_rows <= 0 || d->full_attention_interval <= 0) return 0;
+  return prefill35_layout(*d, dims_of(*d), n_rows).total;
+}
+
+extern "C" int dtree_qwen35_prefill(dtree_qwen35_model* m, const int32_t* tokens, const int32_t* positions,
+                                    int n_rows, const dtree_step_state* state, void* hidden_out, int ld_hidden_out,
+                                    void* norm_out, int32_t* next_token, void* workspace, size_t workspace_bytes,
+                                    void* stream_) {
+  DTREE_CHECK_ARG(m && tokens && positions && state && next_token && workspace, "null pointer");
+  const dtree_qwen35_desc& d = m->d;
+  const Dims& x = m->x;
+  DTREE_CHECK_ARG(n_rows > 0 && n_rows <= d.kv_capacity, "n_rows must be in [1, kv_capacity]");
+  DTREE_CHECK_ARG(d.n_capture == 0 || hidden_out, "null hidden_out with captured layers");
+  DTREE_CHECK_ARG(!hidden_out || ld_hidden_out >= d.hidden * d.n_capture, "ld_hidden_out below n_capture * hidden");
+  const Prefill35Layout Lo = prefill35_layout(d, x, n_rows);
+  DTREE_CHECK_ARG(workspace_bytes >= Lo.total, "prefill workspace too small");
+  cudaStream_t st = static_cast<cudaStream_t>(stream_);
+  char* ws = static_cast<char*>(workspace);
+  auto at = [&](size_t off) { return reinterpret_cast<__nv_bfloat16*>(ws + off); };
+  auto bf = [](const void* p) { return static_cast<const __nv_bfloat16*>(p); };
+  __nv_bfloat16 *h = at(Lo.h), *xn = at(Lo.xn), *big = at(Lo.big), *qkvn = at(Lo.qkvn), *mix = at(Lo.mix);
+  __nv_bfloat16 *q = at(Lo.q), *gate = at(Lo.gate);
+  int32_t* parents = reinterpret_cast<int32_t*>(ws + Lo.parents);
+  uint64_t* anc = reinterpret_cast<uint64_t*>(ws + Lo.anc);
+  dtree_step_state* cstates = reinterpret_cast<dtree_step_state*>(ws + Lo.states);
+  void* gws = ws + Lo.gemm;
+  const size_t gws_bytes = Lo.total - Lo.gemm;
+  const int np = Lo.n_pad;
+  const size_t plane = static_cast<size_t>(d.n_kv_heads) * d.kv_capacity * d.head_dim;
+  const int rot = static_cast<int>(std::lround(d.head_dim * d.partial_rotary_factor));
+  DTREE_CUDA_RET(cudaMemsetAsync(gws, 0, gemm_ws_counter_bytes(), st));
+  const int init_n = std::max({n_rows, 128, Lo.chunks});
+  DTREE_CUDA_RET(launch_pdl(prefill35_init_kernel, dim3((init_n + 255) / 256), dim3(256), 0, st, parents, n_rows, anc,
+                            cstates, Lo.chunks, state));
+  int rc;
+  auto dense = [&](const void* w, int n_out, int k, const __nv_bfloat16* xin, int ldx, int epi, __nv_bfloat16* out,
+                   int ldo, __nv_bfloat16* capture, int ldc) -> int {
+    GemmPlan g;
+    int r = gemm_plan_dense(&g, w, n_out, k, xin, n_rows, np, ldx, epi);
+    if (r) return r;
+    if ((r = gemm_bind_ws(&g, gws, gws_bytes))) return r;
+    g.p.out = out;
+    g.p.ldo = ldo;
+    g.p.capture = capture;
+    g.p.ldc = ldc;
+    return gemm_launch(g, st);
+  };
+  auto capture_ptr = [&](int l) -> __nv_bfloat16* {
+    for (int c = 0; c < d.n_capture; ++c)
+      if (d.capture_layers[c] == l) return static_cast<__nv_bfloat16*>(hidden_out) + static_cast<size_t>(c) * d.hidden;
+    return nullptr;
+  };
+  const void* norm0 = is_attn_layer(d, 0) ? m->att[0].input_norm : m->lin[0].input_norm;
+  if ((rc = rmsnorm_launch(nullptr, 0, tokens, bf(d.embed), h, bf(norm0), xn, d.hidden, n_rows, np, d.rms_eps, st)))
+    return rc;
+  const int G = d.n_heads / d.n_kv_heads;
+  const int nvh = d.head_dim > 128 ? 2 : 1;
+  for (int l = 0; l < d.layers; ++l) {
+    const int s = m->slot[l];
+    const bool attn = is_attn_layer(d, l);
+    const void* post_norm = attn ? m->att[s].post_norm : m->lin[s].post_norm;
+    const void *gate_up, *down;
+    if (attn) {
+      const dtree_qwen35_attn_layer& A = m->att[s];
+      gate_up = A.gate_up;
+      down = A.down;
+      __nv_bfloat16* kc = static_cast<__nv_bfloat16*>(d.kv_cache) + (static_cast<size_t>(s) * 2 + 0) * plane;
+      __nv_bfloat16* vc = static_cast<__nv_bfloat16*>(d.kv_cache) + (static_cast<size_t>(s) * 2 + 1) * plane;
+      if ((rc = dense(A.qkv, x.qkv_w, d.hidden, xn, d.hidden, kEpiStore, big, x.qkv_w, nullptr, 0))) return rc;
+      QkvFinishParams f{};
+      f.dense = big;
+      f.width = x.qkv_w;
+      f.head_dim = d.head_dim;
+      f.n_q_heads = d.n_heads;
+      f.n_kv_heads = d.n_kv_heads;
+      f.q_norm = bf(A.q_norm);
+      f.k_norm = bf(A.k_norm);
+      f.eps = d.rms_eps;
+      f.rope_log2_theta = std::log2(d.rope_theta);
+      f.positions = positions;
+      f.state = state;
+      f.q_out = q;
+      f.k_cache = kc;
+      f.v_cache = vc;
+      f.kv_cap = d.kv_capacity;
+      f.gated = 1;
+      f.gate_out = gate;
+      f.rot_dims = rot;
+      if ((rc = qkv_finish_launch(f, n_rows, st))) return rc;
+      for (int c = 0; c < Lo.chunks; ++c) {  // causal attention, one 128-row chunk per launch
+        const int t = std::min(128, n_rows - c * 128);
+        const size_t off = static_cast<size_t>(c) * 128 * x.q_dim;
+        AttnParams a{};
+        a.q = q + off;
+        a.ldq = x.q_dim;
+        a.k = kc;
+        a.v = vc;
+        a.cap = d.kv_capacity;
+        a.n_q_heads = d.n_heads;
+        a.n_kv_heads = d.n_kv_heads;
+        a.n_nodes = t;
+        a.state = cstates + c;
+        a.anc = anc;
+        a.scale_log2 = static_cast<float>(1.4426950408889634 / std::sqrt(static_cast<double>(d.head_dim)));
+        a.splits = std::max(1, std::min(kAttnSplitsMax, num_sms() / (d.n_kv_heads * ((G * t + 127) / 128) * nvh)));
+        a.out = mix + off;
+        a.gate = gate + off;
+        if ((rc = attn_launch(a, d.head_dim, m->attn_ws, m->attn_ws_bytes, st))) return rc;
+      }
+      if ((rc = dense(A.o_proj, d.hidden, x.q_dim, mix, x.q_dim, kEpiResidual, h, d.hidden, nullptr, 0))) return rc;
+    } else {
+      const dtree_qwen35_linear_layer& L = m->lin[s];
+      gate_up = L.gate_up;
+      down = L.down;
+      __nv_bfloat16* cst = static_cast<__nv_bfloat16*>(d.conv_state) + static_cast<size_t>(s) * x.keep * x.conv_dim;
+      float* rst = static_cast<float*>(d.rec_state) + static_cast<size_t>(s) * d.lin_v_heads * d.lin_v_dim * d.lin_k_dim;
+      if ((rc = dense(L.in_proj, x.proj_w, d.hidden, xn, d.hidden, kEpiStore, big, x.proj_w, nullptr, 0))) return rc;
+      ConvParams c{};
+      c.x = big;
+      c.ldx = x.proj_w;
+      c.base = cst;
+      c.weight = L.conv_weight;
+      c.parents = parents;
+      c.n_nodes = n_rows;
+      c.conv_dim = x.conv_dim;
+      c.keep = x.keep;
+      c.out = qkvn;
+      c.ldo = x.conv_dim;
+      c.n_norm_heads = 2 * d.lin_k_heads;
+      c.n_q_heads = d.lin_k_heads;
+      if ((rc = tree_conv1d_launch(c, 1, d.lin_k_dim, st))) return rc;
+      DeltaParams dp{};
+      dp.q = qkvn;
+      dp.k = qkvn + x.key_dim;
+      dp.ldqk = x.conv_dim;
+      dp.v = qkvn + 2 * x.key_dim;
+      dp.ldv = x.conv_dim;
+      dp.b = big + x.conv_dim + x.value_dim;
+      dp.a = big + x.conv_dim + x.value_dim + d.lin_v_heads;
+      dp.ldab = x.proj_w;
+      dp.a_log = d.a_log + static_cast<size_t>(s) * d.lin_v_heads;
+      dp.dt_bias = bf(d.dt_bias) + static_cast<size_t>(s) * d.lin_v_heads;
+      dp.state_in = rst;
+      dp.final_state = rst;
+      dp.n_nodes = n_rows;
+      dp.n_k_heads = d.lin_k_heads;
+      dp.n_v_heads = d.lin_v_heads;
+      dp.dv = d.lin_v_dim;
+      dp.y = mix;
+      dp.ldy = x.wide;
+      if ((rc = gated_delta_seq_launch(dp, d.lin_k_dim, st))) return rc;
+      // the conv window advances to the last prompt row (before `big` is reused)
+      if ((rc = conv_state_commit_launch(c, 1, nullptr, nullptr, 1, 0, 0, n_rows - 1, st))) return rc;
+      if ((rc = rmsnorm_gated_launch(mix, x.wide, big + x.conv_dim, x.proj_w, bf(L.norm), d.rms_eps, q, x.wide, n_rows,
+                                     d.lin_v_heads, d.lin_v_dim, st)))
+        return rc;
+      if ((rc = dense(L.out_proj, d.hidden, x.value_dim, q, x.wide, kEpiResidual, h, d.hidden, nullptr, 0))) return rc;
+    }
+    if ((rc = rmsnorm_launch(h, d.hidden, nullptr, nullptr, nullptr, bf(post_norm), xn, d.hidden, n_rows, np,
+                             d.rms_eps, st)))
+      return rc;
+    if ((rc = dense(gate_up, 2 * d.ffn, d.hidden, xn, d.hidden, kEpiSwiglu, big, d.ffn, nullptr, 0))) return rc;
+    if ((rc = dense(down, d.hidden, d.ffn, big, d.ffn, kEpiResidual, h, d.hidden, capture_ptr(l), ld_hidden_out)))
+      return rc;
+    if (l + 1 < d.layers) {
+      const void* nn = is_attn_layer(d, l + 1) ? m->att[m->slot[l + 1]].input_norm : m->lin[m->slot[l + 1]].input_norm;
+      if ((rc = rmsnorm_launch(h, d.hidden, nullptr, nullptr, nullptr, bf(nn), xn, d.hidden, n_rows, np, d.rms_eps,
+                               st)))
+        return rc;
+    }
+  }
+  if (norm_out && (rc = rmsnorm_launch(h, d.hidden, nullptr, nullptr, nullptr, bf(d.final_norm),
+                                       static_cast<__nv_bfloat16*>(norm_out), d.hidden, n_rows, n_rows, d.rms_eps, st)))
+    return rc;
+  __nv_bfloat16* lm_in = at(Lo.lm_in);
+  if ((rc = rmsnorm_launch(h + static_cast<size_t>(n_rows - 1) * d.hidden, d.hidden, nullptr, nullptr, nullptr,
+                           bf(d.final_norm), lm_in, d.hidden, 1, 16, d.rms_eps, st)))
+    return rc;
+  GemmPlan g;
+  if ((rc = gemm_plan(&g, d.embed, d.vocab, d.hidden, lm_in, 16, d.hidden, kEpiArgmax, 0))) return rc;
+  if ((rc = gemm_bind_ws(&g, gws, gws_bytes))) return rc;
+  g.p.n_rows = 1;
+  g.p.vocab = d.vocab;
+  g.p.argmax_out = next_token;
+  g.p.inv_temp = m->inv_temp;
+  g.p.sample_seed = m->sample_seed;
+  g.p.sample_state = state;
+  return gemm_launch(g, st);
+}
+
 extern "C" int dtree_qwen35_set_sampling(dtree_qwen35_model* m, float temperature, uint32_t seed) {
   DTREE_CHECK_ARG(m, "null model");
   DTREE_CHECK_ARG(temperature >= 0.0f, "temperature must be >= 0");

@@ -148,6 +148,39 @@ class Qwen3Engine:
         except Exception:
             pass
 
+    # rows per dense prefill call: its workspace grows ~linearly with the rows
+    # (about 65 KB per row at the 4B shape), longer prompts run in pieces
+    max_prefill_rows = 4096
+
+    def prefill_dense(self, tokens: torch.Tensor, state: torch.Tensor, hidden_out: torch.Tensor | None,
+                      next_token: torch.Tensor, norm_out: torch.Tensor | None = None) -> None:
+        """Dense causal forward of ``tokens`` (int32, device) after the
+        state.start cached rows (``dtree_qwen3_prefill``): K/V into the cache,
+        the captured layers' hidden rows into ``hidden_out`` [n, width], the
+        final-normed rows into ``norm_out`` [n, hidden] (optional) and the last
+        row's argmax (or sample) into ``next_token[0]``."""
+        n = int(tokens.numel())
+        if n <= 0 or n > self.max_prefill_rows:
+            raise ValueError(f"prefill rows must be in [1, {self.max_prefill_rows}], got {n}")
+        need = int(_lib.load().dtree_qwen3_prefill_workspace_bytes(C.byref(self._desc), n))
+        ws = getattr(self, "_prefill_ws", None)
+        if ws is None or ws.numel() < need:
+            self._prefill_ws = ws = torch.empty(need, dtype=torch.uint8, device=self.device)
+        start = int(state[0].item())
+        if start + n > self.kv_capacity:
+            raise ValueError(f"prompt of {start + n} rows exceeds kv_capacity {self.kv_capacity}")
+        pos = torch.arange(start, start + n, dtype=torch.int32, device=self.device)
+        ld = 0
+        if hidden_out is not None:
+            assert hidden_out.is_contiguous() and hidden_out.shape[0] >= n
+            ld = int(hidden_out.shape[1])
+        call("dtree_qwen3_prefill", self._handle, ptr(tokens), ptr(pos), n, ptr(state),
+             ptr(hidden_out) if hidden_out is not None else None, ld,
+             ptr(norm_out) if norm_out is not None else None, ptr(next_token), ptr(ws), ws.numel(), stream_ptr())
+
+    def release_prefill_workspace(self) -> None:
+        self._prefill_ws = None
+
     def set_sampling(self, temperature: float, seed: int) -> None:
         """Posterior tokens of later forwards: greedy (temperature < 1e-5) or
         sampled at `temperature` with Philox noise keyed by seed and step."""
@@ -242,6 +275,21 @@ class DecodeSession:
         self.state[2] = -1
         start = 0
         hidden_rows = []
+        if hasattr(eng, "prefill_dense") and n > chunk:
+            # prompts longer than one verify forward: one dense forward per
+            # piece of <= max_prefill_rows rows (the weights stream once per
+            # piece, not once per 128 rows)
+            self.prompt_hidden = torch.zeros(n, eng.hidden_width, dtype=torch.bfloat16, device=dev)
+            nxt = torch.zeros(1, dtype=torch.int32, device=dev)
+            while start < n:
+                t = min(eng.max_prefill_rows, n - start)
+                self.state[0] = start
+                eng.prefill_dense(toks[start:start + t].contiguous(), self.state,
+                                  self.prompt_hidden[start:start + t] if eng.layer_ids else None, nxt)
+                start += t
+            first = int(nxt.item())
+            self._after_prefill(n, first)
+            return first
         while start < n:
             t = min(chunk, n - start)
             self.state[0] = start
@@ -252,13 +300,17 @@ class DecodeSession:
             start += t
         first = int(self.posterior[t - 1].item())  # last prompt row of the last chunk
         self.prompt_hidden = torch.cat(hidden_rows, dim=0)
+        self._after_prefill(n, first)
+        return first
+
+    def _after_prefill(self, n: int, first: int) -> None:
+        eng = self.engine
         # recurrent targets: remember the post-prompt states so that ``reset``
         # can restart decoding from the prompt (the KV prefix needs no copy)
         self._snapshot = eng.snapshot_states() if hasattr(eng, "snapshot_states") else None
         self.reset(n, first)
         if hasattr(self.drafter, "begin"):  # a model drafter ingests the prompt context
             self.drafter.begin(self)
-        return first
 
     def reset(self, prompt_len: int, first_token: int) -> None:
         """Decode state right after prefill: start = prompt_len, root = first token."""

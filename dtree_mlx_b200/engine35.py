@@ -97,6 +97,37 @@ class Qwen35Engine:
         call("dtree_qwen35_forward", self._handle, ptr(tokens), ptr(positions), ptr(parents), ptr(anc),
              int(n_nodes), int(mode), ptr(state), ptr(posterior), stream_ptr())
 
+    max_prefill_rows = 4096  # rows per dense prefill call (workspace ~100 KB per row at the 9B shape)
+
+    def prefill_dense(self, tokens: torch.Tensor, state: torch.Tensor, hidden_out: torch.Tensor | None,
+                      next_token: torch.Tensor, norm_out: torch.Tensor | None = None) -> None:
+        """Dense causal forward of ``tokens`` after the state.start cached rows
+        (``dtree_qwen35_prefill``): K/V of the attention layers into the
+        cache, every DeltaNet layer's conv / recurrent state advanced to the
+        last row, captured hiddens into ``hidden_out``, the final-normed rows
+        into ``norm_out`` (optional), the next token into ``next_token[0]``."""
+        n = int(tokens.numel())
+        if n <= 0 or n > self.max_prefill_rows:
+            raise ValueError(f"prefill rows must be in [1, {self.max_prefill_rows}], got {n}")
+        need = int(_lib.load().dtree_qwen35_prefill_workspace_bytes(C.byref(self._desc), n))
+        ws = getattr(self, "_prefill_ws", None)
+        if ws is None or ws.numel() < need:
+            self._prefill_ws = ws = torch.empty(need, dtype=torch.uint8, device=self.device)
+        start = int(state[0].item())
+        if start + n > self.kv_capacity:
+            raise ValueError(f"prompt of {start + n} rows exceeds kv_capacity {self.kv_capacity}")
+        pos = torch.arange(start, start + n, dtype=torch.int32, device=self.device)
+        ld = 0
+        if hidden_out is not None:
+            assert hidden_out.is_contiguous() and hidden_out.shape[0] >= n
+            ld = int(hidden_out.shape[1])
+        call("dtree_qwen35_prefill", self._handle, ptr(tokens), ptr(pos), n, ptr(state),
+             ptr(hidden_out) if hidden_out is not None else None, ld,
+             ptr(norm_out) if norm_out is not None else None, ptr(next_token), ptr(ws), ws.numel(), stream_ptr())
+
+    def release_prefill_workspace(self) -> None:
+        self._prefill_ws = None
+
     def set_sampling(self, temperature: float, seed: int) -> None:
         """As Qwen3Engine.set_sampling."""
         call("dtree_qwen35_set_sampling", self._handle, float(temperature), int(seed) & 0xFFFFFFFF)

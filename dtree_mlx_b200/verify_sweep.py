@@ -125,6 +125,68 @@ def run(preset: str, layers: int | None, prefixes: list[int], budgets: list[int]
     return results
 
 
+def measured_tflops() -> tuple[float, str]:
+    """Sustained dense bf16 tensor throughput (a seconds-long GEMM loop)."""
+    p = Path(__file__).resolve().parents[1] / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d.get("bf16_tflops_sustained", d["bf16_tflops"])), "measured sustained"
+    return 1400.0, "fallback sustained"
+
+
+def prefill_flops(cfg, n: int) -> float:
+    """Algorithmic FLOPs of a causal prompt forward of n rows from slot 0:
+    every projection (2 n K N), causal attention (QK^T and PV over the
+    rows' visible keys) and the last row's LM head."""
+    H, L = cfg.hidden_size, cfg.num_hidden_layers
+    qd, kvd = cfg.num_attention_heads * cfg.head_dim, cfg.num_key_value_heads * cfg.head_dim
+    proj = H * (qd + 2 * kvd) + qd * H + 2 * cfg.intermediate_size * H + cfg.intermediate_size * H
+    keys = n * (n + 1) / 2
+    attn = 4.0 * cfg.num_attention_heads * cfg.head_dim * keys
+    return float(L * (2.0 * n * proj + attn) + 2.0 * H * cfg.vocab_size)
+
+
+def run_prefill(preset: str, layers: int | None, n: int, iters: int, quant_bits: int = 16, seed: int = 0) -> dict:
+    """Dense prefill of n prompt rows (dtree_qwen3_prefill) against the
+    verify-path prefill it replaces (128-row forwards)."""
+    from .engine import chain_anc_masks
+
+    cfg = PRESETS[preset]
+    if layers:
+        cfg = replace(cfg, num_hidden_layers=layers)
+    w = random_qwen3_weights(cfg, seed=seed, device="cuda")
+    if quant_bits == 4:
+        w = quantize_weights(w)
+    eng = Qwen3Engine(w, kv_capacity=n + 128, layer_ids=[1])
+    toks = torch.randint(0, cfg.vocab_size, (n,), dtype=torch.int32, device="cuda")
+    state = kernels.new_state("cuda", start=0)
+    hid = torch.zeros(n, cfg.hidden_size, dtype=torch.bfloat16, device="cuda")
+    nxt = torch.zeros(1, dtype=torch.int32, device="cuda")
+    ms_dense = _time(lambda: eng.prefill_dense(toks, state, hid, nxt), iters, True)
+    post = torch.zeros(128, dtype=torch.int32, device="cuda")
+    st2 = kernels.new_state("cuda", start=0)
+    chunks = []
+    for s in range(0, n, 128):
+        t = min(128, n - s)
+        chunks.append((s, t, torch.arange(s, s + t, dtype=torch.int32, device="cuda"),
+                       torch.from_numpy(chain_anc_masks(t).view(np.int64)).to("cuda")))
+
+    def chained():
+        for s, t, pos, anc in chunks:
+            st2[0] = s
+            eng.prefill_chunk(toks[s:s + t], pos, anc, t, st2, post)
+
+    ms_chain = _time(chained, max(1, iters // 2), True)
+    eng.close()
+    flops = prefill_flops(cfg, n)
+    peak, src = measured_tflops()
+    tf = flops / (ms_dense * 1e-3) / 1e12
+    return {"prefill_rows": n, "layers": cfg.num_hidden_layers, "quant_bits": quant_bits,
+            "dense_ms": round(ms_dense, 3), "verify_path_ms": round(ms_chain, 3),
+            "speedup": round(ms_chain / ms_dense, 2), "tflops": round(tf, 1), "peak_tflops": peak,
+            "peak_source": src, "frac_of_tensor_peak": round(tf / peak, 4)}
+
+
 def _time(fn, iters: int, eager_only: bool) -> float:
     for _ in range(3):
         fn()
@@ -287,9 +349,14 @@ def main() -> None:
                     help="4: MLX affine 4-bit projections, group 64 (BASELINE config 3)")
     ap.add_argument("--json", action="store_true")
     ap.add_argument("--drafter", default=None, help="time one DFlash draft step of this drafter preset and exit")
+    ap.add_argument("--prefill", type=int, default=0,
+                    help="time a dense prefill of this many prompt rows (and the verify-path prefill) and exit")
     ap.add_argument("--launches", default=None,
                     help="summarise an ncu launch-list CSV of an --eager sweep (attention/GEMM split) and exit")
     a = ap.parse_args()
+    if a.prefill:
+        print(json.dumps(run_prefill(a.preset, a.layers, a.prefill, a.iters, a.quant_bits)))
+        return
     if a.drafter:
         for P in [int(x) for x in a.prefix.split(",")]:
             print(json.dumps(run_drafter(a.drafter, P, a.iters, a.eager)))

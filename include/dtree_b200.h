@@ -384,6 +384,26 @@ DTREE_API int dtree_qwen3_forward_tree(dtree_qwen3_model* model, const int32_t* 
  * (runtime.py:160-215, dtree_runtime.py:455-470). */
 DTREE_API int dtree_qwen3_set_sampling(dtree_qwen3_model* model, float temperature, uint32_t seed);
 
+/* Dense prompt prefill: replaces Qwen3TargetAdapter.forward_with_hidden_states
+ * over the prompt (adapters.py:494-533; the prefill at dtree_runtime.py:342-349
+ * and runtime.py:459-465).  Rows t < n_rows (tokens[t] at RoPE position
+ * positions[t]) run causally after the state->start cached rows; their K/V go
+ * to cache slots state->start + t (state->start + n_rows <= kv_capacity).
+ * Each projection is one dense tensor-core GEMM over all rows (the weights
+ * stream once per call), the attention one launch per layer over the rows'
+ * 128-row chunks.  hidden_out [n_rows][ld_hidden_out] bf16 receives the
+ * captured layers' hidden states (column block c = capture_layers[c]; may be
+ * null when n_capture == 0); norm_out (nullable) [n_rows][hidden] bf16 the
+ * final-normed rows; next_token[0] = argmax of the last row's logits
+ * (or a sample at the model's temperature, dtree_qwen3_set_sampling, keyed by
+ * state->step, row 0).  workspace >= dtree_qwen3_prefill_workspace_bytes(desc,
+ * n_rows) device bytes, used by nothing else while the call's kernels run. */
+DTREE_API size_t dtree_qwen3_prefill_workspace_bytes(const dtree_qwen3_desc* desc, int n_rows);
+DTREE_API int dtree_qwen3_prefill(dtree_qwen3_model* model, const int32_t* tokens, const int32_t* positions,
+                                  int n_rows, const dtree_step_state* state, void* hidden_out, int ld_hidden_out,
+                                  void* norm_out, int32_t* next_token, void* workspace, size_t workspace_bytes,
+                                  void* stream);
+
 /* ----------------------------------------------- DFlash block drafter
  * The drafter (DFlashDraftModel, draft.py:318-367) is a stack of Qwen3
  * decoder layers held as a dtree_qwen3 model whose `embed` is the TARGET's
@@ -533,6 +553,21 @@ DTREE_API int dtree_qwen35_commit(dtree_qwen35_model* model, const int32_t* pare
 
 /* As dtree_qwen3_set_sampling, for the hybrid model. */
 DTREE_API int dtree_qwen35_set_sampling(dtree_qwen35_model* model, float temperature, uint32_t seed);
+
+/* Dense prompt prefill of the hybrid: replaces Qwen35TargetAdapter's
+ * forward_with_hidden_states over the prompt (adapters.py:216-450, called by
+ * dtree_runtime.py:342-349) with dtree_qwen3_prefill's contract (rows after
+ * state->start, K/V of the attention layers to slots state->start + t,
+ * hidden_out / norm_out / next_token as there).  Each DeltaNet layer's conv
+ * and recurrent state start from the model's current state (zero for a new
+ * sequence) and end at the last row: the recurrence runs as one chain in
+ * f32, as mlx-lm's sequence kernel does.  workspace >=
+ * dtree_qwen35_prefill_workspace_bytes(desc, n_rows). */
+DTREE_API size_t dtree_qwen35_prefill_workspace_bytes(const dtree_qwen35_desc* desc, int n_rows);
+DTREE_API int dtree_qwen35_prefill(dtree_qwen35_model* model, const int32_t* tokens, const int32_t* positions,
+                                   int n_rows, const dtree_step_state* state, void* hidden_out, int ld_hidden_out,
+                                   void* norm_out, int32_t* next_token, void* workspace, size_t workspace_bytes,
+                                   void* stream);
 
 #ifdef __cplusplus
 }
