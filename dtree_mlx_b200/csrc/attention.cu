@@ -377,7 +377,9 @@ __device__ __forceinline__ uint32_t sw128_off(int row, int chunk16) {
   return static_cast<uint32_t>(row * 128 + ((chunk16 ^ (row & 7)) << 4));
 }
 
-template <int HD>
+// PROMPT: the prompt (prefill) instantiation, causal 128-row chunks
+// (AttnParams::chunk_rows); the tree-verify one has none of its code
+template <int HD, bool PROMPT = false>
 __global__ void __launch_bounds__(kTcThreads) tree_attn_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
                                                                    const __grid_constant__ CUtensorMap tmap_v,
                                                                    AttnParams p) {
@@ -405,13 +407,13 @@ __global__ void __launch_bounds__(kTcThreads) tree_attn_tc_kernel(const __grid_c
   const int G = p.n_q_heads / p.n_kv_heads;
   // prompt mode: blockIdx.y = chunk * chunk_rbs + row block; the chunk's
   // rows are queries row0 .. row0 + T - 1 at slots start + row0 ..
-  const bool chunked = p.chunk_rows > 0;
+  constexpr bool chunked = PROMPT;
   const int chunk = chunked ? static_cast<int>(blockIdx.y) / p.chunk_rbs : 0;
   const int rb = chunked ? static_cast<int>(blockIdx.y) % p.chunk_rbs : static_cast<int>(blockIdx.y);
   const int row0 = chunk * p.chunk_rows;
   const int T = chunked ? min(p.chunk_rows, p.n_nodes - row0) : p.n_nodes;
   const int rows_kv = G * T;
-  if (rb * 128 >= rows_kv) return;  // row block past a ragged last chunk (CTA-uniform)
+  if (chunked && rb * 128 >= rows_kv) return;  // row block past a ragged last chunk (CTA-uniform)
 
   if (t == 0) {
     // prefix keys into L2 while the upstream kernels finish.  `start` read
@@ -687,14 +689,16 @@ __global__ void __launch_bounds__(kTcThreads) tree_attn_tc_kernel(const __grid_c
       pml[1] = l_run;
     }
     __syncwarp();
+    if (!chunked) {
 #pragma unroll 4
-    for (int rr = sub; rr < 32 && !chunked; rr += RPI) {
+    for (int rr = sub; rr < 32; rr += RPI) {
       const int rg2 = rb * 128 + (warp & 3) * 32 + rr;
       if (rg2 < rows_kv) {
         const int qrow = (kvh * G + rg2 / T) * T + rg2 % T;
         float4* dst = reinterpret_cast<float4*>(p.part_o + (static_cast<size_t>(split) * rows_total + qrow) * HD + h * OH);
         dst[vi] = *reinterpret_cast<const float4*>(stage + rr * LDS + vi * 4);
       }
+    }
     }
   }
   tc_fence_before();
@@ -852,12 +856,12 @@ int attn_prefill_launch(const AttnParams& p0, int head_dim, cudaStream_t stream)
   if ((rc = plane_tmap(&tv, p.v, rows, head_dim))) return rc;
   const dim3 grid(1, chunks * p.chunk_rbs, p.n_kv_heads);
   if (head_dim == 128) {
-    DTREE_CUDA_RET(ensure_smem_attr(tree_attn_tc_kernel<128>, TcCfg<128>::kSmem));
-    DTREE_CUDA_RET(launch_pdl(tree_attn_tc_kernel<128>, grid, dim3(kTcThreads),
+    DTREE_CUDA_RET(ensure_smem_attr(tree_attn_tc_kernel<128, true>, TcCfg<128>::kSmem));
+    DTREE_CUDA_RET(launch_pdl(tree_attn_tc_kernel<128, true>, grid, dim3(kTcThreads),
                               static_cast<size_t>(TcCfg<128>::kSmem), stream, tk, tv, p));
   } else {
-    DTREE_CUDA_RET(ensure_smem_attr(tree_attn_tc_kernel<64>, TcCfg<64>::kSmem));
-    DTREE_CUDA_RET(launch_pdl(tree_attn_tc_kernel<64>, grid, dim3(kTcThreads),
+    DTREE_CUDA_RET(ensure_smem_attr(tree_attn_tc_kernel<64, true>, TcCfg<64>::kSmem));
+    DTREE_CUDA_RET(launch_pdl(tree_attn_tc_kernel<64, true>, grid, dim3(kTcThreads),
                               static_cast<size_t>(TcCfg<64>::kSmem), stream, tk, tv, p));
   }
   return kOk;

@@ -365,9 +365,9 @@ cudaError_t ensure_smem_attr(K kernel, int bytes) {
 // cuTensorMapEncodeTiled via the runtime's driver entry point (no -lcuda)
 int make_tmap_2d_bf16(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer, uint64_t row_stride_bytes,
                       uint32_t box_inner, uint32_t box_outer, bool swizzle128);
-// uint32 elements, no swizzle (packed 4-bit weight tiles)
+// uint32 elements (packed 4-bit weight tiles); swizzle128 needs 128-byte box rows
 int make_tmap_2d_u32(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer, uint64_t row_stride_bytes,
-                     uint32_t box_inner, uint32_t box_outer);
+                     uint32_t box_inner, uint32_t box_outer, bool swizzle128);
 
 int num_sms();
 

@@ -26,10 +26,12 @@
 //
 // Q4 variant (4-bit affine weights, group 64 along K, MLX layout: packed
 // uint32 [N][K/8] with element 8j+i in bits 4i..4i+3 of word j, bf16 scales
-// and biases [N][K/64]): TMA brings the packed 128x64 tile (4 KB) instead of
-// the bf16 one, and 8 more warps (6..13) dequantize it, w = scale*q + bias
-// rounded once to bf16 (fma.rn.bf16x2), straight into the 128-byte-swizzled
-// K-major layout the MMA reads.  One K block of 64 is exactly one group.
+// and biases [N][K/64]): a stream-K unit is 256 wide in K (4 groups); TMA
+// brings the packed 128x256 tile (16 KB, 128-byte swizzled) and the four
+// 64-wide X blocks, 8 more warps (6..13) dequantize it, w = scale*q + bias
+// rounded once to bf16 (fma.rn.bf16x2), into a TMEM buffer that the MMA
+// reads as its A operand (16 MMAs of K 16 per unit, so the MMA thread's
+// one barrier wait and two commits per unit are spread over 16 MMAs).
 #pragma once
 
 #include "common.cuh"
@@ -56,7 +58,7 @@ struct GemmParams {
   int grid;    // CTAs (stream-K ranges, or m_tiles * split)
   int split;   // > 0: tile-aligned split-K (CTA c -> tile c / split, split c % split); 0: stream-K
   float* out_f32;  // kEpiPartial output [split][TPAD][ldo]
-  float* ws;            // [grid][2][TPAD][128] fp32 partial tiles
+  float* ws;            // [grid][2][128][TPAD] fp32 partial tiles (row-major per slot)
   uint32_t* tile_cnt;   // [m_tiles] arrival counters (zero between launches)
   // store / residual / swiglu
   __nv_bfloat16* out;
@@ -86,34 +88,33 @@ struct GemmParams {
   float inv_temp;
   uint32_t sample_seed;
   const dtree_step_state* sample_state;
-  // q4 weights: bf16 scale / bias per (row, group of 64); row stride = kb
+  // q4 weights: bf16 scale / bias per (row, group of 64); row stride =
+  // k_groups = K / 64 (a unit spans 4 groups; the last unit of a row may
+  // hold fewer, its missing groups read as zero weights)
   const __nv_bfloat16* q_scales;
   const __nv_bfloat16* q_biases;
+  int k_groups;
 };
 
 constexpr int kGemmThreads = 192;
-constexpr int kDeqWarps = 8;                             // q4 dequant warps
+constexpr int kDeqWarps = 8;                             // q4 dequant warps (two per TMEM lane quarter)
 constexpr int kQ4BudgetKB = 150;                         // q4 CTA shared memory (one CTA per SM)
-constexpr int kDeqGroups = 2;                            // units dequantized concurrently
-constexpr int kDeqGroupWarps = kDeqWarps / kDeqGroups;
 constexpr int kGemmThreadsQ4 = 192 + kDeqWarps * 32;
-constexpr int kDeqTpr = kDeqGroupWarps * 32 / 128;       // threads per tile row (within a group)
-constexpr int kDeqWpt = 8 / kDeqTpr;                     // packed words (8 weights) per thread
 constexpr int kWTileBytes = 128 * 64 * 2;
-constexpr int kPkTileBytes = 128 * 64 / 2;  // packed 4-bit tile
+constexpr int kPkTileBytes = 128 * 64 / 2;  // packed 4-bit tile of one 64-wide K block
+constexpr int kQ4Kb = 4;                    // q4: 64-wide K blocks per stream-K unit
 
 template <int TPAD, int EPI, bool Q4 = false>
 struct GemmCfg {
-  static constexpr int kXBytes = TPAD * 64 * 2;
-  // bf16 stage: [W 16 KB][X]; q4 stage: [X][packed 4 KB] (X stays 1024-aligned)
-  static constexpr int kStageBytes = (Q4 ? kPkTileBytes : kWTileBytes) + kXBytes;
+  // 64-wide K blocks per stream-K unit: 1 (bf16) or kQ4Kb (q4: the MMA
+  // thread waits and commits once per 4 * kQ4Kb MMAs)
+  static constexpr int kKb = Q4 ? kQ4Kb : 1;
+  static constexpr int kXBlock = TPAD * 64 * 2;  // X of one K block (128-byte swizzled rows)
+  static constexpr int kXBytes = kXBlock * kKb;
+  // bf16 stage: [W 16 KB][X]; q4 stage: [X blocks][packed tile] (X stays 1024-aligned)
+  static constexpr int kStageBytes = (Q4 ? kPkTileBytes * kKb : kWTileBytes) + kXBytes;
   static constexpr int kXOff = Q4 ? 0 : kWTileBytes;
   static constexpr int kWOff = Q4 ? kXBytes : 0;
-  // dequantized W units in TMEM (32 columns each, beside the accumulators).
-  // The producer loads unit i only once the MMA of unit i - kDeq is done, so
-  // a landed stage also means a free buffer: kDeq is the q4 load lookahead.
-  static constexpr int kDeq = Q4 ? (TPAD >= 128 ? 4 : (TPAD >= 64 ? 8 : 12)) : 0;
-  static constexpr int kLookahead = Q4 ? kDeq : 0;  // 0: the whole ring
   static constexpr int kBarBytes = Q4 ? 512 : 256;
   static constexpr int kXchBytes = (EPI == kEpiQkv || EPI == kEpiSwiglu) ? 128 * 8 * 4 : 0;
   // [0,256): per-warp reductions of one 8-row chunk; then s_best / s_pos
@@ -128,19 +129,17 @@ struct GemmCfg {
   static constexpr int kFixed = 1024 /*align*/ + kBarBytes + kXchBytes + kRedBytes;
   static constexpr int kStagesRaw = (kBudget - kFixed) / kStageBytes;
   static constexpr int kMaxStages = Q4 ? 16 : 8;
-  // units per empty / deq_full barrier phase: the MMA thread's mbarrier
-  // operations (a few hundred cycles each next to in-flight MMAs) are paid
-  // once per group of kUpb q4 units
-  static constexpr int kUpb = Q4 ? (TPAD >= 64 ? 2 : 4) : 1;
-  static constexpr int kStages0 = kStagesRaw < 2 ? 2 : (kStagesRaw > kMaxStages ? kMaxStages : kStagesRaw);
-  static constexpr int kStages = (kStages0 / kUpb) * kUpb;
+  static constexpr int kStages = kStagesRaw < 2 ? 2 : (kStagesRaw > kMaxStages ? kMaxStages : kStagesRaw);
   static constexpr int kSmem = kFixed + kStages * kStageBytes;
   // TMEM: accumulator buffers (two, so a segment's MMAs overlap the previous
-  // segment's epilogue; one for q4 at TPAD 128) and, for q4, the dequantized
-  // W units (the MMA's A operand: 128 lanes x 32 columns of bf16 pairs each)
+  // segment's epilogue; one for q4 at TPAD 128) and, for q4, kDeq buffers of
+  // dequantized W units (the MMA's A operand: 128 lanes x 32 * kKb columns
+  // of bf16 pairs); the dequant warps refill buffer i % kDeq once the MMA
+  // of unit i - kDeq has committed it free
   static constexpr int kAccBufs = (Q4 && TPAD >= 128) ? 1 : 2;
   static constexpr int kTmemAcc = kAccBufs * TPAD;
-  static constexpr int kTmemNeed = kTmemAcc + (Q4 ? kDeq * 32 : 0);
+  static constexpr int kDeq = Q4 ? (512 - kTmemAcc) / (32 * kKb) : 0;
+  static constexpr int kTmemNeed = kTmemAcc + (Q4 ? kDeq * 32 * kKb : 0);
   static constexpr int kTmemCols =
       kTmemNeed <= 32 ? 32 : (kTmemNeed <= 64 ? 64 : (kTmemNeed <= 128 ? 128 : (kTmemNeed <= 256 ? 256 : 512)));
   static constexpr uint32_t kIdesc = idesc_bf16_f32(128, TPAD);
@@ -156,6 +155,29 @@ __device__ __forceinline__ int sk_cta_of(long long u, long long U, int G) {
 }
 
 __device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+
+// CW (16 or 32) consecutive accumulator columns of this thread's TMEM lane
+template <int CW>
+__device__ __forceinline__ void tmem_ld_cols(uint32_t taddr, float (&g)[CW]) {
+  if constexpr (CW == 32) {
+    uint32_t r[32];
+    tmem_ld_x32(taddr, r);
+    tmem_wait_ld();
+#pragma unroll
+    for (int j = 0; j < 32; ++j) g[j] = __uint_as_float(r[j]);
+  } else {
+    static_assert(CW == 16, "column group of 16 or 32");
+    uint32_t r0[8], r1[8];
+    tmem_ld_x8(taddr, r0);
+    tmem_ld_x8(taddr + 8, r1);
+    tmem_wait_ld();
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      g[j] = __uint_as_float(r0[j]);
+      g[8 + j] = __uint_as_float(r1[j]);
+    }
+  }
+}
 
 __device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
   uint32_t d;
@@ -200,11 +222,11 @@ __global__ void __launch_bounds__(Q4 ? kGemmThreadsQ4 : kGemmThreads, 1)
   uint64_t* empty_bar = full_bar + S;
   uint64_t* tfull_bar = empty_bar + S;
   uint64_t* tempty_bar = tfull_bar + 2;
-  // q4: deq_full[d] completes when the dequant warps have written buffer d
-  // (and, through their own wait, the stage's X tile has landed).  Buffer d
-  // of unit i is free again once the MMA of unit i - D completed, which the
-  // dequant warps read off that unit's empty_bar phase: one commit per unit.
+  // q4: deq_full[d] completes when the dequant warps have written TMEM
+  // buffer d (and, through their own wait, the stage's X blocks landed);
+  // tfree[d] when the MMAs that read buffer d completed.
   uint64_t* deq_full = tempty_bar + 2;   // [D] (q4 only)
+  uint64_t* tfree = deq_full + D;        // [D] (q4 only)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(deq_full + 2 * D);
   int* s_flag = reinterpret_cast<int*>(tmem_slot + 1);
   float* xch = reinterpret_cast<float*>(bar_base + C::kBarBytes);
@@ -212,7 +234,10 @@ __global__ void __launch_bounds__(Q4 ? kGemmThreadsQ4 : kGemmThreads, 1)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int G = p.grid;
-  const long long U = static_cast<long long>(p.m_tiles) * p.n_tiles * p.kb;
+  // token tiles: dense (prefill) tiles only; a tree verify has one
+  constexpr bool kDense = TPAD >= 256;
+  const int NT = kDense ? p.n_tiles : 1;
+  const long long U = static_cast<long long>(p.m_tiles) * NT * p.kb;
   const int cta = blockIdx.x;
   long long u0, u1;
   if (p.split > 0) {  // tile-aligned split-K: one segment per CTA
@@ -236,7 +261,8 @@ __global__ void __launch_bounds__(Q4 ? kGemmThreadsQ4 : kGemmThreads, 1)
         mbar_init(&tempty_bar[b], 4);
       }
       for (int b = 0; b < D; ++b) {
-        mbar_init(&deq_full[b], kDeqWarps * (C::kUpb / kDeqGroups));  // one arrival per dequant warp and unit
+        mbar_init(&deq_full[b], kDeqWarps);  // one arrival per dequant warp and unit
+        mbar_init(&tfree[b], 1);
       }
       fence_barrier_init();
       tma_prefetch_desc(&tmap_w);
@@ -253,46 +279,68 @@ __global__ void __launch_bounds__(Q4 ? kGemmThreadsQ4 : kGemmThreads, 1)
   if (warp == 0) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
-      const uint64_t pol_w = l2_policy_evict_first();
+      // weights stream once per verify (evict first); a dense tile's weights
+      // are re-read by every token tile (keep them)
+      const uint64_t pol_w = kDense ? l2_policy_evict_last() : l2_policy_evict_first();
       const uint64_t pol_x = l2_policy_evict_last();
-      constexpr int LA = C::kLookahead > 0 ? C::kLookahead : S;  // units in flight
+      constexpr int LA = S;  // units in flight: the whole ring
       const int pre = n_units < LA ? n_units : LA;
       // weights do not depend on the upstream kernel (unless w_dep): start
       // streaming now
       if (p.w_dep) pdl_wait();
-      for (int i = 0; i < pre; ++i) {
-        const long long u = u0 + i;
-        const int tile = static_cast<int>(u / p.kb), kblk = static_cast<int>(u % p.kb);
-        mbar_arrive_expect_tx(&full_bar[i], C::kStageBytes);
-        tma_load_2d(stage_base + i * C::kStageBytes + C::kWOff, &tmap_w, &full_bar[i], kblk * (Q4 ? 8 : 64),
-                    (tile / p.n_tiles) * 128, pol_w);
+      // the prefetched units' X coordinates are computed here, before the
+      // dependency wait: after it only the TMA issues remain
+      int xk[S], xr[S];
+      {
+        int tile = static_cast<int>(u0 / p.kb), kblk = static_cast<int>(u0 % p.kb);
+        int mt = tile / NT, nt = tile % NT;
+#pragma unroll
+        for (int i = 0; i < S; ++i) {
+          if (i < pre) {
+            mbar_arrive_expect_tx(&full_bar[i], C::kStageBytes);
+            tma_load_2d(stage_base + i * C::kStageBytes + C::kWOff, &tmap_w, &full_bar[i],
+                        kblk * (Q4 ? 8 * C::kKb : 64), mt * 128, pol_w);
+          }
+          xk[i] = kblk * C::kKb * 64;
+          xr[i] = nt * TPAD;
+          if (++kblk == p.kb) {
+            kblk = 0;
+            if (++nt == NT) {
+              nt = 0;
+              ++mt;
+            }
+          }
+        }
       }
       pdl_wait();
-      for (int i = 0; i < pre; ++i) {
-        const long long u = u0 + i;
-        const int tile = static_cast<int>(u / p.kb), kblk = static_cast<int>(u % p.kb);
-        tma_load_2d(stage_base + i * C::kStageBytes + C::kXOff, &tmap_x, &full_bar[i], kblk * 64,
-                    (tile % p.n_tiles) * TPAD, pol_x);
+#pragma unroll
+      for (int i = 0; i < S; ++i) {
+        if (i < pre) {
+#pragma unroll
+          for (int k2 = 0; k2 < C::kKb; ++k2)
+            tma_load_2d(stage_base + i * C::kStageBytes + C::kXOff + k2 * C::kXBlock, &tmap_x, &full_bar[i],
+                        xk[i] + k2 * 64, xr[i], pol_x);
+        }
       }
       bool ok = true;
       // (tile, kblk) of unit `pre`, advanced incrementally (no 64-bit division per unit)
       int tile = static_cast<int>((u0 + pre) / p.kb), kblk = static_cast<int>((u0 + pre) % p.kb);
-      int mt = tile / p.n_tiles, nt = tile % p.n_tiles;  // weight tile, token tile
+      int mt = tile / NT, nt = tile % NT;  // weight tile, token tile
       int s = pre % S;
       for (int i = pre; i < n_units && ok; ++i) {
-        if ((i - LA) % C::kUpb == 0) {  // the MMA of units i - LA .. (their phase's commit)
-          // released this stage and the next kUpb - 1 (and, for q4, their TMEM buffers)
-          const int jp = (i - LA) / C::kUpb;
-          ok = mbar_wait(&empty_bar[jp % (S / C::kUpb)], static_cast<uint32_t>(jp / (S / C::kUpb)) & 1u, 1);
-        }
+        // the MMA of unit i - S released this stage
+        ok = mbar_wait(&empty_bar[s], static_cast<uint32_t>((i - S) / S) & 1u, 1);
         if (!ok) break;
         mbar_arrive_expect_tx(&full_bar[s], C::kStageBytes);
         uint8_t* st = stage_base + s * C::kStageBytes;
-        tma_load_2d(st + C::kWOff, &tmap_w, &full_bar[s], kblk * (Q4 ? 8 : 64), mt * 128, pol_w);
-        tma_load_2d(st + C::kXOff, &tmap_x, &full_bar[s], kblk * 64, nt * TPAD, pol_x);
+        tma_load_2d(st + C::kWOff, &tmap_w, &full_bar[s], kblk * (Q4 ? 8 * C::kKb : 64), mt * 128, pol_w);
+#pragma unroll
+        for (int k2 = 0; k2 < C::kKb; ++k2)
+          tma_load_2d(st + C::kXOff + k2 * C::kXBlock, &tmap_x, &full_bar[s], (kblk * C::kKb + k2) * 64, nt * TPAD,
+                      pol_x);
         if (++kblk == p.kb) {
           kblk = 0;
-          if (++nt == p.n_tiles) {
+          if (++nt == NT) {
             nt = 0;
             ++mt;
           }
@@ -314,7 +362,7 @@ __global__ void __launch_bounds__(Q4 ? kGemmThreadsQ4 : kGemmThreads, 1)
       const uint64_t b_base = sw128_kmajor_desc(smem_u32(stage_base + C::kXOff));
       long long u = u0;
       int i = 0, seg = 0;
-      int s = 0, d = 0, dp = 0;  // stage, dequant buffer, deq_full phase slot
+      int s = 0, d = 0;  // stage, dequant buffer
       uint32_t ph = 0, phd = 0;
       bool ok = true;
       while (u < u1) {
@@ -326,21 +374,22 @@ __global__ void __launch_bounds__(Q4 ? kGemmThreadsQ4 : kGemmThreads, 1)
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(b * TPAD);
         for (int j = 0; j < len; ++j, ++i) {
-          if (i % C::kUpb == 0) {  // first unit of a barrier phase
-            if constexpr (Q4) {
-              if (ok) ok = mbar_wait(&deq_full[dp], phd, 8);
-            } else {
-              if (ok) ok = mbar_wait(&full_bar[s], ph, 4);
-            }
-            tc_fence_after();
+          if constexpr (Q4) {
+            if (ok) ok = mbar_wait(&deq_full[d], phd, 8);
+          } else {
+            if (ok) ok = mbar_wait(&full_bar[s], ph, 4);
           }
+          tc_fence_after();
           if (ok) {
             const uint64_t b0 = b_base + ((s * C::kStageBytes) >> 4);
             if constexpr (Q4) {  // A = the dequantized unit in TMEM, 8 columns per K step of 16
-              const uint32_t a_tmem = tmem_base + static_cast<uint32_t>(C::kTmemAcc + d * 32);
+              const uint32_t a_tmem = tmem_base + static_cast<uint32_t>(C::kTmemAcc + d * 32 * C::kKb);
 #pragma unroll
-              for (int kk = 0; kk < 4; ++kk)
-                umma_bf16_ts(d_tmem, a_tmem + kk * 8, b0 + kk * 2, C::kIdesc, (j > 0 || kk > 0) ? 1u : 0u);
+              for (int k2 = 0; k2 < C::kKb; ++k2)
+#pragma unroll
+                for (int kk = 0; kk < 4; ++kk)
+                  umma_bf16_ts(d_tmem, a_tmem + k2 * 32 + kk * 8, b0 + ((k2 * C::kXBlock) >> 4) + kk * 2, C::kIdesc,
+                               (j > 0 || k2 > 0 || kk > 0) ? 1u : 0u);
             } else {
               const uint64_t a0 = a_base + ((s * C::kStageBytes) >> 4);
 #pragma unroll
@@ -348,21 +397,17 @@ __global__ void __launch_bounds__(Q4 ? kGemmThreadsQ4 : kGemmThreads, 1)
                 umma_bf16(d_tmem, a0 + kk * 2, b0 + kk * 2, C::kIdesc, (j > 0 || kk > 0) ? 1u : 0u);
             }
           }
-          if (i % C::kUpb == C::kUpb - 1 || i == n_units - 1) {
-            umma_commit(&empty_bar[(i / C::kUpb) % (S / C::kUpb)]);
-            if constexpr (Q4) {
-              if (++dp == D / C::kUpb) {
-                dp = 0;
-                phd ^= 1u;
-              }
-            }
-          }
+          umma_commit(&empty_bar[s]);
+          if constexpr (Q4) umma_commit(&tfree[d]);
           if (++s == S) {
             s = 0;
             ph ^= 1u;
           }
           if constexpr (Q4) {
-            if (++d == D) d = 0;
+            if (++d == D) {
+              d = 0;
+              phd ^= 1u;
+            }
           }
         }
         umma_commit(&tfull_bar[b]);
@@ -372,101 +417,69 @@ __global__ void __launch_bounds__(Q4 ? kGemmThreadsQ4 : kGemmThreads, 1)
     }
   } else if (Q4 && warp >= 6) {
     // ------------------------------------------------------------ dequant (q4)
-    // kDeqGroups groups of warps work on different units at once (group g:
-    // units i = g, g + kDeqGroups, ...), so the per-unit chain of waits,
-    // shared-memory round trips and arrivals of one unit overlaps the
-    // others'.  Within a group, thread tt dequantizes row tt / kDeqTpr, part
-    // tt % kDeqTpr of the unit (kDeqWpt packed words -> kDeqWpt 16-byte
-    // chunks of the 128-byte-swizzled bf16 row).
-    // Scales / biases (no upstream dependency) come 8 groups per 16-byte
-    // load when rows are 16-byte aligned (kb % 8 == 0): `cur` holds the
-    // 8-group block of the current unit, `nxt` the following block.
-    const int t = threadIdx.x - kGemmThreads;
-    const int grp = t / (kDeqGroupWarps * 32), tt = t % (kDeqGroupWarps * 32);
-    // one tile row per thread: the TMEM lane this warp may write (lanes
-    // 32 * (warp % 4) ..), which the group's four warps cover once
-    static_assert(kDeqTpr == 1 && kDeqWpt == 8, "q4 dequant: one thread per tile row");
+    // All 8 warps work on one unit at a time: thread = (tile row r, K half
+    // h of the unit), warps 6..9 h = 0, 10..13 h = 1, each warp on the TMEM
+    // lane quarter it may write (lanes 32 * (warp % 4) ..).  A thread turns
+    // its 16 packed words (two groups of 64) into 64 TMEM columns of bf16
+    // pairs.  The packed tile arrives 128-byte swizzled (16-byte chunk c of
+    // row r at chunk c ^ (r % 8)), so a quarter-warp's chunk reads hit 8
+    // different bank groups.
     const int r = 32 * (warp & 3) + lane;
+    const int h = (warp - 6) >> 2;
     const uint32_t t_lane = static_cast<uint32_t>(32 * (warp & 3)) << 16;
-    (void)tt;
-    const bool vec = (p.kb & 7) == 0 &&
-                     ((reinterpret_cast<uintptr_t>(p.q_scales) | reinterpret_cast<uintptr_t>(p.q_biases)) & 15u) == 0;
-    const long long ug = u0 + grp;
-    int tile = static_cast<int>(ug / p.kb), kblk = static_cast<int>(ug % p.kb);
-    int cur_t = -1, cur_k = -1, nxt_t = -1, nxt_k = -1;  // 8-group blocks held in cur / nxt
-    uint4 cur_s = make_uint4(0, 0, 0, 0), cur_b = cur_s, nxt_s = cur_s, nxt_b = cur_s;
-    auto load_block = [&](int tl, int kb0, uint4& vs, uint4& vb) {
-      const int nn = tl * 128 + r;
-      if (nn < p.n_out) {
-        const size_t off = static_cast<size_t>(nn) * p.kb + kb0;
-        vs = __ldg(reinterpret_cast<const uint4*>(p.q_scales + off));
-        vb = __ldg(reinterpret_cast<const uint4*>(p.q_biases + off));
-      } else {
-        vs = make_uint4(0, 0, 0, 0);
-        vb = vs;
+    const int G_row = p.k_groups;  // scale / bias groups per row (K / 64)
+    // scales / biases of this thread's two groups of a unit (no upstream
+    // dependency), loaded two units ahead; groups past K (a ragged last
+    // unit) stay zero: zero weights there, against the zero-filled X columns
+    auto load_sb = [&](int tl, int kb_, __nv_bfloat162& sc2, __nv_bfloat162& bi2) {
+      sc2 = __floats2bfloat162_rn(0.0f, 0.0f);
+      bi2 = sc2;
+      const int n = tl * 128 + r;
+      const int g0 = kb_ * C::kKb + 2 * h;
+      if (n < p.n_out) {
+        const size_t rb = static_cast<size_t>(n) * G_row;
+        if (g0 < G_row) {
+          sc2.x = p.q_scales[rb + g0];
+          bi2.x = p.q_biases[rb + g0];
+        }
+        if (g0 + 1 < G_row) {
+          sc2.y = p.q_scales[rb + g0 + 1];
+          bi2.y = p.q_biases[rb + g0 + 1];
+        }
       }
     };
-    static_assert(!Q4 || S >= D, "q4 needs at least as many stages as dequant buffers");
-    static_assert(!Q4 || D % kDeqGroups == 0, "dequant buffers per group must be whole");
-    static_assert(!Q4 || (C::kUpb % kDeqGroups == 0 && D % C::kUpb == 0 && S >= C::kLookahead + C::kUpb),
-                  "q4 barrier phases: whole units per group, whole phases of buffers, stages ahead of buffers");
-    constexpr int NS = D / C::kUpb;  // deq_full slots
+    // (tile, kblk) of units i, i + 1, i + 2
+    int tile = static_cast<int>(u0 / p.kb), kblk = static_cast<int>(u0 % p.kb);
+    int tile1 = tile, kblk1 = kblk + 1;
+    if (kblk1 == p.kb) {
+      kblk1 = 0;
+      ++tile1;
+    }
+    int tile2 = tile1, kblk2 = kblk1 + 1;
+    if (kblk2 == p.kb) {
+      kblk2 = 0;
+      ++tile2;
+    }
+    __nv_bfloat162 sc_c, bi_c, sc_1, bi_1, sc_2, bi_2;
+    load_sb(tile, kblk, sc_c, bi_c);
+    if (n_units > 1) load_sb(tile1, kblk1, sc_1, bi_1);
     bool ok = true;
-    // every unit of a phase gets one arrival per warp of its group on the
-    // phase's deq_full barrier, also the units past the CTA's last one that
-    // fill its last phase
-    const int n_pairs_units = ((n_units + C::kUpb - 1) / C::kUpb) * C::kUpb;
-    for (int i = grp; i < n_pairs_units && ok; i += kDeqGroups) {
-      if (i >= n_units) {
-        // no load orders this arrival after the slot's previous phase
-        // (phase jp - NS): wait for that phase to complete first
-        const int jp = i / C::kUpb;
-        if (jp >= NS) ok = mbar_wait(&deq_full[jp % NS], static_cast<uint32_t>((jp - NS) / NS) & 1u, 9);
-        ok = __all_sync(0xffffffffu, ok);
-        if (!ok) break;
-      }
-      if (i < n_units) {
-        const int n = tile * 128 + r;
-        __nv_bfloat16 sc = __float2bfloat16_rn(0.0f), bi = sc;
-        if (vec) {
-          const int k8 = kblk & ~7;
-          if (tile != cur_t || k8 != cur_k) {
-            if (tile == nxt_t && k8 == nxt_k) {
-              cur_s = nxt_s;
-              cur_b = nxt_b;
-            } else {
-              load_block(tile, k8, cur_s, cur_b);
-            }
-            cur_t = tile;
-            cur_k = k8;
-            // prefetch the following block if this CTA's range reaches it
-            if (n_units - i > 8 - (kblk & 7)) {
-              nxt_t = k8 + 8 < p.kb ? tile : tile + 1;
-              nxt_k = k8 + 8 < p.kb ? k8 + 8 : 0;
-              load_block(nxt_t, nxt_k, nxt_s, nxt_b);
-            }
-          }
-          const int g = kblk & 7, wi = g >> 1;
-          const uint32_t ws = wi == 0 ? cur_s.x : wi == 1 ? cur_s.y : wi == 2 ? cur_s.z : cur_s.w;
-          const uint32_t wb = wi == 0 ? cur_b.x : wi == 1 ? cur_b.y : wi == 2 ? cur_b.z : cur_b.w;
-          const int sh = (g & 1) * 16;
-          sc = __ushort_as_bfloat16(static_cast<unsigned short>((ws >> sh) & 0xFFFFu));
-          bi = __ushort_as_bfloat16(static_cast<unsigned short>((wb >> sh) & 0xFFFFu));
-        } else if (n < p.n_out) {
-          sc = p.q_scales[static_cast<size_t>(n) * p.kb + kblk];
-          bi = p.q_biases[static_cast<size_t>(n) * p.kb + kblk];
-        }
-        const int s = i % S, d = i % D;
-        ok = mbar_wait(&full_bar[s], static_cast<uint32_t>(i / S) & 1u, 6);
-        // (the producer loaded unit i after the MMA of unit i - D, the last
-        // reader of buffer d, completed)
-        ok = __all_sync(0xffffffffu, ok);  // the TMEM store below is warp-wide
-        if (!ok) break;
-        tc_fence_after();
-        // the row's 64 packed weights -> 32 columns of bf16 pairs (K order) in
-        // the unit's TMEM buffer
-        const uint4* src = reinterpret_cast<const uint4*>(stage_base + s * C::kStageBytes + C::kWOff + r * 32);
-        const uint4 pa = src[0], pb = src[1];
+    for (int i = 0; i < n_units && ok; ++i) {
+      const int s = i % S, d = i % D;
+      if (i + 2 < n_units) load_sb(tile2, kblk2, sc_2, bi_2);
+      const __nv_bfloat162 sc2 = sc_c, bi2 = bi_c;
+      ok = mbar_wait(&full_bar[s], static_cast<uint32_t>(i / S) & 1u, 6);
+      if (ok && i >= D) ok = mbar_wait(&tfree[d], static_cast<uint32_t>(i / D - 1) & 1u, 9);
+      ok = __all_sync(0xffffffffu, ok);  // the TMEM stores below are warp-wide
+      if (!ok) break;
+      tc_fence_after();
+      const uint8_t* rowp = stage_base + s * C::kStageBytes + C::kWOff + r * 128;
+#pragma unroll
+      for (int gq = 0; gq < 2; ++gq) {  // group 2h + gq: 8 words, 32 TMEM columns
+        const uint4 pa = *reinterpret_cast<const uint4*>(rowp + (((4 * h + 2 * gq) ^ (r & 7)) << 4));
+        const uint4 pb = *reinterpret_cast<const uint4*>(rowp + (((4 * h + 2 * gq + 1) ^ (r & 7)) << 4));
+        const __nv_bfloat16 sc = gq ? __high2bfloat16(sc2) : __low2bfloat16(sc2);
+        const __nv_bfloat16 bi = gq ? __high2bfloat16(bi2) : __low2bfloat16(bi2);
         const __nv_bfloat162 s2 = __halves2bfloat162(sc, sc), b2 = __halves2bfloat162(bi, bi);
         const uint32_t pk[8] = {pa.x, pa.y, pa.z, pa.w, pb.x, pb.y, pb.z, pb.w};
         uint32_t v[32];
@@ -478,16 +491,21 @@ __global__ void __launch_bounds__(Q4 ? kGemmThreadsQ4 : kGemmThreads, 1)
           v[4 * j + 2] = q.z;
           v[4 * j + 3] = q.w;
         }
-        tmem_st_x32(tmem_base + t_lane + static_cast<uint32_t>(C::kTmemAcc + d * 32), v);
-        tmem_wait_st();
-        tc_fence_before();
+        tmem_st_x32(tmem_base + t_lane + static_cast<uint32_t>(C::kTmemAcc + d * 32 * C::kKb + h * 64 + gq * 32), v);
       }
+      tmem_wait_st();
+      tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&deq_full[(i / C::kUpb) % NS]);
-      kblk += kDeqGroups;
-      while (kblk >= p.kb) {
-        kblk -= p.kb;
-        ++tile;
+      if (lane == 0) mbar_arrive(&deq_full[d]);
+      sc_c = sc_1;
+      bi_c = bi_1;
+      sc_1 = sc_2;
+      bi_1 = bi_2;
+      tile1 = tile2;
+      kblk1 = kblk2;
+      if (++kblk2 == p.kb) {
+        kblk2 = 0;
+        ++tile2;
       }
     }
   } else {
@@ -498,6 +516,10 @@ __global__ void __launch_bounds__(Q4 ? kGemmThreadsQ4 : kGemmThreads, 1)
     const int q = warp & 3;            // TMEM lane quarter
     const int row = q * 32 + lane;     // row of the 128-row tile
     const int et = threadIdx.x - 64;   // 0..127 epilogue thread id
+    // accumulator columns per group (the q4 kernel's 448 threads leave 128
+    // registers a thread) and contributing CTAs' partial rows in flight
+    constexpr int CW = (TPAD % 32 == 0 && !Q4) ? 32 : 16;
+    constexpr int NV = Q4 ? 1 : 2;
     pdl_wait();
     float* red = reinterpret_cast<float*>(red_raw);                                   // [4][8]
     unsigned long long* s_best = reinterpret_cast<unsigned long long*>(red_raw + 256);  // argmax [TPAD]
@@ -531,15 +553,29 @@ __global__ void __launch_bounds__(Q4 ? kGemmThreadsQ4 : kGemmThreads, 1)
       int c_first = cta, c_last = cta;
       if (!full) {
         // this CTA holds part of the tile's K range: publish the partial
+        // (TPAD < 256: [TPAD][128] fp32, thread = row; 256: [128][TPAD],
+        // each thread its own row, 16-byte stores)
         const int which = (tile == first_tile) ? 0 : 1;
         float* slot = p.ws + (static_cast<size_t>(cta) * 2 + which) * TPAD * 128;
+        if constexpr (TPAD >= 256) {
+          float* srow = slot + static_cast<size_t>(row) * TPAD;
 #pragma unroll 1
-        for (int c0 = 0; c0 < TPAD; c0 += 8) {
-          uint32_t r[8];
-          tmem_ld_x8(taddr + c0, r);
-          tmem_wait_ld();
+          for (int cg = 0; cg < TPAD; cg += CW) {
+            float g[CW];
+            tmem_ld_cols<CW>(taddr + cg, g);
 #pragma unroll
-          for (int j = 0; j < 8; ++j) slot[(c0 + j) * 128 + row] = __uint_as_float(r[j]);
+            for (int j = 0; j < CW; j += 4)
+              *reinterpret_cast<float4*>(srow + cg + j) = make_float4(g[j], g[j + 1], g[j + 2], g[j + 3]);
+          }
+        } else {
+#pragma unroll 1
+          for (int c0 = 0; c0 < TPAD; c0 += 8) {
+            uint32_t r[8];
+            tmem_ld_x8(taddr + c0, r);
+            tmem_wait_ld();
+#pragma unroll
+            for (int j = 0; j < 8; ++j) slot[(c0 + j) * 128 + row] = __uint_as_float(r[j]);
+          }
         }
         __threadfence();
         epi_bar();
@@ -558,187 +594,245 @@ __global__ void __launch_bounds__(Q4 ? kGemmThreadsQ4 : kGemmThreads, 1)
         }
       }
       if (have) {
-        const int mt = tile / p.n_tiles;        // weight tile
-        const int tb = (tile % p.n_tiles) * TPAD;  // first token row of the tile
+        const int mt = tile / NT;         // weight tile
+        const int tb = (tile % NT) * TPAD;  // first token row of the tile
         const int n = mt * 128 + row;
-#pragma unroll 1
-        for (int c0 = 0; c0 < TPAD; c0 += 8) {
-          float a[8];
-          if (full) {
-            uint32_t r[8];
-            tmem_ld_x8(taddr + c0, r);
-            tmem_wait_ld();
+        // the epilogue of accumulator columns c0 .. c0 + 7 (values a)
+        auto body = [&](const int c0, float (&a)[8]) {
+            if constexpr (EPI == kEpiPartial) {
+              if (n < p.n_out) {
+                float* o = p.out_f32 + static_cast<size_t>(cta % p.split) * TPAD * p.ldo + n;
 #pragma unroll
-            for (int j = 0; j < 8; ++j) a[j] = __uint_as_float(r[j]);
-          } else {
-            // sum the partials in CTA order (deterministic), 8 in flight
+                for (int j = 0; j < 8; ++j) o[static_cast<size_t>(c0 + j) * p.ldo] = a[j];
+              }
+            } else if constexpr (EPI == kEpiStore) {
+              if (n < p.n_out) {
 #pragma unroll
-            for (int j = 0; j < 8; ++j) a[j] = 0.0f;
-            for (int c = c_first; c <= c_last; c += 8) {
-              float v[8][8];
-#pragma unroll
-              for (int i = 0; i < 8; ++i) {
-                if (c + i <= c_last) {
-                  const int w2 = (tile == static_cast<int>(sk_u0(c + i, U, G) / p.kb)) ? 0 : 1;
-                  const float* sl = p.ws + (static_cast<size_t>(c + i) * 2 + w2) * TPAD * 128 + c0 * 128 + row;
-#pragma unroll
-                  for (int j = 0; j < 8; ++j) v[i][j] = __ldcg(sl + j * 128);
+                for (int j = 0; j < 8; ++j) {
+                  const int t = tb + c0 + j;
+                  p.out[static_cast<size_t>(t) * p.ldo + n] = __float2bfloat16_rn(t < p.n_rows ? a[j] : 0.0f);
                 }
               }
+            } else if constexpr (EPI == kEpiResidual) {
+              if (n < p.n_out) {
+                __nv_bfloat16 hv[8];
 #pragma unroll
-              for (int i = 0; i < 8; ++i)
-                if (c + i <= c_last) {
-#pragma unroll
-                  for (int j = 0; j < 8; ++j) a[j] += v[i][j];
+                for (int j = 0; j < 8; ++j) {
+                  const int t = tb + c0 + j;
+                  hv[j] = t < p.n_rows ? p.out[static_cast<size_t>(t) * p.ldo + n] : __float2bfloat16_rn(0.0f);
                 }
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                  const int t = tb + c0 + j;
+                  __nv_bfloat16 hn = __float2bfloat16_rn(0.0f);
+                  if (t < p.n_rows) hn = __float2bfloat16_rn(__bfloat162float(hv[j]) + bf16_round(a[j]));
+                  p.out[static_cast<size_t>(t) * p.ldo + n] = hn;
+                  if (p.capture && t < p.n_rows) p.capture[static_cast<size_t>(t) * p.ldc + n] = hn;
+                }
+              }
+            } else if constexpr (EPI == kEpiSwiglu) {
+              if (row >= 64) {
+#pragma unroll
+                for (int j = 0; j < 8; ++j) xch[j * 128 + row] = a[j];
+              }
+              epi_bar();
+              if (row < 64) {
+                const int jf = mt * 64 + row;
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                  const int t = tb + c0 + j;
+                  const float g = bf16_round(a[j]);
+                  const float uu = bf16_round(xch[j * 128 + row + 64]);
+                  const float sg = bf16_round(1.0f / (1.0f + expf(-g)));
+                  const float sl = bf16_round(g * sg);
+                  p.out[static_cast<size_t>(t) * p.ldo + jf] = __float2bfloat16_rn(t < p.n_rows ? sl * uu : 0.0f);
+                }
+              }
+              epi_bar();
+            } else if constexpr (EPI == kEpiQkv) {
+              const int hd = p.head_dim;
+              const int gh = n / hd;  // global head index across q | k | v
+              const int d = n % hd;
+              if (gh >= p.n_q_heads + p.n_kv_heads) {
+                const int kvh = gh - p.n_q_heads - p.n_kv_heads;
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                  const int t = c0 + j;
+                  if (t < p.n_rows) {
+                    const int slot = start + t;
+                    if (slot < p.kv_cap)
+                      p.v_cache[(static_cast<size_t>(kvh) * p.kv_cap + slot) * hd + d] = __float2bfloat16_rn(a[j]);
+                    else
+                      dev_error(0x2001u);
+                  }
+                }
+              } else {
+                // RMSNorm over the head (hd rows = hd/32 warps), then RoPE
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                  a[j] = bf16_round(a[j]);
+                  float v = a[j] * a[j];
+                  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+                  if (lane == 0) red[q * 8 + j] = v;
+                }
+                epi_bar();
+                const int wph = hd / 32;
+                const int w0 = (q / wph) * wph;
+                const float nw = __bfloat162float((gh < p.n_q_heads ? p.q_norm : p.k_norm)[d]);
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                  float ss = 0.0f;
+                  for (int w = w0; w < w0 + wph; ++w) ss += red[w * 8 + j];
+                  const float rms = rsqrtf(ss / static_cast<float>(hd) + p.eps);
+                  a[j] = bf16_round(a[j] * rms * nw);
+                  xch[j * 128 + row] = a[j];
+                }
+                epi_bar();
+                const int half = hd / 2;
+                const int i_f = d % half;
+                const float inv_freq =
+                    exp2f(-(2.0f * static_cast<float>(i_f) / static_cast<float>(hd)) * p.rope_log2_theta);
+                const int partner = (d < half) ? row + half : row - half;
+                const bool is_q = gh < p.n_q_heads;
+                const int kvh = gh - p.n_q_heads;
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                  const int t = c0 + j;
+                  float outv = 0.0f;
+                  if (t < p.n_rows) {
+                    float sn, cs;
+                    sincosf(s_pos[t] * inv_freq, &sn, &cs);
+                    const float y = a[j], yp = xch[j * 128 + partner];
+                    outv = (d < half) ? (y * cs - yp * sn) : (y * cs + yp * sn);
+                  }
+                  if (is_q) {
+                    p.q_out[static_cast<size_t>(t) * p.ldq + gh * hd + d] = __float2bfloat16_rn(outv);
+                  } else if (t < p.n_rows) {
+                    const int slot = start + t;
+                    if (slot < p.kv_cap)
+                      p.k_cache[(static_cast<size_t>(kvh) * p.kv_cap + slot) * hd + d] = __float2bfloat16_rn(outv);
+                    else
+                      dev_error(0x2001u);
+                  }
+                }
+                epi_bar();
+              }
+            } else if constexpr (EPI == kEpiArgmax) {
+              // per tree row: max over this tile's 128 vocab rows (ties -> smallest id)
+              const bool valid = n < p.vocab;
+              unsigned long long* rk = reinterpret_cast<unsigned long long*>(red_raw + 256 + TPAD * 8);  // [4][8]
+#pragma unroll
+              for (int j = 0; j < 8; ++j) {
+                unsigned long long key = 0ull;
+                if (valid) {
+                  float v = bf16_round(a[j]);
+                  if (p.inv_temp > 0.0f)
+                    v = v * p.inv_temp + gumbel_noise(p.sample_seed, kSampleTagVerify, sample_step,
+                                                      static_cast<uint32_t>(c0 + j), static_cast<uint32_t>(n));
+                  key = (static_cast<unsigned long long>(float_order_key(v)) << 32) |
+                        static_cast<unsigned long long>(0xFFFFFFFFu - static_cast<uint32_t>(n));
+                }
+                for (int o = 16; o > 0; o >>= 1) {
+                  const unsigned long long ok2 = __shfl_xor_sync(0xffffffffu, key, o);
+                  key = ok2 > key ? ok2 : key;
+                }
+                if (lane == 0) rk[q * 8 + j] = key;
+              }
+              epi_bar();
+              if (et < 8) {
+                unsigned long long bk = s_best[c0 + et];
+                for (int w = 0; w < 4; ++w) bk = rk[w * 8 + et] > bk ? rk[w * 8 + et] : bk;
+                s_best[c0 + et] = bk;
+              }
+              epi_bar();
+            }
+        };
+        if constexpr (TPAD >= 256) {
+          // column groups of CW: one TMEM load, or one round of 16-byte
+          // partial loads per NV contributing CTAs, per group; the body then
+          // runs on 8 columns at a time (rolled, the group shifted down)
+#pragma unroll 1
+          for (int cg = 0; cg < TPAD; cg += CW) {
+            float g[CW];
+            if (full) {
+              tmem_ld_cols<CW>(taddr + cg, g);
+            } else {
+              // sum the partials in CTA order (deterministic)
+#pragma unroll
+              for (int j = 0; j < CW; ++j) g[j] = 0.0f;
+              for (int c = c_first; c <= c_last; c += NV) {
+                float4 v[NV][CW / 4];
+#pragma unroll
+                for (int i = 0; i < NV; ++i) {
+                  if (c + i <= c_last) {
+                    const int w2 = (tile == static_cast<int>(sk_u0(c + i, U, G) / p.kb)) ? 0 : 1;
+                    const float4* sl = reinterpret_cast<const float4*>(
+                        p.ws + (static_cast<size_t>(c + i) * 2 + w2) * TPAD * 128 + static_cast<size_t>(row) * TPAD +
+                        cg);
+#pragma unroll
+                    for (int j = 0; j < CW / 4; ++j) v[i][j] = __ldcg(sl + j);
+                  }
+                }
+#pragma unroll
+                for (int i = 0; i < NV; ++i)
+                  if (c + i <= c_last) {
+#pragma unroll
+                    for (int j = 0; j < CW / 4; ++j) {
+                      g[4 * j] += v[i][j].x;
+                      g[4 * j + 1] += v[i][j].y;
+                      g[4 * j + 2] += v[i][j].z;
+                      g[4 * j + 3] += v[i][j].w;
+                    }
+                  }
+              }
+            }
+#pragma unroll 1
+            for (int sub = 0; sub < CW / 8; ++sub) {
+              float a[8];
+#pragma unroll
+              for (int j = 0; j < 8; ++j) a[j] = g[j];
+#pragma unroll
+              for (int j = 0; j < CW - 8; ++j) g[j] = g[j + 8];
+              body(cg + sub * 8, a);
             }
           }
-          if constexpr (EPI == kEpiPartial) {
-            if (n < p.n_out) {
-              float* o = p.out_f32 + static_cast<size_t>(cta % p.split) * TPAD * p.ldo + n;
+        } else {
+          // Processes the 128 x TPAD accumulator in chunks of 8 tree rows
+          // (TMEM columns) in a rolled loop: the code stays small and hot in
+          // the instruction cache although it runs only once or twice per tile.
+#pragma unroll 1
+          for (int c0 = 0; c0 < TPAD; c0 += 8) {
+            float a[8];
+            if (full) {
+              uint32_t r[8];
+              tmem_ld_x8(taddr + c0, r);
+              tmem_wait_ld();
 #pragma unroll
-              for (int j = 0; j < 8; ++j) o[static_cast<size_t>(c0 + j) * p.ldo] = a[j];
-            }
-          } else if constexpr (EPI == kEpiStore) {
-            if (n < p.n_out) {
-#pragma unroll
-              for (int j = 0; j < 8; ++j) {
-                const int t = tb + c0 + j;
-                p.out[static_cast<size_t>(t) * p.ldo + n] = __float2bfloat16_rn(t < p.n_rows ? a[j] : 0.0f);
-              }
-            }
-          } else if constexpr (EPI == kEpiResidual) {
-            if (n < p.n_out) {
-              __nv_bfloat16 hv[8];
-#pragma unroll
-              for (int j = 0; j < 8; ++j) {
-                const int t = tb + c0 + j;
-                hv[j] = t < p.n_rows ? p.out[static_cast<size_t>(t) * p.ldo + n] : __float2bfloat16_rn(0.0f);
-              }
-#pragma unroll
-              for (int j = 0; j < 8; ++j) {
-                const int t = tb + c0 + j;
-                __nv_bfloat16 hn = __float2bfloat16_rn(0.0f);
-                if (t < p.n_rows) hn = __float2bfloat16_rn(__bfloat162float(hv[j]) + bf16_round(a[j]));
-                p.out[static_cast<size_t>(t) * p.ldo + n] = hn;
-                if (p.capture && t < p.n_rows) p.capture[static_cast<size_t>(t) * p.ldc + n] = hn;
-              }
-            }
-          } else if constexpr (EPI == kEpiSwiglu) {
-            if (row >= 64) {
-#pragma unroll
-              for (int j = 0; j < 8; ++j) xch[j * 128 + row] = a[j];
-            }
-            epi_bar();
-            if (row < 64) {
-              const int jf = mt * 64 + row;
-#pragma unroll
-              for (int j = 0; j < 8; ++j) {
-                const int t = tb + c0 + j;
-                const float g = bf16_round(a[j]);
-                const float uu = bf16_round(xch[j * 128 + row + 64]);
-                const float sg = bf16_round(1.0f / (1.0f + expf(-g)));
-                const float sl = bf16_round(g * sg);
-                p.out[static_cast<size_t>(t) * p.ldo + jf] = __float2bfloat16_rn(t < p.n_rows ? sl * uu : 0.0f);
-              }
-            }
-            epi_bar();
-          } else if constexpr (EPI == kEpiQkv) {
-            const int hd = p.head_dim;
-            const int gh = n / hd;  // global head index across q | k | v
-            const int d = n % hd;
-            if (gh >= p.n_q_heads + p.n_kv_heads) {
-              const int kvh = gh - p.n_q_heads - p.n_kv_heads;
-#pragma unroll
-              for (int j = 0; j < 8; ++j) {
-                const int t = c0 + j;
-                if (t < p.n_rows) {
-                  const int slot = start + t;
-                  if (slot < p.kv_cap)
-                    p.v_cache[(static_cast<size_t>(kvh) * p.kv_cap + slot) * hd + d] = __float2bfloat16_rn(a[j]);
-                  else
-                    dev_error(0x2001u);
-                }
-              }
+              for (int j = 0; j < 8; ++j) a[j] = __uint_as_float(r[j]);
             } else {
-              // RMSNorm over the head (hd rows = hd/32 warps), then RoPE
+              // sum the partials in CTA order (deterministic), 8 in flight
 #pragma unroll
-              for (int j = 0; j < 8; ++j) {
-                a[j] = bf16_round(a[j]);
-                float v = a[j] * a[j];
-                for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-                if (lane == 0) red[q * 8 + j] = v;
-              }
-              epi_bar();
-              const int wph = hd / 32;
-              const int w0 = (q / wph) * wph;
-              const float nw = __bfloat162float((gh < p.n_q_heads ? p.q_norm : p.k_norm)[d]);
+              for (int j = 0; j < 8; ++j) a[j] = 0.0f;
+              for (int c = c_first; c <= c_last; c += 8) {
+                float v[8][8];
 #pragma unroll
-              for (int j = 0; j < 8; ++j) {
-                float ss = 0.0f;
-                for (int w = w0; w < w0 + wph; ++w) ss += red[w * 8 + j];
-                const float rms = rsqrtf(ss / static_cast<float>(hd) + p.eps);
-                a[j] = bf16_round(a[j] * rms * nw);
-                xch[j * 128 + row] = a[j];
-              }
-              epi_bar();
-              const int half = hd / 2;
-              const int i_f = d % half;
-              const float inv_freq =
-                  exp2f(-(2.0f * static_cast<float>(i_f) / static_cast<float>(hd)) * p.rope_log2_theta);
-              const int partner = (d < half) ? row + half : row - half;
-              const bool is_q = gh < p.n_q_heads;
-              const int kvh = gh - p.n_q_heads;
+                for (int i = 0; i < 8; ++i) {
+                  if (c + i <= c_last) {
+                    const int w2 = (tile == static_cast<int>(sk_u0(c + i, U, G) / p.kb)) ? 0 : 1;
+                    const float* sl = p.ws + (static_cast<size_t>(c + i) * 2 + w2) * TPAD * 128 + c0 * 128 + row;
 #pragma unroll
-              for (int j = 0; j < 8; ++j) {
-                const int t = c0 + j;
-                float outv = 0.0f;
-                if (t < p.n_rows) {
-                  float sn, cs;
-                  sincosf(s_pos[t] * inv_freq, &sn, &cs);
-                  const float y = a[j], yp = xch[j * 128 + partner];
-                  outv = (d < half) ? (y * cs - yp * sn) : (y * cs + yp * sn);
+                    for (int j = 0; j < 8; ++j) v[i][j] = __ldcg(sl + j * 128);
+                  }
                 }
-                if (is_q) {
-                  p.q_out[static_cast<size_t>(t) * p.ldq + gh * hd + d] = __float2bfloat16_rn(outv);
-                } else if (t < p.n_rows) {
-                  const int slot = start + t;
-                  if (slot < p.kv_cap)
-                    p.k_cache[(static_cast<size_t>(kvh) * p.kv_cap + slot) * hd + d] = __float2bfloat16_rn(outv);
-                  else
-                    dev_error(0x2001u);
-                }
-              }
-              epi_bar();
-            }
-          } else if constexpr (EPI == kEpiArgmax) {
-            // per tree row: max over this tile's 128 vocab rows (ties -> smallest id)
-            const bool valid = n < p.vocab;
-            unsigned long long* rk = reinterpret_cast<unsigned long long*>(red_raw + 256 + TPAD * 8);  // [4][8]
 #pragma unroll
-            for (int j = 0; j < 8; ++j) {
-              unsigned long long key = 0ull;
-              if (valid) {
-                float v = bf16_round(a[j]);
-                if (p.inv_temp > 0.0f)
-                  v = v * p.inv_temp + gumbel_noise(p.sample_seed, kSampleTagVerify, sample_step,
-                                                    static_cast<uint32_t>(c0 + j), static_cast<uint32_t>(n));
-                key = (static_cast<unsigned long long>(float_order_key(v)) << 32) |
-                      static_cast<unsigned long long>(0xFFFFFFFFu - static_cast<uint32_t>(n));
+                for (int i = 0; i < 8; ++i)
+                  if (c + i <= c_last) {
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) a[j] += v[i][j];
+                  }
               }
-              for (int o = 16; o > 0; o >>= 1) {
-                const unsigned long long ok2 = __shfl_xor_sync(0xffffffffu, key, o);
-                key = ok2 > key ? ok2 : key;
-              }
-              if (lane == 0) rk[q * 8 + j] = key;
             }
-            epi_bar();
-            if (et < 8) {
-              unsigned long long bk = s_best[c0 + et];
-              for (int w = 0; w < 4; ++w) bk = rk[w * 8 + et] > bk ? rk[w * 8 + et] : bk;
-              s_best[c0 + et] = bk;
-            }
-            epi_bar();
+            body(c0, a);
           }
         }
       }

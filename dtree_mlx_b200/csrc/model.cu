@@ -656,7 +656,7 @@ extern "C" int dtree_qwen3_prefill(dtree_qwen3_model* m, const int32_t* tokens, 
       f.k_cache = kc;
       f.v_cache = vc;
       f.kv_cap = d.kv_capacity;
-      if ((rc = qkv_finish_launch(f, n_rows, st))) return rc;
+      if ((rc = qkv_rows_launch(f, n_rows, st))) return rc;
     }
     {  // causal attention, 128-row chunks
       AttnParams a{};

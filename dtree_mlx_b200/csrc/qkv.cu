@@ -1,6 +1,5 @@
 // Finish of the fused q|k|v projection (qwen3_tree.py:50-65): sums the
-// split-K fp32 partials of the QKV GEMM in split order (or reads the bf16
-// projection of a dense prompt GEMM, the same bf16 value), then per head
+// split-K fp32 partials of the QKV GEMM in split order, then per head
 //   q, k: RMSNorm over head_dim (q_norm / k_norm), half-split RoPE at the
 //         node's position, q -> q buffer, k -> K cache slot start + t
 //   v:    -> V cache slot start + t
@@ -12,6 +11,8 @@
 // rotates only the first rot_dims features (partial_rotary_factor), pairs
 // (i, i + rot_dims/2) with inv_freq_i = theta^(-2i/rot_dims) (mlx RoPE with
 // dims = rot_dims, traditional = False); the rest pass through.
+#include <algorithm>
+
 #include "qkv.cuh"
 
 namespace dtree {
@@ -29,7 +30,6 @@ __global__ void __launch_bounds__(256) qkv_finish_kernel(QkvFinishParams p) {
   const int col = gh < p.n_q_heads ? gh * qcols + d : p.n_q_heads * qcols + (gh - p.n_q_heads) * hd + d;
   const size_t stride = static_cast<size_t>(p.part_rows) * p.width;
   auto sum_splits = [&](int c) {
-    if (p.dense) return __bfloat162float(p.dense[static_cast<size_t>(t) * p.width + c]);
     // up to 16 splits' loads in flight at once (one round trip), summed in
     // split order
     const float* src = p.partials + static_cast<size_t>(t) * p.width + c;
@@ -101,10 +101,138 @@ __global__ void __launch_bounds__(256) qkv_finish_kernel(QkvFinishParams p) {
   }
 }
 
+// Prompt rows (dense bf16 projection [rows][width], slot = start + t): one
+// warp per (row, head), EPL = head_dim / 32 consecutive features per lane,
+// 16-byte or 8-byte loads; the head's sum of squares and the RoPE partner
+// (feature i <-> i + rot/2, lane l <-> l ^ (rot/2 / EPL)) move by shuffles,
+// so there is no shared memory and no block barrier.  Same arithmetic and
+// rounding points as qkv_finish_kernel.
+template <int EPL>
+__global__ void __launch_bounds__(256) qkv_rows_kernel(QkvFinishParams p) {
+  pdl_trigger();
+  const int lane = threadIdx.x & 31;
+  const int heads = p.n_q_heads + 2 * p.n_kv_heads;
+  const long long tasks = static_cast<long long>(p.n_rows) * heads;
+  const int hd = EPL * 32;
+  const int qcols = p.gated ? 2 * hd : hd;
+  const int rd = p.rot_dims > 0 ? p.rot_dims : hd;
+  const int half = rd / 2;
+  const int pmask = half / EPL;  // partner lane offset (a power of two)
+  pdl_wait();
+  const int start = p.state->start;
+  for (long long task = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5; task < tasks;
+       task += (static_cast<long long>(gridDim.x) * blockDim.x) >> 5) {
+    const int t = static_cast<int>(task / heads), gh = static_cast<int>(task % heads);
+    const int d0 = lane * EPL;
+    const int col = gh < p.n_q_heads ? gh * qcols + d0 : p.n_q_heads * qcols + (gh - p.n_q_heads) * hd + d0;
+    const __nv_bfloat16* src = p.dense + static_cast<size_t>(t) * p.width + col;
+    __nv_bfloat16 xv[EPL];
+    if constexpr (EPL == 8) {
+      *reinterpret_cast<uint4*>(xv) = *reinterpret_cast<const uint4*>(src);
+    } else if constexpr (EPL == 4) {
+      *reinterpret_cast<uint2*>(xv) = *reinterpret_cast<const uint2*>(src);
+    } else {
+      *reinterpret_cast<uint32_t*>(xv) = *reinterpret_cast<const uint32_t*>(src);
+    }
+    const int slot = start + t;
+    if (gh >= p.n_q_heads + p.n_kv_heads) {  // v
+      const int kvh = gh - p.n_q_heads - p.n_kv_heads;
+      if (slot >= 0 && slot < p.kv_cap) {
+        __nv_bfloat16* dst = p.v_cache + (static_cast<size_t>(kvh) * p.kv_cap + slot) * hd + d0;
+#pragma unroll
+        for (int i = 0; i < EPL; ++i) dst[i] = xv[i];
+      } else if (lane == 0) {
+        dev_error(0x2001u);
+      }
+      continue;
+    }
+    if (p.gated && gh < p.n_q_heads) {
+      const __nv_bfloat16* gsrc = src + hd;
+      __nv_bfloat16* gdst = p.gate_out + static_cast<size_t>(t) * (p.n_q_heads * hd) + gh * hd + d0;
+#pragma unroll
+      for (int i = 0; i < EPL; ++i) gdst[i] = gsrc[i];
+    }
+    float x[EPL];
+    float sq = 0.0f;
+#pragma unroll
+    for (int i = 0; i < EPL; ++i) {
+      x[i] = __bfloat162float(xv[i]);
+      sq = fmaf(x[i], x[i], sq);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
+    const bool is_q = gh < p.n_q_heads;
+    const __nv_bfloat16* nwp = (is_q ? p.q_norm : p.k_norm) + d0;
+    const float rs = rsqrtf(sq / static_cast<float>(hd) + p.eps);
+    float y[EPL], yp[EPL];
+#pragma unroll
+    for (int i = 0; i < EPL; ++i) y[i] = bf16_round(x[i] * rs * __bfloat162float(nwp[i]));
+#pragma unroll
+    for (int i = 0; i < EPL; ++i) yp[i] = __shfl_xor_sync(0xffffffffu, y[i], pmask);
+    const float pos_t = static_cast<float>(p.positions[t]);
+    __nv_bfloat16 ov[EPL];
+#pragma unroll
+    for (int i = 0; i < EPL; ++i) {
+      const int d = d0 + i;
+      float outv = y[i];
+      if (d < rd) {
+        const int i_f = d % half;
+        const float inv_freq = exp2f(-(2.0f * static_cast<float>(i_f) / static_cast<float>(rd)) * p.rope_log2_theta);
+        float sn, cs;
+        sincosf(pos_t * inv_freq, &sn, &cs);
+        outv = (d < half) ? (y[i] * cs - yp[i] * sn) : (y[i] * cs + yp[i] * sn);
+      }
+      ov[i] = __float2bfloat16_rn(outv);
+    }
+    __nv_bfloat16* dst;
+    if (is_q) {
+      dst = p.q_out + static_cast<size_t>(t) * (p.n_q_heads * hd) + gh * hd + d0;
+    } else {
+      if (slot < 0 || slot >= p.kv_cap) {
+        if (lane == 0) dev_error(0x2001u);
+        continue;
+      }
+      dst = p.k_cache + (static_cast<size_t>(gh - p.n_q_heads) * p.kv_cap + slot) * hd + d0;
+    }
+    if constexpr (EPL == 8) {
+      *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(ov);
+    } else if constexpr (EPL == 4) {
+      *reinterpret_cast<uint2*>(dst) = *reinterpret_cast<const uint2*>(ov);
+    } else {
+      *reinterpret_cast<uint32_t*>(dst) = *reinterpret_cast<const uint32_t*>(ov);
+    }
+  }
+}
+
+int qkv_rows_launch(const QkvFinishParams& p, int n_rows, cudaStream_t stream) {
+  DTREE_CHECK_ARG(p.dense && p.positions && p.state && p.q_out && p.k_cache && p.v_cache, "prompt QKV: null pointer");
+  DTREE_CHECK_ARG(p.slot_mode == 0 && p.n_q_heads > 0, "prompt QKV: rows at start + t only");
+  DTREE_CHECK_ARG(!p.gated || p.gate_out, "gated projection needs gate_out");
+  const int hd = p.head_dim;
+  const int rd = p.rot_dims > 0 ? p.rot_dims : hd;
+  const int epl = hd / 32;
+  DTREE_CHECK_ARG(hd == 64 || hd == 128 || hd == 256, "prompt QKV: head_dim 64, 128 or 256");
+  DTREE_CHECK_ARG(rd % 2 == 0 && (rd / 2) % epl == 0 && (((rd / 2) / epl) & ((rd / 2) / epl - 1)) == 0 &&
+                      (rd / 2) / epl < 32,
+                  "prompt QKV: rot_dims / 2 must be a power-of-two multiple of head_dim / 32");
+  DTREE_CHECK_ARG(p.width % 8 == 0, "prompt QKV: width must be a multiple of 8");
+  QkvFinishParams q = p;
+  q.n_rows = n_rows;
+  const long long tasks = static_cast<long long>(n_rows) * (p.n_q_heads + 2 * p.n_kv_heads);
+  const int grid = static_cast<int>(std::min<long long>((tasks + 7) / 8, 16ll * num_sms()));
+  switch (epl) {
+    case 2: DTREE_CUDA_RET(launch_pdl(qkv_rows_kernel<2>, dim3(grid), dim3(256), 0, stream, q)); break;
+    case 4: DTREE_CUDA_RET(launch_pdl(qkv_rows_kernel<4>, dim3(grid), dim3(256), 0, stream, q)); break;
+    default: DTREE_CUDA_RET(launch_pdl(qkv_rows_kernel<8>, dim3(grid), dim3(256), 0, stream, q)); break;
+  }
+  return kOk;
+}
+
 int qkv_finish_launch(const QkvFinishParams& p, int n_rows, cudaStream_t stream) {
   DTREE_CHECK_ARG(p.head_dim % 32 == 0 && p.head_dim <= 256, "head_dim must be a multiple of 32, <= 256");
   DTREE_CHECK_ARG(p.rot_dims >= 0 && p.rot_dims <= p.head_dim && p.rot_dims % 2 == 0, "bad rot_dims");
   DTREE_CHECK_ARG(!p.gated || p.gate_out, "gated projection needs gate_out");
+  DTREE_CHECK_ARG(p.partials && !p.dense, "qkv_finish sums split partials (prompt rows: qkv_rows_launch)");
   DTREE_CUDA_RET(launch_pdl(qkv_finish_kernel, dim3(n_rows, p.n_q_heads + 2 * p.n_kv_heads), dim3(p.head_dim), 0,
                             stream, p));
   return kOk;

@@ -10,6 +10,7 @@ struct QkvFinishParams {
   const float* partials;  // [split][part_rows][width]
   int split, part_rows, width;
   const __nv_bfloat16* dense;  // non-null: the projection as bf16 [rows][width] instead of partials
+  int n_rows;                  // rows (set by qkv_finish_launch)
   int head_dim, n_q_heads, n_kv_heads;
   const __nv_bfloat16* q_norm;
   const __nv_bfloat16* k_norm;
@@ -44,5 +45,7 @@ __device__ __forceinline__ int ring_slot(int r, int sink, int window) {
 }
 
 int qkv_finish_launch(const QkvFinishParams& p, int n_rows, cudaStream_t stream);
+// prompt rows: dense bf16 projection in, slots start + t (slot_mode 0)
+int qkv_rows_launch(const QkvFinishParams& p, int n_rows, cudaStream_t stream);
 
 }  // namespace dtree

@@ -578,7 +578,7 @@ extern "C" int dtree_qwen35_prefill(dtree_qwen35_model* m, const int32_t* tokens
       f.gated = 1;
       f.gate_out = gate;
       f.rot_dims = rot;
-      if ((rc = qkv_finish_launch(f, n_rows, st))) return rc;
+      if ((rc = qkv_rows_launch(f, n_rows, st))) return rc;
       for (int c = 0; c < Lo.chunks; ++c) {  // causal attention, one 128-row chunk per launch
         const int t = std::min(128, n_rows - c * 128);
         const size_t off = static_cast<size_t>(c) * 128 * x.q_dim;

@@ -146,23 +146,51 @@ def prefill_flops(cfg, n: int) -> float:
     return float(L * (2.0 * n * proj + attn) + 2.0 * H * cfg.vocab_size)
 
 
+def hybrid_prefill_flops(cfg, n: int) -> float:
+    """Algorithmic FLOPs of the hybrid's prompt forward of n rows from slot
+    0: projections (2 n K N), the gated attention layers' causal attention,
+    the DeltaNet recurrence (4 Hv Dv Dk per row) and the last row's LM head."""
+    H = cfg.hidden_size
+    kd, vd = cfg.linear_num_key_heads * cfg.linear_key_head_dim, cfg.linear_num_value_heads * cfg.linear_value_head_dim
+    proj_w = 2 * kd + vd + vd + 2 * cfg.linear_num_value_heads
+    qd = cfg.num_attention_heads * cfg.head_dim
+    kvd = cfg.num_key_value_heads * cfg.head_dim
+    mlp = 3 * H * cfg.intermediate_size
+    lin = 2.0 * n * (H * proj_w + vd * H + mlp) + 4.0 * n * cfg.linear_num_value_heads * cfg.linear_value_head_dim * \
+        cfg.linear_key_head_dim
+    att = 2.0 * n * (H * (2 * qd + 2 * kvd) + qd * H + mlp) + 4.0 * cfg.num_attention_heads * cfg.head_dim * n * (n + 1) / 2
+    return float(cfg.n_linear * lin + cfg.n_attn * att + 2.0 * H * cfg.vocab_size)
+
+
 def run_prefill(preset: str, layers: int | None, n: int, iters: int, quant_bits: int = 16, seed: int = 0) -> dict:
-    """Dense prefill of n prompt rows (dtree_qwen3_prefill) against the
-    verify-path prefill it replaces (128-row forwards)."""
+    """Dense prefill of n prompt rows (dtree_qwen3_prefill /
+    dtree_qwen35_prefill) against the verify-path prefill it replaces
+    (128-row forwards)."""
     from .engine import chain_anc_masks
 
-    cfg = PRESETS[preset]
+    hybrid = preset.startswith("qwen35")
+    cfg = (QWEN35_PRESETS if hybrid else PRESETS)[preset]
     if layers:
         cfg = replace(cfg, num_hidden_layers=layers)
-    w = random_qwen3_weights(cfg, seed=seed, device="cuda")
-    if quant_bits == 4:
-        w = quantize_weights(w)
-    eng = Qwen3Engine(w, kv_capacity=n + 128, layer_ids=[1])
+    if hybrid:
+        from .engine35 import Qwen35Engine
+
+        eng = Qwen35Engine(random_qwen35_weights(cfg, seed=seed, device="cuda"), kv_capacity=n + 128, layer_ids=[1])
+    else:
+        w = random_qwen3_weights(cfg, seed=seed, device="cuda")
+        if quant_bits == 4:
+            w = quantize_weights(w)
+        eng = Qwen3Engine(w, kv_capacity=n + 128, layer_ids=[1])
     toks = torch.randint(0, cfg.vocab_size, (n,), dtype=torch.int32, device="cuda")
     state = kernels.new_state("cuda", start=0)
     hid = torch.zeros(n, cfg.hidden_size, dtype=torch.bfloat16, device="cuda")
     nxt = torch.zeros(1, dtype=torch.int32, device="cuda")
-    ms_dense = _time(lambda: eng.prefill_dense(toks, state, hid, nxt), iters, True)
+    def dense():
+        if hybrid:
+            eng.reset_states()
+        eng.prefill_dense(toks, state, hid, nxt)
+
+    ms_dense = _time(dense, iters, True)
     post = torch.zeros(128, dtype=torch.int32, device="cuda")
     st2 = kernels.new_state("cuda", start=0)
     chunks = []
@@ -172,13 +200,15 @@ def run_prefill(preset: str, layers: int | None, n: int, iters: int, quant_bits:
                        torch.from_numpy(chain_anc_masks(t).view(np.int64)).to("cuda")))
 
     def chained():
+        if hybrid:
+            eng.reset_states()
         for s, t, pos, anc in chunks:
             st2[0] = s
             eng.prefill_chunk(toks[s:s + t], pos, anc, t, st2, post)
 
     ms_chain = _time(chained, max(1, iters // 2), True)
     eng.close()
-    flops = prefill_flops(cfg, n)
+    flops = hybrid_prefill_flops(cfg, n) if hybrid else prefill_flops(cfg, n)
     peak, src = measured_tflops()
     tf = flops / (ms_dense * 1e-3) / 1e12
     return {"prefill_rows": n, "layers": cfg.num_hidden_layers, "quant_bits": quant_bits,

@@ -29,7 +29,8 @@ DEV = "cuda"
 
 
 def _rel(a, b):
-    a, b = a.float().cpu().double(), b.float().cpu().double()
+    a = a.float().cpu().double() if torch.is_tensor(a) else torch.as_tensor(np.asarray(a)).double()
+    b = b.float().cpu().double() if torch.is_tensor(b) else torch.as_tensor(np.asarray(b)).double()
     return float((a - b).norm() / max(float(b.norm()), 1e-30))
 
 

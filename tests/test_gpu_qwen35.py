@@ -10,12 +10,12 @@ Two oracles run side by side on the same bf16 weights and the same trees:
 The two oracles differ from each other by max |d logits| ~ 0.065 (mean
 ~ 0.009, logit std 0.46) on this model: that is bf16 rounding noise, not a
 semantic difference, and it bounds how close any bf16 implementation can
-get.  Tolerances, with S = the measured oracle-to-oracle spread of the same
-step (max and mean |d logits|):
-  vs bf16 oracle  logits max <= 1.5 S_max, mean <= 1.5 S_mean; hidden / states rel <= 3e-2
-  vs fp32 oracle  logits max <= 2 S_max,   mean <= 2 S_mean;   hidden / states rel <= 4e-2
+get.  Fixed tolerances (1.5x / 2x that measured spread, frozen as numbers;
+the spread itself is printed, not used):
+  vs bf16 oracle  logits max <= 0.10, mean <= 0.014; hidden / states rel <= 3e-2
+  vs fp32 oracle  logits max <= 0.13, mean <= 0.018; hidden / states rel <= 4e-2
 Posterior tokens must equal the bf16 oracle's argmax except at near-ties
-(top-2 gap below S_max), which are counted.
+(top-2 gap below 0.10), which are counted.
 """
 from __future__ import annotations
 
@@ -29,7 +29,9 @@ from oracle.runtime import near_tie
 
 pytestmark = pytest.mark.gpu
 DEV = "cuda"
-SPREAD = {"bf16": 1.5, "fp32": 2.0}   # logit tolerance in units of the oracle-to-oracle spread
+LOGIT_MAX = {"bf16": 0.10, "fp32": 0.13}
+LOGIT_MEAN = {"bf16": 0.014, "fp32": 0.018}
+NEAR_TIE = 0.10
 REL = {"bf16": 3e-2, "fp32": 4e-2}
 
 
@@ -110,13 +112,12 @@ def test_prefill_tree_commit_match_oracle(hybrid):
             err = (g_log - logs[name]).abs()
             rel = _rel(eng.norm_out[:T], outs[name])
             print(f"step {step} vs {name}: norm_out rel {rel:.2e} logits max {err.max():.3e} mean {err.mean():.3e}")
-            k = SPREAD[name]
-            assert rel < REL[name] and err.max() <= k * s_max and err.mean() <= k * s_mean, (step, name)
+            assert rel < REL[name] and err.max() <= LOGIT_MAX[name] and err.mean() <= LOGIT_MEAN[name], (step, name)
         near = 0
         for t in range(T):
             ref = int(torch.argmax(logs["bf16"][t]))
             if gpost[t] != ref:
-                assert near_tie(logs["bf16"][t], gpost[t], ref, s_max), (step, t)
+                assert near_tie(logs["bf16"][t], gpost[t], ref, NEAR_TIE), (step, t)
                 near += 1
         print(f"step {step}: near-tie posterior mismatches {near}/{T}")
         accepted, nxt = OT.follow_verified_tree(child_maps, gpost)
