@@ -199,7 +199,7 @@ def run_ours(args, rank, world, local, dist) -> dict | None:
     def one_generation():
         session.reset(PROMPT_LEN, first)
         for _ in range(n_steps):
-            session.graph.replay()
+            session.replay()
 
     for _ in range(args.warmup):
         one_generation()
@@ -319,6 +319,7 @@ def run_ours(args, rank, world, local, dist) -> dict | None:
             "mean_accepted_per_step": round(agg["mean_accepted"], 3),
             "mean_accepted_per_step_rank0": round(sum(accept) / n_steps, 3),
             "tree_rows": n_nodes,
+            **({"qwen35_tree_mode": "full_tree"} if PRESET.startswith("qwen35") else {}),
             "fixed_point_iterations": fixed_iters,
             "continuation_converged": bool(converged),
             "l2": f"inputs larger than L2 ({target.model.weights.streamed_bytes() / 1e9:.1f} GB of weights "
@@ -471,6 +472,10 @@ def main():
         global PRESET, PROMPT_LEN, KV_CAP
         PRESET, PROMPT_LEN, KV_CAP = "qwen35-9b", 2048, 2048 + 512 + 160
         args.no_cpu = True
+        # the timed loop is the device-resident full-tree step (per-node
+        # recurrent-state propagation, accepted-path commit) replayed as one
+        # CUDA graph per step, not the reference's host-driven lazy walk
+        os.environ["DTREE_QWEN35_TREE_MODE"] = "full_tree"
     # stdout carries the one JSON line only: everything else written to it
     # (libraries' banners such as NCCL's version line included) goes to stderr
     sys.stdout.flush()

@@ -215,7 +215,7 @@ class Qwen3TargetAdapter(TargetAdapter):
         post = torch.zeros(128, dtype=torch.int32, device=dev)
         norm_rows, cap_rows = [], []
         s = 0
-        if anc_rows is None and positions is None and n > eng.t_cap:
+        if anc_rows is None and positions is None and n > eng.t_cap and n >= eng.dense_prefill_min_rows:
             # a causal sequence longer than one verify forward: dense prefill
             width = eng.cfg.hidden_size * max(1, len(eng.layer_ids))
             norm = torch.zeros(n, eng.cfg.hidden_size, dtype=torch.bfloat16, device=dev)
@@ -359,7 +359,7 @@ class Qwen35TargetAdapter(Qwen3TargetAdapter):
             cache.offset += n
             norm = eng.norm_out[:n].clone()[None]
             hid = eng.capture[:n].clone()[None]
-        elif n > eng.t_cap:  # a long causal sequence: dense prefill, states advance to its end
+        elif n > eng.t_cap and n >= eng.dense_prefill_min_rows:  # a long causal sequence: dense prefill
             width = eng.cfg.hidden_size * max(1, len(eng.layer_ids))
             norm = torch.zeros(n, eng.cfg.hidden_size, dtype=torch.bfloat16, device=dev)
             hid = torch.zeros(n, width, dtype=torch.bfloat16, device=dev)

@@ -55,19 +55,23 @@ int make_tmap_2d_bf16(CUtensorMap* map, const void* base, uint64_t inner, uint64
 }
 
 int make_tmap_2d_u32(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer, uint64_t row_stride_bytes,
-                     uint32_t box_inner, uint32_t box_outer, bool swizzle128) {
+                     uint32_t box_inner, uint32_t box_outer, int swizzle_bytes) {
   EncodeTiledFn fn = encode_fn();
   if (!fn) return fail(kErrCuda, "cuTensorMapEncodeTiled unavailable");
   if ((reinterpret_cast<uintptr_t>(base) & 15u) != 0) return fail(kErrInvalidArg, "TMA base not 16-byte aligned");
   if (row_stride_bytes % 16 != 0) return fail(kErrInvalidArg, "TMA row stride not a multiple of 16 bytes");
   if ((box_inner * 4) % 16 != 0) return fail(kErrInvalidArg, "TMA box inner extent not a multiple of 16 bytes");
-  if (swizzle128 && box_inner * 4 != 128) return fail(kErrInvalidArg, "128-byte swizzle needs a 128-byte box row");
+  if (swizzle_bytes != 0 && swizzle_bytes != 64 && swizzle_bytes != 128) return fail(kErrInvalidArg, "bad TMA swizzle");
+  if (swizzle_bytes && box_inner * 4 != static_cast<uint32_t>(swizzle_bytes))
+    return fail(kErrInvalidArg, "a swizzled u32 box row must span the swizzle width");
   cuuint64_t dims[2] = {inner, outer};
   cuuint64_t strides[1] = {row_stride_bytes};
   cuuint32_t box[2] = {box_inner, box_outer};
   cuuint32_t estr[2] = {1, 1};
   CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT32, 2, const_cast<void*>(base), dims, strides, box, estr,
-                  CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  swizzle_bytes == 128 ? CU_TENSOR_MAP_SWIZZLE_128B
+                                       : (swizzle_bytes == 64 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_NONE),
                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(kErrCuda, "cuTensorMapEncodeTiled failed: " + std::to_string(static_cast<int>(r)));

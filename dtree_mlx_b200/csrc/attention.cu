@@ -400,16 +400,19 @@ __global__ void __launch_bounds__(kTcThreads) tree_attn_tc_kernel(const __grid_c
   float* red_max = reinterpret_cast<float*>(sm + C::kRed);  // [2][128]
   float* red_sum = red_max + 2 * 128;                       // [2][128]
 
-  const int split = blockIdx.x, kvh = blockIdx.z;
   const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
   const int r = (warp & 3) * 32 + lane;  // softmax / output row (TMEM lane)
   const int h = warp >> 2;               // key half (S) and column half (O)
   const int G = p.n_q_heads / p.n_kv_heads;
-  // prompt mode: blockIdx.y = chunk * chunk_rbs + row block; the chunk's
-  // rows are queries row0 .. row0 + T - 1 at slots start + row0 ..
+  // prompt mode: blockIdx.x = kv head * chunk_rbs + row block, blockIdx.y
+  // counts chunks from the last (chunk c takes c + 1 passes, so the longest
+  // CTAs launch first); the chunk's rows are queries row0 .. row0 + T - 1
+  // at slots start + row0 ..
   constexpr bool chunked = PROMPT;
-  const int chunk = chunked ? static_cast<int>(blockIdx.y) / p.chunk_rbs : 0;
-  const int rb = chunked ? static_cast<int>(blockIdx.y) % p.chunk_rbs : static_cast<int>(blockIdx.y);
+  const int split = chunked ? 0 : static_cast<int>(blockIdx.x);
+  const int kvh = chunked ? static_cast<int>(blockIdx.x) / p.chunk_rbs : static_cast<int>(blockIdx.z);
+  const int chunk = chunked ? static_cast<int>(gridDim.y - 1 - blockIdx.y) : 0;
+  const int rb = chunked ? static_cast<int>(blockIdx.x) % p.chunk_rbs : static_cast<int>(blockIdx.y);
   const int row0 = chunk * p.chunk_rows;
   const int T = chunked ? min(p.chunk_rows, p.n_nodes - row0) : p.n_nodes;
   const int rows_kv = G * T;
@@ -844,7 +847,7 @@ int attn_prefill_launch(const AttnParams& p0, int head_dim, cudaStream_t stream)
   const int G = p.n_q_heads / p.n_kv_heads;
   p.chunk_rbs = (G * p.chunk_rows + 127) / 128;
   const int chunks = (p.n_nodes + p.chunk_rows - 1) / p.chunk_rows;
-  DTREE_CHECK_ARG(static_cast<long long>(chunks) * p.chunk_rbs < 65536, "prompt too long for one launch");
+  DTREE_CHECK_ARG(chunks < 65536, "prompt too long for one launch");
   p.splits = 1;
   p.key_align = kTcKeys;
   p.part_o = nullptr;
@@ -854,7 +857,7 @@ int attn_prefill_launch(const AttnParams& p0, int head_dim, cudaStream_t stream)
   int rc = plane_tmap(&tk, p.k, rows, head_dim);
   if (rc) return rc;
   if ((rc = plane_tmap(&tv, p.v, rows, head_dim))) return rc;
-  const dim3 grid(1, chunks * p.chunk_rbs, p.n_kv_heads);
+  const dim3 grid(p.n_kv_heads * p.chunk_rbs, chunks, 1);
   if (head_dim == 128) {
     DTREE_CUDA_RET(ensure_smem_attr(tree_attn_tc_kernel<128, true>, TcCfg<128>::kSmem));
     DTREE_CUDA_RET(launch_pdl(tree_attn_tc_kernel<128, true>, grid, dim3(kTcThreads),

@@ -365,9 +365,10 @@ cudaError_t ensure_smem_attr(K kernel, int bytes) {
 // cuTensorMapEncodeTiled via the runtime's driver entry point (no -lcuda)
 int make_tmap_2d_bf16(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer, uint64_t row_stride_bytes,
                       uint32_t box_inner, uint32_t box_outer, bool swizzle128);
-// uint32 elements (packed 4-bit weight tiles); swizzle128 needs 128-byte box rows
+// uint32 elements (packed 4-bit weight tiles); swizzle_bytes 0, 64 or 128
+// (a swizzled box row spans exactly the swizzle width)
 int make_tmap_2d_u32(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer, uint64_t row_stride_bytes,
-                     uint32_t box_inner, uint32_t box_outer, bool swizzle128);
+                     uint32_t box_inner, uint32_t box_outer, int swizzle_bytes);
 
 int num_sms();
 

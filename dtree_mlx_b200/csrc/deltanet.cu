@@ -117,6 +117,75 @@ __global__ void tree_conv1d_kernel(ConvParams p) {
   if (ok) st_f(static_cast<InT*>(p.out) + static_cast<size_t>(t) * p.ldo + c, y);
 }
 
+// Prompt rows as one chain (row t's predecessors t-1, t-2, .. then the base
+// window: position j < 0 is base row keep + j): block = kConvSeqRows rows x
+// one channel block (one head with head normalization); each thread slides
+// its channel's window through the rows in registers, one load per row.
+// Same arithmetic, order and rounding as tree_conv1d_kernel.
+constexpr int kConvSeqRows = 16;
+
+// KEEP > 0: the window length at compile time (registers); 0: keep
+template <typename InT, int KEEP>
+__global__ void conv1d_seq_kernel(ConvParams p) {
+  const int keep = KEEP > 0 ? KEEP : p.keep;
+  pdl_trigger();
+  __shared__ float s_red[32];
+  const int t0 = blockIdx.x * kConvSeqRows;
+  const int c = blockIdx.y * blockDim.x + threadIdx.x;
+  const int head = blockIdx.y;
+  const bool ok = c < p.conv_dim;
+  const InT* x = static_cast<const InT*>(p.x);
+  const InT* base = static_cast<const InT*>(p.base);
+  const InT* w = static_cast<const InT*>(p.weight);
+  float wk[kMaxKeep + 1];
+#pragma unroll
+  for (int k = 0; k <= keep; ++k) wk[k] = ok ? ld_f(w + static_cast<size_t>(k) * p.conv_dim + c) : 0.0f;
+  pdl_wait();
+  // win[k] = the input at position t - keep + k, k < keep
+  float win[kMaxKeep];
+#pragma unroll
+  for (int k = 0; k < keep; ++k) {
+    const int j = t0 - keep + k;
+    win[k] = !ok ? 0.0f
+                 : (j >= 0 ? ld_f(x + static_cast<size_t>(j) * p.ldx + c)
+                           : ld_f(base + static_cast<size_t>(keep + j) * p.conv_dim + c));
+  }
+  const int t1 = min(t0 + kConvSeqRows, p.n_nodes);
+  // the block's rows of this channel, all loads in flight at once
+  float xs[kConvSeqRows];
+#pragma unroll
+  for (int i = 0; i < kConvSeqRows; ++i)
+    xs[i] = (ok && t0 + i < t1) ? ld_f(x + static_cast<size_t>(t0 + i) * p.ldx + c) : 0.0f;
+#pragma unroll
+  for (int i = 0; i < kConvSeqRows; ++i) {
+    const int t = t0 + i;
+    if (t >= t1) break;  // (uniform per block)
+    const float xt = xs[i];
+    float acc = 0.0f;
+#pragma unroll
+    for (int k = 0; k < keep; ++k) acc = fmaf(win[k], wk[k], acc);
+    acc = fmaf(xt, wk[keep], acc);
+#pragma unroll
+    for (int k = 0; k + 1 < keep; ++k) win[k] = win[k + 1];
+    win[keep - 1] = xt;
+    float y = round_to<InT>(acc / (1.0f + expf(-acc)));
+    if (head < p.n_norm_heads) {
+      const int D = blockDim.x;
+      float ss = y * y;
+      for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+      if ((threadIdx.x & 31) == 0) s_red[threadIdx.x >> 5] = ss;
+      __syncthreads();
+      float tot = 0.0f;
+      for (int i = 0; i < (D + 31) / 32; ++i) tot += s_red[i];
+      __syncthreads();  // s_red is rewritten by the next row
+      const float r = round_to<InT>(y * rsqrtf(tot / static_cast<float>(D) + 1e-6f));
+      const float scale = head < p.n_q_heads ? 1.0f / static_cast<float>(D) : rsqrtf(static_cast<float>(D));
+      y = round_to<InT>(r * scale);
+    }
+    if (ok) st_f(static_cast<InT*>(p.out) + static_cast<size_t>(t) * p.ldo + c, y);
+  }
+}
+
 // ------------------------------------------------------------ gated delta
 
 
@@ -135,27 +204,33 @@ __device__ __forceinline__ void node_gates(const DeltaParams& p, int t, int hv, 
   }
 }
 
-// One node of the recurrence on a state row held as NP floats per lane.
+// One node of the recurrence on a state row held as NP floats per lane:
+//   S' = S g;  kv = S' k;  delta = (v - kv) beta;  S'' = S' + k delta;
+//   y = S'' q = g (S q) + delta (k q)
+// The three reductions (S k, S q, k q) of the incoming state run side by
+// side, one butterfly deep instead of two after each other.  The tree
+// kernel and the commit replay share this step, so a replayed node state
+// equals the tree kernel's bit for bit.
 template <typename InT, int NP>
 __device__ __forceinline__ float delta_step(float (&s)[NP], const float (&kk)[NP], const float (&qq)[NP], float v,
                                             float g, float beta, bool rnd = true) {
-  float kv = 0.0f;
+  float sk = 0.0f, sq = 0.0f, kq = 0.0f;
 #pragma unroll
   for (int i = 0; i < NP; ++i) {
-    s[i] = s[i] * g;
-    kv = fmaf(s[i], kk[i], kv);
+    sk = fmaf(s[i], kk[i], sk);
+    sq = fmaf(s[i], qq[i], sq);
+    kq = fmaf(kk[i], qq[i], kq);
   }
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) kv += __shfl_xor_sync(0xffffffffu, kv, o);
-  const float delta = (v - kv) * beta;
-  float out = 0.0f;
-#pragma unroll
-  for (int i = 0; i < NP; ++i) {
-    s[i] = fmaf(kk[i], delta, s[i]);
-    out = fmaf(s[i], qq[i], out);
+  for (int o = 16; o > 0; o >>= 1) {
+    sk += __shfl_xor_sync(0xffffffffu, sk, o);
+    sq += __shfl_xor_sync(0xffffffffu, sq, o);
+    kq += __shfl_xor_sync(0xffffffffu, kq, o);
   }
+  const float delta = (v - g * sk) * beta;
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) out += __shfl_xor_sync(0xffffffffu, out, o);
+  for (int i = 0; i < NP; ++i) s[i] = fmaf(kk[i], delta, s[i] * g);
+  const float out = fmaf(g, sq, delta * kq);
   if (rnd) {
 #pragma unroll
     for (int i = 0; i < NP; ++i) s[i] = round_to<InT>(s[i]);
@@ -165,8 +240,9 @@ __device__ __forceinline__ float delta_step(float (&s)[NP], const float (&kk)[NP
 
 // grid (Hv * Dv / rows_per_cta), block rows_per_cta warps.  Lane l of a warp
 // holds state elements l*NP .. l*NP+NP-1 of its row (the reference's
-// n_per_t split).  Shared memory: q/k of the head for every node (f32),
-// v / g / beta per node and row, and the rounded node states (InT).
+// n_per_t split).  Shared memory: q/k of the head for every node (InT, as
+// they arrive), v / g / beta per node and row, and the rounded node states
+// (InT); 16 rows per CTA keep the verify's CTAs within one wave.
 template <typename InT, typename StT, int DK>
 __global__ void tree_gated_delta_kernel(DeltaParams p) {
   constexpr int NP = DK / 32;
@@ -174,9 +250,9 @@ __global__ void tree_gated_delta_kernel(DeltaParams p) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
   const int T = p.n_nodes;
   const int R = p.rows_per_cta;
-  float* s_q = reinterpret_cast<float*>(smem_raw);           // [T][DK]
-  float* s_k = s_q + T * DK;                                  // [T][DK]
-  float* s_g = s_k + T * DK;                                  // [T]
+  InT* s_q = reinterpret_cast<InT*>(smem_raw);               // [T][DK]
+  InT* s_k = s_q + T * DK;                                    // [T][DK]
+  float* s_g = reinterpret_cast<float*>(s_k + T * DK);        // [T]
   float* s_b = s_g + T;                                       // [T]
   float* s_v = s_b + T;                                       // [T][R]
   InT* s_state = reinterpret_cast<InT*>(s_v + T * R);         // [R][T][DK]
@@ -194,8 +270,8 @@ __global__ void tree_gated_delta_kernel(DeltaParams p) {
   const InT* v = static_cast<const InT*>(p.v);
   for (int e = threadIdx.x; e < T * DK; e += blockDim.x) {
     const int t = e / DK, d = e % DK;
-    s_q[e] = ld_f(q + static_cast<size_t>(t) * p.ldqk + hk * DK + d);
-    s_k[e] = ld_f(k + static_cast<size_t>(t) * p.ldqk + hk * DK + d);
+    s_q[e] = q[static_cast<size_t>(t) * p.ldqk + hk * DK + d];
+    s_k[e] = k[static_cast<size_t>(t) * p.ldqk + hk * DK + d];
   }
   for (int t = threadIdx.x; t < T; t += blockDim.x) {
     float g, beta;
@@ -234,8 +310,8 @@ __global__ void tree_gated_delta_kernel(DeltaParams p) {
     float kk[NP], qq[NP];
 #pragma unroll
     for (int i = 0; i < NP; ++i) {
-      kk[i] = s_k[t * DK + lane * NP + i];
-      qq[i] = s_q[t * DK + lane * NP + i];
+      kk[i] = ld_f(s_k + t * DK + lane * NP + i);
+      qq[i] = ld_f(s_q + t * DK + lane * NP + i);
     }
     const float out = delta_step<InT, NP>(s, kk, qq, s_v[t * R + warp], s_g[t], s_b[t], !p.no_round);
     if (lane == 0) st_f(y + static_cast<size_t>(t) * p.ldy + hv * p.dv + dv, out);
@@ -258,74 +334,127 @@ __global__ void tree_gated_delta_kernel(DeltaParams p) {
 // Prompt (sequence) recurrence: rows 0..n_nodes-1 form one chain from
 // state_in, the state stays in f32 registers from the first row to the last
 // (mlx-lm's sequence kernel; no per-row rounding) and is written to
-// final_state.  One warp per state row (hv, dv), Dk/32 elements per lane,
-// every warp independent (no shared memory, no block barrier); each row's
-// q / k / v / a / b are loaded kPf rows ahead into registers.  Per row
+// final_state.  CTA = kSeqWarps warps = that many consecutive state rows of
+// one value head (they share the head's q / k); one warp per state row,
+// Dk/32 elements per lane.  The rows' inputs arrive in blocks of kSeqRows in
+// shared memory by cp.async, double buffered (block b + 2 is fetched while
+// block b + 1 lands and block b is computed): per row the head's q and k
+// (Dk bf16 each), the CTA's kSeqWarps v values and the a / b gate inputs.
+// Per row
 //   S' = S g;  kv = S' k;  delta = (v - kv) beta;  S'' = S' + k delta;
 //   y = S'' q = g (S q) + delta (k q)
-// so the two reductions of a row (S k and S q of the incoming state, plus
-// the state-free k q) run side by side instead of one after the other.
-constexpr int kSeqPf = 4;
+// so the three reductions (S k, S q, k q) run side by side.
+constexpr int kSeqWarps = 8;
+constexpr int kSeqRows = 32;
 
-template <typename InT, typename StT, int DK>
-__global__ void __launch_bounds__(256) gated_delta_seq_kernel(DeltaParams p) {
+__device__ __forceinline__ void seq_cp16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void seq_cp4(void* dst, const void* src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+
+template <int DK>
+struct SeqBuf {
+  __nv_bfloat16 q[kSeqRows][DK];
+  __nv_bfloat16 k[kSeqRows][DK];
+  __nv_bfloat16 v[kSeqRows][kSeqWarps];
+  uint32_t a[kSeqRows];  // the bf16 pair holding this head's a (hv & ~1, hv | 1)
+  uint32_t b[kSeqRows];
+  float g[kSeqRows];     // the rows' gates, computed once per CTA from a / b
+  float beta[kSeqRows];
+};
+
+template <int DK>
+__global__ void __launch_bounds__(kSeqWarps * 32) gated_delta_seq_kernel(DeltaParams p) {
   constexpr int NP = DK / 32;
+  static_assert(NP == 2 || NP == 4, "sequence gated delta: head_k_dim 64 or 128");
   pdl_trigger();
-  const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  const int lane = threadIdx.x & 31;
-  const bool live = row < p.n_v_heads * p.dv;
-  const int hv = live ? row / p.dv : 0, dv = live ? row % p.dv : 0;
+  __shared__ __align__(16) SeqBuf<DK> buf[2];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int rows_per_head = p.dv / kSeqWarps;
+  const int hv = blockIdx.x / rows_per_head;
+  const int dv0 = (blockIdx.x % rows_per_head) * kSeqWarps;
+  const int dv = dv0 + warp;
   const int hk = hv / (p.n_v_heads / p.n_k_heads);
-  pdl_wait();
-  if (!live) return;  // (whole warps)
-  const InT* q = static_cast<const InT*>(p.q) + hk * DK + lane * NP;
-  const InT* k = static_cast<const InT*>(p.k) + hk * DK + lane * NP;
-  const InT* v = static_cast<const InT*>(p.v) + hv * p.dv + dv;
-  const InT* a = static_cast<const InT*>(p.a) + hv;
-  const InT* b = static_cast<const InT*>(p.b) + hv;
-  const float dt_b = ld_f(static_cast<const InT*>(p.dt_bias) + hv);
+  const int T = p.n_nodes;
+  const __nv_bfloat16* q = static_cast<const __nv_bfloat16*>(p.q) + hk * DK;
+  const __nv_bfloat16* k = static_cast<const __nv_bfloat16*>(p.k) + hk * DK;
+  const __nv_bfloat16* v = static_cast<const __nv_bfloat16*>(p.v) + hv * p.dv + dv0;
+  const __nv_bfloat16* a = static_cast<const __nv_bfloat16*>(p.a) + (hv & ~1);
+  const __nv_bfloat16* b = static_cast<const __nv_bfloat16*>(p.b) + (hv & ~1);
+  const float dt_b = __bfloat162float(static_cast<const __nv_bfloat16*>(p.dt_bias)[hv]);
   const float ea = expf(p.a_log[hv]);
-  const StT* st_in = static_cast<const StT*>(p.state_in) + (static_cast<size_t>(hv) * p.dv + dv) * DK + lane * NP;
+  pdl_wait();
+  // copies of row block blk into buffer blk % 2: q / k rows 16 bytes a
+  // thread-chunk, then v (16 bytes) and the a / b pairs (4 bytes) per row
+  auto issue = [&](int blk) {
+    SeqBuf<DK>& B = buf[blk & 1];
+    const int r0 = blk * kSeqRows;
+    constexpr int CPR = DK * 2 / 16;  // 16-byte chunks per q (or k) row
+    for (int c = threadIdx.x; c < kSeqRows * CPR * 2; c += blockDim.x) {
+      const int which = c / (kSeqRows * CPR), rem = c % (kSeqRows * CPR);
+      const int r = rem / CPR, ch = rem % CPR;
+      if (r0 + r < T) {
+        const __nv_bfloat16* src = (which ? k : q) + static_cast<size_t>(r0 + r) * p.ldqk + ch * 8;
+        seq_cp16((which ? &B.k[r][0] : &B.q[r][0]) + ch * 8, src);
+      }
+    }
+    for (int r = threadIdx.x; r < kSeqRows; r += blockDim.x) {
+      if (r0 + r < T) {
+        seq_cp16(&B.v[r][0], v + static_cast<size_t>(r0 + r) * p.ldv);
+        seq_cp4(&B.a[r], a + static_cast<size_t>(r0 + r) * p.ldab);
+        seq_cp4(&B.b[r], b + static_cast<size_t>(r0 + r) * p.ldab);
+      }
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  };
+  const float* st_in = static_cast<const float*>(p.state_in) + (static_cast<size_t>(hv) * p.dv + dv) * DK + lane * NP;
   float s[NP];
 #pragma unroll
-  for (int i = 0; i < NP; ++i) s[i] = ld_f(st_in + i);
-  InT* y = static_cast<InT*>(p.y) + hv * p.dv + dv;
-  const int T = p.n_nodes;
-  // register ring of the next kPf rows' inputs
-  InT rq[kSeqPf][NP], rk[kSeqPf][NP];
-  float rv[kSeqPf], ra[kSeqPf], rb[kSeqPf];
-  auto fetch = [&](int j, int t) {
-    if (t < T) {
-#pragma unroll
-      for (int i = 0; i < NP; ++i) {
-        rq[j][i] = q[static_cast<size_t>(t) * p.ldqk + i];
-        rk[j][i] = k[static_cast<size_t>(t) * p.ldqk + i];
-      }
-      rv[j] = ld_f(v + static_cast<size_t>(t) * p.ldv);
-      ra[j] = ld_f(a + static_cast<size_t>(t) * p.ldab);
-      rb[j] = ld_f(b + static_cast<size_t>(t) * p.ldab);
+  for (int i = 0; i < NP; ++i) s[i] = st_in[i];
+  __nv_bfloat16* y = static_cast<__nv_bfloat16*>(p.y) + hv * p.dv + dv;
+  const int nblk = (T + kSeqRows - 1) / kSeqRows;
+  issue(0);
+  if (nblk > 1) issue(1);
+  else asm volatile("cp.async.commit_group;" ::: "memory");
+  const bool hi = (hv & 1) != 0;
+  for (int blk = 0; blk < nblk; ++blk) {
+    asm volatile("cp.async.wait_group 1;" ::: "memory");  // block blk landed (this thread's copies)
+    __syncthreads();                                       // ... and everyone's
+    SeqBuf<DK>& B = buf[blk & 1];
+    const int rn = min(kSeqRows, T - blk * kSeqRows);
+    // the rows' gates, once per CTA (node_gates with a, b):
+    // g = exp(-exp(A_log) softplus(a + dt_bias)), beta = sigmoid(b)
+    if (threadIdx.x < rn) {
+      const int r = threadIdx.x;
+      const __nv_bfloat162 a2 = *reinterpret_cast<const __nv_bfloat162*>(&B.a[r]);
+      const __nv_bfloat162 b2 = *reinterpret_cast<const __nv_bfloat162*>(&B.b[r]);
+      const float x = round_to<__nv_bfloat16>(__bfloat162float(hi ? a2.y : a2.x) + dt_b);
+      const float sp = round_to<__nv_bfloat16>(x > 20.0f ? x : log1pf(expf(x)));
+      B.g[r] = expf(-ea * sp);
+      B.beta[r] = round_to<__nv_bfloat16>(1.0f / (1.0f + expf(-__bfloat162float(hi ? b2.y : b2.x))));
     }
-  };
-#pragma unroll
-  for (int j = 0; j < kSeqPf; ++j) fetch(j, j);
-  for (int t0 = 0; t0 < T; t0 += kSeqPf) {
-#pragma unroll
-    for (int j = 0; j < kSeqPf; ++j) {
-      const int t = t0 + j;
-      if (t >= T) break;
+    __syncthreads();
+    for (int r = 0; r < rn; ++r) {
       float kk[NP], qq[NP];
-#pragma unroll
-      for (int i = 0; i < NP; ++i) {
-        kk[i] = ld_f(&rk[j][i]);
-        qq[i] = ld_f(&rq[j][i]);
+      if constexpr (NP == 4) {
+        const uint2 kw = *reinterpret_cast<const uint2*>(&B.k[r][lane * 4]);
+        const uint2 qw = *reinterpret_cast<const uint2*>(&B.q[r][lane * 4]);
+        const float2 k0 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&kw.x));
+        const float2 k1 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&kw.y));
+        const float2 q0 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&qw.x));
+        const float2 q1 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&qw.y));
+        kk[0] = k0.x; kk[1] = k0.y; kk[2] = k1.x; kk[3] = k1.y;
+        qq[0] = q0.x; qq[1] = q0.y; qq[2] = q1.x; qq[3] = q1.y;
+      } else {
+        const float2 k0 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&B.k[r][lane * 2]));
+        const float2 q0 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&B.q[r][lane * 2]));
+        kk[0] = k0.x; kk[1] = k0.y;
+        qq[0] = q0.x; qq[1] = q0.y;
       }
-      const float vv = rv[j];
-      // gates (node_gates with a, b): g = exp(-exp(A_log) softplus(a + dt_bias)), beta = sigmoid(b)
-      const float x = round_to<InT>(ra[j] + dt_b);
-      const float sp = round_to<InT>(x > 20.0f ? x : log1pf(expf(x)));
-      const float g = expf(-ea * sp);
-      const float beta = round_to<InT>(1.0f / (1.0f + expf(-rb[j])));
-      fetch(j, t + kSeqPf);
+      const float vv = __bfloat162float(B.v[r][warp]);
+      const float g = B.g[r], beta = B.beta[r];
       float sk = 0.0f, sq = 0.0f, kq = 0.0f;
 #pragma unroll
       for (int i = 0; i < NP; ++i) {
@@ -342,12 +471,16 @@ __global__ void __launch_bounds__(256) gated_delta_seq_kernel(DeltaParams p) {
       const float delta = (vv - g * sk) * beta;
 #pragma unroll
       for (int i = 0; i < NP; ++i) s[i] = fmaf(kk[i], delta, s[i] * g);
-      if (lane == 0) st_f(y + static_cast<size_t>(t) * p.ldy, fmaf(g, sq, delta * kq));
+      if (lane == 0) y[static_cast<size_t>(blk * kSeqRows + r) * p.ldy] = __float2bfloat16_rn(fmaf(g, sq, delta * kq));
     }
+    __syncthreads();  // buffer blk % 2 is refilled next
+    if (blk + 2 < nblk) issue(blk + 2);
+    else asm volatile("cp.async.commit_group;" ::: "memory");
   }
-  StT* fs = static_cast<StT*>(p.final_state) + (static_cast<size_t>(hv) * p.dv + dv) * DK + lane * NP;
+  asm volatile("cp.async.wait_group 0;" ::: "memory");
+  float* fs = static_cast<float*>(p.final_state) + (static_cast<size_t>(hv) * p.dv + dv) * DK + lane * NP;
 #pragma unroll
-  for (int i = 0; i < NP; ++i) st_f(fs + i, s[i]);
+  for (int i = 0; i < NP; ++i) fs[i] = s[i];
 }
 
 // Commit: advance each layer's recurrent state along the accepted path with
@@ -455,7 +588,17 @@ __global__ void rmsnorm_gated_kernel(const InT* __restrict__ y, int ldy, const I
 
 // ------------------------------------------------------------ launchers
 static size_t delta_smem(int T, int R, int dk, int in_bytes) {
-  return static_cast<size_t>(2 * T * dk + 2 * T + T * R) * 4 + static_cast<size_t>(R) * T * dk * in_bytes;
+  const size_t qk = (static_cast<size_t>(2) * T * dk * in_bytes + 15) & ~static_cast<size_t>(15);
+  return qk + static_cast<size_t>(2 * T + T * R) * 4 + static_cast<size_t>(R) * T * dk * in_bytes;
+}
+
+int conv1d_seq_launch(const ConvParams& p, int block, cudaStream_t st) {
+  DTREE_CHECK_ARG(p.keep >= 1 && p.keep <= kMaxKeep && p.n_nodes > 0, "sequence conv: bad shape");
+  DTREE_CHECK_ARG(p.n_norm_heads == 0 || block % 32 == 0, "sequence conv: head blocks of whole warps");
+  dim3 grid((p.n_nodes + kConvSeqRows - 1) / kConvSeqRows, (p.conv_dim + block - 1) / block);
+  if (p.keep == 3) DTREE_CUDA_RET(launch_pdl(conv1d_seq_kernel<__nv_bfloat16, 3>, grid, dim3(block), 0, st, p));
+  else DTREE_CUDA_RET(launch_pdl(conv1d_seq_kernel<__nv_bfloat16, 0>, grid, dim3(block), 0, st, p));
+  return kOk;
 }
 
 int tree_conv1d_launch(const ConvParams& p, int dtype, int block, cudaStream_t st) {
@@ -468,7 +611,7 @@ int tree_conv1d_launch(const ConvParams& p, int dtype, int block, cudaStream_t s
 template <typename InT, typename StT>
 static int delta_launch_t(DeltaParams p, int dk, cudaStream_t st) {
   const int in_bytes = static_cast<int>(sizeof(InT));
-  int R = 8;
+  int R = 16;
   while (R > 1 && (p.dv % R != 0 || delta_smem(p.n_nodes, R, dk, in_bytes) > 200 * 1024)) R >>= 1;
   DTREE_CHECK_ARG(delta_smem(p.n_nodes, R, dk, in_bytes) <= 200 * 1024, "gated delta: tree too large for shared memory");
   p.rows_per_cta = R;
@@ -491,13 +634,16 @@ static int delta_launch_t(DeltaParams p, int dk, cudaStream_t st) {
 int gated_delta_seq_launch(const DeltaParams& p, int dk, cudaStream_t st) {
   DTREE_CHECK_ARG(p.q && p.k && p.v && p.a && p.b && p.a_log && p.dt_bias && p.state_in && p.final_state && p.y,
                   "sequence gated delta: null pointer (gates come from a / b)");
-  DTREE_CHECK_ARG(p.n_nodes > 0 && p.n_v_heads % p.n_k_heads == 0, "bad sequence gated delta shape");
-  const int rows = p.n_v_heads * p.dv;
-  const dim3 grid((rows + 7) / 8), block(256);
-  using B = __nv_bfloat16;
+  DTREE_CHECK_ARG(p.n_nodes > 0 && p.n_v_heads % p.n_k_heads == 0 && p.dv % kSeqWarps == 0,
+                  "sequence gated delta: bad shape (head_v_dim a multiple of 8)");
+  auto al = [](const void* x, uintptr_t m) { return (reinterpret_cast<uintptr_t>(x) & (m - 1)) == 0; };
+  DTREE_CHECK_ARG(al(p.q, 16) && al(p.k, 16) && al(p.v, 16) && p.ldqk % 8 == 0 && p.ldv % 8 == 0,
+                  "sequence gated delta: q / k / v rows must be 16-byte aligned");
+  DTREE_CHECK_ARG(al(p.a, 4) && al(p.b, 4) && p.ldab % 2 == 0, "sequence gated delta: a / b must be 4-byte aligned");
+  const dim3 grid(p.n_v_heads * p.dv / kSeqWarps), block(kSeqWarps * 32);
   switch (dk) {
-    case 64: DTREE_CUDA_RET(launch_pdl(gated_delta_seq_kernel<B, float, 64>, grid, block, 0, st, p)); return kOk;
-    case 128: DTREE_CUDA_RET(launch_pdl(gated_delta_seq_kernel<B, float, 128>, grid, block, 0, st, p)); return kOk;
+    case 64: DTREE_CUDA_RET(launch_pdl(gated_delta_seq_kernel<64>, grid, block, 0, st, p)); return kOk;
+    case 128: DTREE_CUDA_RET(launch_pdl(gated_delta_seq_kernel<128>, grid, block, 0, st, p)); return kOk;
   }
   return fail(kErrInvalidArg, "sequence gated delta: head_k_dim must be 64 or 128");
 }

@@ -63,6 +63,8 @@ struct DeltaParams {
 };
 
 int tree_conv1d_launch(const ConvParams& p, int dtype, int block, cudaStream_t st);
+// prompt rows as one chain from the base window (parents unused), bf16
+int conv1d_seq_launch(const ConvParams& p, int block, cudaStream_t st);
 int tree_gated_delta_launch(const DeltaParams& p, int dk, int dtype, int state_dtype, cudaStream_t st);
 // prompt rows as one chain, bf16 inputs, f32 state (state_in -> final_state;
 // gates from a / b); any n_nodes

@@ -74,9 +74,9 @@ static GemmWs ws_split(void* base) {
 static bool valid_tpad(int t) { return t == 16 || t == 32 || t == 64 || t == 80 || t == 128; }
 
 // activation map, split / grid choice and parameters shared by both weight formats
-// `wide` kernels (the q4 variant: 448 threads, ~146 KB shared memory) fit
-// one CTA per SM, so a grid above the SM count would run a second wave.
-// `kunit` = K elements per stream-K unit (64 bf16, 256 for 4-bit weights).
+// `wide` kernels (one CTA per SM) would run a second wave above the SM
+// count; both weight formats now fit two CTAs per SM.
+// `kunit` = K elements per stream-K unit (64 bf16, 128 for 4-bit weights).
 static int plan_common(GemmPlan* plan, int n_out, int k, const void* x, int t_pad, int x_row_stride_elems, int epi,
                        int grid, bool wide, int kunit) {
   DTREE_CHECK_ARG(valid_tpad(t_pad), "t_pad must be 16, 32, 64, 80 or 128");
@@ -131,12 +131,12 @@ int gemm_plan_q4(GemmPlan* plan, const void* w_packed, const void* scales, const
   DTREE_CHECK_ARG(w_packed && scales && biases, "null q4 weight pointer");
   DTREE_CHECK_ARG(epi == kEpiStore || epi == kEpiPartial || epi == kEpiSwiglu,
                   "q4 GEMM supports the store, split-K partial and SwiGLU epilogues");
-  int rc = plan_common(plan, n_out, k, x, t_pad, x_row_stride_elems, epi, grid, true, 64 * kQ4Kb);
+  int rc = plan_common(plan, n_out, k, x, t_pad, x_row_stride_elems, epi, grid, false, 64 * kQ4Kb);
   if (rc) return rc;
-  // packed weight map: box 8 * kQ4Kb words (one stream-K unit of K, 128 B)
-  // x 128 rows, 128-byte swizzled
+  // packed weight map: box 8 * kQ4Kb words (one stream-K unit of K, 64 B)
+  // x 128 rows, 64-byte swizzled
   rc = make_tmap_2d_u32(&plan->tmap_w, w_packed, static_cast<uint64_t>(k / 8), static_cast<uint64_t>(n_out),
-                        static_cast<uint64_t>(k / 2), 8 * kQ4Kb, 128, true);
+                        static_cast<uint64_t>(k / 2), 8 * kQ4Kb, 128, 32 * kQ4Kb);
   if (rc) return rc;
   plan->p.q_scales = static_cast<const __nv_bfloat16*>(scales);
   plan->p.q_biases = static_cast<const __nv_bfloat16*>(biases);

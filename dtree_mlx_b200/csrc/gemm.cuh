@@ -97,12 +97,12 @@ struct GemmParams {
 };
 
 constexpr int kGemmThreads = 192;
-constexpr int kDeqWarps = 8;                             // q4 dequant warps (two per TMEM lane quarter)
-constexpr int kQ4BudgetKB = 150;                         // q4 CTA shared memory (one CTA per SM)
+constexpr int kDeqWarps = 4;                             // q4 dequant warps (one per TMEM lane quarter)
+constexpr int kQ4BudgetKB = 110;                         // q4 CTA shared memory (two CTAs per SM)
 constexpr int kGemmThreadsQ4 = 192 + kDeqWarps * 32;
 constexpr int kWTileBytes = 128 * 64 * 2;
 constexpr int kPkTileBytes = 128 * 64 / 2;  // packed 4-bit tile of one 64-wide K block
-constexpr int kQ4Kb = 4;                    // q4: 64-wide K blocks per stream-K unit
+constexpr int kQ4Kb = 2;                    // q4: 64-wide K blocks per stream-K unit (64-byte packed rows)
 
 template <int TPAD, int EPI, bool Q4 = false>
 struct GemmCfg {
@@ -126,19 +126,25 @@ struct GemmCfg {
   // bytes in flight)
   // (TPAD 256, dense prefill: one CTA per SM with a 4-stage ring)
   static constexpr int kBudget = (Q4 ? kQ4BudgetKB : (TPAD >= 256 ? 200 : 110)) * 1024;
-  static constexpr int kFixed = 1024 /*align*/ + kBarBytes + kXchBytes + kRedBytes;
+  // q4: per dequant thread a ring of kSb units' (scale pair, bias pair),
+  // filled by cp.async kSb - 1 units ahead
+  static constexpr int kSb = 4;
+  static constexpr int kSbBytes = Q4 ? kSb * kDeqWarps * 32 * 8 : 0;
+  static constexpr int kFixed = 1024 /*align*/ + kBarBytes + kXchBytes + kRedBytes + kSbBytes;
   static constexpr int kStagesRaw = (kBudget - kFixed) / kStageBytes;
   static constexpr int kMaxStages = Q4 ? 16 : 8;
   static constexpr int kStages = kStagesRaw < 2 ? 2 : (kStagesRaw > kMaxStages ? kMaxStages : kStagesRaw);
   static constexpr int kSmem = kFixed + kStages * kStageBytes;
   // TMEM: accumulator buffers (two, so a segment's MMAs overlap the previous
-  // segment's epilogue; one for q4 at TPAD 128) and, for q4, kDeq buffers of
-  // dequantized W units (the MMA's A operand: 128 lanes x 32 * kKb columns
-  // of bf16 pairs); the dequant warps refill buffer i % kDeq once the MMA
-  // of unit i - kDeq has committed it free
-  static constexpr int kAccBufs = (Q4 && TPAD >= 128) ? 1 : 2;
+  // segment's epilogue; one for q4 from TPAD 80) and, for q4, kDeq buffers
+  // of dequantized W units (the MMA's A operand: 128 lanes x 32 * kKb
+  // columns of bf16 pairs); the dequant warps refill buffer i % kDeq once
+  // the MMA of unit i - kDeq has committed it free.  A q4 CTA holds at most
+  // 256 columns, so two CTAs share an SM (the next GEMM's CTA streams its
+  // weights while this one drains)
+  static constexpr int kAccBufs = (Q4 && TPAD >= 80) ? 1 : 2;
   static constexpr int kTmemAcc = kAccBufs * TPAD;
-  static constexpr int kDeq = Q4 ? (512 - kTmemAcc) / (32 * kKb) : 0;
+  static constexpr int kDeq = Q4 ? (256 - kTmemAcc) / (32 * kKb) : 0;
   static constexpr int kTmemNeed = kTmemAcc + (Q4 ? kDeq * 32 * kKb : 0);
   static constexpr int kTmemCols =
       kTmemNeed <= 32 ? 32 : (kTmemNeed <= 64 ? 64 : (kTmemNeed <= 128 ? 128 : (kTmemNeed <= 256 ? 256 : 512)));
@@ -184,6 +190,16 @@ __device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
   asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(sel));
   return d;
 }
+// 4-byte asynchronous global -> shared copy (cp.async, no register
+// dependency), its commit group and the wait for all but N newest groups
+__device__ __forceinline__ void cp_async_4(void* smem_dst, const void* gsrc) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(smem_dst)), "l"(gsrc) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
 __device__ __forceinline__ __nv_bfloat162 u32_as_bf162(uint32_t v) { return *reinterpret_cast<__nv_bfloat162*>(&v); }
 __device__ __forceinline__ uint32_t bf162_as_u32(__nv_bfloat162 v) { return *reinterpret_cast<uint32_t*>(&v); }
 
@@ -207,7 +223,7 @@ __device__ __forceinline__ uint4 dequant8(uint32_t x, __nv_bfloat162 s2, __nv_bf
 }
 
 template <int TPAD, int EPI, bool Q4>
-__global__ void __launch_bounds__(Q4 ? kGemmThreadsQ4 : kGemmThreads, 1)
+__global__ void __launch_bounds__(Q4 ? kGemmThreadsQ4 : kGemmThreads, Q4 ? 2 : 1)
     gemm_streamk_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_x,
                         GemmParams p) {
   using C = GemmCfg<TPAD, EPI, Q4>;
@@ -231,6 +247,7 @@ __global__ void __launch_bounds__(Q4 ? kGemmThreadsQ4 : kGemmThreads, 1)
   int* s_flag = reinterpret_cast<int*>(tmem_slot + 1);
   float* xch = reinterpret_cast<float*>(bar_base + C::kBarBytes);
   uint8_t* red_raw = bar_base + C::kBarBytes + C::kXchBytes;
+  uint32_t* sb_ring = reinterpret_cast<uint32_t*>(red_raw + C::kRedBytes);  // q4 only
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int G = p.grid;
@@ -417,67 +434,85 @@ __global__ void __launch_bounds__(Q4 ? kGemmThreadsQ4 : kGemmThreads, 1)
     }
   } else if (Q4 && warp >= 6) {
     // ------------------------------------------------------------ dequant (q4)
-    // All 8 warps work on one unit at a time: thread = (tile row r, K half
-    // h of the unit), warps 6..9 h = 0, 10..13 h = 1, each warp on the TMEM
-    // lane quarter it may write (lanes 32 * (warp % 4) ..).  A thread turns
-    // its 16 packed words (two groups of 64) into 64 TMEM columns of bf16
-    // pairs.  The packed tile arrives 128-byte swizzled (16-byte chunk c of
-    // row r at chunk c ^ (r % 8)), so a quarter-warp's chunk reads hit 8
-    // different bank groups.
+    // All 4 warps work on one unit at a time: thread = tile row r, each warp
+    // on the TMEM lane quarter it may write (lanes 32 * (warp % 4) ..).  A
+    // thread turns its row's 16 packed words (two groups of 64) into 64 TMEM
+    // columns of bf16 pairs.  The packed tile arrives 64-byte swizzled
+    // (16-byte chunk c of the 64-byte row r at chunk c ^ ((r / 2) % 4)), so
+    // a quarter-warp's chunk reads hit 8 different bank groups.
     const int r = 32 * (warp & 3) + lane;
     const int h = (warp - 6) >> 2;
     const uint32_t t_lane = static_cast<uint32_t>(32 * (warp & 3)) << 16;
     const int G_row = p.k_groups;  // scale / bias groups per row (K / 64)
-    // scales / biases of this thread's two groups of a unit (no upstream
-    // dependency), loaded two units ahead; groups past K (a ragged last
-    // unit) stay zero: zero weights there, against the zero-filled X columns
-    auto load_sb = [&](int tl, int kb_, __nv_bfloat162& sc2, __nv_bfloat162& bi2) {
-      sc2 = __floats2bfloat162_rn(0.0f, 0.0f);
-      bi2 = sc2;
+    // this thread's (scale pair, bias pair) of unit i sits in ring slot
+    // i % kSb (no upstream dependency): cp.async, kSb - 1 units ahead, so
+    // the global-load latency never meets the dequant arithmetic; groups
+    // past K (a ragged last unit) read as zero (zero weights against the
+    // zero-filled X columns), as do rows past N
+    constexpr int SB = C::kSb;
+    const int dq = threadIdx.x - kGemmThreads;  // 0..255
+    const bool pair_ok = (G_row & 1) == 0;      // 4-byte aligned group pairs
+    auto issue_sb = [&](int slot, int tl, int kb_) {
+      uint32_t* dst = sb_ring + (slot * (kDeqWarps * 32) + dq) * 2;
       const int n = tl * 128 + r;
       const int g0 = kb_ * C::kKb + 2 * h;
-      if (n < p.n_out) {
-        const size_t rb = static_cast<size_t>(n) * G_row;
-        if (g0 < G_row) {
-          sc2.x = p.q_scales[rb + g0];
-          bi2.x = p.q_biases[rb + g0];
+      if (n < p.n_out && pair_ok && g0 + 1 < G_row) {
+        const size_t off = static_cast<size_t>(n) * G_row + g0;
+        cp_async_4(dst, p.q_scales + off);
+        cp_async_4(dst + 1, p.q_biases + off);
+      } else {
+        __nv_bfloat162 sc2 = __floats2bfloat162_rn(0.0f, 0.0f), bi2 = sc2;
+        if (n < p.n_out) {
+          const size_t rb = static_cast<size_t>(n) * G_row;
+          if (g0 < G_row) {
+            sc2.x = p.q_scales[rb + g0];
+            bi2.x = p.q_biases[rb + g0];
+          }
+          if (g0 + 1 < G_row) {
+            sc2.y = p.q_scales[rb + g0 + 1];
+            bi2.y = p.q_biases[rb + g0 + 1];
+          }
         }
-        if (g0 + 1 < G_row) {
-          sc2.y = p.q_scales[rb + g0 + 1];
-          bi2.y = p.q_biases[rb + g0 + 1];
-        }
+        dst[0] = bf162_as_u32(sc2);
+        dst[1] = bf162_as_u32(bi2);
       }
+      cp_async_commit();
     };
-    // (tile, kblk) of units i, i + 1, i + 2
     int tile = static_cast<int>(u0 / p.kb), kblk = static_cast<int>(u0 % p.kb);
-    int tile1 = tile, kblk1 = kblk + 1;
-    if (kblk1 == p.kb) {
-      kblk1 = 0;
-      ++tile1;
+    // (tile, kblk) of the next unit to prefetch
+    int ptile = tile, pkblk = kblk;
+#pragma unroll
+    for (int j = 0; j < SB - 1; ++j) {
+      if (j < n_units) issue_sb(j, ptile, pkblk);
+      else cp_async_commit();
+      if (++pkblk == p.kb) {
+        pkblk = 0;
+        ++ptile;
+      }
     }
-    int tile2 = tile1, kblk2 = kblk1 + 1;
-    if (kblk2 == p.kb) {
-      kblk2 = 0;
-      ++tile2;
-    }
-    __nv_bfloat162 sc_c, bi_c, sc_1, bi_1, sc_2, bi_2;
-    load_sb(tile, kblk, sc_c, bi_c);
-    if (n_units > 1) load_sb(tile1, kblk1, sc_1, bi_1);
     bool ok = true;
     for (int i = 0; i < n_units && ok; ++i) {
       const int s = i % S, d = i % D;
-      if (i + 2 < n_units) load_sb(tile2, kblk2, sc_2, bi_2);
-      const __nv_bfloat162 sc2 = sc_c, bi2 = bi_c;
+      if (i + SB - 1 < n_units) issue_sb((i + SB - 1) % SB, ptile, pkblk);
+      else cp_async_commit();  // (empty group: the wait below counts groups)
+      if (++pkblk == p.kb) {
+        pkblk = 0;
+        ++ptile;
+      }
+      cp_async_wait<SB - 1>();  // unit i's group has landed
+      const uint32_t* sbp = sb_ring + ((i % SB) * (kDeqWarps * 32) + dq) * 2;
+      const __nv_bfloat162 sc2 = u32_as_bf162(sbp[0]), bi2 = u32_as_bf162(sbp[1]);
       ok = mbar_wait(&full_bar[s], static_cast<uint32_t>(i / S) & 1u, 6);
       if (ok && i >= D) ok = mbar_wait(&tfree[d], static_cast<uint32_t>(i / D - 1) & 1u, 9);
       ok = __all_sync(0xffffffffu, ok);  // the TMEM stores below are warp-wide
       if (!ok) break;
       tc_fence_after();
-      const uint8_t* rowp = stage_base + s * C::kStageBytes + C::kWOff + r * 128;
+      const uint8_t* rowp = stage_base + s * C::kStageBytes + C::kWOff + r * 64;
+      const int sw = (r >> 1) & 3;
 #pragma unroll
       for (int gq = 0; gq < 2; ++gq) {  // group 2h + gq: 8 words, 32 TMEM columns
-        const uint4 pa = *reinterpret_cast<const uint4*>(rowp + (((4 * h + 2 * gq) ^ (r & 7)) << 4));
-        const uint4 pb = *reinterpret_cast<const uint4*>(rowp + (((4 * h + 2 * gq + 1) ^ (r & 7)) << 4));
+        const uint4 pa = *reinterpret_cast<const uint4*>(rowp + (((4 * h + 2 * gq) ^ sw) << 4));
+        const uint4 pb = *reinterpret_cast<const uint4*>(rowp + (((4 * h + 2 * gq + 1) ^ sw) << 4));
         const __nv_bfloat16 sc = gq ? __high2bfloat16(sc2) : __low2bfloat16(sc2);
         const __nv_bfloat16 bi = gq ? __high2bfloat16(bi2) : __low2bfloat16(bi2);
         const __nv_bfloat162 s2 = __halves2bfloat162(sc, sc), b2 = __halves2bfloat162(bi, bi);
@@ -497,17 +532,8 @@ __global__ void __launch_bounds__(Q4 ? kGemmThreadsQ4 : kGemmThreads, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&deq_full[d]);
-      sc_c = sc_1;
-      bi_c = bi_1;
-      sc_1 = sc_2;
-      bi_1 = bi_2;
-      tile1 = tile2;
-      kblk1 = kblk2;
-      if (++kblk2 == p.kb) {
-        kblk2 = 0;
-        ++tile2;
-      }
     }
+    cp_async_wait<0>();  // no copy outlives the CTA
   } else {
     // ------------------------------------------------------------ epilogue
     // Processes the 128 x TPAD accumulator in chunks of 8 tree rows (TMEM
@@ -598,7 +624,9 @@ __global__ void __launch_bounds__(Q4 ? kGemmThreadsQ4 : kGemmThreads, 1)
         const int tb = (tile % NT) * TPAD;  // first token row of the tile
         const int n = mt * 128 + row;
         // the epilogue of accumulator columns c0 .. c0 + 7 (values a)
-        auto body = [&](const int c0, float (&a)[8]) {
+        // (hv_in, have_h: the residual rows, already loaded by a dense
+        // tile's group prefetch)
+        auto body = [&](const int c0, float (&a)[8], const __nv_bfloat16 (&hv_in)[8], const bool have_h) {
             if constexpr (EPI == kEpiPartial) {
               if (n < p.n_out) {
                 float* o = p.out_f32 + static_cast<size_t>(cta % p.split) * TPAD * p.ldo + n;
@@ -619,7 +647,8 @@ __global__ void __launch_bounds__(Q4 ? kGemmThreadsQ4 : kGemmThreads, 1)
 #pragma unroll
                 for (int j = 0; j < 8; ++j) {
                   const int t = tb + c0 + j;
-                  hv[j] = t < p.n_rows ? p.out[static_cast<size_t>(t) * p.ldo + n] : __float2bfloat16_rn(0.0f);
+                  hv[j] = have_h ? hv_in[j]
+                                 : (t < p.n_rows ? p.out[static_cast<size_t>(t) * p.ldo + n] : __float2bfloat16_rn(0.0f));
                 }
 #pragma unroll
                 for (int j = 0; j < 8; ++j) {
@@ -786,14 +815,31 @@ __global__ void __launch_bounds__(Q4 ? kGemmThreadsQ4 : kGemmThreads, 1)
                   }
               }
             }
+            // the residual rows of the whole group, all loads in flight at once
+            __nv_bfloat16 hg[CW];
+            if constexpr (EPI == kEpiResidual) {
+#pragma unroll
+              for (int j = 0; j < CW; ++j) {
+                const int t = tb + cg + j;
+                hg[j] = (n < p.n_out && t < p.n_rows) ? p.out[static_cast<size_t>(t) * p.ldo + n]
+                                                      : __float2bfloat16_rn(0.0f);
+              }
+            }
 #pragma unroll 1
             for (int sub = 0; sub < CW / 8; ++sub) {
               float a[8];
+              __nv_bfloat16 h8[8];
 #pragma unroll
               for (int j = 0; j < 8; ++j) a[j] = g[j];
 #pragma unroll
               for (int j = 0; j < CW - 8; ++j) g[j] = g[j + 8];
-              body(cg + sub * 8, a);
+              if constexpr (EPI == kEpiResidual) {
+#pragma unroll
+                for (int j = 0; j < 8; ++j) h8[j] = hg[j];
+#pragma unroll
+                for (int j = 0; j < CW - 8; ++j) hg[j] = hg[j + 8];
+              }
+              body(cg + sub * 8, a, h8, EPI == kEpiResidual);
             }
           }
         } else {
@@ -832,7 +878,8 @@ __global__ void __launch_bounds__(Q4 ? kGemmThreadsQ4 : kGemmThreads, 1)
                   }
               }
             }
-            body(c0, a);
+            const __nv_bfloat16 h8[8] = {};
+            body(c0, a, h8, false);
           }
         }
       }

@@ -83,14 +83,12 @@ static size_t gemm_ws_need(const dtree_qwen3_desc& d) { return gemm_ws_bytes(pad
 static size_t attn_ws_need(const dtree_qwen3_desc& d) {
   return attn_ws_bytes(d.n_heads, d.t_cap, d.head_dim, kAttnMaxSplits);
 }
-// Split-K of a projection: enough CTAs for two per SM with bf16 weights (a
-// CTA's ring fits half an SM's shared memory), so twice the weight bytes sit
-// in the rings when the inputs arrive; one per SM for the 448-thread 4-bit
-// kernel, whose CTAs fill an SM (a second wave would follow).
+// Split-K of a projection: enough CTAs for two per SM (a CTA's ring fits
+// half an SM's shared memory, bf16 and 4-bit alike), so twice the weight
+// bytes sit in the rings when the inputs arrive.
 static int proj_split(const dtree_qwen3_desc& d, int n_out) {
   const int tiles = (n_out + 127) / 128;
-  const int per_sm = d.quant_bits == 4 ? 1 : 2;
-  return std::max(1, std::min(kMaxProjSplit, per_sm * num_sms() / tiles));
+  return std::max(1, std::min(kMaxProjSplit, 2 * num_sms() / tiles));
 }
 static int qkv_width(const dtree_qwen3_desc& d) { return (d.n_heads + 2 * d.n_kv_heads) * d.head_dim; }
 static size_t partials_need(const dtree_qwen3_desc& d) {

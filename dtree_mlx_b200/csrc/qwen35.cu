@@ -620,7 +620,7 @@ extern "C" int dtree_qwen35_prefill(dtree_qwen35_model* m, const int32_t* tokens
       c.ldo = x.conv_dim;
       c.n_norm_heads = 2 * d.lin_k_heads;
       c.n_q_heads = d.lin_k_heads;
-      if ((rc = tree_conv1d_launch(c, 1, d.lin_k_dim, st))) return rc;
+      if ((rc = conv1d_seq_launch(c, d.lin_k_dim, st))) return rc;
       DeltaParams dp{};
       dp.q = qkvn;
       dp.k = qkvn + x.key_dim;

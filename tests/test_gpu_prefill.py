@@ -139,6 +139,7 @@ def test_session_prefill_uses_dense_path(lib):
     w = random_qwen3_weights(cfg, seed=4, device=DEV, norm_jitter=0.1)
     ids = [0, 2]
     eng = Qwen3Engine(w, kv_capacity=1024, layer_ids=ids)
+    eng.dense_prefill_min_rows = 129  # (the default routes prompts this short to 128-row verify forwards)
     sess = DecodeSession(eng, StepConfig(mode="dtree", rows=15, budget=24, n_nodes=25), 1024, drafter=None)
     prompt = np.random.default_rng(5).integers(cfg.vocab_size, size=300).tolist()
     first = sess.prefill(prompt)
