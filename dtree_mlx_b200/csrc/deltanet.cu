@@ -334,18 +334,19 @@ __global__ void tree_gated_delta_kernel(DeltaParams p) {
 // Prompt (sequence) recurrence: rows 0..n_nodes-1 form one chain from
 // state_in, the state stays in f32 registers from the first row to the last
 // (mlx-lm's sequence kernel; no per-row rounding) and is written to
-// final_state.  CTA = kSeqWarps warps = that many consecutive state rows of
-// one value head (they share the head's q / k); one warp per state row,
-// Dk/32 elements per lane.  The rows' inputs arrive in blocks of kSeqRows in
-// shared memory by cp.async, double buffered (block b + 2 is fetched while
-// block b + 1 lands and block b is computed): per row the head's q and k
-// (Dk bf16 each), the CTA's kSeqWarps v values and the a / b gate inputs.
-// Per row
+// final_state.  CTA = kSeqWarps warps x 2 state rows = 16 consecutive state
+// rows of one value head (they share the head's q / k); a half-warp holds a
+// state row, Dk/16 elements per lane.  The rows' inputs arrive in blocks of
+// kSeqRows in shared memory by cp.async, double buffered (block b + 2 is
+// fetched while block b + 1 lands and block b is computed): per row the
+// head's q and k (Dk bf16 each), the CTA's 16 v values and the a / b gate
+// inputs, from which the rows' gates are computed once per CTA.  Per row
 //   S' = S g;  kv = S' k;  delta = (v - kv) beta;  S'' = S' + k delta;
 //   y = S'' q = g (S q) + delta (k q)
 // so the three reductions (S k, S q, k q) run side by side.
 constexpr int kSeqWarps = 8;
-constexpr int kSeqRows = 32;
+constexpr int kSeqCtaRows = 2 * kSeqWarps;  // state rows per CTA
+constexpr int kSeqRows = 32;                // prompt rows per staged block
 
 __device__ __forceinline__ void seq_cp16(void* dst, const void* src) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
@@ -358,7 +359,7 @@ template <int DK>
 struct SeqBuf {
   __nv_bfloat16 q[kSeqRows][DK];
   __nv_bfloat16 k[kSeqRows][DK];
-  __nv_bfloat16 v[kSeqRows][kSeqWarps];
+  __nv_bfloat16 v[kSeqRows][kSeqCtaRows];
   uint32_t a[kSeqRows];  // the bf16 pair holding this head's a (hv & ~1, hv | 1)
   uint32_t b[kSeqRows];
   float g[kSeqRows];     // the rows' gates, computed once per CTA from a / b
@@ -367,15 +368,17 @@ struct SeqBuf {
 
 template <int DK>
 __global__ void __launch_bounds__(kSeqWarps * 32) gated_delta_seq_kernel(DeltaParams p) {
-  constexpr int NP = DK / 32;
-  static_assert(NP == 2 || NP == 4, "sequence gated delta: head_k_dim 64 or 128");
+  constexpr int NP = DK / 16;
+  static_assert(NP == 4 || NP == 8, "sequence gated delta: head_k_dim 64 or 128");
   pdl_trigger();
   __shared__ __align__(16) SeqBuf<DK> buf[2];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int rows_per_head = p.dv / kSeqWarps;
+  const int sub = lane >> 4, l16 = lane & 15;  // state row of the half-warp, lane within it
+  const int rows_per_head = p.dv / kSeqCtaRows;
   const int hv = blockIdx.x / rows_per_head;
-  const int dv0 = (blockIdx.x % rows_per_head) * kSeqWarps;
-  const int dv = dv0 + warp;
+  const int dv0 = (blockIdx.x % rows_per_head) * kSeqCtaRows;
+  const int rl = warp * 2 + sub;  // state row within the CTA
+  const int dv = dv0 + rl;
   const int hk = hv / (p.n_v_heads / p.n_k_heads);
   const int T = p.n_nodes;
   const __nv_bfloat16* q = static_cast<const __nv_bfloat16*>(p.q) + hk * DK;
@@ -386,8 +389,8 @@ __global__ void __launch_bounds__(kSeqWarps * 32) gated_delta_seq_kernel(DeltaPa
   const float dt_b = __bfloat162float(static_cast<const __nv_bfloat16*>(p.dt_bias)[hv]);
   const float ea = expf(p.a_log[hv]);
   pdl_wait();
-  // copies of row block blk into buffer blk % 2: q / k rows 16 bytes a
-  // thread-chunk, then v (16 bytes) and the a / b pairs (4 bytes) per row
+  // copies of row block blk into buffer blk % 2: q / k rows in 16-byte
+  // chunks, then per row v (two 16-byte chunks) and the a / b pairs
   auto issue = [&](int blk) {
     SeqBuf<DK>& B = buf[blk & 1];
     const int r0 = blk * kSeqRows;
@@ -400,16 +403,19 @@ __global__ void __launch_bounds__(kSeqWarps * 32) gated_delta_seq_kernel(DeltaPa
         seq_cp16((which ? &B.k[r][0] : &B.q[r][0]) + ch * 8, src);
       }
     }
+    for (int c = threadIdx.x; c < kSeqRows * 2; c += blockDim.x) {
+      const int r = c >> 1, half = c & 1;
+      if (r0 + r < T) seq_cp16(&B.v[r][half * 8], v + static_cast<size_t>(r0 + r) * p.ldv + half * 8);
+    }
     for (int r = threadIdx.x; r < kSeqRows; r += blockDim.x) {
       if (r0 + r < T) {
-        seq_cp16(&B.v[r][0], v + static_cast<size_t>(r0 + r) * p.ldv);
         seq_cp4(&B.a[r], a + static_cast<size_t>(r0 + r) * p.ldab);
         seq_cp4(&B.b[r], b + static_cast<size_t>(r0 + r) * p.ldab);
       }
     }
     asm volatile("cp.async.commit_group;" ::: "memory");
   };
-  const float* st_in = static_cast<const float*>(p.state_in) + (static_cast<size_t>(hv) * p.dv + dv) * DK + lane * NP;
+  const float* st_in = static_cast<const float*>(p.state_in) + (static_cast<size_t>(hv) * p.dv + dv) * DK + l16 * NP;
   float s[NP];
 #pragma unroll
   for (int i = 0; i < NP; ++i) s[i] = st_in[i];
@@ -438,22 +444,18 @@ __global__ void __launch_bounds__(kSeqWarps * 32) gated_delta_seq_kernel(DeltaPa
     __syncthreads();
     for (int r = 0; r < rn; ++r) {
       float kk[NP], qq[NP];
-      if constexpr (NP == 4) {
-        const uint2 kw = *reinterpret_cast<const uint2*>(&B.k[r][lane * 4]);
-        const uint2 qw = *reinterpret_cast<const uint2*>(&B.q[r][lane * 4]);
+#pragma unroll
+      for (int c = 0; c < NP / 4; ++c) {
+        const uint2 kw = *reinterpret_cast<const uint2*>(&B.k[r][l16 * NP + c * 4]);
+        const uint2 qw = *reinterpret_cast<const uint2*>(&B.q[r][l16 * NP + c * 4]);
         const float2 k0 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&kw.x));
         const float2 k1 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&kw.y));
         const float2 q0 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&qw.x));
         const float2 q1 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&qw.y));
-        kk[0] = k0.x; kk[1] = k0.y; kk[2] = k1.x; kk[3] = k1.y;
-        qq[0] = q0.x; qq[1] = q0.y; qq[2] = q1.x; qq[3] = q1.y;
-      } else {
-        const float2 k0 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&B.k[r][lane * 2]));
-        const float2 q0 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&B.q[r][lane * 2]));
-        kk[0] = k0.x; kk[1] = k0.y;
-        qq[0] = q0.x; qq[1] = q0.y;
+        kk[c * 4] = k0.x; kk[c * 4 + 1] = k0.y; kk[c * 4 + 2] = k1.x; kk[c * 4 + 3] = k1.y;
+        qq[c * 4] = q0.x; qq[c * 4 + 1] = q0.y; qq[c * 4 + 2] = q1.x; qq[c * 4 + 3] = q1.y;
       }
-      const float vv = __bfloat162float(B.v[r][warp]);
+      const float vv = __bfloat162float(B.v[r][rl]);
       const float g = B.g[r], beta = B.beta[r];
       float sk = 0.0f, sq = 0.0f, kq = 0.0f;
 #pragma unroll
@@ -463,7 +465,7 @@ __global__ void __launch_bounds__(kSeqWarps * 32) gated_delta_seq_kernel(DeltaPa
         kq = fmaf(kk[i], qq[i], kq);
       }
 #pragma unroll
-      for (int o = 16; o > 0; o >>= 1) {
+      for (int o = 8; o > 0; o >>= 1) {  // within the half-warp
         sk += __shfl_xor_sync(0xffffffffu, sk, o);
         sq += __shfl_xor_sync(0xffffffffu, sq, o);
         kq += __shfl_xor_sync(0xffffffffu, kq, o);
@@ -471,14 +473,14 @@ __global__ void __launch_bounds__(kSeqWarps * 32) gated_delta_seq_kernel(DeltaPa
       const float delta = (vv - g * sk) * beta;
 #pragma unroll
       for (int i = 0; i < NP; ++i) s[i] = fmaf(kk[i], delta, s[i] * g);
-      if (lane == 0) y[static_cast<size_t>(blk * kSeqRows + r) * p.ldy] = __float2bfloat16_rn(fmaf(g, sq, delta * kq));
+      if (l16 == 0) y[static_cast<size_t>(blk * kSeqRows + r) * p.ldy] = __float2bfloat16_rn(fmaf(g, sq, delta * kq));
     }
     __syncthreads();  // buffer blk % 2 is refilled next
     if (blk + 2 < nblk) issue(blk + 2);
     else asm volatile("cp.async.commit_group;" ::: "memory");
   }
   asm volatile("cp.async.wait_group 0;" ::: "memory");
-  float* fs = static_cast<float*>(p.final_state) + (static_cast<size_t>(hv) * p.dv + dv) * DK + lane * NP;
+  float* fs = static_cast<float*>(p.final_state) + (static_cast<size_t>(hv) * p.dv + dv) * DK + l16 * NP;
 #pragma unroll
   for (int i = 0; i < NP; ++i) fs[i] = s[i];
 }
@@ -634,13 +636,13 @@ static int delta_launch_t(DeltaParams p, int dk, cudaStream_t st) {
 int gated_delta_seq_launch(const DeltaParams& p, int dk, cudaStream_t st) {
   DTREE_CHECK_ARG(p.q && p.k && p.v && p.a && p.b && p.a_log && p.dt_bias && p.state_in && p.final_state && p.y,
                   "sequence gated delta: null pointer (gates come from a / b)");
-  DTREE_CHECK_ARG(p.n_nodes > 0 && p.n_v_heads % p.n_k_heads == 0 && p.dv % kSeqWarps == 0,
-                  "sequence gated delta: bad shape (head_v_dim a multiple of 8)");
+  DTREE_CHECK_ARG(p.n_nodes > 0 && p.n_v_heads % p.n_k_heads == 0 && p.dv % kSeqCtaRows == 0,
+                  "sequence gated delta: bad shape (head_v_dim a multiple of 16)");
   auto al = [](const void* x, uintptr_t m) { return (reinterpret_cast<uintptr_t>(x) & (m - 1)) == 0; };
   DTREE_CHECK_ARG(al(p.q, 16) && al(p.k, 16) && al(p.v, 16) && p.ldqk % 8 == 0 && p.ldv % 8 == 0,
                   "sequence gated delta: q / k / v rows must be 16-byte aligned");
   DTREE_CHECK_ARG(al(p.a, 4) && al(p.b, 4) && p.ldab % 2 == 0, "sequence gated delta: a / b must be 4-byte aligned");
-  const dim3 grid(p.n_v_heads * p.dv / kSeqWarps), block(kSeqWarps * 32);
+  const dim3 grid(p.n_v_heads * p.dv / kSeqCtaRows), block(kSeqWarps * 32);
   switch (dk) {
     case 64: DTREE_CUDA_RET(launch_pdl(gated_delta_seq_kernel<64>, grid, block, 0, st, p)); return kOk;
     case 128: DTREE_CUDA_RET(launch_pdl(gated_delta_seq_kernel<128>, grid, block, 0, st, p)); return kOk;

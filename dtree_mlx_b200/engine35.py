@@ -99,8 +99,8 @@ class Qwen35Engine:
 
     max_prefill_rows = 4096  # rows per dense prefill call (workspace ~100 KB per row at the 9B shape)
     # every prompt longer than one verify forward runs dense: the 128-row
-    # sequence forwards cost ~45 ms each at the 9B shape (tree kernels on a
-    # 128-node chain) against 95 ms for a whole 2048-row dense prefill
+    # sequence forwards cost ~21 ms each at the 9B shape (tree kernels on a
+    # 128-node chain) against 70 ms for a whole 2048-row dense prefill
     dense_prefill_min_rows = 129
 
     def prefill_dense(self, tokens: torch.Tensor, state: torch.Tensor, hidden_out: torch.Tensor | None,
