@@ -667,15 +667,24 @@ __global__ void __launch_bounds__(Q4 ? kGemmThreadsQ4 : kGemmThreads, Q4 ? 2 : 1
               epi_bar();
               if (row < 64) {
                 const int jf = mt * 64 + row;
+                // every exchange load, then every column's arithmetic, then
+                // every store: a store may alias the (generic) exchange
+                // pointer, so a load after it could not be hoisted and the
+                // eight expf / divide chains would run one after another
+                float uu[8];
+#pragma unroll
+                for (int j = 0; j < 8; ++j) uu[j] = bf16_round(xch[j * 128 + row + 64]);
+                __nv_bfloat16 o[8];
 #pragma unroll
                 for (int j = 0; j < 8; ++j) {
                   const int t = tb + c0 + j;
                   const float g = bf16_round(a[j]);
-                  const float uu = bf16_round(xch[j * 128 + row + 64]);
                   const float sg = bf16_round(1.0f / (1.0f + expf(-g)));
                   const float sl = bf16_round(g * sg);
-                  p.out[static_cast<size_t>(t) * p.ldo + jf] = __float2bfloat16_rn(t < p.n_rows ? sl * uu : 0.0f);
+                  o[j] = __float2bfloat16_rn(t < p.n_rows ? sl * uu[j] : 0.0f);
                 }
+#pragma unroll
+                for (int j = 0; j < 8; ++j) p.out[static_cast<size_t>(tb + c0 + j) * p.ldo + jf] = o[j];
               }
               epi_bar();
             } else if constexpr (EPI == kEpiQkv) {
