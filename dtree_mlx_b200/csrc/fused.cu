@@ -1074,7 +1074,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
                   const int t = c0 + e;
                   const float gt = bf16_round(a[e]);
                   const float uu = bf16_round(xch[e * 128 + row + 64]);
-                  const float sg2 = bf16_round(1.0f / (1.0f + expf(-gt)));
+                  const float sg2 = bf16_round(__fdividef(1.0f, 1.0f + __expf(-gt)));  // as the GEMM epilogue
                   const float sl = bf16_round(gt * sg2);
                   if (t < p.n_rows) p.act[static_cast<size_t>(t) * p.ffn + jf] = __float2bfloat16_rn(sl * uu);
                 }

@@ -26,12 +26,12 @@
 //
 // Q4 variant (4-bit affine weights, group 64 along K, MLX layout: packed
 // uint32 [N][K/8] with element 8j+i in bits 4i..4i+3 of word j, bf16 scales
-// and biases [N][K/64]): a stream-K unit is 256 wide in K (4 groups); TMA
-// brings the packed 128x256 tile (16 KB, 128-byte swizzled) and the four
-// 64-wide X blocks, 8 more warps (6..13) dequantize it, w = scale*q + bias
-// rounded once to bf16 (fma.rn.bf16x2), into a TMEM buffer that the MMA
-// reads as its A operand (16 MMAs of K 16 per unit, so the MMA thread's
-// one barrier wait and two commits per unit are spread over 16 MMAs).
+// and biases [N][K/64]): a stream-K unit is 128 wide in K (2 groups); TMA
+// brings the packed 128x128 tile (8 KB, 64-byte swizzled) and the two
+// 64-wide X blocks; 4 more warps (6..9, 320 threads, two CTAs per SM)
+// dequantize it, w = scale*q + bias rounded once to bf16 (fma.rn.bf16x2),
+// into a TMEM buffer that the MMA reads as its A operand (8 MMAs of K 16
+// per unit).
 #pragma once
 
 #include "common.cuh"
@@ -89,7 +89,7 @@ struct GemmParams {
   uint32_t sample_seed;
   const dtree_step_state* sample_state;
   // q4 weights: bf16 scale / bias per (row, group of 64); row stride =
-  // k_groups = K / 64 (a unit spans 4 groups; the last unit of a row may
+  // k_groups = K / 64 (a unit spans kQ4Kb groups; the last unit of a row may
   // hold fewer, its missing groups read as zero weights)
   const __nv_bfloat16* q_scales;
   const __nv_bfloat16* q_biases;
@@ -679,7 +679,11 @@ __global__ void __launch_bounds__(Q4 ? kGemmThreadsQ4 : kGemmThreads, Q4 ? 2 : 1
                 for (int j = 0; j < 8; ++j) {
                   const int t = tb + c0 + j;
                   const float g = bf16_round(a[j]);
-                  const float sg = bf16_round(1.0f / (1.0f + expf(-g)));
+                  // branch-free approximate exp / divide: their few-ulp fp32
+                  // error is far below the bf16 rounding that follows, and
+                  // the IEEE divide's guarded slow path kept the eight
+                  // columns' chains from overlapping
+                  const float sg = bf16_round(__fdividef(1.0f, 1.0f + __expf(-g)));
                   const float sl = bf16_round(g * sg);
                   o[j] = __float2bfloat16_rn(t < p.n_rows ? sl * uu[j] : 0.0f);
                 }
