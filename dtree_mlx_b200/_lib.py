@@ -170,6 +170,7 @@ PROTOTYPES = {
     "dtree_linear_workspace_bytes": (SZ, [I, I]),
     "dtree_linear_bf16": (I, [P, I, I, P, I, P, P, SZ, I, P]),
     "dtree_linear_q4": (I, [P, I, I, P, P, P, I, P, P, SZ, I, P]),
+    "dtree_linear_q4_workspace_bytes": (SZ, [I, I, I]),
     "dtree_tree_conv1d": (I, [P, I, P, P, P, I, I, I, I, P, P, P]),
     "dtree_tree_gated_delta": (I, [P, P, P, P, P, P, P, I, I, I, I, I, I, I, P, P, P]),
     "dtree_gated_delta_commit": (I, [P, P, P, P, P, P, P, I, I, I, I, I, I, I, P, P]),

@@ -91,7 +91,6 @@ static int plan_common(GemmPlan* plan, int n_out, int k, const void* x, int t_pa
   p = GemmParams{};
   p.n_out = n_out;
   p.kb = (k + kunit - 1) / kunit;  // (4-bit: the last unit of a row may be partial)
-  p.k_groups = k / 64;
   p.m_tiles = m_tiles;
   p.n_rows = t_pad;
   p.n_tiles = 1;
@@ -126,9 +125,10 @@ int gemm_plan(GemmPlan* plan, const void* w, int n_out, int k, const void* x, in
                            static_cast<uint64_t>(k) * 2, 64, 128, true);
 }
 
-int gemm_plan_q4(GemmPlan* plan, const void* w_packed, const void* scales, const void* biases, int n_out, int k,
-                 const void* x, int t_pad, int x_row_stride_elems, int epi, int grid) {
-  DTREE_CHECK_ARG(w_packed && scales && biases, "null q4 weight pointer");
+int gemm_plan_q4(GemmPlan* plan, const void* w_packed, const void* sb, int n_out, int k, const void* x, int t_pad,
+                 int x_row_stride_elems, int epi, int grid) {
+  DTREE_CHECK_ARG(w_packed && sb, "null q4 weight pointer");
+  DTREE_CHECK_ARG(reinterpret_cast<uintptr_t>(sb) % 16 == 0, "q4 scale / bias blocks must be 16-byte aligned");
   DTREE_CHECK_ARG(epi == kEpiStore || epi == kEpiPartial || epi == kEpiSwiglu,
                   "q4 GEMM supports the store, split-K partial and SwiGLU epilogues");
   int rc = plan_common(plan, n_out, k, x, t_pad, x_row_stride_elems, epi, grid, false, 64 * kQ4Kb);
@@ -138,9 +138,55 @@ int gemm_plan_q4(GemmPlan* plan, const void* w_packed, const void* scales, const
   rc = make_tmap_2d_u32(&plan->tmap_w, w_packed, static_cast<uint64_t>(k / 8), static_cast<uint64_t>(n_out),
                         static_cast<uint64_t>(k / 2), 8 * kQ4Kb, 128, 32 * kQ4Kb);
   if (rc) return rc;
-  plan->p.q_scales = static_cast<const __nv_bfloat16*>(scales);
-  plan->p.q_biases = static_cast<const __nv_bfloat16*>(biases);
+  plan->p.q_sb = static_cast<const uint8_t*>(sb);
   plan->q4 = true;
+  return kOk;
+}
+
+size_t q4_sb_bytes(int n_out, int k) {
+  const size_t m_tiles = (static_cast<size_t>(n_out) + 127) / 128;
+  const size_t units = (static_cast<size_t>(k) + 64 * kQ4Kb - 1) / (64 * kQ4Kb);
+  return m_tiles * units * kQ4SbBlock;
+}
+
+// One thread per (m tile, unit, row): the row's (s0, s1, b0, b1) for the
+// unit's groups 2u, 2u + 1 (MLX bf16 [n][k/64] scales and biases), zeros
+// past the last row or group.
+__global__ void q4_sb_repack_kernel(const __nv_bfloat16* __restrict__ scales, const __nv_bfloat16* __restrict__ biases,
+                                    int n_out, int groups, int units, long long total, uint2* __restrict__ out) {
+  const long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= total) return;
+  const int r = static_cast<int>(i % 128);
+  const long long tu = i / 128;
+  const int u = static_cast<int>(tu % units);
+  const long long n = (tu / units) * 128 + r;
+  __nv_bfloat16 v[4];
+  const __nv_bfloat16 z = __float2bfloat16_rn(0.0f);
+#pragma unroll
+  for (int j = 0; j < 2; ++j) {
+    const int g = u * kQ4Kb + j;
+    const bool in = n < n_out && g < groups;
+    v[j] = in ? scales[n * groups + g] : z;
+    v[2 + j] = in ? biases[n * groups + g] : z;
+  }
+  uint2 o;
+  o.x = static_cast<uint32_t>(__bfloat16_as_ushort(v[0])) | (static_cast<uint32_t>(__bfloat16_as_ushort(v[1])) << 16);
+  o.y = static_cast<uint32_t>(__bfloat16_as_ushort(v[2])) | (static_cast<uint32_t>(__bfloat16_as_ushort(v[3])) << 16);
+  out[i] = o;
+}
+
+int q4_sb_repack_launch(const void* scales, const void* biases, int n_out, int k, void* sb, cudaStream_t stream) {
+  DTREE_CHECK_ARG(scales && biases && sb, "null pointer");
+  DTREE_CHECK_ARG(k % 64 == 0 && k > 0 && n_out > 0, "q4 repack: K must be a positive multiple of 64");
+  static_assert(kQ4Kb == 2, "a scale / bias block holds two groups per row");
+  const int groups = k / 64;
+  const int units = (k + 64 * kQ4Kb - 1) / (64 * kQ4Kb);
+  const long long total = static_cast<long long>((n_out + 127) / 128) * units * 128;
+  const int threads = 256;
+  q4_sb_repack_kernel<<<static_cast<unsigned>((total + threads - 1) / threads), threads, 0, stream>>>(
+      static_cast<const __nv_bfloat16*>(scales), static_cast<const __nv_bfloat16*>(biases), n_out, groups, units,
+      total, static_cast<uint2*>(sb));
+  DTREE_CUDA_RET(cudaGetLastError());
   return kOk;
 }
 
@@ -262,14 +308,27 @@ extern "C" int dtree_linear_bf16(const void* x, int t_pad, int k, const void* w,
   return gemm_launch(plan, static_cast<cudaStream_t>(stream));
 }
 
+extern "C" size_t dtree_linear_q4_workspace_bytes(int t_pad, int n, int k) {
+  return ((gemm_ws_bytes(t_pad, 2 * num_sms()) + 255) & ~static_cast<size_t>(255)) + q4_sb_bytes(n, k);
+}
+
 extern "C" int dtree_linear_q4(const void* x, int t_pad, int k, const void* w_packed, const void* scales,
                                const void* biases, int n, void* y, void* workspace, size_t workspace_bytes,
                                int split_k, void* stream) {
-  DTREE_CHECK_ARG(x && y, "null pointer");
-  GemmPlan plan;
-  int rc = gemm_plan_q4(&plan, w_packed, scales, biases, n, k, x, t_pad, k, kEpiStore, split_k > 0 ? split_k : 0);
+  DTREE_CHECK_ARG(x && y && workspace, "null pointer");
+  DTREE_CHECK_ARG(n > 0 && k > 0 && k % 64 == 0, "N must be positive and K a positive multiple of 64");
+  DTREE_CHECK_ARG(workspace_bytes >= dtree_linear_q4_workspace_bytes(t_pad, n, k),
+                  "workspace smaller than dtree_linear_q4_workspace_bytes");
+  const size_t ws_gemm = (gemm_ws_bytes(t_pad, 2 * num_sms()) + 255) & ~static_cast<size_t>(255);
+  void* sb = static_cast<char*>(workspace) + ws_gemm;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  // the scale / bias blocks of this call's weight, then the GEMM
+  int rc = q4_sb_repack_launch(scales, biases, n, k, sb, st);
   if (rc) return rc;
-  rc = gemm_bind_ws(&plan, workspace, workspace_bytes);
+  GemmPlan plan;
+  rc = gemm_plan_q4(&plan, w_packed, sb, n, k, x, t_pad, k, kEpiStore, split_k > 0 ? split_k : 0);
+  if (rc) return rc;
+  rc = gemm_bind_ws(&plan, workspace, ws_gemm);
   if (rc) return rc;
   plan.p.out = static_cast<__nv_bfloat16*>(y);
   plan.p.ldo = n;

@@ -88,13 +88,14 @@ struct GemmParams {
   float inv_temp;
   uint32_t sample_seed;
   const dtree_step_state* sample_state;
-  // q4 weights: bf16 scale / bias per (row, group of 64); row stride =
-  // k_groups = K / 64 (a unit spans kQ4Kb groups; the last unit of a row may
-  // hold fewer, its missing groups read as zero weights)
-  const __nv_bfloat16* q_scales;
-  const __nv_bfloat16* q_biases;
-  int k_groups;
+  // q4 scales and biases, repacked once per weight (q4_sb_repack_launch):
+  // per (m tile, unit) one 1 KB block of 128 rows x (s0, s1, b0, b1) bf16
+  // for the unit's two groups of 64; rows past N and groups past K are zero
+  const uint8_t* q_sb;
 };
+
+// bytes of a weight's repacked q4 scale / bias blocks
+constexpr int kQ4SbBlock = 128 * 4 * 2;
 
 constexpr int kGemmThreads = 192;
 constexpr int kDeqWarps = 4;                             // q4 dequant warps (one per TMEM lane quarter)
@@ -111,10 +112,12 @@ struct GemmCfg {
   static constexpr int kKb = Q4 ? kQ4Kb : 1;
   static constexpr int kXBlock = TPAD * 64 * 2;  // X of one K block (128-byte swizzled rows)
   static constexpr int kXBytes = kXBlock * kKb;
-  // bf16 stage: [W 16 KB][X]; q4 stage: [X blocks][packed tile] (X stays 1024-aligned)
-  static constexpr int kStageBytes = (Q4 ? kPkTileBytes * kKb : kWTileBytes) + kXBytes;
+  // bf16 stage: [W 16 KB][X]; q4 stage: [X blocks][packed tile][scale /
+  // bias block 1 KB] (X stays 1024-aligned)
+  static constexpr int kStageBytes = (Q4 ? kPkTileBytes * kKb + kQ4SbBlock : kWTileBytes) + kXBytes;
   static constexpr int kXOff = Q4 ? 0 : kWTileBytes;
   static constexpr int kWOff = Q4 ? kXBytes : 0;
+  static constexpr int kSbOff = kWOff + kPkTileBytes * kKb;  // q4 only
   static constexpr int kBarBytes = Q4 ? 512 : 256;
   static constexpr int kXchBytes = (EPI == kEpiQkv || EPI == kEpiSwiglu) ? 128 * 8 * 4 : 0;
   // [0,256): per-warp reductions of one 8-row chunk; then s_best / s_pos
@@ -126,15 +129,10 @@ struct GemmCfg {
   // bytes in flight)
   // (TPAD 256, dense prefill: one CTA per SM with a 4-stage ring)
   static constexpr int kBudget = (Q4 ? kQ4BudgetKB : (TPAD >= 256 ? 200 : 110)) * 1024;
-  // q4: per dequant thread a ring of kSb units' (scale pair, bias pair),
-  // filled by cp.async kSb - 1 units ahead
-  static constexpr int kSb = 4;
-  static constexpr int kSbBytes = Q4 ? kSb * kDeqWarps * 32 * 8 : 0;
-  static constexpr int kFixed = 1024 /*align*/ + kBarBytes + kXchBytes + kRedBytes + kSbBytes;
+  static constexpr int kFixed = 1024 /*align*/ + kBarBytes + kXchBytes + kRedBytes;
   static constexpr int kStagesRaw = (kBudget - kFixed) / kStageBytes;
   static constexpr int kMaxStages = Q4 ? 16 : 8;
-  static constexpr int kStages = kStagesRaw < 2 ? 2 : (kStagesRaw > kMaxStages ? kMaxStages : kStagesRaw);
-  static constexpr int kSmem = kFixed + kStages * kStageBytes;
+  static constexpr int kStagesFit = kStagesRaw < 2 ? 2 : (kStagesRaw > kMaxStages ? kMaxStages : kStagesRaw);
   // TMEM: accumulator buffers (two, so a segment's MMAs overlap the previous
   // segment's epilogue; one for q4 from TPAD 80) and, for q4, kDeq buffers
   // of dequantized W units (the MMA's A operand: 128 lanes x 32 * kKb
@@ -146,6 +144,12 @@ struct GemmCfg {
   static constexpr int kTmemAcc = kAccBufs * TPAD;
   static constexpr int kDeq = Q4 ? (256 - kTmemAcc) / (32 * kKb) : 0;
   static constexpr int kTmemNeed = kTmemAcc + (Q4 ? kDeq * 32 * kKb : 0);
+  // q4 with at least 3 dequant buffers: a ring of exactly kDeq stages, so a
+  // stage's arrival (its refill waited for the MMAs of the unit kDeq back)
+  // also proves that unit's TMEM buffer free (the dequant warps skip that
+  // wait); the TMA copies land well within 3 units' time
+  static constexpr int kStages = (Q4 && kDeq >= 3 && kDeq <= kStagesFit) ? kDeq : kStagesFit;
+  static constexpr int kSmem = kFixed + kStages * kStageBytes;
   static constexpr int kTmemCols =
       kTmemNeed <= 32 ? 32 : (kTmemNeed <= 64 ? 64 : (kTmemNeed <= 128 ? 128 : (kTmemNeed <= 256 ? 256 : 512)));
   static constexpr uint32_t kIdesc = idesc_bf16_f32(128, TPAD);
@@ -189,16 +193,6 @@ __device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
   uint32_t d;
   asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(sel));
   return d;
-}
-// 4-byte asynchronous global -> shared copy (cp.async, no register
-// dependency), its commit group and the wait for all but N newest groups
-__device__ __forceinline__ void cp_async_4(void* smem_dst, const void* gsrc) {
-  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(smem_dst)), "l"(gsrc) : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() {
-  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 __device__ __forceinline__ __nv_bfloat162 u32_as_bf162(uint32_t v) { return *reinterpret_cast<__nv_bfloat162*>(&v); }
 __device__ __forceinline__ uint32_t bf162_as_u32(__nv_bfloat162 v) { return *reinterpret_cast<uint32_t*>(&v); }
@@ -247,7 +241,6 @@ __global__ void __launch_bounds__(Q4 ? kGemmThreadsQ4 : kGemmThreads, Q4 ? 2 : 1
   int* s_flag = reinterpret_cast<int*>(tmem_slot + 1);
   float* xch = reinterpret_cast<float*>(bar_base + C::kBarBytes);
   uint8_t* red_raw = bar_base + C::kBarBytes + C::kXchBytes;
-  uint32_t* sb_ring = reinterpret_cast<uint32_t*>(red_raw + C::kRedBytes);  // q4 only
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int G = p.grid;
@@ -317,6 +310,10 @@ __global__ void __launch_bounds__(Q4 ? kGemmThreadsQ4 : kGemmThreads, Q4 ? 2 : 1
             mbar_arrive_expect_tx(&full_bar[i], C::kStageBytes);
             tma_load_2d(stage_base + i * C::kStageBytes + C::kWOff, &tmap_w, &full_bar[i],
                         kblk * (Q4 ? 8 * C::kKb : 64), mt * 128, pol_w);
+            if constexpr (Q4)
+              bulk_load_1d(stage_base + i * C::kStageBytes + C::kSbOff,
+                           p.q_sb + (static_cast<size_t>(mt) * p.kb + kblk) * kQ4SbBlock, kQ4SbBlock, &full_bar[i],
+                           pol_w);
           }
           xk[i] = kblk * C::kKb * 64;
           xr[i] = nt * TPAD;
@@ -351,6 +348,9 @@ __global__ void __launch_bounds__(Q4 ? kGemmThreadsQ4 : kGemmThreads, Q4 ? 2 : 1
         mbar_arrive_expect_tx(&full_bar[s], C::kStageBytes);
         uint8_t* st = stage_base + s * C::kStageBytes;
         tma_load_2d(st + C::kWOff, &tmap_w, &full_bar[s], kblk * (Q4 ? 8 * C::kKb : 64), mt * 128, pol_w);
+        if constexpr (Q4)
+          bulk_load_1d(st + C::kSbOff, p.q_sb + (static_cast<size_t>(mt) * p.kb + kblk) * kQ4SbBlock, kQ4SbBlock,
+                       &full_bar[s], pol_w);
 #pragma unroll
         for (int k2 = 0; k2 < C::kKb; ++k2)
           tma_load_2d(st + C::kXOff + k2 * C::kXBlock, &tmap_x, &full_bar[s], (kblk * C::kKb + k2) * 64, nt * TPAD,
@@ -439,80 +439,36 @@ __global__ void __launch_bounds__(Q4 ? kGemmThreadsQ4 : kGemmThreads, Q4 ? 2 : 1
     // thread turns its row's 16 packed words (two groups of 64) into 64 TMEM
     // columns of bf16 pairs.  The packed tile arrives 64-byte swizzled
     // (16-byte chunk c of the 64-byte row r at chunk c ^ ((r / 2) % 4)), so
-    // a quarter-warp's chunk reads hit 8 different bank groups.
+    // a quarter-warp's chunk reads hit 8 different bank groups; the row's
+    // scales and biases come with the stage (its 1 KB block, 8 B a row).
+    static_assert(kDeqWarps == 4, "one dequant thread per tile row");
     const int r = 32 * (warp & 3) + lane;
-    const int h = (warp - 6) >> 2;
+    constexpr int h = 0;
     const uint32_t t_lane = static_cast<uint32_t>(32 * (warp & 3)) << 16;
-    const int G_row = p.k_groups;  // scale / bias groups per row (K / 64)
-    // this thread's (scale pair, bias pair) of unit i sits in ring slot
-    // i % kSb (no upstream dependency): cp.async, kSb - 1 units ahead, so
-    // the global-load latency never meets the dequant arithmetic; groups
-    // past K (a ragged last unit) read as zero (zero weights against the
-    // zero-filled X columns), as do rows past N
-    constexpr int SB = C::kSb;
-    const int dq = threadIdx.x - kGemmThreads;  // 0..255
-    const bool pair_ok = (G_row & 1) == 0;      // 4-byte aligned group pairs
-    auto issue_sb = [&](int slot, int tl, int kb_) {
-      uint32_t* dst = sb_ring + (slot * (kDeqWarps * 32) + dq) * 2;
-      const int n = tl * 128 + r;
-      const int g0 = kb_ * C::kKb + 2 * h;
-      if (n < p.n_out && pair_ok && g0 + 1 < G_row) {
-        const size_t off = static_cast<size_t>(n) * G_row + g0;
-        cp_async_4(dst, p.q_scales + off);
-        cp_async_4(dst + 1, p.q_biases + off);
-      } else {
-        __nv_bfloat162 sc2 = __floats2bfloat162_rn(0.0f, 0.0f), bi2 = sc2;
-        if (n < p.n_out) {
-          const size_t rb = static_cast<size_t>(n) * G_row;
-          if (g0 < G_row) {
-            sc2.x = p.q_scales[rb + g0];
-            bi2.x = p.q_biases[rb + g0];
-          }
-          if (g0 + 1 < G_row) {
-            sc2.y = p.q_scales[rb + g0 + 1];
-            bi2.y = p.q_biases[rb + g0 + 1];
-          }
-        }
-        dst[0] = bf162_as_u32(sc2);
-        dst[1] = bf162_as_u32(bi2);
-      }
-      cp_async_commit();
-    };
-    int tile = static_cast<int>(u0 / p.kb), kblk = static_cast<int>(u0 % p.kb);
-    // (tile, kblk) of the next unit to prefetch
-    int ptile = tile, pkblk = kblk;
-#pragma unroll
-    for (int j = 0; j < SB - 1; ++j) {
-      if (j < n_units) issue_sb(j, ptile, pkblk);
-      else cp_async_commit();
-      if (++pkblk == p.kb) {
-        pkblk = 0;
-        ++ptile;
-      }
-    }
     bool ok = true;
     for (int i = 0; i < n_units && ok; ++i) {
       const int s = i % S, d = i % D;
-      if (i + SB - 1 < n_units) issue_sb((i + SB - 1) % SB, ptile, pkblk);
-      else cp_async_commit();  // (empty group: the wait below counts groups)
-      if (++pkblk == p.kb) {
-        pkblk = 0;
-        ++ptile;
-      }
-      cp_async_wait<SB - 1>();  // unit i's group has landed
-      const uint32_t* sbp = sb_ring + ((i % SB) * (kDeqWarps * 32) + dq) * 2;
-      const __nv_bfloat162 sc2 = u32_as_bf162(sbp[0]), bi2 = u32_as_bf162(sbp[1]);
       ok = mbar_wait(&full_bar[s], static_cast<uint32_t>(i / S) & 1u, 6);
-      if (ok && i >= D) ok = mbar_wait(&tfree[d], static_cast<uint32_t>(i / D - 1) & 1u, 9);
+      // (a ring of S <= D stages: the stage's arrival already proves the
+      // MMAs of unit i - D, and with them TMEM buffer d, done)
+      if constexpr (S > D)
+        if (ok && i >= D) ok = mbar_wait(&tfree[d], static_cast<uint32_t>(i / D - 1) & 1u, 9);
       ok = __all_sync(0xffffffffu, ok);  // the TMEM stores below are warp-wide
       if (!ok) break;
       tc_fence_after();
-      const uint8_t* rowp = stage_base + s * C::kStageBytes + C::kWOff + r * 64;
+      const uint8_t* stg = stage_base + s * C::kStageBytes;
+      const uint8_t* rowp = stg + C::kWOff + r * 64;
       const int sw = (r >> 1) & 3;
+      // this row's scale pair and bias pair, and all four packed chunks,
+      // loaded before the first TMEM store
+      const uint2 sbv = *reinterpret_cast<const uint2*>(stg + C::kSbOff + r * 8);
+      const __nv_bfloat162 sc2 = u32_as_bf162(sbv.x), bi2 = u32_as_bf162(sbv.y);
+      uint4 pc[4];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) pc[c] = *reinterpret_cast<const uint4*>(rowp + (((4 * h + c) ^ sw) << 4));
 #pragma unroll
       for (int gq = 0; gq < 2; ++gq) {  // group 2h + gq: 8 words, 32 TMEM columns
-        const uint4 pa = *reinterpret_cast<const uint4*>(rowp + (((4 * h + 2 * gq) ^ sw) << 4));
-        const uint4 pb = *reinterpret_cast<const uint4*>(rowp + (((4 * h + 2 * gq + 1) ^ sw) << 4));
+        const uint4 pa = pc[2 * gq], pb = pc[2 * gq + 1];
         const __nv_bfloat16 sc = gq ? __high2bfloat16(sc2) : __low2bfloat16(sc2);
         const __nv_bfloat16 bi = gq ? __high2bfloat16(bi2) : __low2bfloat16(bi2);
         const __nv_bfloat162 s2 = __halves2bfloat162(sc, sc), b2 = __halves2bfloat162(bi, bi);
@@ -533,7 +489,6 @@ __global__ void __launch_bounds__(Q4 ? kGemmThreadsQ4 : kGemmThreads, Q4 ? 2 : 1
       __syncwarp();
       if (lane == 0) mbar_arrive(&deq_full[d]);
     }
-    cp_async_wait<0>();  // no copy outlives the CTA
   } else {
     // ------------------------------------------------------------ epilogue
     // Processes the 128 x TPAD accumulator in chunks of 8 tree rows (TMEM
@@ -953,8 +908,13 @@ int gemm_plan(GemmPlan* plan, const void* w, int n_out, int k, const void* x, in
               int epi, int grid);
 // 4-bit affine weights (MLX layout): packed uint32 [n_out][k/8], bf16
 // scales / biases [n_out][k/64]; epilogues kEpiStore, kEpiPartial, kEpiSwiglu
-int gemm_plan_q4(GemmPlan* plan, const void* w_packed, const void* scales, const void* biases, int n_out, int k,
-                 const void* x, int t_pad, int x_row_stride_elems, int epi, int grid);
+// q4 plan: sb = the weight's scale / bias blocks from q4_sb_repack_launch
+int gemm_plan_q4(GemmPlan* plan, const void* w_packed, const void* sb, int n_out, int k, const void* x, int t_pad,
+                 int x_row_stride_elems, int epi, int grid);
+// bytes of a [n_out][k] weight's repacked scale / bias blocks, and the
+// repack of MLX scales / biases bf16 [n_out][k/64] into them
+size_t q4_sb_bytes(int n_out, int k);
+int q4_sb_repack_launch(const void* scales, const void* biases, int n_out, int k, void* sb, cudaStream_t stream);
 size_t gemm_ws_counter_bytes();  // the counter block at the start of a workspace (zero between launches)
 // 4-bit affine weights (MLX layout) -> bf16 [n_out][k]
 int dequant_q4_launch(const void* packed, const void* scales, const void* biases, int n_out, int k, void* out,

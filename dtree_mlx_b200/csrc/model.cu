@@ -18,6 +18,7 @@
 // by the RMSNorm kernel that follows anyway, so the GEMM has no reduction
 // tail.
 #include <algorithm>
+#include <array>
 #include <cmath>
 #include <vector>
 
@@ -64,6 +65,9 @@ struct dtree_qwen3_model {
   dtree_qwen3_desc d;
   std::vector<dtree_qwen3_layer> layers;
   std::vector<dtree_qwen3_q4_layer> q4_layers;
+  // 4-bit: per layer the repacked scale / bias blocks of qkv, o, gate|up,
+  // down (in the workspace, filled at creation)
+  std::vector<std::array<const void*, 4>> q4_sb;
   dtree::PlanSet plans[5];
   void* gemm_ws = nullptr;
   size_t gemm_ws_bytes = 0;
@@ -91,6 +95,16 @@ static int proj_split(const dtree_qwen3_desc& d, int n_out) {
   return std::max(1, std::min(kMaxProjSplit, 2 * num_sms() / tiles));
 }
 static int qkv_width(const dtree_qwen3_desc& d) { return (d.n_heads + 2 * d.n_kv_heads) * d.head_dim; }
+// the four projections of a layer as (rows N, K)
+static std::array<std::pair<int, int>, 4> layer_shapes(const dtree_qwen3_desc& d) {
+  return {{{qkv_width(d), d.hidden}, {d.hidden, d.n_heads * d.head_dim}, {2 * d.ffn, d.hidden}, {d.hidden, d.ffn}}};
+}
+static size_t q4_sb_need(const dtree_qwen3_desc& d) {
+  if (d.quant_bits != 4) return 0;
+  size_t b = 0;
+  for (const auto& nk : layer_shapes(d)) b += (q4_sb_bytes(nk.first, nk.second) + 255) & ~static_cast<size_t>(255);
+  return b * d.layers;
+}
 static size_t partials_need(const dtree_qwen3_desc& d) {
   const size_t a = static_cast<size_t>(proj_split(d, d.hidden)) * d.hidden;
   const size_t b = static_cast<size_t>(proj_split(d, qkv_width(d))) * qkv_width(d);
@@ -111,24 +125,18 @@ static int build_plans(dtree_qwen3_model* m, int t_pad) {
   for (int l = 0; l < d.layers; ++l) {
     const dtree_qwen3_layer& L = m->layers[l];
     // bf16 or MLX 4-bit weights behind the same plan
-    auto plan = [&](GemmPlan* g, const void* w, const void* sc, const void* bi, int n, int k, const void* x,
-                    int epi, int grid) {
-      return q4 ? gemm_plan_q4(g, w, sc, bi, n, k, x, t_pad, k, epi, grid)
+    auto plan = [&](GemmPlan* g, const void* w, const void* sb_w, int n, int k, const void* x, int epi, int grid) {
+      return q4 ? gemm_plan_q4(g, w, sb_w, n, k, x, t_pad, k, epi, grid)
                 : gemm_plan(g, w, n, k, x, t_pad, k, epi, grid);
     };
-    const dtree_qwen3_q4_layer Q = q4 ? m->q4_layers[l] : dtree_qwen3_q4_layer{};
+    const std::array<const void*, 4> sb = q4 ? m->q4_sb[l] : std::array<const void*, 4>{};
     int rc;
-    if ((rc = plan(&ps.qkv[l], L.qkv, Q.qkv_scales, Q.qkv_biases, qkv_rows, d.hidden, d.xn, kEpiPartial,
-                   proj_split(d, qkv_rows))))
+    if ((rc = plan(&ps.qkv[l], L.qkv, sb[0], qkv_rows, d.hidden, d.xn, kEpiPartial, proj_split(d, qkv_rows))))
       return rc;
-    if ((rc = plan(&ps.o[l], L.o_proj, Q.o_scales, Q.o_biases, d.hidden, qd, d.attn, kEpiPartial,
-                   proj_split(d, d.hidden))))
+    if ((rc = plan(&ps.o[l], L.o_proj, sb[1], d.hidden, qd, d.attn, kEpiPartial, proj_split(d, d.hidden))))
       return rc;
-    if ((rc = plan(&ps.gu[l], L.gate_up, Q.gate_up_scales, Q.gate_up_biases, 2 * d.ffn, d.hidden, d.xn, kEpiSwiglu,
-                   0)))
-      return rc;
-    if ((rc = plan(&ps.down[l], L.down, Q.down_scales, Q.down_biases, d.hidden, d.ffn, d.act, kEpiPartial,
-                   proj_split(d, d.hidden))))
+    if ((rc = plan(&ps.gu[l], L.gate_up, sb[2], 2 * d.ffn, d.hidden, d.xn, kEpiSwiglu, 0))) return rc;
+    if ((rc = plan(&ps.down[l], L.down, sb[3], d.hidden, d.ffn, d.act, kEpiPartial, proj_split(d, d.hidden))))
       return rc;
     if (ps.o[l].p.split > kMaxProjSplit || ps.down[l].p.split > kMaxProjSplit || ps.qkv[l].p.split > kMaxProjSplit)
       return fail(kErrUnsupported, "projection split exceeds the partial buffer");
@@ -164,7 +172,7 @@ extern "C" int dtree_qwen3_buffer_bytes(const dtree_qwen3_desc* d, size_t out[9]
   out[7] = tc * d->hidden * (d->n_capture > 0 ? d->n_capture : 1) * 2;
   out[8] = ((gemm_ws_need(*d) + 255) & ~static_cast<size_t>(255)) +
            ((attn_ws_need(*d) + 255) & ~static_cast<size_t>(255)) + ((partials_need(*d) + 255) & ~static_cast<size_t>(255)) +
-           fused_ws_bytes(*d);
+           ((fused_ws_bytes(*d) + 255) & ~static_cast<size_t>(255)) + q4_sb_need(*d);
   return kOk;
 }
 
@@ -213,6 +221,38 @@ extern "C" int dtree_qwen3_create(const dtree_qwen3_desc* desc, dtree_qwen3_mode
   m->attn_ws_bytes = attn_ws_need(d);
   m->proj_partials = reinterpret_cast<float*>(static_cast<char*>(m->attn_ws) +
                                               ((m->attn_ws_bytes + 255) & ~static_cast<size_t>(255)));
+  if (d.quant_bits == 4) {
+    // the scale / bias blocks of every 4-bit projection, after the other
+    // workspace regions (the weights must be complete: wait for the device)
+    char* sbp = reinterpret_cast<char*>(m->proj_partials) + ((partials_need(d) + 255) & ~static_cast<size_t>(255)) +
+                ((fused_ws_bytes(d) + 255) & ~static_cast<size_t>(255));
+    cudaError_t e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) {
+      delete m;
+      return fail(kErrCuda, std::string("dtree_qwen3_create (4-bit repack): ") + cudaGetErrorString(e));
+    }
+    const auto shapes = layer_shapes(d);
+    m->q4_sb.resize(d.layers);
+    for (int l = 0; l < d.layers; ++l) {
+      const dtree_qwen3_q4_layer& Q = m->q4_layers[l];
+      const void* sc[4] = {Q.qkv_scales, Q.o_scales, Q.gate_up_scales, Q.down_scales};
+      const void* bi[4] = {Q.qkv_biases, Q.o_biases, Q.gate_up_biases, Q.down_biases};
+      for (int j = 0; j < 4; ++j) {
+        int rc = q4_sb_repack_launch(sc[j], bi[j], shapes[j].first, shapes[j].second, sbp, nullptr);
+        if (rc) {
+          delete m;
+          return rc;
+        }
+        m->q4_sb[l][j] = sbp;
+        sbp += (q4_sb_bytes(shapes[j].first, shapes[j].second) + 255) & ~static_cast<size_t>(255);
+      }
+    }
+    e = cudaStreamSynchronize(nullptr);
+    if (e != cudaSuccess) {
+      delete m;
+      return fail(kErrCuda, std::string("dtree_qwen3_create (4-bit repack): ") + cudaGetErrorString(e));
+    }
+  }
   if (d.verify_path == 1 && fused_supported(d)) {
     m->fused_ws = reinterpret_cast<char*>(m->proj_partials) + ((partials_need(d) + 255) & ~static_cast<size_t>(255));
     std::vector<std::pair<int, __nv_bfloat16*>> caps;

@@ -192,8 +192,8 @@ def linear_q4(x: torch.Tensor, w, out: torch.Tensor | None = None, split_k: int 
         raise ValueError(f"x has K={k} but w has K={kw}")
     if out is None:
         out = torch.empty(t_pad, n, dtype=torch.bfloat16, device=x.device)
-    nbytes = int(_lib.load().dtree_linear_workspace_bytes(t_pad, n))
-    ws = _workspace(("gemm", t_pad), nbytes, x.device)
+    nbytes = int(_lib.load().dtree_linear_q4_workspace_bytes(t_pad, n, k))
+    ws = _workspace(("gemm_q4", t_pad, n, k), nbytes, x.device)
     call("dtree_linear_q4", ptr(x), t_pad, k, ptr(w.packed), ptr(w.scales), ptr(w.biases), n, ptr(out), ptr(ws),
          ws.numel(), int(split_k), stream_ptr())
     return out

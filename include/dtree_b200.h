@@ -197,9 +197,12 @@ DTREE_API int dtree_linear_bf16(const void* x, int t_pad, int k, const void* w, 
  * quantize_model(bits=4, group_size=64) puts in the target (api.py:46-54;
  * mx.quantized_matmul(transpose=True), also adapters.py:63-71).  MLX layout:
  * w_packed uint32 [n][k/8], element 8j+i of a row in bits 4i..4i+3 of word
- * j; scales, biases bf16 [n][k/64].  The weights are dequantized into shared
+ * j; scales, biases bf16 [n][k/64].  The weights are dequantized into tensor
  * memory (one bf16 rounding of scale*q + bias) and fed to the same tcgen05
- * GEMM as dtree_linear_bf16.  k % 64 == 0; workspace as dtree_linear_bf16. */
+ * GEMM as dtree_linear_bf16.  k % 64 == 0.  workspace:
+ * dtree_linear_q4_workspace_bytes(t_pad, n, k) (the GEMM's, plus the scales
+ * and biases repacked for this call into 1 KB blocks per 128 rows x 128 K). */
+DTREE_API size_t dtree_linear_q4_workspace_bytes(int t_pad, int n, int k);
 DTREE_API int dtree_linear_q4(const void* x, int t_pad, int k, const void* w_packed, const void* scales,
                     const void* biases, int n, void* y, void* workspace, size_t workspace_bytes, int split_k,
                     void* stream);
@@ -360,7 +363,11 @@ typedef struct dtree_qwen3_desc {
 typedef struct dtree_qwen3_model dtree_qwen3_model;
 
 /* Bytes each caller buffer must hold: out[0..8] = kv_cache, h, xn, q, attn,
- * act, norm_out, capture, workspace. */
+ * act, norm_out, capture, workspace.  With quant_bits == 4 the workspace
+ * also holds every projection's scales and biases repacked into 1 KB blocks
+ * (128 rows x 128 K); dtree_qwen3_create fills them from q4_layer after a
+ * device synchronize, so the weights must be complete when it is called and
+ * later changes to the scales / biases need a new model. */
 DTREE_API int dtree_qwen3_buffer_bytes(const dtree_qwen3_desc* desc, size_t out[9]);
 DTREE_API int dtree_qwen3_create(const dtree_qwen3_desc* desc, dtree_qwen3_model** out);
 DTREE_API int dtree_qwen3_destroy(dtree_qwen3_model* model);
