@@ -107,6 +107,9 @@ class Qwen3Desc(C.Structure):
         ("group_size", C.c_int),
         ("q4_layer", C.POINTER(Qwen3Q4Layer)),
         ("verify_path", C.c_int),
+        ("embed_q4_packed", C.c_void_p),
+        ("embed_q4_scales", C.c_void_p),
+        ("embed_q4_biases", C.c_void_p),
     ]
 
 

@@ -129,8 +129,8 @@ int gemm_plan_q4(GemmPlan* plan, const void* w_packed, const void* sb, int n_out
                  int x_row_stride_elems, int epi, int grid) {
   DTREE_CHECK_ARG(w_packed && sb, "null q4 weight pointer");
   DTREE_CHECK_ARG(reinterpret_cast<uintptr_t>(sb) % 16 == 0, "q4 scale / bias blocks must be 16-byte aligned");
-  DTREE_CHECK_ARG(epi == kEpiStore || epi == kEpiPartial || epi == kEpiSwiglu,
-                  "q4 GEMM supports the store, split-K partial and SwiGLU epilogues");
+  DTREE_CHECK_ARG(epi == kEpiStore || epi == kEpiPartial || epi == kEpiSwiglu || epi == kEpiArgmax,
+                  "q4 GEMM supports the store, split-K partial, SwiGLU and argmax epilogues");
   int rc = plan_common(plan, n_out, k, x, t_pad, x_row_stride_elems, epi, grid, false, 64 * kQ4Kb);
   if (rc) return rc;
   // packed weight map: box 8 * kQ4Kb words (one stream-K unit of K, 64 B)
@@ -254,6 +254,7 @@ static int launch_epi(const GemmPlan& pl, cudaStream_t st) {
       case kEpiStore: return launch_t<TPAD, kEpiStore, true>(pl, st);
       case kEpiSwiglu: return launch_t<TPAD, kEpiSwiglu, true>(pl, st);
       case kEpiPartial: return launch_t<TPAD, kEpiPartial, true>(pl, st);
+      case kEpiArgmax: return launch_t<TPAD, kEpiArgmax, true>(pl, st);
     }
     return fail(kErrInvalidArg, "epilogue not available for q4 weights");
   }

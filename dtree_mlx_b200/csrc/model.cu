@@ -68,6 +68,7 @@ struct dtree_qwen3_model {
   // 4-bit: per layer the repacked scale / bias blocks of qkv, o, gate|up,
   // down (in the workspace, filled at creation)
   std::vector<std::array<const void*, 4>> q4_sb;
+  const void* embed_sb = nullptr;  // 4-bit LM head: the embedding's blocks
   dtree::PlanSet plans[5];
   void* gemm_ws = nullptr;
   size_t gemm_ws_bytes = 0;
@@ -100,10 +101,12 @@ static std::array<std::pair<int, int>, 4> layer_shapes(const dtree_qwen3_desc& d
   return {{{qkv_width(d), d.hidden}, {d.hidden, d.n_heads * d.head_dim}, {2 * d.ffn, d.hidden}, {d.hidden, d.ffn}}};
 }
 static size_t q4_sb_need(const dtree_qwen3_desc& d) {
-  if (d.quant_bits != 4) return 0;
   size_t b = 0;
-  for (const auto& nk : layer_shapes(d)) b += (q4_sb_bytes(nk.first, nk.second) + 255) & ~static_cast<size_t>(255);
-  return b * d.layers;
+  if (d.quant_bits == 4)
+    for (const auto& nk : layer_shapes(d)) b += (q4_sb_bytes(nk.first, nk.second) + 255) & ~static_cast<size_t>(255);
+  b *= d.layers;
+  if (d.embed_q4_packed) b += (q4_sb_bytes(d.vocab, d.hidden) + 255) & ~static_cast<size_t>(255);
+  return b;
 }
 static size_t partials_need(const dtree_qwen3_desc& d) {
   const size_t a = static_cast<size_t>(proj_split(d, d.hidden)) * d.hidden;
@@ -143,10 +146,17 @@ static int build_plans(dtree_qwen3_model* m, int t_pad) {
     for (GemmPlan* g : {&ps.qkv[l], &ps.o[l], &ps.gu[l], &ps.down[l]})
       if ((rc = gemm_bind_ws(g, m->gemm_ws, m->gemm_ws_bytes))) return rc;
   }
-  int rc = gemm_plan(&ps.lm, d.embed, d.vocab, d.hidden, d.norm_out, t_pad, d.hidden, kEpiArgmax, 0);
+  // LM head: the bf16 embedding, or the 4-bit one (stream-K over both CTA
+  // slots of every SM)
+  int rc = m->embed_sb ? gemm_plan_q4(&ps.lm, d.embed_q4_packed, m->embed_sb, d.vocab, d.hidden, d.norm_out, t_pad,
+                                      d.hidden, kEpiArgmax, 2 * num_sms())
+                       : gemm_plan(&ps.lm, d.embed, d.vocab, d.hidden, d.norm_out, t_pad, d.hidden, kEpiArgmax, 0);
   if (rc) return rc;
   if ((rc = gemm_bind_ws(&ps.lm, m->gemm_ws, m->gemm_ws_bytes))) return rc;
-  if ((rc = gemm_plan(&ps.lm_logits, d.embed, d.vocab, d.hidden, d.norm_out, t_pad, d.hidden, kEpiPartial, 1)))
+  if ((rc = m->embed_sb ? gemm_plan_q4(&ps.lm_logits, d.embed_q4_packed, m->embed_sb, d.vocab, d.hidden, d.norm_out,
+                                       t_pad, d.hidden, kEpiPartial, 1)
+                        : gemm_plan(&ps.lm_logits, d.embed, d.vocab, d.hidden, d.norm_out, t_pad, d.hidden, kEpiPartial,
+                                    1)))
     return rc;
   if ((rc = gemm_bind_ws(&ps.lm_logits, m->gemm_ws, m->gemm_ws_bytes))) return rc;
   ps.ready = true;
@@ -207,6 +217,8 @@ extern "C" int dtree_qwen3_create(const dtree_qwen3_desc* desc, dtree_qwen3_mode
                       "null q4 scales / biases");
     }
   }
+  DTREE_CHECK_ARG(!d.embed_q4_packed || (d.embed_q4_scales && d.embed_q4_biases),
+                  "a 4-bit LM head needs embed_q4_scales and embed_q4_biases");
   auto* m = new dtree_qwen3_model();
   m->d = d;
   m->layers.assign(d.layer, d.layer + d.layers);
@@ -221,9 +233,10 @@ extern "C" int dtree_qwen3_create(const dtree_qwen3_desc* desc, dtree_qwen3_mode
   m->attn_ws_bytes = attn_ws_need(d);
   m->proj_partials = reinterpret_cast<float*>(static_cast<char*>(m->attn_ws) +
                                               ((m->attn_ws_bytes + 255) & ~static_cast<size_t>(255)));
-  if (d.quant_bits == 4) {
-    // the scale / bias blocks of every 4-bit projection, after the other
-    // workspace regions (the weights must be complete: wait for the device)
+  if (d.quant_bits == 4 || d.embed_q4_packed) {
+    // the scale / bias blocks of every 4-bit projection (and of a 4-bit LM
+    // head), after the other workspace regions (the weights must be
+    // complete: wait for the device)
     char* sbp = reinterpret_cast<char*>(m->proj_partials) + ((partials_need(d) + 255) & ~static_cast<size_t>(255)) +
                 ((fused_ws_bytes(d) + 255) & ~static_cast<size_t>(255));
     cudaError_t e = cudaDeviceSynchronize();
@@ -232,8 +245,8 @@ extern "C" int dtree_qwen3_create(const dtree_qwen3_desc* desc, dtree_qwen3_mode
       return fail(kErrCuda, std::string("dtree_qwen3_create (4-bit repack): ") + cudaGetErrorString(e));
     }
     const auto shapes = layer_shapes(d);
-    m->q4_sb.resize(d.layers);
-    for (int l = 0; l < d.layers; ++l) {
+    m->q4_sb.resize(d.quant_bits == 4 ? d.layers : 0);
+    for (int l = 0; l < static_cast<int>(m->q4_sb.size()); ++l) {
       const dtree_qwen3_q4_layer& Q = m->q4_layers[l];
       const void* sc[4] = {Q.qkv_scales, Q.o_scales, Q.gate_up_scales, Q.down_scales};
       const void* bi[4] = {Q.qkv_biases, Q.o_biases, Q.gate_up_biases, Q.down_biases};
@@ -246,6 +259,14 @@ extern "C" int dtree_qwen3_create(const dtree_qwen3_desc* desc, dtree_qwen3_mode
         m->q4_sb[l][j] = sbp;
         sbp += (q4_sb_bytes(shapes[j].first, shapes[j].second) + 255) & ~static_cast<size_t>(255);
       }
+    }
+    if (d.embed_q4_packed) {
+      int rc = q4_sb_repack_launch(d.embed_q4_scales, d.embed_q4_biases, d.vocab, d.hidden, sbp, nullptr);
+      if (rc) {
+        delete m;
+        return rc;
+      }
+      m->embed_sb = sbp;
     }
     e = cudaStreamSynchronize(nullptr);
     if (e != cudaSuccess) {
@@ -740,7 +761,10 @@ extern "C" int dtree_qwen3_prefill(dtree_qwen3_model* m, const int32_t* tokens, 
                            bf(d.final_norm), lm_in, d.hidden, 1, 16, d.rms_eps, st)))
     return rc;
   GemmPlan g;
-  if ((rc = gemm_plan(&g, d.embed, d.vocab, d.hidden, lm_in, 16, d.hidden, kEpiArgmax, 0))) return rc;
+  if ((rc = m->embed_sb ? gemm_plan_q4(&g, d.embed_q4_packed, m->embed_sb, d.vocab, d.hidden, lm_in, 16, d.hidden,
+                                      kEpiArgmax, 0)
+                        : gemm_plan(&g, d.embed, d.vocab, d.hidden, lm_in, 16, d.hidden, kEpiArgmax, 0)))
+    return rc;
   if ((rc = gemm_bind_ws(&g, gws, gws_bytes))) return rc;
   g.p.n_rows = 1;
   g.p.vocab = d.vocab;

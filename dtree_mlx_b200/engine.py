@@ -108,6 +108,9 @@ class Qwen3Engine:
         for i, l in enumerate(self.layer_ids):
             d.capture_layers[i] = l
         d.embed, d.final_norm = ptr(weights.embed), ptr(weights.final_norm)
+        eq = getattr(weights, "embed_q4", None)
+        if eq is not None:  # 4-bit tied LM head
+            d.embed_q4_packed, d.embed_q4_scales, d.embed_q4_biases = ptr(eq.packed), ptr(eq.scales), ptr(eq.biases)
         d.layer = C.cast(self._layers, C.POINTER(Qwen3Layer))
         if self._q4 is not None:
             d.quant_bits, d.group_size = 4, 64

@@ -120,6 +120,9 @@ class Qwen3Weights:
     post_norm: list[torch.Tensor] = field(default_factory=list)
     gate_up: list[torch.Tensor] = field(default_factory=list)
     down: list[torch.Tensor] = field(default_factory=list)
+    # 4-bit tied LM head (quantize_model quantizes the embedding too); `embed`
+    # then holds its dequantized rows, the table input tokens are looked up in
+    embed_q4: Q4Tensor | None = None
 
     @property
     def device(self) -> torch.device:
@@ -130,7 +133,7 @@ class Qwen3Weights:
         return 4 if isinstance(self.qkv[0], Q4Tensor) else 16
 
     def nbytes(self) -> int:
-        ts = [self.embed, self.final_norm]
+        ts = [self.embed, self.final_norm] + ([self.embed_q4] if self.embed_q4 is not None else [])
         for name in ("input_norm", "qkv", "q_norm", "k_norm", "o_proj", "post_norm", "gate_up", "down"):
             ts += getattr(self, name)
         return sum(tensor_bytes(t) for t in ts)
@@ -138,7 +141,8 @@ class Qwen3Weights:
     def streamed_bytes(self) -> int:
         """Bytes one verify forward must read: embedding (tied LM head) + the
         four projections of every layer (norm vectors are negligible)."""
-        ts = [self.embed, *self.qkv, *self.o_proj, *self.gate_up, *self.down]
+        head = self.embed_q4 if self.embed_q4 is not None else self.embed
+        ts = [head, *self.qkv, *self.o_proj, *self.gate_up, *self.down]
         return sum(tensor_bytes(t) for t in ts)
 
     def reference_weights(self, layer: int) -> dict:
@@ -167,17 +171,26 @@ class Qwen3Weights:
         w = Qwen3Weights(self.cfg, mv(self.embed), mv(self.final_norm))
         for name in ("input_norm", "qkv", "q_norm", "k_norm", "o_proj", "post_norm", "gate_up", "down"):
             setattr(w, name, [mv(t) for t in getattr(self, name)])
+        if self.embed_q4 is not None:
+            w.embed_q4 = mv(self.embed_q4)
         return w
 
 
 def quantize_weights(w: Qwen3Weights, bits: int = 4, group_size: int = 64) -> Qwen3Weights:
     """The target after ``quantize_model(model, bits, group_size)``
     (dtree_mlx/api.py:46-54): every layer's q/k/v, o, gate/up and down
-    projections become 4-bit affine; embedding and norms are kept."""
+    projections become 4-bit affine, and so does the embedding (mlx-lm
+    quantizes every module with ``to_quantized``, ``nn.Embedding`` included),
+    which makes the tied LM head a 4-bit matmul (``as_linear``,
+    adapters.py:491); the lookup table is its dequantized rows.  Norms are
+    kept."""
     if bits != 4 or group_size != 64:
         raise NotImplementedError("only 4-bit affine weights with group_size 64 are supported")
-    q = Qwen3Weights(w.cfg, w.embed, w.final_norm, list(w.input_norm), [], list(w.q_norm), list(w.k_norm), [],
-                     list(w.post_norm), [], [])
+    from .weights_io import dequantize_q4
+
+    emb_q = quantize_affine_q4(w.embed, group_size)
+    q = Qwen3Weights(w.cfg, dequantize_q4(emb_q), w.final_norm, list(w.input_norm), [], list(w.q_norm),
+                     list(w.k_norm), [], list(w.post_norm), [], [], embed_q4=emb_q)
     for name in ("qkv", "o_proj", "gate_up", "down"):
         setattr(q, name, [quantize_affine_q4(t, group_size) for t in getattr(w, name)])
     return q

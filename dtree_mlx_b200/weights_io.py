@@ -10,8 +10,8 @@ straight into the engine's packed layouts:
   ``model.embed_tokens`` (tied LM head) and ``model.norm``.  MLX 4-bit
   layers (``.weight`` uint32 [out, in/8] + ``.scales`` / ``.biases`` bf16
   [out, in/64], mlx ``quantize`` layout) load as ``Q4Tensor``; a quantized
-  embedding is dequantized to bf16 (the verify engine's tied LM head is
-  bf16).
+  embedding is kept as the 4-bit tied LM head and its dequantized bf16 rows
+  become the lookup table.
 * Qwen3.5 (``model_type`` "qwen3_5", the text model of a "text_config"
   checkpoint): the reference's ``sanitize`` rules
   (custom_qwen35_model.py:1251-1275, 1365-1379) -- vision / ``mtp.`` tensors
@@ -189,12 +189,13 @@ def qwen3_weights_from_tensors(config: dict, t: dict[str, torch.Tensor], device=
     if q and int(q.get("bits", 4)) != 4:
         raise ValueError("only 4-bit MLX quantization is supported")
     emb = _linear(t, "model.embed_tokens", device, gs)
+    emb_q = None
     if isinstance(emb, Q4Tensor):
-        emb = dequantize_q4(emb)
+        emb_q, emb = emb, dequantize_q4(emb)
     if not cfg.tie_word_embeddings and "lm_head.weight" in t:
         raise NotImplementedError("untied LM heads are not supported by the verify engine (the tied head is "
                                   "the embedding)")
-    w = Qwen3Weights(cfg, embed=_bf16(emb, device), final_norm=_bf16(t["model.norm.weight"], device))
+    w = Qwen3Weights(cfg, embed=_bf16(emb, device), final_norm=_bf16(t["model.norm.weight"], device), embed_q4=emb_q)
     for i in range(cfg.num_hidden_layers):
         p = f"model.layers.{i}."
         lin = lambda n: _linear(t, p + n, device, gs)  # noqa: E731
@@ -226,6 +227,8 @@ def save_qwen3_mlx(w: Qwen3Weights, path: str | Path) -> None:
     c = w.cfg
     out: dict[str, torch.Tensor] = {"model.embed_tokens.weight": w.embed, "model.norm.weight": w.final_norm}
     u32: set[str] = set()
+    if w.embed_q4 is not None:
+        _put_linear(out, "model.embed_tokens", w.embed_q4, u32)
     for i in range(c.num_hidden_layers):
         r = w.reference_weights(i)
         p = f"model.layers.{i}."

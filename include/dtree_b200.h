@@ -358,6 +358,15 @@ typedef struct dtree_qwen3_desc {
    * through the glue phases) where the model supports it (bf16 weights,
    * head_dim 128, <= 64 tree rows), else the chain */
   int verify_path;
+  /* 4-bit tied LM head: mlx-lm's quantize_model (api.py:46-54) quantizes
+   * the embedding too, so the reference's LM head of a 4-bit target is the
+   * quantized embedding's as_linear (adapters.py:491).  MLX packed
+   * [vocab][hidden/8] and bf16 scales / biases [vocab][hidden/64]; all null:
+   * the bf16 `embed` is the LM head.  `embed` stays the table the input rows
+   * are gathered from (the dequantized rows for a 4-bit embedding). */
+  const void* embed_q4_packed;
+  const void* embed_q4_scales;
+  const void* embed_q4_biases;
 } dtree_qwen3_desc;
 
 typedef struct dtree_qwen3_model dtree_qwen3_model;

@@ -69,12 +69,15 @@ def test_qwen3_checkpoint_roundtrip(tmp_path, quant):
     mt, back = W.load_target_weights(tmp_path, device="cpu")
     assert mt == "qwen3" and back.cfg == w.cfg and back.quant_bits == w.quant_bits
     assert _same(back.embed, w.embed) and _same(back.final_norm, w.final_norm)
+    assert (back.embed_q4 is None) == (not quant)
+    if quant:  # the 4-bit tied LM head survives the round trip
+        assert _same(back.embed_q4, w.embed_q4)
     for name in ("input_norm", "qkv", "q_norm", "k_norm", "o_proj", "post_norm", "gate_up", "down"):
         for a, b in zip(getattr(back, name), getattr(w, name)):
             assert _same(a, b), name
 
 
-def test_qwen3_quantized_embedding_is_dequantized(tmp_path):
+def test_qwen3_quantized_embedding_is_lm_head_and_lookup(tmp_path):
     w = random_qwen3_weights(PRESETS["qwen3-tiny"], seed=2, device="cpu")
     W.save_qwen3_mlx(w, tmp_path)
     raw = W.read_safetensors(tmp_path / "model.safetensors")
@@ -83,7 +86,10 @@ def test_qwen3_quantized_embedding_is_dequantized(tmp_path):
     raw["model.embed_tokens.biases"] = q.biases
     cfg = json.loads((tmp_path / "config.json").read_text())
     back = W.qwen3_weights_from_tensors(cfg, raw, device="cpu")
+    # lookups read the dequantized rows; the 4-bit form is the tied LM head
     assert torch.equal(back.embed, W.dequantize_q4(q))
+    assert torch.equal(back.embed_q4.packed, q.packed) and torch.equal(back.embed_q4.scales, q.scales)
+    assert torch.equal(back.embed_q4.biases, q.biases)
 
 
 def test_qwen35_hf_checkpoint_sanitized_roundtrip(tmp_path):
