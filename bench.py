@@ -56,8 +56,8 @@ WORKLOADS = {
     "qwen35-9b": "BASELINE config 4: Qwen3.5-9B-style hybrid (24 gated DeltaNet + 8 gated attention layers) DTree, "
                  "prompt 2048, 512 new tokens, spec 16, budget 24",
     16: "BASELINE config 1: Qwen3-4B-shape DTree, prompt 256, 512 new tokens, spec 16, budget 24",
-    4: "BASELINE config 3: Qwen3-4B-shape DTree with MLX affine 4-bit projections (group 64), prompt 256, "
-       "512 new tokens, spec 16, budget 24",
+    4: "BASELINE config 3: Qwen3-4B-shape DTree with MLX affine 4-bit projections (group 64; embedding / tied "
+       "LM head bf16), prompt 256, 512 new tokens, spec 16, budget 24",
 }
 UNIT = "tokens/s"
 
@@ -172,7 +172,8 @@ def run_ours(args, rank, world, local, dist) -> dict | None:
     dev = torch.device("cuda", local)
     target = load_target_model(f"synthetic:{PRESET}:seed=0:kv={KV_CAP}")
     if args.quant_bits == 4:
-        quantize_target_model(target, 4, 64)
+        # all linear layers except the embedding
+        quantize_target_model(target, 4, 64, embedding=False)
     cfg = target.model.cfg
     drafter = PlantedDrafter(seed=1000 + rank, p_correct=P_CORRECT, block_size=SPEC)
     gen = DFlashGenerator.from_components(target, drafter)

@@ -582,9 +582,11 @@ def parse_synthetic_spec(spec: str) -> dict:
     return out
 
 
-def quantize_target_model(target: "LoadedTargetModel", bits: int = 4, group_size: int = 64) -> dict:
+def quantize_target_model(target: "LoadedTargetModel", bits: int = 4, group_size: int = 64,
+                          embedding: bool = True) -> dict:
     """``quantize_model`` on a loaded target (api.py:46-54): its projections
-    become MLX affine 4-bit, engines built for the bf16 weights are released.
+    and (``embedding``, as mlx-lm does) its embedding / tied LM head become
+    MLX affine 4-bit; engines built for the bf16 weights are released.
     Returns the ``quantization`` config entry."""
     from .synthetic import Qwen35Weights, quantize_weights
 
@@ -594,7 +596,7 @@ def quantize_target_model(target: "LoadedTargetModel", bits: int = 4, group_size
     for eng in list(model.engines.values()):
         eng.close()
     model.engines.clear()
-    model.weights = quantize_weights(model.weights, bits, group_size)
+    model.weights = quantize_weights(model.weights, bits, group_size, embedding=embedding)
     torch.cuda.empty_cache()
     return {"group_size": group_size, "bits": bits}
 

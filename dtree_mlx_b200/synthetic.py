@@ -176,20 +176,26 @@ class Qwen3Weights:
         return w
 
 
-def quantize_weights(w: Qwen3Weights, bits: int = 4, group_size: int = 64) -> Qwen3Weights:
-    """The target after ``quantize_model(model, bits, group_size)``
-    (dtree_mlx/api.py:46-54): every layer's q/k/v, o, gate/up and down
-    projections become 4-bit affine, and so does the embedding (mlx-lm
-    quantizes every module with ``to_quantized``, ``nn.Embedding`` included),
-    which makes the tied LM head a 4-bit matmul (``as_linear``,
-    adapters.py:491); the lookup table is its dequantized rows.  Norms are
-    kept."""
+def quantize_weights(w: Qwen3Weights, bits: int = 4, group_size: int = 64, embedding: bool = False) -> Qwen3Weights:
+    """4-bit affine (MLX layout) q/k/v, o, gate/up and down projections of
+    every layer; norms are kept.  ``embedding=False`` keeps the embedding
+    (and with it the tied LM head) bf16: the BASELINE config-3 target ("all
+    linear layers except embeddings").  ``embedding=True`` is the target
+    after the reference's ``quantize_model(model, bits, group_size)``
+    (dtree_mlx/api.py:46-54): mlx-lm quantizes every module with
+    ``to_quantized``, ``nn.Embedding`` included, so the tied LM head becomes a
+    4-bit matmul (``as_linear``, adapters.py:491) and the lookup table holds
+    the dequantized rows."""
     if bits != 4 or group_size != 64:
         raise NotImplementedError("only 4-bit affine weights with group_size 64 are supported")
-    from .weights_io import dequantize_q4
+    if embedding:
+        from .weights_io import dequantize_q4
 
-    emb_q = quantize_affine_q4(w.embed, group_size)
-    q = Qwen3Weights(w.cfg, dequantize_q4(emb_q), w.final_norm, list(w.input_norm), [], list(w.q_norm),
+        emb_q = quantize_affine_q4(w.embed, group_size)
+        emb = dequantize_q4(emb_q)
+    else:
+        emb_q, emb = w.embed_q4, w.embed
+    q = Qwen3Weights(w.cfg, emb, w.final_norm, list(w.input_norm), [], list(w.q_norm),
                      list(w.k_norm), [], list(w.post_norm), [], [], embed_q4=emb_q)
     for name in ("qkv", "o_proj", "gate_up", "down"):
         setattr(q, name, [quantize_affine_q4(t, group_size) for t in getattr(w, name)])

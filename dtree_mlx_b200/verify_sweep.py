@@ -65,7 +65,7 @@ def measured_hbm_gbs() -> tuple[float, str]:
 
 
 def run(preset: str, layers: int | None, prefixes: list[int], budgets: list[int], iters: int, seed: int = 0,
-        eager_only: bool = False, quant_bits: int = 16) -> list[dict]:
+        eager_only: bool = False, quant_bits: int = 16, q4_embedding: bool = False) -> list[dict]:
     if preset in QWEN35_PRESETS:
         return run_hybrid(preset, layers, prefixes, budgets, iters, seed, eager_only)
     cfg = PRESETS[preset]
@@ -74,7 +74,7 @@ def run(preset: str, layers: int | None, prefixes: list[int], budgets: list[int]
     dev = torch.device("cuda")
     w = random_qwen3_weights(cfg, seed=seed, device=dev)
     if quant_bits == 4:
-        w = quantize_weights(w)
+        w = quantize_weights(w, embedding=q4_embedding)
         torch.cuda.empty_cache()
     eng = Qwen3Engine(w, kv_capacity=max(prefixes) + 160)
     g = torch.Generator(device=dev).manual_seed(seed + 1)
@@ -119,7 +119,8 @@ def run(preset: str, layers: int | None, prefixes: list[int], budgets: list[int]
             results.append({"prefix": P, "tree_budget": budget, "tree_rows": n, "verify_ms": round(ms, 4),
                             "algorithmic_gb": round(nbytes / 1e9, 4), "achieved_gbs": round(gbs, 1),
                             "frac_of_hbm": round(gbs / peak, 4), "peak_gbs": peak, "peak_source": peak_src,
-                            "layers": cfg.num_hidden_layers, "quant_bits": quant_bits})
+                            "layers": cfg.num_hidden_layers, "quant_bits": quant_bits,
+                            "q4_embedding": bool(quant_bits == 4 and q4_embedding)})
             del graph
     eng.close()
     return results
@@ -377,6 +378,9 @@ def main() -> None:
     ap.add_argument("--eager", action="store_true", help="launch eagerly (no CUDA graph), e.g. under a profiler")
     ap.add_argument("--quant-bits", type=int, default=16, choices=[16, 4],
                     help="4: MLX affine 4-bit projections, group 64 (BASELINE config 3)")
+    ap.add_argument("--q4-embedding", action="store_true",
+                    help="with --quant-bits 4: quantize the embedding too (the reference's quantize_model), so the "
+                         "tied LM head runs the 4-bit GEMM")
     ap.add_argument("--json", action="store_true")
     ap.add_argument("--drafter", default=None, help="time one DFlash draft step of this drafter preset and exit")
     ap.add_argument("--prefill", type=int, default=0,
@@ -399,7 +403,7 @@ def main() -> None:
             print(json.dumps({"prefix": p, "tree_budget": b, **row}))
         return
     res = run(a.preset, a.layers, [int(x) for x in a.prefix.split(",")], [int(x) for x in a.budget.split(",")],
-              a.iters, eager_only=a.eager, quant_bits=a.quant_bits)
+              a.iters, eager_only=a.eager, quant_bits=a.quant_bits, q4_embedding=a.q4_embedding)
     if a.json:
         print(json.dumps(res))
     else:

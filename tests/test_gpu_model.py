@@ -26,17 +26,18 @@ LOGIT_MEAN_TOL = 5e-3
 REL_TOL = 2e-2
 
 
-@pytest.fixture(scope="module", params=["bf16", "q4"])
+@pytest.fixture(scope="module", params=["bf16", "q4", "q4_embed"])
 def tiny(lib, request):
     """Tiny Qwen3 target, bf16 or with MLX affine 4-bit projections (the
-    oracle dequantizes the packed weights itself)."""
+    oracle dequantizes the packed weights itself); q4_embed also quantizes
+    the embedding, so the tied LM head runs the 4-bit GEMM."""
     from dtree_mlx_b200.config import PRESETS
     from dtree_mlx_b200.synthetic import quantize_weights, random_qwen3_weights
 
     cfg = PRESETS["qwen3-tiny"]
     w = random_qwen3_weights(cfg, seed=0, device=DEV, norm_jitter=0.1)
-    if request.param == "q4":
-        w = quantize_weights(w)
+    if request.param != "bf16":
+        w = quantize_weights(w, embedding=request.param == "q4_embed")
     return cfg, w
 
 

@@ -79,12 +79,15 @@ def test_quantized_weights_keep_row_order():
         assert torch.equal(got[name].scales, direct.scales), name
     gate, up = split_gate_up(q.gate_up[0])
     assert gate.shape == (cfg.intermediate_size, cfg.hidden_size) and up.shape == gate.shape
-    # the embedding is quantized too (mlx-lm quantizes nn.Embedding): the
-    # tied LM head is 4-bit and the lookup table its dequantized rows
+    # BASELINE config 3 keeps the embedding; quantize_model's form
+    # (embedding=True) quantizes it too: the tied LM head is 4-bit and the
+    # lookup table holds its dequantized rows
     from dtree_mlx_b200.weights_io import dequantize_q4
 
-    assert q.embed_q4 is not None and torch.equal(q.embed_q4.packed, quantize_affine_q4(w.embed).packed)
-    assert torch.equal(q.embed, dequantize_q4(q.embed_q4))
+    assert q.embed_q4 is None and torch.equal(q.embed, w.embed)
+    qe = quantize_weights(w, embedding=True)
+    assert qe.embed_q4 is not None and torch.equal(qe.embed_q4.packed, quantize_affine_q4(w.embed).packed)
+    assert torch.equal(qe.embed, dequantize_q4(qe.embed_q4))
     # 0.5625 bytes per parameter (+ the bf16 lookup table and norms)
     proj = sum(t.nbytes() for t in (*q.qkv, *q.o_proj, *q.gate_up, *q.down))
     n_param = sum(t.shape[0] * t.shape[1] for t in (*q.qkv, *q.o_proj, *q.gate_up, *q.down))
