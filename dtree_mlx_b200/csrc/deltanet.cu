@@ -241,8 +241,11 @@ __device__ __forceinline__ float delta_step(float (&s)[NP], const float (&kk)[NP
 // grid (Hv * Dv / rows_per_cta), block rows_per_cta warps.  Lane l of a warp
 // holds state elements l*NP .. l*NP+NP-1 of its row (the reference's
 // n_per_t split).  Shared memory: q/k of the head for every node (InT, as
-// they arrive), v / g / beta per node and row, and the rounded node states
-// (InT); 16 rows per CTA keep the verify's CTAs within one wave.
+// they arrive), v / g / beta per node and row, and the rounded states of
+// nodes 0 .. T-2 (InT; a node's state is reloaded only by a child that is
+// not the next node, and the last node has none).  At 25 nodes 16 rows per
+// CTA take 110 KB, so two CTAs share an SM and the verify's 256 CTAs run in
+// one wave.
 template <typename InT, typename StT, int DK>
 __global__ void tree_gated_delta_kernel(DeltaParams p) {
   constexpr int NP = DK / 32;
@@ -255,7 +258,7 @@ __global__ void tree_gated_delta_kernel(DeltaParams p) {
   float* s_g = reinterpret_cast<float*>(s_k + T * DK);        // [T]
   float* s_b = s_g + T;                                       // [T]
   float* s_v = s_b + T;                                       // [T][R]
-  InT* s_state = reinterpret_cast<InT*>(s_v + T * R);         // [R][T][DK]
+  InT* s_state = reinterpret_cast<InT*>(s_v + T * R);         // [R][T - 1][DK]
 
   const int rows_per_head = p.dv / R;
   const int hv = blockIdx.x / rows_per_head;
@@ -289,7 +292,8 @@ __global__ void tree_gated_delta_kernel(DeltaParams p) {
   float base[NP];
 #pragma unroll
   for (int i = 0; i < NP; ++i) base[i] = ld_f(st_in + lane * NP + i);
-  InT* my_states = s_state + static_cast<size_t>(warp) * T * DK;
+  // node states a later node may branch from (the last node has no child)
+  InT* my_states = s_state + static_cast<size_t>(warp) * (T - 1) * DK;
   InT* y = static_cast<InT*>(p.y);
   StT* ns = static_cast<StT*>(p.node_states);
 
@@ -315,8 +319,10 @@ __global__ void tree_gated_delta_kernel(DeltaParams p) {
     }
     const float out = delta_step<InT, NP>(s, kk, qq, s_v[t * R + warp], s_g[t], s_b[t], !p.no_round);
     if (lane == 0) st_f(y + static_cast<size_t>(t) * p.ldy + hv * p.dv + dv, out);
+    if (t < T - 1) {
 #pragma unroll
-    for (int i = 0; i < NP; ++i) st_f(my_states + static_cast<size_t>(t) * DK + lane * NP + i, s[i]);
+      for (int i = 0; i < NP; ++i) st_f(my_states + static_cast<size_t>(t) * DK + lane * NP + i, s[i]);
+    }
     if (ns) {
 #pragma unroll
       for (int i = 0; i < NP; ++i)
@@ -591,7 +597,7 @@ __global__ void rmsnorm_gated_kernel(const InT* __restrict__ y, int ldy, const I
 // ------------------------------------------------------------ launchers
 static size_t delta_smem(int T, int R, int dk, int in_bytes) {
   const size_t qk = (static_cast<size_t>(2) * T * dk * in_bytes + 15) & ~static_cast<size_t>(15);
-  return qk + static_cast<size_t>(2 * T + T * R) * 4 + static_cast<size_t>(R) * T * dk * in_bytes;
+  return qk + static_cast<size_t>(2 * T + T * R) * 4 + static_cast<size_t>(R) * (T > 1 ? T - 1 : 1) * dk * in_bytes;
 }
 
 int conv1d_seq_launch(const ConvParams& p, int block, cudaStream_t st) {

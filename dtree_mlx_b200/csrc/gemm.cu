@@ -105,8 +105,11 @@ static int plan_common(GemmPlan* plan, int n_out, int k, const void* x, int t_pa
     p.grid = m_tiles * split;
   } else if (grid > 0) {
     p.grid = static_cast<int>(units < grid ? units : grid);
-  } else if (m_tiles >= (sms * 9) / 10 && m_tiles <= (wide ? sms : (sms * 5) / 4)) {
-    p.grid = m_tiles;  // about one whole tile per CTA (two CTAs fit an SM): no partial tiles at all
+  } else if (m_tiles >= (sms * 9) / 10 && m_tiles <= (wide ? sms : 2 * sms)) {
+    // one whole tile per CTA, up to two CTAs per SM (both fit), all in one
+    // wave: no partial tiles at all (the Qwen3.5-9B gate|up, 192 tiles, ran
+    // 0.16 ms faster per verify than stream-K over 148 CTAs)
+    p.grid = m_tiles;
   } else {
     p.grid = static_cast<int>(units < sms ? units : sms);
   }
