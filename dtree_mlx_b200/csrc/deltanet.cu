@@ -45,6 +45,33 @@ __device__ __forceinline__ float round_to(float v) {
   else return __bfloat162float(__float2bfloat16_rn(v));
 }
 
+// 4 consecutive elements as one 8-byte (bf16) or 16-byte (float) access;
+// the address must be aligned to that size
+template <typename T>
+__device__ __forceinline__ void ld4_f(const T* p, float (&v)[4]) {
+  if constexpr (std::is_same<T, float>::value) {
+    const float4 x = *reinterpret_cast<const float4*>(p);
+    v[0] = x.x, v[1] = x.y, v[2] = x.z, v[3] = x.w;
+  } else {
+    const uint2 x = *reinterpret_cast<const uint2*>(p);
+    const __nv_bfloat162 a = *reinterpret_cast<const __nv_bfloat162*>(&x.x);
+    const __nv_bfloat162 b = *reinterpret_cast<const __nv_bfloat162*>(&x.y);
+    v[0] = __low2float(a), v[1] = __high2float(a), v[2] = __low2float(b), v[3] = __high2float(b);
+  }
+}
+template <typename T>
+__device__ __forceinline__ void st4_f(T* p, const float (&v)[4]) {
+  if constexpr (std::is_same<T, float>::value) {
+    *reinterpret_cast<float4*>(p) = make_float4(v[0], v[1], v[2], v[3]);
+  } else {
+    const __nv_bfloat162 a = __floats2bfloat162_rn(v[0], v[1]), b = __floats2bfloat162_rn(v[2], v[3]);
+    uint2 x;
+    x.x = *reinterpret_cast<const uint32_t*>(&a);
+    x.y = *reinterpret_cast<const uint32_t*>(&b);
+    *reinterpret_cast<uint2*>(p) = x;
+  }
+}
+
 constexpr int kMaxKeep = 8;
 
 // ------------------------------------------------------------------ conv1d
@@ -258,7 +285,8 @@ __global__ void tree_gated_delta_kernel(DeltaParams p) {
   float* s_g = reinterpret_cast<float*>(s_k + T * DK);        // [T]
   float* s_b = s_g + T;                                       // [T]
   float* s_v = s_b + T;                                       // [T][R]
-  InT* s_state = reinterpret_cast<InT*>(s_v + T * R);         // [R][T - 1][DK]
+  // [R][T - 1][DK], 16-byte aligned for the 4-element accesses
+  InT* s_state = reinterpret_cast<InT*>((reinterpret_cast<uintptr_t>(s_v + T * R) + 15) & ~static_cast<uintptr_t>(15));
 
   const int rows_per_head = p.dv / R;
   const int hv = blockIdx.x / rows_per_head;
@@ -271,10 +299,40 @@ __global__ void tree_gated_delta_kernel(DeltaParams p) {
   const InT* q = static_cast<const InT*>(p.q);
   const InT* k = static_cast<const InT*>(p.k);
   const InT* v = static_cast<const InT*>(p.v);
-  for (int e = threadIdx.x; e < T * DK; e += blockDim.x) {
-    const int t = e / DK, d = e % DK;
-    s_q[e] = q[static_cast<size_t>(t) * p.ldqk + hk * DK + d];
-    s_k[e] = k[static_cast<size_t>(t) * p.ldqk + hk * DK + d];
+  // q / k of the head for every node: 16-byte copies (all issued before the
+  // first lands) when the rows allow, else element by element
+  constexpr int VE = 16 / static_cast<int>(sizeof(InT));  // elements per 16 bytes
+  const bool vec = ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k)) & 15) == 0 &&
+                   (static_cast<size_t>(p.ldqk) * sizeof(InT)) % 16 == 0;
+  if (vec) {
+    constexpr int kPer = 4;  // 16-byte chunks in flight per thread and matrix
+    for (int e0 = threadIdx.x * kPer; e0 < T * DK / VE; e0 += blockDim.x * kPer) {
+      uint4 aq[kPer], ak[kPer];
+#pragma unroll
+      for (int j = 0; j < kPer; ++j) {
+        const int e = e0 + j;
+        if (e < T * DK / VE) {
+          const int t = e / (DK / VE), c = e % (DK / VE);
+          const size_t off = static_cast<size_t>(t) * p.ldqk + hk * DK + c * VE;
+          aq[j] = *reinterpret_cast<const uint4*>(q + off);
+          ak[j] = *reinterpret_cast<const uint4*>(k + off);
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < kPer; ++j) {
+        const int e = e0 + j;
+        if (e < T * DK / VE) {
+          reinterpret_cast<uint4*>(s_q)[e] = aq[j];
+          reinterpret_cast<uint4*>(s_k)[e] = ak[j];
+        }
+      }
+    }
+  } else {
+    for (int e = threadIdx.x; e < T * DK; e += blockDim.x) {
+      const int t = e / DK, d = e % DK;
+      s_q[e] = q[static_cast<size_t>(t) * p.ldqk + hk * DK + d];
+      s_k[e] = k[static_cast<size_t>(t) * p.ldqk + hk * DK + d];
+    }
   }
   for (int t = threadIdx.x; t < T; t += blockDim.x) {
     float g, beta;
@@ -308,20 +366,33 @@ __global__ void tree_gated_delta_kernel(DeltaParams p) {
 #pragma unroll
       for (int i = 0; i < NP; ++i) s[i] = base[i];
     } else if (par != t - 1) {
+      if constexpr (NP == 4) {
+        ld4_f(my_states + static_cast<size_t>(par) * DK + lane * NP, s);
+      } else {
 #pragma unroll
-      for (int i = 0; i < NP; ++i) s[i] = ld_f(my_states + static_cast<size_t>(par) * DK + lane * NP + i);
+        for (int i = 0; i < NP; ++i) s[i] = ld_f(my_states + static_cast<size_t>(par) * DK + lane * NP + i);
+      }
     }  // par == t - 1: the previous node's state is still in registers
     float kk[NP], qq[NP];
+    if constexpr (NP == 4) {
+      ld4_f(s_k + t * DK + lane * NP, kk);
+      ld4_f(s_q + t * DK + lane * NP, qq);
+    } else {
 #pragma unroll
-    for (int i = 0; i < NP; ++i) {
-      kk[i] = ld_f(s_k + t * DK + lane * NP + i);
-      qq[i] = ld_f(s_q + t * DK + lane * NP + i);
+      for (int i = 0; i < NP; ++i) {
+        kk[i] = ld_f(s_k + t * DK + lane * NP + i);
+        qq[i] = ld_f(s_q + t * DK + lane * NP + i);
+      }
     }
     const float out = delta_step<InT, NP>(s, kk, qq, s_v[t * R + warp], s_g[t], s_b[t], !p.no_round);
     if (lane == 0) st_f(y + static_cast<size_t>(t) * p.ldy + hv * p.dv + dv, out);
     if (t < T - 1) {
+      if constexpr (NP == 4) {
+        st4_f(my_states + static_cast<size_t>(t) * DK + lane * NP, s);
+      } else {
 #pragma unroll
-      for (int i = 0; i < NP; ++i) st_f(my_states + static_cast<size_t>(t) * DK + lane * NP + i, s[i]);
+        for (int i = 0; i < NP; ++i) st_f(my_states + static_cast<size_t>(t) * DK + lane * NP + i, s[i]);
+      }
     }
     if (ns) {
 #pragma unroll
@@ -597,7 +668,8 @@ __global__ void rmsnorm_gated_kernel(const InT* __restrict__ y, int ldy, const I
 // ------------------------------------------------------------ launchers
 static size_t delta_smem(int T, int R, int dk, int in_bytes) {
   const size_t qk = (static_cast<size_t>(2) * T * dk * in_bytes + 15) & ~static_cast<size_t>(15);
-  return qk + static_cast<size_t>(2 * T + T * R) * 4 + static_cast<size_t>(R) * (T > 1 ? T - 1 : 1) * dk * in_bytes;
+  return qk + static_cast<size_t>(2 * T + T * R) * 4 + 16 /* state alignment */ +
+         static_cast<size_t>(R) * (T > 1 ? T - 1 : 1) * dk * in_bytes;
 }
 
 int conv1d_seq_launch(const ConvParams& p, int block, cudaStream_t st) {
