@@ -238,26 +238,44 @@ __device__ __forceinline__ void node_gates(const DeltaParams& p, int t, int hv, 
 // side, one butterfly deep instead of two after each other.  The tree
 // kernel and the commit replay share this step, so a replayed node state
 // equals the tree kernel's bit for bit.
-template <typename InT, int NP>
-__device__ __forceinline__ float delta_step(float (&s)[NP], const float (&kk)[NP], const float (&qq)[NP], float v,
-                                            float g, float beta, bool rnd = true) {
-  float sk = 0.0f, sq = 0.0f, kq = 0.0f;
+// k·q of a node: the same per-lane chain and butterfly as delta_step's, so
+// a value computed once per node (the tree kernel) equals the one each
+// row's step would reduce (the replay) bit for bit
+template <int NP>
+__device__ __forceinline__ float node_kq(const float (&kk)[NP], const float (&qq)[NP]) {
+  float kq = 0.0f;
+#pragma unroll
+  for (int i = 0; i < NP; ++i) kq = fmaf(kk[i], qq[i], kq);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) kq += __shfl_xor_sync(0xffffffffu, kq, o);
+  return kq;
+}
+// the step given k·q: S k and S q reduced side by side, the update (the
+// state left unrounded: the caller rounds)
+template <int NP>
+__device__ __forceinline__ float delta_update(float (&s)[NP], const float (&kk)[NP], const float (&qq)[NP], float kq,
+                                              float v, float g, float beta) {
+  float sk = 0.0f, sq = 0.0f;
 #pragma unroll
   for (int i = 0; i < NP; ++i) {
     sk = fmaf(s[i], kk[i], sk);
     sq = fmaf(s[i], qq[i], sq);
-    kq = fmaf(kk[i], qq[i], kq);
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {
     sk += __shfl_xor_sync(0xffffffffu, sk, o);
     sq += __shfl_xor_sync(0xffffffffu, sq, o);
-    kq += __shfl_xor_sync(0xffffffffu, kq, o);
   }
   const float delta = (v - g * sk) * beta;
 #pragma unroll
   for (int i = 0; i < NP; ++i) s[i] = fmaf(kk[i], delta, s[i] * g);
-  const float out = fmaf(g, sq, delta * kq);
+  return fmaf(g, sq, delta * kq);
+}
+template <typename InT, int NP>
+__device__ __forceinline__ float delta_step(float (&s)[NP], const float (&kk)[NP], const float (&qq)[NP], float v,
+                                            float g, float beta, bool rnd = true) {
+  const float kq = node_kq(kk, qq);
+  const float out = delta_update(s, kk, qq, kq, v, g, beta);
   if (rnd) {
 #pragma unroll
     for (int i = 0; i < NP; ++i) s[i] = round_to<InT>(s[i]);
@@ -285,8 +303,10 @@ __global__ void tree_gated_delta_kernel(DeltaParams p) {
   float* s_g = reinterpret_cast<float*>(s_k + T * DK);        // [T]
   float* s_b = s_g + T;                                       // [T]
   float* s_v = s_b + T;                                       // [T][R]
+  float* s_kq = s_v + T * R;                                  // [T]: k·q per node
+  int* s_par = reinterpret_cast<int*>(s_kq + T);              // [T]: validated parents
   // [R][T - 1][DK], 16-byte aligned for the 4-element accesses
-  InT* s_state = reinterpret_cast<InT*>((reinterpret_cast<uintptr_t>(s_v + T * R) + 15) & ~static_cast<uintptr_t>(15));
+  InT* s_state = reinterpret_cast<InT*>((reinterpret_cast<uintptr_t>(s_par + T) + 15) & ~static_cast<uintptr_t>(15));
 
   const int rows_per_head = p.dv / R;
   const int hv = blockIdx.x / rows_per_head;
@@ -339,10 +359,34 @@ __global__ void tree_gated_delta_kernel(DeltaParams p) {
     node_gates<InT>(p, t, hv, g, beta);
     s_g[t] = g;
     s_b[t] = beta;
+    int par = p.parents[t];
+    if (par >= t || (p.no_round && par != t - 1)) {  // malformed tree / prefill needs a chain
+      dev_error(0x2004u);
+      par = -1;
+    }
+    s_par[t] = par;
   }
   for (int e = threadIdx.x; e < T * R; e += blockDim.x) {
     const int t = e / R, r = e % R;
     s_v[e] = ld_f(v + static_cast<size_t>(t) * p.ldv + hv * p.dv + dv0 + r);
+  }
+  __syncthreads();
+  // k·q of every node once per CTA (the same chain and butterfly as each
+  // row's step would run): warp w takes nodes w, w + warps, ...
+  for (int t = warp; t < T; t += static_cast<int>(blockDim.x >> 5)) {
+    float kk[NP], qq[NP];
+    if constexpr (NP == 4) {
+      ld4_f(s_k + t * DK + lane * NP, kk);
+      ld4_f(s_q + t * DK + lane * NP, qq);
+    } else {
+#pragma unroll
+      for (int i = 0; i < NP; ++i) {
+        kk[i] = ld_f(s_k + t * DK + lane * NP + i);
+        qq[i] = ld_f(s_q + t * DK + lane * NP + i);
+      }
+    }
+    const float kq = node_kq(kk, qq);
+    if (lane == 0) s_kq[t] = kq;
   }
   __syncthreads();
 
@@ -357,11 +401,7 @@ __global__ void tree_gated_delta_kernel(DeltaParams p) {
 
   float s[NP];
   for (int t = 0; t < T; ++t) {
-    int par = p.parents[t];
-    if (par >= t || (p.no_round && par != t - 1)) {  // malformed tree / prefill needs a chain
-      dev_error(0x2004u);
-      par = -1;
-    }
+    const int par = s_par[t];
     if (par < 0) {
 #pragma unroll
       for (int i = 0; i < NP; ++i) s[i] = base[i];
@@ -384,14 +424,29 @@ __global__ void tree_gated_delta_kernel(DeltaParams p) {
         qq[i] = ld_f(s_q + t * DK + lane * NP + i);
       }
     }
-    const float out = delta_step<InT, NP>(s, kk, qq, s_v[t * R + warp], s_g[t], s_b[t], !p.no_round);
+    const float out = delta_update(s, kk, qq, s_kq[t], s_v[t * R + warp], s_g[t], s_b[t]);
     if (lane == 0) st_f(y + static_cast<size_t>(t) * p.ldy + hv * p.dv + dv, out);
-    if (t < T - 1) {
-      if constexpr (NP == 4) {
-        st4_f(my_states + static_cast<size_t>(t) * DK + lane * NP, s);
-      } else {
+    InT* row = my_states + static_cast<size_t>(t) * DK + lane * NP;
+    if constexpr (std::is_same<InT, __nv_bfloat16>::value && NP == 4) {
+      // round to bf16 once: the packed pairs are the stored row and, read
+      // back, the state the children continue from (delta_step's rounding)
+      const __nv_bfloat162 a = __floats2bfloat162_rn(s[0], s[1]), b = __floats2bfloat162_rn(s[2], s[3]);
+      if (!p.no_round) s[0] = __low2float(a), s[1] = __high2float(a), s[2] = __low2float(b), s[3] = __high2float(b);
+      if (t < T - 1)
+        *reinterpret_cast<uint2*>(row) =
+            make_uint2(*reinterpret_cast<const uint32_t*>(&a), *reinterpret_cast<const uint32_t*>(&b));
+    } else {
+      if (!p.no_round) {
 #pragma unroll
-        for (int i = 0; i < NP; ++i) st_f(my_states + static_cast<size_t>(t) * DK + lane * NP + i, s[i]);
+        for (int i = 0; i < NP; ++i) s[i] = round_to<InT>(s[i]);
+      }
+      if (t < T - 1) {
+        if constexpr (NP == 4) {
+          st4_f(row, s);
+        } else {
+#pragma unroll
+          for (int i = 0; i < NP; ++i) st_f(row + i, s[i]);
+        }
       }
     }
     if (ns) {
@@ -668,7 +723,7 @@ __global__ void rmsnorm_gated_kernel(const InT* __restrict__ y, int ldy, const I
 // ------------------------------------------------------------ launchers
 static size_t delta_smem(int T, int R, int dk, int in_bytes) {
   const size_t qk = (static_cast<size_t>(2) * T * dk * in_bytes + 15) & ~static_cast<size_t>(15);
-  return qk + static_cast<size_t>(2 * T + T * R) * 4 + 16 /* state alignment */ +
+  return qk + static_cast<size_t>(4 * T + T * R) * 4 + 16 /* state alignment */ +
          static_cast<size_t>(R) * (T > 1 ? T - 1 : 1) * dk * in_bytes;
 }
 
