@@ -106,8 +106,11 @@ __global__ void __launch_bounds__(256) qkv_finish_kernel(QkvFinishParams p) {
 // 16-byte or 8-byte loads; the head's sum of squares and the RoPE partner
 // (feature i <-> i + rot/2, lane l <-> l ^ (rot/2 / EPL)) move by shuffles,
 // so there is no shared memory and no block barrier.  Same arithmetic and
-// rounding points as qkv_finish_kernel.
-template <int EPL>
+// rounding points as qkv_finish_kernel.  PART: the tree verify's split-K
+// fp32 partials in place of the dense projection (summed in split order and
+// rounded to bf16, as qkv_finish_kernel does), for plain heads (no output
+// gate, full RoPE) at slots start + t.
+template <int EPL, bool PART = false>
 __global__ void __launch_bounds__(256) qkv_rows_kernel(QkvFinishParams p) {
   pdl_trigger();
   const int lane = threadIdx.x & 31;
@@ -125,9 +128,39 @@ __global__ void __launch_bounds__(256) qkv_rows_kernel(QkvFinishParams p) {
     const int t = static_cast<int>(task / heads), gh = static_cast<int>(task % heads);
     const int d0 = lane * EPL;
     const int col = gh < p.n_q_heads ? gh * qcols + d0 : p.n_q_heads * qcols + (gh - p.n_q_heads) * hd + d0;
-    const __nv_bfloat16* src = p.dense + static_cast<size_t>(t) * p.width + col;
+    const __nv_bfloat16* src = PART ? nullptr : p.dense + static_cast<size_t>(t) * p.width + col;
     __nv_bfloat16 xv[EPL];
-    if constexpr (EPL == 8) {
+    if constexpr (PART) {
+      // up to 8 splits' loads in flight at once, summed in split order
+      static_assert(EPL % 2 == 0, "partials in float2 / float4 pieces");
+      const float* fsrc = p.partials + static_cast<size_t>(t) * p.width + col;
+      const size_t stride = static_cast<size_t>(p.part_rows) * p.width;
+      float a[EPL];
+#pragma unroll
+      for (int i = 0; i < EPL; ++i) a[i] = 0.0f;
+      for (int s0 = 0; s0 < p.split; s0 += 8) {
+        float v[8][EPL];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          if (s0 + k < p.split) {
+            const float* q = fsrc + (s0 + k) * stride;
+#pragma unroll
+            for (int c = 0; c < EPL; c += 2) {
+              const float2 w = __ldcg(reinterpret_cast<const float2*>(q + c));
+              v[k][c] = w.x, v[k][c + 1] = w.y;
+            }
+          }
+        }
+#pragma unroll
+        for (int k = 0; k < 8; ++k)
+          if (s0 + k < p.split) {
+#pragma unroll
+            for (int i = 0; i < EPL; ++i) a[i] += v[k][i];
+          }
+      }
+#pragma unroll
+      for (int i = 0; i < EPL; ++i) xv[i] = __float2bfloat16_rn(a[i]);
+    } else if constexpr (EPL == 8) {
       *reinterpret_cast<uint4*>(xv) = *reinterpret_cast<const uint4*>(src);
     } else if constexpr (EPL == 4) {
       *reinterpret_cast<uint2*>(xv) = *reinterpret_cast<const uint2*>(src);
@@ -146,7 +179,7 @@ __global__ void __launch_bounds__(256) qkv_rows_kernel(QkvFinishParams p) {
       }
       continue;
     }
-    if (p.gated && gh < p.n_q_heads) {
+    if (!PART && p.gated && gh < p.n_q_heads) {
       const __nv_bfloat16* gsrc = src + hd;
       __nv_bfloat16* gdst = p.gate_out + static_cast<size_t>(t) * (p.n_q_heads * hd) + gh * hd + d0;
 #pragma unroll
@@ -233,6 +266,25 @@ int qkv_finish_launch(const QkvFinishParams& p, int n_rows, cudaStream_t stream)
   DTREE_CHECK_ARG(p.rot_dims >= 0 && p.rot_dims <= p.head_dim && p.rot_dims % 2 == 0, "bad rot_dims");
   DTREE_CHECK_ARG(!p.gated || p.gate_out, "gated projection needs gate_out");
   DTREE_CHECK_ARG(p.partials && !p.dense, "qkv_finish sums split partials (prompt rows: qkv_rows_launch)");
+  // (at most 16 rows the one-block-per-(row, head) kernel below is faster:
+  // 2.415 against 2.432 ms per 9-row verify; 25 rows 2.557 against 2.542)
+  if (n_rows > 16 && p.slot_mode == 0 && !p.gated && (p.rot_dims == 0 || p.rot_dims == p.head_dim) &&
+      p.n_q_heads > 0 &&
+      (p.head_dim == 64 || p.head_dim == 128) && p.width % 4 == 0 && p.positions &&
+      (reinterpret_cast<uintptr_t>(p.partials) & 15) == 0) {
+    // tree rows of plain heads: a warp per (row, head), no block barriers
+    QkvFinishParams q = p;
+    q.n_rows = n_rows;
+    const long long tasks = static_cast<long long>(n_rows) * (p.n_q_heads + 2 * p.n_kv_heads);
+    // warps per block: at least two blocks per SM where the tasks allow
+    const int wpb = static_cast<int>(std::max(1ll, std::min(8ll, tasks / (2ll * num_sms()))));
+    const int grid = static_cast<int>(std::min<long long>((tasks + wpb - 1) / wpb, 16ll * num_sms()));
+    if (p.head_dim == 128)
+      DTREE_CUDA_RET(launch_pdl(qkv_rows_kernel<4, true>, dim3(grid), dim3(32 * wpb), 0, stream, q));
+    else
+      DTREE_CUDA_RET(launch_pdl(qkv_rows_kernel<2, true>, dim3(grid), dim3(32 * wpb), 0, stream, q));
+    return kOk;
+  }
   DTREE_CUDA_RET(launch_pdl(qkv_finish_kernel, dim3(n_rows, p.n_q_heads + 2 * p.n_kv_heads), dim3(p.head_dim), 0,
                             stream, p));
   return kOk;
