@@ -245,6 +245,8 @@ def run_ours(args, rank, world, local, dist) -> dict | None:
     for P in (PROMPT_LEN + MAX_NEW // 2, 2048):
         st = kernels.new_state(dev, start=P, root_token=first)
         post = torch.zeros(128, dtype=torch.int32, device=dev)
+        if hasattr(eng, "use_attention_shape"):  # the shape a decode step at this prefix uses
+            eng.use_attention_shape(P, n_nodes)
         verify_call(eng, session.tree, n_nodes, st, post)
         torch.cuda.synchronize()
         s = torch.cuda.Stream()

@@ -194,6 +194,7 @@ PROTOTYPES = {
     "dtree_lm_head_sample": (I, [P, I, I, I, P, I, C.c_float, C.c_uint32, P, P, P, SZ, P]),
     "dtree_chain_sample": (I, [P, I, I, C.c_float, C.c_uint32, P, P, P, P, P, P, P]),
     "dtree_qwen3_set_sampling": (I, [P, C.c_float, C.c_uint32]),
+    "dtree_qwen3_set_attention_keys": (I, [P, I]),
     "dtree_qwen3_prefill_workspace_bytes": (C.c_size_t, [P, I]),
     "dtree_qwen3_prefill": (I, [P, P, P, I, P, P, I, P, P, P, C.c_size_t, P]),
     "dtree_qwen35_set_sampling": (I, [P, C.c_float, C.c_uint32]),

@@ -378,8 +378,17 @@ __device__ __forceinline__ uint32_t sw128_off(int row, int chunk16) {
 }
 
 // PROMPT: the prompt (prefill) instantiation, causal 128-row chunks
-// (AttnParams::chunk_rows); the tree-verify one has none of its code
-template <int HD, bool PROMPT = false>
+// (AttnParams::chunk_rows); the tree-verify one has none of its code.
+// CL: the splits of one (row block, KV head) form one thread-block cluster
+// (cluster size = gridDim.x = splits <= 8) and merge their partials through
+// distributed shared memory instead of the global workspace and
+// attn_combine_kernel: each CTA stages its unnormalised O and (m, l) in its
+// own shared memory, and after a cluster barrier CTA c merges rows
+// c, c + splits, ... of the block with the combine kernel's arithmetic in the
+// same order (bit-identical output).  Any prefix is covered (keys per split
+// grow with it); the launch pays off while 8 x 128 keys cover the prefix and
+// the tree (one pass per CTA, 8 CTAs per KV head instead of ~18).
+template <int HD, bool PROMPT = false, bool CL = false>
 __global__ void __launch_bounds__(kTcThreads) tree_attn_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
                                                                    const __grid_constant__ CUtensorMap tmap_v,
                                                                    AttnParams p) {
@@ -685,14 +694,14 @@ __global__ void __launch_bounds__(kTcThreads) tree_attn_tc_kernel(const __grid_c
         }
       }
     }
-    if (row_ok && h == 0 && !chunked) {
+    if (row_ok && h == 0 && !chunked && !CL) {
       const int qrow = (kvh * G + g) * T + node;  // [head][node]
       float* pml = p.part_ml + (static_cast<size_t>(split) * rows_total + qrow) * 2;
       pml[0] = m_run;
       pml[1] = l_run;
     }
     __syncwarp();
-    if (!chunked) {
+    if (!chunked && !CL) {
 #pragma unroll 4
     for (int rr = sub; rr < 32; rr += RPI) {
       const int rg2 = rb * 128 + (warp & 3) * 32 + rr;
@@ -703,6 +712,79 @@ __global__ void __launch_bounds__(kTcThreads) tree_attn_tc_kernel(const __grid_c
       }
     }
     }
+  }
+  if constexpr (CL) {
+    // ---- merge of the cluster's splits.  Staged O of split s, row q, column
+    // d: CTA s's `stage` of warp (d / OH) * 4 + q / 32, row q % 32, column
+    // d % OH; its (m, l) in red_max[q], red_sum[q] (-inf / 0: no keys)
+    constexpr int LDS = OH + 4;
+    float* const stage0 = reinterpret_cast<float*>(sq);
+    float* const s_w = stage0 + 8 * 32 * LDS;  // [my rows][splits] weights
+    float* const s_il = s_w + 136;             // [my rows] 1 / sum of weights
+    static_assert((8 * 32 * LDS + 136 + 128) * 4 <= C::kBar, "merge scratch exceeds the operand space");
+    const bool live = ok && n_pass > 0;
+    if (h == 0) {
+      red_max[r] = live ? m_run : -INFINITY;
+      red_sum[r] = live ? l_run : 0.0f;
+    }
+    cluster_arrive();  // staged O and (m, l) of every split are published
+    cluster_wait();
+    const int S = p.splits;  // == cluster size <= 8
+    const int active = min(S, (L + kps - 1) / kps);  // splits holding keys: 0 .. active-1
+    const int rows_here = min(128, rows_kv - rb * 128);
+    const int n_mine = split < rows_here ? (rows_here - split + S - 1) / S : 0;
+    // weights of my rows (split, split + S, ...): warp per row, lane s =
+    // split s, attn_combine_kernel's arithmetic in its order
+    for (int i = warp; i < n_mine; i += kTcThreads / 32) {
+      const int q = split + i * S;
+      float m = -INFINITY, l = 0.0f;
+      if (lane < active) {
+        m = ld_dsmem_f32(red_max + q, static_cast<uint32_t>(lane));
+        l = ld_dsmem_f32(red_sum + q, static_cast<uint32_t>(lane));
+      }
+      float M = m;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+      const float m_use = (M == -INFINITY) ? 0.0f : M;
+      const float w = (lane < active) ? exp2f(m - m_use) : 0.0f;
+      const float wl = w * l;
+      float Ls = 0.0f;  // fixed order (split 0, 1, ...)
+      for (int s2 = 0; s2 < active; ++s2) Ls += __shfl_sync(0xffffffffu, wl, s2);
+      if (lane < S) s_w[i * S + lane] = w;
+      if (lane == 0) s_il[i] = Ls > 0.0f ? 1.0f / Ls : 0.0f;
+    }
+    __syncthreads();
+    // O: one 4-column group of one of my rows per thread and round, every
+    // split's 16 bytes loaded before the ordered sum; O / l in bf16 to `out`
+    constexpr int G4 = HD / 4;
+    for (int slot = t; slot < n_mine * G4; slot += kTcThreads) {
+      const int i = slot / G4, d = (slot % G4) * 4;
+      const int q = split + i * S;
+      const float* src = stage0 + ((d / OH) * 4 + q / 32) * 32 * LDS + (q % 32) * LDS + (d % OH);
+      float4 v[8];
+#pragma unroll
+      for (int s2 = 0; s2 < 8; ++s2)
+        v[s2] = s2 < active ? ld_dsmem_f32x4(src, static_cast<uint32_t>(s2)) : make_float4(0.f, 0.f, 0.f, 0.f);
+      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+      for (int s2 = 0; s2 < 8; ++s2) {
+        if (s2 < active) {
+          const float w = s_w[i * S + s2];
+          acc.x += w * v[s2].x;
+          acc.y += w * v[s2].y;
+          acc.z += w * v[s2].z;
+          acc.w += w * v[s2].w;
+        }
+      }
+      const float il = s_il[i];
+      const int rg2 = rb * 128 + q;
+      uint2 pk;
+      pk.x = pack_bf16(acc.x * il, acc.y * il);
+      pk.y = pack_bf16(acc.z * il, acc.w * il);
+      *reinterpret_cast<uint2*>(p.out + static_cast<size_t>(rg2 % T) * p.ldq + (kvh * G + rg2 / T) * HD + d) = pk;
+    }
+    cluster_arrive();  // no CTA leaves while another reads its shared memory
+    cluster_wait();
   }
   tc_fence_before();
   __syncthreads();
@@ -821,6 +903,33 @@ static int plane_tmap(CUtensorMap* out, const void* plane, int rows, int hd) {
   return kOk;
 }
 
+// Largest cluster (<= 8, the merge's register array) that the cluster-merge
+// kernel can be launched with, from the occupancy query with its shared memory
+// (asked once per kernel; 0 on error).  Also opts the kernel into its shared
+// memory.
+template <typename K>
+static int attn_cluster_max(K kern, int smem) {
+  static std::mutex mu;
+  static std::map<const void*, int> known;
+  std::lock_guard<std::mutex> lock(mu);
+  const void* key = reinterpret_cast<const void*>(kern);
+  auto it = known.find(key);
+  if (it != known.end()) return it->second;
+  if (ensure_smem_attr(kern, smem) != cudaSuccess) return 0;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(8, 1, 8);
+  cfg.blockDim = dim3(kTcThreads);
+  cfg.dynamicSmemBytes = static_cast<size_t>(smem);
+  int n = 0;
+  if (cudaOccupancyMaxPotentialClusterSize(&n, kern, &cfg) != cudaSuccess) {
+    cudaGetLastError();
+    n = 8;  // the portable cluster size
+  }
+  n = std::max(1, std::min(n, 8));
+  known.emplace(key, n);
+  return n;
+}
+
 template <int HD>
 static int attn_launch_tc(const AttnParams& p, int rb, cudaStream_t stream) {
   using C = TcCfg<HD>;
@@ -829,11 +938,40 @@ static int attn_launch_tc(const AttnParams& p, int rb, cudaStream_t stream) {
   int rc = plane_tmap(&tk, p.k, rows, HD);
   if (rc) return rc;
   if ((rc = plane_tmap(&tv, p.v, rows, HD))) return rc;
+  const int want = p.cluster_keys > 0 ? (p.cluster_keys + kTcKeys - 1) / kTcKeys : 0;
+  if (p.gate == nullptr && want >= 1 && want <= 8 && want * rb * p.n_kv_heads <= num_sms()) {
+    // every split of a (row block, KV head) in one cluster, merged in
+    // shared memory (one wave of CTAs at one per SM)
+    auto kern = tree_attn_tc_kernel<HD, false, true>;
+    const int cmax = attn_cluster_max(kern, C::kSmem);
+    if (want <= cmax) {
+      AttnParams pc = p;
+      pc.splits = want;
+      DTREE_CUDA_RET(launch_pdl_cluster(kern, dim3(want, rb, p.n_kv_heads), dim3(kTcThreads),
+                                        static_cast<size_t>(C::kSmem), stream, want, tk, tv, pc));
+      return kOk;
+    }
+  }
   auto kern = tree_attn_tc_kernel<HD>;
   DTREE_CUDA_RET(ensure_smem_attr(kern, C::kSmem));
   DTREE_CUDA_RET(launch_pdl(kern, dim3(p.splits, rb, p.n_kv_heads), dim3(kTcThreads), static_cast<size_t>(C::kSmem),
                             stream, tk, tv, p));
   DTREE_CUDA_RET(launch_pdl(attn_combine_kernel<HD>, dim3(p.n_q_heads * p.n_nodes), dim3(HD), 0, stream, p));
+  return kOk;
+}
+
+int attn_prepare(int head_dim) {
+  // shared-memory opt-ins and the cluster query of both tree-attention
+  // shapes, outside any stream capture
+  if (head_dim == 128) {
+    DTREE_CUDA_RET(ensure_smem_attr(tree_attn_tc_kernel<128>, TcCfg<128>::kSmem));
+    if (attn_cluster_max(tree_attn_tc_kernel<128, false, true>, TcCfg<128>::kSmem) < 1)
+      return fail(kErrCuda, "tree attention: cluster size query failed");
+  } else if (head_dim == 64) {
+    DTREE_CUDA_RET(ensure_smem_attr(tree_attn_tc_kernel<64>, TcCfg<64>::kSmem));
+    if (attn_cluster_max(tree_attn_tc_kernel<64, false, true>, TcCfg<64>::kSmem) < 1)
+      return fail(kErrCuda, "tree attention: cluster size query failed");
+  }
   return kOk;
 }
 
@@ -930,6 +1068,7 @@ extern "C" int dtree_tree_attention(const void* q, int ldq, const void* k_plane,
   p.anc = anc_mask;
   p.scale_log2 = static_cast<float>(1.4426950408889634 / std::sqrt(static_cast<double>(head_dim)));
   p.splits = splits > 0 ? splits : std::min(32, attn_default_splits(n_kv_heads, n_q_heads, n_nodes));
+  p.cluster_keys = splits > 0 ? 0 : kv_cap;  // automatic splits: merged in a cluster when the cache is short
   p.out = static_cast<__nv_bfloat16*>(out);
   return attn_launch(p, head_dim, workspace, workspace_bytes, static_cast<cudaStream_t>(stream));
 }

@@ -30,11 +30,21 @@ struct AttnParams {
   // chain mask `anc` within the chunk, and writes O / l straight to `out`
   int chunk_rows;
   int chunk_rbs;        // 128-row blocks per chunk (set by attn_prefill_launch)
+  // tree path, head_dim 64 / 128, no gate: a bound on prefix + tree keys
+  // (0: none).  When ceil(bound / 128) <= 8 (and those CTAs for every row
+  // block and KV head fit one per SM) the splits are that many CTAs of one
+  // thread-block cluster per (row block, KV head) that merge in shared memory
+  // (no attn_combine_kernel); keys past the bound stay correct (more passes
+  // per CTA)
+  int cluster_keys;
 };
 
 size_t attn_ws_bytes(int n_q_heads, int t_pad, int head_dim, int splits);
 int attn_default_splits(int n_kv_heads, int n_q_heads, int n_nodes);
 int attn_launch(const AttnParams& p, int head_dim, void* ws, size_t ws_bytes, cudaStream_t stream);
+// kernel attributes and launch queries of the tree attention for head_dim
+// (call once, outside stream capture)
+int attn_prepare(int head_dim);
 // prompt (causal) attention over n_nodes rows in chunks of 128; anc = the
 // 128-row chain masks; head_dim 64 or 128; no workspace
 int attn_prefill_launch(const AttnParams& p, int head_dim, cudaStream_t stream);

@@ -361,6 +361,18 @@ __device__ __forceinline__ float ld_dsmem_f32(const void* local, uint32_t cta_ra
   asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(remote) : "memory");
   return v;
 }
+// 16 bytes of CTA `cta_rank`'s shared memory at this CTA's offset `local`
+// (16-byte aligned)
+__device__ __forceinline__ float4 ld_dsmem_f32x4(const void* local, uint32_t cta_rank) {
+  uint32_t remote;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(smem_u32(local)), "r"(cta_rank));
+  float4 v;
+  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(remote)
+               : "memory");
+  return v;
+}
 
 // Opt a kernel into `bytes` of dynamic shared memory once per process (the
 // library drives one device per process), so that launches recorded into a

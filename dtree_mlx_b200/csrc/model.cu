@@ -80,6 +80,7 @@ struct dtree_qwen3_model {
   bool fused_ready[3] = {false, false, false};
   float inv_temp = 0.0f;  // posterior sampling (0: greedy argmax)
   uint32_t sample_seed = 0;
+  int attn_keys = 0;      // bound on prefix + tree keys of the next forwards (0: the KV capacity)
 };
 
 namespace dtree {
@@ -233,6 +234,10 @@ extern "C" int dtree_qwen3_create(const dtree_qwen3_desc* desc, dtree_qwen3_mode
   m->attn_ws_bytes = attn_ws_need(d);
   m->proj_partials = reinterpret_cast<float*>(static_cast<char*>(m->attn_ws) +
                                               ((m->attn_ws_bytes + 255) & ~static_cast<size_t>(255)));
+  if (int rc = attn_prepare(d.head_dim)) {
+    delete m;
+    return rc;
+  }
   if (d.quant_bits == 4 || d.embed_q4_packed) {
     // the scale / bias blocks of every 4-bit projection (and of a 4-bit LM
     // head), after the other workspace regions (the weights must be
@@ -524,6 +529,7 @@ static int forward_impl(dtree_qwen3_model* m, const int32_t* tree_tokens, const 
       a.anc = anc_mask;
       a.scale_log2 = static_cast<float>(1.4426950408889634 / std::sqrt(static_cast<double>(d.head_dim)));
       a.splits = splits;
+      a.cluster_keys = m->attn_keys > 0 ? std::min(m->attn_keys, d.kv_capacity) : d.kv_capacity;
       a.out = bw(d.attn);
       if ((rc = attn_launch(a, d.head_dim, m->attn_ws, m->attn_ws_bytes, st))) return rc;
     }
@@ -773,6 +779,13 @@ extern "C" int dtree_qwen3_prefill(dtree_qwen3_model* m, const int32_t* tokens, 
   g.p.sample_seed = m->sample_seed;
   g.p.sample_state = state;
   return gemm_launch(g, st);
+}
+
+extern "C" int dtree_qwen3_set_attention_keys(dtree_qwen3_model* m, int max_keys) {
+  DTREE_CHECK_ARG(m, "null model");
+  DTREE_CHECK_ARG(max_keys >= 0, "max_keys must be >= 0");
+  m->attn_keys = max_keys;
+  return kOk;
 }
 
 extern "C" int dtree_qwen3_set_sampling(dtree_qwen3_model* m, float temperature, uint32_t seed) {

@@ -194,6 +194,22 @@ class Qwen3Engine:
         sampled at `temperature` with Philox noise keyed by seed and step."""
         call("dtree_qwen3_set_sampling", self._handle, float(temperature), int(seed) & 0xFFFFFFFF)
 
+    # prefix + tree keys up to which the tree attention can run one cluster
+    # of <= 8 CTAs per KV head (8 x 128 keys, one pass each)
+    short_attention_keys = 1024
+
+    def set_attention_keys(self, max_keys: int) -> None:
+        """Bound on prefix + tree keys of the following forwards (0: the KV
+        capacity): a launch-shape hint only, results do not depend on it."""
+        call("dtree_qwen3_set_attention_keys", self._handle, int(max_keys))
+
+    def use_attention_shape(self, start: int, n_nodes: int) -> None:
+        """The attention launch shape for forwards of n_nodes rows at prefix
+        lengths up to `start`: one short cluster per KV head while the keys
+        fit ``short_attention_keys``, else the split shape."""
+        fits = start + n_nodes <= self.short_attention_keys
+        self.set_attention_keys(self.short_attention_keys if fits else 0)
+
     def forward_tree(self, tokens: torch.Tensor, positions: torch.Tensor, anc: torch.Tensor, n_nodes: int,
                      state: torch.Tensor, posterior: torch.Tensor | None) -> None:
         """Tree-verify forward of rows [0, n_nodes) at prefix length state.start."""
@@ -263,6 +279,10 @@ class DecodeSession:
         )
         self.drafter = drafter
         self.graph: torch.cuda.CUDAGraph | None = None
+        # step graphs by attention launch shape (see ``_attention_class``);
+        # ``graph`` is the one captured last, None until the first capture
+        self.graphs: dict[int, torch.cuda.CUDAGraph] = {}
+        self.host_start = 0  # the last prefix length the host knows of
 
     # ------------------------------------------------------------ prefill
     def prefill(self, prompt: list[int]) -> int:
@@ -324,6 +344,7 @@ class DecodeSession:
         """Decode state right after prefill: start = prompt_len, root = first token."""
         self.state.zero_()
         self.state[0] = prompt_len
+        self.host_start = prompt_len
         self.state[1] = first_token
         self.output[prompt_len] = first_token
         self.prompt_len = prompt_len
@@ -331,10 +352,23 @@ class DecodeSession:
             self.engine.restore_states(self._snapshot)
 
     # ------------------------------------------------------------ one step
+    def _attention_class(self) -> int:
+        """1 while the next verify's keys (prefix + tree rows) fit the short
+        attention shape of the engine, else 0.  The host learns the prefix
+        length after each step (``host_start``); steps replayed without that
+        keep the last known value, which changes only the launch shape."""
+        lim = getattr(self.engine, "short_attention_keys", 0)
+        return 1 if lim and self.host_start + self.cfg.n_nodes <= lim else 0
+
+    def _set_attention_shape(self, cls: int) -> None:
+        if hasattr(self.engine, "set_attention_keys"):
+            self.engine.set_attention_keys(self.engine.short_attention_keys if cls == 1 else 0)
+
     def step(self) -> None:
         """One decode step, launched on the current stream (no host sync)."""
         eng = self.engine
         c = self.cfg
+        self._set_attention_shape(self._attention_class())
         self.drafter.draft(self)
         if c.mode == "dtree":
             self.builder.build(self.draft_logits, self.state, self.tree, keep_topk=False)
@@ -349,7 +383,12 @@ class DecodeSession:
 
     def capture_step(self) -> torch.cuda.CUDAGraph:
         """Record ``step`` into a CUDA graph (after one eager warm-up step has
-        built every plan); replay it with ``replay``."""
+        built every plan) for the current attention shape, dropping graphs
+        captured before; replay it with ``replay``."""
+        self.graphs = {}
+        return self._capture(self._attention_class())
+
+    def _capture(self, cls: int) -> torch.cuda.CUDAGraph:
         s = torch.cuda.Stream()
         s.wait_stream(torch.cuda.current_stream())
         g = torch.cuda.CUDAGraph()
@@ -357,13 +396,22 @@ class DecodeSession:
             self.step()
         torch.cuda.current_stream().wait_stream(s)
         self.graph = g
+        self.graphs[cls] = g
         return g
 
     def replay(self) -> None:
+        """One step: the captured graph of the current attention shape
+        (captured here the first time that shape comes up), or an eager
+        step before any capture."""
         if self.graph is None:
+            self.graphs = {}
             self.step()
-        else:
-            self.graph.replay()
+            return
+        cls = self._attention_class()
+        g = self.graphs.get(cls)
+        if g is None:
+            g = self._capture(cls)
+        g.replay()
 
     def read_state(self) -> dict[str, int]:
         return kernels.state_dict(self.state)

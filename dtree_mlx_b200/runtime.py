@@ -153,6 +153,7 @@ def run_decode(target, draft, prompt_tokens, max_new_tokens: int, stop_token_ids
     decode_start = time.perf_counter()
     steps = 0
     while start < total_max_tokens:
+        session.host_start = start
         if profile:
             _profiled_step(session, stages)
         elif use_graph and session.graph is None and (steps >= 1 or getattr(session, "warm", False)):

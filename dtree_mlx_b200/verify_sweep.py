@@ -89,6 +89,7 @@ def run(preset: str, layers: int | None, prefixes: list[int], budgets: list[int]
             kernels.TreeBuilder(16, cfg.vocab_size, budget, dev).build(logits, st, tree, keep_topk=False)
             n = int(st[6].item())
             post = torch.zeros(128, dtype=torch.int32, device=dev)
+            eng.use_attention_shape(P, n)  # the shape a decode step at this prefix uses
 
             def fwd():
                 eng.forward_tree(tree.tokens, tree.positions, tree.anc, n, st, post)

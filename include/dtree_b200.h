@@ -400,6 +400,17 @@ DTREE_API int dtree_qwen3_forward_tree(dtree_qwen3_model* model, const int32_t* 
  * (runtime.py:160-215, dtree_runtime.py:455-470). */
 DTREE_API int dtree_qwen3_set_sampling(dtree_qwen3_model* model, float temperature, uint32_t seed);
 
+/* Bound on prefix + tree keys (state->start + n_nodes) that the following
+ * forwards attend over (0: the KV capacity, the default).  A launch-shape
+ * hint for the tree attention (the scaled_dot_product_attention step of
+ * dtree_mlx/qwen3_tree.py:67-76): while the bound is at most 1024 the KV
+ * splits of a head run as one cluster of ceil(bound / 128) CTAs that merge
+ * their partials in shared memory, otherwise as ~one CTA per SM merged by a
+ * second kernel.  Results never depend on it (a longer prefix only takes more
+ * passes per CTA); forwards captured in a CUDA graph keep the shape that was
+ * current at capture. */
+DTREE_API int dtree_qwen3_set_attention_keys(dtree_qwen3_model* model, int max_keys);
+
 /* Dense prompt prefill: replaces Qwen3TargetAdapter.forward_with_hidden_states
  * over the prompt (adapters.py:494-533; the prefill at dtree_runtime.py:342-349
  * and runtime.py:459-465).  Rows t < n_rows (tokens[t] at RoPE position

@@ -57,7 +57,8 @@ def _reference(q, k_plane, v_plane, start, n, masks, n_q_heads):
 @pytest.mark.parametrize("heads", [(32, 8, 128), (8, 4, 64), (16, 4, 256)])
 @pytest.mark.parametrize("start,n,splits", [(0, 1, 0), (5, 25, 0), (200, 64, 0), (2048, 25, 0), (3000, 25, 0),
                                             (2048, 25, 3), (777, 7, 0), (2048, 65, 0), (8192, 65, 0),
-                                            (8192, 25, 0), (513, 100, 0), (8192, 128, 0), (0, 128, 0)])
+                                            (8192, 25, 0), (513, 100, 0), (8192, 128, 0), (0, 128, 0),
+                                            (2048, 25, 16), (2048, 25, 32), (100, 25, 16), (1500, 64, 13)])
 def test_tree_attention_matches_fp32(lib, heads, start, n, splits):
     from dtree_mlx_b200 import kernels
 

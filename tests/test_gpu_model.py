@@ -191,3 +191,30 @@ def test_generate_api_tiny(lib, quant_bits):
     first_diff = next((i for i, (a, b) in enumerate(zip(r_tree.generated_tokens, r_lin.generated_tokens)) if a != b),
                       64)
     assert first_diff >= 16
+
+
+def test_attention_shape_switch_keeps_the_stream(lib, monkeypatch):
+    """A generation whose keys cross the short attention bound (1024) midway
+    replays the step graph of the cluster shape, then captures and replays
+    the split one; its tokens equal those of a run pinned to the split shape
+    (the two give bit-identical attention while the keys fit: same 128-key
+    splits, the same merge arithmetic in the same order)."""
+    from dtree_mlx_b200 import DFlashGenerator
+    from dtree_mlx_b200.engine import Qwen3Engine
+    from dtree_mlx_b200.synthetic import random_prompt
+
+    prompt = random_prompt(960, 32768, seed=3)
+    kw = dict(max_new_tokens=128, decode_mode="dtree", speculative_tokens=16, tree_budget=24)
+    spec = dict(target_model="synthetic:qwen3-tiny:seed=0:kv=1536", draft_model="planted:p=0.8:seed=1")
+    r_switch = DFlashGenerator(**spec).generate_from_tokens(prompt, **kw)
+    monkeypatch.setattr(Qwen3Engine, "short_attention_keys", 0)
+    r_split = DFlashGenerator(**spec).generate_from_tokens(prompt, **kw)
+    assert len(r_switch.output_tokens) == 960 + 128
+    assert r_switch.output_tokens == r_split.output_tokens
+    assert _lib_device_error() == 0
+
+
+def _lib_device_error() -> int:
+    from dtree_mlx_b200 import _lib
+
+    return _lib.device_error()
