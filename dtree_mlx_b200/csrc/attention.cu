@@ -903,29 +903,34 @@ static int plane_tmap(CUtensorMap* out, const void* plane, int rows, int hd) {
   return kOk;
 }
 
-// Largest cluster (<= 8, the merge's register array) that the cluster-merge
-// kernel can be launched with, from the occupancy query with its shared memory
-// (asked once per kernel; 0 on error).  Also opts the kernel into its shared
-// memory.
+// How many clusters of `size` CTAs of the cluster-merge kernel can be resident
+// at once (the driver's occupancy query with its shared memory; asked once per
+// kernel and size, 0 on error).  Also opts the kernel into its shared memory.
 template <typename K>
-static int attn_cluster_max(K kern, int smem) {
+static int attn_cluster_capacity(K kern, int smem, int size) {
   static std::mutex mu;
-  static std::map<const void*, int> known;
+  static std::map<std::pair<const void*, int>, int> known;
   std::lock_guard<std::mutex> lock(mu);
-  const void* key = reinterpret_cast<const void*>(kern);
+  const auto key = std::make_pair(reinterpret_cast<const void*>(kern), size);
   auto it = known.find(key);
   if (it != known.end()) return it->second;
   if (ensure_smem_attr(kern, smem) != cudaSuccess) return 0;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(8, 1, 8);
+  cfg.gridDim = dim3(size, 1, 1);
   cfg.blockDim = dim3(kTcThreads);
   cfg.dynamicSmemBytes = static_cast<size_t>(smem);
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = static_cast<unsigned>(size);
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
   int n = 0;
-  if (cudaOccupancyMaxPotentialClusterSize(&n, kern, &cfg) != cudaSuccess) {
+  if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess) {
     cudaGetLastError();
-    n = 8;  // the portable cluster size
+    n = 0;
   }
-  n = std::max(1, std::min(n, 8));
   known.emplace(key, n);
   return n;
 }
@@ -939,12 +944,13 @@ static int attn_launch_tc(const AttnParams& p, int rb, cudaStream_t stream) {
   if (rc) return rc;
   if ((rc = plane_tmap(&tv, p.v, rows, HD))) return rc;
   const int want = p.cluster_keys > 0 ? (p.cluster_keys + kTcKeys - 1) / kTcKeys : 0;
-  if (p.gate == nullptr && want >= 1 && want <= 8 && want * rb * p.n_kv_heads <= num_sms()) {
+  if (p.gate == nullptr && want >= 1 && want <= 8) {
     // every split of a (row block, KV head) in one cluster, merged in
-    // shared memory (one wave of CTAs at one per SM)
+    // shared memory, when all the clusters can be resident at once (whole
+    // clusters are placed within one GPC: a cluster that waits for room
+    // would run as a second wave)
     auto kern = tree_attn_tc_kernel<HD, false, true>;
-    const int cmax = attn_cluster_max(kern, C::kSmem);
-    if (want <= cmax) {
+    if (attn_cluster_capacity(kern, C::kSmem, want) >= rb * p.n_kv_heads) {
       AttnParams pc = p;
       pc.splits = want;
       DTREE_CUDA_RET(launch_pdl_cluster(kern, dim3(want, rb, p.n_kv_heads), dim3(kTcThreads),
@@ -965,12 +971,10 @@ int attn_prepare(int head_dim) {
   // shapes, outside any stream capture
   if (head_dim == 128) {
     DTREE_CUDA_RET(ensure_smem_attr(tree_attn_tc_kernel<128>, TcCfg<128>::kSmem));
-    if (attn_cluster_max(tree_attn_tc_kernel<128, false, true>, TcCfg<128>::kSmem) < 1)
-      return fail(kErrCuda, "tree attention: cluster size query failed");
+    for (int c = 1; c <= 8; ++c) attn_cluster_capacity(tree_attn_tc_kernel<128, false, true>, TcCfg<128>::kSmem, c);
   } else if (head_dim == 64) {
     DTREE_CUDA_RET(ensure_smem_attr(tree_attn_tc_kernel<64>, TcCfg<64>::kSmem));
-    if (attn_cluster_max(tree_attn_tc_kernel<64, false, true>, TcCfg<64>::kSmem) < 1)
-      return fail(kErrCuda, "tree attention: cluster size query failed");
+    for (int c = 1; c <= 8; ++c) attn_cluster_capacity(tree_attn_tc_kernel<64, false, true>, TcCfg<64>::kSmem, c);
   }
   return kOk;
 }

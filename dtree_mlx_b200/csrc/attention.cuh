@@ -31,8 +31,9 @@ struct AttnParams {
   int chunk_rows;
   int chunk_rbs;        // 128-row blocks per chunk (set by attn_prefill_launch)
   // tree path, head_dim 64 / 128, no gate: a bound on prefix + tree keys
-  // (0: none).  When ceil(bound / 128) <= 8 (and those CTAs for every row
-  // block and KV head fit one per SM) the splits are that many CTAs of one
+  // (0: none).  When ceil(bound / 128) <= 8 (and a cluster of that many CTAs
+  // for every row block and KV head can be resident at once) the splits are
+  // that many CTAs of one
   // thread-block cluster per (row block, KV head) that merge in shared memory
   // (no attn_combine_kernel); keys past the bound stay correct (more passes
   // per CTA)
