@@ -235,7 +235,9 @@ DTREE_API int dtree_lm_head_sample(const void* h, int t_pad, int n_rows, int hid
  * the prefix [0, state->start) and the tree keys at slots start..start+n-1;
  * anc_mask: [n_nodes][2] (bit j of node t: tree slot j visible); out:
  * [n_nodes][ldq] bf16.  head_dim 64, 128 (tcgen05) or 256; splits <= 32
- * (0: one CTA per SM). */
+ * (0: automatic — one CTA per SM, or for head_dim 64 / 128 with
+ * kv_cap <= 1024 ceil(kv_cap / 128) CTAs per KV head as one thread-block
+ * cluster that merges its splits in shared memory). */
 DTREE_API size_t dtree_tree_attention_workspace_bytes(int n_q_heads, int n_nodes, int head_dim, int splits);
 DTREE_API int dtree_tree_attention(const void* q, int ldq, const void* k_plane, const void* v_plane, int kv_cap,
                                    int n_q_heads, int n_kv_heads, int head_dim, int n_nodes,
