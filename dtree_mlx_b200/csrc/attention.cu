@@ -719,7 +719,7 @@ __global__ void __launch_bounds__(kTcThreads) tree_attn_tc_kernel(const __grid_c
     // d % OH; its (m, l) in red_max[q], red_sum[q] (-inf / 0: no keys)
     constexpr int LDS = OH + 4;
     float* const stage0 = reinterpret_cast<float*>(sq);
-    float* const s_w = stage0 + 8 * 32 * LDS;  // [my rows][splits] weights
+    float* const s_w = stage0 + 8 * 32 * LDS;  // [my rows][splits] weights (my rows * splits <= 128 + 7)
     float* const s_il = s_w + 136;             // [my rows] 1 / sum of weights
     static_assert((8 * 32 * LDS + 136 + 128) * 4 <= C::kBar, "merge scratch exceeds the operand space");
     const bool live = ok && n_pass > 0;
