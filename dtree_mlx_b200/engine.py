@@ -200,7 +200,8 @@ class Qwen3Engine:
 
     def set_attention_keys(self, max_keys: int) -> None:
         """Bound on prefix + tree keys of the following forwards (0: the KV
-        capacity): a launch-shape hint only, results do not depend on it."""
+        capacity): a launch-shape hint; forwards within it give the same
+        bits in either shape."""
         call("dtree_qwen3_set_attention_keys", self._handle, int(max_keys))
 
     def use_attention_shape(self, start: int, n_nodes: int) -> None:
@@ -356,7 +357,10 @@ class DecodeSession:
         """1 while the next verify's keys (prefix + tree rows) fit the short
         attention shape of the engine, else 0.  The host learns the prefix
         length after each step (``host_start``); steps replayed without that
-        keep the last known value, which changes only the launch shape."""
+        keep the last known value.  Within the bound the two shapes give
+        bit-identical attention (the same 128-key splits merged in the same
+        order); a short-shape graph replayed past it stays correct with
+        longer splits, rounded differently from the split shape."""
         lim = getattr(self.engine, "short_attention_keys", 0)
         return 1 if lim and self.host_start + self.cfg.n_nodes <= lim else 0
 

@@ -408,9 +408,11 @@ DTREE_API int dtree_qwen3_set_sampling(dtree_qwen3_model* model, float temperatu
  * dtree_mlx/qwen3_tree.py:67-76): while the bound is at most 1024 the KV
  * splits of a head run as one cluster of ceil(bound / 128) CTAs that merge
  * their partials in shared memory, otherwise as ~one CTA per SM merged by a
- * second kernel.  Results never depend on it (a longer prefix only takes more
- * passes per CTA); forwards captured in a CUDA graph keep the shape that was
- * current at capture. */
+ * second kernel.  Both shapes split the keys into the same 128-key blocks
+ * and merge them in the same order while the keys fit the bound, so the
+ * outputs are bit-identical; past the bound the cluster shape stays correct
+ * with longer splits (rounded differently).  Forwards captured in a CUDA
+ * graph keep the shape that was current at capture. */
 DTREE_API int dtree_qwen3_set_attention_keys(dtree_qwen3_model* model, int max_keys);
 
 /* Dense prompt prefill: replaces Qwen3TargetAdapter.forward_with_hidden_states
