@@ -6,7 +6,7 @@
 //   xn   = RMSNorm(h, input_norm)                       rmsnorm / residual_rmsnorm
 //   p    = xn @ Wqkv^T (split-K fp32 partials)          gemm<kEpiPartial>
 //   q,k,v= sum(p); q/k RMSNorm + RoPE; k,v -> cache     qkv_finish_kernel
-//   a    = softmax(q k^T / sqrt(d) + tree mask) v       tree_attn + combine
+//   a    = softmax(q k^T / sqrt(d) + tree mask) v       tree_attn (+ combine; merged in-cluster <= 1024 keys)
 //   p    = a @ Wo^T  (split-K fp32 partials)           gemm<kEpiPartial>
 //   h   += sum(p); xn = RMSNorm(h, post_norm)           residual_rmsnorm_kernel
 //   act  = silu(xn Wg^T) * (xn Wu^T)                    gemm<kEpiSwiglu>
