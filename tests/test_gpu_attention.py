@@ -121,3 +121,32 @@ def test_tree_attention_start_changed_upstream(lib, p_early, p_late):
         err = (out.float() - ref).abs().max().item()
         assert err <= 2e-2, f"max abs err {err}"
     assert _lib.device_error() == 0
+
+
+@pytest.mark.parametrize("heads", [(32, 8, 128), (8, 4, 64)])
+@pytest.mark.parametrize("start,n", [(0, 1), (300, 25), (700, 9), (999, 25), (900, 64)])
+def test_cluster_merge_bit_identical_to_split_shape(lib, heads, start, n):
+    """With kv_cap <= 1024 and automatic splits the KV splits of a head run as
+    one cluster that merges in shared memory; explicit splits of the same
+    count run the split shape with attn_combine_kernel.  Both cut the keys
+    into the same 128-key blocks and merge in split order, so the outputs
+    agree bit for bit."""
+    from dtree_mlx_b200 import kernels
+
+    n_q, n_kv, hd = heads
+    dev = torch.device("cuda")
+    gen = torch.Generator().manual_seed(start * 7 + n + hd)
+    cap = 1024
+    k_plane = torch.randn(n_kv, cap, hd, generator=gen).to(torch.bfloat16)
+    v_plane = torch.randn(n_kv, cap, hd, generator=gen).to(torch.bfloat16)
+    k_plane[:, start + n:] = float("nan")
+    v_plane[:, start + n:] = float("nan")
+    q = torch.randn(n, n_q * hd, generator=gen).to(torch.bfloat16)
+    masks, anc = _random_tree(n, gen)
+    k_plane, v_plane, q, anc = k_plane.to(dev), v_plane.to(dev), q.to(dev), anc.to(dev)
+    state = kernels.new_state(dev, start=start)
+    out_cluster = kernels.tree_attention(q, k_plane, v_plane, state, anc, n, n_q, splits=0)
+    out_split = kernels.tree_attention(q, k_plane, v_plane, state, anc, n, n_q, splits=cap // 128)
+    torch.cuda.synchronize()
+    assert torch.isfinite(out_cluster.float()).all()
+    assert torch.equal(out_cluster, out_split)
